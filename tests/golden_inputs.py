@@ -1,0 +1,59 @@
+"""Seeded inputs shared by the golden-fixture generator and the tests.
+
+Shapes and value distributions follow the benchmark configs: KV caches and embeddings are
+N(0,1) rounded to fp16 (then widened to fp32 for the CPU checkers), prompt rows mix text
+rows (audio codes = pad 1024) with voice-frame rows (16 codes each), codes are uniform in
+[0, 1024).
+"""
+from __future__ import annotations
+
+import hashlib
+
+import numpy as np
+
+WEIGHTS_SEED = 0
+HIDDEN, NVQ, CODEBOOK, LAYERS = 768, 16, 1024, 12
+
+
+def sha(a: np.ndarray) -> str:
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()[:16]
+
+
+def fp16_normal(rng, shape) -> np.ndarray:
+    return rng.standard_normal(shape, dtype=np.float32).astype(np.float16).astype(np.float32)
+
+
+def global_state(L: int, seed: int = 1):
+    """KV [12][L][768] x2, a last hidden [768], and the next embedding [768]."""
+    rng = np.random.default_rng(seed)
+    k = fp16_normal(rng, (LAYERS, L, HIDDEN))
+    v = fp16_normal(rng, (LAYERS, L, HIDDEN))
+    h0 = rng.standard_normal(HIDDEN, dtype=np.float32)
+    x = fp16_normal(rng, HIDDEN)
+    return k, v, h0, x
+
+
+def prompt_rows(n: int, seed: int) -> np.ndarray:
+    """[n][17] int32: text rows with a voice-frame block in the middle third."""
+    rng = np.random.default_rng(seed)
+    rows = np.full((n, NVQ + 1), 1024, np.int32)
+    rows[:, 0] = rng.integers(0, 16384, n)
+    a, b = n // 3, 2 * n // 3
+    rows[a:b, 0] = 8  # user-slot text id of a voice-frame row (prompt.h:14)
+    rows[a:b, 1:] = rng.integers(0, CODEBOOK, (b - a, NVQ))
+    return rows
+
+
+def forced_codes(frames: int, seed: int) -> np.ndarray:
+    rng = np.random.default_rng(seed)
+    return rng.integers(0, CODEBOOK, (frames, NVQ)).astype(np.int32)
+
+
+def sampler_case(case: int):
+    """(logits[1024], history, greedy, seed) for the sampler fixture."""
+    rng = np.random.default_rng(100 + case)
+    logits = (rng.standard_normal(CODEBOOK, dtype=np.float32) * 2.0).astype(np.float32)
+    top = int(np.argmax(logits))
+    prev = np.concatenate([rng.integers(0, CODEBOOK, 12), [top, top, top]]).astype(np.int32)
+    greedy = int(case % 2 == 0)
+    return logits, prev, greedy, 1000 + case
