@@ -1,1 +1,316 @@
-"""moss_b200 -- B200-native engine for MOSS-TTS-Nano's per-frame LLM step (placeholder)."""
+"""moss_b200 -- B200-native engine for MOSS-TTS-Nano's per-frame LLM step.
+
+The product is libmossgpu.so (C ABI: include/mossgpu.h; CUDA kernels for sm_100a in
+csrc/).  This module is the Python host side over that ABI:
+
+* `Engine`   -- the batched engine: stream slots, prefill, one-frame steps over many
+                streams, state access.  One instance per GPU.
+* `LlmModel` -- the reference's single-stream `moss::LlmModel` interface
+                (csrc/include/moss/llm.h:39-90 in the reference) on top of one Engine
+                stream, with the same method names, argument meaning and error behaviour
+                (load() returns (ok, err); generate() stops on the end gate, honours
+                teacher forcing, the cancel flag and the logits dump).
+
+There is no CPU fallback: constructing an Engine without the built library or without a
+CUDA device raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import threading
+from dataclasses import dataclass
+from pathlib import Path
+
+import numpy as np
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "libmossgpu.so"
+
+HIDDEN, HEADS, HEAD_DIM, FF, VOCAB = 768, 12, 64, 3072, 16384
+NVQ, CODEBOOK, AUDIO_PAD, SLOT_TOKEN, END_TOKEN, LOCAL_LEN, LAYERS = 16, 1024, 1024, 9, 7, 17, 12
+
+# Every symbol include/mossgpu.h declares (checked by the tests).
+EXPORTS = [
+    "mossgpu_create", "mossgpu_destroy", "mossgpu_last_error", "mossgpu_version", "mossgpu_set_cuda_stream",
+    "mossgpu_stream_open", "mossgpu_stream_close", "mossgpu_stream_reset", "mossgpu_stream_position",
+    "mossgpu_prefill", "mossgpu_prefill_embeds", "mossgpu_generate_begin", "mossgpu_step",
+    "mossgpu_global_step_embed", "mossgpu_set_state", "mossgpu_get_kv", "mossgpu_get_hidden",
+    "mossgpu_debug_matrix_bytes", "mossgpu_last_launch_count",
+]
+
+
+class MossGpuError(RuntimeError):
+    pass
+
+
+class SampleParams(C.Structure):
+    """moss::SampleParams (reference csrc/include/moss/sampler.h:8-22)."""
+    _fields_ = [("greedy", C.c_int), ("temperature", C.c_float), ("top_k", C.c_int), ("top_p", C.c_float),
+                ("repetition_penalty", C.c_float), ("end_greedy", C.c_int), ("min_frames", C.c_int),
+                ("greedy_frames", C.c_int)]
+
+    @classmethod
+    def make(cls, greedy=True, temperature=1.0, top_k=0, top_p=1.0, repetition_penalty=1.0, end_greedy=True,
+             min_frames=0, greedy_frames=0) -> "SampleParams":
+        return cls(int(greedy), temperature, top_k, top_p, repetition_penalty, int(end_greedy), min_frames,
+                   greedy_frames)
+
+
+_f32 = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+_i32 = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+_LIB = None
+_LIB_LOCK = threading.Lock()
+
+
+def build(force: bool = False) -> Path:
+    from . import buildlib as _b  # noqa: PLC0415
+    return _b.build(force=force)
+
+
+def lib() -> C.CDLL:
+    """Load libmossgpu.so; raises if it has not been built (no fallback)."""
+    global _LIB
+    with _LIB_LOCK:
+        if _LIB is not None:
+            return _LIB
+        if not LIB_PATH.exists():
+            raise MossGpuError(f"{LIB_PATH} is missing: build it with moss_b200.build() (nvcc, sm_100a)")
+        L = C.CDLL(str(LIB_PATH))
+        L.mossgpu_create.restype = C.c_void_p
+        L.mossgpu_create.argtypes = [C.c_char_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_char_p, C.c_int]
+        L.mossgpu_destroy.argtypes = [C.c_void_p]
+        L.mossgpu_last_error.restype = C.c_char_p
+        L.mossgpu_last_error.argtypes = [C.c_void_p]
+        L.mossgpu_version.restype = C.c_char_p
+        L.mossgpu_set_cuda_stream.argtypes = [C.c_void_p, C.c_void_p]
+        L.mossgpu_stream_open.argtypes = [C.c_void_p, C.POINTER(C.c_int)]
+        L.mossgpu_stream_close.argtypes = [C.c_void_p, C.c_int]
+        L.mossgpu_stream_reset.argtypes = [C.c_void_p, C.c_int]
+        L.mossgpu_stream_position.argtypes = [C.c_void_p, C.c_int, C.POINTER(C.c_int)]
+        L.mossgpu_prefill.argtypes = [C.c_void_p, C.c_int, _i32, C.c_int, C.c_int]
+        L.mossgpu_prefill_embeds.argtypes = [C.c_void_p, C.c_int, _f32, C.c_int, C.c_int]
+        L.mossgpu_generate_begin.argtypes = [C.c_void_p, C.c_int, C.c_uint64]
+        L.mossgpu_step.argtypes = [C.c_void_p, _i32, C.c_int, C.POINTER(SampleParams), C.c_void_p, _i32, C.c_void_p,
+                                   C.c_void_p, C.c_void_p, C.c_int]
+        L.mossgpu_global_step_embed.argtypes = [C.c_void_p, _i32, C.c_int, _f32, C.c_void_p]
+        L.mossgpu_set_state.argtypes = [C.c_void_p, C.c_int, _f32, _f32, C.c_int, C.c_void_p]
+        L.mossgpu_get_kv.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
+        L.mossgpu_get_hidden.argtypes = [C.c_void_p, C.c_int, _f32]
+        L.mossgpu_debug_matrix_bytes.argtypes = [C.c_void_p, C.c_char_p,
+                                                 np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS"), C.c_size_t]
+        L.mossgpu_last_launch_count.argtypes = [C.c_void_p]
+        _LIB = L
+        return L
+
+
+def _ptr(a):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+class Engine:
+    """One GPU's batched engine (mossgpu_create)."""
+
+    def __init__(self, weights: str, device: int = 0, max_streams: int = 64, max_ctx: int = 4608, kv_pages: int = 0):
+        self.lib = lib()
+        err = C.create_string_buffer(1024)
+        self.h = self.lib.mossgpu_create(str(weights).encode(), device, max_streams, max_ctx, kv_pages, err, 1024)
+        if not self.h:
+            raise MossGpuError(err.value.decode(errors="replace"))
+        self.max_streams, self.max_ctx = max_streams, max_ctx
+
+    def _check(self, rc: int):
+        if rc != 0:
+            raise MossGpuError(self.lib.mossgpu_last_error(self.h).decode(errors="replace"))
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.mossgpu_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def set_cuda_stream(self, stream_handle: int | None):
+        self._check(self.lib.mossgpu_set_cuda_stream(self.h, C.c_void_p(stream_handle or 0)))
+
+    def open(self) -> int:
+        sid = C.c_int()
+        self._check(self.lib.mossgpu_stream_open(self.h, C.byref(sid)))
+        return sid.value
+
+    def close_stream(self, sid: int):
+        self._check(self.lib.mossgpu_stream_close(self.h, sid))
+
+    def reset(self, sid: int):
+        self._check(self.lib.mossgpu_stream_reset(self.h, sid))
+
+    def position(self, sid: int) -> int:
+        p = C.c_int()
+        self._check(self.lib.mossgpu_stream_position(self.h, sid, C.byref(p)))
+        return p.value
+
+    def prefill(self, sid: int, rows, start: int = 0):
+        rows = np.ascontiguousarray(rows, np.int32).reshape(-1, NVQ + 1)
+        self._check(self.lib.mossgpu_prefill(self.h, sid, rows, rows.shape[0], start))
+
+    def prefill_embeds(self, sid: int, x, start: int = 0):
+        x = np.ascontiguousarray(x, np.float32).reshape(-1, HIDDEN)
+        self._check(self.lib.mossgpu_prefill_embeds(self.h, sid, x, x.shape[0], start))
+
+    def generate_begin(self, sid: int, seed: int = 0):
+        self._check(self.lib.mossgpu_generate_begin(self.h, sid, seed))
+
+    def step(self, sids, params: SampleParams, forced=None, want_logits=False, run_global=True):
+        """One frame for every stream in `sids`.  Returns (codes[n][16], stop[n], gate[n][2], logits)."""
+        sids = np.ascontiguousarray(sids, np.int32).reshape(-1)
+        n = sids.size
+        codes = np.zeros((n, NVQ), np.int32)
+        stop = np.zeros(n, np.uint8)
+        gate = np.zeros((n, 2), np.float32)
+        logits = np.zeros((n, NVQ, CODEBOOK), np.float32) if want_logits else None
+        f = None if forced is None else np.ascontiguousarray(forced, np.int32).reshape(n, NVQ)
+        self._check(self.lib.mossgpu_step(self.h, sids, n, C.byref(params), _ptr(f), codes, _ptr(stop), _ptr(logits),
+                                          _ptr(gate), int(run_global)))
+        return codes, stop.astype(bool), gate, logits
+
+    def global_step_embed(self, sids, x, want_hidden=True):
+        sids = np.ascontiguousarray(sids, np.int32).reshape(-1)
+        x = np.ascontiguousarray(x, np.float32).reshape(sids.size, HIDDEN)
+        out = np.zeros((sids.size, HIDDEN), np.float32) if want_hidden else None
+        self._check(self.lib.mossgpu_global_step_embed(self.h, sids, sids.size, x, _ptr(out)))
+        return out
+
+    def set_state(self, sid: int, k, v, hidden=None):
+        k = np.ascontiguousarray(k, np.float32)
+        v = np.ascontiguousarray(v, np.float32)
+        h = None if hidden is None else np.ascontiguousarray(hidden, np.float32)
+        self._check(self.lib.mossgpu_set_state(self.h, sid, k, v, k.shape[1], _ptr(h)))
+
+    def kv(self, sid: int, layer: int, p0: int, n: int):
+        k = np.zeros((n, HIDDEN), np.float32)
+        v = np.zeros((n, HIDDEN), np.float32)
+        self._check(self.lib.mossgpu_get_kv(self.h, sid, layer, p0, n, _ptr(k), _ptr(v)))
+        return k, v
+
+    def hidden(self, sid: int) -> np.ndarray:
+        out = np.zeros(HIDDEN, np.float32)
+        self._check(self.lib.mossgpu_get_hidden(self.h, sid, out))
+        return out
+
+    def matrix_bytes(self, name: str, rows: int, cols: int) -> np.ndarray:
+        out = np.zeros((rows // 4) * (cols // 32) * 136, np.uint8)
+        self._check(self.lib.mossgpu_debug_matrix_bytes(self.h, name.encode(), out, out.size))
+        return out
+
+    def last_launch_count(self) -> int:
+        return self.lib.mossgpu_last_launch_count(self.h)
+
+
+@dataclass
+class FrameTiming:
+    """moss::FrameTiming (llm.h:34-37)."""
+    global_ms: float = 0.0
+    local_ms: float = 0.0
+
+
+class LlmModel:
+    """The reference's moss::LlmModel interface (llm.h:39-90) over one Engine stream."""
+
+    def __init__(self, device: int = 0, max_ctx: int = 4608, engine: Engine | None = None):
+        self._device, self._max_ctx = device, max_ctx
+        self._engine = engine
+        self._sid = None
+        self._prefix_pos = 0
+        self._prefix_kv = None
+        self._logits_dump_path = ""
+        self._gate_dump_path = ""
+        self._cancel = None
+
+    # llm.h:46 -- bool load(path, std::string* err)
+    def load(self, weights_path: str) -> tuple[bool, str]:
+        try:
+            if self._engine is None:
+                self._engine = Engine(weights_path, self._device, max_streams=1, max_ctx=self._max_ctx)
+            self._sid = self._engine.open()
+        except (MossGpuError, OSError) as e:
+            return False, str(e)
+        return True, ""
+
+    def reset(self):  # llm.h:49
+        self._engine.reset(self._sid)
+
+    def prefill(self, rows, start: int = 0):  # llm.h:53
+        self._engine.prefill(self._sid, rows, start)
+
+    def snapshot_prefix(self):  # llm.h:57, llm.cpp:455-467
+        self._prefix_pos = self.position()
+        if self._prefix_pos > 0:
+            self._prefix_kv = [self._engine.kv(self._sid, l, 0, self._prefix_pos) for l in range(LAYERS)]
+
+    def restore_prefix(self):  # llm.h:59, llm.cpp:469-483
+        if self._prefix_pos <= 0:
+            self._engine.reset(self._sid)
+            return
+        k = np.stack([kv[0] for kv in self._prefix_kv])
+        v = np.stack([kv[1] for kv in self._prefix_kv])
+        self._engine.set_state(self._sid, k, v, None)
+
+    def prefix_pos(self) -> int:
+        return self._prefix_pos
+
+    def set_logits_dump(self, path: str):  # llm.h:76
+        self._logits_dump_path = path
+
+    def set_gate_dump(self, path: str):  # llm.h:79
+        self._gate_dump_path = path
+
+    def set_cancel_flag(self, flag):  # llm.h:83: any object with is_set() (threading.Event)
+        self._cancel = flag
+
+    def hidden(self) -> np.ndarray:
+        return self._engine.hidden(self._sid)
+
+    def position(self) -> int:
+        return self._engine.position(self._sid)
+
+    def generate(self, max_frames: int, params: SampleParams, seed: int = 0, timing: list | None = None,
+                 forced=None, on_frame=None) -> list[list[int]]:
+        """llm.cpp:634-733.  Returns rows [0, code0..code15] like moss::Row (text slot 0)."""
+        import time
+        frames = []
+        logits_dump = [] if self._logits_dump_path else None
+        gate_dump = [] if self._gate_dump_path else None
+        self._engine.generate_begin(self._sid, seed)
+        forced = None if forced is None else np.asarray(forced, np.int32).reshape(-1, NVQ)
+        for f in range(max_frames):
+            if self.position() >= self._max_ctx:
+                break
+            if self._cancel is not None and self._cancel.is_set():
+                break
+            t0 = time.perf_counter()
+            last = not (f + 1 < max_frames)
+            fr = None if forced is None else forced[f]
+            codes, stop, gate, logits = self._engine.step([self._sid], params, forced=fr,
+                                                          want_logits=logits_dump is not None, run_global=not last)
+            dt = (time.perf_counter() - t0) * 1e3
+            if gate_dump is not None:
+                gate_dump.append((f, float(gate[0, 1] - gate[0, 0])))
+            if stop[0]:
+                break
+            if logits_dump is not None:
+                logits_dump.append(logits[0])
+            row = [0] + [int(c) for c in codes[0]]
+            frames.append(row)
+            if timing is not None:
+                timing.append(FrameTiming(global_ms=0.0 if last else dt, local_ms=0.0))
+            if on_frame is not None:
+                on_frame(f, row)
+        if logits_dump is not None:
+            np.asarray(logits_dump, np.float32).tofile(self._logits_dump_path)
+        if gate_dump is not None:
+            with open(self._gate_dump_path, "w") as fh:
+                fh.write("frame,slot_minus_end\n")
+                for f, m in gate_dump:
+                    fh.write(f"{f},{m:.4f}\n")
+        return frames

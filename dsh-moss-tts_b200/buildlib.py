@@ -1,0 +1,34 @@
+"""Build libmossgpu.so (the C-ABI engine) in-tree with nvcc for sm_100a."""
+from __future__ import annotations
+
+import os
+import subprocess
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+CSRC = PKG / "csrc"
+LIB = PKG / "libmossgpu.so"
+SOURCES = ["engine.cu", "capi.cpp"]
+HEADERS = ["types.h", "kernels.cuh", "engine.h", "../../include/mossgpu.h"]
+NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
+FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
+         "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall", "-diag-suppress", "550", "-shared"]
+
+
+def stale() -> bool:
+    if not LIB.exists():
+        return True
+    t = LIB.stat().st_mtime
+    deps = [CSRC / s for s in SOURCES] + [CSRC / h for h in HEADERS] + [Path(__file__)]
+    return any(p.stat().st_mtime > t for p in deps if p.exists())
+
+
+def build(force: bool = False, verbose: bool = False) -> Path:
+    if force or stale():
+        cmd = [NVCC, *FLAGS, "-o", str(LIB), *[str(CSRC / s) for s in SOURCES]]
+        r = subprocess.run(cmd, cwd=CSRC, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"nvcc failed ({r.returncode}):\n{r.stdout}\n{r.stderr}")
+        if verbose:
+            print(r.stdout + r.stderr)
+    return LIB

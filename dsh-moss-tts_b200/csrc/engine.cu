@@ -1,0 +1,784 @@
+// engine.cu -- host side of the B200 engine: .moss upload + repack, the paged KV cache,
+// stream slots, and the launch sequences of one frame (local decoder, gate, codes, global
+// step) and of a prefill.  Exposed through the C ABI in capi.cpp (include/mossgpu.h).
+#include "engine.h"
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <stdexcept>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "kernels.cuh"
+
+namespace mossgpu {
+
+#define CK(call)                                                                                   \
+    do {                                                                                           \
+        cudaError_t e_ = (call);                                                                   \
+        if (e_ != cudaSuccess)                                                                     \
+            throw std::runtime_error(std::string(#call) + ": " + cudaGetErrorString(e_));          \
+    } while (0)
+
+namespace {
+
+template <class T>
+T *dalloc(size_t n, std::vector<void *> &owned) {
+    void *p = nullptr;
+    CK(cudaMalloc(&p, std::max<size_t>(n, 1) * sizeof(T)));
+    owned.push_back(p);
+    return static_cast<T *>(p);
+}
+
+struct Entry {
+    int dtype = 0, rows = 0, cols = 0;
+    uint64_t off = 0, nbytes = 0;
+};
+
+uint64_t fnv(uint64_t h, const void *data, size_t n) {
+    const uint8_t *p = static_cast<const uint8_t *>(data);
+    for (size_t i = 0; i < n; ++i) {
+        h ^= p[i];
+        h *= 1099511628211ull;
+    }
+    return h;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ construction
+
+Engine::Engine(const std::string &path, int device, int max_streams, int max_ctx, int kv_pages)
+    : device_(device), max_streams_(max_streams), max_ctx_(max_ctx) {
+    if (max_streams <= 0 || max_ctx <= 0) throw std::runtime_error("max_streams and max_ctx must be positive");
+    CK(cudaSetDevice(device));
+    CK(cudaStreamCreateWithFlags(&own_stream_, cudaStreamNonBlocking));
+    stream_ = own_stream_;
+    load_weights(path);
+    pages_per_stream_ = (max_ctx + kPage - 1) / kPage;
+    n_pages_ = kv_pages > 0 ? kv_pages : max_streams * pages_per_stream_;
+    r_max_ = std::max(max_streams, kPrefillRows);
+    allocate_state();
+}
+
+Engine::~Engine() {
+    cudaSetDevice(device_);
+    if (stream_) cudaStreamSynchronize(stream_);
+    for (void *p : owned_) cudaFree(p);
+    for (void *p : pinned_) cudaFreeHost(p);
+    if (own_stream_) cudaStreamDestroy(own_stream_);
+}
+
+void Engine::load_weights(const std::string &path) {
+    std::ifstream f(path, std::ios::binary | std::ios::ate);
+    if (!f) throw std::runtime_error("cannot open weights: " + path);
+    const std::streamsize size = f.tellg();
+    if (size <= 16) throw std::runtime_error("weights file too small: " + path);
+    std::vector<uint8_t> file(static_cast<size_t>(size));
+    f.seekg(0);
+    if (!f.read(reinterpret_cast<char *>(file.data()), size)) throw std::runtime_error("short read: " + path);
+    // llm.cpp:426-439: weights fingerprint = FNV-1a over the file size and the first 4 KB
+    const int64_t sz = size;
+    weights_fp_ = fnv(fnv(1469598103934665603ull, &sz, sizeof(sz)), file.data(), std::min<size_t>(4096, file.size()));
+    // weights.cpp:27-126: header, 80-byte entries, payload bounds
+    if (std::memcmp(file.data(), "MOSW", 4) != 0) throw std::runtime_error("bad magic (not a .moss file)");
+    uint32_t version = 0, n_tensors = 0;
+    std::memcpy(&version, file.data() + 4, 4);
+    std::memcpy(&n_tensors, file.data() + 8, 4);
+    if (version != 1) throw std::runtime_error("unsupported .moss version " + std::to_string(version));
+    if (16 + size_t(n_tensors) * 80 > file.size()) throw std::runtime_error("tensor table out of bounds");
+    std::unordered_map<std::string, Entry> ents;
+    for (uint32_t i = 0; i < n_tensors; ++i) {
+        const uint8_t *b = file.data() + 16 + size_t(i) * 80;
+        std::string name(reinterpret_cast<const char *>(b), strnlen(reinterpret_cast<const char *>(b), 48));
+        Entry e;
+        e.dtype = b[48];
+        uint32_t dims[3];
+        std::memcpy(dims, b + 52, 12);
+        std::memcpy(&e.off, b + 64, 8);
+        std::memcpy(&e.nbytes, b + 72, 8);
+        if (e.off + e.nbytes > file.size()) throw std::runtime_error("tensor out of bounds: " + name);
+        e.rows = int(dims[0]);
+        e.cols = int(dims[1]);
+        ents[name] = e;
+    }
+    uint8_t *staging = nullptr;
+    CK(cudaMalloc(&staging, file.size()));
+    CK(cudaMemcpy(staging, file.data(), file.size(), cudaMemcpyHostToDevice));
+
+    auto mat = [&](const std::string &name, int rows, int cols) -> DevMat {
+        auto it = ents.find(name);
+        if (it == ents.end()) throw std::runtime_error("missing matrix: " + name);
+        const Entry &e = it->second;
+        if (e.dtype != 4 || e.rows != rows || e.cols != cols || e.nbytes != uint64_t(rows / 4) * (cols / 32) * 136)
+            throw std::runtime_error("matrix is not q8_0_4x4 [" + std::to_string(rows) + "x" + std::to_string(cols) +
+                                     "]: " + name);
+        DevMat m;
+        m.rows = rows;
+        m.cols = cols;
+        const long long nblocks = (long long)(rows / 4) * (cols / 32);
+        m.qs = dalloc<int8_t>(size_t(nblocks) * 128, owned_);
+        m.sc = dalloc<__half>(size_t(nblocks) * 4, owned_);
+        const long long words = nblocks * 17;
+        k_repack_q8x4<<<unsigned((words + 255) / 256), 256>>>(staging + e.off, m.qs, m.sc, nblocks);
+        CK(cudaGetLastError());
+        mats_[name] = m;
+        return m;
+    };
+    std::vector<std::pair<std::string, int>> vec_list;
+    auto vec = [&](const std::string &name, int n) -> float * {
+        auto it = ents.find(name);
+        if (it == ents.end()) throw std::runtime_error("missing vector: " + name);
+        const Entry &e = it->second;
+        if (e.dtype != 3 || e.rows * e.cols != n || e.nbytes != uint64_t(n) * 4)
+            throw std::runtime_error("vector is not f32[" + std::to_string(n) + "]: " + name);
+        float *d = dalloc<float>(n, owned_);
+        CK(cudaMemcpy(d, staging + e.off, size_t(n) * 4, cudaMemcpyDeviceToDevice));
+        return d;
+    };
+    auto layer = [&](const std::string &p) {
+        Layer L;
+        L.ln1_w = vec(p + "ln1.w", kHidden);
+        L.ln1_b = vec(p + "ln1.b", kHidden);
+        L.ln2_w = vec(p + "ln2.w", kHidden);
+        L.ln2_b = vec(p + "ln2.b", kHidden);
+        L.attn = mat(p + "attn.w", kQKV, kHidden);
+        L.attn_b = vec(p + "attn.b", kQKV);
+        L.proj = mat(p + "proj.w", kHidden, kHidden);
+        L.proj_b = vec(p + "proj.b", kHidden);
+        L.fc_in = mat(p + "fc_in.w", kFF, kHidden);
+        L.fc_in_b = vec(p + "fc_in.b", kFF);
+        L.fc_out = mat(p + "fc_out.w", kHidden, kFF);
+        L.fc_out_b = vec(p + "fc_out.b", kHidden);
+        return L;
+    };
+    for (int i = 0; i < kLayers; ++i) global_[i] = layer("g" + std::to_string(i) + ".");
+    local_ = layer("local.");
+    lnf_w_ = vec("lnf.w", kHidden);
+    lnf_b_ = vec("lnf.b", kHidden);
+    llnf_w_ = vec("local.lnf.w", kHidden);
+    llnf_b_ = vec("local.lnf.b", kHidden);
+    wte_ = mat("wte", kVocab, kHidden);
+    for (int ch = 0; ch < kNVq; ++ch) aemb_[ch] = mat("aemb." + std::to_string(ch), kCodebook, kHidden);
+    CK(cudaDeviceSynchronize());
+    CK(cudaFree(staging));
+    weights_bytes_ = file.size();
+}
+
+void Engine::allocate_state() {
+    kv_ = dalloc<__half>(size_t(kLayers) * n_pages_ * kPageHalfs, owned_);
+    page_table_ = dalloc<int>(size_t(max_streams_) * pages_per_stream_, owned_);
+    CK(cudaMemset(page_table_, 0, size_t(max_streams_) * pages_per_stream_ * sizeof(int)));
+    hidden_ = dalloc<float>(size_t(max_streams_) * kHidden, owned_);
+    CK(cudaMemset(hidden_, 0, size_t(max_streams_) * kHidden * sizeof(float)));
+    lkv_ = dalloc<float>(size_t(max_streams_) * 2 * kLocalLen * kHidden, owned_);
+    counts_ = dalloc<uint16_t>(size_t(max_streams_) * kNVq * kCodebook, owned_);
+    CK(cudaMemset(counts_, 0, size_t(max_streams_) * kNVq * kCodebook * sizeof(uint16_t)));
+
+    const size_t R = size_t(r_max_);
+    x_ = dalloc<float>(R * kHidden, owned_);
+    lx_ = dalloc<float>(R * kHidden, owned_);
+    q_ = dalloc<float>(R * kHidden, owned_);
+    attn_ = dalloc<float>(R * kHidden, owned_);
+    mlp_ = dalloc<float>(R * kFF, owned_);
+    logits_ = dalloc<float>(size_t(max_streams_) * kNVq * kCodebook, owned_);
+    plan_ = dalloc<int>(R + 3, owned_);
+    part_ = dalloc<float>(size_t(kAttnItems) * kPartStride, owned_);
+    counter_ = dalloc<int>(R * kHeads, owned_);
+    CK(cudaMemset(counter_, 0, R * kHeads * sizeof(int)));
+    active_ = dalloc<int>(R, owned_);
+    codes_ = dalloc<int>(R * kNVq, owned_);
+    used_ = dalloc<int>(R * kNVq, owned_);
+    gate_ = dalloc<float>(R * 2, owned_);
+    rows17_ = dalloc<int>(R * (kNVq + 1), owned_);
+
+    // control block: [slot R][pos R][frame R][forced 16R][page updates 1 + 3R][FrameCtl]
+    ctl_ints_ = off_fctl() + int(sizeof(FrameCtl) / sizeof(int)) + 4;
+    d_ctl_ = dalloc<int>(ctl_ints_, owned_);
+    void *hp = nullptr;
+    CK(cudaMallocHost(&hp, size_t(ctl_ints_) * sizeof(int)));
+    pinned_.push_back(hp);
+    h_ctl_ = static_cast<int *>(hp);
+    std::memset(h_ctl_, 0, size_t(ctl_ints_) * sizeof(int));
+    const size_t out_bytes = R * kNVq * 4 * 2 + R * 4 + R * 2 * 4 + size_t(max_streams_) * kNVq * kCodebook * 4 +
+                             R * kHidden * 4;
+    CK(cudaMallocHost(&hp, out_bytes));
+    pinned_.push_back(hp);
+    h_out_ = static_cast<uint8_t *>(hp);
+
+    // RoPE table in double precision, cast to fp32 (llm.cpp:90-102)
+    // rows for every global position and for the 17 local positions
+    const int rope_rows = std::max(max_ctx_, kLocalLen);
+    std::vector<float2> rope(size_t(rope_rows) * (kHeadDim / 2));
+    for (int pos = 0; pos < rope_rows; ++pos)
+        for (int i = 0; i < kHeadDim / 2; ++i) {
+            const double inv = 1.0 / std::pow(10000.0, double(2 * i) / kHeadDim);
+            const double ang = double(pos) * inv;
+            rope[size_t(pos) * (kHeadDim / 2) + i] = make_float2(float(std::cos(ang)), float(std::sin(ang)));
+        }
+    rope_ = dalloc<float2>(rope.size(), owned_);
+    CK(cudaMemcpy(rope_, rope.data(), rope.size() * sizeof(float2), cudaMemcpyHostToDevice));
+
+    slots_.assign(size_t(max_streams_), Slot{});
+    free_pages_.clear();
+    for (int p = n_pages_ - 1; p >= 0; --p) free_pages_.push_back(p);
+
+    set_smem_limits();
+}
+
+// ------------------------------------------------------------------ GEMV launch
+
+namespace {
+
+struct GemvShape {
+    int ks, gpc;
+};
+
+GemvShape shape_for(int cols) {
+    // 2 chunks of 16 B per lane: K=768 -> 3 slices of 8 blocks, 2 groups per CTA (6 warps);
+    // K=3072 -> 12 slices of 8 blocks, 1 group per CTA (12 warps)
+    return cols == kFF ? GemvShape{12, 1} : GemvShape{3, 2};
+}
+
+template <int PRO, int EPI, int MAXR>
+void set_attr() {
+    CK(cudaFuncSetAttribute(k_gemv<PRO, EPI, MAXR>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+}
+
+template <int PRO, int EPI>
+void set_attr_all() {
+    set_attr<PRO, EPI, 1>();
+    set_attr<PRO, EPI, 2>();
+    set_attr<PRO, EPI, 4>();
+    set_attr<PRO, EPI, 8>();
+}
+
+template <int PRO, int EPI, int MAXR>
+void launch_gemv_r(const GemvArgs &a, cudaStream_t st) {
+    const GemvShape s{a.ks, a.gpc};
+    const int warps = s.ks * s.gpc;
+    const int groups = a.w.rows / 4;
+    dim3 grid((groups + s.gpc - 1) / s.gpc, (a.nrows + MAXR - 1) / MAXR);
+    const size_t smem = (size_t(MAXR) * a.w.cols + size_t(warps) * 4 * MAXR + size_t(s.gpc) * 4 * MAXR) * sizeof(float);
+    k_gemv<PRO, EPI, MAXR><<<grid, warps * 32, smem, st>>>(a);
+}
+
+template <int PRO, int EPI>
+void launch_gemv(GemvArgs a, cudaStream_t st) {
+    const GemvShape s = shape_for(a.w.cols);
+    a.ks = s.ks;
+    a.gpc = s.gpc;
+    if (a.nrows <= 1) launch_gemv_r<PRO, EPI, 1>(a, st);
+    else if (a.nrows <= 2) launch_gemv_r<PRO, EPI, 2>(a, st);
+    else if (a.nrows <= 4) launch_gemv_r<PRO, EPI, 4>(a, st);
+    else launch_gemv_r<PRO, EPI, 8>(a, st);
+}
+
+}  // namespace
+
+void Engine::set_smem_limits() {
+    set_attr_all<PRO_LN, EPI_QKV>();
+    set_attr_all<PRO_NONE, EPI_RESID>();
+    set_attr_all<PRO_LN, EPI_GELU>();
+    set_attr_all<PRO_LN, EPI_STORE>();
+}
+
+QMat Engine::qm(const DevMat &m) const { return QMat{m.qs, m.sc, m.rows, m.cols}; }
+
+EmbedTables Engine::tables() const {
+    EmbedTables t;
+    t.wte = qm(wte_);
+    for (int ch = 0; ch < kNVq; ++ch) t.aemb[ch] = qm(aemb_[ch]);
+    return t;
+}
+
+// ------------------------------------------------------------------ launch sequences
+
+// One transformer block over the row batch (llm.cpp:230-246).  local=false: global layer
+// `li` with the paged KV at row_pos; local=true: the local layer at local position lpos.
+void Engine::block(const Layer &L, int li, bool local, int R, const int *row_slot, const int *row_pos, int lpos,
+                   float *x) {
+    GemvArgs a{};
+    a.nrows = R;
+    // LN1 -> QKV + bias + RoPE + KV append
+    a.w = qm(L.attn);
+    a.bias = L.attn_b;
+    a.x = x;
+    a.ldx = kHidden;
+    a.ln_w = L.ln1_w;
+    a.ln_b = L.ln1_b;
+    a.q_out = q_;
+    a.row_slot = row_slot;
+    a.row_pos = local ? nullptr : row_pos;
+    a.fixed_pos = lpos;
+    a.rope = rope_;
+    if (local) {
+        a.kv = nullptr;
+        a.lkv = lkv_;
+    } else {
+        a.kv = kv_ + size_t(li) * n_pages_ * kPageHalfs;
+        a.page_table = page_table_;
+        a.pages_per_stream = pages_per_stream_;
+    }
+    launch_gemv<PRO_LN, EPI_QKV>(a, stream_);
+    ++launches_;
+    // attention
+    if (local) {
+        const int warps = R * kHeads;
+        k_attn_local<<<(warps + 11) / 12, 384, 0, stream_>>>(q_, lkv_, row_slot, lpos, R, attn_);
+    } else {
+        AttnArgs t{};
+        t.q = q_;
+        t.kv = a.kv;
+        t.page_table = page_table_;
+        t.pages_per_stream = pages_per_stream_;
+        t.row_slot = row_slot;
+        t.row_pos = row_pos;
+        t.plan = plan_;
+        t.R = R;
+        t.part = part_;
+        t.counter = counter_;
+        t.out = attn_;
+        k_attn_decode<<<kAttnGrid, 256, 0, stream_>>>(t);
+    }
+    ++launches_;
+    // proj + residual
+    GemvArgs p{};
+    p.nrows = R;
+    p.w = qm(L.proj);
+    p.bias = L.proj_b;
+    p.x = attn_;
+    p.ldx = kHidden;
+    p.out = x;
+    p.ldo = kHidden;
+    launch_gemv<PRO_NONE, EPI_RESID>(p, stream_);
+    ++launches_;
+    // LN2 -> fc_in + gelu
+    GemvArgs f{};
+    f.nrows = R;
+    f.w = qm(L.fc_in);
+    f.bias = L.fc_in_b;
+    f.x = x;
+    f.ldx = kHidden;
+    f.ln_w = L.ln2_w;
+    f.ln_b = L.ln2_b;
+    f.out = mlp_;
+    f.ldo = kFF;
+    launch_gemv<PRO_LN, EPI_GELU>(f, stream_);
+    ++launches_;
+    // fc_out + residual
+    GemvArgs o{};
+    o.nrows = R;
+    o.w = qm(L.fc_out);
+    o.bias = L.fc_out_b;
+    o.x = mlp_;
+    o.ldx = kFF;
+    o.out = x;
+    o.ldo = kHidden;
+    launch_gemv<PRO_NONE, EPI_RESID>(o, stream_);
+    ++launches_;
+}
+
+// 12 global layers over rows already embedded in x_ (row_pos = positions being written).
+void Engine::global_layers(int R, const int *row_slot, const int *row_pos) {
+    k_attn_plan<<<1, 32, 0, stream_>>>(row_pos, R, kAttnItems, plan_);
+    ++launches_;
+    for (int li = 0; li < kLayers; ++li) block(global_[li], li, false, R, row_slot, row_pos, 0, x_);
+}
+
+// ------------------------------------------------------------------ host helpers
+
+void Engine::check_slot(int sid) const {
+    if (sid < 0 || sid >= max_streams_ || !slots_[size_t(sid)].open)
+        throw std::runtime_error("stream " + std::to_string(sid) + " is not open");
+}
+
+void Engine::ensure_pages(int sid, int upto_pos, std::vector<int> &updates) {
+    Slot &s = slots_[size_t(sid)];
+    const int need = upto_pos / kPage + 1;
+    if (upto_pos >= max_ctx_) throw std::runtime_error("stream " + std::to_string(sid) + " reached max_ctx");
+    while (int(s.pages.size()) < need) {
+        if (free_pages_.empty()) throw std::runtime_error("KV page pool exhausted");
+        const int page = free_pages_.back();
+        free_pages_.pop_back();
+        updates.push_back(sid);
+        updates.push_back(int(s.pages.size()));
+        updates.push_back(page);
+        s.pages.push_back(page);
+    }
+}
+
+void Engine::release_pages(Slot &s) {
+    for (int p : s.pages) free_pages_.push_back(p);
+    s.pages.clear();
+}
+
+// Page-table entries reach the device through the control block (no allocation): at most
+// r_max_ entries per pass, applied by k_page_updates before the pass's kernels.
+void Engine::upload_page_updates(const std::vector<int> &updates) {
+    size_t done = 0;
+    const size_t n = updates.size() / 3;
+    if (n == 0) return;
+    int *h = h_ctl_ + off_pages();
+    do {
+        const size_t m = std::min(n - done, size_t(r_max_));
+        h[0] = int(m);
+        std::memcpy(h + 1, updates.data() + 3 * done, m * 3 * sizeof(int));
+        done += m;
+        if (done < n || n == 0) {
+            // flush now: more entries follow, or a pass that only needs the count reset
+            CK(cudaMemcpyAsync(d_ctl_ + off_pages(), h, (1 + 3 * m) * sizeof(int), cudaMemcpyHostToDevice, stream_));
+            if (m) k_page_updates<<<unsigned((m + 127) / 128), 128, 0, stream_>>>(d_ctl_ + off_pages(), page_table_,
+                                                                                pages_per_stream_);
+            CK(cudaStreamSynchronize(stream_));
+            h[0] = 0;
+        }
+    } while (done < n);
+}
+
+// ------------------------------------------------------------------ public API
+
+int Engine::open_stream() {
+    for (int i = 0; i < max_streams_; ++i) {
+        if (!slots_[size_t(i)].open) {
+            slots_[size_t(i)] = Slot{};
+            slots_[size_t(i)].open = true;
+            return i;
+        }
+    }
+    throw std::runtime_error("no free stream slot (max_streams reached)");
+}
+
+void Engine::close_stream(int sid) {
+    check_slot(sid);
+    release_pages(slots_[size_t(sid)]);
+    slots_[size_t(sid)] = Slot{};
+}
+
+void Engine::reset_stream(int sid) {
+    check_slot(sid);
+    slots_[size_t(sid)].pos = 0;
+}
+
+int Engine::position(int sid) const {
+    check_slot(sid);
+    return slots_[size_t(sid)].pos;
+}
+
+void Engine::prefill_common(int sid, int m, int start, const int32_t *rows, const float *xin) {
+    check_slot(sid);
+    Slot &s = slots_[size_t(sid)];
+    start = std::max(0, std::min(start, max_ctx_));
+    m = std::min(m, max_ctx_ - start);  // llm.cpp:329-331
+    if (m <= 0) return;
+    std::vector<int> upd;
+    ensure_pages(sid, start + m - 1, upd);
+    upload_page_updates(upd);
+    for (int c0 = 0; c0 < m; c0 += r_max_) {
+        const int R = std::min(r_max_, m - c0);
+        int *slot = h_ctl_, *pos = h_ctl_ + r_max_;
+        for (int i = 0; i < R; ++i) {
+            slot[i] = sid;
+            pos[i] = start + c0 + i;
+        }
+        CK(cudaMemcpyAsync(d_ctl_, h_ctl_, size_t(2 * r_max_) * sizeof(int), cudaMemcpyHostToDevice, stream_));
+        if (rows) {
+            CK(cudaMemcpyAsync(rows17_, rows + size_t(c0) * (kNVq + 1), size_t(R) * (kNVq + 1) * sizeof(int),
+                               cudaMemcpyHostToDevice, stream_));
+            k_embed_rows<<<R, 256, 0, stream_>>>(tables(), rows17_, R, x_);
+        } else {
+            CK(cudaMemcpyAsync(x_, xin + size_t(c0) * kHidden, size_t(R) * kHidden * sizeof(float),
+                               cudaMemcpyHostToDevice, stream_));
+        }
+        global_layers(R, d_ctl_, d_ctl_ + r_max_);
+        if (c0 + R == m) {
+            // ln_f of the last row becomes the stream's hidden state (llm.cpp:395-399)
+            k_layernorm_rows<<<1, 256, 0, stream_>>>(x_ + size_t(R - 1) * kHidden, 1, lnf_w_, lnf_b_,
+                                                     hidden_ + size_t(sid) * kHidden, nullptr, nullptr);
+        }
+        CK(cudaGetLastError());
+        CK(cudaStreamSynchronize(stream_));
+    }
+    s.pos = start + m;
+}
+
+void Engine::prefill(int sid, const int32_t *rows, int m, int start) {
+    for (int i = 0; i < m * (kNVq + 1); ++i) {
+        const int v = rows[i];
+        if ((i % (kNVq + 1)) == 0 ? (v < 0 || v >= kVocab) : false)
+            throw std::runtime_error("text id out of range in prefill row " + std::to_string(i / (kNVq + 1)));
+    }
+    prefill_common(sid, m, start, rows, nullptr);
+}
+
+void Engine::prefill_embeds(int sid, const float *x, int m, int start) { prefill_common(sid, m, start, nullptr, x); }
+
+void Engine::generate_begin(int sid, uint64_t seed) {
+    check_slot(sid);
+    Slot &s = slots_[size_t(sid)];
+    s.frame = 0;
+    s.seed = seed;
+    CK(cudaMemsetAsync(counts_ + size_t(sid) * kNVq * kCodebook, 0, size_t(kNVq) * kCodebook * sizeof(uint16_t), stream_));
+    CK(cudaStreamSynchronize(stream_));
+}
+
+void Engine::step(const int32_t *sids, int n, const SampleParamsC &p, const int32_t *forced, int32_t *out_codes,
+                  uint8_t *out_stop, float *out_logits, float *out_gate, bool run_global) {
+    if (n <= 0) return;
+    if (n > max_streams_) throw std::runtime_error("batch larger than max_streams");
+    if (!p.greedy && p.top_k != 1) throw std::runtime_error("stochastic sampling is not supported by this build (greedy only)");
+    if (!p.end_greedy) throw std::runtime_error("sampled end decision is not supported by this build (end_greedy only)");
+    launches_ = 0;
+    std::vector<int> upd;
+    std::vector<char> seen(size_t(max_streams_), 0);
+    for (int r = 0; r < n; ++r) {
+        const int sid = sids[r];
+        check_slot(sid);
+        if (seen[size_t(sid)]) throw std::runtime_error("stream listed twice in one step");
+        seen[size_t(sid)] = 1;
+        if (run_global) ensure_pages(sid, slots_[size_t(sid)].pos, upd);
+    }
+    if (forced) {
+        for (int i = 0; i < n * kNVq; ++i)
+            if (forced[i] < 0 || forced[i] >= kCodebook) throw std::runtime_error("forced code out of range");
+    }
+    const int R = n;
+    int *slot = h_ctl_ + off_slot(), *pos = h_ctl_ + off_pos(), *frame = h_ctl_ + off_frame();
+    int *frc = h_ctl_ + off_forced();
+    FrameCtl *fc = reinterpret_cast<FrameCtl *>(h_ctl_ + off_fctl());
+    for (int r = 0; r < R; ++r) {
+        const Slot &s = slots_[size_t(sids[r])];
+        slot[r] = sids[r];
+        pos[r] = s.pos;
+        frame[r] = s.frame;
+        if (forced) std::memcpy(frc + r * kNVq, forced + size_t(r) * kNVq, kNVq * sizeof(int));
+    }
+    fc->min_frames = p.min_frames;
+    fc->greedy_frames = p.greedy_frames;
+    fc->rep_penalty = p.repetition_penalty;
+    fc->end_greedy = p.end_greedy;
+    fc->has_forced = forced ? 1 : 0;
+    // page updates ride in the same control block copy (decode adds at most one page per row)
+    h_ctl_[off_pages()] = int(upd.size() / 3);
+    std::memcpy(h_ctl_ + off_pages() + 1, upd.data(), upd.size() * sizeof(int));
+    CK(cudaMemcpyAsync(d_ctl_, h_ctl_, size_t(ctl_ints_) * sizeof(int), cudaMemcpyHostToDevice, stream_));
+    k_page_updates<<<unsigned((R + 127) / 128), 128, 0, stream_>>>(d_ctl_ + off_pages(), page_table_, pages_per_stream_);
+    ++launches_;
+    const int *d_slot = d_ctl_ + off_slot(), *d_pos = d_ctl_ + off_pos(), *d_frame = d_ctl_ + off_frame();
+    const int *d_forced = d_ctl_ + off_forced();
+    const FrameCtl *d_fc = reinterpret_cast<const FrameCtl *>(d_ctl_ + off_fctl());
+
+    // ---- local decoder: 17 steps (llm.cpp:648-698)
+    k_gather_rows<<<R, 256, 0, stream_>>>(hidden_, d_slot, R, lx_);
+    ++launches_;
+    for (int ls = 0; ls < kLocalLen; ++ls) {
+        if (ls == 1) {
+            k_lookup_rows<<<R, 256, 0, stream_>>>(qm(wte_), kSlotToken, R, lx_);
+            ++launches_;
+        }
+        block(local_, 0, true, R, d_slot, nullptr, ls, lx_);
+        if (ls == 0) {
+            k_gate<<<R, 256, 0, stream_>>>(lx_, R, llnf_w_, llnf_b_, qm(wte_), d_frame, d_fc, active_, gate_);
+            ++launches_;
+        } else {
+            const int ch = ls - 1;
+            GemvArgs h{};
+            h.nrows = R;
+            h.w = qm(aemb_[ch]);
+            h.x = lx_;
+            h.ldx = kHidden;
+            h.ln_w = llnf_w_;
+            h.ln_b = llnf_b_;
+            h.out = logits_ + size_t(ch) * kCodebook;
+            h.ldo = kNVq * kCodebook;
+            launch_gemv<PRO_LN, EPI_STORE>(h, stream_);
+            ++launches_;
+            k_sample_greedy<<<R, 256, 0, stream_>>>(logits_ + size_t(ch) * kCodebook, kNVq * kCodebook, ch, d_slot, R,
+                                                   counts_, d_fc, d_forced, active_, codes_, used_, qm(aemb_[ch]),
+                                                   ch + 1 < kNVq ? lx_ : nullptr);
+            ++launches_;
+        }
+    }
+    // ---- global step on [9, used codes] (llm.cpp:703-708)
+    if (run_global) {
+        k_embed_frame<<<R, 256, 0, stream_>>>(tables(), used_, R, x_);
+        ++launches_;
+        global_layers(R, d_slot, d_pos);
+        k_layernorm_rows<<<R, 256, 0, stream_>>>(x_, R, lnf_w_, lnf_b_, hidden_, d_slot, active_);
+        ++launches_;
+    }
+    CK(cudaGetLastError());
+    // ---- outputs
+    uint8_t *ho = h_out_;
+    int *h_codes = reinterpret_cast<int *>(ho);
+    int *h_active = h_codes + R * kNVq;
+    float *h_gate = reinterpret_cast<float *>(h_active + R);
+    float *h_logits = h_gate + 2 * R;
+    CK(cudaMemcpyAsync(h_codes, codes_, size_t(R) * kNVq * sizeof(int), cudaMemcpyDeviceToHost, stream_));
+    CK(cudaMemcpyAsync(h_active, active_, size_t(R) * sizeof(int), cudaMemcpyDeviceToHost, stream_));
+    CK(cudaMemcpyAsync(h_gate, gate_, size_t(R) * 2 * sizeof(float), cudaMemcpyDeviceToHost, stream_));
+    if (out_logits)
+        CK(cudaMemcpyAsync(h_logits, logits_, size_t(R) * kNVq * kCodebook * sizeof(float), cudaMemcpyDeviceToHost, stream_));
+    CK(cudaStreamSynchronize(stream_));
+    for (int r = 0; r < R; ++r) {
+        const bool act = h_active[r] != 0;
+        if (out_codes) std::memcpy(out_codes + size_t(r) * kNVq, h_codes + size_t(r) * kNVq, kNVq * sizeof(int));
+        if (out_stop) out_stop[r] = act ? 0 : 1;
+        if (out_gate) {
+            out_gate[2 * r] = h_gate[2 * r];
+            out_gate[2 * r + 1] = h_gate[2 * r + 1];
+        }
+        Slot &s = slots_[size_t(sids[r])];
+        if (act) {
+            s.frame += 1;
+            if (run_global) s.pos += 1;
+        }
+    }
+    if (out_logits) std::memcpy(out_logits, h_logits, size_t(R) * kNVq * kCodebook * sizeof(float));
+}
+
+void Engine::global_step_embed(const int32_t *sids, int n, const float *x, float *hidden_out) {
+    if (n <= 0) return;
+    if (n > max_streams_) throw std::runtime_error("batch larger than max_streams");
+    launches_ = 0;
+    std::vector<int> upd;
+    for (int r = 0; r < n; ++r) {
+        check_slot(sids[r]);
+        ensure_pages(sids[r], slots_[size_t(sids[r])].pos, upd);
+    }
+    upload_page_updates(upd);
+    int *slot = h_ctl_, *pos = h_ctl_ + r_max_;
+    for (int r = 0; r < n; ++r) {
+        slot[r] = sids[r];
+        pos[r] = slots_[size_t(sids[r])].pos;
+    }
+    CK(cudaMemcpyAsync(d_ctl_, h_ctl_, size_t(2 * r_max_) * sizeof(int), cudaMemcpyHostToDevice, stream_));
+    CK(cudaMemcpyAsync(x_, x, size_t(n) * kHidden * sizeof(float), cudaMemcpyHostToDevice, stream_));
+    global_layers(n, d_ctl_, d_ctl_ + r_max_);
+    k_layernorm_rows<<<n, 256, 0, stream_>>>(x_, n, lnf_w_, lnf_b_, hidden_, d_ctl_, nullptr);
+    ++launches_;
+    CK(cudaGetLastError());
+    if (hidden_out) {
+        float *h = reinterpret_cast<float *>(h_out_);
+        k_gather_rows<<<n, 256, 0, stream_>>>(hidden_, d_ctl_, n, q_);
+        CK(cudaMemcpyAsync(h, q_, size_t(n) * kHidden * sizeof(float), cudaMemcpyDeviceToHost, stream_));
+        CK(cudaStreamSynchronize(stream_));
+        std::memcpy(hidden_out, h, size_t(n) * kHidden * sizeof(float));
+    } else {
+        CK(cudaStreamSynchronize(stream_));
+    }
+    for (int r = 0; r < n; ++r) slots_[size_t(sids[r])].pos += 1;
+}
+
+// ------------------------------------------------------------------ state access
+
+namespace {
+
+__global__ void k_kv_scatter(const float *__restrict__ src, int n, int p0, const int *__restrict__ pages,
+                             __half *__restrict__ kv, int n_pages, int kvsel) {
+    // src [12][n][768] fp32 -> pages of this stream
+    const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long long total = (long long)kLayers * n * kHidden;
+    if (t >= total) return;
+    const int c = int(t % kHidden);
+    const int p = int((t / kHidden) % n) + p0;
+    const int l = int(t / ((long long)kHidden * n));
+    const int page = pages[p / kPage];
+    kv[(size_t)l * n_pages * kPageHalfs + (size_t)page * kPageHalfs +
+       ((kvsel * kHeads + c / kHeadDim) * kPage + p % kPage) * kHeadDim + c % kHeadDim] = __float2half_rn(src[t]);
+}
+
+__global__ void k_kv_gather(const __half *__restrict__ kv, int n_pages, int layer, int p0, int n,
+                            const int *__restrict__ pages, int kvsel, float *__restrict__ dst) {
+    const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= (long long)n * kHidden) return;
+    const int c = int(t % kHidden);
+    const int p = int(t / kHidden) + p0;
+    const int page = pages[p / kPage];
+    dst[t] = __half2float(kv[(size_t)layer * n_pages * kPageHalfs + (size_t)page * kPageHalfs +
+                             ((kvsel * kHeads + c / kHeadDim) * kPage + p % kPage) * kHeadDim + c % kHeadDim]);
+}
+
+}  // namespace
+
+void Engine::set_state(int sid, const float *k, const float *v, int n_pos, const float *hidden) {
+    check_slot(sid);
+    if (n_pos <= 0 || n_pos > max_ctx_) throw std::runtime_error("bad state length");
+    Slot &s = slots_[size_t(sid)];
+    std::vector<int> upd;
+    ensure_pages(sid, n_pos - 1, upd);
+    upload_page_updates(upd);
+    const size_t nel = size_t(kLayers) * n_pos * kHidden;
+    float *d = nullptr;
+    int *dp = nullptr;
+    CK(cudaMalloc(&d, nel * sizeof(float)));
+    CK(cudaMalloc(&dp, s.pages.size() * sizeof(int)));
+    CK(cudaMemcpy(dp, s.pages.data(), s.pages.size() * sizeof(int), cudaMemcpyHostToDevice));
+    for (int kvsel = 0; kvsel < 2; ++kvsel) {
+        CK(cudaMemcpy(d, kvsel ? v : k, nel * sizeof(float), cudaMemcpyHostToDevice));
+        k_kv_scatter<<<unsigned((nel + 255) / 256), 256, 0, stream_>>>(d, n_pos, 0, dp, kv_, n_pages_, kvsel);
+        CK(cudaStreamSynchronize(stream_));
+    }
+    if (hidden) CK(cudaMemcpy(hidden_ + size_t(sid) * kHidden, hidden, kHidden * sizeof(float), cudaMemcpyHostToDevice));
+    CK(cudaFree(d));
+    CK(cudaFree(dp));
+    s.pos = n_pos;
+}
+
+void Engine::get_kv(int sid, int layer, int p0, int n, float *k, float *v) {
+    check_slot(sid);
+    const Slot &s = slots_[size_t(sid)];
+    if (layer < 0 || layer >= kLayers || p0 < 0 || n <= 0 || (p0 + n - 1) / kPage >= int(s.pages.size()))
+        throw std::runtime_error("get_kv range outside the stream's pages");
+    float *d = nullptr;
+    int *dp = nullptr;
+    CK(cudaMalloc(&d, size_t(n) * kHidden * sizeof(float)));
+    CK(cudaMalloc(&dp, s.pages.size() * sizeof(int)));
+    CK(cudaMemcpy(dp, s.pages.data(), s.pages.size() * sizeof(int), cudaMemcpyHostToDevice));
+    for (int kvsel = 0; kvsel < 2; ++kvsel) {
+        float *out = kvsel ? v : k;
+        if (!out) continue;
+        k_kv_gather<<<unsigned((size_t(n) * kHidden + 255) / 256), 256, 0, stream_>>>(kv_, n_pages_, layer, p0, n, dp,
+                                                                                       kvsel, d);
+        CK(cudaStreamSynchronize(stream_));
+        CK(cudaMemcpy(out, d, size_t(n) * kHidden * sizeof(float), cudaMemcpyDeviceToHost));
+    }
+    CK(cudaFree(d));
+    CK(cudaFree(dp));
+}
+
+void Engine::get_hidden(int sid, float *out) {
+    check_slot(sid);
+    CK(cudaStreamSynchronize(stream_));
+    CK(cudaMemcpy(out, hidden_ + size_t(sid) * kHidden, kHidden * sizeof(float), cudaMemcpyDeviceToHost));
+}
+
+void Engine::debug_matrix_bytes(const std::string &name, uint8_t *out, size_t out_bytes) {
+    auto it = mats_.find(name);
+    if (it == mats_.end()) throw std::runtime_error("no matrix named " + name);
+    const DevMat &m = it->second;
+    const size_t nblocks = size_t(m.rows / 4) * (m.cols / 32);
+    if (out_bytes < nblocks * 136) throw std::runtime_error("output buffer too small");
+    std::vector<int8_t> qs(nblocks * 128);
+    std::vector<uint16_t> sc(nblocks * 4);
+    CK(cudaStreamSynchronize(stream_));
+    CK(cudaMemcpy(qs.data(), m.qs, qs.size(), cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(sc.data(), m.sc, sc.size() * 2, cudaMemcpyDeviceToHost));
+    for (size_t b = 0; b < nblocks; ++b) {
+        std::memcpy(out + b * 136, sc.data() + b * 4, 8);
+        std::memcpy(out + b * 136 + 8, qs.data() + b * 128, 128);
+    }
+}
+
+void Engine::set_cuda_stream(void *s) {
+    CK(cudaStreamSynchronize(stream_));
+    stream_ = s ? static_cast<cudaStream_t>(s) : own_stream_;
+}
+
+}  // namespace mossgpu

@@ -1,0 +1,134 @@
+// engine.h -- the B200 engine behind include/mossgpu.h.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <array>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "types.h"
+
+namespace mossgpu {
+
+struct SampleParamsC {
+    int greedy;
+    float temperature;
+    int top_k;
+    float top_p;
+    float repetition_penalty;
+    int end_greedy;
+    int min_frames;
+    int greedy_frames;
+};
+
+struct DevMat {
+    int8_t *qs = nullptr;
+    __half *sc = nullptr;
+    int rows = 0, cols = 0;
+};
+
+struct Layer {
+    DevMat attn, proj, fc_in, fc_out;
+    float *ln1_w = nullptr, *ln1_b = nullptr, *ln2_w = nullptr, *ln2_b = nullptr;
+    float *attn_b = nullptr, *proj_b = nullptr, *fc_in_b = nullptr, *fc_out_b = nullptr;
+};
+
+class Engine {
+public:
+    static constexpr int kPrefillRows = 256;    // rows per prefill pass
+    static constexpr int kAttnGrid = 148 * 4;   // CTAs of the decode-attention kernel
+    static constexpr int kAttnItems = kAttnGrid * 8 * 8;  // split-K partial capacity
+
+    Engine(const std::string &weights_path, int device, int max_streams, int max_ctx, int kv_pages);
+    ~Engine();
+    Engine(const Engine &) = delete;
+    Engine &operator=(const Engine &) = delete;
+
+    int open_stream();
+    void close_stream(int sid);
+    void reset_stream(int sid);
+    int position(int sid) const;
+    void prefill(int sid, const int32_t *rows, int m, int start);
+    void prefill_embeds(int sid, const float *x, int m, int start);
+    void generate_begin(int sid, uint64_t seed);
+    void step(const int32_t *sids, int n, const SampleParamsC &p, const int32_t *forced, int32_t *out_codes,
+              uint8_t *out_stop, float *out_logits, float *out_gate, bool run_global);
+    void global_step_embed(const int32_t *sids, int n, const float *x, float *hidden_out);
+    void set_state(int sid, const float *k, const float *v, int n_pos, const float *hidden);
+    void get_kv(int sid, int layer, int p0, int n, float *k, float *v);
+    void get_hidden(int sid, float *out);
+    void debug_matrix_bytes(const std::string &name, uint8_t *out, size_t out_bytes);
+    void set_cuda_stream(void *s);
+    int last_launches() const { return launches_; }
+    uint64_t weights_fingerprint() const { return weights_fp_; }
+    int device() const { return device_; }
+
+private:
+    struct Slot {
+        bool open = false;
+        int pos = 0;
+        int frame = 0;
+        uint64_t seed = 0;
+        std::vector<int> pages;
+    };
+
+    void load_weights(const std::string &path);
+    void allocate_state();
+    void set_smem_limits();
+    QMat qm(const DevMat &m) const;
+    EmbedTables tables() const;
+    void block(const Layer &L, int li, bool local, int R, const int *row_slot, const int *row_pos, int lpos, float *x);
+    void global_layers(int R, const int *row_slot, const int *row_pos);
+    void check_slot(int sid) const;
+    void ensure_pages(int sid, int upto_pos, std::vector<int> &updates);
+    void release_pages(Slot &s);
+    void upload_page_updates(const std::vector<int> &updates);
+    void prefill_common(int sid, int m, int start, const int32_t *rows, const float *x);
+
+    // control-block layout (ints) for R = r_max_ rows
+    int off_slot() const { return 0; }
+    int off_pos() const { return r_max_; }
+    int off_frame() const { return 2 * r_max_; }
+    int off_forced() const { return 3 * r_max_; }
+    int off_pages() const { return 19 * r_max_; }  // [count][slot, index, page] x r_max_
+    int off_fctl() const { return 22 * r_max_ + 1; }
+
+    int device_ = 0;
+    int max_streams_ = 0, max_ctx_ = 0, pages_per_stream_ = 0, n_pages_ = 0, r_max_ = 0;
+    cudaStream_t stream_ = nullptr, own_stream_ = nullptr;
+    std::vector<void *> owned_, pinned_;
+    size_t weights_bytes_ = 0;
+    uint64_t weights_fp_ = 0;
+
+    std::array<Layer, kLayers> global_{};
+    Layer local_{};
+    float *lnf_w_ = nullptr, *lnf_b_ = nullptr, *llnf_w_ = nullptr, *llnf_b_ = nullptr;
+    DevMat wte_{};
+    std::array<DevMat, kNVq> aemb_{};
+    std::unordered_map<std::string, DevMat> mats_;
+
+    // persistent per-stream state
+    __half *kv_ = nullptr;
+    int *page_table_ = nullptr;
+    float *hidden_ = nullptr, *lkv_ = nullptr;
+    uint16_t *counts_ = nullptr;
+    float2 *rope_ = nullptr;
+    // row-batch scratch
+    float *x_ = nullptr, *lx_ = nullptr, *q_ = nullptr, *attn_ = nullptr, *mlp_ = nullptr, *logits_ = nullptr;
+    int *plan_ = nullptr, *counter_ = nullptr, *active_ = nullptr, *codes_ = nullptr, *used_ = nullptr;
+    float *part_ = nullptr, *gate_ = nullptr;
+    int *rows17_ = nullptr;
+    int *d_ctl_ = nullptr, *h_ctl_ = nullptr;
+    int ctl_ints_ = 0;
+    uint8_t *h_out_ = nullptr;
+
+    std::vector<Slot> slots_;
+    std::vector<int> free_pages_;
+    int launches_ = 0;
+};
+
+}  // namespace mossgpu

@@ -1,0 +1,696 @@
+// kernels.cuh -- sm_100a kernels for the MOSS-TTS-Nano per-frame LLM step.
+//
+// Work is expressed over a "row batch": R rows, row r = (stream slot, position).  A decode
+// step is one row per stream; a prefill is one row per prompt position.  Every kernel reads
+// its per-row data (slot, position, frame index, forced codes) from device memory, so the
+// whole frame can be captured once per batch size and replayed as a CUDA graph.
+//
+// Data layout in HBM (see engine.cu for allocation):
+//   weights  Q8_0_4X4 split into two planes per matrix (engine.cu: repack kernel):
+//              qs [R/4][K/32][4][32] int8   (the file's 128 quant bytes of each block)
+//              sc [R/4][K/32][4]     fp16   (the file's 8 scale bytes of each block)
+//   KV       fp16 pages of 16 positions: [layer][page][k|v][head][16][64]
+//   local KV fp32 [slot][k|v][17][768]
+#pragma once
+
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "types.h"
+
+namespace mossgpu {
+
+// --------------------------------------------------------------------------- helpers
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+__device__ __forceinline__ int4 ldg_stream(const void *p) {
+    int4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.s32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+// gelu_new (llm.cpp:22-25), same operation order
+__device__ __forceinline__ float gelu_new(float v) {
+    const float k = 0.7978845608028654f;
+    const float c = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, v), v), v);
+    return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, tanhf(__fmul_rn(k, __fadd_rn(v, c)))));
+}
+
+__device__ __forceinline__ void unpack16(const int4 q, float *w) {
+    const int words[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) w[4 * i + j] = (float)(int8_t)((words[i] >> (8 * j)) & 0xff);
+    }
+}
+
+// LayerNorm of one 768-vector held in shared memory, in place, by one warp (llm.cpp:159-171).
+__device__ __forceinline__ void warp_layernorm(float *x, const float *w, const float *b) {
+    const int lane = threadIdx.x & 31;
+    float s = 0.f;
+    for (int i = lane; i < kHidden; i += 32) s += x[i];
+    const float mean = __fdiv_rn(warp_sum(s), (float)kHidden);
+    float v = 0.f;
+    for (int i = lane; i < kHidden; i += 32) {
+        const float d = x[i] - mean;
+        v = fmaf(d, d, v);
+    }
+    const float var = __fdiv_rn(warp_sum(v), (float)kHidden);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(var + 1e-5f));
+    __syncwarp();
+    for (int i = lane; i < kHidden; i += 32)
+        x[i] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(x[i], mean), inv), w[i]), b[i]);
+}
+
+// --------------------------------------------------------------------------- weights repack
+
+// Split Q8_0_4X4 file bytes (136-byte blocks: 8 scale bytes + 128 quant bytes) into the
+// 16-byte-aligned quant plane and the scale plane.  A pure byte permutation.
+__global__ void k_repack_q8x4(const uint8_t *__restrict__ src, int8_t *__restrict__ qs, __half *__restrict__ sc,
+                              long long nblocks) {
+    const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;  // one thread per 8-byte word
+    const long long words = nblocks * 17;
+    if (t >= words) return;
+    const long long blk = t / 17;
+    const int w = (int)(t - blk * 17);
+    const uint8_t *s = src + blk * 136 + w * 8;  // 8-byte aligned: 136 = 17 * 8
+    const uint2 v = *reinterpret_cast<const uint2 *>(s);
+    if (w == 0) {
+        *reinterpret_cast<uint2 *>(sc + blk * 4) = v;
+    } else {
+        *reinterpret_cast<uint2 *>(qs + blk * 128 + (w - 1) * 8) = v;
+    }
+}
+
+// --------------------------------------------------------------------------- GEMV
+
+enum { PRO_NONE = 0, PRO_LN = 1 };
+enum { EPI_STORE = 0, EPI_QKV = 1, EPI_RESID = 2, EPI_GELU = 3 };
+
+struct GemvArgs {
+    QMat w;
+    const float *bias;     // [rows] or null
+    const float *x;        // input rows [R][ldx]
+    int ldx;
+    const float *ln_w, *ln_b;
+    int nrows;             // R
+    int ks;                // K slices per group (warps per group)
+    int gpc;               // groups per CTA
+    float *out;            // EPI_STORE/GELU: [R][ldo]; EPI_RESID: residual [R][ldo] (in place)
+    int ldo;
+    // EPI_QKV
+    float *q_out;          // [R][768]
+    __half *kv;            // paged global KV for this layer (layer offset applied)
+    const int *page_table; // [slots][pages_per_stream]
+    int pages_per_stream;
+    float *lkv;            // local KV [slots][2][17][768] (when kv == null)
+    const int *row_slot;
+    const int *row_pos;    // position used for RoPE and the KV write (null: fixed_pos)
+    int fixed_pos;         // local decoder: the local position of every row
+    const float2 *rope;    // [max_ctx][32] (cos, sin)
+};
+
+// y[r][row] = sum_k W[row][k] * x'[r][k], x' = LN(x) or x, W in Q8_0_4X4 (fp32 math, A16).
+// A warp owns one (group of 4 rows, K slice); lane l always reads row (l%8)/2, half l%2 of
+// each 32-column block, so a warp's loads are 512 contiguous bytes.
+template <int PRO, int EPI, int MAXR>
+__global__ void __launch_bounds__(512) k_gemv(const GemvArgs a) {
+    extern __shared__ __align__(16) float smem[];
+    const int K = a.w.cols;
+    const int nb = K >> 5;
+    const int r0 = blockIdx.y * MAXR;
+    const int nr = min(MAXR, a.nrows - r0);
+    float *xs = smem;                      // [MAXR][K]
+    float *red = smem + MAXR * K;          // [warps][4][MAXR]
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int nwarps = blockDim.x >> 5;
+
+    // 1. stage the input rows (and LayerNorm them) in shared memory
+    for (int i = tid; i < nr * (K >> 2); i += blockDim.x) {
+        const int r = i / (K >> 2), c = i - r * (K >> 2);
+        reinterpret_cast<float4 *>(xs + r * K)[c] =
+            reinterpret_cast<const float4 *>(a.x + (size_t)(r0 + r) * a.ldx)[c];
+    }
+    __syncthreads();
+    if (PRO == PRO_LN) {
+        for (int r = warp; r < nr; r += nwarps) warp_layernorm(xs + r * K, a.ln_w, a.ln_b);
+        __syncthreads();
+    }
+
+    // 2. dot products
+    const int gl = warp / a.ks, slice = warp - gl * a.ks;
+    const int g = blockIdx.x * a.gpc + gl;
+    const int ngroups = a.w.rows >> 2;
+    const int bps = nb / a.ks;              // blocks per slice
+    const int k = (lane & 7) >> 1, h = lane & 1;
+    float acc[MAXR];
+#pragma unroll
+    for (int r = 0; r < MAXR; ++r) acc[r] = 0.f;
+    if (gl < a.gpc && g < ngroups) {
+        const int8_t *wq = a.w.qs + ((size_t)g * nb + (size_t)slice * bps) * 128;
+        const __half *ws = a.w.sc + ((size_t)g * nb + (size_t)slice * bps) * 4;
+        const int nchunks = bps * 8;
+        for (int i = lane; i < nchunks; i += 64) {
+            int4 q0 = ldg_stream(wq + (size_t)i * 16);
+            int4 q1 = make_int4(0, 0, 0, 0);
+            const bool two = i + 32 < nchunks;
+            if (two) q1 = ldg_stream(wq + (size_t)(i + 32) * 16);
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                if (u == 1 && !two) break;
+                const int ii = i + 32 * u;
+                const int b = ii >> 3;
+                const float d = __half2float(ws[b * 4 + k]);
+                float wf[16];
+                unpack16(u ? q1 : q0, wf);
+                const int xoff = (slice * bps + b) * 32 + h * 16;
+#pragma unroll
+                for (int r = 0; r < MAXR; ++r) {
+                    if (r < nr) {
+                        const float4 *xv = reinterpret_cast<const float4 *>(xs + r * K + xoff);
+                        float s = 0.f;
+#pragma unroll
+                        for (int t = 0; t < 4; ++t) {
+                            const float4 xx = xv[t];
+                            s = fmaf(wf[4 * t + 0], xx.x, s);
+                            s = fmaf(wf[4 * t + 1], xx.y, s);
+                            s = fmaf(wf[4 * t + 2], xx.z, s);
+                            s = fmaf(wf[4 * t + 3], xx.w, s);
+                        }
+                        acc[r] = fmaf(s, d, acc[r]);
+                    }
+                }
+            }
+        }
+    }
+    // reduce the 8 lanes that share row k (xor over h and lane/8)
+#pragma unroll
+    for (int r = 0; r < MAXR; ++r) {
+        float v = acc[r];
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 8);
+        v += __shfl_xor_sync(0xffffffffu, v, 16);
+        acc[r] = v;
+    }
+    if (lane < 8 && (lane & 1) == 0) {
+#pragma unroll
+        for (int r = 0; r < MAXR; ++r) red[(warp * 4 + (lane >> 1)) * MAXR + r] = acc[r];
+    }
+    __syncthreads();
+
+    // 3. epilogue: thread (gl, k, r) sums the K slices of its output
+    float *fin = red + nwarps * 4 * MAXR;   // [gpc][4][MAXR]
+    for (int t = tid; t < a.gpc * 4 * MAXR; t += blockDim.x) {
+        const int egl = t / (4 * MAXR);
+        const int ek = (t / MAXR) & 3;
+        const int er = t % MAXR;
+        float v = 0.f;
+        for (int s = 0; s < a.ks; ++s) v += red[((egl * a.ks + s) * 4 + ek) * MAXR + er];
+        fin[t] = v;
+    }
+    __syncthreads();
+    for (int t = tid; t < a.gpc * 4 * MAXR; t += blockDim.x) {
+        const int egl = t / (4 * MAXR);
+        const int ek = (t / MAXR) & 3;
+        const int er = t % MAXR;
+        const int eg = blockIdx.x * a.gpc + egl;
+        if (er >= nr || eg >= ngroups) continue;
+        const int row = eg * 4 + ek;
+        const int rr = r0 + er;
+        float v = fin[t];
+        if (EPI == EPI_STORE) {
+            if (a.bias) v = __fadd_rn(v, a.bias[row]);
+            a.out[(size_t)rr * a.ldo + row] = v;
+        } else if (EPI == EPI_GELU) {
+            a.out[(size_t)rr * a.ldo + row] = gelu_new(__fadd_rn(v, a.bias[row]));
+        } else if (EPI == EPI_RESID) {
+            float *o = a.out + (size_t)rr * a.ldo + row;
+            *o = __fadd_rn(*o, __fadd_rn(v, a.bias[row]));
+        } else {  // EPI_QKV: bias, RoPE on q and k (pairs 2i,2i+1 share a 4-row group), KV append
+            if (ek & 1) continue;  // the even row of each pair writes both rows
+            const float v0 = __fadd_rn(v, a.bias[row]);
+            const float v1 = __fadd_rn(fin[t + MAXR], a.bias[row + 1]);
+            const int pos = a.row_pos ? a.row_pos[rr] : a.fixed_pos;
+            float o0 = v0, o1 = v1;
+            if (row < 2 * kHidden) {
+                const int i = (row % kHeadDim) >> 1;
+                const float2 cs = a.rope[(size_t)pos * (kHeadDim / 2) + i];
+                o0 = __fsub_rn(__fmul_rn(v0, cs.x), __fmul_rn(v1, cs.y));
+                o1 = __fadd_rn(__fmul_rn(v1, cs.x), __fmul_rn(v0, cs.y));
+            }
+            if (row < kHidden) {
+                a.q_out[(size_t)rr * kHidden + row] = o0;
+                a.q_out[(size_t)rr * kHidden + row + 1] = o1;
+            } else {
+                const int kvsel = row < 2 * kHidden ? 0 : 1;
+                const int c = row - kHidden * (1 + kvsel);
+                const int slot = a.row_slot[rr];
+                if (a.kv) {
+                    const int page = a.page_table[(size_t)slot * a.pages_per_stream + pos / kPage];
+                    __half *dst = a.kv + (size_t)page * kPageHalfs +
+                                  ((kvsel * kHeads + c / kHeadDim) * kPage + pos % kPage) * kHeadDim + (c % kHeadDim);
+                    *reinterpret_cast<__half2 *>(dst) = __floats2half2_rn(o0, o1);
+                } else {
+                    float *dst = a.lkv + (((size_t)slot * 2 + kvsel) * kLocalLen + pos) * kHidden + c;
+                    dst[0] = o0;
+                    dst[1] = o1;
+                }
+            }
+        }
+    }
+}
+
+// --------------------------------------------------------------------------- attention
+
+// Split-K plan over the row batch: row r attends to n_r = pos_r + 1 positions, cut into
+// chunks of `chunk` positions.  item_start[r] = first chunk index of row r; the chunk is the
+// smallest power-of-two multiple of kAttnChunk keeping chunks*heads within `max_items`.
+__global__ void k_attn_plan(const int *__restrict__ row_pos, int R, int max_items, int *__restrict__ plan) {
+    // plan[0] = chunk, plan[1] = total chunks, plan[2 + r] = item_start[r] (R + 1 entries)
+    __shared__ int s_chunk;
+    if (threadIdx.x == 0) {
+        int chunk = kAttnChunk;
+        for (;;) {
+            long long total = 0;
+            for (int r = 0; r < R; ++r) total += (row_pos[r] + 1 + chunk - 1) / chunk;
+            if (total * kHeads <= max_items || chunk >= (1 << 20)) break;
+            chunk *= 2;
+        }
+        s_chunk = chunk;
+        plan[0] = chunk;
+        int acc = 0;
+        for (int r = 0; r < R; ++r) {
+            plan[2 + r] = acc;
+            acc += (row_pos[r] + 1 + chunk - 1) / chunk;
+        }
+        plan[2 + R] = acc;
+        plan[1] = acc;
+    }
+}
+
+struct AttnArgs {
+    const float *q;         // [R][768]
+    const __half *kv;       // layer base of the paged KV
+    const int *page_table;
+    int pages_per_stream;
+    const int *row_slot, *row_pos;
+    const int *plan;        // from k_attn_plan
+    int R;
+    float *part;            // [items][kPartStride] partials: m, l, pad, pad, o[64]
+    int *counter;           // [R][12], zero between launches
+    float *out;             // [R][768]
+};
+
+// Flash-decode over fp16 pages.  One warp per (chunk, head): 8 lanes per position (8 dims
+// each), 4 positions per step, online softmax in fp32, partials merged by the last warp
+// of each (row, head) to finish (atomic arrival count, no waiting).
+__global__ void __launch_bounds__(256) k_attn_decode(const AttnArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int ps = lane >> 3, ds = lane & 7;
+    const int chunk = a.plan[0];
+    const int total = a.plan[1] * kHeads;
+    const int *istart = a.plan + 2;
+    const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int nw = (gridDim.x * blockDim.x) >> 5;
+    for (int item = gw; item < total; item += nw) {
+        const int cg = item / kHeads, hd = item - cg * kHeads;
+        int lo = 0, hi = a.R - 1;  // row r with istart[r] <= cg < istart[r+1]
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (istart[mid] <= cg) lo = mid; else hi = mid - 1;
+        }
+        const int r = lo;
+        const int c = cg - istart[r];
+        const int nchunks = istart[r + 1] - istart[r];
+        const int n = a.row_pos[r] + 1;
+        const int slot = a.row_slot[r];
+        const int p0 = c * chunk, p1 = min(n, p0 + chunk);
+        float qv[8];
+        {
+            const float4 *qp = reinterpret_cast<const float4 *>(a.q + (size_t)r * kHidden + hd * kHeadDim + ds * 8);
+            const float4 x0 = qp[0], x1 = qp[1];
+            qv[0] = x0.x * 0.125f; qv[1] = x0.y * 0.125f; qv[2] = x0.z * 0.125f; qv[3] = x0.w * 0.125f;
+            qv[4] = x1.x * 0.125f; qv[5] = x1.y * 0.125f; qv[6] = x1.z * 0.125f; qv[7] = x1.w * 0.125f;
+        }
+        float m = -INFINITY, l = 0.f, o[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = 0.f;
+        const int *pt = a.page_table + (size_t)slot * a.pages_per_stream;
+        for (int p = p0 + ps; p < p1; p += 4) {
+            const __half *base = a.kv + (size_t)pt[p / kPage] * kPageHalfs + ((size_t)hd * kPage + p % kPage) * kHeadDim + ds * 8;
+            const int4 kr = *reinterpret_cast<const int4 *>(base);
+            const int4 vr = *reinterpret_cast<const int4 *>(base + kHeads * kPage * kHeadDim);
+            const __half2 *kh = reinterpret_cast<const __half2 *>(&kr);
+            float s = 0.f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float2 kf = __half22float2(kh[j]);
+                s = fmaf(qv[2 * j], kf.x, s);
+                s = fmaf(qv[2 * j + 1], kf.y, s);
+            }
+            s += __shfl_xor_sync(0xffffffffu, s, 1);
+            s += __shfl_xor_sync(0xffffffffu, s, 2);
+            s += __shfl_xor_sync(0xffffffffu, s, 4);
+            const float mn = fmaxf(m, s);
+            const float corr = __expf(m - mn);
+            const float pw = __expf(s - mn);
+            l = l * corr + pw;
+            const __half2 *vh = reinterpret_cast<const __half2 *>(&vr);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float2 vf = __half22float2(vh[j]);
+                o[2 * j] = fmaf(pw, vf.x, o[2 * j] * corr);
+                o[2 * j + 1] = fmaf(pw, vf.y, o[2 * j + 1] * corr);
+            }
+            m = mn;
+        }
+        // merge the 4 position groups (lanes ds, ds+8, ds+16, ds+24)
+#pragma unroll
+        for (int off = 8; off <= 16; off <<= 1) {
+            const float mo = __shfl_xor_sync(0xffffffffu, m, off);
+            const float lo2 = __shfl_xor_sync(0xffffffffu, l, off);
+            const float mn = fmaxf(m, mo);
+            const float c1 = (m == -INFINITY) ? 0.f : __expf(m - mn);
+            const float c2 = (mo == -INFINITY) ? 0.f : __expf(mo - mn);
+            l = l * c1 + lo2 * c2;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float oo = __shfl_xor_sync(0xffffffffu, o[j], off);
+                o[j] = o[j] * c1 + oo * c2;
+            }
+            m = mn;
+        }
+        if (nchunks == 1) {
+            if (lane < 8) {
+                const float inv = 1.f / l;
+                float *dst = a.out + (size_t)r * kHidden + hd * kHeadDim + ds * 8;
+                reinterpret_cast<float4 *>(dst)[0] = make_float4(o[0] * inv, o[1] * inv, o[2] * inv, o[3] * inv);
+                reinterpret_cast<float4 *>(dst)[1] = make_float4(o[4] * inv, o[5] * inv, o[6] * inv, o[7] * inv);
+            }
+            continue;
+        }
+        float *pp = a.part + (size_t)item * kPartStride;
+        if (lane < 8) {
+            reinterpret_cast<float4 *>(pp + 4 + ds * 8)[0] = make_float4(o[0], o[1], o[2], o[3]);
+            reinterpret_cast<float4 *>(pp + 4 + ds * 8)[1] = make_float4(o[4], o[5], o[6], o[7]);
+            if (lane == 0) { pp[0] = m; pp[1] = l; }
+        }
+        // publish: the warp's stores, then (one lane) a device fence and the arrival count
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) {
+            __threadfence();
+            last = (atomicAdd(a.counter + r * kHeads + hd, 1) == nchunks - 1);
+            __threadfence();
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (!last) continue;
+        // this warp saw every other chunk arrive: combine all chunks of (r, hd)
+        const size_t ibase = (size_t)istart[r] * kHeads + hd;
+        float M = -INFINITY;
+        for (int cc = lane; cc < nchunks; cc += 32)
+            M = fmaxf(M, __ldcg(a.part + (ibase + (size_t)cc * kHeads) * kPartStride));
+        M = warp_max(M);
+        float L = 0.f;
+        float o0 = 0.f, o1 = 0.f;  // dims 2*lane, 2*lane+1
+        for (int cc = 0; cc < nchunks; ++cc) {
+            const float *q = a.part + (ibase + (size_t)cc * kHeads) * kPartStride;
+            const float w = __expf(__ldcg(q) - M);
+            L = fmaf(__ldcg(q + 1), w, L);
+            const float2 ov = __ldcg(reinterpret_cast<const float2 *>(q + 4) + lane);
+            o0 = fmaf(ov.x, w, o0);
+            o1 = fmaf(ov.y, w, o1);
+        }
+        const float inv = 1.f / L;
+        float *dst = a.out + (size_t)r * kHidden + hd * kHeadDim;
+        reinterpret_cast<float2 *>(dst)[lane] = make_float2(o0 * inv, o1 * inv);
+        if (lane == 0) a.counter[r * kHeads + hd] = 0;
+    }
+}
+
+// Local decoder attention: n = lpos + 1 <= 17 positions of fp32 local KV.
+// One warp per (row, head); scores in llm.cpp:189-217 order per position.
+__global__ void __launch_bounds__(384) k_attn_local(const float *__restrict__ q, const float *__restrict__ lkv,
+                                                    const int *__restrict__ row_slot, int lpos, int R,
+                                                    float *__restrict__ out) {
+    const int lane = threadIdx.x & 31;
+    const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (w >= R * kHeads) return;
+    const int r = w / kHeads, hd = w - r * kHeads;
+    const int slot = row_slot[r];
+    const int n = lpos + 1;
+    const float *kb = lkv + ((size_t)slot * 2 + 0) * kLocalLen * kHidden + hd * kHeadDim;
+    const float *vb = lkv + ((size_t)slot * 2 + 1) * kLocalLen * kHidden + hd * kHeadDim;
+    const float *qh = q + (size_t)r * kHidden + hd * kHeadDim;
+    float s = -INFINITY;
+    if (lane < n) {
+        float dot = 0.f;
+        const float4 *kp = reinterpret_cast<const float4 *>(kb + (size_t)lane * kHidden);
+        const float4 *qp = reinterpret_cast<const float4 *>(qh);
+#pragma unroll
+        for (int d = 0; d < kHeadDim / 4; ++d) {
+            const float4 kk = kp[d], qq = qp[d];
+            dot = fmaf(qq.x, kk.x, dot);
+            dot = fmaf(qq.y, kk.y, dot);
+            dot = fmaf(qq.z, kk.z, dot);
+            dot = fmaf(qq.w, kk.w, dot);
+        }
+        s = dot * 0.125f;
+    }
+    const float mx = warp_max(s);
+    const float e = lane < n ? expf(s - mx) : 0.f;
+    const float sum = warp_sum(e);
+    const float wgt = e * (1.0f / sum);
+    float o0 = 0.f, o1 = 0.f;
+    for (int p = 0; p < n; ++p) {
+        const float wp = __shfl_sync(0xffffffffu, wgt, p);
+        const float2 vv = reinterpret_cast<const float2 *>(vb + (size_t)p * kHidden)[lane];
+        o0 = fmaf(wp, vv.x, o0);
+        o1 = fmaf(wp, vv.y, o1);
+    }
+    reinterpret_cast<float2 *>(out + (size_t)r * kHidden + hd * kHeadDim)[lane] = make_float2(o0, o1);
+}
+
+// --------------------------------------------------------------------------- embeddings
+
+__device__ __forceinline__ float deq_elem(const QMat &m, int row, int col) {
+    const int nb = m.cols >> 5;
+    const size_t blk = (size_t)(row >> 2) * nb + (col >> 5);
+    const float d = __half2float(m.sc[blk * 4 + (row & 3)]);
+    return d * (float)m.qs[blk * 128 + (row & 3) * 32 + (col & 31)];
+}
+
+
+
+// x[r] = deq(wte[row[0]]) + sum_ch deq(aemb[ch][row[ch+1]]) over valid codes (llm.cpp:148-157)
+__global__ void k_embed_rows(const EmbedTables t, const int *__restrict__ rows17, int R, float *__restrict__ x) {
+    const int r = blockIdx.x;
+    if (r >= R) return;
+    const int *row = rows17 + (size_t)r * (kNVq + 1);
+    for (int c = threadIdx.x; c < kHidden; c += blockDim.x) {
+        float v = deq_elem(t.wte, row[0], c);
+        for (int ch = 0; ch < kNVq; ++ch) {
+            const int code = row[ch + 1];
+            if (code == kAudioPad || code < 0 || code >= kCodebook) continue;
+            v = __fadd_rn(v, deq_elem(t.aemb[ch], code, c));
+        }
+        x[(size_t)r * kHidden + c] = v;
+    }
+}
+
+// Global-step input from the codes the local decoder used: row = [9, used codes...]
+__global__ void k_embed_frame(const EmbedTables t, const int *__restrict__ used, int R, float *__restrict__ x) {
+    const int r = blockIdx.x;
+    if (r >= R) return;
+    for (int c = threadIdx.x; c < kHidden; c += blockDim.x) {
+        float v = deq_elem(t.wte, kSlotToken, c);
+        for (int ch = 0; ch < kNVq; ++ch) {
+            const int code = used[r * kNVq + ch];
+            if (code == kAudioPad || code < 0 || code >= kCodebook) continue;
+            v = __fadd_rn(v, deq_elem(t.aemb[ch], code, c));
+        }
+        x[(size_t)r * kHidden + c] = v;
+    }
+}
+
+// lx[r] = deq(wte[row]) (local step 1 input: the slot token row, llm.cpp:682)
+__global__ void k_lookup_rows(const QMat m, int row, int R, float *__restrict__ x) {
+    const int r = blockIdx.x;
+    for (int c = threadIdx.x; c < kHidden; c += blockDim.x) x[(size_t)r * kHidden + c] = deq_elem(m, row, c);
+}
+
+// --------------------------------------------------------------------------- LayerNorm / commit
+
+// out[r] = LN(x[r]) for rows whose commit flag is set (all rows when commit is null);
+// also copies the result to out2[r] when given.
+__global__ void k_layernorm_rows(const float *__restrict__ x, int R, const float *__restrict__ w,
+                                 const float *__restrict__ b, float *__restrict__ out, const int *__restrict__ out_index,
+                                 const int *__restrict__ commit) {
+    __shared__ float xs[kHidden];
+    const int r = blockIdx.x;
+    if (r >= R) return;
+    if (commit && !commit[r]) return;
+    for (int c = threadIdx.x; c < kHidden; c += blockDim.x) xs[c] = x[(size_t)r * kHidden + c];
+    __syncthreads();
+    if (threadIdx.x < 32) warp_layernorm(xs, w, b);
+    __syncthreads();
+    const int dst = out_index ? out_index[r] : r;
+    for (int c = threadIdx.x; c < kHidden; c += blockDim.x) out[(size_t)dst * kHidden + c] = xs[c];
+}
+
+// gather rows: dst[r] = src[index[r]]
+__global__ void k_gather_rows(const float *__restrict__ src, const int *__restrict__ index, int R, float *__restrict__ dst) {
+    const int r = blockIdx.x;
+    for (int c = threadIdx.x; c < kHidden; c += blockDim.x) dst[(size_t)r * kHidden + c] = src[(size_t)index[r] * kHidden + c];
+}
+
+// --------------------------------------------------------------------------- end gate
+
+
+
+// AVX2 horizontal sum tree of the reference (gemv_avx2.cpp:24-31)
+__device__ __forceinline__ float hsum8(const float *v) {
+    const float s0 = __fadd_rn(v[0], v[4]), s1 = __fadd_rn(v[1], v[5]);
+    const float s2 = __fadd_rn(v[2], v[6]), s3 = __fadd_rn(v[3], v[7]);
+    return __fadd_rn(__fadd_rn(s0, s2), __fadd_rn(s1, s3));
+}
+
+// W8A8 two-row gate on LN(lx) (llm.cpp:274-315, quant.cpp:28-54, gemv_avx2.cpp:105-121), in
+// the reference's exact arithmetic order; sets active[r] = 0 when generation ends.
+__global__ void __launch_bounds__(256) k_gate(const float *__restrict__ lx, int R, const float *__restrict__ ln_w,
+                                              const float *__restrict__ ln_b, const QMat wte,
+                                              const int *__restrict__ frame_idx, const FrameCtl *__restrict__ ctl,
+                                              int *__restrict__ active, float *__restrict__ gate_out) {
+    __shared__ float xs[kHidden];
+    __shared__ int8_t qa[kHidden];
+    __shared__ float as[kHidden / 32];
+    __shared__ float pair[2];
+    const int r = blockIdx.x;
+    for (int c = threadIdx.x; c < kHidden; c += blockDim.x) xs[c] = lx[(size_t)r * kHidden + c];
+    __syncthreads();
+    if (threadIdx.x < 32) warp_layernorm(xs, ln_w, ln_b);
+    __syncthreads();
+    if (threadIdx.x < kHidden / 32) {
+        const int b = threadIdx.x;
+        float amax = 0.f;
+        for (int i = 0; i < 32; ++i) {
+            const float v = fabsf(xs[b * 32 + i]);
+            amax = (amax < v) ? v : amax;
+        }
+        const float d = __fdiv_rn(amax, 127.0f);
+        const float id = d > 0.f ? __fdiv_rn(1.0f, d) : 0.f;
+        as[b] = d;
+        for (int i = 0; i < 32; ++i) {
+            int q = __float2int_rn(__fmul_rn(xs[b * 32 + i], id));
+            q = q < -127 ? -127 : (q > 127 ? 127 : q);
+            qa[b * 32 + i] = (int8_t)q;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x < 2) {
+        const int row = threadIdx.x == 0 ? kEndToken : kSlotToken;
+        const int nb = kHidden / 32;
+        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int b = 0; b < nb; ++b) {
+            const size_t blk = (size_t)(row >> 2) * nb + b;
+            const float dw = __half2float(wte.sc[blk * 4 + (row & 3)]);
+            const int8_t *qs = wte.qs + blk * 128 + (row & 3) * 32;
+            const float s = __fmul_rn(dw, as[b]);
+            for (int j = 0; j < 8; ++j) {
+                int p = 0;
+                for (int i = 4 * j; i < 4 * j + 4; ++i) p += (int)qs[i] * (int)qa[b * 32 + i];
+                acc[j] = fmaf((float)p, s, acc[j]);
+            }
+        }
+        pair[threadIdx.x] = hsum8(acc);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const float l_end = pair[0], l_slot = pair[1];
+        if (gate_out) {
+            gate_out[2 * r] = l_end;
+            gate_out[2 * r + 1] = l_slot;
+        }
+        const bool stop = frame_idx[r] >= ctl->min_frames && ctl->end_greedy && (l_end > l_slot);
+        active[r] = stop ? 0 : 1;
+    }
+}
+
+// --------------------------------------------------------------------------- sampler
+
+// Greedy code choice with the reference's repetition penalty (sampler.cpp:9-28): the penalty
+// is applied once per earlier occurrence of the code on this channel, then the first index
+// of the maximum wins.  Then records the used code (forced or predicted), counts it, and
+// writes the next local-decoder input deq(aemb[ch][used]) (llm.cpp:686-698).
+__global__ void __launch_bounds__(256) k_sample_greedy(const float *__restrict__ logits, int ld_logits, int ch,
+                                                       const int *__restrict__ row_slot, int R,
+                                                       uint16_t *__restrict__ counts, const FrameCtl *__restrict__ ctl,
+                                                       const int *__restrict__ forced, const int *__restrict__ active,
+                                                       int *__restrict__ codes_out, int *__restrict__ used_out,
+                                                       const QMat aemb, float *__restrict__ next_x) {
+    __shared__ float bv[8];
+    __shared__ int bi[8];
+    __shared__ int s_used;
+    const int r = blockIdx.x;
+    const int slot = row_slot[r];
+    const float *lg = logits + (size_t)r * ld_logits;
+    uint16_t *cnt = counts + ((size_t)slot * kNVq + ch) * kCodebook;
+    const float p = ctl->rep_penalty;
+    float best = -INFINITY;
+    int besti = 0x7fffffff;
+    for (int t = threadIdx.x; t < kCodebook; t += blockDim.x) {
+        float v = lg[t];
+        if (p != 1.0f) {
+            const int c = cnt[t];
+            for (int j = 0; j < c; ++j) v = v < 0.f ? __fmul_rn(v, p) : __fdiv_rn(v, p);
+        }
+        if (v > best || (v == best && t < besti)) { best = v; besti = t; }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, besti, o);
+        if (ov > best || (ov == best && oi < besti)) { best = ov; besti = oi; }
+    }
+    const int warp = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) { bv[warp] = best; bi[warp] = besti; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+            if (bv[w] > best || (bv[w] == best && bi[w] < besti)) { best = bv[w]; besti = bi[w]; }
+        const int pred = besti;
+        const int used = ctl->has_forced ? forced[r * kNVq + ch] : pred;
+        codes_out[r * kNVq + ch] = pred;
+        used_out[r * kNVq + ch] = used;
+        if (active[r] && used >= 0 && used < kCodebook) cnt[used] = (uint16_t)(cnt[used] + 1);
+        s_used = used;
+    }
+    __syncthreads();
+    if (next_x) {
+        const int used = s_used;
+        for (int c = threadIdx.x; c < kHidden; c += blockDim.x)
+            next_x[(size_t)r * kHidden + c] = (used >= 0 && used < kCodebook) ? deq_elem(aemb, used, c) : 0.f;
+    }
+}
+
+// scatter page-table updates: upd = [count][slot, index, page] x count;
+// table[slot * pps + index] = page
+__global__ void k_page_updates(const int *__restrict__ upd, int *__restrict__ table, int pps) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < upd[0]) table[(size_t)upd[1 + 3 * i] * pps + upd[2 + 3 * i]] = upd[3 + 3 * i];
+}
+
+}  // namespace mossgpu

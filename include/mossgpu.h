@@ -1,0 +1,112 @@
+/*
+ * mossgpu.h -- C ABI of the B200 engine for MOSS-TTS-Nano's per-frame LLM step.
+ *
+ * Drop-in boundary: these entry points replace the single-stream C++ class
+ * moss::LlmModel (reference csrc/include/moss/llm.h:39-158, csrc/src/llm.cpp) with a
+ * batched, device-resident engine.  A thin C++ shim with LlmModel's method names
+ * (dsh-moss-tts_b200/csrc/llm_gpu.h) maps the reference's calls onto them, so the
+ * reference's TtsEngine (engine.cpp) and Runtime (runtime.cpp) keep their signatures.
+ *
+ * Conventions (the reference's capi.cpp:16-23,109 convention): every int-returning call
+ * returns 0 on success and non-zero on failure; the message is kept per engine and read
+ * with mossgpu_last_error().  No call throws across the ABI.  All pointers are host
+ * pointers unless a name says otherwise; sizes are element counts.
+ *
+ * Streams: one "stream" is one utterance's LLM state (global KV, last hidden, local
+ * decoder state, repetition-penalty history).  mossgpu_step() advances any set of open
+ * streams by one audio frame in one batched pass.
+ */
+#ifndef MOSSGPU_H
+#define MOSSGPU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct mossgpu_engine mossgpu_engine;
+
+/* Mirrors moss::SampleParams (reference csrc/include/moss/sampler.h:8-22). */
+typedef struct {
+    int greedy;                /* 1: argmax (after the repetition penalty) */
+    float temperature;         /* stochastic path only */
+    int top_k;                 /* stochastic path only; 1 == greedy */
+    float top_p;               /* stochastic path only */
+    float repetition_penalty;  /* applied once per earlier occurrence (sampler.cpp:14-21) */
+    int end_greedy;            /* 1: stop iff logit(end=7) > logit(slot=9) (llm.cpp:30-35) */
+    int min_frames;            /* no stop before this frame index */
+    int greedy_frames;         /* frames below this index are greedy */
+} mossgpu_sample_params;
+
+/* Engine lifetime.  Replaces LlmModel(threads) + LlmModel::load (llm.cpp:42-110): parses
+ * the .moss file (weights.cpp:27-126 semantics), uploads it to device `device_id`,
+ * repacks every Q8_0_4X4 matrix into 16-byte-aligned quant/scale planes, and allocates the
+ * paged fp16 KV cache.  max_ctx caps positions per stream (reference kMaxCtx, llm.h:28);
+ * kv_pages = 0 sizes the pool for max_streams * max_ctx positions.  Returns NULL on
+ * failure with the reason in err (may be NULL). */
+mossgpu_engine *mossgpu_create(const char *weights_path, int device_id, int max_streams, int max_ctx,
+                               int kv_pages, char *err, int errlen);
+void mossgpu_destroy(mossgpu_engine *e);
+const char *mossgpu_last_error(mossgpu_engine *e);
+const char *mossgpu_version(void);
+
+/* Run all work on the caller's cudaStream_t (passed as void*); NULL = the engine's own. */
+int mossgpu_set_cuda_stream(mossgpu_engine *e, void *cuda_stream);
+
+/* Stream slots.  open = a fresh LlmModel state (reset(), llm.cpp:112). */
+int mossgpu_stream_open(mossgpu_engine *e, int *stream_id);
+int mossgpu_stream_close(mossgpu_engine *e, int stream_id);
+int mossgpu_stream_reset(mossgpu_engine *e, int stream_id);
+int mossgpu_stream_position(mossgpu_engine *e, int stream_id, int *position);
+
+/* LlmModel::prefill(rows, start) (llm.cpp:327-401): rows[m][17] = [text_id, code0..15].
+ * Writes the KV for positions start..start+m-1 and leaves the last row's ln_f output as
+ * the stream's hidden state; position becomes start + m.  Computes in A16 (fp32
+ * activations x int8 weights), the reference's MOSS_A16=all prefill mode. */
+int mossgpu_prefill(mossgpu_engine *e, int stream_id, const int32_t *rows, int m, int start);
+/* Same with the token embeddings given directly, x[m][768] fp32. */
+int mossgpu_prefill_embeds(mossgpu_engine *e, int stream_id, const float *x, int m, int start);
+
+/* Start a generate() call on a stream (llm.cpp:637-641): clears the per-channel code
+ * history and sets the frame counter to 0. */
+int mossgpu_generate_begin(mossgpu_engine *e, int stream_id, uint64_t seed);
+
+/* One frame of LlmModel::generate (llm.cpp:643-712) for n streams at once:
+ * local decoder from the stream's hidden state, the W8A8 end gate, 16 codes (greedy with
+ * repetition penalty), then -- when run_global != 0 -- the 12-layer global step on
+ * [9, codes] that appends one KV position and refreshes the hidden state.
+ *   forced     [n][16] teacher-forcing codes (llm.cpp:694,706) or NULL
+ *   out_codes  [n][16] the model's own predictions
+ *   out_stop   [n]     1 when the gate ended the stream this frame (its codes are void and
+ *                      its state is unchanged, as the reference's `break`)
+ *   out_logits [n][16][1024] audio logits before sampling, or NULL
+ *   out_gate   [n][2]  (logit_end, logit_slot), or NULL */
+int mossgpu_step(mossgpu_engine *e, const int32_t *stream_ids, int n, const mossgpu_sample_params *params,
+                 const int32_t *forced, int32_t *out_codes, uint8_t *out_stop, float *out_logits, float *out_gate,
+                 int run_global);
+
+/* The 12-layer global step alone with the input embedding given (llm.cpp:248-255 with
+ * x_ = x): x[n][768] fp32; hidden_out[n][768] or NULL.  Appends one KV position. */
+int mossgpu_global_step_embed(mossgpu_engine *e, const int32_t *stream_ids, int n, const float *x, float *hidden_out);
+
+/* State access (llm.cpp:588-632 load_state semantics and debugging):
+ * set_state writes K,V fp32 [12][n_pos][768] (stored as fp16 pages) and hidden[768].
+ * get_kv reads layer `layer`, positions p0..p0+n-1, back as fp32 [n][768]. */
+int mossgpu_set_state(mossgpu_engine *e, int stream_id, const float *k, const float *v, int n_pos,
+                      const float *hidden);
+int mossgpu_get_kv(mossgpu_engine *e, int stream_id, int layer, int p0, int n, float *k, float *v);
+int mossgpu_get_hidden(mossgpu_engine *e, int stream_id, float *hidden);
+
+/* Read back one repacked matrix (by .moss tensor name) as the original Q8_0_4X4 bytes,
+ * rows/4 * cols/32 * 136 bytes, to prove the device repack is a byte permutation. */
+int mossgpu_debug_matrix_bytes(mossgpu_engine *e, const char *name, uint8_t *out, size_t out_bytes);
+
+/* Kernel launches issued by the last mossgpu_step / mossgpu_global_step_embed call. */
+int mossgpu_last_launch_count(mossgpu_engine *e);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
