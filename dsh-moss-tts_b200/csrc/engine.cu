@@ -230,6 +230,9 @@ void Engine::allocate_state() {
     for (int p = n_pages_ - 1; p >= 0; --p) free_pages_.push_back(p);
 
     set_smem_limits();
+    // the set-up copies and memsets above ran on the legacy stream; finish them before any
+    // work is issued on the engine's (non-blocking) stream
+    CK(cudaDeviceSynchronize());
 }
 
 // ------------------------------------------------------------------ GEMV launch
@@ -422,24 +425,19 @@ void Engine::release_pages(Slot &s) {
 // Page-table entries reach the device through the control block (no allocation): at most
 // r_max_ entries per pass, applied by k_page_updates before the pass's kernels.
 void Engine::upload_page_updates(const std::vector<int> &updates) {
-    size_t done = 0;
     const size_t n = updates.size() / 3;
-    if (n == 0) return;
     int *h = h_ctl_ + off_pages();
-    do {
+    for (size_t done = 0; done < n;) {
         const size_t m = std::min(n - done, size_t(r_max_));
         h[0] = int(m);
         std::memcpy(h + 1, updates.data() + 3 * done, m * 3 * sizeof(int));
+        CK(cudaMemcpyAsync(d_ctl_ + off_pages(), h, (1 + 3 * m) * sizeof(int), cudaMemcpyHostToDevice, stream_));
+        k_page_updates<<<unsigned((m + 127) / 128), 128, 0, stream_>>>(d_ctl_ + off_pages(), page_table_,
+                                                                      pages_per_stream_);
+        CK(cudaStreamSynchronize(stream_));  // the pinned staging is reused by the next pass
         done += m;
-        if (done < n || n == 0) {
-            // flush now: more entries follow, or a pass that only needs the count reset
-            CK(cudaMemcpyAsync(d_ctl_ + off_pages(), h, (1 + 3 * m) * sizeof(int), cudaMemcpyHostToDevice, stream_));
-            if (m) k_page_updates<<<unsigned((m + 127) / 128), 128, 0, stream_>>>(d_ctl_ + off_pages(), page_table_,
-                                                                                pages_per_stream_);
-            CK(cudaStreamSynchronize(stream_));
-            h[0] = 0;
-        }
-    } while (done < n);
+    }
+    h[0] = 0;
 }
 
 // ------------------------------------------------------------------ public API
@@ -719,13 +717,18 @@ void Engine::set_state(int sid, const float *k, const float *v, int n_pos, const
     int *dp = nullptr;
     CK(cudaMalloc(&d, nel * sizeof(float)));
     CK(cudaMalloc(&dp, s.pages.size() * sizeof(int)));
-    CK(cudaMemcpy(dp, s.pages.data(), s.pages.size() * sizeof(int), cudaMemcpyHostToDevice));
+    // every copy goes through the engine's stream: a blocking cudaMemcpy from pageable memory
+    // may return before its DMA lands and is not ordered with a non-blocking stream
+    CK(cudaMemcpyAsync(dp, s.pages.data(), s.pages.size() * sizeof(int), cudaMemcpyHostToDevice, stream_));
     for (int kvsel = 0; kvsel < 2; ++kvsel) {
-        CK(cudaMemcpy(d, kvsel ? v : k, nel * sizeof(float), cudaMemcpyHostToDevice));
+        CK(cudaMemcpyAsync(d, kvsel ? v : k, nel * sizeof(float), cudaMemcpyHostToDevice, stream_));
         k_kv_scatter<<<unsigned((nel + 255) / 256), 256, 0, stream_>>>(d, n_pos, 0, dp, kv_, n_pages_, kvsel);
         CK(cudaStreamSynchronize(stream_));
     }
-    if (hidden) CK(cudaMemcpy(hidden_ + size_t(sid) * kHidden, hidden, kHidden * sizeof(float), cudaMemcpyHostToDevice));
+    if (hidden)
+        CK(cudaMemcpyAsync(hidden_ + size_t(sid) * kHidden, hidden, kHidden * sizeof(float), cudaMemcpyHostToDevice,
+                           stream_));
+    CK(cudaStreamSynchronize(stream_));
     CK(cudaFree(d));
     CK(cudaFree(dp));
     s.pos = n_pos;
@@ -740,14 +743,14 @@ void Engine::get_kv(int sid, int layer, int p0, int n, float *k, float *v) {
     int *dp = nullptr;
     CK(cudaMalloc(&d, size_t(n) * kHidden * sizeof(float)));
     CK(cudaMalloc(&dp, s.pages.size() * sizeof(int)));
-    CK(cudaMemcpy(dp, s.pages.data(), s.pages.size() * sizeof(int), cudaMemcpyHostToDevice));
+    CK(cudaMemcpyAsync(dp, s.pages.data(), s.pages.size() * sizeof(int), cudaMemcpyHostToDevice, stream_));
     for (int kvsel = 0; kvsel < 2; ++kvsel) {
         float *out = kvsel ? v : k;
         if (!out) continue;
         k_kv_gather<<<unsigned((size_t(n) * kHidden + 255) / 256), 256, 0, stream_>>>(kv_, n_pages_, layer, p0, n, dp,
                                                                                        kvsel, d);
+        CK(cudaMemcpyAsync(out, d, size_t(n) * kHidden * sizeof(float), cudaMemcpyDeviceToHost, stream_));
         CK(cudaStreamSynchronize(stream_));
-        CK(cudaMemcpy(out, d, size_t(n) * kHidden * sizeof(float), cudaMemcpyDeviceToHost));
     }
     CK(cudaFree(d));
     CK(cudaFree(dp));
@@ -755,8 +758,8 @@ void Engine::get_kv(int sid, int layer, int p0, int n, float *k, float *v) {
 
 void Engine::get_hidden(int sid, float *out) {
     check_slot(sid);
+    CK(cudaMemcpyAsync(out, hidden_ + size_t(sid) * kHidden, kHidden * sizeof(float), cudaMemcpyDeviceToHost, stream_));
     CK(cudaStreamSynchronize(stream_));
-    CK(cudaMemcpy(out, hidden_ + size_t(sid) * kHidden, kHidden * sizeof(float), cudaMemcpyDeviceToHost));
 }
 
 void Engine::debug_matrix_bytes(const std::string &name, uint8_t *out, size_t out_bytes) {

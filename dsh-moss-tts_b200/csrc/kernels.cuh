@@ -350,10 +350,18 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnArgs a) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) o[j] = 0.f;
         const int *pt = a.page_table + (size_t)slot * a.pages_per_stream;
-        for (int p = p0 + ps; p < p1; p += 4) {
-            const __half *base = a.kv + (size_t)pt[p / kPage] * kPageHalfs + ((size_t)hd * kPage + p % kPage) * kHeadDim + ds * 8;
-            const int4 kr = *reinterpret_cast<const int4 *>(base);
-            const int4 vr = *reinterpret_cast<const int4 *>(base + kHeads * kPage * kHeadDim);
+        // every lane runs the same trip count (the shuffles below need the whole warp);
+        // lanes whose position is past the chunk end load nothing and skip the update
+        for (int pb = p0; pb < p1; pb += 4) {
+            const int p = pb + ps;
+            const bool valid = p < p1;
+            int4 kr = make_int4(0, 0, 0, 0), vr = make_int4(0, 0, 0, 0);
+            if (valid) {
+                const __half *base = a.kv + (size_t)pt[p / kPage] * kPageHalfs +
+                                     ((size_t)hd * kPage + p % kPage) * kHeadDim + ds * 8;
+                kr = *reinterpret_cast<const int4 *>(base);
+                vr = *reinterpret_cast<const int4 *>(base + kHeads * kPage * kHeadDim);
+            }
             const __half2 *kh = reinterpret_cast<const __half2 *>(&kr);
             float s = 0.f;
 #pragma unroll
@@ -365,6 +373,7 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnArgs a) {
             s += __shfl_xor_sync(0xffffffffu, s, 1);
             s += __shfl_xor_sync(0xffffffffu, s, 2);
             s += __shfl_xor_sync(0xffffffffu, s, 4);
+            if (!valid) continue;
             const float mn = fmaxf(m, s);
             const float corr = __expf(m - mn);
             const float pw = __expf(s - mn);
