@@ -36,7 +36,8 @@ EXPORTS = [
     "mossgpu_stream_open", "mossgpu_stream_close", "mossgpu_stream_reset", "mossgpu_stream_position",
     "mossgpu_prefill", "mossgpu_prefill_embeds", "mossgpu_generate_begin", "mossgpu_step",
     "mossgpu_global_step_embed", "mossgpu_set_state", "mossgpu_get_kv", "mossgpu_get_hidden",
-    "mossgpu_debug_matrix_bytes", "mossgpu_last_launch_count",
+    "mossgpu_debug_matrix_bytes", "mossgpu_last_launch_count", "mossgpu_fill_state_random", "mossgpu_set_graphs",
+    "mossgpu_kernel_profile", "mossgpu_kernel_profile_read", "mossgpu_kernel_name", "mossgpu_step_frames",
 ]
 
 
@@ -100,6 +101,15 @@ def lib() -> C.CDLL:
         L.mossgpu_debug_matrix_bytes.argtypes = [C.c_void_p, C.c_char_p,
                                                  np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS"), C.c_size_t]
         L.mossgpu_last_launch_count.argtypes = [C.c_void_p]
+        L.mossgpu_fill_state_random.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_uint64]
+        L.mossgpu_step_frames.argtypes = [C.c_void_p, _i32, C.c_int, C.POINTER(SampleParams), C.c_int, C.c_void_p,
+                                          C.c_void_p]
+        L.mossgpu_set_graphs.argtypes = [C.c_void_p, C.c_int]
+        L.mossgpu_kernel_profile.argtypes = [C.c_void_p, C.c_int]
+        L.mossgpu_kernel_profile_read.argtypes = [C.c_void_p, _f32, np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS"),
+                                                  C.c_int, C.POINTER(C.c_int)]
+        L.mossgpu_kernel_name.restype = C.c_char_p
+        L.mossgpu_kernel_name.argtypes = [C.c_int]
         _LIB = L
         return L
 
@@ -174,6 +184,15 @@ class Engine:
                                           _ptr(gate), int(run_global)))
         return codes, stop.astype(bool), gate, logits
 
+    def step_frames(self, sids, params: SampleParams, n_frames: int, want_codes=True):
+        """n_frames free-running frames on the device.  Returns (codes[n_frames][n][16], frames_done[n])."""
+        sids = np.ascontiguousarray(sids, np.int32).reshape(-1)
+        codes = np.zeros((n_frames, sids.size, NVQ), np.int32) if want_codes else None
+        done = np.zeros(sids.size, np.int32)
+        self._check(self.lib.mossgpu_step_frames(self.h, sids, sids.size, C.byref(params), n_frames, _ptr(codes),
+                                                 _ptr(done)))
+        return codes, done
+
     def global_step_embed(self, sids, x, want_hidden=True):
         sids = np.ascontiguousarray(sids, np.int32).reshape(-1)
         x = np.ascontiguousarray(x, np.float32).reshape(sids.size, HIDDEN)
@@ -205,6 +224,23 @@ class Engine:
 
     def last_launch_count(self) -> int:
         return self.lib.mossgpu_last_launch_count(self.h)
+
+    def fill_state_random(self, sid: int, n_pos: int, seed: int = 0):
+        self._check(self.lib.mossgpu_fill_state_random(self.h, sid, n_pos, seed))
+
+    def set_graphs(self, enable: bool):
+        self._check(self.lib.mossgpu_set_graphs(self.h, int(enable)))
+
+    def kernel_profile(self, enable: bool):
+        self._check(self.lib.mossgpu_kernel_profile(self.h, int(enable)))
+
+    def kernel_profile_read(self) -> dict[str, tuple[float, int]]:
+        """{kernel class: (summed ms, launches)} since kernel_profile(True)."""
+        ms = np.zeros(64, np.float32)
+        n = np.zeros(64, np.int32)
+        k = C.c_int()
+        self._check(self.lib.mossgpu_kernel_profile_read(self.h, ms, n, 64, C.byref(k)))
+        return {self.lib.mossgpu_kernel_name(i).decode(): (float(ms[i]), int(n[i])) for i in range(k.value)}
 
 
 @dataclass

@@ -25,10 +25,13 @@ def stale() -> bool:
 
 def build(force: bool = False, verbose: bool = False) -> Path:
     if force or stale():
-        cmd = [NVCC, *FLAGS, "-o", str(LIB), *[str(CSRC / s) for s in SOURCES]]
+        tmp = LIB.with_name(f".libmossgpu.{os.getpid()}.so")
+        cmd = [NVCC, *FLAGS, "-o", str(tmp), *[str(CSRC / s) for s in SOURCES]]
         r = subprocess.run(cmd, cwd=CSRC, capture_output=True, text=True)
         if r.returncode != 0:
+            tmp.unlink(missing_ok=True)
             raise RuntimeError(f"nvcc failed ({r.returncode}):\n{r.stdout}\n{r.stderr}")
+        os.replace(tmp, LIB)  # atomic: concurrent builders never expose a half-written library
         if verbose:
             print(r.stdout + r.stderr)
     return LIB

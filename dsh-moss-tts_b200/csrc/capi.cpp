@@ -124,6 +124,17 @@ int mossgpu_step(mossgpu_engine *e, const int32_t *stream_ids, int n, const moss
     });
 }
 
+int mossgpu_step_frames(mossgpu_engine *e, const int32_t *stream_ids, int n, const mossgpu_sample_params *params,
+                        int n_frames, int32_t *out_codes, int32_t *out_frames_done) {
+    return guarded(e, [&](mossgpu::Engine &g) {
+        if (!stream_ids || !params) throw std::runtime_error("stream_ids and params are required");
+        mossgpu::SampleParamsC p{params->greedy,           params->temperature, params->top_k,
+                                 params->top_p,            params->repetition_penalty, params->end_greedy,
+                                 params->min_frames,       params->greedy_frames};
+        g.step_frames(stream_ids, n, p, n_frames, out_codes, out_frames_done);
+    });
+}
+
 int mossgpu_global_step_embed(mossgpu_engine *e, const int32_t *stream_ids, int n, const float *x, float *hidden_out) {
     return guarded(e, [&](mossgpu::Engine &g) {
         if (!stream_ids || !x) throw std::runtime_error("stream_ids and x are required");
@@ -158,5 +169,23 @@ int mossgpu_debug_matrix_bytes(mossgpu_engine *e, const char *name, uint8_t *out
 }
 
 int mossgpu_last_launch_count(mossgpu_engine *e) { return (e && e->eng) ? e->eng->last_launches() : -1; }
+
+int mossgpu_fill_state_random(mossgpu_engine *e, int stream_id, int n_pos, uint64_t seed) {
+    return guarded(e, [&](mossgpu::Engine &g) { g.fill_state_random(stream_id, n_pos, seed); });
+}
+
+int mossgpu_set_graphs(mossgpu_engine *e, int enable) {
+    return guarded(e, [&](mossgpu::Engine &g) { g.set_use_graphs(enable != 0); });
+}
+
+int mossgpu_kernel_profile(mossgpu_engine *e, int enable) {
+    return guarded(e, [&](mossgpu::Engine &g) { g.set_kernel_timing(enable != 0); });
+}
+
+int mossgpu_kernel_profile_read(mossgpu_engine *e, float *total_ms, int *launches, int max_kinds, int *n_kinds) {
+    return guarded(e, [&](mossgpu::Engine &g) { g.read_kernel_timing(total_ms, launches, max_kinds, n_kinds); });
+}
+
+const char *mossgpu_kernel_name(int kind) { return mossgpu::kernel_kind_name(kind); }
 
 }  // extern "C"

@@ -70,6 +70,10 @@ Engine::Engine(const std::string &path, int device, int max_streams, int max_ctx
 Engine::~Engine() {
     cudaSetDevice(device_);
     if (stream_) cudaStreamSynchronize(stream_);
+    for (auto &kv : graphs_) {
+        if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+        for (cudaEvent_t ev : kv.second.events) cudaEventDestroy(ev);
+    }
     for (void *p : owned_) cudaFree(p);
     for (void *p : pinned_) cudaFreeHost(p);
     if (own_stream_) cudaStreamDestroy(own_stream_);
@@ -197,9 +201,11 @@ void Engine::allocate_state() {
     used_ = dalloc<int>(R * kNVq, owned_);
     gate_ = dalloc<float>(R * 2, owned_);
     rows17_ = dalloc<int>(R * (kNVq + 1), owned_);
+    codes_hist_ = dalloc<int>(size_t(kMaxFramesPerCall) * max_streams_ * kNVq, owned_);
 
     // control block: [slot R][pos R][frame R][forced 16R][page updates 1 + 3R][FrameCtl]
-    ctl_ints_ = off_fctl() + int(sizeof(FrameCtl) / sizeof(int)) + 4;
+    static_assert(sizeof(FrameCtl) <= 8 * sizeof(int), "FrameCtl must fit its 8 reserved ints");
+    ctl_ints_ = off_fslot() + 4;
     d_ctl_ = dalloc<int>(ctl_ints_, owned_);
     void *hp = nullptr;
     CK(cudaMallocHost(&hp, size_t(ctl_ints_) * sizeof(int)));
@@ -330,11 +336,12 @@ void Engine::block(const Layer &L, int li, bool local, int R, const int *row_slo
         a.pages_per_stream = pages_per_stream_;
     }
     launch_gemv<PRO_LN, EPI_QKV>(a, stream_);
-    ++launches_;
+    mark(local ? KK_QKV_L : KK_QKV_G);
     // attention
     if (local) {
         const int warps = R * kHeads;
         k_attn_local<<<(warps + 11) / 12, 384, 0, stream_>>>(q_, lkv_, row_slot, lpos, R, attn_);
+        mark(KK_ATTN_LOCAL);
     } else {
         AttnArgs t{};
         t.q = q_;
@@ -349,8 +356,8 @@ void Engine::block(const Layer &L, int li, bool local, int R, const int *row_slo
         t.counter = counter_;
         t.out = attn_;
         k_attn_decode<<<kAttnGrid, 256, 0, stream_>>>(t);
+        mark(KK_ATTN_DECODE);
     }
-    ++launches_;
     // proj + residual
     GemvArgs p{};
     p.nrows = R;
@@ -361,7 +368,7 @@ void Engine::block(const Layer &L, int li, bool local, int R, const int *row_slo
     p.out = x;
     p.ldo = kHidden;
     launch_gemv<PRO_NONE, EPI_RESID>(p, stream_);
-    ++launches_;
+    mark(local ? KK_PROJ_L : KK_PROJ_G);
     // LN2 -> fc_in + gelu
     GemvArgs f{};
     f.nrows = R;
@@ -374,7 +381,7 @@ void Engine::block(const Layer &L, int li, bool local, int R, const int *row_slo
     f.out = mlp_;
     f.ldo = kFF;
     launch_gemv<PRO_LN, EPI_GELU>(f, stream_);
-    ++launches_;
+    mark(local ? KK_FCIN_L : KK_FCIN_G);
     // fc_out + residual
     GemvArgs o{};
     o.nrows = R;
@@ -385,13 +392,13 @@ void Engine::block(const Layer &L, int li, bool local, int R, const int *row_slo
     o.out = x;
     o.ldo = kHidden;
     launch_gemv<PRO_NONE, EPI_RESID>(o, stream_);
-    ++launches_;
+    mark(local ? KK_FCOUT_L : KK_FCOUT_G);
 }
 
 // 12 global layers over rows already embedded in x_ (row_pos = positions being written).
 void Engine::global_layers(int R, const int *row_slot, const int *row_pos) {
     k_attn_plan<<<1, 32, 0, stream_>>>(row_pos, R, kAttnItems, plan_);
-    ++launches_;
+    mark(KK_PLAN);
     for (int li = 0; li < kLayers; ++li) block(global_[li], li, false, R, row_slot, row_pos, 0, x_);
 }
 
@@ -555,8 +562,10 @@ void Engine::step(const int32_t *sids, int n, const SampleParamsC &p, const int3
         slot[r] = sids[r];
         pos[r] = s.pos;
         frame[r] = s.frame;
+        h_ctl_[off_active_in() + r] = 1;
         if (forced) std::memcpy(frc + r * kNVq, forced + size_t(r) * kNVq, kNVq * sizeof(int));
     }
+    h_ctl_[off_fslot()] = 0;
     fc->min_frames = p.min_frames;
     fc->greedy_frames = p.greedy_frames;
     fc->rep_penalty = p.repetition_penalty;
@@ -566,52 +575,7 @@ void Engine::step(const int32_t *sids, int n, const SampleParamsC &p, const int3
     h_ctl_[off_pages()] = int(upd.size() / 3);
     std::memcpy(h_ctl_ + off_pages() + 1, upd.data(), upd.size() * sizeof(int));
     CK(cudaMemcpyAsync(d_ctl_, h_ctl_, size_t(ctl_ints_) * sizeof(int), cudaMemcpyHostToDevice, stream_));
-    k_page_updates<<<unsigned((R + 127) / 128), 128, 0, stream_>>>(d_ctl_ + off_pages(), page_table_, pages_per_stream_);
-    ++launches_;
-    const int *d_slot = d_ctl_ + off_slot(), *d_pos = d_ctl_ + off_pos(), *d_frame = d_ctl_ + off_frame();
-    const int *d_forced = d_ctl_ + off_forced();
-    const FrameCtl *d_fc = reinterpret_cast<const FrameCtl *>(d_ctl_ + off_fctl());
-
-    // ---- local decoder: 17 steps (llm.cpp:648-698)
-    k_gather_rows<<<R, 256, 0, stream_>>>(hidden_, d_slot, R, lx_);
-    ++launches_;
-    for (int ls = 0; ls < kLocalLen; ++ls) {
-        if (ls == 1) {
-            k_lookup_rows<<<R, 256, 0, stream_>>>(qm(wte_), kSlotToken, R, lx_);
-            ++launches_;
-        }
-        block(local_, 0, true, R, d_slot, nullptr, ls, lx_);
-        if (ls == 0) {
-            k_gate<<<R, 256, 0, stream_>>>(lx_, R, llnf_w_, llnf_b_, qm(wte_), d_frame, d_fc, active_, gate_);
-            ++launches_;
-        } else {
-            const int ch = ls - 1;
-            GemvArgs h{};
-            h.nrows = R;
-            h.w = qm(aemb_[ch]);
-            h.x = lx_;
-            h.ldx = kHidden;
-            h.ln_w = llnf_w_;
-            h.ln_b = llnf_b_;
-            h.out = logits_ + size_t(ch) * kCodebook;
-            h.ldo = kNVq * kCodebook;
-            launch_gemv<PRO_LN, EPI_STORE>(h, stream_);
-            ++launches_;
-            k_sample_greedy<<<R, 256, 0, stream_>>>(logits_ + size_t(ch) * kCodebook, kNVq * kCodebook, ch, d_slot, R,
-                                                   counts_, d_fc, d_forced, active_, codes_, used_, qm(aemb_[ch]),
-                                                   ch + 1 < kNVq ? lx_ : nullptr);
-            ++launches_;
-        }
-    }
-    // ---- global step on [9, used codes] (llm.cpp:703-708)
-    if (run_global) {
-        k_embed_frame<<<R, 256, 0, stream_>>>(tables(), used_, R, x_);
-        ++launches_;
-        global_layers(R, d_slot, d_pos);
-        k_layernorm_rows<<<R, 256, 0, stream_>>>(x_, R, lnf_w_, lnf_b_, hidden_, d_slot, active_);
-        ++launches_;
-    }
-    CK(cudaGetLastError());
+    run_captured((uint64_t(1) << 40) | (uint64_t(run_global) << 32) | uint64_t(R), [&] { issue_frame(R, run_global); });
     // ---- outputs
     uint8_t *ho = h_out_;
     int *h_codes = reinterpret_cast<int *>(ho);
@@ -624,6 +588,7 @@ void Engine::step(const int32_t *sids, int n, const SampleParamsC &p, const int3
     if (out_logits)
         CK(cudaMemcpyAsync(h_logits, logits_, size_t(R) * kNVq * kCodebook * sizeof(float), cudaMemcpyDeviceToHost, stream_));
     CK(cudaStreamSynchronize(stream_));
+    accumulate_timing();
     for (int r = 0; r < R; ++r) {
         const bool act = h_active[r] != 0;
         if (out_codes) std::memcpy(out_codes + size_t(r) * kNVq, h_codes + size_t(r) * kNVq, kNVq * sizeof(int));
@@ -639,6 +604,71 @@ void Engine::step(const int32_t *sids, int n, const SampleParamsC &p, const int3
         }
     }
     if (out_logits) std::memcpy(out_logits, h_logits, size_t(R) * kNVq * kCodebook * sizeof(float));
+}
+
+// n_frames consecutive frames for n streams without a host round trip between frames: the
+// frame graph is replayed back to back and k_frame_commit advances positions, frame indices
+// and active flags on the device.  Pages for every position the call can write are
+// reserved up front.  out_codes [n_frames][n][16] (-1 after a stream stopped);
+// out_frames_done [n] = frames each stream produced.
+void Engine::step_frames(const int32_t *sids, int n, const SampleParamsC &p, int n_frames, int32_t *out_codes,
+                         int32_t *out_frames_done) {
+    if (n <= 0 || n_frames <= 0) return;
+    if (n > max_streams_) throw std::runtime_error("batch larger than max_streams");
+    if (n_frames > kMaxFramesPerCall) throw std::runtime_error("n_frames above the per-call limit");
+    if (!p.greedy && p.top_k != 1) throw std::runtime_error("stochastic sampling is not supported by this build (greedy only)");
+    if (!p.end_greedy) throw std::runtime_error("sampled end decision is not supported by this build (end_greedy only)");
+    std::vector<int> upd;
+    std::vector<char> seen(size_t(max_streams_), 0);
+    for (int r = 0; r < n; ++r) {
+        const int sid = sids[r];
+        check_slot(sid);
+        if (seen[size_t(sid)]) throw std::runtime_error("stream listed twice in one step");
+        seen[size_t(sid)] = 1;
+        ensure_pages(sid, slots_[size_t(sid)].pos + n_frames - 1, upd);
+    }
+    upload_page_updates(upd);
+    const int R = n;
+    for (int r = 0; r < R; ++r) {
+        const Slot &s = slots_[size_t(sids[r])];
+        h_ctl_[off_slot() + r] = sids[r];
+        h_ctl_[off_pos() + r] = s.pos;
+        h_ctl_[off_frame() + r] = s.frame;
+        h_ctl_[off_active_in() + r] = 1;
+    }
+    h_ctl_[off_pages()] = 0;
+    h_ctl_[off_fslot()] = 0;
+    FrameCtl *fc = reinterpret_cast<FrameCtl *>(h_ctl_ + off_fctl());
+    fc->min_frames = p.min_frames;
+    fc->greedy_frames = p.greedy_frames;
+    fc->rep_penalty = p.repetition_penalty;
+    fc->end_greedy = p.end_greedy;
+    fc->has_forced = 0;
+    CK(cudaMemcpyAsync(d_ctl_, h_ctl_, size_t(ctl_ints_) * sizeof(int), cudaMemcpyHostToDevice, stream_));
+    int total_launches = 0;
+    for (int f = 0; f < n_frames; ++f) {
+        run_captured((uint64_t(1) << 40) | (uint64_t(1) << 32) | uint64_t(R), [&] { issue_frame(R, true); });
+        total_launches += launches_;
+        if (timing_ && f + 1 < n_frames) {
+            CK(cudaStreamSynchronize(stream_));
+            accumulate_timing();
+        }
+    }
+    int *h_frames = reinterpret_cast<int *>(h_out_);
+    CK(cudaMemcpyAsync(h_frames, d_ctl_ + off_frame(), size_t(R) * sizeof(int), cudaMemcpyDeviceToHost, stream_));
+    if (out_codes)
+        CK(cudaMemcpyAsync(out_codes, codes_hist_, size_t(n_frames) * R * kNVq * sizeof(int), cudaMemcpyDeviceToHost,
+                           stream_));
+    CK(cudaStreamSynchronize(stream_));
+    accumulate_timing();
+    launches_ = total_launches;
+    for (int r = 0; r < R; ++r) {
+        Slot &s = slots_[size_t(sids[r])];
+        const int done = h_frames[r] - s.frame;
+        s.frame += done;
+        s.pos += done;
+        if (out_frames_done) out_frames_done[r] = done;
+    }
 }
 
 void Engine::global_step_embed(const int32_t *sids, int n, const float *x, float *hidden_out) {
@@ -658,10 +688,7 @@ void Engine::global_step_embed(const int32_t *sids, int n, const float *x, float
     }
     CK(cudaMemcpyAsync(d_ctl_, h_ctl_, size_t(2 * r_max_) * sizeof(int), cudaMemcpyHostToDevice, stream_));
     CK(cudaMemcpyAsync(x_, x, size_t(n) * kHidden * sizeof(float), cudaMemcpyHostToDevice, stream_));
-    global_layers(n, d_ctl_, d_ctl_ + r_max_);
-    k_layernorm_rows<<<n, 256, 0, stream_>>>(x_, n, lnf_w_, lnf_b_, hidden_, d_ctl_, nullptr);
-    ++launches_;
-    CK(cudaGetLastError());
+    run_captured((uint64_t(2) << 40) | uint64_t(n), [&] { issue_global_embed(n); });
     if (hidden_out) {
         float *h = reinterpret_cast<float *>(h_out_);
         k_gather_rows<<<n, 256, 0, stream_>>>(hidden_, d_ctl_, n, q_);
@@ -671,7 +698,162 @@ void Engine::global_step_embed(const int32_t *sids, int n, const float *x, float
     } else {
         CK(cudaStreamSynchronize(stream_));
     }
+    accumulate_timing();
     for (int r = 0; r < n; ++r) slots_[size_t(sids[r])].pos += 1;
+}
+
+// The launch sequence of one frame for R rows (llm.cpp:643-712); all per-call data comes
+// from the control block already copied to d_ctl_, so the sequence is graph-capturable.
+void Engine::issue_frame(int R, bool run_global) {
+    const int *d_slot = d_ctl_ + off_slot(), *d_pos = d_ctl_ + off_pos(), *d_frame = d_ctl_ + off_frame();
+    const int *d_forced = d_ctl_ + off_forced();
+    const FrameCtl *d_fc = reinterpret_cast<const FrameCtl *>(d_ctl_ + off_fctl());
+    k_page_updates<<<unsigned((R + 127) / 128), 128, 0, stream_>>>(d_ctl_ + off_pages(), page_table_, pages_per_stream_);
+    mark(KK_PAGES);
+    // ---- local decoder: 17 steps (llm.cpp:648-698)
+    k_gather_rows<<<R, 256, 0, stream_>>>(hidden_, d_slot, R, lx_);
+    mark(KK_GATHER);
+    for (int ls = 0; ls < kLocalLen; ++ls) {
+        if (ls == 1) {
+            k_lookup_rows<<<R, 256, 0, stream_>>>(qm(wte_), kSlotToken, R, lx_);
+            mark(KK_LOOKUP);
+        }
+        block(local_, 0, true, R, d_slot, nullptr, ls, lx_);
+        if (ls == 0) {
+            k_gate<<<R, 256, 0, stream_>>>(lx_, R, llnf_w_, llnf_b_, qm(wte_), d_frame, d_fc,
+                                           d_ctl_ + off_active_in(), active_, gate_);
+            mark(KK_GATE);
+        } else {
+            const int ch = ls - 1;
+            GemvArgs h{};
+            h.nrows = R;
+            h.w = qm(aemb_[ch]);
+            h.x = lx_;
+            h.ldx = kHidden;
+            h.ln_w = llnf_w_;
+            h.ln_b = llnf_b_;
+            h.out = logits_ + size_t(ch) * kCodebook;
+            h.ldo = kNVq * kCodebook;
+            launch_gemv<PRO_LN, EPI_STORE>(h, stream_);
+            mark(KK_HEADS);
+            k_sample_greedy<<<R, 256, 0, stream_>>>(logits_ + size_t(ch) * kCodebook, kNVq * kCodebook, ch, d_slot, R,
+                                                   counts_, d_fc, d_forced, active_, codes_, used_, qm(aemb_[ch]),
+                                                   ch + 1 < kNVq ? lx_ : nullptr);
+            mark(KK_SAMPLE);
+        }
+    }
+    // ---- global step on [9, used codes] (llm.cpp:703-708)
+    if (run_global) {
+        k_embed_frame<<<R, 256, 0, stream_>>>(tables(), used_, R, x_);
+        mark(KK_EMBED);
+        global_layers(R, d_slot, d_pos);
+        k_layernorm_rows<<<R, 256, 0, stream_>>>(x_, R, lnf_w_, lnf_b_, hidden_, d_slot, active_);
+        mark(KK_LNF);
+    }
+    k_frame_commit<<<1, 256, 0, stream_>>>(codes_, active_, R, run_global ? 1 : 0, d_ctl_ + off_pos(),
+                                           d_ctl_ + off_frame(), d_ctl_ + off_active_in(), d_ctl_ + off_fslot(),
+                                           kMaxFramesPerCall, codes_hist_);
+    mark(KK_COMMIT);
+}
+
+// 12 global layers + ln_f on embeddings already in x_ (llm.cpp:248-255).
+void Engine::issue_global_embed(int R) {
+    global_layers(R, d_ctl_ + off_slot(), d_ctl_ + off_pos());
+    k_layernorm_rows<<<R, 256, 0, stream_>>>(x_, R, lnf_w_, lnf_b_, hidden_, d_ctl_ + off_slot(), nullptr);
+    mark(KK_LNF);
+}
+
+// ------------------------------------------------------------------ graphs and timing
+
+const char *kernel_kind_name(int kind) {
+    static const char *names[KK_COUNT] = {
+        "page_updates", "gather_hidden", "lookup_slot_row", "embed_frame", "attn_plan",
+        "gemv_qkv_global", "attn_decode_paged", "gemv_proj_global", "gemv_fc_in_global", "gemv_fc_out_global", "ln_f",
+        "gemv_qkv_local", "attn_local", "gemv_proj_local", "gemv_fc_in_local", "gemv_fc_out_local", "gate_w8a8",
+        "gemv_audio_heads", "sample_greedy", "frame_commit"};
+    return (kind >= 0 && kind < KK_COUNT) ? names[kind] : "?";
+}
+
+void Engine::mark(int kind) {
+    ++launches_;
+    if (capturing_ && timing_) {
+        cudaEvent_t ev;
+        CK(cudaEventCreate(&ev));
+        CK(cudaEventRecordWithFlags(ev, stream_, cudaEventRecordExternal));  // a timed node of the graph
+        capturing_->events.push_back(ev);
+        capturing_->kinds.push_back(kind);
+    }
+}
+
+template <class F>
+void Engine::run_captured(uint64_t key, F &&issue) {
+    launches_ = 0;
+    last_graph_ = nullptr;
+    if (!use_graphs_) {
+        issue();
+        CK(cudaGetLastError());
+        return;
+    }
+    key |= uint64_t(timing_) << 48;
+    auto it = graphs_.find(key);
+    if (it == graphs_.end()) {
+        CapturedGraph g;
+        capturing_ = &g;
+        cudaGraph_t graph = nullptr;
+        CK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+        if (timing_) {
+            cudaEvent_t ev;
+            CK(cudaEventCreate(&ev));
+            CK(cudaEventRecordWithFlags(ev, stream_, cudaEventRecordExternal));  // a timed node of the graph
+            g.events.push_back(ev);
+        }
+        try {
+            issue();
+        } catch (...) {
+            cudaStreamEndCapture(stream_, &graph);
+            if (graph) cudaGraphDestroy(graph);
+            capturing_ = nullptr;
+            throw;
+        }
+        capturing_ = nullptr;
+        CK(cudaStreamEndCapture(stream_, &graph));
+        CK(cudaGraphInstantiate(&g.exec, graph, 0));
+        CK(cudaGraphDestroy(graph));
+        g.launches = launches_;
+        it = graphs_.emplace(key, std::move(g)).first;
+    }
+    CK(cudaGraphLaunch(it->second.exec, stream_));
+    launches_ = it->second.launches;
+    last_graph_ = timing_ ? &it->second : nullptr;
+}
+
+void Engine::accumulate_timing() {
+    if (!timing_ || !last_graph_) return;
+    const CapturedGraph &g = *last_graph_;
+    for (size_t i = 0; i + 1 < g.events.size(); ++i) {
+        float ms = 0.f;
+        CK(cudaEventElapsedTime(&ms, g.events[i], g.events[i + 1]));
+        prof_ms_[g.kinds[i]] += ms;
+        prof_n_[g.kinds[i]] += 1;
+    }
+    last_graph_ = nullptr;
+}
+
+void Engine::set_kernel_timing(bool on) {
+    timing_ = on;
+    for (int k = 0; k < KK_COUNT; ++k) {
+        prof_ms_[k] = 0.0;
+        prof_n_[k] = 0;
+    }
+}
+
+void Engine::read_kernel_timing(float *total_ms, int *launches, int max_kinds, int *n_kinds) const {
+    const int n = std::min(max_kinds, int(KK_COUNT));
+    for (int k = 0; k < n; ++k) {
+        if (total_ms) total_ms[k] = float(prof_ms_[k]);
+        if (launches) launches[k] = prof_n_[k];
+    }
+    if (n_kinds) *n_kinds = KK_COUNT;
 }
 
 // ------------------------------------------------------------------ state access
@@ -782,6 +964,54 @@ void Engine::debug_matrix_bytes(const std::string &name, uint8_t *out, size_t ou
 void Engine::set_cuda_stream(void *s) {
     CK(cudaStreamSynchronize(stream_));
     stream_ = s ? static_cast<cudaStream_t>(s) : own_stream_;
+}
+
+namespace {
+
+// N(0,1) from a counter-based hash (splitmix64) and the Box-Muller transform.
+__device__ __forceinline__ float hashed_normal(uint64_t seed, uint64_t i) {
+    uint64_t z = seed + (i + 1) * 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    z ^= z >> 31;
+    const float u1 = (float((z >> 40) & 0xFFFFFF) + 1.0f) * (1.0f / 16777216.0f);
+    const float u2 = float(z & 0xFFFFFF) * (1.0f / 16777216.0f);
+    return sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
+}
+
+__global__ void k_fill_state_normal(__half *__restrict__ kv, int n_pages, const int *__restrict__ pages, int n_pos,
+                                    uint64_t seed, float *__restrict__ hidden) {
+    const long long total = 2LL * kLayers * n_pos * kHidden;
+    for (long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x; t < total;
+         t += (long long)gridDim.x * blockDim.x) {
+        const int c = int(t % kHidden);
+        const int p = int((t / kHidden) % n_pos);
+        const int kvsel = int((t / ((long long)kHidden * n_pos)) & 1);
+        const int l = int(t / (2LL * kHidden * n_pos));
+        kv[(size_t)l * n_pages * kPageHalfs + (size_t)pages[p / kPage] * kPageHalfs +
+           ((kvsel * kHeads + c / kHeadDim) * kPage + p % kPage) * kHeadDim + c % kHeadDim] =
+            __float2half_rn(hashed_normal(seed, uint64_t(t)));
+    }
+    if (blockIdx.x == 0)
+        for (int c = threadIdx.x; c < kHidden; c += blockDim.x) hidden[c] = hashed_normal(~seed, uint64_t(c));
+}
+
+}  // namespace
+
+// Synthetic prefilled state for benchmarks and tests: K, V ~ N(0,1) rounded to fp16 for
+// positions 0..n_pos-1 of every layer, hidden ~ N(0,1); deterministic for a seed.
+void Engine::fill_state_random(int sid, int n_pos, uint64_t seed) {
+    check_slot(sid);
+    if (n_pos <= 0 || n_pos > max_ctx_) throw std::runtime_error("bad state length");
+    Slot &s = slots_[size_t(sid)];
+    std::vector<int> upd;
+    ensure_pages(sid, n_pos - 1, upd);
+    upload_page_updates(upd);
+    k_fill_state_normal<<<148 * 8, 256, 0, stream_>>>(kv_, n_pages_, page_table_ + size_t(sid) * pages_per_stream_,
+                                                      n_pos, seed, hidden_ + size_t(sid) * kHidden);
+    CK(cudaGetLastError());
+    CK(cudaStreamSynchronize(stream_));
+    s.pos = n_pos;
 }
 
 }  // namespace mossgpu

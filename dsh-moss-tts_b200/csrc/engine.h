@@ -37,6 +37,23 @@ struct Layer {
     float *attn_b = nullptr, *proj_b = nullptr, *fc_in_b = nullptr, *fc_out_b = nullptr;
 };
 
+// Kernel classes reported by the per-kernel timing (mossgpu_kernel_profile_read).
+enum KernelKind {
+    KK_PAGES, KK_GATHER, KK_LOOKUP, KK_EMBED, KK_PLAN,
+    KK_QKV_G, KK_ATTN_DECODE, KK_PROJ_G, KK_FCIN_G, KK_FCOUT_G, KK_LNF,
+    KK_QKV_L, KK_ATTN_LOCAL, KK_PROJ_L, KK_FCIN_L, KK_FCOUT_L, KK_GATE, KK_HEADS, KK_SAMPLE, KK_COMMIT,
+    KK_COUNT
+};
+const char *kernel_kind_name(int kind);
+
+// One captured launch sequence (a frame, or a global step) for a fixed row count.
+struct CapturedGraph {
+    cudaGraphExec_t exec = nullptr;
+    int launches = 0;
+    std::vector<cudaEvent_t> events;  // timed graphs: one before the first kernel, one after each
+    std::vector<int> kinds;
+};
+
 class Engine {
 public:
     static constexpr int kPrefillRows = 256;    // rows per prefill pass
@@ -57,12 +74,19 @@ public:
     void generate_begin(int sid, uint64_t seed);
     void step(const int32_t *sids, int n, const SampleParamsC &p, const int32_t *forced, int32_t *out_codes,
               uint8_t *out_stop, float *out_logits, float *out_gate, bool run_global);
+    static constexpr int kMaxFramesPerCall = 1024;
+    void step_frames(const int32_t *sids, int n, const SampleParamsC &p, int n_frames, int32_t *out_codes,
+                     int32_t *out_frames_done);
     void global_step_embed(const int32_t *sids, int n, const float *x, float *hidden_out);
     void set_state(int sid, const float *k, const float *v, int n_pos, const float *hidden);
     void get_kv(int sid, int layer, int p0, int n, float *k, float *v);
     void get_hidden(int sid, float *out);
     void debug_matrix_bytes(const std::string &name, uint8_t *out, size_t out_bytes);
     void set_cuda_stream(void *s);
+    void fill_state_random(int sid, int n_pos, uint64_t seed);
+    void set_kernel_timing(bool on);
+    void read_kernel_timing(float *total_ms, int *launches, int max_kinds, int *n_kinds) const;
+    void set_use_graphs(bool on) { use_graphs_ = on; }
     int last_launches() const { return launches_; }
     uint64_t weights_fingerprint() const { return weights_fp_; }
     int device() const { return device_; }
@@ -83,6 +107,14 @@ private:
     EmbedTables tables() const;
     void block(const Layer &L, int li, bool local, int R, const int *row_slot, const int *row_pos, int lpos, float *x);
     void global_layers(int R, const int *row_slot, const int *row_pos);
+    void issue_frame(int R, bool run_global);
+    void issue_global_embed(int R);
+    // Launch the sequence `issue` for key: replay its CUDA graph (captured on first use), or
+    // launch it directly when graphs are off.
+    template <class F>
+    void run_captured(uint64_t key, F &&issue);
+    void mark(int kind);
+    void accumulate_timing();
     void check_slot(int sid) const;
     void ensure_pages(int sid, int upto_pos, std::vector<int> &updates);
     void release_pages(Slot &s);
@@ -95,7 +127,9 @@ private:
     int off_frame() const { return 2 * r_max_; }
     int off_forced() const { return 3 * r_max_; }
     int off_pages() const { return 19 * r_max_; }  // [count][slot, index, page] x r_max_
-    int off_fctl() const { return 22 * r_max_ + 1; }
+    int off_fctl() const { return 22 * r_max_ + 1; }   // FrameCtl (8 ints reserved)
+    int off_active_in() const { return off_fctl() + 8; }
+    int off_fslot() const { return off_active_in() + r_max_; }  // frames committed in this call
 
     int device_ = 0;
     int max_streams_ = 0, max_ctx_ = 0, pages_per_stream_ = 0, n_pages_ = 0, r_max_ = 0;
@@ -122,6 +156,7 @@ private:
     int *plan_ = nullptr, *counter_ = nullptr, *active_ = nullptr, *codes_ = nullptr, *used_ = nullptr;
     float *part_ = nullptr, *gate_ = nullptr;
     int *rows17_ = nullptr;
+    int *codes_hist_ = nullptr;  // [kMaxFramesPerCall][max_streams][16] codes of a multi-frame call
     int *d_ctl_ = nullptr, *h_ctl_ = nullptr;
     int ctl_ints_ = 0;
     uint8_t *h_out_ = nullptr;
@@ -129,6 +164,15 @@ private:
     std::vector<Slot> slots_;
     std::vector<int> free_pages_;
     int launches_ = 0;
+
+    // CUDA graphs and per-kernel timing
+    bool use_graphs_ = true;
+    bool timing_ = false;
+    std::unordered_map<uint64_t, CapturedGraph> graphs_;
+    CapturedGraph *capturing_ = nullptr;
+    CapturedGraph *last_graph_ = nullptr;
+    double prof_ms_[KK_COUNT] = {};
+    int prof_n_[KK_COUNT] = {};
 };
 
 }  // namespace mossgpu

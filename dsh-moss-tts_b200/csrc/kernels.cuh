@@ -583,7 +583,8 @@ __device__ __forceinline__ float hsum8(const float *v) {
 __global__ void __launch_bounds__(256) k_gate(const float *__restrict__ lx, int R, const float *__restrict__ ln_w,
                                               const float *__restrict__ ln_b, const QMat wte,
                                               const int *__restrict__ frame_idx, const FrameCtl *__restrict__ ctl,
-                                              int *__restrict__ active, float *__restrict__ gate_out) {
+                                              const int *__restrict__ active_in, int *__restrict__ active,
+                                              float *__restrict__ gate_out) {
     __shared__ float xs[kHidden];
     __shared__ int8_t qa[kHidden];
     __shared__ float as[kHidden / 32];
@@ -635,8 +636,33 @@ __global__ void __launch_bounds__(256) k_gate(const float *__restrict__ lx, int 
             gate_out[2 * r + 1] = l_slot;
         }
         const bool stop = frame_idx[r] >= ctl->min_frames && ctl->end_greedy && (l_end > l_slot);
-        active[r] = stop ? 0 : 1;
+        active[r] = (active_in[r] && !stop) ? 1 : 0;  // a stream that stopped stays stopped
     }
+}
+
+// End of a frame: record this frame's codes (-1 for streams that are not active), then
+// advance each active stream's position and frame index and carry its active flag to the
+// next frame of the same call.  One CTA, so the frame counter moves after every read of it.
+__global__ void __launch_bounds__(256) k_frame_commit(const int *__restrict__ codes, const int *__restrict__ active,
+                                                      int R, int run_global, int *__restrict__ pos,
+                                                      int *__restrict__ frame_idx, int *__restrict__ active_in,
+                                                      int *__restrict__ fslot, int max_frames,
+                                                      int *__restrict__ codes_hist) {
+    const int f = *fslot;
+    if (f < max_frames) {
+        for (int i = threadIdx.x; i < R * kNVq; i += blockDim.x)
+            codes_hist[((size_t)f * R) * kNVq + i] = active[i / kNVq] ? codes[i] : -1;
+    }
+    __syncthreads();
+    for (int r = threadIdx.x; r < R; r += blockDim.x) {
+        const int a = active[r];
+        if (a) {
+            frame_idx[r] += 1;
+            if (run_global) pos[r] += 1;
+        }
+        active_in[r] = a;
+    }
+    if (threadIdx.x == 0) *fslot = f + 1;
 }
 
 // --------------------------------------------------------------------------- sampler

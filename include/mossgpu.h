@@ -87,6 +87,14 @@ int mossgpu_step(mossgpu_engine *e, const int32_t *stream_ids, int n, const moss
                  const int32_t *forced, int32_t *out_codes, uint8_t *out_stop, float *out_logits, float *out_gate,
                  int run_global);
 
+/* n_frames consecutive frames of generate() for n streams in one call, free-running (no
+ * teacher forcing), with no host round trip between frames: positions, frame indices and
+ * the end gate advance on the device.  out_codes [n_frames][n][16] holds -1 for frames after
+ * a stream stopped; out_frames_done [n] is the number of frames each stream produced
+ * (< n_frames when its gate ended it).  n_frames <= 1024. */
+int mossgpu_step_frames(mossgpu_engine *e, const int32_t *stream_ids, int n, const mossgpu_sample_params *params,
+                        int n_frames, int32_t *out_codes, int32_t *out_frames_done);
+
 /* The 12-layer global step alone with the input embedding given (llm.cpp:248-255 with
  * x_ = x): x[n][768] fp32; hidden_out[n][768] or NULL.  Appends one KV position. */
 int mossgpu_global_step_embed(mossgpu_engine *e, const int32_t *stream_ids, int n, const float *x, float *hidden_out);
@@ -105,6 +113,22 @@ int mossgpu_debug_matrix_bytes(mossgpu_engine *e, const char *name, uint8_t *out
 
 /* Kernel launches issued by the last mossgpu_step / mossgpu_global_step_embed call. */
 int mossgpu_last_launch_count(mossgpu_engine *e);
+
+/* Synthetic prefilled state (benchmarks and tests; the reference's nearest counterpart is
+ * load_state, llm.cpp:588-632): K, V ~ N(0,1) rounded to fp16 for positions 0..n_pos-1 of
+ * every layer and hidden ~ N(0,1), generated on the device from `seed`. */
+int mossgpu_fill_state_random(mossgpu_engine *e, int stream_id, int n_pos, uint64_t seed);
+
+/* Execution options: graphs = 1 (default) replays each frame as a CUDA graph captured on
+ * first use per batch size; 0 launches kernels one by one. */
+int mossgpu_set_graphs(mossgpu_engine *e, int enable);
+
+/* Per-kernel device timing, measured with CUDA events recorded between the kernels of the
+ * captured frame.  enable = 1 clears the totals and starts accumulating; read returns, per
+ * kernel class, the summed milliseconds and launch counts (n_kinds = number of classes). */
+int mossgpu_kernel_profile(mossgpu_engine *e, int enable);
+int mossgpu_kernel_profile_read(mossgpu_engine *e, float *total_ms, int *launches, int max_kinds, int *n_kinds);
+const char *mossgpu_kernel_name(int kind);
 
 #ifdef __cplusplus
 }

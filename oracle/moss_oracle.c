@@ -763,6 +763,35 @@ static void prefill_impl(or_model *m, const float *x_in, const int32_t *rows, in
 void or_prefill_rows(or_model *m, const int32_t *rows, int n, int start) { prefill_impl(m, NULL, rows, n, start); }
 void or_prefill_embeds(or_model *m, const float *x, int n, int start) { prefill_impl(m, x, NULL, n, start); }
 
+/* n_frames whole frames = generate()'s loop body (llm.cpp:647-708) with the global step
+ * always taken and greedy codes; used to time the C port per frame.  codes [n_frames][16]. */
+void or_frames(or_model *m, int n_frames, float rep, int32_t *codes) {
+    or_sample_params p = {1, 1.0f, 0, 1.0f, rep, 1, 0, 0};
+    uint32_t rng[4];
+    or_rng_seed(rng, 0);
+    int *history = (int *)malloc(sizeof(int) * (size_t)OR_NVQ * (n_frames > 0 ? n_frames : 1));
+    float lx[OR_HIDDEN], input[OR_HIDDEN], logits[OR_CODEBOOK], pair[2];
+    for (int f = 0; f < n_frames && m->pos < m->max_ctx; ++f) {
+        or_local_step(m, 0, m->hidden, lx);
+        or_assistant_logits(m, lx, pair);
+        lookup_row(&m->wte, OR_SLOT, input);
+        int32_t next[17];
+        next[0] = OR_SLOT;
+        for (int ch = 0; ch < OR_NVQ; ++ch) {
+            or_local_step(m, ch + 1, input, lx);
+            or_audio_logits(m, ch, lx, logits);
+            int *hist = history + (size_t)ch * n_frames;
+            const int pred = or_sample_token(logits, OR_CODEBOOK, &p, hist, f, rng);
+            hist[f] = pred;
+            next[ch + 1] = pred;
+            codes[(size_t)f * OR_NVQ + ch] = pred;
+            lookup_row(&m->aemb[ch], pred, input);
+        }
+        or_global_step_row(m, next, NULL);
+    }
+    free(history);
+}
+
 /* llm.cpp:634-712 */
 int or_generate(or_model *m, int max_frames, const or_sample_params *p, uint64_t seed, const int32_t *forced,
                 int32_t *codes, float *logits_out, float *gate_out) {

@@ -95,6 +95,8 @@ void or_assistant_logits(const or_model *m, const float *hidden, float *pair);
  * Returns the number of frames produced. */
 int or_generate(or_model *m, int max_frames, const or_sample_params *p, uint64_t seed,
                 const int32_t *forced, int32_t *codes, float *logits, float *gate);
+/* n_frames whole frames (local decoder + greedy codes + global step each); for timing */
+void or_frames(or_model *m, int n_frames, float rep, int32_t *codes);
 
 #ifdef __cplusplus
 }

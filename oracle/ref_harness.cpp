@@ -163,6 +163,43 @@ int ref_generate(void *h, int max_frames, int greedy, float temperature, int top
     return static_cast<int>(out.size());
 }
 
+// n_frames whole frames, each = the body of generate()'s loop (llm.cpp:647-708) with the
+// global step always taken: local decoder from hidden_, the end gate (not acted on), 16
+// greedy codes with the repetition penalty, then global_step([9, codes]).  Used to time the
+// reference per frame.  codes [n_frames][16].
+void ref_frames(void *h, int n_frames, float rep, int32_t *codes) {
+    auto *m = static_cast<LlmModel *>(h);
+    SampleParams p;
+    p.greedy = true;
+    p.repetition_penalty = rep;
+    Rng rng;
+    rng.seed(0);
+    std::array<std::vector<int>, kNVq> history;
+    for (int f = 0; f < n_frames && m->pos_ < kMaxCtx; ++f) {
+        m->local_reset();
+        m->local_step(m->hidden_.data(), m->lx_.data());
+        float pair[2];
+        m->assistant_logits(m->lx_.data(), pair);
+        Row frame{};
+        std::array<float, kHidden> input{};
+        m->lookup_row(m->wte_, kSlotToken, input.data());
+        for (int ch = 0; ch < kNVq; ++ch) {
+            m->local_step(input.data(), m->lx_.data());
+            m->audio_logits(ch, m->lx_.data(), m->logits_.data());
+            const int pred = sample_token(m->logits_.data(), kCodebook, p, history[ch].data(),
+                                          static_cast<int>(history[ch].size()), rng, m->sample_scratch_);
+            frame[ch + 1] = pred;
+            history[ch].push_back(pred);
+            m->lookup_row(m->aemb_[ch], pred, input.data());
+            codes[static_cast<size_t>(f) * kNVq + ch] = pred;
+        }
+        Row next{};
+        next[0] = kSlotToken;
+        for (int ch = 0; ch < kNVq; ++ch) next[ch + 1] = frame[ch + 1];
+        m->global_step(next, m->hidden_.data());
+    }
+}
+
 // ---- kernel-level entry points (fp16.cpp, quant.cpp, gemv_avx2.cpp, sampler.cpp) ----
 void ref_half_to_float_n(const uint16_t *h, int n, float *out) {
     for (int i = 0; i < n; ++i) out[i] = half_to_float(h[i]);
