@@ -38,6 +38,7 @@ EXPORTS = [
     "mossgpu_global_step_embed", "mossgpu_set_state", "mossgpu_get_kv", "mossgpu_get_hidden",
     "mossgpu_debug_matrix_bytes", "mossgpu_last_launch_count", "mossgpu_fill_state_random", "mossgpu_set_graphs",
     "mossgpu_kernel_profile", "mossgpu_kernel_profile_read", "mossgpu_kernel_name", "mossgpu_step_frames",
+    "mossgpu_attention_workspace_bytes", "mossgpu_attention_decode_paged", "mossgpu_op_last_error",
 ]
 
 
@@ -110,6 +111,12 @@ def lib() -> C.CDLL:
                                                   C.c_int, C.POINTER(C.c_int)]
         L.mossgpu_kernel_name.restype = C.c_char_p
         L.mossgpu_kernel_name.argtypes = [C.c_int]
+        L.mossgpu_attention_workspace_bytes.restype = C.c_size_t
+        L.mossgpu_attention_workspace_bytes.argtypes = [C.c_int]
+        L.mossgpu_attention_decode_paged.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p,
+                                                     C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_size_t,
+                                                     C.c_void_p]
+        L.mossgpu_op_last_error.restype = C.c_char_p
         _LIB = L
         return L
 

@@ -19,6 +19,9 @@
 #include "types.h"
 
 namespace mossgpu {
+// Internal linkage: every translation unit that launches these kernels (engine.cu, ops.cu)
+// compiles its own copy, so no host stub is defined twice.
+namespace {
 
 // --------------------------------------------------------------------------- helpers
 
@@ -728,4 +731,5 @@ __global__ void k_page_updates(const int *__restrict__ upd, int *__restrict__ ta
     if (i < upd[0]) table[(size_t)upd[1 + 3 * i] * pps + upd[2 + 3 * i]] = upd[3 + 3 * i];
 }
 
+}  // namespace
 }  // namespace mossgpu

@@ -1,0 +1,99 @@
+// ops.cu -- standalone kernel-level C entry points over caller-owned device buffers.
+//
+// mossgpu_attention_decode_paged: the engine's paged fp16 flash-decode (one layer) for
+// callers that keep their own KV pages, e.g. a host framework that manages the cache and
+// only wants the attention kernel.  Every pointer is a device pointer; the caller also
+// provides the scratch workspace (plan, split-K partials, arrival counters).
+#include "../../include/mossgpu.h"
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <string>
+
+#include "kernels.cuh"
+
+namespace {
+
+thread_local std::string g_op_error;
+
+int op_fail(const std::string &msg) {
+    g_op_error = msg;
+    return 1;
+}
+
+constexpr size_t kAlign = 256;
+
+size_t round_up(size_t n) { return (n + kAlign - 1) / kAlign * kAlign; }
+
+// Workspace layout for R rows: [plan: 2 + R + 1 ints][counters: R * 12 ints][partials]
+struct Layout {
+    size_t plan, counters, part, total;
+    int items;
+};
+
+Layout layout_for(int R, size_t bytes) {
+    Layout l{};
+    l.plan = 0;
+    l.counters = round_up(sizeof(int) * (size_t(R) + 3));
+    l.part = l.counters + round_up(sizeof(int) * size_t(R) * mossgpu::kHeads);
+    const size_t part_bytes = bytes > l.part ? bytes - l.part : 0;
+    l.items = int(std::min<size_t>(part_bytes / (sizeof(float) * mossgpu::kPartStride), 1u << 30));
+    l.total = bytes;
+    return l;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *mossgpu_op_last_error(void) { return g_op_error.c_str(); }
+
+size_t mossgpu_attention_workspace_bytes(int R) {
+    if (R <= 0) return 0;
+    // room for 8 split-K chunks per (row, head); the plan widens chunks to fit any length
+    const Layout l = layout_for(R, 0);
+    return l.part + sizeof(float) * mossgpu::kPartStride * size_t(R) * mossgpu::kHeads * 8;
+}
+
+int mossgpu_attention_decode_paged(const float *q, const void *kv_layer, const int32_t *page_table,
+                                   int pages_per_stream, const int32_t *row_slot, const int32_t *row_pos, int R,
+                                   float *out, void *workspace, size_t workspace_bytes, void *cuda_stream) {
+    using namespace mossgpu;
+    if (R <= 0) return 0;
+    if (!q || !kv_layer || !page_table || !row_slot || !row_pos || !out || !workspace)
+        return op_fail("attention_decode_paged: a required pointer is NULL");
+    if (pages_per_stream <= 0) return op_fail("attention_decode_paged: pages_per_stream must be positive");
+    const Layout l = layout_for(R, workspace_bytes);
+    if (l.items < R * kHeads)
+        return op_fail("attention_decode_paged: workspace too small (need mossgpu_attention_workspace_bytes(R))");
+    if (reinterpret_cast<uintptr_t>(workspace) % 16 != 0)
+        return op_fail("attention_decode_paged: workspace must be 16-byte aligned");
+    cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
+    char *ws = static_cast<char *>(workspace);
+    int *plan = reinterpret_cast<int *>(ws + l.plan);
+    int *counter = reinterpret_cast<int *>(ws + l.counters);
+    float *part = reinterpret_cast<float *>(ws + l.part);
+    // arrival counters must start at zero (the workspace's contents are unspecified)
+    cudaError_t e = cudaMemsetAsync(counter, 0, sizeof(int) * size_t(R) * kHeads, st);
+    if (e != cudaSuccess) return op_fail(std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
+    k_attn_plan<<<1, 32, 0, st>>>(row_pos, R, l.items, plan);
+    AttnArgs t{};
+    t.q = q;
+    t.kv = static_cast<const __half *>(kv_layer);
+    t.page_table = page_table;
+    t.pages_per_stream = pages_per_stream;
+    t.row_slot = row_slot;
+    t.row_pos = row_pos;
+    t.plan = plan;
+    t.R = R;
+    t.part = part;
+    t.counter = counter;
+    t.out = out;
+    k_attn_decode<<<148 * 4, 256, 0, st>>>(t);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return op_fail(std::string("attention_decode_paged launch: ") + cudaGetErrorString(e));
+    return 0;
+}
+
+}  // extern "C"

@@ -130,6 +130,25 @@ int mossgpu_kernel_profile(mossgpu_engine *e, int enable);
 int mossgpu_kernel_profile_read(mossgpu_engine *e, float *total_ms, int *launches, int max_kinds, int *n_kinds);
 const char *mossgpu_kernel_name(int kind);
 
+/* ---- standalone kernel-level ops (no engine handle; all pointers are DEVICE pointers) ----
+ *
+ * mossgpu_attention_decode_paged: decode attention of one layer over an fp16 paged KV cache
+ * -- the engine's split-K flash-decode, with the reference's attention semantics
+ * (llm.cpp:189-228: scores q.k / 8, max-subtracted softmax, weighted sum of v):
+ *   q          [R][768] fp32 queries (RoPE already applied)
+ *   kv_layer   one layer's pages, fp16 [n_pages][2 (k, v)][12 heads][16 positions][64]
+ *   page_table [slots][pages_per_stream] int32; row r reads pages of slot row_slot[r]
+ *   row_pos    [R] int32; row r attends to positions 0..row_pos[r]
+ *   out        [R][768] fp32
+ *   workspace  >= mossgpu_attention_workspace_bytes(R) bytes, 16-byte aligned, any contents
+ * cuda_stream is a cudaStream_t (NULL = legacy default stream); the call only enqueues work.
+ * Errors: non-zero return, message from mossgpu_op_last_error() (per thread). */
+size_t mossgpu_attention_workspace_bytes(int R);
+int mossgpu_attention_decode_paged(const float *q, const void *kv_layer, const int32_t *page_table,
+                                   int pages_per_stream, const int32_t *row_slot, const int32_t *row_pos, int R,
+                                   float *out, void *workspace, size_t workspace_bytes, void *cuda_stream);
+const char *mossgpu_op_last_error(void);
+
 #ifdef __cplusplus
 }
 #endif
