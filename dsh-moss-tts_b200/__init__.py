@@ -39,6 +39,7 @@ EXPORTS = [
     "mossgpu_debug_matrix_bytes", "mossgpu_last_launch_count", "mossgpu_fill_state_random", "mossgpu_set_graphs",
     "mossgpu_kernel_profile", "mossgpu_kernel_profile_read", "mossgpu_kernel_name", "mossgpu_step_frames",
     "mossgpu_attention_workspace_bytes", "mossgpu_attention_decode_paged", "mossgpu_op_last_error",
+    "mossgpu_attention_decode_paged_noalloc",
 ]
 
 
@@ -117,6 +118,8 @@ def lib() -> C.CDLL:
                                                      C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_size_t,
                                                      C.c_void_p]
         L.mossgpu_op_last_error.restype = C.c_char_p
+        L.mossgpu_attention_decode_paged_noalloc.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p,
+                                                             C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]
         _LIB = L
         return L
 

@@ -9,6 +9,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <mutex>
 #include <string>
 
 #include "kernels.cuh"
@@ -97,3 +98,91 @@ int mossgpu_attention_decode_paged(const float *q, const void *kv_layer, const i
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------
+// Allocation-free variant of mossgpu_attention_decode_paged.
+//
+// Some callers cannot allocate device memory at the moment they need attention: a real-time
+// audio callback in a plugin host (cudaMalloc and cudaFree can block for milliseconds, and
+// cudaFree synchronises the whole device), or a host program whose device memory is owned by
+// another allocator that it may not go around.  For them the scratch this kernel needs (the
+// split-K plan, the arrival counters and the partial results) lives in the fixed array below,
+// which the CUDA runtime creates on every GPU that loads this library and keeps until the
+// process exits.
+namespace {
+
+constexpr int kNoAllocMaxRows = 256;    // rows per call
+constexpr int kNoAllocMaxItems = 4096;  // split-K (chunk, head) partials; chunks widen to fit
+constexpr size_t kNoAllocPlanBytes = 2048;                                   // 2 + R + 1 ints
+constexpr size_t kNoAllocCounterBytes = sizeof(int) * kNoAllocMaxRows * mossgpu::kHeads;  // 12 KiB
+constexpr size_t kNoAllocPartBytes = sizeof(float) * mossgpu::kPartStride * kNoAllocMaxItems;
+constexpr size_t kNoAllocScratchBytes = kNoAllocPlanBytes + kNoAllocCounterBytes + kNoAllocPartBytes;  // ~1.08 MiB
+static_assert(kNoAllocPlanBytes >= sizeof(int) * (kNoAllocMaxRows + 3), "plan area too small");
+
+static __device__ __align__(256) unsigned char g_attn_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of the array, looked up once per device (with that device current).  In host
+// code the array's name is only a host-side handle, never a device address.
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void *g_noalloc_ptr[kMaxDevices] = {};
+
+int noalloc_scratch(void **out) {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return op_fail(std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+    if (dev < 0 || dev >= kMaxDevices) return op_fail("attention_decode_paged_noalloc: device ordinal out of range");
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_attn_noalloc_scratch);
+        if (e != cudaSuccess || !p) return op_fail(std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+        g_noalloc_ptr[dev] = p;
+    }
+    *out = g_noalloc_ptr[dev];
+    return 0;
+}
+
+}  // namespace
+
+extern "C" int mossgpu_attention_decode_paged_noalloc(const float *q, const void *kv_layer, const int32_t *page_table,
+                                                      int pages_per_stream, const int32_t *row_slot,
+                                                      const int32_t *row_pos, int R, float *out, void *cuda_stream) {
+    using namespace mossgpu;
+    if (R <= 0) return 0;
+    if (R > kNoAllocMaxRows)
+        return op_fail("attention_decode_paged_noalloc: R = " + std::to_string(R) + " rows exceeds the limit of " +
+                       std::to_string(kNoAllocMaxRows) + " (use mossgpu_attention_decode_paged with a workspace)");
+    if (!q || !kv_layer || !page_table || !row_slot || !row_pos || !out)
+        return op_fail("attention_decode_paged_noalloc: a required pointer is NULL");
+    if (pages_per_stream <= 0) return op_fail("attention_decode_paged_noalloc: pages_per_stream must be positive");
+    void *scratch = nullptr;
+    if (noalloc_scratch(&scratch) != 0) return 1;
+    cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
+    char *base = static_cast<char *>(scratch);
+    int *plan = reinterpret_cast<int *>(base);
+    int *counter = reinterpret_cast<int *>(base + kNoAllocPlanBytes);
+    float *part = reinterpret_cast<float *>(base + kNoAllocPlanBytes + kNoAllocCounterBytes);
+    // the array keeps whatever the previous call left: the arrival counters must start at zero
+    // (the plan is rewritten and the partials are written before they are read)
+    cudaError_t e = cudaMemsetAsync(counter, 0, sizeof(int) * size_t(R) * kHeads, st);
+    if (e != cudaSuccess) return op_fail(std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
+    k_attn_plan<<<1, 32, 0, st>>>(row_pos, R, kNoAllocMaxItems, plan);
+    AttnArgs t{};
+    t.q = q;
+    t.kv = static_cast<const __half *>(kv_layer);
+    t.page_table = page_table;
+    t.pages_per_stream = pages_per_stream;
+    t.row_slot = row_slot;
+    t.row_pos = row_pos;
+    t.plan = plan;
+    t.R = R;
+    t.part = part;
+    t.counter = counter;
+    t.out = out;
+    k_attn_decode<<<148 * 4, 256, 0, st>>>(t);
+    e = cudaGetLastError();
+    if (e != cudaSuccess)
+        return op_fail(std::string("attention_decode_paged_noalloc launch: ") + cudaGetErrorString(e));
+    return 0;
+}

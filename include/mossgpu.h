@@ -149,6 +149,25 @@ int mossgpu_attention_decode_paged(const float *q, const void *kv_layer, const i
                                    float *out, void *workspace, size_t workspace_bytes, void *cuda_stream);
 const char *mossgpu_op_last_error(void);
 
+/* mossgpu_attention_decode_paged_noalloc: the same attention for callers that cannot
+ * allocate device memory when they run it -- for example a real-time audio callback in a
+ * plugin host, where cudaMalloc/cudaFree may block for milliseconds (cudaFree synchronises
+ * the device), or a program whose device memory belongs to another allocator.  It takes no
+ * workspace and allocates nothing: its scratch (~1.08 MiB) is a fixed array that the library
+ * places on every GPU that loads it, kept until the process exits.
+ *   - R must be <= 256 rows; larger batches are rejected with an error (use the workspace
+ *     entry point above).
+ *   - The first call on each device looks up that array's device address (with the device
+ *     current); make that first call before any CUDA stream capture.
+ *   - All calls on a device share the one array.  Each call clears the parts that must start
+ *     at zero, but two calls whose kernels overlap on the GPU (different streams, or other
+ *     host threads) race on it: serialise them on one stream.
+ * Arguments, results and errors are those of mossgpu_attention_decode_paged.  This entry
+ * point has no counterpart in the reference (its CPU attention needs no scratch). */
+int mossgpu_attention_decode_paged_noalloc(const float *q, const void *kv_layer, const int32_t *page_table,
+                                           int pages_per_stream, const int32_t *row_slot, const int32_t *row_pos,
+                                           int R, float *out, void *cuda_stream);
+
 #ifdef __cplusplus
 }
 #endif
