@@ -39,7 +39,7 @@ EXPORTS = [
     "mossgpu_debug_matrix_bytes", "mossgpu_last_launch_count", "mossgpu_fill_state_random", "mossgpu_set_graphs",
     "mossgpu_kernel_profile", "mossgpu_kernel_profile_read", "mossgpu_kernel_name", "mossgpu_step_frames",
     "mossgpu_attention_workspace_bytes", "mossgpu_attention_decode_paged", "mossgpu_op_last_error",
-    "mossgpu_attention_decode_paged_noalloc",
+    "mossgpu_attention_decode_paged_noalloc", "mossgpu_set_gemm_path", "mossgpu_debug_matrix_tile_bytes",
 ]
 
 
@@ -107,6 +107,9 @@ def lib() -> C.CDLL:
         L.mossgpu_step_frames.argtypes = [C.c_void_p, _i32, C.c_int, C.POINTER(SampleParams), C.c_int, C.c_void_p,
                                           C.c_void_p]
         L.mossgpu_set_graphs.argtypes = [C.c_void_p, C.c_int]
+        L.mossgpu_set_gemm_path.argtypes = [C.c_void_p, C.c_int]
+        L.mossgpu_debug_matrix_tile_bytes.argtypes = [C.c_void_p, C.c_char_p,
+                                                      np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS"), C.c_size_t]
         L.mossgpu_kernel_profile.argtypes = [C.c_void_p, C.c_int]
         L.mossgpu_kernel_profile_read.argtypes = [C.c_void_p, _f32, np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS"),
                                                   C.c_int, C.POINTER(C.c_int)]
@@ -240,6 +243,15 @@ class Engine:
 
     def set_graphs(self, enable: bool):
         self._check(self.lib.mossgpu_set_graphs(self.h, int(enable)))
+
+    def set_gemm_path(self, mode: int):
+        """0 = automatic, 1 = CUDA-core GEMV, 2 = tcgen05 tensor cores (rows <= 256)."""
+        self._check(self.lib.mossgpu_set_gemm_path(self.h, mode))
+
+    def matrix_tile_bytes(self, name: str, rows: int, cols: int) -> np.ndarray:
+        out = np.zeros((rows // 4) * (cols // 32) * 136, np.uint8)
+        self._check(self.lib.mossgpu_debug_matrix_tile_bytes(self.h, name.encode(), out, out.size))
+        return out
 
     def kernel_profile(self, enable: bool):
         self._check(self.lib.mossgpu_kernel_profile(self.h, int(enable)))

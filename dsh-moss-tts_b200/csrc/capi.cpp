@@ -178,6 +178,17 @@ int mossgpu_set_graphs(mossgpu_engine *e, int enable) {
     return guarded(e, [&](mossgpu::Engine &g) { g.set_use_graphs(enable != 0); });
 }
 
+int mossgpu_set_gemm_path(mossgpu_engine *e, int mode) {
+    return guarded(e, [&](mossgpu::Engine &g) { g.set_gemm_path(mode); });
+}
+
+int mossgpu_debug_matrix_tile_bytes(mossgpu_engine *e, const char *name, uint8_t *out, size_t out_bytes) {
+    return guarded(e, [&](mossgpu::Engine &g) {
+        if (!name || !out) throw std::runtime_error("name and out are required");
+        g.debug_matrix_tile_bytes(name, out, out_bytes);
+    });
+}
+
 int mossgpu_kernel_profile(mossgpu_engine *e, int enable) {
     return guarded(e, [&](mossgpu::Engine &g) { g.set_kernel_timing(enable != 0); });
 }

@@ -16,6 +16,7 @@
 #include <vector>
 
 #include "kernels.cuh"
+#include "gemm_tc.cuh"
 
 namespace mossgpu {
 
@@ -132,6 +133,13 @@ void Engine::load_weights(const std::string &path) {
         const long long words = nblocks * 17;
         k_repack_q8x4<<<unsigned((words + 255) / 256), 256>>>(staging + e.off, m.qs, m.sc, nblocks);
         CK(cudaGetLastError());
+        if (rows % kTcM == 0 && cols % kTcK == 0) {  // every matrix of this model qualifies
+            m.qt = dalloc<int8_t>(size_t(rows) * cols, owned_);
+            m.st = dalloc<__half>(size_t(rows) * (cols / 32), owned_);
+            const long long items = (long long)rows * (cols / 32);
+            k_repack_tiles<<<unsigned((items + 255) / 256), 256>>>(staging + e.off, rows, cols, m.qt, m.st);
+            CK(cudaGetLastError());
+        }
         mats_[name] = m;
         return m;
     };
@@ -202,6 +210,17 @@ void Engine::allocate_state() {
     gate_ = dalloc<float>(R * 2, owned_);
     rows17_ = dalloc<int>(R * (kNVq + 1), owned_);
     codes_hist_ = dalloc<int>(size_t(kMaxFramesPerCall) * max_streams_ * kNVq, owned_);
+    bimg_a_ = dalloc<uint8_t>(2 * size_t(kHidden) * kTcMaxRows * 2, owned_);  // hi and lo parts
+    bimg_mlp_ = dalloc<uint8_t>(2 * size_t(kFF) * kTcMaxRows * 2, owned_);
+    dev_err_ = dalloc<int>(4, owned_);
+    CK(cudaMemset(dev_err_, 0, 4 * sizeof(int)));
+    {
+        void *he = nullptr;
+        CK(cudaMallocHost(&he, 4 * sizeof(int)));
+        pinned_.push_back(he);
+        h_err_ = static_cast<int *>(he);
+        *h_err_ = 0;
+    }
 
     // control block: [slot R][pos R][frame R][forced 16R][page updates 1 + 3R][FrameCtl]
     static_assert(sizeof(FrameCtl) <= 8 * sizeof(int), "FrameCtl must fit its 8 reserved ints");
@@ -296,6 +315,181 @@ void Engine::set_smem_limits() {
     set_attr_all<PRO_NONE, EPI_RESID>();
     set_attr_all<PRO_LN, EPI_GELU>();
     set_attr_all<PRO_LN, EPI_STORE>();
+    // the stage count depends on N, so the largest footprint is not necessarily at N = 256
+    int s1 = 0, s3 = 0;
+    for (int n = 16; n <= kTcMaxRows; n += 16) {
+        s1 = std::max(s1, tc_smem_bytes(n, TC_F16));
+        s3 = std::max(s3, tc_smem_bytes(n, TC_F16X3));
+    }
+    CK(cudaFuncSetAttribute(k_gemm_tc<TC_STORE, TC_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, s1));
+    CK(cudaFuncSetAttribute(k_gemm_tc<TC_QKV, TC_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, s1));
+    CK(cudaFuncSetAttribute(k_gemm_tc<TC_RESID, TC_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, s1));
+    CK(cudaFuncSetAttribute(k_gemm_tc<TC_GELU_B, TC_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, s1));
+    CK(cudaFuncSetAttribute(k_gemm_tc<TC_STORE, TC_F16X3>, cudaFuncAttributeMaxDynamicSharedMemorySize, s3));
+    CK(cudaFuncSetAttribute(k_gemm_tc<TC_QKV, TC_F16X3>, cudaFuncAttributeMaxDynamicSharedMemorySize, s3));
+    CK(cudaFuncSetAttribute(k_gemm_tc<TC_RESID, TC_F16X3>, cudaFuncAttributeMaxDynamicSharedMemorySize, s3));
+    CK(cudaFuncSetAttribute(k_gemm_tc<TC_GELU_B, TC_F16X3>, cudaFuncAttributeMaxDynamicSharedMemorySize, s3));
+    CK(cudaFuncSetAttribute(k_build_bimg, cudaFuncAttributeMaxDynamicSharedMemorySize, kFF * 4));
+}
+
+void Engine::set_gemm_path(int mode) {
+    if (mode < 0 || mode > 3)
+        throw std::runtime_error("gemm path must be 0 (auto), 1 (CUDA cores), 2 (tensor cores, fp16x3) or 3 (tensor "
+                                 "cores, fp16)");
+    gemm_path_ = mode;
+}
+
+bool Engine::use_tc(int R) const {
+    if (R > kTcMaxRows || gemm_path_ == 1) return false;
+    return gemm_path_ >= 2 || R > kGemvMaxRows;
+}
+
+namespace {
+
+template <int EPI>
+void launch_tc(TcArgs a, int ksplit, int prec, cudaStream_t st) {
+    const int nchunks = a.K / kTcK;
+    a.ksplit = ksplit;
+    dim3 grid(a.rows / kTcM, (nchunks + ksplit - 1) / ksplit);
+    if (prec == TC_F16X3)
+        k_gemm_tc<EPI, TC_F16X3><<<grid, kTcThreads, tc_smem_bytes(a.N, TC_F16X3), st>>>(a);
+    else
+        k_gemm_tc<EPI, TC_F16><<<grid, kTcThreads, tc_smem_bytes(a.N, TC_F16), st>>>(a);
+}
+
+}  // namespace
+
+// The block of llm.cpp:230-246 on tensor cores (R > 8 rows): activation images built by
+// k_build_bimg (LayerNorm fused), tcgen05 GEMMs with fused epilogues, split-K with atomic
+// residual adds for the two 768-row outputs (proj, fc_out) so that enough SMs stream weights.
+void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_slot, const int *row_pos, int lpos,
+                      float *x) {
+    const int N = (R + 15) / 16 * 16;
+    const int prec = gemm_path_ == 3 ? TC_F16 : TC_F16X3;
+    k_build_bimg<<<N, 256, kHidden * 4, stream_>>>(x, kHidden, R, N, kHidden, L.ln1_w, L.ln1_b, tc_parts(prec), bimg_a_);
+    mark(KK_BIMG);
+    TcArgs a{};
+    a.N = N;
+    a.R = R;
+    a.err = dev_err_;
+    a.bimg = bimg_a_;
+    a.qt = L.attn.qt;
+    a.st = L.attn.st;
+    a.rows = kQKV;
+    a.K = kHidden;
+    a.bias = L.attn_b;
+    a.q_out = q_;
+    a.row_slot = row_slot;
+    a.row_pos = local ? nullptr : row_pos;
+    a.fixed_pos = lpos;
+    a.rope = rope_;
+    if (local) {
+        a.lkv = lkv_;
+    } else {
+        a.kv = kv_ + size_t(li) * n_pages_ * kPageHalfs;
+        a.page_table = page_table_;
+        a.pages_per_stream = pages_per_stream_;
+    }
+    launch_tc<TC_QKV>(a, kHidden / kTcK, prec, stream_);
+    mark(local ? KK_QKV_L : KK_QKV_G);
+    if (local) {
+        const int warps = R * kHeads;
+        k_attn_local<<<(warps + 11) / 12, 384, 0, stream_>>>(q_, lkv_, row_slot, lpos, R, attn_);
+        mark(KK_ATTN_LOCAL);
+    } else {
+        AttnArgs t{};
+        t.q = q_;
+        t.kv = a.kv;
+        t.page_table = page_table_;
+        t.pages_per_stream = pages_per_stream_;
+        t.row_slot = row_slot;
+        t.row_pos = row_pos;
+        t.plan = plan_;
+        t.R = R;
+        t.part = part_;
+        t.counter = counter_;
+        t.out = attn_;
+        k_attn_decode<<<kAttnGrid, 256, 0, stream_>>>(t);
+        mark(KK_ATTN_DECODE);
+    }
+    k_build_bimg<<<N, 256, kHidden * 4, stream_>>>(attn_, kHidden, R, N, kHidden, nullptr, nullptr, tc_parts(prec), bimg_a_);
+    mark(KK_BIMG);
+    TcArgs p{};
+    p.N = N;
+    p.R = R;
+    p.err = dev_err_;
+    p.bimg = bimg_a_;
+    p.qt = L.proj.qt;
+    p.st = L.proj.st;
+    p.rows = kHidden;
+    p.K = kHidden;
+    p.bias = L.proj_b;
+    p.out = x;
+    p.ldo = kHidden;
+    launch_tc<TC_RESID>(p, 3, prec, stream_);  // 6 tiles x 4 K-splits
+    mark(local ? KK_PROJ_L : KK_PROJ_G);
+    k_build_bimg<<<N, 256, kHidden * 4, stream_>>>(x, kHidden, R, N, kHidden, L.ln2_w, L.ln2_b, tc_parts(prec), bimg_a_);
+    mark(KK_BIMG);
+    TcArgs f{};
+    f.N = N;
+    f.R = R;
+    f.err = dev_err_;
+    f.bimg = bimg_a_;
+    f.qt = L.fc_in.qt;
+    f.st = L.fc_in.st;
+    f.rows = kFF;
+    f.K = kHidden;
+    f.bias = L.fc_in_b;
+    f.bimg_out = bimg_mlp_;
+    launch_tc<TC_GELU_B>(f, kHidden / kTcK, prec, stream_);
+    mark(local ? KK_FCIN_L : KK_FCIN_G);
+    TcArgs o{};
+    o.N = N;
+    o.R = R;
+    o.err = dev_err_;
+    o.bimg = bimg_mlp_;
+    o.qt = L.fc_out.qt;
+    o.st = L.fc_out.st;
+    o.rows = kHidden;
+    o.K = kFF;
+    o.bias = L.fc_out_b;
+    o.out = x;
+    o.ldo = kHidden;
+    launch_tc<TC_RESID>(o, 6, prec, stream_);  // 6 tiles x 8 K-splits
+    mark(local ? KK_FCOUT_L : KK_FCOUT_G);
+}
+
+// audio head ch on tensor cores: logits[r][ch] = aemb[ch] . LN(lx[r]) (llm.cpp:268-270)
+void Engine::heads_tc(int ch, int R) {
+    const int N = (R + 15) / 16 * 16;
+    const int prec = gemm_path_ == 3 ? TC_F16 : TC_F16X3;
+    k_build_bimg<<<N, 256, kHidden * 4, stream_>>>(lx_, kHidden, R, N, kHidden, llnf_w_, llnf_b_, tc_parts(prec), bimg_a_);
+    mark(KK_BIMG);
+    TcArgs h{};
+    h.N = N;
+    h.R = R;
+    h.err = dev_err_;
+    h.bimg = bimg_a_;
+    h.qt = aemb_[ch].qt;
+    h.st = aemb_[ch].st;
+    h.rows = kCodebook;
+    h.K = kHidden;
+    h.out = logits_ + size_t(ch) * kCodebook;
+    h.ldo = kNVq * kCodebook;
+    launch_tc<TC_STORE>(h, kHidden / kTcK, prec, stream_);
+    mark(KK_HEADS);
+}
+
+// A tensor-core kernel that timed out on one of its barriers leaves a code in dev_err_.
+// Callers enqueue the copy of the flag into h_err_ before their final synchronisation.
+void Engine::check_device_error() {
+    const int e = *h_err_;
+    if (e != 0) {
+        *h_err_ = 0;
+        CK(cudaMemsetAsync(dev_err_, 0, sizeof(int), stream_));
+        CK(cudaStreamSynchronize(stream_));
+        throw std::runtime_error("tensor-core GEMM barrier wait timed out (code " + std::to_string(e) + ")");
+    }
 }
 
 QMat Engine::qm(const DevMat &m) const { return QMat{m.qs, m.sc, m.rows, m.cols}; }
@@ -313,6 +507,10 @@ EmbedTables Engine::tables() const {
 // `li` with the paged KV at row_pos; local=true: the local layer at local position lpos.
 void Engine::block(const Layer &L, int li, bool local, int R, const int *row_slot, const int *row_pos, int lpos,
                    float *x) {
+    if (use_tc(R)) {
+        block_tc(L, li, local, R, row_slot, row_pos, lpos, x);
+        return;
+    }
     GemvArgs a{};
     a.nrows = R;
     // LN1 -> QKV + bias + RoPE + KV append
@@ -508,7 +706,9 @@ void Engine::prefill_common(int sid, int m, int start, const int32_t *rows, cons
                                                      hidden_ + size_t(sid) * kHidden, nullptr, nullptr);
         }
         CK(cudaGetLastError());
+        CK(cudaMemcpyAsync(h_err_, dev_err_, sizeof(int), cudaMemcpyDeviceToHost, stream_));
         CK(cudaStreamSynchronize(stream_));
+        check_device_error();
     }
     s.pos = start + m;
 }
@@ -587,7 +787,9 @@ void Engine::step(const int32_t *sids, int n, const SampleParamsC &p, const int3
     CK(cudaMemcpyAsync(h_gate, gate_, size_t(R) * 2 * sizeof(float), cudaMemcpyDeviceToHost, stream_));
     if (out_logits)
         CK(cudaMemcpyAsync(h_logits, logits_, size_t(R) * kNVq * kCodebook * sizeof(float), cudaMemcpyDeviceToHost, stream_));
+    CK(cudaMemcpyAsync(h_err_, dev_err_, sizeof(int), cudaMemcpyDeviceToHost, stream_));
     CK(cudaStreamSynchronize(stream_));
+    check_device_error();
     accumulate_timing();
     for (int r = 0; r < R; ++r) {
         const bool act = h_active[r] != 0;
@@ -659,7 +861,9 @@ void Engine::step_frames(const int32_t *sids, int n, const SampleParamsC &p, int
     if (out_codes)
         CK(cudaMemcpyAsync(out_codes, codes_hist_, size_t(n_frames) * R * kNVq * sizeof(int), cudaMemcpyDeviceToHost,
                            stream_));
+    CK(cudaMemcpyAsync(h_err_, dev_err_, sizeof(int), cudaMemcpyDeviceToHost, stream_));
     CK(cudaStreamSynchronize(stream_));
+    check_device_error();
     accumulate_timing();
     launches_ = total_launches;
     for (int r = 0; r < R; ++r) {
@@ -689,15 +893,15 @@ void Engine::global_step_embed(const int32_t *sids, int n, const float *x, float
     CK(cudaMemcpyAsync(d_ctl_, h_ctl_, size_t(2 * r_max_) * sizeof(int), cudaMemcpyHostToDevice, stream_));
     CK(cudaMemcpyAsync(x_, x, size_t(n) * kHidden * sizeof(float), cudaMemcpyHostToDevice, stream_));
     run_captured((uint64_t(2) << 40) | uint64_t(n), [&] { issue_global_embed(n); });
+    float *h = reinterpret_cast<float *>(h_out_);
     if (hidden_out) {
-        float *h = reinterpret_cast<float *>(h_out_);
         k_gather_rows<<<n, 256, 0, stream_>>>(hidden_, d_ctl_, n, q_);
         CK(cudaMemcpyAsync(h, q_, size_t(n) * kHidden * sizeof(float), cudaMemcpyDeviceToHost, stream_));
-        CK(cudaStreamSynchronize(stream_));
-        std::memcpy(hidden_out, h, size_t(n) * kHidden * sizeof(float));
-    } else {
-        CK(cudaStreamSynchronize(stream_));
     }
+    CK(cudaMemcpyAsync(h_err_, dev_err_, sizeof(int), cudaMemcpyDeviceToHost, stream_));
+    CK(cudaStreamSynchronize(stream_));
+    check_device_error();
+    if (hidden_out) std::memcpy(hidden_out, h, size_t(n) * kHidden * sizeof(float));
     accumulate_timing();
     for (int r = 0; r < n; ++r) slots_[size_t(sids[r])].pos += 1;
 }
@@ -725,17 +929,21 @@ void Engine::issue_frame(int R, bool run_global) {
             mark(KK_GATE);
         } else {
             const int ch = ls - 1;
-            GemvArgs h{};
-            h.nrows = R;
-            h.w = qm(aemb_[ch]);
-            h.x = lx_;
-            h.ldx = kHidden;
-            h.ln_w = llnf_w_;
-            h.ln_b = llnf_b_;
-            h.out = logits_ + size_t(ch) * kCodebook;
-            h.ldo = kNVq * kCodebook;
-            launch_gemv<PRO_LN, EPI_STORE>(h, stream_);
-            mark(KK_HEADS);
+            if (use_tc(R)) {
+                heads_tc(ch, R);
+            } else {
+                GemvArgs h{};
+                h.nrows = R;
+                h.w = qm(aemb_[ch]);
+                h.x = lx_;
+                h.ldx = kHidden;
+                h.ln_w = llnf_w_;
+                h.ln_b = llnf_b_;
+                h.out = logits_ + size_t(ch) * kCodebook;
+                h.ldo = kNVq * kCodebook;
+                launch_gemv<PRO_LN, EPI_STORE>(h, stream_);
+                mark(KK_HEADS);
+            }
             k_sample_greedy<<<R, 256, 0, stream_>>>(logits_ + size_t(ch) * kCodebook, kNVq * kCodebook, ch, d_slot, R,
                                                    counts_, d_fc, d_forced, active_, codes_, used_, qm(aemb_[ch]),
                                                    ch + 1 < kNVq ? lx_ : nullptr);
@@ -770,7 +978,7 @@ const char *kernel_kind_name(int kind) {
         "page_updates", "gather_hidden", "lookup_slot_row", "embed_frame", "attn_plan",
         "gemv_qkv_global", "attn_decode_paged", "gemv_proj_global", "gemv_fc_in_global", "gemv_fc_out_global", "ln_f",
         "gemv_qkv_local", "attn_local", "gemv_proj_local", "gemv_fc_in_local", "gemv_fc_out_local", "gate_w8a8",
-        "gemv_audio_heads", "sample_greedy", "frame_commit"};
+        "gemv_audio_heads", "sample_greedy", "frame_commit", "build_activation_image"};
     return (kind >= 0 && kind < KK_COUNT) ? names[kind] : "?";
 }
 
@@ -794,7 +1002,7 @@ void Engine::run_captured(uint64_t key, F &&issue) {
         CK(cudaGetLastError());
         return;
     }
-    key |= uint64_t(timing_) << 48;
+    key |= (uint64_t(timing_) << 48) | (uint64_t(gemm_path_) << 50);  // both change what is captured
     auto it = graphs_.find(key);
     if (it == graphs_.end()) {
         CapturedGraph g;
@@ -958,6 +1166,34 @@ void Engine::debug_matrix_bytes(const std::string &name, uint8_t *out, size_t ou
     for (size_t b = 0; b < nblocks; ++b) {
         std::memcpy(out + b * 136, sc.data() + b * 4, 8);
         std::memcpy(out + b * 136 + 8, qs.data() + b * 128, 128);
+    }
+}
+
+// The tensor-core tile copy of a matrix turned back into Q8_0_4X4 file bytes (inverse of
+// k_repack_tiles), to prove that layout is a byte permutation of the file too.
+void Engine::debug_matrix_tile_bytes(const std::string &name, uint8_t *out, size_t out_bytes) {
+    auto it = mats_.find(name);
+    if (it == mats_.end()) throw std::runtime_error("no matrix named " + name);
+    const DevMat &m = it->second;
+    if (!m.qt) throw std::runtime_error("matrix has no tensor-core tile layout: " + name);
+    const int nb = m.cols / 32, nch = m.cols / kTcK;
+    if (out_bytes < size_t(m.rows / 4) * nb * 136) throw std::runtime_error("output buffer too small");
+    std::vector<int8_t> qt(size_t(m.rows) * m.cols);
+    std::vector<uint16_t> st(size_t(m.rows) * nb);
+    CK(cudaMemcpyAsync(qt.data(), m.qt, qt.size(), cudaMemcpyDeviceToHost, stream_));
+    CK(cudaMemcpyAsync(st.data(), m.st, st.size() * 2, cudaMemcpyDeviceToHost, stream_));
+    CK(cudaStreamSynchronize(stream_));
+    for (int row = 0; row < m.rows; ++row) {
+        const int tile = row / kTcM, mm = row % kTcM, k4 = row & 3;
+        for (int c = 0; c < nch; ++c) {
+            const size_t base = (size_t(tile) * nch + c) * kTcM + mm;
+            for (int j = 0; j < 4; ++j) {
+                const int b = 2 * c + (j >> 1);
+                uint8_t *blk = out + (size_t(row >> 2) * nb + b) * 136;
+                std::memcpy(blk + 8 + k4 * 32 + (j & 1) * 16, qt.data() + base * 64 + ((j ^ ((mm >> 1) & 3)) << 4), 16);
+                if ((j & 1) == 0) std::memcpy(blk + k4 * 2, st.data() + base * 2 + (j >> 1), 2);
+            }
+        }
     }
 }
 

@@ -26,8 +26,10 @@ struct SampleParamsC {
 };
 
 struct DevMat {
-    int8_t *qs = nullptr;
-    __half *sc = nullptr;
+    int8_t *qs = nullptr;   // GEMV planes: [rows/4][cols/32][4][32] int8
+    __half *sc = nullptr;   //              [rows/4][cols/32][4] fp16
+    int8_t *qt = nullptr;   // tensor-core tiles: [rows/128][cols/64][128][64] int8 (swizzled pieces)
+    __half *st = nullptr;   //                    [rows/128][cols/64][128][2] fp16
     int rows = 0, cols = 0;
 };
 
@@ -42,6 +44,7 @@ enum KernelKind {
     KK_PAGES, KK_GATHER, KK_LOOKUP, KK_EMBED, KK_PLAN,
     KK_QKV_G, KK_ATTN_DECODE, KK_PROJ_G, KK_FCIN_G, KK_FCOUT_G, KK_LNF,
     KK_QKV_L, KK_ATTN_LOCAL, KK_PROJ_L, KK_FCIN_L, KK_FCOUT_L, KK_GATE, KK_HEADS, KK_SAMPLE, KK_COMMIT,
+    KK_BIMG,
     KK_COUNT
 };
 const char *kernel_kind_name(int kind);
@@ -82,11 +85,16 @@ public:
     void get_kv(int sid, int layer, int p0, int n, float *k, float *v);
     void get_hidden(int sid, float *out);
     void debug_matrix_bytes(const std::string &name, uint8_t *out, size_t out_bytes);
+    void debug_matrix_tile_bytes(const std::string &name, uint8_t *out, size_t out_bytes);
     void set_cuda_stream(void *s);
     void fill_state_random(int sid, int n_pos, uint64_t seed);
     void set_kernel_timing(bool on);
     void read_kernel_timing(float *total_ms, int *launches, int max_kinds, int *n_kinds) const;
     void set_use_graphs(bool on) { use_graphs_ = on; }
+    // 0 = automatic (tensor cores above kGemvMaxRows rows), 1 = CUDA-core GEMV, 2 = tensor cores
+    void set_gemm_path(int mode);
+    static constexpr int kGemvMaxRows = 8;
+    static constexpr int kTcMaxRows = 256;
     int last_launches() const { return launches_; }
     uint64_t weights_fingerprint() const { return weights_fp_; }
     int device() const { return device_; }
@@ -106,6 +114,10 @@ private:
     QMat qm(const DevMat &m) const;
     EmbedTables tables() const;
     void block(const Layer &L, int li, bool local, int R, const int *row_slot, const int *row_pos, int lpos, float *x);
+    bool use_tc(int R) const;
+    void block_tc(const Layer &L, int li, bool local, int R, const int *row_slot, const int *row_pos, int lpos, float *x);
+    void heads_tc(int ch, int R);
+    void check_device_error();
     void global_layers(int R, const int *row_slot, const int *row_pos);
     void issue_frame(int R, bool run_global);
     void issue_global_embed(int R);
@@ -157,6 +169,11 @@ private:
     float *part_ = nullptr, *gate_ = nullptr;
     int *rows17_ = nullptr;
     int *codes_hist_ = nullptr;  // [kMaxFramesPerCall][max_streams][16] codes of a multi-frame call
+    uint8_t *bimg_a_ = nullptr;    // activation image, K = 768, up to 256 rows
+    uint8_t *bimg_mlp_ = nullptr;  // activation image, K = 3072 (fc_in output -> fc_out input)
+    int *dev_err_ = nullptr;       // tensor-core kernels' time-out flag
+    int *h_err_ = nullptr;         // pinned host copy of it
+    int gemm_path_ = 0;
     int *d_ctl_ = nullptr, *h_ctl_ = nullptr;
     int ctl_ints_ = 0;
     uint8_t *h_out_ = nullptr;

@@ -1,0 +1,446 @@
+// gemm_tc.cuh -- tcgen05 (5th-generation tensor core) W8A16 GEMM for batched rows, sm_100a.
+//
+//   Y[n][m] = sum_k X[n][k] * W[m][k],   W = int8 Q8_0 blocks x fp16 scales, X fp16
+//
+// "Swap AB" so the weight rows form the MMA M dimension (128 per CTA) and the batch rows the
+// N dimension (16..256): D[128][N] fp32 lives in tensor memory (TMEM).  Per K chunk of 64:
+//   - one producer thread bulk-copies (cp.async.bulk, no tensor map, no multicast) the
+//     weight tile's int8 quants (8 KB), its fp16 scales (512 B) and the activation tile
+//     (N x 128 B, already stored in the SWIZZLE_128B K-major image by the previous kernel);
+//   - four dequant warps convert int8 x scale -> fp16 into the A tile (SWIZZLE_128B K-major
+//     image, 16 KB), fence the async proxy and arrive;
+//   - one MMA thread issues four tcgen05.mma.kind::f16 (K = 16 each) and commits to the
+//     stage's "empty" barrier.
+// After the last chunk the same four warps read D back with tcgen05.ld and run the epilogue
+// (bias / RoPE / KV append, GELU into the next GEMM's activation image, residual add, or a
+// plain store).  Every mbarrier wait is bounded: on time-out the kernel records an error code
+// and leaves through the normal exit path (TMEM is always freed).
+//
+// Weight layout (repacked from the file at load, a byte permutation):
+//   qt [rows/128][K/64][128][64] int8, the four 16-byte pieces of each 64-byte row stored at
+//      piece ^ ((row >> 1) & 3) so that the dequant warps read shared memory without bank
+//      conflicts;
+//   st [rows/128][K/64][128][2] fp16 (the scales of blocks 2c and 2c+1 of each row).
+// Activation image ("B image") for N padded rows and K columns:
+//   [K/64][N][128 B], element (n, k) at byte ((k/64)*N + n)*128 + (((k%64)/8) ^ (n%8))*16 + (k%8)*2
+//   -- exactly what a SWIZZLE_128B K-major operand looks like in shared memory.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "types.h"
+
+namespace mossgpu {
+namespace {
+
+constexpr int kTcM = 128;      // weight rows per CTA (MMA M)
+constexpr int kTcK = 64;       // K per pipeline stage (one 128-byte swizzle row of fp16)
+constexpr int kTcThreads = 192;
+constexpr int kTcMaxN = 256;
+
+enum { TC_STORE = 0, TC_QKV = 1, TC_RESID = 2, TC_GELU_B = 3 };
+
+struct TcArgs {
+    const int8_t *qt;       // weight quants, tile layout
+    const __half *st;       // weight scales, tile layout
+    int rows, K;            // weight matrix shape
+    const uint8_t *bimg;    // activation image [K/64][N][128 B]
+    int N;                  // padded batch rows (multiple of 16, <= 256)
+    int R;                  // real batch rows (<= N)
+    int ksplit;             // K chunks per CTA along gridDim.y (split-K, TC_RESID/TC_STORE only)
+    const float *bias;
+    float *out;             // TC_STORE: [R][ldo]; TC_RESID: residual [R][ldo] (atomic add)
+    int ldo;
+    // TC_QKV
+    float *q_out;
+    __half *kv;
+    const int *page_table;
+    int pages_per_stream;
+    float *lkv;
+    const int *row_slot;
+    const int *row_pos;
+    int fixed_pos;
+    const float2 *rope;
+    // TC_GELU_B: output activation image for the next GEMM (K_next = rows)
+    uint8_t *bimg_out;
+    int *err;               // error flag (0 = fine)
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+// Bounded wait for the phase with the given parity.  Returns false (and records `code`)
+// after about a second without progress.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code) {
+    const uint32_t addr = smem_u32(bar);
+    for (uint32_t it = 0; it < (1u << 22); ++it) {
+        uint32_t done;
+        asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+                     : "=r"(done)
+                     : "r"(addr), "r"(parity)
+                     : "memory");
+        if (done) return true;
+        if (it > 64) __nanosleep(256);
+    }
+    atomicCAS(err, 0, code);
+    return false;
+}
+
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    // K-major SWIZZLE_128B canonical layout: 8-row atoms of 1024 B, SBO = 1024 B, LBO unused (1),
+    // descriptor version 1 (sm100), base offset 0 (atoms are 1024-byte aligned)
+    return (uint64_t((saddr >> 4) & 0x3FFF)) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) |
+           (uint64_t(1) << 46) | (uint64_t(2) << 61);
+}
+
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, float *v) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Precision modes.  TC_F16: one MMA per K step on fp16 operands (fp16 rounding of the
+// dequantised weight and of the activation, ~5e-4 relative).  TC_F16X3: each operand is split
+// into a high fp16 part and the fp16 of its remainder (w = w_hi + w_lo, x = x_hi + x_lo) and
+// three MMAs accumulate w_hi.x_hi + w_hi.x_lo + w_lo.x_hi in fp32 -- close to the fp32
+// arithmetic of the reference's W8A16 dot product, at three times the (small) MMA work.
+enum { TC_F16 = 1, TC_F16X3 = 3 };
+
+__host__ __device__ constexpr int tc_parts(int prec) { return prec == TC_F16X3 ? 2 : 1; }
+
+__host__ __device__ constexpr int tc_stage_bytes(int N, int prec) {
+    // [A tiles 16 KB each][B tiles N*128 each][W8 8 KB][scales 512 B], padded to 1 KB so that
+    // every A and B tile starts on a 1 KB boundary
+    return (16384 * tc_parts(prec) + N * 128 * tc_parts(prec) + 8192 + 512 + 1023) / 1024 * 1024;
+}
+
+__host__ __device__ constexpr int tc_stages(int N, int prec) {
+    return (220 * 1024 / tc_stage_bytes(N, prec)) < 4 ? (220 * 1024 / tc_stage_bytes(N, prec)) : 4;
+}
+
+__host__ __device__ constexpr int tc_smem_bytes(int N, int prec) {
+    return tc_stages(N, prec) * tc_stage_bytes(N, prec) + 1024;
+}
+
+// byte offset of element (n, k) in an activation image with N rows
+__device__ __forceinline__ size_t bimg_off(int n, int k, int N) {
+    return ((size_t)(k >> 6) * N + n) * 128 + ((((k & 63) >> 3) ^ (n & 7)) << 4) + ((k & 7) << 1);
+}
+
+template <int EPI, int PREC>
+__global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
+    extern __shared__ uint8_t tc_smem_raw[];
+    __shared__ __align__(8) uint64_t full_bar[4], dq_bar[4], empty_bar[4], acc_bar;
+    __shared__ uint32_t tmem_base_sh;
+    constexpr int NP = tc_parts(PREC);  // operand parts (hi, lo)
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int N = a.N;
+    const int S = tc_stages(N, PREC);
+    const int SB = tc_stage_bytes(N, PREC);
+    // stage layout: [A part 0..NP-1: 16 KB each][B part 0..NP-1: N*128 each][W8 8 KB][scales]
+    const int OFF_B = 16384 * NP;
+    const int OFF_W8 = OFF_B + N * 128 * NP;
+    const int OFF_SC = OFF_W8 + 8192;
+    const size_t bimg_part = (size_t)a.K * N * 2;  // bytes of one activation image part
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
+    const int tile = blockIdx.x;
+    const int nchunks_total = a.K / kTcK;
+    const int c0 = blockIdx.y * a.ksplit;
+    const int c1 = min(nchunks_total, c0 + a.ksplit);
+    const int nch = c1 - c0;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&dq_bar[s], 128);
+            mbar_init(&empty_bar[s], 1);
+        }
+        mbar_init(&acc_bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    uint32_t ncols = 32;
+    while (ncols < (uint32_t)N) ncols <<= 1;
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_sh)),
+                     "r"(ncols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = tmem_base_sh;
+
+    const size_t wtile = (size_t)tile * nchunks_total;  // (tile, chunk) index base
+    if (warp == 0) {
+        // ---------------- producer
+        if (lane == 0 && nch > 0) {
+            int issued = 0;
+            for (int i = 0; i < nch; ++i) {
+                const int s = i % S;
+                if (i >= S && !mbar_wait(&empty_bar[s], ((i / S) - 1) & 1, a.err, 1)) break;
+                uint8_t *st = smem + (size_t)s * SB;
+                const int c = c0 + i;
+                mbar_expect_tx(&full_bar[s], 8192 + 512 + (uint32_t)(N * 128 * NP));
+                bulk_g2s(st + OFF_W8, a.qt + (wtile + c) * 8192, 8192, &full_bar[s]);
+                bulk_g2s(st + OFF_SC, a.st + (wtile + c) * 256, 512, &full_bar[s]);
+#pragma unroll
+                for (int p = 0; p < NP; ++p)
+                    bulk_g2s(st + OFF_B + p * N * 128, a.bimg + p * bimg_part + (size_t)c * N * 128, (uint32_t)N * 128,
+                             &full_bar[s]);
+                ++issued;
+            }
+            // leave only after every copy this CTA issued has landed
+            for (int i = max(0, issued - S); i < issued; ++i) mbar_wait(&full_bar[i % S], (i / S) & 1, a.err, 2);
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer
+        if (lane == 0 && nch > 0) {
+            const uint32_t idesc = (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(kTcM >> 4) << 24);
+            bool ok = true;
+            int done = 0;
+            for (int i = 0; i < nch; ++i) {
+                const int s = i % S;
+                if (!mbar_wait(&dq_bar[s], (i / S) & 1, a.err, 3)) {
+                    ok = false;
+                    break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                uint8_t *st = smem + (size_t)s * SB;
+                const uint32_t abase = smem_u32(st), bbase = smem_u32(st + OFF_B);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    tc_mma(tmem, sw128_desc(abase + k * 32), sw128_desc(bbase + k * 32), idesc, (i > 0 || k > 0) ? 1u : 0u);
+                    if (NP == 2) {  // + w_hi.x_lo + w_lo.x_hi
+                        tc_mma(tmem, sw128_desc(abase + k * 32), sw128_desc(bbase + N * 128 + k * 32), idesc, 1u);
+                        tc_mma(tmem, sw128_desc(abase + 16384 + k * 32), sw128_desc(bbase + k * 32), idesc, 1u);
+                    }
+                }
+                tc_commit(&empty_bar[s]);
+                ++done;
+            }
+            (void)ok;
+            // acc_bar completes when every MMA issued above has finished (also on the error path)
+            tc_commit(&acc_bar);
+        }
+    } else {
+        // ---------------- dequant (then epilogue): warps 2..5, 128 threads
+        const int t = threadIdx.x - 64;  // 0..127: the weight row this thread dequantises
+        bool ok = true;
+        for (int i = 0; i < nch && ok; ++i) {
+            const int s = i % S;
+            if (!mbar_wait(&full_bar[s], (i / S) & 1, a.err, 4)) {
+                ok = false;
+                break;
+            }
+            uint8_t *st = smem + (size_t)s * SB;
+            const int8_t *w8 = reinterpret_cast<const int8_t *>(st + OFF_W8) + t * 64;
+            const __half *sc = reinterpret_cast<const __half *>(st + OFF_SC) + t * 2;
+            const float d0 = __half2float(sc[0]), d1 = __half2float(sc[1]);
+            uint8_t *arow = st + t * 128;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {  // 16-byte piece j of the row = k 16j..16j+15
+                const int4 q = *reinterpret_cast<const int4 *>(w8 + ((j ^ ((t >> 1) & 3)) << 4));
+                const float d = j < 2 ? d0 : d1;
+                const int words[4] = {q.x, q.y, q.z, q.w};
+                __align__(16) __half h[16];
+                __align__(16) __half l[16];
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    // q * d is exact in fp32 (8-bit x 11-bit significands)
+                    const float w = (float)(int8_t)((words[e >> 2] >> (8 * (e & 3))) & 0xff) * d;
+                    h[e] = __float2half_rn(w);
+                    if (NP == 2) l[e] = __float2half_rn(w - __half2float(h[e]));
+                }
+                // k = 16j + e -> 16-byte unit u = 2j (+1), stored at u ^ (t % 8)
+                *reinterpret_cast<int4 *>(arow + (((2 * j) ^ (t & 7)) << 4)) = *reinterpret_cast<const int4 *>(h);
+                *reinterpret_cast<int4 *>(arow + (((2 * j + 1) ^ (t & 7)) << 4)) = *reinterpret_cast<const int4 *>(h + 8);
+                if (NP == 2) {
+                    *reinterpret_cast<int4 *>(arow + 16384 + (((2 * j) ^ (t & 7)) << 4)) =
+                        *reinterpret_cast<const int4 *>(l);
+                    *reinterpret_cast<int4 *>(arow + 16384 + (((2 * j + 1) ^ (t & 7)) << 4)) =
+                        *reinterpret_cast<const int4 *>(l + 8);
+                }
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_arrive(&dq_bar[s]);
+        }
+        // ---------------- epilogue
+        const int q = warp & 3;                 // TMEM lane quarter this warp may read
+        const int m = q * 32 + lane;            // weight row within the tile
+        const int gm = tile * kTcM + m;         // global weight row
+        const bool acc_ok = nch > 0 && mbar_wait(&acc_bar, 0, a.err, 5);
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        if (acc_ok && ok) {
+            for (int n0 = 0; n0 < N; n0 += 16) {
+                float v[16];
+                tc_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)n0, v);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int rr = n0 + j;
+                    float y = v[j];
+                    if (EPI == TC_STORE) {
+                        if (rr < a.R) {
+                            if (a.bias) y = __fadd_rn(y, a.bias[gm]);
+                            a.out[(size_t)rr * a.ldo + gm] = y;
+                        }
+                    } else if (EPI == TC_RESID) {
+                        if (rr < a.R) {
+                            if (blockIdx.y == 0) y = __fadd_rn(y, a.bias[gm]);
+                            atomicAdd(a.out + (size_t)rr * a.ldo + gm, y);
+                        }
+                    } else if (EPI == TC_GELU_B) {
+                        const float g = rr < a.R ? gelu_new(__fadd_rn(y, a.bias[gm])) : 0.f;
+                        const __half gh = __float2half_rn(g);
+                        const size_t off = bimg_off(rr, gm, N);
+                        *reinterpret_cast<__half *>(a.bimg_out + off) = gh;
+                        if (NP == 2)  // the next GEMM's K is this one's rows
+                            *reinterpret_cast<__half *>(a.bimg_out + (size_t)a.rows * N * 2 + off) =
+                                __float2half_rn(g - __half2float(gh));
+                    } else {  // TC_QKV: bias, RoPE on q/k pairs (adjacent lanes), q out / KV append
+                        const float yb = __fadd_rn(y, a.bias[gm]);
+                        const float other = __shfl_xor_sync(0xffffffffu, yb, 1);
+                        if (rr < a.R && (gm & 1) == 0) {
+                            const int pos = a.row_pos ? a.row_pos[rr] : a.fixed_pos;
+                            float o0 = yb, o1 = other;
+                            if (gm < 2 * kHidden) {
+                                const float2 cs = a.rope[(size_t)pos * (kHeadDim / 2) + ((gm % kHeadDim) >> 1)];
+                                o0 = __fsub_rn(__fmul_rn(yb, cs.x), __fmul_rn(other, cs.y));
+                                o1 = __fadd_rn(__fmul_rn(other, cs.x), __fmul_rn(yb, cs.y));
+                            }
+                            if (gm < kHidden) {
+                                a.q_out[(size_t)rr * kHidden + gm] = o0;
+                                a.q_out[(size_t)rr * kHidden + gm + 1] = o1;
+                            } else {
+                                const int kvsel = gm < 2 * kHidden ? 0 : 1;
+                                const int c = gm - kHidden * (1 + kvsel);
+                                const int slot = a.row_slot[rr];
+                                if (a.kv) {
+                                    const int page = a.page_table[(size_t)slot * a.pages_per_stream + pos / kPage];
+                                    __half *dst = a.kv + (size_t)page * kPageHalfs +
+                                                  ((kvsel * kHeads + c / kHeadDim) * kPage + pos % kPage) * kHeadDim +
+                                                  (c % kHeadDim);
+                                    *reinterpret_cast<__half2 *>(dst) = __floats2half2_rn(o0, o1);
+                                } else {
+                                    float *dst = a.lkv + (((size_t)slot * 2 + kvsel) * kLocalLen + pos) * kHidden + c;
+                                    dst[0] = o0;
+                                    dst[1] = o1;
+                                }
+                            }
+                        }
+                    }
+                }
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 1) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols));
+    }
+}
+
+// x fp32 [R][K] (optionally LayerNormed, K = 768) -> activation image with N padded rows;
+// rows R..N-1 are written as zeros.  parts = 2 also writes the image of the fp16 remainders
+// (x - fp16(x)) right after the first one.  One CTA per padded row.
+__global__ void __launch_bounds__(256) k_build_bimg(const float *__restrict__ x, int ldx, int R, int N, int K,
+                                                    const float *__restrict__ ln_w, const float *__restrict__ ln_b,
+                                                    int parts, uint8_t *__restrict__ bimg) {
+    extern __shared__ __align__(16) float xs_b[];
+    const int n = blockIdx.x;
+    const size_t part = (size_t)K * N * 2;
+    if (n >= R) {
+        for (int k = threadIdx.x * 8; k < K; k += blockDim.x * 8)
+            for (int p = 0; p < parts; ++p)
+                *reinterpret_cast<int4 *>(bimg + p * part + bimg_off(n, k, N)) = make_int4(0, 0, 0, 0);
+        return;
+    }
+    for (int k = threadIdx.x; k < K; k += blockDim.x) xs_b[k] = x[(size_t)n * ldx + k];
+    __syncthreads();
+    if (ln_w) {
+        if (threadIdx.x < 32) warp_layernorm(xs_b, ln_w, ln_b);
+        __syncthreads();
+    }
+    for (int k = threadIdx.x * 8; k < K; k += blockDim.x * 8) {
+        __align__(16) __half h[8];
+        __align__(16) __half l[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            h[e] = __float2half_rn(xs_b[k + e]);
+            l[e] = __float2half_rn(xs_b[k + e] - __half2float(h[e]));
+        }
+        *reinterpret_cast<int4 *>(bimg + bimg_off(n, k, N)) = *reinterpret_cast<const int4 *>(h);
+        if (parts == 2) *reinterpret_cast<int4 *>(bimg + part + bimg_off(n, k, N)) = *reinterpret_cast<const int4 *>(l);
+    }
+}
+
+// File bytes of one Q8_0_4X4 matrix -> tile layout (qt, st).  One thread per (row, block).
+__global__ void k_repack_tiles(const uint8_t *__restrict__ src, int rows, int K, int8_t *__restrict__ qt,
+                               __half *__restrict__ st) {
+    const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const int nb = K / 32;
+    if (t >= (long long)rows * nb) return;
+    const int m = int(t / nb), b = int(t % nb);
+    const uint8_t *blk = src + ((size_t)(m >> 2) * nb + b) * 136;
+    const int k4 = m & 3;
+    const int tile = m / kTcM, mm = m % kTcM, c = b >> 1, hb = b & 1;
+    const size_t base = ((size_t)tile * (K / kTcK) + c) * kTcM + mm;
+    int8_t *row = qt + base * 64;
+    const uint8_t *qs = blk + 8 + k4 * 32;  // 8-byte aligned
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {  // 16-byte piece j = 2*hb + p
+        const int j = 2 * hb + p;
+        const uint2 lo = *reinterpret_cast<const uint2 *>(qs + 16 * p);
+        const uint2 hi = *reinterpret_cast<const uint2 *>(qs + 16 * p + 8);
+        int8_t *dst = row + ((j ^ ((mm >> 1) & 3)) << 4);
+        *reinterpret_cast<uint2 *>(dst) = lo;
+        *reinterpret_cast<uint2 *>(dst + 8) = hi;
+    }
+    uint16_t d;
+    memcpy(&d, blk + k4 * 2, 2);
+    reinterpret_cast<uint16_t *>(st)[base * 2 + hb] = d;
+}
+
+}  // namespace
+}  // namespace mossgpu

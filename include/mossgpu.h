@@ -120,8 +120,16 @@ int mossgpu_last_launch_count(mossgpu_engine *e);
 int mossgpu_fill_state_random(mossgpu_engine *e, int stream_id, int n_pos, uint64_t seed);
 
 /* Execution options: graphs = 1 (default) replays each frame as a CUDA graph captured on
- * first use per batch size; 0 launches kernels one by one. */
+ * first use per batch size; 0 launches kernels one by one.
+ * gemm_path: 0 = automatic (CUDA-core GEMV up to 8 rows, tcgen05 tensor-core GEMM for 9..256
+ * rows), 1 = always the CUDA-core GEMV, 2 = tensor cores whenever rows <= 256, 3 = as 2 but
+ * with single fp16 operands instead of the default hi/lo fp16 split (faster, ~5e-4 relative
+ * rounding on weights and activations; the default split keeps fp32-level accuracy). */
 int mossgpu_set_graphs(mossgpu_engine *e, int enable);
+int mossgpu_set_gemm_path(mossgpu_engine *e, int mode);
+
+/* Same as mossgpu_debug_matrix_bytes for the tensor-core tile copy of the matrix. */
+int mossgpu_debug_matrix_tile_bytes(mossgpu_engine *e, const char *name, uint8_t *out, size_t out_bytes);
 
 /* Per-kernel device timing, measured with CUDA events recorded between the kernels of the
  * captured frame.  enable = 1 clears the totals and starts accumulating; read returns, per
