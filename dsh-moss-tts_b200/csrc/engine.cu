@@ -7,6 +7,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <fstream>
@@ -61,6 +62,7 @@ Engine::Engine(const std::string &path, int device, int max_streams, int max_ctx
     CK(cudaSetDevice(device));
     CK(cudaStreamCreateWithFlags(&own_stream_, cudaStreamNonBlocking));
     stream_ = own_stream_;
+    if (const char *v = std::getenv("MOSSGPU_PDL")) pdl_ = std::strcmp(v, "0") != 0;
     load_weights(path);
     pages_per_stream_ = (max_ctx + kPage - 1) / kPage;
     n_pages_ = kv_pages > 0 ? kv_pages : max_streams * pages_per_stream_;
@@ -260,6 +262,29 @@ void Engine::allocate_state() {
     CK(cudaDeviceSynchronize());
 }
 
+namespace {
+
+// Kernel launch with programmatic dependent launch (PDL) allowed: the kernel may begin while
+// the previous kernel on the stream is still running, and orders itself with pdl_wait()
+// (every kernel of the frame calls it before touching data an earlier kernel produced).
+template <typename... KArgs, typename... Args>
+void launch_k(bool pdl, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+              Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    CK(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+}
+
+}  // namespace
+
 // ------------------------------------------------------------------ GEMV launch
 
 namespace {
@@ -288,24 +313,24 @@ void set_attr_all() {
 }
 
 template <int PRO, int EPI, int MAXR>
-void launch_gemv_r(const GemvArgs &a, cudaStream_t st) {
+void launch_gemv_r(const GemvArgs &a, cudaStream_t st, bool pdl) {
     const GemvShape s{a.ks, a.gpc};
     const int warps = s.ks * s.gpc;
     const int groups = a.w.rows / 4;
     dim3 grid((groups + s.gpc - 1) / s.gpc, (a.nrows + MAXR - 1) / MAXR);
     const size_t smem = (size_t(MAXR) * a.w.cols + size_t(warps) * 4 * MAXR + size_t(s.gpc) * 4 * MAXR) * sizeof(float);
-    k_gemv<PRO, EPI, MAXR><<<grid, warps * 32, smem, st>>>(a);
+    launch_k(pdl, k_gemv<PRO, EPI, MAXR>, grid, dim3(warps * 32), smem, st, a);
 }
 
 template <int PRO, int EPI>
-void launch_gemv(GemvArgs a, cudaStream_t st) {
+void launch_gemv(GemvArgs a, cudaStream_t st, bool pdl) {
     const GemvShape s = shape_for(a.w.cols);
     a.ks = s.ks;
     a.gpc = s.gpc;
-    if (a.nrows <= 1) launch_gemv_r<PRO, EPI, 1>(a, st);
-    else if (a.nrows <= 2) launch_gemv_r<PRO, EPI, 2>(a, st);
-    else if (a.nrows <= 4) launch_gemv_r<PRO, EPI, 4>(a, st);
-    else launch_gemv_r<PRO, EPI, 8>(a, st);
+    if (a.nrows <= 1) launch_gemv_r<PRO, EPI, 1>(a, st, pdl);
+    else if (a.nrows <= 2) launch_gemv_r<PRO, EPI, 2>(a, st, pdl);
+    else if (a.nrows <= 4) launch_gemv_r<PRO, EPI, 4>(a, st, pdl);
+    else launch_gemv_r<PRO, EPI, 8>(a, st, pdl);
 }
 
 }  // namespace
@@ -346,15 +371,21 @@ bool Engine::use_tc(int R) const {
 
 namespace {
 
+// Grid: weight tiles x K splits x batch splits.  Splitting the batch rows (nsub per CTA)
+// multiplies the CTAs that stream weights in parallel -- at 64 rows a QKV GEMM has only 18
+// weight tiles -- at the price of reading each weight tile once per batch split (from L2).
 template <int EPI>
-void launch_tc(TcArgs a, int ksplit, int prec, cudaStream_t st) {
+void launch_tc(TcArgs a, int ksplit, int prec, cudaStream_t st, bool pdl) {
     const int nchunks = a.K / kTcK;
     a.ksplit = ksplit;
-    dim3 grid(a.rows / kTcM, (nchunks + ksplit - 1) / ksplit);
+    int nsub = a.N <= 128 ? 32 : 64;
+    while (a.N % nsub) nsub >>= 1;  // N is a multiple of 16
+    a.nsub = nsub;
+    dim3 grid(a.rows / kTcM, (nchunks + ksplit - 1) / ksplit, a.N / nsub);
     if (prec == TC_F16X3)
-        k_gemm_tc<EPI, TC_F16X3><<<grid, kTcThreads, tc_smem_bytes(a.N, TC_F16X3), st>>>(a);
+        launch_k(pdl, k_gemm_tc<EPI, TC_F16X3>, grid, dim3(kTcThreads), tc_smem_bytes(nsub, TC_F16X3), st, a);
     else
-        k_gemm_tc<EPI, TC_F16><<<grid, kTcThreads, tc_smem_bytes(a.N, TC_F16), st>>>(a);
+        launch_k(pdl, k_gemm_tc<EPI, TC_F16>, grid, dim3(kTcThreads), tc_smem_bytes(nsub, TC_F16), st, a);
 }
 
 }  // namespace
@@ -366,7 +397,7 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
                       float *x) {
     const int N = (R + 15) / 16 * 16;
     const int prec = gemm_path_ == 3 ? TC_F16 : TC_F16X3;
-    k_build_bimg<<<N, 256, kHidden * 4, stream_>>>(x, kHidden, R, N, kHidden, L.ln1_w, L.ln1_b, tc_parts(prec), bimg_a_);
+    launch_k(pdl_, k_build_bimg, dim3(N), dim3(256), kHidden * 4, stream_, x, kHidden, R, N, kHidden, L.ln1_w, L.ln1_b, tc_parts(prec), bimg_a_);
     mark(KK_BIMG);
     TcArgs a{};
     a.N = N;
@@ -390,11 +421,11 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
         a.page_table = page_table_;
         a.pages_per_stream = pages_per_stream_;
     }
-    launch_tc<TC_QKV>(a, kHidden / kTcK, prec, stream_);
+    launch_tc<TC_QKV>(a, kHidden / kTcK, prec, stream_, pdl_);
     mark(local ? KK_QKV_L : KK_QKV_G);
     if (local) {
         const int warps = R * kHeads;
-        k_attn_local<<<(warps + 11) / 12, 384, 0, stream_>>>(q_, lkv_, row_slot, lpos, R, attn_);
+        launch_k(pdl_, k_attn_local, dim3((warps + 11) / 12), dim3(384), 0, stream_, q_, lkv_, row_slot, lpos, R, attn_);
         mark(KK_ATTN_LOCAL);
     } else {
         AttnArgs t{};
@@ -409,11 +440,19 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
         t.part = part_;
         t.counter = counter_;
         t.out = attn_;
-        k_attn_decode<<<kAttnGrid, 256, 0, stream_>>>(t);
+        // straight into proj's activation image; its padding rows are still zero from the
+        // LN1 image built above with the same N
+        t.bimg = bimg_a_;
+        t.bimg_N = N;
+        t.bimg_parts = tc_parts(prec);
+        launch_k(pdl_, k_attn_decode, dim3(kAttnGrid), dim3(256), 0, stream_, t);
         mark(KK_ATTN_DECODE);
     }
-    k_build_bimg<<<N, 256, kHidden * 4, stream_>>>(attn_, kHidden, R, N, kHidden, nullptr, nullptr, tc_parts(prec), bimg_a_);
-    mark(KK_BIMG);
+    if (local) {
+        launch_k(pdl_, k_build_bimg, dim3(N), dim3(256), kHidden * 4, stream_, attn_, kHidden, R, N, kHidden, nullptr, nullptr, tc_parts(prec),
+                                                       bimg_a_);
+        mark(KK_BIMG);
+    }
     TcArgs p{};
     p.N = N;
     p.R = R;
@@ -426,9 +465,9 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
     p.bias = L.proj_b;
     p.out = x;
     p.ldo = kHidden;
-    launch_tc<TC_RESID>(p, 3, prec, stream_);  // 6 tiles x 4 K-splits
+    launch_tc<TC_RESID>(p, 3, prec, stream_, pdl_);  // 6 tiles x 4 K-splits
     mark(local ? KK_PROJ_L : KK_PROJ_G);
-    k_build_bimg<<<N, 256, kHidden * 4, stream_>>>(x, kHidden, R, N, kHidden, L.ln2_w, L.ln2_b, tc_parts(prec), bimg_a_);
+    launch_k(pdl_, k_build_bimg, dim3(N), dim3(256), kHidden * 4, stream_, x, kHidden, R, N, kHidden, L.ln2_w, L.ln2_b, tc_parts(prec), bimg_a_);
     mark(KK_BIMG);
     TcArgs f{};
     f.N = N;
@@ -441,7 +480,7 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
     f.K = kHidden;
     f.bias = L.fc_in_b;
     f.bimg_out = bimg_mlp_;
-    launch_tc<TC_GELU_B>(f, kHidden / kTcK, prec, stream_);
+    launch_tc<TC_GELU_B>(f, kHidden / kTcK, prec, stream_, pdl_);
     mark(local ? KK_FCIN_L : KK_FCIN_G);
     TcArgs o{};
     o.N = N;
@@ -455,7 +494,7 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
     o.bias = L.fc_out_b;
     o.out = x;
     o.ldo = kHidden;
-    launch_tc<TC_RESID>(o, 6, prec, stream_);  // 6 tiles x 8 K-splits
+    launch_tc<TC_RESID>(o, 6, prec, stream_, pdl_);  // 6 tiles x 8 K-splits
     mark(local ? KK_FCOUT_L : KK_FCOUT_G);
 }
 
@@ -463,7 +502,7 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
 void Engine::heads_tc(int ch, int R) {
     const int N = (R + 15) / 16 * 16;
     const int prec = gemm_path_ == 3 ? TC_F16 : TC_F16X3;
-    k_build_bimg<<<N, 256, kHidden * 4, stream_>>>(lx_, kHidden, R, N, kHidden, llnf_w_, llnf_b_, tc_parts(prec), bimg_a_);
+    launch_k(pdl_, k_build_bimg, dim3(N), dim3(256), kHidden * 4, stream_, lx_, kHidden, R, N, kHidden, llnf_w_, llnf_b_, tc_parts(prec), bimg_a_);
     mark(KK_BIMG);
     TcArgs h{};
     h.N = N;
@@ -476,7 +515,7 @@ void Engine::heads_tc(int ch, int R) {
     h.K = kHidden;
     h.out = logits_ + size_t(ch) * kCodebook;
     h.ldo = kNVq * kCodebook;
-    launch_tc<TC_STORE>(h, kHidden / kTcK, prec, stream_);
+    launch_tc<TC_STORE>(h, kHidden / kTcK, prec, stream_, pdl_);
     mark(KK_HEADS);
 }
 
@@ -533,12 +572,12 @@ void Engine::block(const Layer &L, int li, bool local, int R, const int *row_slo
         a.page_table = page_table_;
         a.pages_per_stream = pages_per_stream_;
     }
-    launch_gemv<PRO_LN, EPI_QKV>(a, stream_);
+    launch_gemv<PRO_LN, EPI_QKV>(a, stream_, pdl_);
     mark(local ? KK_QKV_L : KK_QKV_G);
     // attention
     if (local) {
         const int warps = R * kHeads;
-        k_attn_local<<<(warps + 11) / 12, 384, 0, stream_>>>(q_, lkv_, row_slot, lpos, R, attn_);
+        launch_k(pdl_, k_attn_local, dim3((warps + 11) / 12), dim3(384), 0, stream_, q_, lkv_, row_slot, lpos, R, attn_);
         mark(KK_ATTN_LOCAL);
     } else {
         AttnArgs t{};
@@ -553,7 +592,7 @@ void Engine::block(const Layer &L, int li, bool local, int R, const int *row_slo
         t.part = part_;
         t.counter = counter_;
         t.out = attn_;
-        k_attn_decode<<<kAttnGrid, 256, 0, stream_>>>(t);
+        launch_k(pdl_, k_attn_decode, dim3(kAttnGrid), dim3(256), 0, stream_, t);
         mark(KK_ATTN_DECODE);
     }
     // proj + residual
@@ -565,7 +604,7 @@ void Engine::block(const Layer &L, int li, bool local, int R, const int *row_slo
     p.ldx = kHidden;
     p.out = x;
     p.ldo = kHidden;
-    launch_gemv<PRO_NONE, EPI_RESID>(p, stream_);
+    launch_gemv<PRO_NONE, EPI_RESID>(p, stream_, pdl_);
     mark(local ? KK_PROJ_L : KK_PROJ_G);
     // LN2 -> fc_in + gelu
     GemvArgs f{};
@@ -578,7 +617,7 @@ void Engine::block(const Layer &L, int li, bool local, int R, const int *row_slo
     f.ln_b = L.ln2_b;
     f.out = mlp_;
     f.ldo = kFF;
-    launch_gemv<PRO_LN, EPI_GELU>(f, stream_);
+    launch_gemv<PRO_LN, EPI_GELU>(f, stream_, pdl_);
     mark(local ? KK_FCIN_L : KK_FCIN_G);
     // fc_out + residual
     GemvArgs o{};
@@ -589,13 +628,14 @@ void Engine::block(const Layer &L, int li, bool local, int R, const int *row_slo
     o.ldx = kFF;
     o.out = x;
     o.ldo = kHidden;
-    launch_gemv<PRO_NONE, EPI_RESID>(o, stream_);
+    launch_gemv<PRO_NONE, EPI_RESID>(o, stream_, pdl_);
     mark(local ? KK_FCOUT_L : KK_FCOUT_G);
 }
 
 // 12 global layers over rows already embedded in x_ (row_pos = positions being written).
 void Engine::global_layers(int R, const int *row_slot, const int *row_pos) {
-    k_attn_plan<<<1, 32, 0, stream_>>>(row_pos, R, kAttnItems, plan_);
+    // ordinary launch: in a global step alone this kernel follows a host-to-device copy
+    launch_k(false, k_attn_plan, dim3(1), dim3(32), 0, stream_, row_pos, R, kAttnItems, plan_);
     mark(KK_PLAN);
     for (int li = 0; li < kLayers; ++li) block(global_[li], li, false, R, row_slot, row_pos, 0, x_);
 }
@@ -694,7 +734,7 @@ void Engine::prefill_common(int sid, int m, int start, const int32_t *rows, cons
         if (rows) {
             CK(cudaMemcpyAsync(rows17_, rows + size_t(c0) * (kNVq + 1), size_t(R) * (kNVq + 1) * sizeof(int),
                                cudaMemcpyHostToDevice, stream_));
-            k_embed_rows<<<R, 256, 0, stream_>>>(tables(), rows17_, R, x_);
+            launch_k(false, k_embed_rows, dim3(R), dim3(256), 0, stream_, tables(), rows17_, R, x_);
         } else {
             CK(cudaMemcpyAsync(x_, xin + size_t(c0) * kHidden, size_t(R) * kHidden * sizeof(float),
                                cudaMemcpyHostToDevice, stream_));
@@ -702,7 +742,7 @@ void Engine::prefill_common(int sid, int m, int start, const int32_t *rows, cons
         global_layers(R, d_ctl_, d_ctl_ + r_max_);
         if (c0 + R == m) {
             // ln_f of the last row becomes the stream's hidden state (llm.cpp:395-399)
-            k_layernorm_rows<<<1, 256, 0, stream_>>>(x_ + size_t(R - 1) * kHidden, 1, lnf_w_, lnf_b_,
+            launch_k(pdl_, k_layernorm_rows, dim3(1), dim3(256), 0, stream_, x_ + size_t(R - 1) * kHidden, 1, lnf_w_, lnf_b_,
                                                      hidden_ + size_t(sid) * kHidden, nullptr, nullptr);
         }
         CK(cudaGetLastError());
@@ -895,7 +935,7 @@ void Engine::global_step_embed(const int32_t *sids, int n, const float *x, float
     run_captured((uint64_t(2) << 40) | uint64_t(n), [&] { issue_global_embed(n); });
     float *h = reinterpret_cast<float *>(h_out_);
     if (hidden_out) {
-        k_gather_rows<<<n, 256, 0, stream_>>>(hidden_, d_ctl_, n, q_);
+        launch_k(false, k_gather_rows, dim3(n), dim3(256), 0, stream_, hidden_, d_ctl_, n, q_);
         CK(cudaMemcpyAsync(h, q_, size_t(n) * kHidden * sizeof(float), cudaMemcpyDeviceToHost, stream_));
     }
     CK(cudaMemcpyAsync(h_err_, dev_err_, sizeof(int), cudaMemcpyDeviceToHost, stream_));
@@ -915,16 +955,16 @@ void Engine::issue_frame(int R, bool run_global) {
     k_page_updates<<<unsigned((R + 127) / 128), 128, 0, stream_>>>(d_ctl_ + off_pages(), page_table_, pages_per_stream_);
     mark(KK_PAGES);
     // ---- local decoder: 17 steps (llm.cpp:648-698)
-    k_gather_rows<<<R, 256, 0, stream_>>>(hidden_, d_slot, R, lx_);
+    launch_k(pdl_, k_gather_rows, dim3(R), dim3(256), 0, stream_, hidden_, d_slot, R, lx_);
     mark(KK_GATHER);
     for (int ls = 0; ls < kLocalLen; ++ls) {
         if (ls == 1) {
-            k_lookup_rows<<<R, 256, 0, stream_>>>(qm(wte_), kSlotToken, R, lx_);
+            launch_k(pdl_, k_lookup_rows, dim3(R), dim3(256), 0, stream_, qm(wte_), kSlotToken, R, lx_);
             mark(KK_LOOKUP);
         }
         block(local_, 0, true, R, d_slot, nullptr, ls, lx_);
         if (ls == 0) {
-            k_gate<<<R, 256, 0, stream_>>>(lx_, R, llnf_w_, llnf_b_, qm(wte_), d_frame, d_fc,
+            launch_k(pdl_, k_gate, dim3(R), dim3(256), 0, stream_, lx_, R, llnf_w_, llnf_b_, qm(wte_), d_frame, d_fc,
                                            d_ctl_ + off_active_in(), active_, gate_);
             mark(KK_GATE);
         } else {
@@ -941,10 +981,10 @@ void Engine::issue_frame(int R, bool run_global) {
                 h.ln_b = llnf_b_;
                 h.out = logits_ + size_t(ch) * kCodebook;
                 h.ldo = kNVq * kCodebook;
-                launch_gemv<PRO_LN, EPI_STORE>(h, stream_);
+                launch_gemv<PRO_LN, EPI_STORE>(h, stream_, pdl_);
                 mark(KK_HEADS);
             }
-            k_sample_greedy<<<R, 256, 0, stream_>>>(logits_ + size_t(ch) * kCodebook, kNVq * kCodebook, ch, d_slot, R,
+            launch_k(pdl_, k_sample_greedy, dim3(R), dim3(256), 0, stream_, logits_ + size_t(ch) * kCodebook, kNVq * kCodebook, ch, d_slot, R,
                                                    counts_, d_fc, d_forced, active_, codes_, used_, qm(aemb_[ch]),
                                                    ch + 1 < kNVq ? lx_ : nullptr);
             mark(KK_SAMPLE);
@@ -952,13 +992,13 @@ void Engine::issue_frame(int R, bool run_global) {
     }
     // ---- global step on [9, used codes] (llm.cpp:703-708)
     if (run_global) {
-        k_embed_frame<<<R, 256, 0, stream_>>>(tables(), used_, R, x_);
+        launch_k(pdl_, k_embed_frame, dim3(R), dim3(256), 0, stream_, tables(), used_, R, x_);
         mark(KK_EMBED);
         global_layers(R, d_slot, d_pos);
-        k_layernorm_rows<<<R, 256, 0, stream_>>>(x_, R, lnf_w_, lnf_b_, hidden_, d_slot, active_);
+        launch_k(pdl_, k_layernorm_rows, dim3(R), dim3(256), 0, stream_, x_, R, lnf_w_, lnf_b_, hidden_, d_slot, active_);
         mark(KK_LNF);
     }
-    k_frame_commit<<<1, 256, 0, stream_>>>(codes_, active_, R, run_global ? 1 : 0, d_ctl_ + off_pos(),
+    launch_k(pdl_, k_frame_commit, dim3(1), dim3(256), 0, stream_, codes_, active_, R, run_global ? 1 : 0, d_ctl_ + off_pos(),
                                            d_ctl_ + off_frame(), d_ctl_ + off_active_in(), d_ctl_ + off_fslot(),
                                            kMaxFramesPerCall, codes_hist_);
     mark(KK_COMMIT);
@@ -967,7 +1007,7 @@ void Engine::issue_frame(int R, bool run_global) {
 // 12 global layers + ln_f on embeddings already in x_ (llm.cpp:248-255).
 void Engine::issue_global_embed(int R) {
     global_layers(R, d_ctl_ + off_slot(), d_ctl_ + off_pos());
-    k_layernorm_rows<<<R, 256, 0, stream_>>>(x_, R, lnf_w_, lnf_b_, hidden_, d_ctl_ + off_slot(), nullptr);
+    launch_k(pdl_, k_layernorm_rows, dim3(R), dim3(256), 0, stream_, x_, R, lnf_w_, lnf_b_, hidden_, d_ctl_ + off_slot(), nullptr);
     mark(KK_LNF);
 }
 

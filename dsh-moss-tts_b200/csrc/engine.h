@@ -182,8 +182,9 @@ private:
     std::vector<int> free_pages_;
     int launches_ = 0;
 
-    // CUDA graphs and per-kernel timing
+    // CUDA graphs, programmatic dependent launch and per-kernel timing
     bool use_graphs_ = true;
+    bool pdl_ = true;  // MOSSGPU_PDL=0 in the environment turns it off (A/B measurements)
     bool timing_ = false;
     std::unordered_map<uint64_t, CapturedGraph> graphs_;
     CapturedGraph *capturing_ = nullptr;

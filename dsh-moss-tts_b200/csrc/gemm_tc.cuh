@@ -46,7 +46,8 @@ struct TcArgs {
     const __half *st;       // weight scales, tile layout
     int rows, K;            // weight matrix shape
     const uint8_t *bimg;    // activation image [K/64][N][128 B]
-    int N;                  // padded batch rows (multiple of 16, <= 256)
+    int N;                  // padded batch rows (multiple of 16, <= 256): rows of the activation image
+    int nsub;               // batch rows per CTA along gridDim.z (divides N, multiple of 16)
     int R;                  // real batch rows (<= N)
     int ksplit;             // K chunks per CTA along gridDim.y (split-K, TC_RESID/TC_STORE only)
     const float *bias;
@@ -163,24 +164,23 @@ __host__ __device__ constexpr int tc_smem_bytes(int N, int prec) {
     return tc_stages(N, prec) * tc_stage_bytes(N, prec) + 1024;
 }
 
-// byte offset of element (n, k) in an activation image with N rows
-__device__ __forceinline__ size_t bimg_off(int n, int k, int N) {
-    return ((size_t)(k >> 6) * N + n) * 128 + ((((k & 63) >> 3) ^ (n & 7)) << 4) + ((k & 7) << 1);
-}
 
 template <int EPI, int PREC>
 __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
     extern __shared__ uint8_t tc_smem_raw[];
-    __shared__ __align__(8) uint64_t full_bar[4], dq_bar[4], empty_bar[4], acc_bar;
+    __shared__ __align__(8) uint64_t full_bar[4], bfull_bar[4], dq_bar[4], empty_bar[4], acc_bar;
     __shared__ uint32_t tmem_base_sh;
+    __shared__ int s_pos[kTcMaxN], s_dst[kTcMaxN];  // TC_QKV: per batch row position and page/slot
     constexpr int NP = tc_parts(PREC);  // operand parts (hi, lo)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int N = a.N;
-    const int S = tc_stages(N, PREC);
-    const int SB = tc_stage_bytes(N, PREC);
-    // stage layout: [A part 0..NP-1: 16 KB each][B part 0..NP-1: N*128 each][W8 8 KB][scales]
+    const int N = a.N;                  // rows of the activation image
+    const int NS = a.nsub;              // rows handled by this CTA (MMA N)
+    const int r0 = blockIdx.z * NS;     // first batch row of this CTA
+    const int S = tc_stages(NS, PREC);
+    const int SB = tc_stage_bytes(NS, PREC);
+    // stage layout: [A part 0..NP-1: 16 KB each][B part 0..NP-1: NS*128 each][W8 8 KB][scales]
     const int OFF_B = 16384 * NP;
-    const int OFF_W8 = OFF_B + N * 128 * NP;
+    const int OFF_W8 = OFF_B + NS * 128 * NP;
     const int OFF_SC = OFF_W8 + 8192;
     const size_t bimg_part = (size_t)a.K * N * 2;  // bytes of one activation image part
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
@@ -192,7 +192,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
-            mbar_init(&full_bar[s], 1);
+            mbar_init(&full_bar[s], 1);   // weight quants + scales of the stage landed
+            mbar_init(&bfull_bar[s], 1);  // activation tile(s) of the stage landed
             mbar_init(&dq_bar[s], 128);
             mbar_init(&empty_bar[s], 1);
         }
@@ -200,7 +201,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     uint32_t ncols = 32;
-    while (ncols < (uint32_t)N) ncols <<= 1;
+    while (ncols < (uint32_t)NS) ncols <<= 1;
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_sh)),
                      "r"(ncols));
@@ -215,36 +216,53 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
     if (warp == 0) {
         // ---------------- producer
         if (lane == 0 && nch > 0) {
-            int issued = 0;
-            for (int i = 0; i < nch; ++i) {
+            auto load_w = [&](int i) {
                 const int s = i % S;
-                if (i >= S && !mbar_wait(&empty_bar[s], ((i / S) - 1) & 1, a.err, 1)) break;
                 uint8_t *st = smem + (size_t)s * SB;
                 const int c = c0 + i;
-                mbar_expect_tx(&full_bar[s], 8192 + 512 + (uint32_t)(N * 128 * NP));
+                mbar_expect_tx(&full_bar[s], 8192 + 512);
                 bulk_g2s(st + OFF_W8, a.qt + (wtile + c) * 8192, 8192, &full_bar[s]);
                 bulk_g2s(st + OFF_SC, a.st + (wtile + c) * 256, 512, &full_bar[s]);
+            };
+            auto load_b = [&](int i) {
+                const int s = i % S;
+                uint8_t *st = smem + (size_t)s * SB;
+                const int c = c0 + i;
+                mbar_expect_tx(&bfull_bar[s], (uint32_t)(NS * 128 * NP));
 #pragma unroll
                 for (int p = 0; p < NP; ++p)
-                    bulk_g2s(st + OFF_B + p * N * 128, a.bimg + p * bimg_part + (size_t)c * N * 128, (uint32_t)N * 128,
-                             &full_bar[s]);
+                    bulk_g2s(st + OFF_B + p * NS * 128, a.bimg + p * bimg_part + ((size_t)c * N + r0) * 128,
+                             (uint32_t)NS * 128, &bfull_bar[s]);
+            };
+            // weights are static: the first stages are fetched (and dequantised) while the
+            // kernel that produces the activations may still be running
+            const int pre = min(S, nch);
+            for (int i = 0; i < pre; ++i) load_w(i);
+            pdl_wait();
+            pdl_trigger();
+            for (int i = 0; i < pre; ++i) load_b(i);
+            int issued = pre;
+            for (int i = pre; i < nch; ++i) {
+                const int s = i % S;
+                if (!mbar_wait(&empty_bar[s], ((i / S) - 1) & 1, a.err, 1)) break;
+                load_w(i);
+                load_b(i);
                 ++issued;
             }
             // leave only after every copy this CTA issued has landed
-            for (int i = max(0, issued - S); i < issued; ++i) mbar_wait(&full_bar[i % S], (i / S) & 1, a.err, 2);
+            for (int i = max(0, issued - S); i < issued; ++i) {
+                mbar_wait(&full_bar[i % S], (i / S) & 1, a.err, 2);
+                mbar_wait(&bfull_bar[i % S], (i / S) & 1, a.err, 2);
+            }
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer
         if (lane == 0 && nch > 0) {
-            const uint32_t idesc = (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(kTcM >> 4) << 24);
-            bool ok = true;
-            int done = 0;
+            const uint32_t idesc = (1u << 4) | ((uint32_t)(NS >> 3) << 17) | ((uint32_t)(kTcM >> 4) << 24);
             for (int i = 0; i < nch; ++i) {
                 const int s = i % S;
-                if (!mbar_wait(&dq_bar[s], (i / S) & 1, a.err, 3)) {
-                    ok = false;
-                    break;
-                }
+                if (!mbar_wait(&dq_bar[s], (i / S) & 1, a.err, 3)) break;
+                if (!mbar_wait(&bfull_bar[s], (i / S) & 1, a.err, 6)) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 uint8_t *st = smem + (size_t)s * SB;
                 const uint32_t abase = smem_u32(st), bbase = smem_u32(st + OFF_B);
@@ -252,14 +270,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
                 for (int k = 0; k < 4; ++k) {
                     tc_mma(tmem, sw128_desc(abase + k * 32), sw128_desc(bbase + k * 32), idesc, (i > 0 || k > 0) ? 1u : 0u);
                     if (NP == 2) {  // + w_hi.x_lo + w_lo.x_hi
-                        tc_mma(tmem, sw128_desc(abase + k * 32), sw128_desc(bbase + N * 128 + k * 32), idesc, 1u);
+                        tc_mma(tmem, sw128_desc(abase + k * 32), sw128_desc(bbase + NS * 128 + k * 32), idesc, 1u);
                         tc_mma(tmem, sw128_desc(abase + 16384 + k * 32), sw128_desc(bbase + k * 32), idesc, 1u);
                     }
                 }
                 tc_commit(&empty_bar[s]);
-                ++done;
             }
-            (void)ok;
             // acc_bar completes when every MMA issued above has finished (also on the error path)
             tc_commit(&acc_bar);
         }
@@ -306,65 +322,89 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
             mbar_arrive(&dq_bar[s]);
         }
         // ---------------- epilogue
+        pdl_wait();  // from here on this warp touches data of earlier kernels (outputs, row metadata)
+        if (EPI == TC_QKV) {
+            // per-row position and KV page (or local slot), fetched once per CTA
+            for (int j = t; j < NS; j += 128) {
+                const int rr = r0 + j;
+                int pos = 0, dst = 0;
+                if (rr < a.R) {
+                    pos = a.row_pos ? a.row_pos[rr] : a.fixed_pos;
+                    const int slot = a.row_slot[rr];
+                    dst = a.kv ? a.page_table[(size_t)slot * a.pages_per_stream + pos / kPage] : slot;
+                }
+                s_pos[j] = pos;
+                s_dst[j] = dst;
+            }
+            asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps only
+        }
         const int q = warp & 3;                 // TMEM lane quarter this warp may read
         const int m = q * 32 + lane;            // weight row within the tile
         const int gm = tile * kTcM + m;         // global weight row
         const bool acc_ok = nch > 0 && mbar_wait(&acc_bar, 0, a.err, 5);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         if (acc_ok && ok) {
-            for (int n0 = 0; n0 < N; n0 += 16) {
+            const float bias = a.bias ? a.bias[gm] : 0.f;
+            for (int n0 = 0; n0 < NS; n0 += 16) {
                 float v[16];
                 tc_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)n0, v);
+                if (EPI == TC_STORE) {
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int rr = n0 + j;
-                    float y = v[j];
-                    if (EPI == TC_STORE) {
-                        if (rr < a.R) {
-                            if (a.bias) y = __fadd_rn(y, a.bias[gm]);
-                            a.out[(size_t)rr * a.ldo + gm] = y;
-                        }
-                    } else if (EPI == TC_RESID) {
-                        if (rr < a.R) {
-                            if (blockIdx.y == 0) y = __fadd_rn(y, a.bias[gm]);
-                            atomicAdd(a.out + (size_t)rr * a.ldo + gm, y);
-                        }
-                    } else if (EPI == TC_GELU_B) {
-                        const float g = rr < a.R ? gelu_new(__fadd_rn(y, a.bias[gm])) : 0.f;
+                    for (int j = 0; j < 16; ++j) {
+                        const int rr = r0 + n0 + j;
+                        if (rr < a.R) a.out[(size_t)rr * a.ldo + gm] = a.bias ? __fadd_rn(v[j], bias) : v[j];
+                    }
+                } else if (EPI == TC_RESID) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int rr = r0 + n0 + j;
+                        if (rr < a.R) atomicAdd(a.out + (size_t)rr * a.ldo + gm, blockIdx.y == 0 ? __fadd_rn(v[j], bias) : v[j]);
+                    }
+                } else if (EPI == TC_GELU_B) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int rr = r0 + n0 + j;
+                        const float g = rr < a.R ? gelu_new(__fadd_rn(v[j], bias)) : 0.f;
                         const __half gh = __float2half_rn(g);
                         const size_t off = bimg_off(rr, gm, N);
                         *reinterpret_cast<__half *>(a.bimg_out + off) = gh;
                         if (NP == 2)  // the next GEMM's K is this one's rows
                             *reinterpret_cast<__half *>(a.bimg_out + (size_t)a.rows * N * 2 + off) =
                                 __float2half_rn(g - __half2float(gh));
-                    } else {  // TC_QKV: bias, RoPE on q/k pairs (adjacent lanes), q out / KV append
-                        const float yb = __fadd_rn(y, a.bias[gm]);
+                    }
+                } else {  // TC_QKV: bias, RoPE on q/k pairs (adjacent lanes), q out / KV append
+                    const bool rot = gm < 2 * kHidden;
+                    const int ri = (gm % kHeadDim) >> 1;
+                    float2 cs[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)  // independent loads first
+                        cs[j] = rot ? a.rope[(size_t)s_pos[n0 + j] * (kHeadDim / 2) + ri] : make_float2(1.f, 0.f);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int rr = r0 + n0 + j;
+                        const float yb = __fadd_rn(v[j], bias);
                         const float other = __shfl_xor_sync(0xffffffffu, yb, 1);
                         if (rr < a.R && (gm & 1) == 0) {
-                            const int pos = a.row_pos ? a.row_pos[rr] : a.fixed_pos;
+                            const int pos = s_pos[n0 + j];
                             float o0 = yb, o1 = other;
-                            if (gm < 2 * kHidden) {
-                                const float2 cs = a.rope[(size_t)pos * (kHeadDim / 2) + ((gm % kHeadDim) >> 1)];
-                                o0 = __fsub_rn(__fmul_rn(yb, cs.x), __fmul_rn(other, cs.y));
-                                o1 = __fadd_rn(__fmul_rn(other, cs.x), __fmul_rn(yb, cs.y));
+                            if (rot) {
+                                o0 = __fsub_rn(__fmul_rn(yb, cs[j].x), __fmul_rn(other, cs[j].y));
+                                o1 = __fadd_rn(__fmul_rn(other, cs[j].x), __fmul_rn(yb, cs[j].y));
                             }
                             if (gm < kHidden) {
-                                a.q_out[(size_t)rr * kHidden + gm] = o0;
-                                a.q_out[(size_t)rr * kHidden + gm + 1] = o1;
+                                *reinterpret_cast<float2 *>(a.q_out + (size_t)rr * kHidden + gm) = make_float2(o0, o1);
                             } else {
                                 const int kvsel = gm < 2 * kHidden ? 0 : 1;
                                 const int c = gm - kHidden * (1 + kvsel);
-                                const int slot = a.row_slot[rr];
                                 if (a.kv) {
-                                    const int page = a.page_table[(size_t)slot * a.pages_per_stream + pos / kPage];
-                                    __half *dst = a.kv + (size_t)page * kPageHalfs +
+                                    __half *dst = a.kv + (size_t)s_dst[n0 + j] * kPageHalfs +
                                                   ((kvsel * kHeads + c / kHeadDim) * kPage + pos % kPage) * kHeadDim +
                                                   (c % kHeadDim);
                                     *reinterpret_cast<__half2 *>(dst) = __floats2half2_rn(o0, o1);
                                 } else {
-                                    float *dst = a.lkv + (((size_t)slot * 2 + kvsel) * kLocalLen + pos) * kHidden + c;
-                                    dst[0] = o0;
-                                    dst[1] = o1;
+                                    float *dst =
+                                        a.lkv + (((size_t)s_dst[n0 + j] * 2 + kvsel) * kLocalLen + pos) * kHidden + c;
+                                    *reinterpret_cast<float2 *>(dst) = make_float2(o0, o1);
                                 }
                             }
                         }
@@ -388,6 +428,7 @@ __global__ void __launch_bounds__(256) k_build_bimg(const float *__restrict__ x,
                                                     const float *__restrict__ ln_w, const float *__restrict__ ln_b,
                                                     int parts, uint8_t *__restrict__ bimg) {
     extern __shared__ __align__(16) float xs_b[];
+    pdl_enter();
     const int n = blockIdx.x;
     const size_t part = (size_t)K * N * 2;
     if (n >= R) {
@@ -398,8 +439,38 @@ __global__ void __launch_bounds__(256) k_build_bimg(const float *__restrict__ x,
     }
     for (int k = threadIdx.x; k < K; k += blockDim.x) xs_b[k] = x[(size_t)n * ldx + k];
     __syncthreads();
-    if (ln_w) {
-        if (threadIdx.x < 32) warp_layernorm(xs_b, ln_w, ln_b);
+    if (ln_w) {  // LayerNorm (llm.cpp:159-171) with CTA-wide reductions, K = 768
+        __shared__ float red[8];
+        __shared__ float stat[2];
+        float s = 0.f;
+        for (int k = threadIdx.x; k < kHidden; k += blockDim.x) s += xs_b[k];
+        s = warp_sum(s);
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float t = 0.f;
+            for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+            stat[0] = __fdiv_rn(t, (float)kHidden);
+        }
+        __syncthreads();
+        const float mean = stat[0];
+        float v = 0.f;
+        for (int k = threadIdx.x; k < kHidden; k += blockDim.x) {
+            const float d = xs_b[k] - mean;
+            v = fmaf(d, d, v);
+        }
+        v = warp_sum(v);
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float t = 0.f;
+            for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+            stat[1] = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(t, (float)kHidden) + 1e-5f));
+        }
+        __syncthreads();
+        const float inv = stat[1];
+        for (int k = threadIdx.x; k < kHidden; k += blockDim.x)
+            xs_b[k] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xs_b[k], mean), inv), ln_w[k]), ln_b[k]);
         __syncthreads();
     }
     for (int k = threadIdx.x * 8; k < K; k += blockDim.x * 8) {

@@ -45,6 +45,18 @@ __device__ __forceinline__ int4 ldg_stream(const void *p) {
     return r;
 }
 
+// Programmatic dependent launch.  Kernels of a frame are launched so that each may start
+// while its predecessor is still running: work that only touches weights goes before
+// pdl_wait(); pdl_wait() returns once the predecessor grid has completed and its writes are
+// visible; pdl_trigger() then lets the successor grid start its own prologue.  Launched
+// without the attribute, both are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_enter() {
+    pdl_wait();
+    pdl_trigger();
+}
+
 // gelu_new (llm.cpp:22-25), same operation order
 __device__ __forceinline__ float gelu_new(float v) {
     const float k = 0.7978845608028654f;
@@ -141,6 +153,29 @@ __global__ void __launch_bounds__(512) k_gemv(const GemvArgs a) {
     float *red = smem + MAXR * K;          // [warps][4][MAXR]
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int nwarps = blockDim.x >> 5;
+    const int gl = warp / a.ks, slice = warp - gl * a.ks;
+    const int g = blockIdx.x * a.gpc + gl;
+    const int ngroups = a.w.rows >> 2;
+    const int bps = nb / a.ks;              // blocks per slice
+    const int k = (lane & 7) >> 1, h = lane & 1;
+    const bool active = gl < a.gpc && g < ngroups;
+    const int8_t *wq = a.w.qs + ((size_t)g * nb + (size_t)slice * bps) * 128;
+    const __half *ws = a.w.sc + ((size_t)g * nb + (size_t)slice * bps) * 4;
+    const int nchunks = bps * 8;
+
+    // 0. this lane's first two weight chunks and scales: static data, fetched before waiting
+    //    for the kernel that produces x, so the HBM latency overlaps it
+    int4 pq0 = make_int4(0, 0, 0, 0), pq1 = make_int4(0, 0, 0, 0);
+    float pd0 = 0.f, pd1 = 0.f;
+    if (active && lane < nchunks) {
+        pq0 = ldg_stream(wq + (size_t)lane * 16);
+        pd0 = __half2float(ws[(lane >> 3) * 4 + k]);
+    }
+    if (active && lane + 32 < nchunks) {
+        pq1 = ldg_stream(wq + (size_t)(lane + 32) * 16);
+        pd1 = __half2float(ws[((lane + 32) >> 3) * 4 + k]);
+    }
+    pdl_enter();
 
     // 1. stage the input rows (and LayerNorm them) in shared memory
     for (int i = tid; i < nr * (K >> 2); i += blockDim.x) {
@@ -155,29 +190,28 @@ __global__ void __launch_bounds__(512) k_gemv(const GemvArgs a) {
     }
 
     // 2. dot products
-    const int gl = warp / a.ks, slice = warp - gl * a.ks;
-    const int g = blockIdx.x * a.gpc + gl;
-    const int ngroups = a.w.rows >> 2;
-    const int bps = nb / a.ks;              // blocks per slice
-    const int k = (lane & 7) >> 1, h = lane & 1;
     float acc[MAXR];
 #pragma unroll
     for (int r = 0; r < MAXR; ++r) acc[r] = 0.f;
-    if (gl < a.gpc && g < ngroups) {
-        const int8_t *wq = a.w.qs + ((size_t)g * nb + (size_t)slice * bps) * 128;
-        const __half *ws = a.w.sc + ((size_t)g * nb + (size_t)slice * bps) * 4;
-        const int nchunks = bps * 8;
+    if (active) {
         for (int i = lane; i < nchunks; i += 64) {
-            int4 q0 = ldg_stream(wq + (size_t)i * 16);
-            int4 q1 = make_int4(0, 0, 0, 0);
+            int4 q0 = pq0, q1 = pq1;
+            float d0 = pd0, d1 = pd1;
             const bool two = i + 32 < nchunks;
-            if (two) q1 = ldg_stream(wq + (size_t)(i + 32) * 16);
+            if (i != lane) {  // chunks beyond the prefetched pair
+                q0 = ldg_stream(wq + (size_t)i * 16);
+                d0 = __half2float(ws[(i >> 3) * 4 + k]);
+                if (two) {
+                    q1 = ldg_stream(wq + (size_t)(i + 32) * 16);
+                    d1 = __half2float(ws[((i + 32) >> 3) * 4 + k]);
+                }
+            }
 #pragma unroll
             for (int u = 0; u < 2; ++u) {
                 if (u == 1 && !two) break;
                 const int ii = i + 32 * u;
                 const int b = ii >> 3;
-                const float d = __half2float(ws[b * 4 + k]);
+                const float d = u ? d1 : d0;
                 float wf[16];
                 unpack16(u ? q1 : q0, wf);
                 const int xoff = (slice * bps + b) * 32 + h * 16;
@@ -283,6 +317,7 @@ __global__ void __launch_bounds__(512) k_gemv(const GemvArgs a) {
 // chunks of `chunk` positions.  item_start[r] = first chunk index of row r; the chunk is the
 // smallest power-of-two multiple of kAttnChunk keeping chunks*heads within `max_items`.
 __global__ void k_attn_plan(const int *__restrict__ row_pos, int R, int max_items, int *__restrict__ plan) {
+    pdl_enter();
     // plan[0] = chunk, plan[1] = total chunks, plan[2 + r] = item_start[r] (R + 1 entries)
     __shared__ int s_chunk;
     if (threadIdx.x == 0) {
@@ -316,12 +351,23 @@ struct AttnArgs {
     float *part;            // [items][kPartStride] partials: m, l, pad, pad, o[64]
     int *counter;           // [R][12], zero between launches
     float *out;             // [R][768]
+    // tensor-core path: write the output straight into the next GEMM's fp16 activation image
+    // (bimg_parts = 1: fp16; 2: fp16 and fp16 remainder) instead of `out`
+    uint8_t *bimg;
+    int bimg_N, bimg_parts;
 };
+
+// byte offset of element (n, k) in a tensor-core activation image with N rows: the
+// SWIZZLE_128B K-major layout [k/64][n][128 B], 16-byte unit (k%64)/8 stored at unit ^ (n%8)
+__device__ __forceinline__ size_t bimg_off(int n, int k, int N) {
+    return ((size_t)(k >> 6) * N + n) * 128 + ((((k & 63) >> 3) ^ (n & 7)) << 4) + ((k & 7) << 1);
+}
 
 // Flash-decode over fp16 pages.  One warp per (chunk, head): 8 lanes per position (8 dims
 // each), 4 positions per step, online softmax in fp32, partials merged by the last warp
 // of each (row, head) to finish (atomic arrival count, no waiting).
 __global__ void __launch_bounds__(256) k_attn_decode(const AttnArgs a) {
+    pdl_enter();
     const int lane = threadIdx.x & 31;
     const int ps = lane >> 3, ds = lane & 7;
     const int chunk = a.plan[0];
@@ -409,9 +455,24 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnArgs a) {
         if (nchunks == 1) {
             if (lane < 8) {
                 const float inv = 1.f / l;
-                float *dst = a.out + (size_t)r * kHidden + hd * kHeadDim + ds * 8;
-                reinterpret_cast<float4 *>(dst)[0] = make_float4(o[0] * inv, o[1] * inv, o[2] * inv, o[3] * inv);
-                reinterpret_cast<float4 *>(dst)[1] = make_float4(o[4] * inv, o[5] * inv, o[6] * inv, o[7] * inv);
+                if (a.bimg) {  // 8 dims = one 16-byte unit of the activation image
+                    __align__(16) __half h[8], lo[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const float y = o[j] * inv;
+                        h[j] = __float2half_rn(y);
+                        lo[j] = __float2half_rn(y - __half2float(h[j]));
+                    }
+                    const size_t off = bimg_off(r, hd * kHeadDim + ds * 8, a.bimg_N);
+                    *reinterpret_cast<int4 *>(a.bimg + off) = *reinterpret_cast<const int4 *>(h);
+                    if (a.bimg_parts == 2)
+                        *reinterpret_cast<int4 *>(a.bimg + (size_t)kHidden * a.bimg_N * 2 + off) =
+                            *reinterpret_cast<const int4 *>(lo);
+                } else {
+                    float *dst = a.out + (size_t)r * kHidden + hd * kHeadDim + ds * 8;
+                    reinterpret_cast<float4 *>(dst)[0] = make_float4(o[0] * inv, o[1] * inv, o[2] * inv, o[3] * inv);
+                    reinterpret_cast<float4 *>(dst)[1] = make_float4(o[4] * inv, o[5] * inv, o[6] * inv, o[7] * inv);
+                }
             }
             continue;
         }
@@ -448,8 +509,18 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnArgs a) {
             o1 = fmaf(ov.y, w, o1);
         }
         const float inv = 1.f / L;
-        float *dst = a.out + (size_t)r * kHidden + hd * kHeadDim;
-        reinterpret_cast<float2 *>(dst)[lane] = make_float2(o0 * inv, o1 * inv);
+        if (a.bimg) {
+            const float y0 = o0 * inv, y1 = o1 * inv;
+            const __half2 h = __floats2half2_rn(y0, y1);
+            const size_t off = bimg_off(r, hd * kHeadDim + 2 * lane, a.bimg_N);
+            *reinterpret_cast<__half2 *>(a.bimg + off) = h;
+            if (a.bimg_parts == 2)
+                *reinterpret_cast<__half2 *>(a.bimg + (size_t)kHidden * a.bimg_N * 2 + off) =
+                    __floats2half2_rn(y0 - __low2float(h), y1 - __high2float(h));
+        } else {
+            float *dst = a.out + (size_t)r * kHidden + hd * kHeadDim;
+            reinterpret_cast<float2 *>(dst)[lane] = make_float2(o0 * inv, o1 * inv);
+        }
         if (lane == 0) a.counter[r * kHeads + hd] = 0;
     }
 }
@@ -459,6 +530,7 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnArgs a) {
 __global__ void __launch_bounds__(384) k_attn_local(const float *__restrict__ q, const float *__restrict__ lkv,
                                                     const int *__restrict__ row_slot, int lpos, int R,
                                                     float *__restrict__ out) {
+    pdl_enter();
     const int lane = threadIdx.x & 31;
     const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     if (w >= R * kHeads) return;
@@ -510,6 +582,7 @@ __device__ __forceinline__ float deq_elem(const QMat &m, int row, int col) {
 
 // x[r] = deq(wte[row[0]]) + sum_ch deq(aemb[ch][row[ch+1]]) over valid codes (llm.cpp:148-157)
 __global__ void k_embed_rows(const EmbedTables t, const int *__restrict__ rows17, int R, float *__restrict__ x) {
+    pdl_enter();
     const int r = blockIdx.x;
     if (r >= R) return;
     const int *row = rows17 + (size_t)r * (kNVq + 1);
@@ -526,6 +599,7 @@ __global__ void k_embed_rows(const EmbedTables t, const int *__restrict__ rows17
 
 // Global-step input from the codes the local decoder used: row = [9, used codes...]
 __global__ void k_embed_frame(const EmbedTables t, const int *__restrict__ used, int R, float *__restrict__ x) {
+    pdl_enter();
     const int r = blockIdx.x;
     if (r >= R) return;
     for (int c = threadIdx.x; c < kHidden; c += blockDim.x) {
@@ -541,6 +615,7 @@ __global__ void k_embed_frame(const EmbedTables t, const int *__restrict__ used,
 
 // lx[r] = deq(wte[row]) (local step 1 input: the slot token row, llm.cpp:682)
 __global__ void k_lookup_rows(const QMat m, int row, int R, float *__restrict__ x) {
+    pdl_enter();
     const int r = blockIdx.x;
     for (int c = threadIdx.x; c < kHidden; c += blockDim.x) x[(size_t)r * kHidden + c] = deq_elem(m, row, c);
 }
@@ -553,6 +628,7 @@ __global__ void k_layernorm_rows(const float *__restrict__ x, int R, const float
                                  const float *__restrict__ b, float *__restrict__ out, const int *__restrict__ out_index,
                                  const int *__restrict__ commit) {
     __shared__ float xs[kHidden];
+    pdl_enter();
     const int r = blockIdx.x;
     if (r >= R) return;
     if (commit && !commit[r]) return;
@@ -566,6 +642,7 @@ __global__ void k_layernorm_rows(const float *__restrict__ x, int R, const float
 
 // gather rows: dst[r] = src[index[r]]
 __global__ void k_gather_rows(const float *__restrict__ src, const int *__restrict__ index, int R, float *__restrict__ dst) {
+    pdl_enter();
     const int r = blockIdx.x;
     for (int c = threadIdx.x; c < kHidden; c += blockDim.x) dst[(size_t)r * kHidden + c] = src[(size_t)index[r] * kHidden + c];
 }
@@ -592,6 +669,7 @@ __global__ void __launch_bounds__(256) k_gate(const float *__restrict__ lx, int 
     __shared__ int8_t qa[kHidden];
     __shared__ float as[kHidden / 32];
     __shared__ float pair[2];
+    pdl_enter();
     const int r = blockIdx.x;
     for (int c = threadIdx.x; c < kHidden; c += blockDim.x) xs[c] = lx[(size_t)r * kHidden + c];
     __syncthreads();
@@ -651,6 +729,7 @@ __global__ void __launch_bounds__(256) k_frame_commit(const int *__restrict__ co
                                                       int *__restrict__ frame_idx, int *__restrict__ active_in,
                                                       int *__restrict__ fslot, int max_frames,
                                                       int *__restrict__ codes_hist) {
+    pdl_enter();
     const int f = *fslot;
     if (f < max_frames) {
         for (int i = threadIdx.x; i < R * kNVq; i += blockDim.x)
@@ -683,6 +762,7 @@ __global__ void __launch_bounds__(256) k_sample_greedy(const float *__restrict__
     __shared__ float bv[8];
     __shared__ int bi[8];
     __shared__ int s_used;
+    pdl_enter();
     const int r = blockIdx.x;
     const int slot = row_slot[r];
     const float *lg = logits + (size_t)r * ld_logits;
@@ -727,6 +807,7 @@ __global__ void __launch_bounds__(256) k_sample_greedy(const float *__restrict__
 // scatter page-table updates: upd = [count][slot, index, page] x count;
 // table[slot * pps + index] = page
 __global__ void k_page_updates(const int *__restrict__ upd, int *__restrict__ table, int pps) {
+    pdl_enter();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < upd[0]) table[(size_t)upd[1 + 3 * i] * pps + upd[2 + 3 * i]] = upd[3 + 3 * i];
 }
