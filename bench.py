@@ -196,12 +196,17 @@ def run_ours(args, rank, world, local_rank, dist):
     eng.set_cuda_stream(torch.cuda.current_stream().cuda_stream)
     rng = np.random.default_rng(1234 + rank)
     lens = [int(x) for x in rng.integers(args.lmin, args.lmax + 1, B)]
-    sids = []
-    for i, L in enumerate(lens):
-        s = eng.open()
-        eng.fill_state_random(s, L, seed=1000 * rank + i)
-        eng.generate_begin(s, 0)
-        sids.append(s)
+    sids = [eng.open() for _ in lens]
+
+    def reset_states():
+        # every measured phase starts from the same cached lengths (lmin..lmax), not from
+        # where the previous phase left the streams
+        for i, (s, L) in enumerate(zip(sids, lens)):
+            eng.fill_state_random(s, L, seed=1000 * rank + i)
+            eng.generate_begin(s, 0)
+        torch.cuda.synchronize()
+
+    reset_states()
     params = pkg.SampleParams.make(greedy=True, repetition_penalty=1.2, min_frames=1 << 30)
 
     # warm-up: captures both the multi-frame and the single-frame graphs
@@ -216,6 +221,7 @@ def run_ours(args, rank, world, local_rank, dist):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    reset_states()
     clocks = Clocks(local_rank)
     # ---- value: K frames resident on the device
     if dist is not None:
@@ -230,6 +236,7 @@ def run_ours(args, rank, world, local_rank, dist):
     launches = eng.last_launch_count()
     assert int(done.min()) == K, "a stream stopped during the timed region"
     # ---- e2e: K calls through the C ABI, host buffers in and out every frame
+    reset_states()
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize()
@@ -241,6 +248,7 @@ def run_ours(args, rank, world, local_rank, dist):
     clk = clocks.stop()
 
     # ---- per-kernel device time (separate pass, events inside the frame graph)
+    reset_states()
     eng.kernel_profile(True)
     base_pos = [eng.position(s) for s in sids]
     eng.step_frames(sids, params, prof_frames, want_codes=False)

@@ -206,6 +206,8 @@ void Engine::allocate_state() {
     part_ = dalloc<float>(size_t(kAttnItems) * kPartStride, owned_);
     counter_ = dalloc<int>(R * kHeads, owned_);
     CK(cudaMemset(counter_, 0, R * kHeads * sizeof(int)));
+    work_ = dalloc<int>(kLayers, owned_);  // per-layer chunk counters of the decode attention
+    CK(cudaMemset(work_, 0, kLayers * sizeof(int)));
     active_ = dalloc<int>(R, owned_);
     codes_ = dalloc<int>(R * kNVq, owned_);
     used_ = dalloc<int>(R * kNVq, owned_);
@@ -336,6 +338,7 @@ void launch_gemv(GemvArgs a, cudaStream_t st, bool pdl) {
 }  // namespace
 
 void Engine::set_smem_limits() {
+    CK(cudaFuncSetAttribute(k_attn_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem));
     set_attr_all<PRO_LN, EPI_QKV>();
     set_attr_all<PRO_NONE, EPI_RESID>();
     set_attr_all<PRO_LN, EPI_GELU>();
@@ -423,9 +426,12 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
     }
     launch_tc<TC_QKV>(a, kHidden / kTcK, prec, stream_, pdl_);
     mark(local ? KK_QKV_L : KK_QKV_G);
+    // attention writes straight into proj's activation image; its padding rows are still
+    // zero from the LN1 image built above with the same N
     if (local) {
         const int warps = R * kHeads;
-        launch_k(pdl_, k_attn_local, dim3((warps + 11) / 12), dim3(384), 0, stream_, q_, lkv_, row_slot, lpos, R, attn_);
+        launch_k(pdl_, k_attn_local, dim3((warps + 11) / 12), dim3(384), 0, stream_, q_, lkv_, row_slot, lpos, R,
+                 attn_, bimg_a_, N, tc_parts(prec));
         mark(KK_ATTN_LOCAL);
     } else {
         AttnArgs t{};
@@ -440,18 +446,13 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
         t.part = part_;
         t.counter = counter_;
         t.out = attn_;
-        // straight into proj's activation image; its padding rows are still zero from the
-        // LN1 image built above with the same N
         t.bimg = bimg_a_;
         t.bimg_N = N;
         t.bimg_parts = tc_parts(prec);
-        launch_k(pdl_, k_attn_decode, dim3(kAttnGrid), dim3(256), 0, stream_, t);
+        t.work = work_ + li;
+        t.err = dev_err_;
+        launch_k(pdl_, k_attn_decode, dim3(kAttnGrid), dim3(kAttnThreads), kAttnSmem, stream_, t);
         mark(KK_ATTN_DECODE);
-    }
-    if (local) {
-        launch_k(pdl_, k_build_bimg, dim3(N), dim3(256), kHidden * 4, stream_, attn_, kHidden, R, N, kHidden, nullptr, nullptr, tc_parts(prec),
-                                                       bimg_a_);
-        mark(KK_BIMG);
     }
     TcArgs p{};
     p.N = N;
@@ -519,7 +520,8 @@ void Engine::heads_tc(int ch, int R) {
     mark(KK_HEADS);
 }
 
-// A tensor-core kernel that timed out on one of its barriers leaves a code in dev_err_.
+// A kernel that timed out on one of its barriers (tensor-core GEMM, decode attention) leaves
+// a code in dev_err_.
 // Callers enqueue the copy of the flag into h_err_ before their final synchronisation.
 void Engine::check_device_error() {
     const int e = *h_err_;
@@ -527,7 +529,8 @@ void Engine::check_device_error() {
         *h_err_ = 0;
         CK(cudaMemsetAsync(dev_err_, 0, sizeof(int), stream_));
         CK(cudaStreamSynchronize(stream_));
-        throw std::runtime_error("tensor-core GEMM barrier wait timed out (code " + std::to_string(e) + ")");
+        throw std::runtime_error(std::string(e == 7 || e == 8 ? "decode-attention page ring" : "tensor-core GEMM barrier") +
+                                 " wait timed out (code " + std::to_string(e) + ")");
     }
 }
 
@@ -577,7 +580,8 @@ void Engine::block(const Layer &L, int li, bool local, int R, const int *row_slo
     // attention
     if (local) {
         const int warps = R * kHeads;
-        launch_k(pdl_, k_attn_local, dim3((warps + 11) / 12), dim3(384), 0, stream_, q_, lkv_, row_slot, lpos, R, attn_);
+        launch_k(pdl_, k_attn_local, dim3((warps + 11) / 12), dim3(384), 0, stream_, q_, lkv_, row_slot, lpos, R,
+                 attn_, static_cast<uint8_t *>(nullptr), 0, 0);
         mark(KK_ATTN_LOCAL);
     } else {
         AttnArgs t{};
@@ -592,7 +596,9 @@ void Engine::block(const Layer &L, int li, bool local, int R, const int *row_slo
         t.part = part_;
         t.counter = counter_;
         t.out = attn_;
-        launch_k(pdl_, k_attn_decode, dim3(kAttnGrid), dim3(256), 0, stream_, t);
+        t.work = work_ + li;
+        t.err = dev_err_;
+        launch_k(pdl_, k_attn_decode, dim3(kAttnGrid), dim3(kAttnThreads), kAttnSmem, stream_, t);
         mark(KK_ATTN_DECODE);
     }
     // proj + residual
@@ -635,7 +641,7 @@ void Engine::block(const Layer &L, int li, bool local, int R, const int *row_slo
 // 12 global layers over rows already embedded in x_ (row_pos = positions being written).
 void Engine::global_layers(int R, const int *row_slot, const int *row_pos) {
     // ordinary launch: in a global step alone this kernel follows a host-to-device copy
-    launch_k(false, k_attn_plan, dim3(1), dim3(32), 0, stream_, row_pos, R, kAttnItems, plan_);
+    launch_k(false, k_attn_plan, dim3(1), dim3(32), 0, stream_, row_pos, R, kAttnItems, plan_, work_, kLayers);
     mark(KK_PLAN);
     for (int li = 0; li < kLayers; ++li) block(global_[li], li, false, R, row_slot, row_pos, 0, x_);
 }

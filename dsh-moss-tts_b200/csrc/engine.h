@@ -60,8 +60,8 @@ struct CapturedGraph {
 class Engine {
 public:
     static constexpr int kPrefillRows = 256;    // rows per prefill pass
-    static constexpr int kAttnGrid = 148 * 4;   // CTAs of the decode-attention kernel
-    static constexpr int kAttnItems = kAttnGrid * 8 * 8;  // split-K partial capacity
+    static constexpr int kAttnGrid = 148;       // decode-attention CTAs: one per SM (205 KB smem each)
+    static constexpr int kAttnItems = kAttnGrid * 8 * kHeads;  // split-K partials: ~8 chunks per CTA
 
     Engine(const std::string &weights_path, int device, int max_streams, int max_ctx, int kv_pages);
     ~Engine();
@@ -165,7 +165,7 @@ private:
     float2 *rope_ = nullptr;
     // row-batch scratch
     float *x_ = nullptr, *lx_ = nullptr, *q_ = nullptr, *attn_ = nullptr, *mlp_ = nullptr, *logits_ = nullptr;
-    int *plan_ = nullptr, *counter_ = nullptr, *active_ = nullptr, *codes_ = nullptr, *used_ = nullptr;
+    int *plan_ = nullptr, *counter_ = nullptr, *work_ = nullptr, *active_ = nullptr, *codes_ = nullptr, *used_ = nullptr;
     float *part_ = nullptr, *gate_ = nullptr;
     int *rows17_ = nullptr;
     int *codes_hist_ = nullptr;  // [kMaxFramesPerCall][max_streams][16] codes of a multi-frame call

@@ -57,6 +57,50 @@ __device__ __forceinline__ void pdl_enter() {
     pdl_trigger();
 }
 
+// ---- shared-memory barriers and bulk copies (cp.async.bulk, no tensor map, no multicast)
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+// Bounded wait for the phase with the given parity.  Returns false (and records `code`)
+// after about a second without progress.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code) {
+    const uint32_t addr = smem_u32(bar);
+    for (uint32_t it = 0; it < (1u << 22); ++it) {
+        uint32_t done;
+        asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+                     : "=r"(done)
+                     : "r"(addr), "r"(parity)
+                     : "memory");
+        if (done) return true;
+        if (it > 64) __nanosleep(256);
+    }
+    if (err) atomicCAS(err, 0, code);
+    return false;
+}
+
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
 // gelu_new (llm.cpp:22-25), same operation order
 __device__ __forceinline__ float gelu_new(float v) {
     const float k = 0.7978845608028654f;
@@ -314,47 +358,61 @@ __global__ void __launch_bounds__(512) k_gemv(const GemvArgs a) {
 // --------------------------------------------------------------------------- attention
 
 // Split-K plan over the row batch: row r attends to n_r = pos_r + 1 positions, cut into
-// chunks of `chunk` positions.  item_start[r] = first chunk index of row r; the chunk is the
-// smallest power-of-two multiple of kAttnChunk keeping chunks*heads within `max_items`.
-__global__ void k_attn_plan(const int *__restrict__ row_pos, int R, int max_items, int *__restrict__ plan) {
+// chunks of `chunk` positions (whole pages).  plan[0] = chunk, plan[1] = total chunks,
+// plan[2 + r] = first chunk of row r (R + 1 entries).  The chunk is the smallest power-of-two
+// multiple of kAttnChunk keeping chunks * heads within `max_items` (the partial-result
+// capacity).  One warp; it also zeroes the decode kernel's work counters.
+__global__ void k_attn_plan(const int *__restrict__ row_pos, int R, int max_items, int *__restrict__ plan,
+                            int *__restrict__ work, int nwork) {
     pdl_enter();
-    // plan[0] = chunk, plan[1] = total chunks, plan[2 + r] = item_start[r] (R + 1 entries)
-    __shared__ int s_chunk;
-    if (threadIdx.x == 0) {
-        int chunk = kAttnChunk;
-        for (;;) {
-            long long total = 0;
-            for (int r = 0; r < R; ++r) total += (row_pos[r] + 1 + chunk - 1) / chunk;
-            if (total * kHeads <= max_items || chunk >= (1 << 20)) break;
-            chunk *= 2;
+    const int lane = threadIdx.x & 31;
+    for (int i = lane; i < nwork; i += 32) work[i] = 0;
+    int chunk = kAttnChunk;
+    for (;;) {
+        long long t = 0;
+        for (int r = lane; r < R; r += 32) t += max(0, row_pos[r] + chunk) / chunk;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+        if (t * kHeads <= max_items || chunk >= (1 << 20)) break;
+        chunk *= 2;
+    }
+    int acc = 0;
+    for (int b = 0; b < R; b += 32) {  // exclusive prefix sum of chunk counts, 32 rows at a time
+        const int r = b + lane;
+        const int v = r < R ? max(0, row_pos[r] + chunk) / chunk : 0;  // rows with pos < 0: none
+        int inc = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, inc, o);
+            if (lane >= o) inc += y;
         }
-        s_chunk = chunk;
+        if (r < R) plan[2 + r] = acc + inc - v;
+        acc += __shfl_sync(0xffffffffu, inc, 31);
+    }
+    if (lane == 0) {
         plan[0] = chunk;
-        int acc = 0;
-        for (int r = 0; r < R; ++r) {
-            plan[2 + r] = acc;
-            acc += (row_pos[r] + 1 + chunk - 1) / chunk;
-        }
-        plan[2 + R] = acc;
         plan[1] = acc;
+        plan[2 + R] = acc;
     }
 }
 
 struct AttnArgs {
-    const float *q;         // [R][768]
-    const __half *kv;       // layer base of the paged KV
+    const float *q;         // [R][768], 16-byte aligned
+    const __half *kv;       // layer base of the paged KV, 16-byte aligned
     const int *page_table;
     int pages_per_stream;
     const int *row_slot, *row_pos;
     const int *plan;        // from k_attn_plan
     int R;
-    float *part;            // [items][kPartStride] partials: m, l, pad, pad, o[64]
-    int *counter;           // [R][12], zero between launches
+    float *part;            // [chunks * 12][kPartStride] partials: m, l, pad, pad, o[64]
+    int *counter;           // [R][12] arrival counts, zero between launches
+    int *work;              // next chunk to hand out; zeroed by k_attn_plan
     float *out;             // [R][768]
     // tensor-core path: write the output straight into the next GEMM's fp16 activation image
     // (bimg_parts = 1: fp16; 2: fp16 and fp16 remainder) instead of `out`
     uint8_t *bimg;
     int bimg_N, bimg_parts;
+    int *err;               // bounded-wait time-out flag (may be null)
 };
 
 // byte offset of element (n, k) in a tensor-core activation image with N rows: the
@@ -363,103 +421,233 @@ __device__ __forceinline__ size_t bimg_off(int n, int k, int N) {
     return ((size_t)(k >> 6) * N + n) * 128 + ((((k & 63) >> 3) ^ (n & 7)) << 4) + ((k & 7) << 1);
 }
 
-// Flash-decode over fp16 pages.  One warp per (chunk, head): 8 lanes per position (8 dims
-// each), 4 positions per step, online softmax in fp32, partials merged by the last warp
-// of each (row, head) to finish (atomic arrival count, no waiting).
-__global__ void __launch_bounds__(256) k_attn_decode(const AttnArgs a) {
-    pdl_enter();
-    const int lane = threadIdx.x & 31;
-    const int ps = lane >> 3, ds = lane & 7;
-    const int chunk = a.plan[0];
-    const int total = a.plan[1] * kHeads;
-    const int *istart = a.plan + 2;
-    const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int nw = (gridDim.x * blockDim.x) >> 5;
-    for (int item = gw; item < total; item += nw) {
-        const int cg = item / kHeads, hd = item - cg * kHeads;
-        int lo = 0, hi = a.R - 1;  // row r with istart[r] <= cg < istart[r+1]
-        while (lo < hi) {
-            const int mid = (lo + hi + 1) >> 1;
-            if (istart[mid] <= cg) lo = mid; else hi = mid - 1;
+// Flash-decode over fp16 pages, one CTA per SM.  A page of one layer holds K and V of all 12
+// heads for 16 positions, 48 KB contiguous ([k|v][head][16][64] fp16), so the whole page
+// moves with one cp.async.bulk.  A producer warp hands out chunks (whole pages of one row)
+// through an atomic counter and streams their pages -- with the row's query on the chunk's
+// first page -- into a 4-stage ring in shared memory; 12 consumer warps, one per head, each
+// read their head's 2 KB K and V blocks from the stage (8 lanes per position, 8 dims a lane,
+// 4 positions per step, online softmax in fp32).  At the end of a chunk a warp writes its
+// (row, head) result, or a split-K partial; the last chunk of a (row, head) to arrive merges
+// all partials (atomic arrival count, no waiting).  Every barrier wait is bounded.
+constexpr int kAttnConsumers = kHeads;                     // consumer warps: one per head
+constexpr int kAttnThreads = (kAttnConsumers + 1) * 32;    // + the producer warp
+constexpr int kAttnStages = 4;
+constexpr int kAttnPageBytes = kPageHalfs * 2;             // 49152
+constexpr int kAttnQBytes = kHidden * 4;                   // one query row, fp32
+constexpr int kAttnSmem = kAttnStages * (kAttnPageBytes + kAttnQBytes) + 1024;  // 209,920
+
+struct AttnStage {  // written by the producer before the stage's barrier arrive
+    int r;          // row
+    int pb;         // first position of the page
+    int p1;         // end of the chunk (exclusive)
+    int flags;      // 1: first page of a chunk (query copied), 2: last page, 4: no more work
+    int grp;        // global chunk index (partials live at grp * 12 + head)
+    int gbase;      // first chunk of row r
+    int nchunks;    // chunks of row r
+    int pad;
+};
+
+__global__ void __launch_bounds__(kAttnThreads, 1) k_attn_decode(const AttnArgs a) {
+    extern __shared__ __align__(128) uint8_t attn_smem[];
+    uint8_t *pages = attn_smem;                                          // [stage][49152]
+    float *qs = reinterpret_cast<float *>(attn_smem + kAttnStages * kAttnPageBytes);  // [stage][768]
+    AttnStage *meta = reinterpret_cast<AttnStage *>(attn_smem + kAttnStages * (kAttnPageBytes + kAttnQBytes));
+    uint64_t *full = reinterpret_cast<uint64_t *>(meta + kAttnStages);  // [stage]
+    uint64_t *empty = full + kAttnStages;                               // [stage]
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kAttnStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kAttnConsumers);
         }
-        const int r = lo;
-        const int c = cg - istart[r];
-        const int nchunks = istart[r + 1] - istart[r];
-        const int n = a.row_pos[r] + 1;
-        const int slot = a.row_slot[r];
-        const int p0 = c * chunk, p1 = min(n, p0 + chunk);
-        float qv[8];
-        {
-            const float4 *qp = reinterpret_cast<const float4 *>(a.q + (size_t)r * kHidden + hd * kHeadDim + ds * 8);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    pdl_enter();
+    const int total = a.plan[1];
+    const int *istart = a.plan + 2;
+
+    if (wid == kAttnConsumers) {
+        // ------------------------------------------------------------------ producer warp
+        const int chunk = a.plan[0];
+        int seq = 0;
+        bool ok = true;
+        int grp = 0;
+        if (lane == 0) grp = atomicAdd(a.work, 1);
+        grp = __shfl_sync(0xffffffffu, grp, 0);
+        while (ok) {
+            int stop = grp >= total;
+            int next = 0;
+            if (!stop && lane == 0) next = atomicAdd(a.work, 1);  // fetched early, used after this chunk
+            int r = 0, gbase = 0, nch = 0, p0 = 0, p1 = 0, npg = 0;
+            const int *pt = nullptr;
+            if (!stop) {
+                int cnt = 0;  // rows whose first chunk is <= grp
+                for (int b = 0; b < a.R; b += 32) {
+                    const int i = b + lane;
+                    const bool in = i < a.R;
+                    const int st = in ? istart[i] : 0;
+                    cnt += __popc(__ballot_sync(0xffffffffu, in && st <= grp));
+                    if (__ballot_sync(0xffffffffu, in && st > grp)) break;
+                }
+                r = cnt - 1;
+                gbase = istart[r];
+                nch = istart[r + 1] - gbase;
+                p0 = (grp - gbase) * chunk;
+                p1 = min(a.row_pos[r] + 1, p0 + chunk);
+                npg = (p1 - p0 + kPage - 1) / kPage;
+                pt = a.page_table + (size_t)a.row_slot[r] * a.pages_per_stream + p0 / kPage;
+            }
+            for (int jb = 0; jb < (stop ? 1 : npg); jb += 32) {
+                const int pid = (!stop && jb + lane < npg) ? pt[jb + lane] : 0;
+                const int jend = stop ? jb + 1 : min(npg, jb + 32);
+                for (int j = jb; j < jend; ++j) {
+                    const int page = __shfl_sync(0xffffffffu, pid, j - jb);
+                    if (lane == 0) {
+                        const int s = seq % kAttnStages;
+                        if (!mbar_wait(&empty[s], ((seq / kAttnStages) & 1) ^ 1, a.err, 8)) {
+                            ok = false;
+                        } else {
+                            AttnStage &m = meta[s];
+                            m.r = r;
+                            m.pb = p0 + j * kPage;
+                            m.p1 = p1;
+                            m.flags = stop ? 4 : ((j == 0 ? 1 : 0) | (j == npg - 1 ? 2 : 0));
+                            m.grp = grp;
+                            m.gbase = gbase;
+                            m.nchunks = nch;
+                            if (stop) {
+                                mbar_arrive(&full[s]);
+                            } else {
+                                const uint32_t bytes = kAttnPageBytes + (j == 0 ? kAttnQBytes : 0);
+                                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                                mbar_expect_tx(&full[s], bytes);
+                                bulk_g2s(pages + (size_t)s * kAttnPageBytes, a.kv + (size_t)page * kPageHalfs,
+                                         kAttnPageBytes, &full[s]);
+                                if (j == 0)
+                                    bulk_g2s(qs + s * kHidden, a.q + (size_t)r * kHidden, kAttnQBytes, &full[s]);
+                            }
+                        }
+                    }
+                    ok = __shfl_sync(0xffffffffu, ok, 0);
+                    ++seq;
+                    if (!ok) break;
+                }
+                if (!ok) break;
+            }
+            if (stop || !ok) break;
+            grp = __shfl_sync(0xffffffffu, next, 0);
+        }
+        if (!ok && lane == 0) {
+            // a consumer stopped answering: let the copies already issued land before exiting
+            for (int k = max(0, seq - kAttnStages); k < seq - 1; ++k)
+                mbar_wait(&full[k % kAttnStages], (k / kAttnStages) & 1, nullptr, 0);
+        }
+        return;
+    }
+
+    // ---------------------------------------------------------------------- consumer warps
+    const int hd = wid;
+    const int ps = lane >> 3, ds = lane & 7;
+    float qv[8];
+    float m = -INFINITY, l = 0.f, o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = 0.f;
+    for (int seq = 0;; ++seq) {
+        const int s = seq % kAttnStages;
+        if (!mbar_wait(&full[s], (seq / kAttnStages) & 1, a.err, 7)) return;
+        const AttnStage st = meta[s];
+        if (st.flags & 4) break;
+        if (st.flags & 1) {
+            const float4 *qp = reinterpret_cast<const float4 *>(qs + s * kHidden + hd * kHeadDim + ds * 8);
             const float4 x0 = qp[0], x1 = qp[1];
             qv[0] = x0.x * 0.125f; qv[1] = x0.y * 0.125f; qv[2] = x0.z * 0.125f; qv[3] = x0.w * 0.125f;
             qv[4] = x1.x * 0.125f; qv[5] = x1.y * 0.125f; qv[6] = x1.z * 0.125f; qv[7] = x1.w * 0.125f;
         }
-        float m = -INFINITY, l = 0.f, o[8];
+        const uint8_t *kb = pages + (size_t)s * kAttnPageBytes + hd * (kPage * kHeadDim * 2) + ds * 16;
+        const uint8_t *vb = kb + kHeads * kPage * kHeadDim * 2;
+        float sc[4];
+        int4 vr[4];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) o[j] = 0.f;
-        const int *pt = a.page_table + (size_t)slot * a.pages_per_stream;
-        // every lane runs the same trip count (the shuffles below need the whole warp);
-        // lanes whose position is past the chunk end load nothing and skip the update
-        for (int pb = p0; pb < p1; pb += 4) {
-            const int p = pb + ps;
-            const bool valid = p < p1;
-            int4 kr = make_int4(0, 0, 0, 0), vr = make_int4(0, 0, 0, 0);
-            if (valid) {
-                const __half *base = a.kv + (size_t)pt[p / kPage] * kPageHalfs +
-                                     ((size_t)hd * kPage + p % kPage) * kHeadDim + ds * 8;
-                kr = *reinterpret_cast<const int4 *>(base);
-                vr = *reinterpret_cast<const int4 *>(base + kHeads * kPage * kHeadDim);
-            }
+        for (int u = 0; u < 4; ++u) {
+            const int pp = ps + 4 * u;  // position within the page
+            const int4 kr = *reinterpret_cast<const int4 *>(kb + pp * 128);
+            vr[u] = *reinterpret_cast<const int4 *>(vb + pp * 128);
+            if (st.pb + pp >= st.p1) vr[u] = make_int4(0, 0, 0, 0);  // past the end: stale bits
             const __half2 *kh = reinterpret_cast<const __half2 *>(&kr);
-            float s = 0.f;
+            float d = 0.f;
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const float2 kf = __half22float2(kh[j]);
-                s = fmaf(qv[2 * j], kf.x, s);
-                s = fmaf(qv[2 * j + 1], kf.y, s);
+            for (int e = 0; e < 4; ++e) {
+                const float2 kf = __half22float2(kh[e]);
+                d = fmaf(qv[2 * e], kf.x, d);
+                d = fmaf(qv[2 * e + 1], kf.y, d);
             }
-            s += __shfl_xor_sync(0xffffffffu, s, 1);
-            s += __shfl_xor_sync(0xffffffffu, s, 2);
-            s += __shfl_xor_sync(0xffffffffu, s, 4);
-            if (!valid) continue;
-            const float mn = fmaxf(m, s);
-            const float corr = __expf(m - mn);
-            const float pw = __expf(s - mn);
-            l = l * corr + pw;
-            const __half2 *vh = reinterpret_cast<const __half2 *>(&vr);
+            sc[u] = d;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);  // the stage's data is in registers now
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const float2 vf = __half22float2(vh[j]);
-                o[2 * j] = fmaf(pw, vf.x, o[2 * j] * corr);
-                o[2 * j + 1] = fmaf(pw, vf.y, o[2 * j + 1] * corr);
+        for (int u = 0; u < 4; ++u) {
+            sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], 1);
+            sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], 2);
+            sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], 4);
+            if (st.pb + ps + 4 * u >= st.p1) sc[u] = -INFINITY;
+        }
+        const float mn = fmaxf(fmaxf(m, fmaxf(sc[0], sc[1])), fmaxf(sc[2], sc[3]));
+        if (mn != -INFINITY) {  // else: no valid position for this lane group yet
+            const float corr = __expf(m - mn);
+            float pw[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) pw[u] = __expf(sc[u] - mn);  // 0 for -inf scores
+            l = l * corr + ((pw[0] + pw[1]) + (pw[2] + pw[3]));
+#pragma unroll
+            for (int e = 0; e < 8; ++e) o[e] *= corr;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const __half2 *vh = reinterpret_cast<const __half2 *>(&vr[u]);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 vf = __half22float2(vh[e]);
+                    o[2 * e] = fmaf(pw[u], vf.x, o[2 * e]);
+                    o[2 * e + 1] = fmaf(pw[u], vf.y, o[2 * e + 1]);
+                }
             }
             m = mn;
         }
-        // merge the 4 position groups (lanes ds, ds+8, ds+16, ds+24)
+        if (!(st.flags & 2)) continue;
+
+        // ---- end of the chunk: merge the 4 position groups (lanes ds, ds+8, ds+16, ds+24)
+        const int r = st.r, nchunks = st.nchunks;
 #pragma unroll
         for (int off = 8; off <= 16; off <<= 1) {
             const float mo = __shfl_xor_sync(0xffffffffu, m, off);
             const float lo2 = __shfl_xor_sync(0xffffffffu, l, off);
-            const float mn = fmaxf(m, mo);
-            const float c1 = (m == -INFINITY) ? 0.f : __expf(m - mn);
-            const float c2 = (mo == -INFINITY) ? 0.f : __expf(mo - mn);
+            const float mx = fmaxf(m, mo);
+            const float c1 = (m == -INFINITY) ? 0.f : __expf(m - mx);
+            const float c2 = (mo == -INFINITY) ? 0.f : __expf(mo - mx);
             l = l * c1 + lo2 * c2;
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
                 const float oo = __shfl_xor_sync(0xffffffffu, o[j], off);
                 o[j] = o[j] * c1 + oo * c2;
             }
-            m = mn;
+            m = mx;
         }
+        const float mf = m, lf = l;
+        float of[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) { of[j] = o[j]; o[j] = 0.f; }
+        m = -INFINITY;
+        l = 0.f;
         if (nchunks == 1) {
             if (lane < 8) {
-                const float inv = 1.f / l;
+                const float inv = 1.f / lf;
                 if (a.bimg) {  // 8 dims = one 16-byte unit of the activation image
                     __align__(16) __half h[8], lo[8];
 #pragma unroll
                     for (int j = 0; j < 8; ++j) {
-                        const float y = o[j] * inv;
+                        const float y = of[j] * inv;
                         h[j] = __float2half_rn(y);
                         lo[j] = __float2half_rn(y - __half2float(h[j]));
                     }
@@ -470,17 +658,19 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnArgs a) {
                             *reinterpret_cast<const int4 *>(lo);
                 } else {
                     float *dst = a.out + (size_t)r * kHidden + hd * kHeadDim + ds * 8;
-                    reinterpret_cast<float4 *>(dst)[0] = make_float4(o[0] * inv, o[1] * inv, o[2] * inv, o[3] * inv);
-                    reinterpret_cast<float4 *>(dst)[1] = make_float4(o[4] * inv, o[5] * inv, o[6] * inv, o[7] * inv);
+                    reinterpret_cast<float4 *>(dst)[0] =
+                        make_float4(of[0] * inv, of[1] * inv, of[2] * inv, of[3] * inv);
+                    reinterpret_cast<float4 *>(dst)[1] =
+                        make_float4(of[4] * inv, of[5] * inv, of[6] * inv, of[7] * inv);
                 }
             }
             continue;
         }
-        float *pp = a.part + (size_t)item * kPartStride;
+        float *pp = a.part + ((size_t)st.grp * kHeads + hd) * kPartStride;
         if (lane < 8) {
-            reinterpret_cast<float4 *>(pp + 4 + ds * 8)[0] = make_float4(o[0], o[1], o[2], o[3]);
-            reinterpret_cast<float4 *>(pp + 4 + ds * 8)[1] = make_float4(o[4], o[5], o[6], o[7]);
-            if (lane == 0) { pp[0] = m; pp[1] = l; }
+            reinterpret_cast<float4 *>(pp + 4 + ds * 8)[0] = make_float4(of[0], of[1], of[2], of[3]);
+            reinterpret_cast<float4 *>(pp + 4 + ds * 8)[1] = make_float4(of[4], of[5], of[6], of[7]);
+            if (lane == 0) { pp[0] = mf; pp[1] = lf; }
         }
         // publish: the warp's stores, then (one lane) a device fence and the arrival count
         __syncwarp();
@@ -493,7 +683,7 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnArgs a) {
         last = __shfl_sync(0xffffffffu, last, 0);
         if (!last) continue;
         // this warp saw every other chunk arrive: combine all chunks of (r, hd)
-        const size_t ibase = (size_t)istart[r] * kHeads + hd;
+        const size_t ibase = (size_t)st.gbase * kHeads + hd;
         float M = -INFINITY;
         for (int cc = lane; cc < nchunks; cc += 32)
             M = fmaxf(M, __ldcg(a.part + (ibase + (size_t)cc * kHeads) * kPartStride));
@@ -526,10 +716,12 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnArgs a) {
 }
 
 // Local decoder attention: n = lpos + 1 <= 17 positions of fp32 local KV.
-// One warp per (row, head); scores in llm.cpp:189-217 order per position.
+// One warp per (row, head); scores in llm.cpp:189-217 order per position.  With bimg set the
+// output goes straight into the next tensor-core GEMM's activation image (N rows, parts).
 __global__ void __launch_bounds__(384) k_attn_local(const float *__restrict__ q, const float *__restrict__ lkv,
                                                     const int *__restrict__ row_slot, int lpos, int R,
-                                                    float *__restrict__ out) {
+                                                    float *__restrict__ out, uint8_t *__restrict__ bimg, int bimg_N,
+                                                    int bimg_parts) {
     pdl_enter();
     const int lane = threadIdx.x & 31;
     const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -566,7 +758,16 @@ __global__ void __launch_bounds__(384) k_attn_local(const float *__restrict__ q,
         o0 = fmaf(wp, vv.x, o0);
         o1 = fmaf(wp, vv.y, o1);
     }
-    reinterpret_cast<float2 *>(out + (size_t)r * kHidden + hd * kHeadDim)[lane] = make_float2(o0, o1);
+    if (bimg) {
+        const __half2 hv = __floats2half2_rn(o0, o1);
+        const size_t off = bimg_off(r, hd * kHeadDim + 2 * lane, bimg_N);
+        *reinterpret_cast<__half2 *>(bimg + off) = hv;
+        if (bimg_parts == 2)
+            *reinterpret_cast<__half2 *>(bimg + (size_t)kHidden * bimg_N * 2 + off) =
+                __floats2half2_rn(o0 - __low2float(hv), o1 - __high2float(hv));
+    } else {
+        reinterpret_cast<float2 *>(out + (size_t)r * kHidden + hd * kHeadDim)[lane] = make_float2(o0, o1);
+    }
 }
 
 // --------------------------------------------------------------------------- embeddings

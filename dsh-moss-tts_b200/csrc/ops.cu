@@ -25,9 +25,43 @@ int op_fail(const std::string &msg) {
 
 constexpr size_t kAlign = 256;
 
+// The decode-attention kernel uses 205 KB of dynamic shared memory (its page ring), above the
+// 48 KB a launch gets without opting in; the opt-in is per device.
+constexpr int kMaxDevices = 64;
+std::mutex g_attr_mu;
+bool g_attr_set[kMaxDevices] = {};
+
+int launch_decode(const mossgpu::AttnArgs &t, cudaStream_t st, const char *who) {
+    using namespace mossgpu;
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return op_fail(std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+    if (dev < 0 || dev >= kMaxDevices) return op_fail(std::string(who) + ": device ordinal out of range");
+    {
+        std::lock_guard<std::mutex> lock(g_attr_mu);
+        if (!g_attr_set[dev]) {
+            e = cudaFuncSetAttribute(k_attn_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem);
+            if (e != cudaSuccess) return op_fail(std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+            g_attr_set[dev] = true;
+        }
+    }
+    k_attn_decode<<<148, kAttnThreads, kAttnSmem, st>>>(t);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return op_fail(std::string(who) + " launch: " + cudaGetErrorString(e));
+    return 0;
+}
+
+// q rows are read as float4 and the pages are fetched with 16-byte bulk copies
+int check_alignment(const float *q, const void *kv_layer, const char *who) {
+    if (reinterpret_cast<uintptr_t>(q) % 16 != 0 || reinterpret_cast<uintptr_t>(kv_layer) % 16 != 0)
+        return op_fail(std::string(who) + ": q and kv_layer must be 16-byte aligned");
+    return 0;
+}
+
 size_t round_up(size_t n) { return (n + kAlign - 1) / kAlign * kAlign; }
 
-// Workspace layout for R rows: [plan: 2 + R + 1 ints][counters: R * 12 ints][partials]
+// Workspace layout for R rows: [plan: 2 + R + 1 ints][counters: R * 12 ints, chunk counter]
+// [partials]
 struct Layout {
     size_t plan, counters, part, total;
     int items;
@@ -37,7 +71,7 @@ Layout layout_for(int R, size_t bytes) {
     Layout l{};
     l.plan = 0;
     l.counters = round_up(sizeof(int) * (size_t(R) + 3));
-    l.part = l.counters + round_up(sizeof(int) * size_t(R) * mossgpu::kHeads);
+    l.part = l.counters + round_up(sizeof(int) * (size_t(R) * mossgpu::kHeads + 1));
     const size_t part_bytes = bytes > l.part ? bytes - l.part : 0;
     l.items = int(std::min<size_t>(part_bytes / (sizeof(float) * mossgpu::kPartStride), 1u << 30));
     l.total = bytes;
@@ -70,6 +104,7 @@ int mossgpu_attention_decode_paged(const float *q, const void *kv_layer, const i
         return op_fail("attention_decode_paged: workspace too small (need mossgpu_attention_workspace_bytes(R))");
     if (reinterpret_cast<uintptr_t>(workspace) % 16 != 0)
         return op_fail("attention_decode_paged: workspace must be 16-byte aligned");
+    if (check_alignment(q, kv_layer, "attention_decode_paged") != 0) return 1;
     cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
     char *ws = static_cast<char *>(workspace);
     int *plan = reinterpret_cast<int *>(ws + l.plan);
@@ -78,7 +113,7 @@ int mossgpu_attention_decode_paged(const float *q, const void *kv_layer, const i
     // arrival counters must start at zero (the workspace's contents are unspecified)
     cudaError_t e = cudaMemsetAsync(counter, 0, sizeof(int) * size_t(R) * kHeads, st);
     if (e != cudaSuccess) return op_fail(std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
-    k_attn_plan<<<1, 32, 0, st>>>(row_pos, R, l.items, plan);
+    k_attn_plan<<<1, 32, 0, st>>>(row_pos, R, l.items, plan, counter + R * kHeads, 1);
     AttnArgs t{};
     t.q = q;
     t.kv = static_cast<const __half *>(kv_layer);
@@ -90,11 +125,9 @@ int mossgpu_attention_decode_paged(const float *q, const void *kv_layer, const i
     t.R = R;
     t.part = part;
     t.counter = counter;
+    t.work = counter + R * kHeads;
     t.out = out;
-    k_attn_decode<<<148 * 4, 256, 0, st>>>(t);
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return op_fail(std::string("attention_decode_paged launch: ") + cudaGetErrorString(e));
-    return 0;
+    return launch_decode(t, st, "attention_decode_paged");
 }
 
 }  // extern "C"
@@ -114,7 +147,7 @@ namespace {
 constexpr int kNoAllocMaxRows = 256;    // rows per call
 constexpr int kNoAllocMaxItems = 4096;  // split-K (chunk, head) partials; chunks widen to fit
 constexpr size_t kNoAllocPlanBytes = 2048;                                   // 2 + R + 1 ints
-constexpr size_t kNoAllocCounterBytes = sizeof(int) * kNoAllocMaxRows * mossgpu::kHeads;  // 12 KiB
+constexpr size_t kNoAllocCounterBytes = sizeof(int) * kNoAllocMaxRows * mossgpu::kHeads + 256;  // + chunk counter
 constexpr size_t kNoAllocPartBytes = sizeof(float) * mossgpu::kPartStride * kNoAllocMaxItems;
 constexpr size_t kNoAllocScratchBytes = kNoAllocPlanBytes + kNoAllocCounterBytes + kNoAllocPartBytes;  // ~1.08 MiB
 static_assert(kNoAllocPlanBytes >= sizeof(int) * (kNoAllocMaxRows + 3), "plan area too small");
@@ -123,7 +156,6 @@ static __device__ __align__(256) unsigned char g_attn_noalloc_scratch[kNoAllocSc
 
 // Device address of the array, looked up once per device (with that device current).  In host
 // code the array's name is only a host-side handle, never a device address.
-constexpr int kMaxDevices = 64;
 std::mutex g_noalloc_mu;
 void *g_noalloc_ptr[kMaxDevices] = {};
 
@@ -156,6 +188,7 @@ extern "C" int mossgpu_attention_decode_paged_noalloc(const float *q, const void
     if (!q || !kv_layer || !page_table || !row_slot || !row_pos || !out)
         return op_fail("attention_decode_paged_noalloc: a required pointer is NULL");
     if (pages_per_stream <= 0) return op_fail("attention_decode_paged_noalloc: pages_per_stream must be positive");
+    if (check_alignment(q, kv_layer, "attention_decode_paged_noalloc") != 0) return 1;
     void *scratch = nullptr;
     if (noalloc_scratch(&scratch) != 0) return 1;
     cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
@@ -167,7 +200,8 @@ extern "C" int mossgpu_attention_decode_paged_noalloc(const float *q, const void
     // (the plan is rewritten and the partials are written before they are read)
     cudaError_t e = cudaMemsetAsync(counter, 0, sizeof(int) * size_t(R) * kHeads, st);
     if (e != cudaSuccess) return op_fail(std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
-    k_attn_plan<<<1, 32, 0, st>>>(row_pos, R, kNoAllocMaxItems, plan);
+    int *work = counter + kNoAllocMaxRows * kHeads;  // zeroed by the plan kernel
+    k_attn_plan<<<1, 32, 0, st>>>(row_pos, R, kNoAllocMaxItems, plan, work, 1);
     AttnArgs t{};
     t.q = q;
     t.kv = static_cast<const __half *>(kv_layer);
@@ -179,10 +213,7 @@ extern "C" int mossgpu_attention_decode_paged_noalloc(const float *q, const void
     t.R = R;
     t.part = part;
     t.counter = counter;
+    t.work = work;
     t.out = out;
-    k_attn_decode<<<148 * 4, 256, 0, st>>>(t);
-    e = cudaGetLastError();
-    if (e != cudaSuccess)
-        return op_fail(std::string("attention_decode_paged_noalloc launch: ") + cudaGetErrorString(e));
-    return 0;
+    return launch_decode(t, st, "attention_decode_paged_noalloc");
 }

@@ -78,6 +78,20 @@ def test_attention_op_long_rows_use_many_chunks(lib):
     assert (out.cpu() - ref).abs().max().item() < 1e-4
 
 
+def test_attention_op_many_ragged_rows(lib):
+    # more rows than one 32-row search step, rows of one position next to rows of many
+    # chunks, and several chunks handed to every CTA
+    import torch
+    rng = np.random.default_rng(11)
+    positions = tuple(int(x) for x in rng.integers(0, 2000, 150)) + (0, 1, 15, 16, 17)
+    q, kv, table, slots, pos = paged_case(seed=5, n_pages=400, pps=128, positions=positions)
+    ref = torch_reference(q, kv, table, slots, pos)
+    rc, out = call(lib, *[t.cuda() for t in (q, kv, table, slots, pos)])
+    assert rc == 0, lib.mossgpu_op_last_error()
+    assert torch.isfinite(out).all()
+    assert (out.cpu() - ref).abs().max().item() < 1e-4
+
+
 def test_attention_op_rejects_small_workspace(lib):
     q, kv, table, slots, pos = [t.cuda() for t in paged_case()]
     rc, _ = call(lib, q, kv, table, slots, pos, ws_bytes=64)
