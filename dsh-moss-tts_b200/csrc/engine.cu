@@ -203,9 +203,10 @@ void Engine::allocate_state() {
     mlp_ = dalloc<float>(R * kFF, owned_);
     logits_ = dalloc<float>(size_t(max_streams_) * kNVq * kCodebook, owned_);
     plan_ = dalloc<int>(R + 3, owned_);
-    part_ = dalloc<float>(size_t(kAttnItems) * kPartStride, owned_);
-    counter_ = dalloc<int>(R * kHeads, owned_);
-    CK(cudaMemset(counter_, 0, R * kHeads * sizeof(int)));
+    // split-K capacity: ~8 chunks per CTA, and never less than one chunk per row
+    attn_items_ = std::max(kAttnItems, r_max_ * kHeads);
+    part_ = dalloc<float>(size_t(attn_items_) * kPartStride, owned_);
+    desc_ = dalloc<int4>(attn_items_ / kHeads, owned_);
     work_ = dalloc<int>(kLayers, owned_);  // per-layer chunk counters of the decode attention
     CK(cudaMemset(work_, 0, kLayers * sizeof(int)));
     active_ = dalloc<int>(R, owned_);
@@ -444,7 +445,7 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
         t.plan = plan_;
         t.R = R;
         t.part = part_;
-        t.counter = counter_;
+        t.desc = desc_;
         t.out = attn_;
         t.bimg = bimg_a_;
         t.bimg_N = N;
@@ -453,6 +454,8 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
         t.err = dev_err_;
         launch_k(pdl_, k_attn_decode, dim3(kAttnGrid), dim3(kAttnThreads), kAttnSmem, stream_, t);
         mark(KK_ATTN_DECODE);
+        launch_k(pdl_, k_attn_combine, dim3((R * kHeads + 7) / 8), dim3(256), 0, stream_, t);
+        mark(KK_ATTN_COMBINE);
     }
     TcArgs p{};
     p.N = N;
@@ -594,12 +597,14 @@ void Engine::block(const Layer &L, int li, bool local, int R, const int *row_slo
         t.plan = plan_;
         t.R = R;
         t.part = part_;
-        t.counter = counter_;
+        t.desc = desc_;
         t.out = attn_;
         t.work = work_ + li;
         t.err = dev_err_;
         launch_k(pdl_, k_attn_decode, dim3(kAttnGrid), dim3(kAttnThreads), kAttnSmem, stream_, t);
         mark(KK_ATTN_DECODE);
+        launch_k(pdl_, k_attn_combine, dim3((R * kHeads + 7) / 8), dim3(256), 0, stream_, t);
+        mark(KK_ATTN_COMBINE);
     }
     // proj + residual
     GemvArgs p{};
@@ -641,7 +646,8 @@ void Engine::block(const Layer &L, int li, bool local, int R, const int *row_slo
 // 12 global layers over rows already embedded in x_ (row_pos = positions being written).
 void Engine::global_layers(int R, const int *row_slot, const int *row_pos) {
     // ordinary launch: in a global step alone this kernel follows a host-to-device copy
-    launch_k(false, k_attn_plan, dim3(1), dim3(32), 0, stream_, row_pos, R, kAttnItems, plan_, work_, kLayers);
+    launch_k(false, k_attn_plan, dim3(1), dim3(32), 0, stream_, row_pos, row_slot, pages_per_stream_, R, attn_items_,
+             plan_, desc_, work_, kLayers);
     mark(KK_PLAN);
     for (int li = 0; li < kLayers; ++li) block(global_[li], li, false, R, row_slot, row_pos, 0, x_);
 }
@@ -1024,7 +1030,7 @@ const char *kernel_kind_name(int kind) {
         "page_updates", "gather_hidden", "lookup_slot_row", "embed_frame", "attn_plan",
         "gemv_qkv_global", "attn_decode_paged", "gemv_proj_global", "gemv_fc_in_global", "gemv_fc_out_global", "ln_f",
         "gemv_qkv_local", "attn_local", "gemv_proj_local", "gemv_fc_in_local", "gemv_fc_out_local", "gate_w8a8",
-        "gemv_audio_heads", "sample_greedy", "frame_commit", "build_activation_image"};
+        "gemv_audio_heads", "sample_greedy", "frame_commit", "build_activation_image", "attn_combine"};
     return (kind >= 0 && kind < KK_COUNT) ? names[kind] : "?";
 }
 

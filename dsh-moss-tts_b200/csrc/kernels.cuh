@@ -77,18 +77,33 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
                  : "memory");
 }
 
-// Bounded wait for the phase with the given parity.  Returns false (and records `code`)
-// after about a second without progress.
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ bool mbar_try(uint32_t addr, uint32_t parity) {
+    uint32_t done;
+    asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(done)
+                 : "r"(addr), "r"(parity)
+                 : "memory");
+    return done != 0;
+}
+
+// Bounded wait for the phase with the given parity: try_wait (which suspends the thread in
+// hardware for a while) in a tight loop, then 1 us sleeps until about a second has passed.
+// Returns false, and records `code` in *err when err is not null, on time-out.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code) {
     const uint32_t addr = smem_u32(bar);
-    for (uint32_t it = 0; it < (1u << 22); ++it) {
-        uint32_t done;
-        asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
-                     : "=r"(done)
-                     : "r"(addr), "r"(parity)
-                     : "memory");
-        if (done) return true;
-        if (it > 64) __nanosleep(256);
+    for (int it = 0; it < 4096; ++it)
+        if (mbar_try(addr, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        if (mbar_try(addr, parity)) return true;
+        if (global_ns() - t0 > 1000000000ull) break;
+        __nanosleep(1000);
     }
     if (err) atomicCAS(err, 0, code);
     return false;
@@ -361,8 +376,11 @@ __global__ void __launch_bounds__(512) k_gemv(const GemvArgs a) {
 // chunks of `chunk` positions (whole pages).  plan[0] = chunk, plan[1] = total chunks,
 // plan[2 + r] = first chunk of row r (R + 1 entries).  The chunk is the smallest power-of-two
 // multiple of kAttnChunk keeping chunks * heads within `max_items` (the partial-result
-// capacity).  One warp; it also zeroes the decode kernel's work counters.
-__global__ void k_attn_plan(const int *__restrict__ row_pos, int R, int max_items, int *__restrict__ plan,
+// capacity).  desc[g] describes chunk g for the decode kernel: {row | split << 30, first
+// position, end position, page-table offset of the first page}, split = the row has more
+// than one chunk.  One warp; it also zeroes the decode kernel's work counters.
+__global__ void k_attn_plan(const int *__restrict__ row_pos, const int *__restrict__ row_slot, int pages_per_stream,
+                            int R, int max_items, int *__restrict__ plan, int4 *__restrict__ desc,
                             int *__restrict__ work, int nwork) {
     pdl_enter();
     const int lane = threadIdx.x & 31;
@@ -377,16 +395,28 @@ __global__ void k_attn_plan(const int *__restrict__ row_pos, int R, int max_item
         chunk *= 2;
     }
     int acc = 0;
-    for (int b = 0; b < R; b += 32) {  // exclusive prefix sum of chunk counts, 32 rows at a time
+    for (int b = 0; b < R; b += 32) {  // 32 rows at a time: prefix sum of chunk counts
         const int r = b + lane;
-        const int v = r < R ? max(0, row_pos[r] + chunk) / chunk : 0;  // rows with pos < 0: none
+        const int n = r < R ? row_pos[r] + 1 : 0;
+        const int base = r < R ? row_slot[r] * pages_per_stream : 0;
+        const int v = max(0, n - 1 + chunk) / chunk;  // rows with pos < 0 have no chunk
         int inc = v;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const int y = __shfl_up_sync(0xffffffffu, inc, o);
             if (lane >= o) inc += y;
         }
-        if (r < R) plan[2 + r] = acc + inc - v;
+        const int g0 = acc + inc - v;
+        if (r < R) plan[2 + r] = g0;
+        const int rows = min(32, R - b);
+        for (int k = 0; k < rows; ++k) {
+            const int nk = __shfl_sync(0xffffffffu, n, k), ck = __shfl_sync(0xffffffffu, v, k);
+            const int bk = __shfl_sync(0xffffffffu, base, k), gk = __shfl_sync(0xffffffffu, g0, k);
+            for (int c = lane; c < ck; c += 32) {
+                const int p0 = c * chunk;
+                desc[gk + c] = make_int4((b + k) | ((ck > 1) << 30), p0, min(nk, p0 + chunk), bk + p0 / kPage);
+            }
+        }
         acc += __shfl_sync(0xffffffffu, inc, 31);
     }
     if (lane == 0) {
@@ -403,9 +433,9 @@ struct AttnArgs {
     int pages_per_stream;
     const int *row_slot, *row_pos;
     const int *plan;        // from k_attn_plan
+    const int4 *desc;       // chunk descriptors from k_attn_plan
     int R;
     float *part;            // [chunks * 12][kPartStride] partials: m, l, pad, pad, o[64]
-    int *counter;           // [R][12] arrival counts, zero between launches
     int *work;              // next chunk to hand out; zeroed by k_attn_plan
     float *out;             // [R][768]
     // tensor-core path: write the output straight into the next GEMM's fp16 activation image
@@ -421,15 +451,35 @@ __device__ __forceinline__ size_t bimg_off(int n, int k, int N) {
     return ((size_t)(k >> 6) * N + n) * 128 + ((((k & 63) >> 3) ^ (n & 7)) << 4) + ((k & 7) << 1);
 }
 
+// Store 8 consecutive output dims (one lane's share of a head) of row r.
+__device__ __forceinline__ void attn_store8(const AttnArgs &a, int r, int k0, const float *y) {
+    if (a.bimg) {  // 8 dims = one 16-byte unit of the activation image
+        __align__(16) __half h[8], lo[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            h[j] = __float2half_rn(y[j]);
+            lo[j] = __float2half_rn(y[j] - __half2float(h[j]));
+        }
+        const size_t off = bimg_off(r, k0, a.bimg_N);
+        *reinterpret_cast<int4 *>(a.bimg + off) = *reinterpret_cast<const int4 *>(h);
+        if (a.bimg_parts == 2)
+            *reinterpret_cast<int4 *>(a.bimg + (size_t)kHidden * a.bimg_N * 2 + off) = *reinterpret_cast<const int4 *>(lo);
+    } else {
+        float *dst = a.out + (size_t)r * kHidden + k0;
+        reinterpret_cast<float4 *>(dst)[0] = make_float4(y[0], y[1], y[2], y[3]);
+        reinterpret_cast<float4 *>(dst)[1] = make_float4(y[4], y[5], y[6], y[7]);
+    }
+}
+
 // Flash-decode over fp16 pages, one CTA per SM.  A page of one layer holds K and V of all 12
 // heads for 16 positions, 48 KB contiguous ([k|v][head][16][64] fp16), so the whole page
-// moves with one cp.async.bulk.  A producer warp hands out chunks (whole pages of one row)
-// through an atomic counter and streams their pages -- with the row's query on the chunk's
-// first page -- into a 4-stage ring in shared memory; 12 consumer warps, one per head, each
-// read their head's 2 KB K and V blocks from the stage (8 lanes per position, 8 dims a lane,
-// 4 positions per step, online softmax in fp32).  At the end of a chunk a warp writes its
-// (row, head) result, or a split-K partial; the last chunk of a (row, head) to arrive merges
-// all partials (atomic arrival count, no waiting).  Every barrier wait is bounded.
+// moves with one cp.async.bulk.  A producer warp claims chunks (whole pages of one row,
+// described by k_attn_plan) from an atomic counter, one chunk ahead, and streams their pages
+// -- with the row's query on the chunk's first page -- into a 4-stage ring in shared memory;
+// 12 consumer warps, one per head, read their head's 2 KB K and V blocks from a stage (8 lanes
+// per position, 8 dims a lane, 4 positions per step, online softmax in fp32) and release it.
+// At the end of a chunk a warp writes its (row, head) result, or, for a row split into several
+// chunks, a partial that k_attn_combine merges.  Every barrier wait is bounded.
 constexpr int kAttnConsumers = kHeads;                     // consumer warps: one per head
 constexpr int kAttnThreads = (kAttnConsumers + 1) * 32;    // + the producer warp
 constexpr int kAttnStages = 4;
@@ -441,11 +491,10 @@ struct AttnStage {  // written by the producer before the stage's barrier arrive
     int r;          // row
     int pb;         // first position of the page
     int p1;         // end of the chunk (exclusive)
-    int flags;      // 1: first page of a chunk (query copied), 2: last page, 4: no more work
-    int grp;        // global chunk index (partials live at grp * 12 + head)
-    int gbase;      // first chunk of row r
-    int nchunks;    // chunks of row r
-    int pad;
+    int flags;      // 1: first page of a chunk (query copied), 2: last page, 4: no more work,
+                    // 8: the row is split (write a partial)
+    int g;          // chunk index (its partials live at g * 12 + head)
+    int pad[3];
 };
 
 __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_decode(const AttnArgs a) {
@@ -466,42 +515,24 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_decode(const AttnArgs 
     __syncthreads();
     pdl_enter();
     const int total = a.plan[1];
-    const int *istart = a.plan + 2;
 
     if (wid == kAttnConsumers) {
         // ------------------------------------------------------------------ producer warp
-        const int chunk = a.plan[0];
         int seq = 0;
         bool ok = true;
-        int grp = 0;
-        if (lane == 0) grp = atomicAdd(a.work, 1);
-        grp = __shfl_sync(0xffffffffu, grp, 0);
-        while (ok) {
-            int stop = grp >= total;
-            int next = 0;
-            if (!stop && lane == 0) next = atomicAdd(a.work, 1);  // fetched early, used after this chunk
-            int r = 0, gbase = 0, nch = 0, p0 = 0, p1 = 0, npg = 0;
-            const int *pt = nullptr;
-            if (!stop) {
-                int cnt = 0;  // rows whose first chunk is <= grp
-                for (int b = 0; b < a.R; b += 32) {
-                    const int i = b + lane;
-                    const bool in = i < a.R;
-                    const int st = in ? istart[i] : 0;
-                    cnt += __popc(__ballot_sync(0xffffffffu, in && st <= grp));
-                    if (__ballot_sync(0xffffffffu, in && st > grp)) break;
-                }
-                r = cnt - 1;
-                gbase = istart[r];
-                nch = istart[r + 1] - gbase;
-                p0 = (grp - gbase) * chunk;
-                p1 = min(a.row_pos[r] + 1, p0 + chunk);
-                npg = (p1 - p0 + kPage - 1) / kPage;
-                pt = a.page_table + (size_t)a.row_slot[r] * a.pages_per_stream + p0 / kPage;
-            }
-            for (int jb = 0; jb < (stop ? 1 : npg); jb += 32) {
-                const int pid = (!stop && jb + lane < npg) ? pt[jb + lane] : 0;
-                const int jend = stop ? jb + 1 : min(npg, jb + 32);
+        int g = 0;
+        if (lane == 0) g = atomicAdd(a.work, 1);
+        g = __shfl_sync(0xffffffffu, g, 0);
+        int4 d = g < total ? a.desc[g] : make_int4(0, 0, 0, 0);
+        for (;;) {
+            const bool stop = g >= total;
+            int gn = 0;
+            if (!stop && lane == 0) gn = atomicAdd(a.work, 1);  // claim the next chunk now
+            const int r = d.x & 0x3fffffff, split = d.x >> 30, p0 = d.y, p1 = d.z;
+            const int npg = stop ? 1 : (p1 - p0 + kPage - 1) / kPage;
+            for (int jb = 0; jb < npg && ok; jb += 32) {
+                const int pid = (!stop && jb + lane < npg) ? a.page_table[d.w + jb + lane] : 0;
+                const int jend = min(npg, jb + 32);
                 for (int j = jb; j < jend; ++j) {
                     const int page = __shfl_sync(0xffffffffu, pid, j - jb);
                     if (lane == 0) {
@@ -513,16 +544,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_decode(const AttnArgs 
                             m.r = r;
                             m.pb = p0 + j * kPage;
                             m.p1 = p1;
-                            m.flags = stop ? 4 : ((j == 0 ? 1 : 0) | (j == npg - 1 ? 2 : 0));
-                            m.grp = grp;
-                            m.gbase = gbase;
-                            m.nchunks = nch;
+                            m.flags = stop ? 4 : ((j == 0 ? 1 : 0) | (j == npg - 1 ? 2 : 0) | (split ? 8 : 0));
+                            m.g = g;
                             if (stop) {
                                 mbar_arrive(&full[s]);
                             } else {
-                                const uint32_t bytes = kAttnPageBytes + (j == 0 ? kAttnQBytes : 0);
-                                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                                mbar_expect_tx(&full[s], bytes);
+                                mbar_expect_tx(&full[s], kAttnPageBytes + (j == 0 ? kAttnQBytes : 0));
                                 bulk_g2s(pages + (size_t)s * kAttnPageBytes, a.kv + (size_t)page * kPageHalfs,
                                          kAttnPageBytes, &full[s]);
                                 if (j == 0)
@@ -534,10 +561,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_decode(const AttnArgs 
                     ++seq;
                     if (!ok) break;
                 }
-                if (!ok) break;
             }
             if (stop || !ok) break;
-            grp = __shfl_sync(0xffffffffu, next, 0);
+            g = __shfl_sync(0xffffffffu, gn, 0);
+            d = g < total ? a.desc[g] : make_int4(0, 0, 0, 0);
         }
         if (!ok && lane == 0) {
             // a consumer stopped answering: let the copies already issued land before exiting
@@ -576,14 +603,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_decode(const AttnArgs 
             vr[u] = *reinterpret_cast<const int4 *>(vb + pp * 128);
             if (st.pb + pp >= st.p1) vr[u] = make_int4(0, 0, 0, 0);  // past the end: stale bits
             const __half2 *kh = reinterpret_cast<const __half2 *>(&kr);
-            float d = 0.f;
+            float dd = 0.f;
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 const float2 kf = __half22float2(kh[e]);
-                d = fmaf(qv[2 * e], kf.x, d);
-                d = fmaf(qv[2 * e + 1], kf.y, d);
+                dd = fmaf(qv[2 * e], kf.x, dd);
+                dd = fmaf(qv[2 * e + 1], kf.y, dd);
             }
-            sc[u] = d;
+            sc[u] = dd;
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);  // the stage's data is in registers now
@@ -618,7 +645,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_decode(const AttnArgs 
         if (!(st.flags & 2)) continue;
 
         // ---- end of the chunk: merge the 4 position groups (lanes ds, ds+8, ds+16, ds+24)
-        const int r = st.r, nchunks = st.nchunks;
 #pragma unroll
         for (int off = 8; off <= 16; off <<= 1) {
             const float mo = __shfl_xor_sync(0xffffffffu, m, off);
@@ -634,84 +660,69 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_decode(const AttnArgs 
             }
             m = mx;
         }
-        const float mf = m, lf = l;
-        float of[8];
+        if (lane < 8) {
+            if (st.flags & 8) {  // split row: partial (m, l, unnormalised o) for k_attn_combine
+                float *pp = a.part + ((size_t)st.g * kHeads + hd) * kPartStride;
+                reinterpret_cast<float4 *>(pp + 4 + ds * 8)[0] = make_float4(o[0], o[1], o[2], o[3]);
+                reinterpret_cast<float4 *>(pp + 4 + ds * 8)[1] = make_float4(o[4], o[5], o[6], o[7]);
+                if (lane == 0) *reinterpret_cast<float2 *>(pp) = make_float2(m, l);
+            } else {
+                const float inv = 1.f / l;
+                float y[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) { of[j] = o[j]; o[j] = 0.f; }
+                for (int j = 0; j < 8; ++j) y[j] = o[j] * inv;
+                attn_store8(a, st.r, hd * kHeadDim + ds * 8, y);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = 0.f;
         m = -INFINITY;
         l = 0.f;
-        if (nchunks == 1) {
-            if (lane < 8) {
-                const float inv = 1.f / lf;
-                if (a.bimg) {  // 8 dims = one 16-byte unit of the activation image
-                    __align__(16) __half h[8], lo[8];
+    }
+}
+
+// Merge the split-K partials of every (row, head) whose row was split into several chunks:
+// out = sum_c exp(m_c - M) o_c / sum_c exp(m_c - M) l_c.  One warp per (row, head); lane i
+// owns dims 8 (i % 8) .. +7 of chunks i / 8, i / 8 + 4, ...
+__global__ void __launch_bounds__(256) k_attn_combine(const AttnArgs a) {
+    pdl_enter();
+    const int lane = threadIdx.x & 31;
+    const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (w >= a.R * kHeads) return;
+    const int r = w / kHeads, hd = w - r * kHeads;
+    const int g0 = a.plan[2 + r], nch = a.plan[3 + r] - g0;
+    if (nch <= 1) return;
+    const float *base = a.part + ((size_t)g0 * kHeads + hd) * kPartStride;
+    float M = -INFINITY;
+    for (int c = lane; c < nch; c += 32) M = fmaxf(M, __ldcg(base + (size_t)c * kHeads * kPartStride));
+    M = warp_max(M);
+    const int cg = lane >> 3, ds = lane & 7;
+    float L = 0.f, y[8];
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const float y = of[j] * inv;
-                        h[j] = __float2half_rn(y);
-                        lo[j] = __float2half_rn(y - __half2float(h[j]));
-                    }
-                    const size_t off = bimg_off(r, hd * kHeadDim + ds * 8, a.bimg_N);
-                    *reinterpret_cast<int4 *>(a.bimg + off) = *reinterpret_cast<const int4 *>(h);
-                    if (a.bimg_parts == 2)
-                        *reinterpret_cast<int4 *>(a.bimg + (size_t)kHidden * a.bimg_N * 2 + off) =
-                            *reinterpret_cast<const int4 *>(lo);
-                } else {
-                    float *dst = a.out + (size_t)r * kHidden + hd * kHeadDim + ds * 8;
-                    reinterpret_cast<float4 *>(dst)[0] =
-                        make_float4(of[0] * inv, of[1] * inv, of[2] * inv, of[3] * inv);
-                    reinterpret_cast<float4 *>(dst)[1] =
-                        make_float4(of[4] * inv, of[5] * inv, of[6] * inv, of[7] * inv);
-                }
-            }
-            continue;
-        }
-        float *pp = a.part + ((size_t)st.grp * kHeads + hd) * kPartStride;
-        if (lane < 8) {
-            reinterpret_cast<float4 *>(pp + 4 + ds * 8)[0] = make_float4(of[0], of[1], of[2], of[3]);
-            reinterpret_cast<float4 *>(pp + 4 + ds * 8)[1] = make_float4(of[4], of[5], of[6], of[7]);
-            if (lane == 0) { pp[0] = mf; pp[1] = lf; }
-        }
-        // publish: the warp's stores, then (one lane) a device fence and the arrival count
-        __syncwarp();
-        int last = 0;
-        if (lane == 0) {
-            __threadfence();
-            last = (atomicAdd(a.counter + r * kHeads + hd, 1) == nchunks - 1);
-            __threadfence();
-        }
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (!last) continue;
-        // this warp saw every other chunk arrive: combine all chunks of (r, hd)
-        const size_t ibase = (size_t)st.gbase * kHeads + hd;
-        float M = -INFINITY;
-        for (int cc = lane; cc < nchunks; cc += 32)
-            M = fmaxf(M, __ldcg(a.part + (ibase + (size_t)cc * kHeads) * kPartStride));
-        M = warp_max(M);
-        float L = 0.f;
-        float o0 = 0.f, o1 = 0.f;  // dims 2*lane, 2*lane+1
-        for (int cc = 0; cc < nchunks; ++cc) {
-            const float *q = a.part + (ibase + (size_t)cc * kHeads) * kPartStride;
-            const float w = __expf(__ldcg(q) - M);
-            L = fmaf(__ldcg(q + 1), w, L);
-            const float2 ov = __ldcg(reinterpret_cast<const float2 *>(q + 4) + lane);
-            o0 = fmaf(ov.x, w, o0);
-            o1 = fmaf(ov.y, w, o1);
-        }
+    for (int j = 0; j < 8; ++j) y[j] = 0.f;
+    for (int c = cg; c < nch; c += 4) {
+        const float *q = base + (size_t)c * kHeads * kPartStride;
+        const float2 ml = __ldcg(reinterpret_cast<const float2 *>(q));
+        const float4 o0 = __ldcg(reinterpret_cast<const float4 *>(q + 4 + ds * 8));
+        const float4 o1 = __ldcg(reinterpret_cast<const float4 *>(q + 4 + ds * 8) + 1);
+        const float wgt = ml.x == -INFINITY ? 0.f : __expf(ml.x - M);
+        L = fmaf(ml.y, wgt, L);
+        y[0] = fmaf(o0.x, wgt, y[0]); y[1] = fmaf(o0.y, wgt, y[1]);
+        y[2] = fmaf(o0.z, wgt, y[2]); y[3] = fmaf(o0.w, wgt, y[3]);
+        y[4] = fmaf(o1.x, wgt, y[4]); y[5] = fmaf(o1.y, wgt, y[5]);
+        y[6] = fmaf(o1.z, wgt, y[6]); y[7] = fmaf(o1.w, wgt, y[7]);
+    }
+#pragma unroll
+    for (int off = 8; off <= 16; off <<= 1) {
+        L += __shfl_xor_sync(0xffffffffu, L, off);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) y[j] += __shfl_xor_sync(0xffffffffu, y[j], off);
+    }
+    if (lane < 8) {
         const float inv = 1.f / L;
-        if (a.bimg) {
-            const float y0 = o0 * inv, y1 = o1 * inv;
-            const __half2 h = __floats2half2_rn(y0, y1);
-            const size_t off = bimg_off(r, hd * kHeadDim + 2 * lane, a.bimg_N);
-            *reinterpret_cast<__half2 *>(a.bimg + off) = h;
-            if (a.bimg_parts == 2)
-                *reinterpret_cast<__half2 *>(a.bimg + (size_t)kHidden * a.bimg_N * 2 + off) =
-                    __floats2half2_rn(y0 - __low2float(h), y1 - __high2float(h));
-        } else {
-            float *dst = a.out + (size_t)r * kHidden + hd * kHeadDim;
-            reinterpret_cast<float2 *>(dst)[lane] = make_float2(o0 * inv, o1 * inv);
-        }
-        if (lane == 0) a.counter[r * kHeads + hd] = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) y[j] *= inv;
+        attn_store8(a, r, hd * kHeadDim + ds * 8, y);
     }
 }
 

@@ -3,7 +3,7 @@
 // mossgpu_attention_decode_paged: the engine's paged fp16 flash-decode (one layer) for
 // callers that keep their own KV pages, e.g. a host framework that manages the cache and
 // only wants the attention kernel.  Every pointer is a device pointer; the caller also
-// provides the scratch workspace (plan, split-K partials, arrival counters).
+// provides the scratch workspace (plan, chunk descriptors and counter, split-K partials).
 #include "../../include/mossgpu.h"
 
 #include <cuda_runtime.h>
@@ -31,7 +31,8 @@ constexpr int kMaxDevices = 64;
 std::mutex g_attr_mu;
 bool g_attr_set[kMaxDevices] = {};
 
-int launch_decode(const mossgpu::AttnArgs &t, cudaStream_t st, const char *who) {
+// plan -> decode -> combine on `st` over caller-provided scratch.
+int run_attention(mossgpu::AttnArgs t, int *work, int4 *desc, int max_items, cudaStream_t st, const char *who) {
     using namespace mossgpu;
     int dev = -1;
     cudaError_t e = cudaGetDevice(&dev);
@@ -45,7 +46,12 @@ int launch_decode(const mossgpu::AttnArgs &t, cudaStream_t st, const char *who) 
             g_attr_set[dev] = true;
         }
     }
+    k_attn_plan<<<1, 32, 0, st>>>(t.row_pos, t.row_slot, t.pages_per_stream, t.R, max_items, const_cast<int *>(t.plan),
+                                  desc, work, 1);
+    t.desc = desc;
+    t.work = work;
     k_attn_decode<<<148, kAttnThreads, kAttnSmem, st>>>(t);
+    k_attn_combine<<<(t.R * kHeads + 7) / 8, 256, 0, st>>>(t);
     e = cudaGetLastError();
     if (e != cudaSuccess) return op_fail(std::string(who) + " launch: " + cudaGetErrorString(e));
     return 0;
@@ -60,21 +66,24 @@ int check_alignment(const float *q, const void *kv_layer, const char *who) {
 
 size_t round_up(size_t n) { return (n + kAlign - 1) / kAlign * kAlign; }
 
-// Workspace layout for R rows: [plan: 2 + R + 1 ints][counters: R * 12 ints, chunk counter]
-// [partials]
+// Workspace layout for R rows: [plan: 2 + R + 1 ints][chunk counter][chunk descriptors:
+// G int4][partials: G * 12 * kPartStride floats], G = chunks the plan may cut (>= R).
+constexpr size_t kGroupBytes = sizeof(float) * mossgpu::kPartStride * mossgpu::kHeads;  // partials of one chunk
 struct Layout {
-    size_t plan, counters, part, total;
-    int items;
+    size_t plan, work, desc, part;
+    int groups;
 };
 
 Layout layout_for(int R, size_t bytes) {
     Layout l{};
     l.plan = 0;
-    l.counters = round_up(sizeof(int) * (size_t(R) + 3));
-    l.part = l.counters + round_up(sizeof(int) * (size_t(R) * mossgpu::kHeads + 1));
-    const size_t part_bytes = bytes > l.part ? bytes - l.part : 0;
-    l.items = int(std::min<size_t>(part_bytes / (sizeof(float) * mossgpu::kPartStride), 1u << 30));
-    l.total = bytes;
+    l.work = round_up(sizeof(int) * (size_t(R) + 3));
+    l.desc = l.work + kAlign;
+    const size_t avail = bytes > l.desc ? bytes - l.desc : 0;
+    size_t g = avail / (kGroupBytes + sizeof(int4));
+    while (g > 0 && round_up(g * sizeof(int4)) + g * kGroupBytes > avail) --g;
+    l.groups = int(std::min<size_t>(g, 1u << 26));
+    l.part = l.desc + round_up(size_t(l.groups) * sizeof(int4));
     return l;
 }
 
@@ -86,9 +95,10 @@ const char *mossgpu_op_last_error(void) { return g_op_error.c_str(); }
 
 size_t mossgpu_attention_workspace_bytes(int R) {
     if (R <= 0) return 0;
-    // room for 8 split-K chunks per (row, head); the plan widens chunks to fit any length
+    // room for 8 split-K chunks per row on average; the plan widens chunks to fit any length
     const Layout l = layout_for(R, 0);
-    return l.part + sizeof(float) * mossgpu::kPartStride * size_t(R) * mossgpu::kHeads * 8;
+    const size_t g = size_t(R) * 8;
+    return l.desc + round_up(g * sizeof(int4)) + g * kGroupBytes;
 }
 
 int mossgpu_attention_decode_paged(const float *q, const void *kv_layer, const int32_t *page_table,
@@ -100,20 +110,12 @@ int mossgpu_attention_decode_paged(const float *q, const void *kv_layer, const i
         return op_fail("attention_decode_paged: a required pointer is NULL");
     if (pages_per_stream <= 0) return op_fail("attention_decode_paged: pages_per_stream must be positive");
     const Layout l = layout_for(R, workspace_bytes);
-    if (l.items < R * kHeads)
+    if (l.groups < R)
         return op_fail("attention_decode_paged: workspace too small (need mossgpu_attention_workspace_bytes(R))");
     if (reinterpret_cast<uintptr_t>(workspace) % 16 != 0)
         return op_fail("attention_decode_paged: workspace must be 16-byte aligned");
     if (check_alignment(q, kv_layer, "attention_decode_paged") != 0) return 1;
-    cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
     char *ws = static_cast<char *>(workspace);
-    int *plan = reinterpret_cast<int *>(ws + l.plan);
-    int *counter = reinterpret_cast<int *>(ws + l.counters);
-    float *part = reinterpret_cast<float *>(ws + l.part);
-    // arrival counters must start at zero (the workspace's contents are unspecified)
-    cudaError_t e = cudaMemsetAsync(counter, 0, sizeof(int) * size_t(R) * kHeads, st);
-    if (e != cudaSuccess) return op_fail(std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
-    k_attn_plan<<<1, 32, 0, st>>>(row_pos, R, l.items, plan, counter + R * kHeads, 1);
     AttnArgs t{};
     t.q = q;
     t.kv = static_cast<const __half *>(kv_layer);
@@ -121,13 +123,12 @@ int mossgpu_attention_decode_paged(const float *q, const void *kv_layer, const i
     t.pages_per_stream = pages_per_stream;
     t.row_slot = row_slot;
     t.row_pos = row_pos;
-    t.plan = plan;
+    t.plan = reinterpret_cast<int *>(ws + l.plan);
     t.R = R;
-    t.part = part;
-    t.counter = counter;
-    t.work = counter + R * kHeads;
+    t.part = reinterpret_cast<float *>(ws + l.part);
     t.out = out;
-    return launch_decode(t, st, "attention_decode_paged");
+    return run_attention(t, reinterpret_cast<int *>(ws + l.work), reinterpret_cast<int4 *>(ws + l.desc),
+                         l.groups * kHeads, static_cast<cudaStream_t>(cuda_stream), "attention_decode_paged");
 }
 
 }  // extern "C"
@@ -139,18 +140,22 @@ int mossgpu_attention_decode_paged(const float *q, const void *kv_layer, const i
 // audio callback in a plugin host (cudaMalloc and cudaFree can block for milliseconds, and
 // cudaFree synchronises the whole device), or a host program whose device memory is owned by
 // another allocator that it may not go around.  For them the scratch this kernel needs (the
-// split-K plan, the arrival counters and the partial results) lives in the fixed array below,
+// split-K plan, the chunk counter and descriptors, the partial results) lives in the fixed array below,
 // which the CUDA runtime creates on every GPU that loads this library and keeps until the
 // process exits.
 namespace {
 
-constexpr int kNoAllocMaxRows = 256;    // rows per call
-constexpr int kNoAllocMaxItems = 4096;  // split-K (chunk, head) partials; chunks widen to fit
-constexpr size_t kNoAllocPlanBytes = 2048;                                   // 2 + R + 1 ints
-constexpr size_t kNoAllocCounterBytes = sizeof(int) * kNoAllocMaxRows * mossgpu::kHeads + 256;  // + chunk counter
-constexpr size_t kNoAllocPartBytes = sizeof(float) * mossgpu::kPartStride * kNoAllocMaxItems;
-constexpr size_t kNoAllocScratchBytes = kNoAllocPlanBytes + kNoAllocCounterBytes + kNoAllocPartBytes;  // ~1.08 MiB
+constexpr int kNoAllocMaxRows = 256;     // rows per call
+constexpr int kNoAllocMaxGroups = 341;   // split-K chunks (12 partials each); chunks widen to fit
+constexpr size_t kNoAllocPlanBytes = 2048;                                    // 2 + R + 1 ints
+constexpr size_t kNoAllocWorkBytes = 256;                                     // chunk counter
+constexpr size_t kNoAllocDescBytes = 5632;                                    // chunk descriptors
+constexpr size_t kNoAllocPartBytes = kGroupBytes * kNoAllocMaxGroups;
+constexpr size_t kNoAllocScratchBytes =
+    kNoAllocPlanBytes + kNoAllocWorkBytes + kNoAllocDescBytes + kNoAllocPartBytes;  // ~1.07 MiB
 static_assert(kNoAllocPlanBytes >= sizeof(int) * (kNoAllocMaxRows + 3), "plan area too small");
+static_assert(kNoAllocDescBytes >= sizeof(int4) * kNoAllocMaxGroups, "descriptor area too small");
+static_assert(kNoAllocMaxGroups >= kNoAllocMaxRows, "every row needs at least one chunk");
 
 static __device__ __align__(256) unsigned char g_attn_noalloc_scratch[kNoAllocScratchBytes];
 
@@ -191,17 +196,9 @@ extern "C" int mossgpu_attention_decode_paged_noalloc(const float *q, const void
     if (check_alignment(q, kv_layer, "attention_decode_paged_noalloc") != 0) return 1;
     void *scratch = nullptr;
     if (noalloc_scratch(&scratch) != 0) return 1;
-    cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
     char *base = static_cast<char *>(scratch);
-    int *plan = reinterpret_cast<int *>(base);
-    int *counter = reinterpret_cast<int *>(base + kNoAllocPlanBytes);
-    float *part = reinterpret_cast<float *>(base + kNoAllocPlanBytes + kNoAllocCounterBytes);
-    // the array keeps whatever the previous call left: the arrival counters must start at zero
-    // (the plan is rewritten and the partials are written before they are read)
-    cudaError_t e = cudaMemsetAsync(counter, 0, sizeof(int) * size_t(R) * kHeads, st);
-    if (e != cudaSuccess) return op_fail(std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
-    int *work = counter + kNoAllocMaxRows * kHeads;  // zeroed by the plan kernel
-    k_attn_plan<<<1, 32, 0, st>>>(row_pos, R, kNoAllocMaxItems, plan, work, 1);
+    // every part of the array is rewritten before it is read: the plan kernel writes the plan
+    // and descriptors and zeroes the chunk counter; partials are written before k_attn_combine
     AttnArgs t{};
     t.q = q;
     t.kv = static_cast<const __half *>(kv_layer);
@@ -209,11 +206,12 @@ extern "C" int mossgpu_attention_decode_paged_noalloc(const float *q, const void
     t.pages_per_stream = pages_per_stream;
     t.row_slot = row_slot;
     t.row_pos = row_pos;
-    t.plan = plan;
+    t.plan = reinterpret_cast<int *>(base);
     t.R = R;
-    t.part = part;
-    t.counter = counter;
-    t.work = work;
+    t.part = reinterpret_cast<float *>(base + kNoAllocPlanBytes + kNoAllocWorkBytes + kNoAllocDescBytes);
     t.out = out;
-    return launch_decode(t, st, "attention_decode_paged_noalloc");
+    return run_attention(t, reinterpret_cast<int *>(base + kNoAllocPlanBytes),
+                         reinterpret_cast<int4 *>(base + kNoAllocPlanBytes + kNoAllocWorkBytes),
+                         kNoAllocMaxGroups * kHeads, static_cast<cudaStream_t>(cuda_stream),
+                         "attention_decode_paged_noalloc");
 }

@@ -161,7 +161,7 @@ const char *mossgpu_op_last_error(void);
  * allocate device memory when they run it -- for example a real-time audio callback in a
  * plugin host, where cudaMalloc/cudaFree may block for milliseconds (cudaFree synchronises
  * the device), or a program whose device memory belongs to another allocator.  It takes no
- * workspace and allocates nothing: its scratch (~1.08 MiB) is a fixed array that the library
+ * workspace and allocates nothing: its scratch (~1.07 MiB) is a fixed array that the library
  * places on every GPU that loads it, kept until the process exits.
  *   - R must be <= 256 rows; larger batches are rejected with an error (use the workspace
  *     entry point above).
