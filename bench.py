@@ -208,6 +208,12 @@ def run_ours(args, rank, world, local_rank, dist):
 
     reset_states()
     params = pkg.SampleParams.make(greedy=True, repetition_penalty=1.2, min_frames=1 << 30)
+    if args.profile_frames:  # the short run the ncu captures use: one warm-up frame, then N
+        eng.step_frames(sids, params, 1, want_codes=False)
+        eng.step_frames(sids, params, args.profile_frames, want_codes=False)
+        torch.cuda.synchronize()
+        eng.close()
+        return
 
     # warm-up: captures both the multi-frame and the single-frame graphs
     eng.step_frames(sids, params, W)
@@ -346,6 +352,9 @@ def main():
     ap.add_argument("--lmin", type=int, default=64)
     ap.add_argument("--lmax", type=int, default=1024)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-frames", type=int, default=0,
+                    help="run this many frames of the N=1 workload after one warm-up frame and exit "
+                         "(the command the ncu captures under profiles/ use)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world = int(os.environ.get("WORLD_SIZE", "1"))

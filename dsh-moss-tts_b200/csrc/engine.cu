@@ -18,6 +18,7 @@
 
 #include "kernels.cuh"
 #include "gemm_tc.cuh"
+#include "step_small.cuh"
 
 namespace mossgpu {
 
@@ -63,6 +64,7 @@ Engine::Engine(const std::string &path, int device, int max_streams, int max_ctx
     CK(cudaStreamCreateWithFlags(&own_stream_, cudaStreamNonBlocking));
     stream_ = own_stream_;
     if (const char *v = std::getenv("MOSSGPU_PDL")) pdl_ = std::strcmp(v, "0") != 0;
+    if (const char *v = std::getenv("MOSSGPU_STEP_KERNEL")) step_kernel_ = std::strcmp(v, "0") != 0;
     load_weights(path);
     pages_per_stream_ = (max_ctx + kPage - 1) / kPage;
     n_pages_ = kv_pages > 0 ? kv_pages : max_streams * pages_per_stream_;
@@ -173,6 +175,17 @@ void Engine::load_weights(const std::string &path) {
         return L;
     };
     for (int i = 0; i < kLayers; ++i) global_[i] = layer("g" + std::to_string(i) + ".");
+    {  // per-layer pointer table of the persistent small-batch step
+        StepLayer h[kLayers];
+        for (int i = 0; i < kLayers; ++i) {
+            const Layer &L = global_[i];
+            h[i] = StepLayer{L.attn.qs, L.proj.qs, L.fc_in.qs, L.fc_out.qs, L.attn.sc, L.proj.sc, L.fc_in.sc,
+                             L.fc_out.sc, L.ln1_w, L.ln1_b, L.ln2_w, L.ln2_b, L.attn_b, L.proj_b, L.fc_in_b,
+                             L.fc_out_b};
+        }
+        step_layers_ = dalloc<StepLayer>(kLayers, owned_);
+        CK(cudaMemcpy(step_layers_, h, sizeof(h), cudaMemcpyHostToDevice));
+    }
     local_ = layer("local.");
     lnf_w_ = vec("lnf.w", kHidden);
     lnf_b_ = vec("lnf.b", kHidden);
@@ -217,6 +230,9 @@ void Engine::allocate_state() {
     codes_hist_ = dalloc<int>(size_t(kMaxFramesPerCall) * max_streams_ * kNVq, owned_);
     bimg_a_ = dalloc<uint8_t>(2 * size_t(kHidden) * kTcMaxRows * 2, owned_);  // hi and lo parts
     bimg_mlp_ = dalloc<uint8_t>(2 * size_t(kFF) * kTcMaxRows * 2, owned_);
+    step_acc_ = dalloc<unsigned long long>(size_t(kLayers) * 2 * kSmallMaxR * kHidden, owned_);
+    step_sync_ = dalloc<unsigned>(kStepSyncs, owned_);
+    step_apart_ = dalloc<float>(size_t(kHeads) * kSmallMaxR * kStepMaxChunks * kPartStride, owned_);
     dev_err_ = dalloc<int>(4, owned_);
     CK(cudaMemset(dev_err_, 0, 4 * sizeof(int)));
     {
@@ -271,19 +287,36 @@ namespace {
 // the previous kernel on the stream is still running, and orders itself with pdl_wait()
 // (every kernel of the frame calls it before touching data an earlier kernel produced).
 template <typename... KArgs, typename... Args>
-void launch_k(bool pdl, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
-              Args &&...args) {
+void launch_kc(bool pdl, int cluster, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+               Args &&...args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[2];
+    int n = 0;
+    if (pdl) {
+        attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[n].val.programmaticStreamSerializationAllowed = 1;
+        ++n;
+    }
+    if (cluster > 0) {
+        attr[n].id = cudaLaunchAttributeClusterDimension;
+        attr[n].val.clusterDim.x = cluster;
+        attr[n].val.clusterDim.y = 1;
+        attr[n].val.clusterDim.z = 1;
+        ++n;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
+    cfg.numAttrs = n;
     CK(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+}
+
+template <typename... KArgs, typename... Args>
+void launch_k(bool pdl, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+              Args &&...args) {
+    launch_kc(pdl, 0, kernel, grid, block, smem, st, std::forward<Args>(args)...);
 }
 
 }  // namespace
@@ -340,15 +373,16 @@ void launch_gemv(GemvArgs a, cudaStream_t st, bool pdl) {
 
 void Engine::set_smem_limits() {
     CK(cudaFuncSetAttribute(k_attn_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem));
+    CK(cudaFuncSetAttribute(k_global_step_small, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kStepSmem)));
     set_attr_all<PRO_LN, EPI_QKV>();
     set_attr_all<PRO_NONE, EPI_RESID>();
     set_attr_all<PRO_LN, EPI_GELU>();
     set_attr_all<PRO_LN, EPI_STORE>();
-    // the stage count depends on N, so the largest footprint is not necessarily at N = 256
+    // largest footprint over the batch slices a launch may use (16..64 rows, most stages)
     int s1 = 0, s3 = 0;
-    for (int n = 16; n <= kTcMaxRows; n += 16) {
-        s1 = std::max(s1, tc_smem_bytes(n, TC_F16));
-        s3 = std::max(s3, tc_smem_bytes(n, TC_F16X3));
+    for (int n = 16; n <= kTcMaxNS; n += 16) {
+        s1 = std::max(s1, tc_smem_bytes(n, TC_F16, tc_max_stages(n, TC_F16)));
+        s3 = std::max(s3, tc_smem_bytes(n, TC_F16X3, tc_max_stages(n, TC_F16X3)));
     }
     CK(cudaFuncSetAttribute(k_gemm_tc<TC_STORE, TC_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, s1));
     CK(cudaFuncSetAttribute(k_gemm_tc<TC_QKV, TC_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, s1));
@@ -375,28 +409,33 @@ bool Engine::use_tc(int R) const {
 
 namespace {
 
-// Grid: weight tiles x K splits x batch splits.  Splitting the batch rows (nsub per CTA)
-// multiplies the CTAs that stream weights in parallel -- at 64 rows a QKV GEMM has only 18
-// weight tiles -- at the price of reading each weight tile once per batch split (from L2).
+// Grid: weight tiles x cluster CTAs (split-K) x batch slices of <= 64 rows.  At 64 rows a QKV
+// GEMM has 18 weight tiles; clusters of 8 give it 144 CTAs streaming 1-2 K chunks each.
 template <int EPI>
-void launch_tc(TcArgs a, int ksplit, int prec, cudaStream_t st, bool pdl) {
-    const int nchunks = a.K / kTcK;
-    a.ksplit = ksplit;
-    int nsub = a.N <= 128 ? 32 : 64;
-    while (a.N % nsub) nsub >>= 1;  // N is a multiple of 16
+void launch_tc(TcArgs a, int prec, cudaStream_t st, bool pdl) {
+    const int tiles = a.rows / kTcM, nchunks = a.K / kTcK;
+    int nsub = std::min(a.N, kTcMaxNS);
+    while (a.N % nsub) nsub -= 16;  // N is a multiple of 16
+    const int nz = a.N / nsub;
+    // split K over the largest cluster (<= 8) that keeps every CTA of the grid resident
+    int C = kTcMaxCluster;
+    while (C > 1 && (tiles * C * nz > 148 || C > nchunks)) C >>= 1;
+    const int per = (nchunks + C - 1) / C;  // most chunks one CTA handles
     a.nsub = nsub;
-    dim3 grid(a.rows / kTcM, (nchunks + ksplit - 1) / ksplit, a.N / nsub);
+    a.csize = C;
+    a.stages = std::min(per, tc_max_stages(nsub, prec));
+    const dim3 grid(tiles * C, 1, nz);
     if (prec == TC_F16X3)
-        launch_k(pdl, k_gemm_tc<EPI, TC_F16X3>, grid, dim3(kTcThreads), tc_smem_bytes(nsub, TC_F16X3), st, a);
+        launch_kc(pdl, C, k_gemm_tc<EPI, TC_F16X3>, grid, dim3(kTcThreads), tc_smem_bytes(nsub, TC_F16X3, a.stages), st,
+                  a);
     else
-        launch_k(pdl, k_gemm_tc<EPI, TC_F16>, grid, dim3(kTcThreads), tc_smem_bytes(nsub, TC_F16), st, a);
+        launch_kc(pdl, C, k_gemm_tc<EPI, TC_F16>, grid, dim3(kTcThreads), tc_smem_bytes(nsub, TC_F16, a.stages), st, a);
 }
 
 }  // namespace
 
 // The block of llm.cpp:230-246 on tensor cores (R > 8 rows): activation images built by
-// k_build_bimg (LayerNorm fused), tcgen05 GEMMs with fused epilogues, split-K with atomic
-// residual adds for the two 768-row outputs (proj, fc_out) so that enough SMs stream weights.
+// k_build_bimg (LayerNorm fused), tcgen05 GEMMs with cluster split-K and fused epilogues.
 void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_slot, const int *row_pos, int lpos,
                       float *x) {
     const int N = (R + 15) / 16 * 16;
@@ -425,7 +464,7 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
         a.page_table = page_table_;
         a.pages_per_stream = pages_per_stream_;
     }
-    launch_tc<TC_QKV>(a, kHidden / kTcK, prec, stream_, pdl_);
+    launch_tc<TC_QKV>(a, prec, stream_, pdl_);
     mark(local ? KK_QKV_L : KK_QKV_G);
     // attention writes straight into proj's activation image; its padding rows are still
     // zero from the LN1 image built above with the same N
@@ -469,7 +508,7 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
     p.bias = L.proj_b;
     p.out = x;
     p.ldo = kHidden;
-    launch_tc<TC_RESID>(p, 3, prec, stream_, pdl_);  // 6 tiles x 4 K-splits
+    launch_tc<TC_RESID>(p, prec, stream_, pdl_);
     mark(local ? KK_PROJ_L : KK_PROJ_G);
     launch_k(pdl_, k_build_bimg, dim3(N), dim3(256), kHidden * 4, stream_, x, kHidden, R, N, kHidden, L.ln2_w, L.ln2_b, tc_parts(prec), bimg_a_);
     mark(KK_BIMG);
@@ -484,7 +523,7 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
     f.K = kHidden;
     f.bias = L.fc_in_b;
     f.bimg_out = bimg_mlp_;
-    launch_tc<TC_GELU_B>(f, kHidden / kTcK, prec, stream_, pdl_);
+    launch_tc<TC_GELU_B>(f, prec, stream_, pdl_);
     mark(local ? KK_FCIN_L : KK_FCIN_G);
     TcArgs o{};
     o.N = N;
@@ -498,7 +537,7 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
     o.bias = L.fc_out_b;
     o.out = x;
     o.ldo = kHidden;
-    launch_tc<TC_RESID>(o, 6, prec, stream_, pdl_);  // 6 tiles x 8 K-splits
+    launch_tc<TC_RESID>(o, prec, stream_, pdl_);
     mark(local ? KK_FCOUT_L : KK_FCOUT_G);
 }
 
@@ -519,7 +558,7 @@ void Engine::heads_tc(int ch, int R) {
     h.K = kHidden;
     h.out = logits_ + size_t(ch) * kCodebook;
     h.ldo = kNVq * kCodebook;
-    launch_tc<TC_STORE>(h, kHidden / kTcK, prec, stream_, pdl_);
+    launch_tc<TC_STORE>(h, prec, stream_, pdl_);
     mark(KK_HEADS);
 }
 
@@ -532,7 +571,9 @@ void Engine::check_device_error() {
         *h_err_ = 0;
         CK(cudaMemsetAsync(dev_err_, 0, sizeof(int), stream_));
         CK(cudaStreamSynchronize(stream_));
-        throw std::runtime_error(std::string(e == 7 || e == 8 ? "decode-attention page ring" : "tensor-core GEMM barrier") +
+        throw std::runtime_error(std::string(e == 7 || e == 8     ? "decode-attention page ring"
+                                             : e >= 11 && e <= 14 ? "persistent global step"
+                                                                  : "tensor-core GEMM barrier") +
                                  " wait timed out (code " + std::to_string(e) + ")");
     }
 }
@@ -644,7 +685,49 @@ void Engine::block(const Layer &L, int li, bool local, int R, const int *row_slo
 }
 
 // 12 global layers over rows already embedded in x_ (row_pos = positions being written).
+// Up to 8 rows on the CUDA-core path: one persistent kernel (step_small.cuh); otherwise the
+// layer-by-layer launches.
 void Engine::global_layers(int R, const int *row_slot, const int *row_pos) {
+    if (step_kernel_ && R <= kSmallMaxR && !use_tc(R)) {
+        StepArgs s{};
+        s.layers = static_cast<const StepLayer *>(step_layers_);
+        s.kv = kv_;
+        s.layer_halfs = size_t(n_pages_) * kPageHalfs;
+        s.page_table = page_table_;
+        s.pages_per_stream = pages_per_stream_;
+        s.row_slot = row_slot;
+        s.row_pos = row_pos;
+        s.R = R;
+        s.rope = rope_;
+        s.x = x_;
+        s.q = q_;
+        s.apart = step_apart_;
+        s.acc = step_acc_;
+        s.sync = step_sync_;
+        s.err = dev_err_;
+        const DevMat *ms[4] = {&global_[0].attn, &global_[0].proj, &global_[0].fc_in, &global_[0].fc_out};
+        for (int i = 0; i < 4; ++i) {
+            s.weight_bytes[2 * i] = size_t(ms[i]->rows / 4) * (ms[i]->cols / 32) * 128;
+            s.weight_bytes[2 * i + 1] = size_t(ms[i]->rows / 4) * (ms[i]->cols / 32) * 8;
+        }
+        // accumulators and counters start at zero (plain stream order: the kernel is not a
+        // programmatic dependent of the memsets)
+        CK(cudaMemsetAsync(step_acc_, 0, sizeof(unsigned long long) * kLayers * 2 * size_t(R) * kHidden, stream_));
+        CK(cudaMemsetAsync(step_sync_, 0, sizeof(unsigned) * kStepSyncs, stream_));
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(kStepCtas);
+        cfg.blockDim = dim3(kStepThreads);
+        cfg.dynamicSmemBytes = kStepSmem;
+        cfg.stream = stream_;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeCooperative;  // all 148 CTAs resident at once
+        attr[0].val.cooperative = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        CK(cudaLaunchKernelEx(&cfg, k_global_step_small, s));
+        mark(KK_STEP_SMALL);
+        return;
+    }
     // ordinary launch: in a global step alone this kernel follows a host-to-device copy
     launch_k(false, k_attn_plan, dim3(1), dim3(32), 0, stream_, row_pos, row_slot, pages_per_stream_, R, attn_items_,
              plan_, desc_, work_, kLayers);
@@ -1030,7 +1113,8 @@ const char *kernel_kind_name(int kind) {
         "page_updates", "gather_hidden", "lookup_slot_row", "embed_frame", "attn_plan",
         "gemv_qkv_global", "attn_decode_paged", "gemv_proj_global", "gemv_fc_in_global", "gemv_fc_out_global", "ln_f",
         "gemv_qkv_local", "attn_local", "gemv_proj_local", "gemv_fc_in_local", "gemv_fc_out_local", "gate_w8a8",
-        "gemv_audio_heads", "sample_greedy", "frame_commit", "build_activation_image", "attn_combine"};
+        "gemv_audio_heads", "sample_greedy", "frame_commit", "build_activation_image", "attn_combine",
+        "global_step_persistent"};
     return (kind >= 0 && kind < KK_COUNT) ? names[kind] : "?";
 }
 

@@ -2,8 +2,10 @@
 //
 //   Y[n][m] = sum_k X[n][k] * W[m][k],   W = int8 Q8_0 blocks x fp16 scales, X fp16
 //
-// "Swap AB" so the weight rows form the MMA M dimension (128 per CTA) and the batch rows the
-// N dimension (16..256): D[128][N] fp32 lives in tensor memory (TMEM).  Per K chunk of 64:
+// "Swap AB" so the weight rows form the MMA M dimension (128 per tile) and the batch rows the
+// N dimension (16..64 per CTA): D[128][N] fp32 lives in tensor memory (TMEM).  The K chunks
+// (64 each) of one weight tile are split over a thread-block cluster of C CTAs (split-K);
+// per K chunk of a CTA:
 //   - one producer thread bulk-copies (cp.async.bulk, no tensor map, no multicast) the
 //     weight tile's int8 quants (8 KB), its fp16 scales (512 B) and the activation tile
 //     (N x 128 B, already stored in the SWIZZLE_128B K-major image by the previous kernel);
@@ -11,10 +13,13 @@
 //     image, 16 KB), fence the async proxy and arrive;
 //   - one MMA thread issues four tcgen05.mma.kind::f16 (K = 16 each) and commits to the
 //     stage's "empty" barrier.
-// After the last chunk the same four warps read D back with tcgen05.ld and run the epilogue
-// (bias / RoPE / KV append, GELU into the next GEMM's activation image, residual add, or a
-// plain store).  Every mbarrier wait is bounded: on time-out the kernel records an error code
-// and leaves through the normal exit path (TMEM is always freed).
+// After the last chunk the four warps read the partial D back with tcgen05.ld and scatter it
+// through distributed shared memory: CTA j of the cluster receives every CTA's partial of
+// tile rows [128 j / C, 128 (j + 1) / C), sums the C partials in a fixed order and runs the
+// epilogue for those rows (bias / RoPE / KV append, GELU into the next GEMM's activation
+// image, residual add, or a plain store).  No atomics; the result does not depend on timing.
+// Every mbarrier wait is bounded: on time-out the kernel records an error code and leaves
+// through the normal exit path (TMEM is always freed, every CTA reaches the cluster barriers).
 //
 // Weight layout (repacked from the file at load, a byte permutation):
 //   qt [rows/128][K/64][128][64] int8, the four 16-byte pieces of each 64-byte row stored at
@@ -37,7 +42,8 @@ namespace {
 constexpr int kTcM = 128;      // weight rows per CTA (MMA M)
 constexpr int kTcK = 64;       // K per pipeline stage (one 128-byte swizzle row of fp16)
 constexpr int kTcThreads = 192;
-constexpr int kTcMaxN = 256;
+constexpr int kTcMaxNS = 64;   // batch rows per CTA (MMA N); more rows split over gridDim.z
+constexpr int kTcMaxCluster = 8;
 
 enum { TC_STORE = 0, TC_QKV = 1, TC_RESID = 2, TC_GELU_B = 3 };
 
@@ -47,11 +53,12 @@ struct TcArgs {
     int rows, K;            // weight matrix shape
     const uint8_t *bimg;    // activation image [K/64][N][128 B]
     int N;                  // padded batch rows (multiple of 16, <= 256): rows of the activation image
-    int nsub;               // batch rows per CTA along gridDim.z (divides N, multiple of 16)
+    int nsub;               // batch rows per CTA along gridDim.z (divides N, multiple of 16, <= 64)
     int R;                  // real batch rows (<= N)
-    int ksplit;             // K chunks per CTA along gridDim.y (split-K, TC_RESID/TC_STORE only)
+    int csize;              // CTAs per cluster (split-K over the tile's K chunks): 1, 2, 4 or 8
+    int stages;             // pipeline stages (<= 4)
     const float *bias;
-    float *out;             // TC_STORE: [R][ldo]; TC_RESID: residual [R][ldo] (atomic add)
+    float *out;             // TC_STORE: [R][ldo]; TC_RESID: residual [R][ldo] (read, added, written)
     int ldo;
     // TC_QKV
     float *q_out;
@@ -114,27 +121,61 @@ __host__ __device__ constexpr int tc_stage_bytes(int N, int prec) {
     return (16384 * tc_parts(prec) + N * 128 * tc_parts(prec) + 8192 + 512 + 1023) / 1024 * 1024;
 }
 
-__host__ __device__ constexpr int tc_stages(int N, int prec) {
-    return (220 * 1024 / tc_stage_bytes(N, prec)) < 4 ? (220 * 1024 / tc_stage_bytes(N, prec)) : 4;
+// receive buffer of the split-K reduction: C partial slices of (128 / C) rows x NS columns
+__host__ __device__ constexpr int tc_recv_bytes(int NS) { return kTcM * NS * 4; }
+
+__host__ __device__ constexpr int tc_smem_bytes(int NS, int prec, int stages) {
+    return stages * tc_stage_bytes(NS, prec) + tc_recv_bytes(NS) + 1024;
 }
 
-__host__ __device__ constexpr int tc_smem_bytes(int N, int prec) {
-    return tc_stages(N, prec) * tc_stage_bytes(N, prec) + 1024;
+// most stages that fit in 227 KB of shared memory (at most 4)
+__host__ __device__ constexpr int tc_max_stages(int NS, int prec) {
+    return ((227 * 1024 - 1024 - tc_recv_bytes(NS)) / tc_stage_bytes(NS, prec)) < 4
+               ? ((227 * 1024 - 1024 - tc_recv_bytes(NS)) / tc_stage_bytes(NS, prec))
+               : 4;
 }
 
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_arrive_relaxed() { asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory"); }
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire;" ::: "memory"); }
+// shared-memory address `saddr` of this CTA -> the same offset in cluster CTA `rank`
+__device__ __forceinline__ uint32_t cluster_map(uint32_t saddr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+
+// int8 pairs -> fp16 pairs, exact: bytes b are placed as the low mantissa byte of 1024.0
+// (0x64bb) after flipping the sign bit, so the half is 1024 + (b + 128); subtracting 1152
+// leaves b.  `sel` picks bytes 0,1 (0x5140) or 2,3 (0x7362) of the word.
+__device__ __forceinline__ __half2 i8x2_to_h2(uint32_t w_flipped, uint32_t sel) {
+    const uint32_t h = __byte_perm(w_flipped, 0x64646464u, sel);
+    return __hsub2(*reinterpret_cast<const __half2 *>(&h), __half2half2(__ushort_as_half((unsigned short)0x6480)));
+}
 
 template <int EPI, int PREC>
 __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
     extern __shared__ uint8_t tc_smem_raw[];
     __shared__ __align__(8) uint64_t full_bar[4], bfull_bar[4], dq_bar[4], empty_bar[4], acc_bar;
     __shared__ uint32_t tmem_base_sh;
-    __shared__ int s_pos[kTcMaxN], s_dst[kTcMaxN];  // TC_QKV: per batch row position and page/slot
+    __shared__ int s_pos[kTcMaxNS], s_dst[kTcMaxNS];  // TC_QKV: per batch row position and page/slot
     constexpr int NP = tc_parts(PREC);  // operand parts (hi, lo)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int N = a.N;                  // rows of the activation image
     const int NS = a.nsub;              // rows handled by this CTA (MMA N)
+    const int C = a.csize;              // CTAs of the cluster (split-K)
+    const int S = a.stages;
+    const int rank = (int)cluster_rank();
+    const int tile = blockIdx.x / C;
     const int r0 = blockIdx.z * NS;     // first batch row of this CTA
-    const int S = tc_stages(NS, PREC);
     const int SB = tc_stage_bytes(NS, PREC);
     // stage layout: [A part 0..NP-1: 16 KB each][B part 0..NP-1: NS*128 each][W8 8 KB][scales]
     const int OFF_B = 16384 * NP;
@@ -142,10 +183,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
     const int OFF_SC = OFF_W8 + 8192;
     const size_t bimg_part = (size_t)a.K * N * 2;  // bytes of one activation image part
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
-    const int tile = blockIdx.x;
+    float *recv = reinterpret_cast<float *>(smem + (size_t)S * SB);  // [C][NS][RS] partial slices
+    const int RS = kTcM / C;                                         // tile rows reduced here
     const int nchunks_total = a.K / kTcK;
-    const int c0 = blockIdx.y * a.ksplit;
-    const int c1 = min(nchunks_total, c0 + a.ksplit);
+    const int c0 = rank * nchunks_total / C;
+    const int c1 = (rank + 1) * nchunks_total / C;
     const int nch = c1 - c0;
 
     if (threadIdx.x == 0) {
@@ -165,6 +207,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
                      "r"(ncols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
+    cluster_arrive_relaxed();  // this CTA runs; matched by the wait before the first remote store
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -250,36 +293,37 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
             uint8_t *st = smem + (size_t)s * SB;
             const int8_t *w8 = reinterpret_cast<const int8_t *>(st + OFF_W8) + t * 64;
             const __half *sc = reinterpret_cast<const __half *>(st + OFF_SC) + t * 2;
-            const float d0 = __half2float(sc[0]), d1 = __half2float(sc[1]);
             uint8_t *arow = st + t * 128;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {  // 16-byte piece j of the row = k 16j..16j+15
                 const int4 q = *reinterpret_cast<const int4 *>(w8 + ((j ^ ((t >> 1) & 3)) << 4));
-                const float d = j < 2 ? d0 : d1;
-                const int words[4] = {q.x, q.y, q.z, q.w};
-                __align__(16) __half h[16];
-                __align__(16) __half l[16];
+                const __half2 d2 = __half2half2(sc[j >> 1]);
+                const uint32_t words[4] = {(uint32_t)q.x ^ 0x80808080u, (uint32_t)q.y ^ 0x80808080u,
+                                           (uint32_t)q.z ^ 0x80808080u, (uint32_t)q.w ^ 0x80808080u};
+                // hi = fp16(q d), lo = fp16(q d - hi): one rounding each, as fp16(fp32 product)
+                // and fp16(fp32 product - hi) (q d is exact in fp32)
+                __align__(16) __half2 h[8];
+                __align__(16) __half2 l[8];
 #pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    // q * d is exact in fp32 (8-bit x 11-bit significands)
-                    const float w = (float)(int8_t)((words[e >> 2] >> (8 * (e & 3))) & 0xff) * d;
-                    h[e] = __float2half_rn(w);
-                    if (NP == 2) l[e] = __float2half_rn(w - __half2float(h[e]));
+                for (int e = 0; e < 8; ++e) {
+                    const __half2 qq = i8x2_to_h2(words[e >> 1], (e & 1) ? 0x7362u : 0x5140u);
+                    h[e] = __hmul2_rn(qq, d2);
+                    if (NP == 2) l[e] = __hfma2(qq, d2, __hneg2(h[e]));
                 }
                 // k = 16j + e -> 16-byte unit u = 2j (+1), stored at u ^ (t % 8)
                 *reinterpret_cast<int4 *>(arow + (((2 * j) ^ (t & 7)) << 4)) = *reinterpret_cast<const int4 *>(h);
-                *reinterpret_cast<int4 *>(arow + (((2 * j + 1) ^ (t & 7)) << 4)) = *reinterpret_cast<const int4 *>(h + 8);
+                *reinterpret_cast<int4 *>(arow + (((2 * j + 1) ^ (t & 7)) << 4)) = *reinterpret_cast<const int4 *>(h + 4);
                 if (NP == 2) {
                     *reinterpret_cast<int4 *>(arow + 16384 + (((2 * j) ^ (t & 7)) << 4)) =
                         *reinterpret_cast<const int4 *>(l);
                     *reinterpret_cast<int4 *>(arow + 16384 + (((2 * j + 1) ^ (t & 7)) << 4)) =
-                        *reinterpret_cast<const int4 *>(l + 8);
+                        *reinterpret_cast<const int4 *>(l + 4);
                 }
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             mbar_arrive(&dq_bar[s]);
         }
-        // ---------------- epilogue
+        // ---------------- partial results -> the CTA of the cluster that reduces each row
         pdl_wait();  // from here on this warp touches data of earlier kernels (outputs, row metadata)
         if (EPI == TC_QKV) {
             // per-row position and KV page (or local slot), fetched once per CTA
@@ -294,78 +338,89 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
                 s_pos[j] = pos;
                 s_dst[j] = dst;
             }
-            asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps only
         }
         const int q = warp & 3;                 // TMEM lane quarter this warp may read
         const int m = q * 32 + lane;            // weight row within the tile
-        const int gm = tile * kTcM + m;         // global weight row
         const bool acc_ok = nch > 0 && mbar_wait(&acc_bar, 0, a.err, 5);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        if (acc_ok && ok) {
-            const float bias = a.bias ? a.bias[gm] : 0.f;
-            for (int n0 = 0; n0 < NS; n0 += 16) {
-                float v[16];
+        cluster_wait();  // every CTA of the cluster is running: its shared memory may be written
+        const uint32_t dst_rank = (uint32_t)(m / RS);
+        const uint32_t rbase =
+            cluster_map(smem_u32(recv), dst_rank) + (uint32_t)(((rank * NS) * RS + (m % RS)) * 4);
+        for (int n0 = 0; n0 < NS; n0 += 16) {
+            float v[16];
+            if (acc_ok && ok) {
                 tc_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)n0, v);
-                if (EPI == TC_STORE) {
+            } else {
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const int rr = r0 + n0 + j;
-                        if (rr < a.R) a.out[(size_t)rr * a.ldo + gm] = a.bias ? __fadd_rn(v[j], bias) : v[j];
-                    }
-                } else if (EPI == TC_RESID) {
+                for (int j = 0; j < 16; ++j) v[j] = 0.f;
+            }
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const int rr = r0 + n0 + j;
-                        if (rr < a.R) atomicAdd(a.out + (size_t)rr * a.ldo + gm, blockIdx.y == 0 ? __fadd_rn(v[j], bias) : v[j]);
-                    }
-                } else if (EPI == TC_GELU_B) {
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const int rr = r0 + n0 + j;
-                        const float g = rr < a.R ? gelu_new(__fadd_rn(v[j], bias)) : 0.f;
-                        const __half gh = __float2half_rn(g);
-                        const size_t off = bimg_off(rr, gm, N);
-                        *reinterpret_cast<__half *>(a.bimg_out + off) = gh;
-                        if (NP == 2)  // the next GEMM's K is this one's rows
-                            *reinterpret_cast<__half *>(a.bimg_out + (size_t)a.rows * N * 2 + off) =
-                                __float2half_rn(g - __half2float(gh));
-                    }
-                } else {  // TC_QKV: bias, RoPE on q/k pairs (adjacent lanes), q out / KV append
-                    const bool rot = gm < 2 * kHidden;
-                    const int ri = (gm % kHeadDim) >> 1;
-                    float2 cs[16];
-#pragma unroll
-                    for (int j = 0; j < 16; ++j)  // independent loads first
-                        cs[j] = rot ? a.rope[(size_t)s_pos[n0 + j] * (kHeadDim / 2) + ri] : make_float2(1.f, 0.f);
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const int rr = r0 + n0 + j;
-                        const float yb = __fadd_rn(v[j], bias);
-                        const float other = __shfl_xor_sync(0xffffffffu, yb, 1);
-                        if (rr < a.R && (gm & 1) == 0) {
-                            const int pos = s_pos[n0 + j];
-                            float o0 = yb, o1 = other;
-                            if (rot) {
-                                o0 = __fsub_rn(__fmul_rn(yb, cs[j].x), __fmul_rn(other, cs[j].y));
-                                o1 = __fadd_rn(__fmul_rn(other, cs[j].x), __fmul_rn(yb, cs[j].y));
-                            }
-                            if (gm < kHidden) {
-                                *reinterpret_cast<float2 *>(a.q_out + (size_t)rr * kHidden + gm) = make_float2(o0, o1);
-                            } else {
-                                const int kvsel = gm < 2 * kHidden ? 0 : 1;
-                                const int c = gm - kHidden * (1 + kvsel);
-                                if (a.kv) {
-                                    __half *dst = a.kv + (size_t)s_dst[n0 + j] * kPageHalfs +
-                                                  ((kvsel * kHeads + c / kHeadDim) * kPage + pos % kPage) * kHeadDim +
-                                                  (c % kHeadDim);
-                                    *reinterpret_cast<__half2 *>(dst) = __floats2half2_rn(o0, o1);
-                                } else {
-                                    float *dst =
-                                        a.lkv + (((size_t)s_dst[n0 + j] * 2 + kvsel) * kLocalLen + pos) * kHidden + c;
-                                    *reinterpret_cast<float2 *>(dst) = make_float2(o0, o1);
-                                }
-                            }
-                        }
+            for (int j = 0; j < 16; ++j) st_cluster_f32(rbase + (uint32_t)((n0 + j) * RS * 4), v[j]);
+        }
+    }
+    // every thread of every CTA: the partial slices are delivered (release / acquire)
+    __syncwarp();
+    if (warp < 2) cluster_wait();  // matches the arrive at the start (warps 2..5 waited above)
+    cluster_arrive();
+    cluster_wait();
+
+    if (warp >= 2) {
+        // ---------------- reduce this CTA's rows and run the epilogue, two rows per item
+        const int t = threadIdx.x - 64;
+        const int HP = RS / 2;
+        const float2 *rv = reinterpret_cast<const float2 *>(recv);  // [C][NS][HP]
+        for (int idx = t; idx < HP * NS; idx += 128) {
+            const int pr = idx % HP, n = idx / HP;
+            float v0 = 0.f, v1 = 0.f;
+            for (int src = 0; src < C; ++src) {
+                const float2 pv = rv[((size_t)src * NS + n) * HP + pr];
+                v0 += pv.x;
+                v1 += pv.y;
+            }
+            const int gm = tile * kTcM + rank * RS + 2 * pr;  // even global weight row
+            const int rr = r0 + n;
+            const float b0 = a.bias ? a.bias[gm] : 0.f, b1 = a.bias ? a.bias[gm + 1] : 0.f;
+            if (EPI == TC_STORE) {
+                if (rr < a.R)
+                    *reinterpret_cast<float2 *>(a.out + (size_t)rr * a.ldo + gm) =
+                        a.bias ? make_float2(__fadd_rn(v0, b0), __fadd_rn(v1, b1)) : make_float2(v0, v1);
+            } else if (EPI == TC_RESID) {
+                if (rr < a.R) {
+                    float2 *o = reinterpret_cast<float2 *>(a.out + (size_t)rr * a.ldo + gm);
+                    const float2 x = *o;
+                    *o = make_float2(__fadd_rn(x.x, __fadd_rn(v0, b0)), __fadd_rn(x.y, __fadd_rn(v1, b1)));
+                }
+            } else if (EPI == TC_GELU_B) {
+                const float g0 = rr < a.R ? gelu_new(__fadd_rn(v0, b0)) : 0.f;
+                const float g1 = rr < a.R ? gelu_new(__fadd_rn(v1, b1)) : 0.f;
+                const __half2 gh = __floats2half2_rn(g0, g1);
+                const size_t off = bimg_off(rr, gm, N);  // gm even: both halves in one 16-byte unit
+                *reinterpret_cast<__half2 *>(a.bimg_out + off) = gh;
+                if (NP == 2)  // the next GEMM's K is this one's rows
+                    *reinterpret_cast<__half2 *>(a.bimg_out + (size_t)a.rows * N * 2 + off) =
+                        __floats2half2_rn(g0 - __low2float(gh), g1 - __high2float(gh));
+            } else if (rr < a.R) {  // TC_QKV: bias, RoPE on the (gm, gm + 1) pair, q out / KV append
+                const int pos = s_pos[n];
+                const float yb = __fadd_rn(v0, b0), other = __fadd_rn(v1, b1);
+                float o0 = yb, o1 = other;
+                if (gm < 2 * kHidden) {
+                    const float2 cs = a.rope[(size_t)pos * (kHeadDim / 2) + ((gm % kHeadDim) >> 1)];
+                    o0 = __fsub_rn(__fmul_rn(yb, cs.x), __fmul_rn(other, cs.y));
+                    o1 = __fadd_rn(__fmul_rn(other, cs.x), __fmul_rn(yb, cs.y));
+                }
+                if (gm < kHidden) {
+                    *reinterpret_cast<float2 *>(a.q_out + (size_t)rr * kHidden + gm) = make_float2(o0, o1);
+                } else {
+                    const int kvsel = gm < 2 * kHidden ? 0 : 1;
+                    const int c = gm - kHidden * (1 + kvsel);
+                    if (a.kv) {
+                        __half *dst = a.kv + (size_t)s_dst[n] * kPageHalfs +
+                                      ((kvsel * kHeads + c / kHeadDim) * kPage + pos % kPage) * kHeadDim + (c % kHeadDim);
+                        *reinterpret_cast<__half2 *>(dst) = __floats2half2_rn(o0, o1);
+                    } else {
+                        float *dst = a.lkv + (((size_t)s_dst[n] * 2 + kvsel) * kLocalLen + pos) * kHidden + c;
+                        *reinterpret_cast<float2 *>(dst) = make_float2(o0, o1);
                     }
                 }
             }
