@@ -14,7 +14,9 @@ is far larger than L2, so no explicit L2 flush is needed between steps.
   e2e     the same K frames as K calls of mossgpu_step through the C ABI with host buffers
           (control block H2D and codes/flags/gate D2H every frame), wall clock, max over ranks.
   roofline: the kernel class with the largest device time, timed live with CUDA events
-          recorded between the kernels of the captured frame graph (a separate pass).
+          recorded between the kernels of the captured frame graph (a separate pass);
+          `rooflines` gives the same figures for every class, `traffic` the DRAM bytes per
+          launch of the committed ncu capture of that kernel (profiles/traffic.json).
 
 --impl reference runs the reference's own CPU implementation (oracle/_ref, compiled from the
 reference sources; the C port in oracle/ when that is absent) on a bounded sample of the
@@ -281,25 +283,57 @@ def run_ours(args, rank, world, local_rank, dist):
         + 485_376 + 36_864 * (128 + n1 // 2 + 1) + 36_864
     pk = peaks()
 
-    # ---- roofline of the dominant kernel class
+    # ---- rooflines.  Classes run on the tcgen05 GEMM (R > 8) or the CUDA-core GEMV (R <= 8);
+    # algorithmic bytes = weights (Q8_0_4X4) + bias + activations in and out, FLOPs = 2 rows K R.
     R = B
     mean_ctx = float(np.mean(base_pos)) + prof_frames / 2.0 + 1.0  # attended positions per row
-    algo = {
-        "attn_decode_paged": R * mean_ctx * 12 * 64 * 2 * 2 + R * 768 * 8,
-        "gemv_qkv_global": q8x4_bytes(2304, 768) + 2304 * 4 + R * (768 * 4 + 768 * 4 + 768 * 4),
-        "gemv_proj_global": q8x4_bytes(768, 768) + 768 * 4 + R * 768 * 12,
-        "gemv_fc_in_global": q8x4_bytes(3072, 768) + 3072 * 4 + R * (768 + 3072) * 4,
-        "gemv_fc_out_global": q8x4_bytes(768, 3072) + 768 * 4 + R * (3072 + 2 * 768) * 4,
-        "gemv_qkv_local": q8x4_bytes(2304, 768) + 2304 * 4 + R * (768 * 4 + 768 * 4 + 2 * 768 * 4),
-        "gemv_proj_local": q8x4_bytes(768, 768) + 768 * 4 + R * 768 * 12,
-        "gemv_fc_in_local": q8x4_bytes(3072, 768) + 3072 * 4 + R * (768 + 3072) * 4,
-        "gemv_fc_out_local": q8x4_bytes(768, 3072) + 768 * 4 + R * (3072 + 2 * 768) * 4,
-        "gemv_audio_heads": q8x4_bytes(1024, 768) + R * (768 + 1024) * 4,
+    act = 4  # bytes per input element: fp32 rows, or the tensor-core image's two fp16 parts
+    gemm = {  # class -> (rows, K, output bytes per row)
+        "qkv_global": (2304, 768, 768 * 4 + 1536 * 2), "proj_global": (768, 768, 768 * 8),
+        "fc_in_global": (3072, 768, 3072 * 4), "fc_out_global": (768, 3072, 768 * 8),
+        "qkv_local": (2304, 768, 768 * 4 + 1536 * 4), "proj_local": (768, 768, 768 * 8),
+        "fc_in_local": (3072, 768, 3072 * 4), "fc_out_local": (768, 3072, 768 * 8),
+        "audio_heads": (1024, 768, 1024 * 4),
     }
-    top = max(prof.items(), key=lambda kv: kv[1][0])
-    name, (tot_ms, nl) = top
+    algo = {k: q8x4_bytes(m, kk) + m * 4 + R * (kk * act + ob) for k, (m, kk, ob) in gemm.items()}
+    flops = {k: 2.0 * m * kk * R for k, (m, kk, _) in gemm.items()}
+    algo.update({
+        "attn_decode_paged": R * mean_ctx * 12 * 64 * 2 * 2 + R * 768 * 8,
+        "attn_combine": R * 12 * 8 * 68 * 4 + R * 768 * 4,
+        "attn_local": R * 9 * 768 * 8 + R * 768 * 8,
+        "build_activation_image": R * 768 * 4 + max(16, R) * 768 * 4,
+        "sample_greedy": R * 1024 * 4 + R * 1024 * 2,
+    })
+    tf = Path(__file__).resolve().parent / "profiles" / "traffic.json"
+    traffic_db = json.loads(tf.read_text()) if tf.exists() else {}  # dram bytes per launch, committed ncu captures
+    rooflines = {}
+    for k, (tot, nl) in prof.items():
+        if nl and k in algo:
+            us = 1000 * tot / nl
+            r_ = {"avg_launch_us": round(us, 2), "achieved_gbs": round(algo[k] / (us / 1e6) / 1e9, 1),
+                  "frac_of_hbm": round(algo[k] / (us / 1e6) / 1e9 / pk["hbm_gbs"], 4)}
+            if k in flops:
+                r_["achieved_tflops"] = round(flops[k] / (us / 1e6) / 1e12, 2)
+            if k in traffic_db:
+                r_["traffic"] = traffic_db[k]["dram_bytes_per_launch"]
+            rooflines[k] = r_
+    # the dominant kernel: the kernel function with the most device time in the profiled
+    # frames; the weight-matrix roles all run one function (k_gemm_tc above 8 rows, else k_gemv)
+    fn_of = {k: ("k_gemm_tc" if R > 8 else "k_gemv") for k in gemm}
+    fns = {}
+    for k, (tot, nl) in prof.items():
+        if nl and k in algo:
+            f = fn_of.get(k, k)
+            e = fns.setdefault(f, [0.0, 0, 0.0, []])
+            e[0] += tot
+            e[1] += nl
+            e[2] += algo[k] * nl
+            e[3].append(k)
+    name, (tot_ms, nl, bytes_all, classes) = max(fns.items(), key=lambda kv: kv[1][0])
     avg_ms = tot_ms / max(nl, 1)
-    achieved = algo.get(name, 0.0) / (avg_ms / 1e3) / 1e9 if name in algo else None
+    algo_launch = bytes_all / max(nl, 1)  # mean algorithmic bytes per launch of that function
+    achieved = algo_launch / (avg_ms / 1e3) / 1e9
+    traffic = traffic_db.get(name, {}).get("dram_bytes_per_launch")
     step_ms = dev_ms / K
     value = B * world * K / (dev_ms / 1e3)
     e2e = B * world * K / e2e_s
@@ -318,11 +352,12 @@ def run_ours(args, rank, world, local_rank, dist):
             "ms_per_step": round(step_ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic (seeded N(0,0.02) Q8_0_4X4 weights, N(0,1) fp16 KV)",
             "config": workload_config(args),
-            "roofline": {"kernel": name, "bound": "hbm", "achieved": round(achieved, 1) if achieved else None,
-                         "peak": pk["hbm_gbs"], "unit": "GB/s",
-                         "frac": round(achieved / pk["hbm_gbs"], 4) if achieved else None,
-                         "traffic": None, "algorithmic_bytes_per_launch": algo.get(name),
+            "roofline": {"kernel": name, "classes": sorted(classes), "bound": "hbm", "achieved": round(achieved, 1),
+                         "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
+                         "traffic": traffic, "algorithmic_bytes_per_launch": round(algo_launch),
+                         "launches_per_frame": nl // prof_frames,
                          "avg_launch_us": round(1000 * avg_ms, 3), "peak_source": pk["source"]},
+            "rooflines": rooflines,
             "cpu_baseline": cpu_baseline,
             "e2e": {"value": round(e2e, 2), "unit": "frames/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "api": "mossgpu_step (C ABI), one call per frame, host buffers"},

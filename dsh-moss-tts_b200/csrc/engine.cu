@@ -18,7 +18,6 @@
 
 #include "kernels.cuh"
 #include "gemm_tc.cuh"
-#include "step_small.cuh"
 
 namespace mossgpu {
 
@@ -64,7 +63,6 @@ Engine::Engine(const std::string &path, int device, int max_streams, int max_ctx
     CK(cudaStreamCreateWithFlags(&own_stream_, cudaStreamNonBlocking));
     stream_ = own_stream_;
     if (const char *v = std::getenv("MOSSGPU_PDL")) pdl_ = std::strcmp(v, "0") != 0;
-    if (const char *v = std::getenv("MOSSGPU_STEP_KERNEL")) step_kernel_ = std::strcmp(v, "0") != 0;
     load_weights(path);
     pages_per_stream_ = (max_ctx + kPage - 1) / kPage;
     n_pages_ = kv_pages > 0 ? kv_pages : max_streams * pages_per_stream_;
@@ -175,17 +173,6 @@ void Engine::load_weights(const std::string &path) {
         return L;
     };
     for (int i = 0; i < kLayers; ++i) global_[i] = layer("g" + std::to_string(i) + ".");
-    {  // per-layer pointer table of the persistent small-batch step
-        StepLayer h[kLayers];
-        for (int i = 0; i < kLayers; ++i) {
-            const Layer &L = global_[i];
-            h[i] = StepLayer{L.attn.qs, L.proj.qs, L.fc_in.qs, L.fc_out.qs, L.attn.sc, L.proj.sc, L.fc_in.sc,
-                             L.fc_out.sc, L.ln1_w, L.ln1_b, L.ln2_w, L.ln2_b, L.attn_b, L.proj_b, L.fc_in_b,
-                             L.fc_out_b};
-        }
-        step_layers_ = dalloc<StepLayer>(kLayers, owned_);
-        CK(cudaMemcpy(step_layers_, h, sizeof(h), cudaMemcpyHostToDevice));
-    }
     local_ = layer("local.");
     lnf_w_ = vec("lnf.w", kHidden);
     lnf_b_ = vec("lnf.b", kHidden);
@@ -230,9 +217,6 @@ void Engine::allocate_state() {
     codes_hist_ = dalloc<int>(size_t(kMaxFramesPerCall) * max_streams_ * kNVq, owned_);
     bimg_a_ = dalloc<uint8_t>(2 * size_t(kHidden) * kTcMaxRows * 2, owned_);  // hi and lo parts
     bimg_mlp_ = dalloc<uint8_t>(2 * size_t(kFF) * kTcMaxRows * 2, owned_);
-    step_acc_ = dalloc<unsigned long long>(size_t(kLayers) * 2 * kSmallMaxR * kHidden, owned_);
-    step_sync_ = dalloc<unsigned>(kStepSyncs, owned_);
-    step_apart_ = dalloc<float>(size_t(kHeads) * kSmallMaxR * kStepMaxChunks * kPartStride, owned_);
     dev_err_ = dalloc<int>(4, owned_);
     CK(cudaMemset(dev_err_, 0, 4 * sizeof(int)));
     {
@@ -373,7 +357,6 @@ void launch_gemv(GemvArgs a, cudaStream_t st, bool pdl) {
 
 void Engine::set_smem_limits() {
     CK(cudaFuncSetAttribute(k_attn_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem));
-    CK(cudaFuncSetAttribute(k_global_step_small, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kStepSmem)));
     set_attr_all<PRO_LN, EPI_QKV>();
     set_attr_all<PRO_NONE, EPI_RESID>();
     set_attr_all<PRO_LN, EPI_GELU>();
@@ -571,9 +554,7 @@ void Engine::check_device_error() {
         *h_err_ = 0;
         CK(cudaMemsetAsync(dev_err_, 0, sizeof(int), stream_));
         CK(cudaStreamSynchronize(stream_));
-        throw std::runtime_error(std::string(e == 7 || e == 8     ? "decode-attention page ring"
-                                             : e >= 11 && e <= 14 ? "persistent global step"
-                                                                  : "tensor-core GEMM barrier") +
+        throw std::runtime_error(std::string(e == 7 || e == 8 ? "decode-attention page ring" : "tensor-core GEMM barrier") +
                                  " wait timed out (code " + std::to_string(e) + ")");
     }
 }
@@ -685,49 +666,7 @@ void Engine::block(const Layer &L, int li, bool local, int R, const int *row_slo
 }
 
 // 12 global layers over rows already embedded in x_ (row_pos = positions being written).
-// Up to 8 rows on the CUDA-core path: one persistent kernel (step_small.cuh); otherwise the
-// layer-by-layer launches.
 void Engine::global_layers(int R, const int *row_slot, const int *row_pos) {
-    if (step_kernel_ && R <= kSmallMaxR && !use_tc(R)) {
-        StepArgs s{};
-        s.layers = static_cast<const StepLayer *>(step_layers_);
-        s.kv = kv_;
-        s.layer_halfs = size_t(n_pages_) * kPageHalfs;
-        s.page_table = page_table_;
-        s.pages_per_stream = pages_per_stream_;
-        s.row_slot = row_slot;
-        s.row_pos = row_pos;
-        s.R = R;
-        s.rope = rope_;
-        s.x = x_;
-        s.q = q_;
-        s.apart = step_apart_;
-        s.acc = step_acc_;
-        s.sync = step_sync_;
-        s.err = dev_err_;
-        const DevMat *ms[4] = {&global_[0].attn, &global_[0].proj, &global_[0].fc_in, &global_[0].fc_out};
-        for (int i = 0; i < 4; ++i) {
-            s.weight_bytes[2 * i] = size_t(ms[i]->rows / 4) * (ms[i]->cols / 32) * 128;
-            s.weight_bytes[2 * i + 1] = size_t(ms[i]->rows / 4) * (ms[i]->cols / 32) * 8;
-        }
-        // accumulators and counters start at zero (plain stream order: the kernel is not a
-        // programmatic dependent of the memsets)
-        CK(cudaMemsetAsync(step_acc_, 0, sizeof(unsigned long long) * kLayers * 2 * size_t(R) * kHidden, stream_));
-        CK(cudaMemsetAsync(step_sync_, 0, sizeof(unsigned) * kStepSyncs, stream_));
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(kStepCtas);
-        cfg.blockDim = dim3(kStepThreads);
-        cfg.dynamicSmemBytes = kStepSmem;
-        cfg.stream = stream_;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeCooperative;  // all 148 CTAs resident at once
-        attr[0].val.cooperative = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        CK(cudaLaunchKernelEx(&cfg, k_global_step_small, s));
-        mark(KK_STEP_SMALL);
-        return;
-    }
     // ordinary launch: in a global step alone this kernel follows a host-to-device copy
     launch_k(false, k_attn_plan, dim3(1), dim3(32), 0, stream_, row_pos, row_slot, pages_per_stream_, R, attn_items_,
              plan_, desc_, work_, kLayers);
@@ -1111,10 +1050,9 @@ void Engine::issue_global_embed(int R) {
 const char *kernel_kind_name(int kind) {
     static const char *names[KK_COUNT] = {
         "page_updates", "gather_hidden", "lookup_slot_row", "embed_frame", "attn_plan",
-        "gemv_qkv_global", "attn_decode_paged", "gemv_proj_global", "gemv_fc_in_global", "gemv_fc_out_global", "ln_f",
-        "gemv_qkv_local", "attn_local", "gemv_proj_local", "gemv_fc_in_local", "gemv_fc_out_local", "gate_w8a8",
-        "gemv_audio_heads", "sample_greedy", "frame_commit", "build_activation_image", "attn_combine",
-        "global_step_persistent"};
+        "qkv_global", "attn_decode_paged", "proj_global", "fc_in_global", "fc_out_global", "ln_f",
+        "qkv_local", "attn_local", "proj_local", "fc_in_local", "fc_out_local", "gate_w8a8",
+        "audio_heads", "sample_greedy", "frame_commit", "build_activation_image", "attn_combine"};
     return (kind >= 0 && kind < KK_COUNT) ? names[kind] : "?";
 }
 

@@ -44,7 +44,7 @@ enum KernelKind {
     KK_PAGES, KK_GATHER, KK_LOOKUP, KK_EMBED, KK_PLAN,
     KK_QKV_G, KK_ATTN_DECODE, KK_PROJ_G, KK_FCIN_G, KK_FCOUT_G, KK_LNF,
     KK_QKV_L, KK_ATTN_LOCAL, KK_PROJ_L, KK_FCIN_L, KK_FCOUT_L, KK_GATE, KK_HEADS, KK_SAMPLE, KK_COMMIT,
-    KK_BIMG, KK_ATTN_COMBINE, KK_STEP_SMALL,
+    KK_BIMG, KK_ATTN_COMBINE,
     KK_COUNT
 };
 const char *kernel_kind_name(int kind);
@@ -169,12 +169,6 @@ private:
     float *part_ = nullptr, *gate_ = nullptr;
     int4 *desc_ = nullptr;  // decode-attention chunk descriptors
     int attn_items_ = 0;    // split-K partial capacity (chunks x heads)
-    // persistent small-batch global step
-    void *step_layers_ = nullptr;  // device StepLayer[12] (step_small.cuh)
-    unsigned long long *step_acc_ = nullptr;
-    unsigned *step_sync_ = nullptr;
-    float *step_apart_ = nullptr;
-    bool step_kernel_ = true;  // MOSSGPU_STEP_KERNEL=0 in the environment turns it off (A/B)
     int *rows17_ = nullptr;
     int *codes_hist_ = nullptr;  // [kMaxFramesPerCall][max_streams][16] codes of a multi-frame call
     uint8_t *bimg_a_ = nullptr;    // activation image, K = 768, up to 256 rows
