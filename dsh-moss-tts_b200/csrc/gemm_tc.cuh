@@ -95,6 +95,7 @@ __device__ __forceinline__ void tc_commit(uint64_t *bar) {
 }
 
 __device__ __forceinline__ void tc_ld16(uint32_t taddr, float *v) {
+    __syncwarp();  // .sync.aligned: the whole warp, converged
     uint32_t r[16];
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
