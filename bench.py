@@ -196,8 +196,12 @@ def run_ours(args, rank, world, local_rank, dist):
     max_ctx = args.lmax + W + 2 * K + prof_frames + 64
     eng = pkg.Engine(weights, device=local_rank, max_streams=B + 1, max_ctx=max_ctx)
     eng.set_cuda_stream(torch.cuda.current_stream().cuda_stream)
-    rng = np.random.default_rng(1234 + rank)
-    lens = [int(x) for x in rng.integers(args.lmin, args.lmax + 1, B)]
+    # one workload of B streams per GPU, KV lengths U{lmin..lmax}, sharded across the ranks
+    # by total KV length (rank 0 decides, every rank gets B streams)
+    import importlib
+    sharding = importlib.import_module("moss_b200.sharding")
+    all_lens = [int(x) for x in np.random.default_rng(1234).integers(args.lmin, args.lmax + 1, B * world)]
+    lens = [all_lens[i] for i in sharding.agree_shards(dist, all_lens, per_rank=B)[rank]]
     sids = [eng.open() for _ in lens]
 
     def reset_states():
@@ -210,6 +214,12 @@ def run_ours(args, rank, world, local_rank, dist):
 
     reset_states()
     params = pkg.SampleParams.make(greedy=True, repetition_penalty=1.2, min_frames=1 << 30)
+    if args.profile_prefill:  # one warm-up prompt, then N prompts of 256 rows (ncu captures)
+        for s_ in sids:
+            eng.close_stream(s_)
+        run_prefill(eng, torch, n_prompts=args.profile_prefill, rows=256)
+        eng.close()
+        return
     if args.profile_frames:  # the short run the ncu captures use: one warm-up frame, then N
         eng.step_frames(sids, params, 1, want_codes=False)
         eng.step_frames(sids, params, args.profile_frames, want_codes=False)
@@ -223,11 +233,7 @@ def run_ours(args, rank, world, local_rank, dist):
     torch.cuda.synchronize()
 
     def max_over_ranks(x: float) -> float:
-        if dist is None:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return sharding.max_over_ranks(dist, x, device="cuda")
 
     reset_states()
     clocks = Clocks(local_rank)
@@ -282,6 +288,14 @@ def run_ours(args, rank, world, local_rank, dist):
     b1_bytes = 12 * (q8x4_bytes(2304, 768) + q8x4_bytes(768, 768) + q8x4_bytes(3072, 768) + q8x4_bytes(768, 3072)) \
         + 485_376 + 36_864 * (128 + n1 // 2 + 1) + 36_864
     pk = peaks()
+
+    # ---- prefill: 16 prompts x 256 rows (192 text + 64 voice-frame embeddings,
+    # N(0,1) rounded to fp16), one 256-row pass per prompt through the 12 layers on the tensor
+    # cores, writing the fp16 KV; embeddings are copied from host memory inside the timing
+    for s_ in sids + [s1]:
+        eng.close_stream(s_)
+    pf = run_prefill(eng, torch, n_prompts=16, rows=256)
+    pf["frac_of_bf16_peak"] = round(pf["tflops"] / pk["bf16_tflops"], 4)
 
     # ---- rooflines.  Classes run on the tcgen05 GEMM (R > 8) or the CUDA-core GEMV (R <= 8);
     # algorithmic bytes = weights (Q8_0_4X4) + bias + activations in and out, FLOPs = 2 rows K R.
@@ -363,6 +377,7 @@ def run_ours(args, rank, world, local_rank, dist):
                     "api": "mossgpu_step (C ABI), one call per frame, host buffers"},
             "gpu_launches": launches,
             "clocks": clk,
+            "prefill": pf,
             "batch1_global_step": {"us": round(b1_us, 2), "kv_len": 128, "algorithmic_bytes": b1_bytes,
                                    "achieved_gbs": round(b1_bytes / (b1_us / 1e6) / 1e9, 1),
                                    "frac_of_hbm": round(b1_bytes / (b1_us / 1e6) / 1e9 / pk["hbm_gbs"], 4)},
@@ -372,9 +387,38 @@ def run_ours(args, rank, world, local_rank, dist):
     eng.close()
 
 
+# model FLOPs per prefilled row: 2 x the 84,934,656 weights of the 12 layers; causal attention
+# adds 12 layers x 2 (scores, weighted sum) x 2 x 768 per attended position
+PREFILL_FLOPS_PER_ROW = 2 * 12 * (2304 * 768 + 768 * 768 + 3072 * 768 + 768 * 3072)
+
+
+def run_prefill(eng, torch, n_prompts: int, rows: int, warmup: int = 1) -> dict:
+    rng = np.random.default_rng(2024)
+    x = rng.standard_normal((n_prompts + warmup, rows, 768), dtype=np.float32).astype(np.float16).astype(np.float32)
+    sids = [eng.open() for _ in range(n_prompts + warmup)]
+    for i in range(warmup):
+        eng.prefill_embeds(sids[i], x[i])
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(warmup, warmup + n_prompts):
+        eng.prefill_embeds(sids[i], x[i])
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    for s in sids:
+        eng.close_stream(s)
+    attn = n_prompts * 12 * 2 * 2 * 768 * rows * (rows + 1) / 2
+    flops = n_prompts * rows * PREFILL_FLOPS_PER_ROW + attn
+    return {"prompts": n_prompts, "rows": rows, "ms": round(ms, 3), "gflop": round(flops / 1e9, 1),
+            "tflops": round(flops / (ms / 1e3) / 1e12, 2), "rows_per_s": round(n_prompts * rows / (ms / 1e3), 1)}
+
+
 def eng_ctl_bytes(B: int) -> int:
+    """Bytes of the engine's per-call control block (engine.h off_* layout): slots, positions,
+    frames, forced codes, page updates, FrameCtl (12 ints), active flags, frame counter."""
     r_max = max(B + 1, 256)
-    return 4 * (22 * r_max + 1 + 8 + r_max + 4)
+    return 4 * (22 * r_max + 1 + 12 + r_max + 4)
 
 
 def main():
@@ -387,6 +431,8 @@ def main():
     ap.add_argument("--lmin", type=int, default=64)
     ap.add_argument("--lmax", type=int, default=1024)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-prefill", type=int, default=0,
+                    help="prefill this many 256-row prompts after one warm-up prompt and exit (ncu captures)")
     ap.add_argument("--profile-frames", type=int, default=0,
                     help="run this many frames of the N=1 workload after one warm-up frame and exit "
                          "(the command the ncu captures under profiles/ use)")

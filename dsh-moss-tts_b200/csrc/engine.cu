@@ -194,6 +194,8 @@ void Engine::allocate_state() {
     lkv_ = dalloc<float>(size_t(max_streams_) * 2 * kLocalLen * kHidden, owned_);
     counts_ = dalloc<uint16_t>(size_t(max_streams_) * kNVq * kCodebook, owned_);
     CK(cudaMemset(counts_, 0, size_t(max_streams_) * kNVq * kCodebook * sizeof(uint16_t)));
+    rng_ = dalloc<uint32_t>(size_t(max_streams_) * 4, owned_);
+    CK(cudaMemset(rng_, 0, size_t(max_streams_) * 4 * sizeof(uint32_t)));
 
     const size_t R = size_t(r_max_);
     x_ = dalloc<float>(R * kHidden, owned_);
@@ -228,7 +230,6 @@ void Engine::allocate_state() {
     }
 
     // control block: [slot R][pos R][frame R][forced 16R][page updates 1 + 3R][FrameCtl]
-    static_assert(sizeof(FrameCtl) <= 8 * sizeof(int), "FrameCtl must fit its 8 reserved ints");
     ctl_ints_ = off_fslot() + 4;
     d_ctl_ = dalloc<int>(ctl_ints_, owned_);
     void *hp = nullptr;
@@ -798,12 +799,36 @@ void Engine::prefill(int sid, const int32_t *rows, int m, int start) {
 
 void Engine::prefill_embeds(int sid, const float *x, int m, int start) { prefill_common(sid, m, start, nullptr, x); }
 
+namespace {
+// The sampler's generator as generate() seeds it (sampler.h:28-48): xoshiro128** with the
+// seed's two halves in the first words, two fixed words, then 8 draws discarded.
+void seed_xoshiro(uint32_t st[4], uint64_t v) {
+    st[0] = uint32_t(v);
+    st[1] = uint32_t(v >> 32) ^ 0x9E3779B9u;
+    st[2] = 0x243F6A88u;
+    st[3] = 0xB7E15162u;
+    auto rotl = [](uint32_t x, int k) { return (x << k) | (x >> (32 - k)); };
+    for (int i = 0; i < 8; ++i) {
+        const uint32_t t = st[1] << 9;
+        st[2] ^= st[0];
+        st[3] ^= st[1];
+        st[1] ^= st[2];
+        st[0] ^= st[3];
+        st[2] ^= t;
+        st[3] = rotl(st[3], 11);
+    }
+}
+}  // namespace
+
 void Engine::generate_begin(int sid, uint64_t seed) {
     check_slot(sid);
     Slot &s = slots_[size_t(sid)];
     s.frame = 0;
     s.seed = seed;
+    uint32_t st[4];
+    seed_xoshiro(st, seed);
     CK(cudaMemsetAsync(counts_ + size_t(sid) * kNVq * kCodebook, 0, size_t(kNVq) * kCodebook * sizeof(uint16_t), stream_));
+    CK(cudaMemcpyAsync(rng_ + size_t(sid) * 4, st, sizeof(st), cudaMemcpyHostToDevice, stream_));
     CK(cudaStreamSynchronize(stream_));
 }
 
@@ -811,8 +836,6 @@ void Engine::step(const int32_t *sids, int n, const SampleParamsC &p, const int3
                   uint8_t *out_stop, float *out_logits, float *out_gate, bool run_global) {
     if (n <= 0) return;
     if (n > max_streams_) throw std::runtime_error("batch larger than max_streams");
-    if (!p.greedy && p.top_k != 1) throw std::runtime_error("stochastic sampling is not supported by this build (greedy only)");
-    if (!p.end_greedy) throw std::runtime_error("sampled end decision is not supported by this build (end_greedy only)");
     launches_ = 0;
     std::vector<int> upd;
     std::vector<char> seen(size_t(max_streams_), 0);
@@ -844,6 +867,10 @@ void Engine::step(const int32_t *sids, int n, const SampleParamsC &p, const int3
     fc->greedy_frames = p.greedy_frames;
     fc->rep_penalty = p.repetition_penalty;
     fc->end_greedy = p.end_greedy;
+    fc->greedy = p.greedy;
+    fc->temperature = p.temperature;
+    fc->top_k = p.top_k;
+    fc->top_p = p.top_p;
     fc->has_forced = forced ? 1 : 0;
     // page updates ride in the same control block copy (decode adds at most one page per row)
     h_ctl_[off_pages()] = int(upd.size() / 3);
@@ -892,8 +919,6 @@ void Engine::step_frames(const int32_t *sids, int n, const SampleParamsC &p, int
     if (n <= 0 || n_frames <= 0) return;
     if (n > max_streams_) throw std::runtime_error("batch larger than max_streams");
     if (n_frames > kMaxFramesPerCall) throw std::runtime_error("n_frames above the per-call limit");
-    if (!p.greedy && p.top_k != 1) throw std::runtime_error("stochastic sampling is not supported by this build (greedy only)");
-    if (!p.end_greedy) throw std::runtime_error("sampled end decision is not supported by this build (end_greedy only)");
     std::vector<int> upd;
     std::vector<char> seen(size_t(max_streams_), 0);
     for (int r = 0; r < n; ++r) {
@@ -919,6 +944,10 @@ void Engine::step_frames(const int32_t *sids, int n, const SampleParamsC &p, int
     fc->greedy_frames = p.greedy_frames;
     fc->rep_penalty = p.repetition_penalty;
     fc->end_greedy = p.end_greedy;
+    fc->greedy = p.greedy;
+    fc->temperature = p.temperature;
+    fc->top_k = p.top_k;
+    fc->top_p = p.top_p;
     fc->has_forced = 0;
     CK(cudaMemcpyAsync(d_ctl_, h_ctl_, size_t(ctl_ints_) * sizeof(int), cudaMemcpyHostToDevice, stream_));
     int total_launches = 0;
@@ -999,7 +1028,7 @@ void Engine::issue_frame(int R, bool run_global) {
         block(local_, 0, true, R, d_slot, nullptr, ls, lx_);
         if (ls == 0) {
             launch_k(pdl_, k_gate, dim3(R), dim3(256), 0, stream_, lx_, R, llnf_w_, llnf_b_, qm(wte_), d_frame, d_fc,
-                                           d_ctl_ + off_active_in(), active_, gate_);
+                     d_ctl_ + off_active_in(), active_, gate_, d_slot, rng_);
             mark(KK_GATE);
         } else {
             const int ch = ls - 1;
@@ -1018,9 +1047,9 @@ void Engine::issue_frame(int R, bool run_global) {
                 launch_gemv<PRO_LN, EPI_STORE>(h, stream_, pdl_);
                 mark(KK_HEADS);
             }
-            launch_k(pdl_, k_sample_greedy, dim3(R), dim3(256), 0, stream_, logits_ + size_t(ch) * kCodebook, kNVq * kCodebook, ch, d_slot, R,
-                                                   counts_, d_fc, d_forced, active_, codes_, used_, qm(aemb_[ch]),
-                                                   ch + 1 < kNVq ? lx_ : nullptr);
+            launch_k(pdl_, k_sample, dim3(R), dim3(256), 0, stream_, logits_ + size_t(ch) * kCodebook, kNVq * kCodebook,
+                     ch, d_slot, R, counts_, d_fc, d_forced, active_, codes_, used_, qm(aemb_[ch]),
+                     ch + 1 < kNVq ? lx_ : nullptr, d_frame, rng_);
             mark(KK_SAMPLE);
         }
     }
@@ -1052,7 +1081,7 @@ const char *kernel_kind_name(int kind) {
         "page_updates", "gather_hidden", "lookup_slot_row", "embed_frame", "attn_plan",
         "qkv_global", "attn_decode_paged", "proj_global", "fc_in_global", "fc_out_global", "ln_f",
         "qkv_local", "attn_local", "proj_local", "fc_in_local", "fc_out_local", "gate_w8a8",
-        "audio_heads", "sample_greedy", "frame_commit", "build_activation_image", "attn_combine"};
+        "audio_heads", "sample", "frame_commit", "build_activation_image", "attn_combine"};
     return (kind >= 0 && kind < KK_COUNT) ? names[kind] : "?";
 }
 

@@ -139,8 +139,8 @@ private:
     int off_frame() const { return 2 * r_max_; }
     int off_forced() const { return 3 * r_max_; }
     int off_pages() const { return 19 * r_max_; }  // [count][slot, index, page] x r_max_
-    int off_fctl() const { return 22 * r_max_ + 1; }   // FrameCtl (8 ints reserved)
-    int off_active_in() const { return off_fctl() + 8; }
+    int off_fctl() const { return 22 * r_max_ + 1; }   // FrameCtl (kFrameCtlInts reserved)
+    int off_active_in() const { return off_fctl() + kFrameCtlInts; }
     int off_fslot() const { return off_active_in() + r_max_; }  // frames committed in this call
 
     int device_ = 0;
@@ -162,6 +162,7 @@ private:
     int *page_table_ = nullptr;
     float *hidden_ = nullptr, *lkv_ = nullptr;
     uint16_t *counts_ = nullptr;
+    uint32_t *rng_ = nullptr;  // [slot][4] xoshiro128** state of the stream's generate() call
     float2 *rope_ = nullptr;
     // row-batch scratch
     float *x_ = nullptr, *lx_ = nullptr, *q_ = nullptr, *attn_ = nullptr, *mlp_ = nullptr, *logits_ = nullptr;

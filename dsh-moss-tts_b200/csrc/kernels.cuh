@@ -116,6 +116,26 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
                  : "memory");
 }
 
+// xoshiro128** step and uniform draw of the reference sampler (sampler.h:25-48), on a
+// stream's state in global memory; one thread per stream draws.
+__device__ __forceinline__ uint32_t rng_rotl(uint32_t x, int k) { return (x << k) | (x >> (32 - k)); }
+__device__ __forceinline__ float rng_uniform(uint32_t *st) {
+    uint32_t s0 = st[0], s1 = st[1], s2 = st[2], s3 = st[3];
+    const uint32_t result = rng_rotl(s1 * 5u, 7) * 9u;
+    const uint32_t t = s1 << 9;
+    s2 ^= s0;
+    s3 ^= s1;
+    s1 ^= s2;
+    s0 ^= s3;
+    s2 ^= t;
+    s3 = rng_rotl(s3, 11);
+    st[0] = s0;
+    st[1] = s1;
+    st[2] = s2;
+    st[3] = s3;
+    return (float)(result >> 8) * (1.0f / 16777216.0f);
+}
+
 // gelu_new (llm.cpp:22-25), same operation order
 __device__ __forceinline__ float gelu_new(float v) {
     const float k = 0.7978845608028654f;
@@ -876,7 +896,8 @@ __global__ void __launch_bounds__(256) k_gate(const float *__restrict__ lx, int 
                                               const float *__restrict__ ln_b, const QMat wte,
                                               const int *__restrict__ frame_idx, const FrameCtl *__restrict__ ctl,
                                               const int *__restrict__ active_in, int *__restrict__ active,
-                                              float *__restrict__ gate_out) {
+                                              float *__restrict__ gate_out, const int *__restrict__ row_slot,
+                                              uint32_t *__restrict__ rng) {
     __shared__ float xs[kHidden];
     __shared__ int8_t qa[kHidden];
     __shared__ float as[kHidden / 32];
@@ -928,7 +949,19 @@ __global__ void __launch_bounds__(256) k_gate(const float *__restrict__ lx, int 
             gate_out[2 * r] = l_end;
             gate_out[2 * r + 1] = l_slot;
         }
-        const bool stop = frame_idx[r] >= ctl->min_frames && ctl->end_greedy && (l_end > l_slot);
+        // end_reached (llm.cpp:30-35): greedy compare, or one draw against p(slot) =
+        // 1 / (1 + e^(l_end - l_slot)) computed in double with the difference clamped to +-80
+        bool stop = false;
+        if (active_in[r] && frame_idx[r] >= ctl->min_frames) {
+            if (ctl->end_greedy) {
+                stop = l_end > l_slot;
+            } else {
+                double d = (double)l_end - (double)l_slot;
+                d = d < -80.0 ? -80.0 : (d > 80.0 ? 80.0 : d);
+                const float p_slot = (float)(1.0 / (1.0 + exp(d)));
+                stop = rng_uniform(rng + (size_t)row_slot[r] * 4) >= p_slot;
+            }
+        }
         active[r] = (active_in[r] && !stop) ? 1 : 0;  // a stream that stopped stays stopped
     }
 }
@@ -965,43 +998,128 @@ __global__ void __launch_bounds__(256) k_frame_commit(const int *__restrict__ co
 // is applied once per earlier occurrence of the code on this channel, then the first index
 // of the maximum wins.  Then records the used code (forced or predicted), counts it, and
 // writes the next local-decoder input deq(aemb[ch][used]) (llm.cpp:686-698).
-__global__ void __launch_bounds__(256) k_sample_greedy(const float *__restrict__ logits, int ld_logits, int ch,
-                                                       const int *__restrict__ row_slot, int R,
-                                                       uint16_t *__restrict__ counts, const FrameCtl *__restrict__ ctl,
-                                                       const int *__restrict__ forced, const int *__restrict__ active,
-                                                       int *__restrict__ codes_out, int *__restrict__ used_out,
-                                                       const QMat aemb, float *__restrict__ next_x) {
+// sample_token (sampler.cpp:9-77) for channel ch of every row, one CTA per row: the
+// repetition penalty once per earlier occurrence (counts), then either the first maximum
+// (greedy, top_k == 1, or frame < greedy_frames), or temperature, a sort by (value desc,
+// index asc), top-k, exp / sum in that order, the top-p cut and one xoshiro128** draw walked
+// down the sorted list.  Writes the prediction, the code used (forced or predicted), the
+// counts update and the next local input row aemb[ch][used].
+__global__ void __launch_bounds__(256) k_sample(const float *__restrict__ logits, int ld_logits, int ch,
+                                                const int *__restrict__ row_slot, int R,
+                                                uint16_t *__restrict__ counts, const FrameCtl *__restrict__ ctl,
+                                                const int *__restrict__ forced, const int *__restrict__ active,
+                                                int *__restrict__ codes_out, int *__restrict__ used_out,
+                                                const QMat aemb, float *__restrict__ next_x,
+                                                const int *__restrict__ frame_idx, uint32_t *__restrict__ rng) {
+    __shared__ float sv[kCodebook];
+    __shared__ int si[kCodebook];
     __shared__ float bv[8];
     __shared__ int bi[8];
-    __shared__ int s_used;
+    __shared__ int s_pred, s_used;
     pdl_enter();
     const int r = blockIdx.x;
     const int slot = row_slot[r];
     const float *lg = logits + (size_t)r * ld_logits;
     uint16_t *cnt = counts + ((size_t)slot * kNVq + ch) * kCodebook;
     const float p = ctl->rep_penalty;
-    float best = -INFINITY;
-    int besti = 0x7fffffff;
+    const bool greedy = ctl->greedy || ctl->top_k == 1 || frame_idx[r] < ctl->greedy_frames;
     for (int t = threadIdx.x; t < kCodebook; t += blockDim.x) {
         float v = lg[t];
         if (p != 1.0f) {
             const int c = cnt[t];
             for (int j = 0; j < c; ++j) v = v < 0.f ? __fmul_rn(v, p) : __fdiv_rn(v, p);
         }
-        if (v > best || (v == best && t < besti)) { best = v; besti = t; }
+        sv[t] = v;
+        si[t] = t;
     }
-    for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, besti, o);
-        if (ov > best || (ov == best && oi < besti)) { best = ov; besti = oi; }
+    if (greedy) {
+        float best = -INFINITY;
+        int besti = 0x7fffffff;
+        for (int t = threadIdx.x; t < kCodebook; t += blockDim.x) {
+            const float v = sv[t];
+            if (v > best || (v == best && t < besti)) { best = v; besti = t; }
+        }
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, besti, o);
+            if (ov > best || (ov == best && oi < besti)) { best = ov; besti = oi; }
+        }
+        const int warp = threadIdx.x >> 5;
+        if ((threadIdx.x & 31) == 0) { bv[warp] = best; bi[warp] = besti; }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+                if (bv[w] > best || (bv[w] == best && bi[w] < besti)) { best = bv[w]; besti = bi[w]; }
+            s_pred = besti;
+        }
+    } else {
+        const float temp = ctl->temperature;
+        if (temp > 0.0f && temp != 1.0f) {
+            const float inv = __fdiv_rn(1.0f, temp);
+            for (int t = threadIdx.x; t < kCodebook; t += blockDim.x) sv[t] = __fmul_rn(sv[t], inv);
+        }
+        __syncthreads();
+        // bitonic sort of (value, index): "before" = larger value, or equal value and lower index
+        for (int k = 2; k <= kCodebook; k <<= 1) {
+            for (int j = k >> 1; j > 0; j >>= 1) {
+                for (int i = threadIdx.x; i < kCodebook; i += blockDim.x) {
+                    const int ixj = i ^ j;
+                    if (ixj > i) {
+                        const float va = sv[i], vb = sv[ixj];
+                        const int ia = si[i], ib = si[ixj];
+                        const bool a_first = va > vb || (va == vb && ia < ib);
+                        if (((i & k) == 0) ? !a_first : a_first) {
+                            sv[i] = vb;
+                            sv[ixj] = va;
+                            si[i] = ib;
+                            si[ixj] = ia;
+                        }
+                    }
+                }
+                __syncthreads();
+            }
+        }
+        if (threadIdx.x == 0) {  // the reference's sequential sums, in sorted order
+            const int kk = ctl->top_k > 0 ? (ctl->top_k < kCodebook ? ctl->top_k : kCodebook) : kCodebook;
+            int size = kk;
+            const float maxv = sv[0];
+            float sum = 0.0f;
+            for (int j = 0; j < size; ++j) {
+                const float e = expf(sv[j] - maxv);
+                sv[j] = e;
+                sum += e;
+            }
+            if (ctl->top_p < 1.0f) {
+                float cum = 0.0f;
+                int keep = 0;
+                for (; keep < size; ++keep) {
+                    cum += sv[keep] / sum;
+                    if (cum >= ctl->top_p) {
+                        ++keep;
+                        break;
+                    }
+                }
+                size = keep > 1 ? keep : 1;
+                sum = 0.0f;
+                for (int j = 0; j < size; ++j) sum += sv[j];
+            }
+            int out = si[size - 1];
+            if (active[r]) {  // a stream that stopped draws nothing more
+                float rr = rng_uniform(rng + (size_t)slot * 4) * sum;
+                for (int j = 0; j < size; ++j) {
+                    rr -= sv[j];
+                    if (rr <= 0.0f) {
+                        out = si[j];
+                        break;
+                    }
+                }
+            }
+            s_pred = out;
+        }
     }
-    const int warp = threadIdx.x >> 5;
-    if ((threadIdx.x & 31) == 0) { bv[warp] = best; bi[warp] = besti; }
     __syncthreads();
     if (threadIdx.x == 0) {
-        for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
-            if (bv[w] > best || (bv[w] == best && bi[w] < besti)) { best = bv[w]; besti = bi[w]; }
-        const int pred = besti;
+        const int pred = s_pred;
         const int used = ctl->has_forced ? forced[r * kNVq + ch] : pred;
         codes_out[r * kNVq + ch] = pred;
         used_out[r * kNVq + ch] = used;

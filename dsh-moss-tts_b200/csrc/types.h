@@ -42,6 +42,12 @@ struct FrameCtl {
     float rep_penalty;
     int end_greedy;
     int has_forced;
+    int greedy;         // sampler.h:8-22
+    float temperature;
+    int top_k;
+    float top_p;
 };
+constexpr int kFrameCtlInts = 12;  // control-block ints reserved for FrameCtl
+static_assert(sizeof(FrameCtl) <= kFrameCtlInts * sizeof(int), "FrameCtl outgrew its control-block slot");
 
 }  // namespace mossgpu
