@@ -28,14 +28,19 @@ extern "C" {
 
 typedef struct mossgpu_engine mossgpu_engine;
 
-/* Mirrors moss::SampleParams (reference csrc/include/moss/sampler.h:8-22). */
+/* Mirrors moss::SampleParams (reference csrc/include/moss/sampler.h:8-22).  Sampling runs on
+ * the device with the reference's arithmetic and draw order (sampler.cpp:9-77): the
+ * repetition penalty, then either the first maximum or temperature -> sort by (value desc,
+ * index asc) -> top-k -> exp/sum -> top-p -> one xoshiro128** draw per channel from the
+ * stream's generator, seeded by mossgpu_generate_begin as generate() seeds it. */
 typedef struct {
     int greedy;                /* 1: argmax (after the repetition penalty) */
     float temperature;         /* stochastic path only */
-    int top_k;                 /* stochastic path only; 1 == greedy */
+    int top_k;                 /* stochastic path only; 1 == greedy, <= 0 == all 1024 codes */
     float top_p;               /* stochastic path only */
     float repetition_penalty;  /* applied once per earlier occurrence (sampler.cpp:14-21) */
-    int end_greedy;            /* 1: stop iff logit(end=7) > logit(slot=9) (llm.cpp:30-35) */
+    int end_greedy;            /* 1: stop iff logit(end=7) > logit(slot=9); 0: one draw against
+                                  p(slot) = 1 / (1 + e^(l_end - l_slot)) (llm.cpp:30-35) */
     int min_frames;            /* no stop before this frame index */
     int greedy_frames;         /* frames below this index are greedy */
 } mossgpu_sample_params;
