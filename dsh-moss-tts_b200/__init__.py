@@ -40,6 +40,7 @@ EXPORTS = [
     "mossgpu_kernel_profile", "mossgpu_kernel_profile_read", "mossgpu_kernel_name", "mossgpu_step_frames",
     "mossgpu_attention_workspace_bytes", "mossgpu_attention_decode_paged", "mossgpu_op_last_error",
     "mossgpu_attention_decode_paged_noalloc", "mossgpu_set_gemm_path", "mossgpu_debug_matrix_tile_bytes",
+    "mossgpu_stream_fork",
 ]
 
 
@@ -91,6 +92,7 @@ def lib() -> C.CDLL:
         L.mossgpu_stream_close.argtypes = [C.c_void_p, C.c_int]
         L.mossgpu_stream_reset.argtypes = [C.c_void_p, C.c_int]
         L.mossgpu_stream_position.argtypes = [C.c_void_p, C.c_int, C.POINTER(C.c_int)]
+        L.mossgpu_stream_fork.argtypes = [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_int)]
         L.mossgpu_prefill.argtypes = [C.c_void_p, C.c_int, _i32, C.c_int, C.c_int]
         L.mossgpu_prefill_embeds.argtypes = [C.c_void_p, C.c_int, _f32, C.c_int, C.c_int]
         L.mossgpu_generate_begin.argtypes = [C.c_void_p, C.c_int, C.c_uint64]
@@ -167,6 +169,12 @@ class Engine:
 
     def reset(self, sid: int):
         self._check(self.lib.mossgpu_stream_reset(self.h, sid))
+
+    def fork(self, src: int, n_pos: int) -> int:
+        """A new stream sharing src's first n_pos KV positions (see mossgpu_stream_fork)."""
+        out = C.c_int(-1)
+        self._check(self.lib.mossgpu_stream_fork(self.h, src, n_pos, C.byref(out)))
+        return out.value
 
     def position(self, sid: int) -> int:
         p = C.c_int()

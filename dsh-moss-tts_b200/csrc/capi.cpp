@@ -87,6 +87,13 @@ int mossgpu_stream_reset(mossgpu_engine *e, int stream_id) {
     return guarded(e, [&](mossgpu::Engine &g) { g.reset_stream(stream_id); });
 }
 
+int mossgpu_stream_fork(mossgpu_engine *e, int src_stream, int n_pos, int *new_stream) {
+    return guarded(e, [&](mossgpu::Engine &g) {
+        if (!new_stream) throw std::runtime_error("new_stream is NULL");
+        *new_stream = g.fork_stream(src_stream, n_pos);
+    });
+}
+
 int mossgpu_stream_position(mossgpu_engine *e, int stream_id, int *position) {
     return guarded(e, [&](mossgpu::Engine &g) {
         if (!position) throw std::runtime_error("position is NULL");

@@ -259,6 +259,7 @@ void Engine::allocate_state() {
     slots_.assign(size_t(max_streams_), Slot{});
     free_pages_.clear();
     for (int p = n_pages_ - 1; p >= 0; --p) free_pages_.push_back(p);
+    page_ref_.assign(size_t(n_pages_), 0);
 
     set_smem_limits();
     // the set-up copies and memsets above ran on the legacy stream; finish them before any
@@ -682,14 +683,42 @@ void Engine::check_slot(int sid) const {
         throw std::runtime_error("stream " + std::to_string(sid) + " is not open");
 }
 
-void Engine::ensure_pages(int sid, int upto_pos, std::vector<int> &updates) {
+int Engine::alloc_page() {
+    if (free_pages_.empty()) throw std::runtime_error("KV page pool exhausted");
+    const int page = free_pages_.back();
+    free_pages_.pop_back();
+    page_ref_[size_t(page)] = 1;
+    return page;
+}
+
+// All 12 layers of one page (48 KB each, n_pages_ pages apart): one strided device copy.
+void Engine::copy_page(int dst, int src) {
+    const size_t bytes = size_t(kPageHalfs) * sizeof(__half);
+    const size_t pitch = size_t(n_pages_) * bytes;
+    CK(cudaMemcpy2DAsync(kv_ + size_t(dst) * kPageHalfs, pitch, kv_ + size_t(src) * kPageHalfs, pitch, bytes, kLayers,
+                         cudaMemcpyDeviceToDevice, stream_));
+}
+
+// Pages for positions from_pos..upto_pos of a stream that is about to write them: a page
+// still shared with another stream (after mossgpu_stream_fork) is copied first, so a write
+// never reaches another stream's KV; missing pages are allocated.
+void Engine::ensure_pages(int sid, int from_pos, int upto_pos, std::vector<int> &updates) {
     Slot &s = slots_[size_t(sid)];
     const int need = upto_pos / kPage + 1;
     if (upto_pos >= max_ctx_) throw std::runtime_error("stream " + std::to_string(sid) + " reached max_ctx");
+    for (int i = std::max(0, from_pos) / kPage; i < std::min(need, int(s.pages.size())); ++i) {
+        const int old = s.pages[size_t(i)];
+        if (page_ref_[size_t(old)] <= 1) continue;
+        const int page = alloc_page();
+        copy_page(page, old);
+        --page_ref_[size_t(old)];
+        s.pages[size_t(i)] = page;
+        updates.push_back(sid);
+        updates.push_back(i);
+        updates.push_back(page);
+    }
     while (int(s.pages.size()) < need) {
-        if (free_pages_.empty()) throw std::runtime_error("KV page pool exhausted");
-        const int page = free_pages_.back();
-        free_pages_.pop_back();
+        const int page = alloc_page();
         updates.push_back(sid);
         updates.push_back(int(s.pages.size()));
         updates.push_back(page);
@@ -698,8 +727,49 @@ void Engine::ensure_pages(int sid, int upto_pos, std::vector<int> &updates) {
 }
 
 void Engine::release_pages(Slot &s) {
-    for (int p : s.pages) free_pages_.push_back(p);
+    for (int p : s.pages)
+        if (--page_ref_[size_t(p)] == 0) free_pages_.push_back(p);
     s.pages.clear();
+}
+
+// A new stream whose first n_pos positions are those of src: the full pages are shared
+// (reference-counted), the partly filled last page is copied, and the hidden state is
+// src's.  Writes of either stream to a shared page go through ensure_pages' copy.
+int Engine::fork_stream(int src, int n_pos) {
+    check_slot(src);
+    const Slot &s = slots_[size_t(src)];
+    if (n_pos < 0 || n_pos > s.pos) throw std::runtime_error("fork length outside the source stream's positions");
+    const int dst = open_stream();
+    std::vector<int> upd;
+    try {
+        Slot &d = slots_[size_t(dst)];
+        const int full = n_pos / kPage;
+        for (int i = 0; i < full; ++i) {
+            const int page = s.pages[size_t(i)];
+            ++page_ref_[size_t(page)];
+            d.pages.push_back(page);
+            upd.push_back(dst);
+            upd.push_back(i);
+            upd.push_back(page);
+        }
+        if (n_pos % kPage) {
+            const int page = alloc_page();
+            copy_page(page, s.pages[size_t(full)]);
+            d.pages.push_back(page);
+            upd.push_back(dst);
+            upd.push_back(full);
+            upd.push_back(page);
+        }
+        d.pos = n_pos;
+        CK(cudaMemcpyAsync(hidden_ + size_t(dst) * kHidden, hidden_ + size_t(src) * kHidden, kHidden * sizeof(float),
+                           cudaMemcpyDeviceToDevice, stream_));
+        upload_page_updates(upd);
+        CK(cudaStreamSynchronize(stream_));
+    } catch (...) {
+        close_stream(dst);
+        throw;
+    }
+    return dst;
 }
 
 // Page-table entries reach the device through the control block (no allocation): at most
@@ -756,7 +826,7 @@ void Engine::prefill_common(int sid, int m, int start, const int32_t *rows, cons
     m = std::min(m, max_ctx_ - start);  // llm.cpp:329-331
     if (m <= 0) return;
     std::vector<int> upd;
-    ensure_pages(sid, start + m - 1, upd);
+    ensure_pages(sid, start, start + m - 1, upd);
     upload_page_updates(upd);
     for (int c0 = 0; c0 < m; c0 += r_max_) {
         const int R = std::min(r_max_, m - c0);
@@ -844,7 +914,7 @@ void Engine::step(const int32_t *sids, int n, const SampleParamsC &p, const int3
         check_slot(sid);
         if (seen[size_t(sid)]) throw std::runtime_error("stream listed twice in one step");
         seen[size_t(sid)] = 1;
-        if (run_global) ensure_pages(sid, slots_[size_t(sid)].pos, upd);
+        if (run_global) ensure_pages(sid, slots_[size_t(sid)].pos, slots_[size_t(sid)].pos, upd);
     }
     if (forced) {
         for (int i = 0; i < n * kNVq; ++i)
@@ -926,7 +996,7 @@ void Engine::step_frames(const int32_t *sids, int n, const SampleParamsC &p, int
         check_slot(sid);
         if (seen[size_t(sid)]) throw std::runtime_error("stream listed twice in one step");
         seen[size_t(sid)] = 1;
-        ensure_pages(sid, slots_[size_t(sid)].pos + n_frames - 1, upd);
+        ensure_pages(sid, slots_[size_t(sid)].pos, slots_[size_t(sid)].pos + n_frames - 1, upd);
     }
     upload_page_updates(upd);
     const int R = n;
@@ -985,7 +1055,7 @@ void Engine::global_step_embed(const int32_t *sids, int n, const float *x, float
     std::vector<int> upd;
     for (int r = 0; r < n; ++r) {
         check_slot(sids[r]);
-        ensure_pages(sids[r], slots_[size_t(sids[r])].pos, upd);
+        ensure_pages(sids[r], slots_[size_t(sids[r])].pos, slots_[size_t(sids[r])].pos, upd);
     }
     upload_page_updates(upd);
     int *slot = h_ctl_, *pos = h_ctl_ + r_max_;
@@ -1203,7 +1273,7 @@ void Engine::set_state(int sid, const float *k, const float *v, int n_pos, const
     if (n_pos <= 0 || n_pos > max_ctx_) throw std::runtime_error("bad state length");
     Slot &s = slots_[size_t(sid)];
     std::vector<int> upd;
-    ensure_pages(sid, n_pos - 1, upd);
+    ensure_pages(sid, 0, n_pos - 1, upd);
     upload_page_updates(upd);
     const size_t nel = size_t(kLayers) * n_pos * kHidden;
     float *d = nullptr;
@@ -1344,7 +1414,7 @@ void Engine::fill_state_random(int sid, int n_pos, uint64_t seed) {
     if (n_pos <= 0 || n_pos > max_ctx_) throw std::runtime_error("bad state length");
     Slot &s = slots_[size_t(sid)];
     std::vector<int> upd;
-    ensure_pages(sid, n_pos - 1, upd);
+    ensure_pages(sid, 0, n_pos - 1, upd);
     upload_page_updates(upd);
     k_fill_state_normal<<<148 * 8, 256, 0, stream_>>>(kv_, n_pages_, page_table_ + size_t(sid) * pages_per_stream_,
                                                       n_pos, seed, hidden_ + size_t(sid) * kHidden);

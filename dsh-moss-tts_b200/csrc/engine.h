@@ -69,6 +69,7 @@ public:
     Engine &operator=(const Engine &) = delete;
 
     int open_stream();
+    int fork_stream(int src, int n_pos);
     void close_stream(int sid);
     void reset_stream(int sid);
     int position(int sid) const;
@@ -128,7 +129,9 @@ private:
     void mark(int kind);
     void accumulate_timing();
     void check_slot(int sid) const;
-    void ensure_pages(int sid, int upto_pos, std::vector<int> &updates);
+    void ensure_pages(int sid, int from_pos, int upto_pos, std::vector<int> &updates);
+    int alloc_page();
+    void copy_page(int dst, int src);
     void release_pages(Slot &s);
     void upload_page_updates(const std::vector<int> &updates);
     void prefill_common(int sid, int m, int start, const int32_t *rows, const float *x);
@@ -183,6 +186,7 @@ private:
 
     std::vector<Slot> slots_;
     std::vector<int> free_pages_;
+    std::vector<int> page_ref_;  // streams using each KV page (prefix sharing)
     int launches_ = 0;
 
     // CUDA graphs, programmatic dependent launch and per-kernel timing

@@ -85,12 +85,14 @@ public:
     }
     ~LlmModel() {
         if (engine_ && sid_ >= 0) mossgpu_stream_close(engine_->handle(), sid_);
+        if (engine_ && prefix_sid_ >= 0) mossgpu_stream_close(engine_->handle(), prefix_sid_);
     }
 
     // llm.h:46
     bool load(const std::string &weights_path, std::string *err) {
         try {
-            if (!engine_) engine_ = std::make_shared<Engine>(weights_path, device_, 1, max_ctx_);
+            // two stream slots: the model's state and its device-side prefix snapshot
+            if (!engine_) engine_ = std::make_shared<Engine>(weights_path, device_, 2, max_ctx_);
             max_ctx_ = engine_->max_ctx();
             engine_->check(mossgpu_stream_open(engine_->handle(), &sid_));
             weights_fp_ = fp_weights(weights_path);
@@ -110,17 +112,23 @@ public:
                                        static_cast<int>(rows.size()), start));
     }
 
-    // llm.h:57-60, llm.cpp:455-483: keep a host copy of the prefix KV
+    // llm.h:57-60, llm.cpp:455-483: the prefix is kept on the device as a second stream that
+    // shares the KV pages (mossgpu_stream_fork); restoring forks it back, copying only the
+    // partly filled last page
     void snapshot_prefix() {
         prefix_pos_ = position();
-        read_kv(prefix_pos_, &p_k_, &p_v_);
+        keep_prefix_on_device();
     }
     void restore_prefix() {
         if (prefix_pos_ <= 0) {
             reset();
             return;
         }
-        engine_->check(mossgpu_set_state(engine_->handle(), sid_, p_k_.data(), p_v_.data(), prefix_pos_, nullptr));
+        if (prefix_sid_ < 0) keep_prefix_on_device();
+        // the prefix stream keeps the shared pages alive: close first, then fork into the slot
+        engine_->check(mossgpu_stream_close(engine_->handle(), sid_));
+        sid_ = -1;
+        engine_->check(mossgpu_stream_fork(engine_->handle(), prefix_sid_, prefix_pos_, &sid_));
     }
     int prefix_pos() const { return prefix_pos_; }
 
@@ -251,6 +259,12 @@ private:
     }
 
     // K and V of positions [0, n) of every layer, fp32 [12][n][768] (fp16 cache widened)
+    void keep_prefix_on_device() {
+        if (prefix_sid_ >= 0) engine_->check(mossgpu_stream_close(engine_->handle(), prefix_sid_));
+        prefix_sid_ = -1;
+        if (prefix_pos_ > 0) engine_->check(mossgpu_stream_fork(engine_->handle(), sid_, prefix_pos_, &prefix_sid_));
+    }
+
     void read_kv(int n, std::vector<float> *k, std::vector<float> *v) const {
         const size_t per = static_cast<size_t>(n) * kHidden;
         k->assign(kLayers * per, 0.f);
@@ -340,8 +354,12 @@ private:
             return false;
         }
         prefix_pos_ = static_cast<int>(h.n_pos);
-        p_k_.swap(k);
-        p_v_.swap(v);
+        try {
+            keep_prefix_on_device();
+        } catch (const std::exception &e) {
+            if (err) *err = e.what();
+            return false;
+        }
         return true;
     }
 
@@ -351,7 +369,7 @@ private:
     int sid_ = -1;
     uint64_t weights_fp_ = 0;
     int prefix_pos_ = 0;
-    std::vector<float> p_k_, p_v_;
+    int prefix_sid_ = -1;  // device stream holding the prefix snapshot (shared KV pages)
     mutable std::vector<float> hidden_;
     const std::atomic<bool> *cancel_ = nullptr;
     std::string info_, logits_dump_path_, gate_dump_path_;

@@ -66,6 +66,15 @@ int mossgpu_stream_close(mossgpu_engine *e, int stream_id);
 int mossgpu_stream_reset(mossgpu_engine *e, int stream_id);
 int mossgpu_stream_position(mossgpu_engine *e, int stream_id, int *position);
 
+/* A new stream whose first n_pos positions are those of src_stream (n_pos <= its position),
+ * for voice-prompt prefixes shared by many utterances (snapshot_prefix / restore_prefix,
+ * llm.cpp:455-483, done on the device): the full 16-position KV pages are shared, not copied
+ * (reference counted), the partly filled last page is copied, the hidden state is src's and
+ * the position is n_pos.  Either stream writing into a shared page first copies it, so the
+ * two never see each other's later positions.  Call mossgpu_generate_begin before stepping
+ * the new stream. */
+int mossgpu_stream_fork(mossgpu_engine *e, int src_stream, int n_pos, int *new_stream);
+
 /* LlmModel::prefill(rows, start) (llm.cpp:327-401): rows[m][17] = [text_id, code0..15].
  * Writes the KV for positions start..start+m-1 and leaves the last row's ln_f output as
  * the stream's hidden state; position becomes start + m.  Computes in A16 (fp32
