@@ -414,6 +414,67 @@ def run_prefill(eng, torch, n_prompts: int, rows: int, warmup: int = 1) -> dict:
             "tflops": round(flops / (ms / 1e3) / 1e12, 2), "rows_per_s": round(n_prompts * rows / (ms / 1e3), 1)}
 
 
+def run_sweep(args, rank, world, local_rank, dist):
+    """Long-form streaming: every stream generates `frames` frames from a
+    starting KV length drawn from U{256..4096}, appending one position per frame.  Streams are
+    sharded over the ranks by KV length; each GPU steps its streams in groups of <= 256 rows
+    through mossgpu_step (C ABI, host buffers).  value = all frames of all streams / the
+    slowest rank's wall time; p50 / p99 = per-call latency of one frame for one group."""
+    import importlib
+    import math
+    import torch
+    torch.cuda.set_device(local_rank)
+    pkg = load_package()
+    if rank == 0:
+        pkg.build()
+    if dist is not None:
+        dist.barrier()
+    from moss_b200 import mossfile
+    sharding = importlib.import_module("moss_b200.sharding")
+    weights = mossfile.ensure_synth_weights(Path(tempfile.gettempdir()) / "moss_b200_w0.moss", 0)
+    frames, n_all, warm = args.sweep_frames, args.sweep_streams, 2
+    all_lens = [int(x) for x in np.random.default_rng(4096).integers(256, 4097, n_all)]
+    mine = [all_lens[i] for i in sharding.agree_shards(dist, all_lens, per_rank=math.ceil(n_all / world))[rank]]
+    pages = sum((L + frames + warm + kPAGE) // kPAGE + 1 for L in mine) + 16
+    eng = pkg.Engine(weights, device=local_rank, max_streams=len(mine) + 1, max_ctx=4096 + frames + warm + 32,
+                     kv_pages=pages)
+    sids = [eng.open() for _ in mine]
+    for i, (s, L) in enumerate(zip(sids, mine)):
+        eng.fill_state_random(s, L, seed=7000 + 1000 * rank + i)
+        eng.generate_begin(s, 0)
+    groups = [sids[i:i + 256] for i in range(0, len(sids), 256)]
+    params = pkg.SampleParams.make(greedy=True, repetition_penalty=1.2, min_frames=1 << 30)
+    for _ in range(warm):
+        for g in groups:
+            eng.step(g, params)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    lat = []
+    t0 = time.perf_counter()
+    for _ in range(frames):
+        for g in groups:
+            c0 = time.perf_counter()
+            eng.step(g, params)  # returns after the frame's codes reached the host
+            lat.append(time.perf_counter() - c0)
+    wall = sharding.max_over_ranks(dist, time.perf_counter() - t0, device="cuda")
+    p50 = sharding.max_over_ranks(dist, float(np.percentile(lat, 50)), device="cuda")
+    p99 = sharding.max_over_ranks(dist, float(np.percentile(lat, 99)), device="cuda")
+    kv_end = sum(L + warm + frames for L in all_lens) * 36_864
+    line = {"metric": "long-form streaming frames/sec (whole box)", "value": round(n_all * frames / wall, 1),
+            "unit": "frames/s", "n_gpus": world, "higher_is_better": True, "scaling": "strong",
+            "config": {"workload": "configs[4]: long-form sweep", "streams": n_all, "frames_per_stream": frames,
+                       "start_kv_len": [256, 4096], "rows_per_step_call": 256, "streams_per_gpu": len(mine)},
+            "p50_step_ms": round(1000 * p50, 3), "p99_step_ms": round(1000 * p99, 3),
+            "wall_s": round(wall, 3), "kv_bytes_at_end": kv_end, "dtype": "f32", "data": "synthetic"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    eng.close()
+
+
+kPAGE = 16
+
+
 def eng_ctl_bytes(B: int) -> int:
     """Bytes of the engine's per-call control block (engine.h off_* layout): slots, positions,
     frames, forced codes, page updates, FrameCtl (12 ints), active flags, frame counter."""
@@ -431,6 +492,11 @@ def main():
     ap.add_argument("--lmin", type=int, default=64)
     ap.add_argument("--lmax", type=int, default=1024)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sweep", action="store_true",
+                    help="BASELINE configs[4] instead: 512 streams from KV lengths U{256..4096}, 400 frames each, "
+                         "sharded over the ranks; sustained frames/s and p50/p99 step latency")
+    ap.add_argument("--sweep-frames", type=int, default=400)
+    ap.add_argument("--sweep-streams", type=int, default=512)
     ap.add_argument("--profile-prefill", type=int, default=0,
                     help="prefill this many 256-row prompts after one warm-up prompt and exit (ncu captures)")
     ap.add_argument("--profile-frames", type=int, default=0,
@@ -454,7 +520,10 @@ def main():
                                  device_id=torch.device("cuda", local_rank))
         dist = tdist
     try:
-        run_ours(args, rank, world, local_rank, dist)
+        if args.sweep:
+            run_sweep(args, rank, world, local_rank, dist)
+        else:
+            run_ours(args, rank, world, local_rank, dist)
     finally:
         if dist is not None:
             dist.destroy_process_group()
