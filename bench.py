@@ -214,11 +214,9 @@ def run_ours(args, rank, world, local_rank, dist):
 
     reset_states()
     params = pkg.SampleParams.make(greedy=True, repetition_penalty=1.2, min_frames=1 << 30)
-    if args.profile_prefill:  # one warm-up prompt, then N prompts of 256 rows (ncu captures)
-        for s_ in sids:
-            eng.close_stream(s_)
-        run_prefill(eng, torch, n_prompts=args.profile_prefill, rows=256)
+    if args.profile_prefill:  # one warm-up batch, then one batch of N prompts x 256 rows (ncu)
         eng.close()
+        run_prefill(pkg, weights, local_rank, torch, n_prompts=args.profile_prefill, rows=256)
         return
     if args.profile_frames:  # the short run the ncu captures use: one warm-up frame, then N
         eng.step_frames(sids, params, 1, want_codes=False)
@@ -290,11 +288,11 @@ def run_ours(args, rank, world, local_rank, dist):
     pk = peaks()
 
     # ---- prefill: 16 prompts x 256 rows (192 text + 64 voice-frame embeddings,
-    # N(0,1) rounded to fp16), one 256-row pass per prompt through the 12 layers on the tensor
-    # cores, writing the fp16 KV; embeddings are copied from host memory inside the timing
+    # N(0,1) rounded to fp16) in one 4096-row pass through the 12 layers on the tensor cores,
+    # writing the fp16 KV; embeddings are copied from host memory inside the timing
     for s_ in sids + [s1]:
         eng.close_stream(s_)
-    pf = run_prefill(eng, torch, n_prompts=16, rows=256)
+    pf = run_prefill(pkg, weights, local_rank, torch, n_prompts=16, rows=256)
     pf["frac_of_bf16_peak"] = round(pf["tflops"] / pk["bf16_tflops"], 4)
 
     # ---- rooflines.  Classes run on the tcgen05 GEMM (R > 8) or the CUDA-core GEMV (R <= 8);
@@ -392,22 +390,27 @@ def run_ours(args, rank, world, local_rank, dist):
 PREFILL_FLOPS_PER_ROW = 2 * 12 * (2304 * 768 + 768 * 768 + 3072 * 768 + 768 * 3072)
 
 
-def run_prefill(eng, torch, n_prompts: int, rows: int, warmup: int = 1) -> dict:
+def run_prefill(pkg, weights, device, torch, n_prompts: int, rows: int, warmup: int = 1) -> dict:
+    """All prompts in one mossgpu_prefill_embeds_batch call: one pass of n_prompts x rows rows
+    through the layers (an engine sized for it: max_rows = n_prompts x rows)."""
+    eng = pkg.Engine(weights, device=device, max_streams=n_prompts, max_ctx=rows + 16, max_rows=n_prompts * rows)
+    eng.set_cuda_stream(torch.cuda.current_stream().cuda_stream)
     rng = np.random.default_rng(2024)
-    x = rng.standard_normal((n_prompts + warmup, rows, 768), dtype=np.float32).astype(np.float16).astype(np.float32)
-    sids = [eng.open() for _ in range(n_prompts + warmup)]
-    for i in range(warmup):
-        eng.prefill_embeds(sids[i], x[i])
+    x = rng.standard_normal((n_prompts * rows, 768), dtype=np.float32).astype(np.float16).astype(np.float32)
+    m = np.full(n_prompts, rows, np.int32)
+    sids = [eng.open() for _ in range(n_prompts)]
+    for _ in range(warmup):
+        eng.prefill_embeds_batch(sids, x, m=m)
+        for s in sids:
+            eng.reset(s)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for i in range(warmup, warmup + n_prompts):
-        eng.prefill_embeds(sids[i], x[i])
+    eng.prefill_embeds_batch(sids, x, m=m)
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
-    for s in sids:
-        eng.close_stream(s)
+    eng.close()
     attn = n_prompts * 12 * 2 * 2 * 768 * rows * (rows + 1) / 2
     flops = n_prompts * rows * PREFILL_FLOPS_PER_ROW + attn
     return {"prompts": n_prompts, "rows": rows, "ms": round(ms, 3), "gflop": round(flops / 1e9, 1),

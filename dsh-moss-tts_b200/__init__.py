@@ -40,7 +40,8 @@ EXPORTS = [
     "mossgpu_kernel_profile", "mossgpu_kernel_profile_read", "mossgpu_kernel_name", "mossgpu_step_frames",
     "mossgpu_attention_workspace_bytes", "mossgpu_attention_decode_paged", "mossgpu_op_last_error",
     "mossgpu_attention_decode_paged_noalloc", "mossgpu_set_gemm_path", "mossgpu_debug_matrix_tile_bytes",
-    "mossgpu_stream_fork",
+    "mossgpu_stream_fork", "mossgpu_create_rows", "mossgpu_prefill_batch", "mossgpu_prefill_embeds_batch",
+    "mossgpu_set_tc_policy",
 ]
 
 
@@ -83,6 +84,11 @@ def lib() -> C.CDLL:
         L = C.CDLL(str(LIB_PATH))
         L.mossgpu_create.restype = C.c_void_p
         L.mossgpu_create.argtypes = [C.c_char_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_char_p, C.c_int]
+        L.mossgpu_create_rows.restype = C.c_void_p
+        L.mossgpu_create_rows.argtypes = [C.c_char_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_char_p, C.c_int]
+        L.mossgpu_prefill_batch.argtypes = [C.c_void_p, C.c_int, _i32, _i32, _i32, _i32]
+        L.mossgpu_prefill_embeds_batch.argtypes = [C.c_void_p, C.c_int, _i32, _i32, _i32, _f32]
+        L.mossgpu_set_tc_policy.argtypes = [C.c_void_p, C.c_int, C.c_int]
         L.mossgpu_destroy.argtypes = [C.c_void_p]
         L.mossgpu_last_error.restype = C.c_char_p
         L.mossgpu_last_error.argtypes = [C.c_void_p]
@@ -136,10 +142,12 @@ def _ptr(a):
 class Engine:
     """One GPU's batched engine (mossgpu_create)."""
 
-    def __init__(self, weights: str, device: int = 0, max_streams: int = 64, max_ctx: int = 4608, kv_pages: int = 0):
+    def __init__(self, weights: str, device: int = 0, max_streams: int = 64, max_ctx: int = 4608, kv_pages: int = 0,
+                 max_rows: int = 0):
         self.lib = lib()
         err = C.create_string_buffer(1024)
-        self.h = self.lib.mossgpu_create(str(weights).encode(), device, max_streams, max_ctx, kv_pages, err, 1024)
+        self.h = self.lib.mossgpu_create_rows(str(weights).encode(), device, max_streams, max_ctx, kv_pages, max_rows,
+                                              err, 1024)
         if not self.h:
             raise MossGpuError(err.value.decode(errors="replace"))
         self.max_streams, self.max_ctx = max_streams, max_ctx
@@ -188,6 +196,38 @@ class Engine:
     def prefill_embeds(self, sid: int, x, start: int = 0):
         x = np.ascontiguousarray(x, np.float32).reshape(-1, HIDDEN)
         self._check(self.lib.mossgpu_prefill_embeds(self.h, sid, x, x.shape[0], start))
+
+    @staticmethod
+    def _batch(sids, parts, starts, m, width, dtype):
+        sids = np.ascontiguousarray(sids, np.int32)
+        if m is None:  # a list of per-stream arrays
+            arrs = [np.ascontiguousarray(p, dtype).reshape(-1, width) for p in parts]
+            m = np.array([a.shape[0] for a in arrs], np.int32)
+            flat = np.concatenate(arrs) if arrs else np.zeros((0, width), dtype)
+        else:  # one array holding the streams' rows one after the other, m[i] rows each
+            m = np.ascontiguousarray(m, np.int32)
+            flat = np.ascontiguousarray(parts, dtype).reshape(-1, width)
+            if flat.shape[0] < int(m.sum()):
+                raise ValueError("fewer rows than sum(m)")
+        if flat.shape[0] == 0:
+            flat = np.zeros((1, width), dtype)
+        st = np.zeros(len(sids), np.int32) if starts is None else np.ascontiguousarray(starts, np.int32)
+        if not (len(sids) == len(m) == len(st)):
+            raise ValueError("stream ids, row counts and starts differ in length")
+        return sids, m, st, flat
+
+    def prefill_batch(self, sids, rows, starts=None, m=None):
+        """Several streams' prompts in shared passes: rows = a list of [m_i][17] arrays (one per
+        stream of sids), or one [sum m][17] array with the row counts in m."""
+        s, m, st, flat = self._batch(sids, rows, starts, m, NVQ + 1, np.int32)
+        self._check(self.lib.mossgpu_prefill_batch(self.h, len(s), s, m, st, flat))
+
+    def prefill_embeds_batch(self, sids, x, starts=None, m=None):
+        s, m, st, flat = self._batch(sids, x, starts, m, HIDDEN, np.float32)
+        self._check(self.lib.mossgpu_prefill_embeds_batch(self.h, len(s), s, m, st, flat))
+
+    def set_tc_policy(self, direct_min_rows: int = 512, direct_rows: int = 256):
+        self._check(self.lib.mossgpu_set_tc_policy(self.h, direct_min_rows, direct_rows))
 
     def generate_begin(self, sid: int, seed: int = 0):
         self._check(self.lib.mossgpu_generate_begin(self.h, sid, seed))
@@ -253,7 +293,7 @@ class Engine:
         self._check(self.lib.mossgpu_set_graphs(self.h, int(enable)))
 
     def set_gemm_path(self, mode: int):
-        """0 = automatic, 1 = CUDA-core GEMV, 2 = tcgen05 tensor cores (rows <= 256)."""
+        """0 = automatic, 1 = CUDA-core GEMV, 2 = tcgen05 tensor cores, 3 = tensor cores with single fp16 operands."""
         self._check(self.lib.mossgpu_set_gemm_path(self.h, mode))
 
     def matrix_tile_bytes(self, name: str, rows: int, cols: int) -> np.ndarray:

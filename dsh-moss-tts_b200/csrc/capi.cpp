@@ -46,13 +46,18 @@ extern "C" {
 
 mossgpu_engine *mossgpu_create(const char *weights_path, int device_id, int max_streams, int max_ctx, int kv_pages,
                                char *err, int errlen) {
+    return mossgpu_create_rows(weights_path, device_id, max_streams, max_ctx, kv_pages, 0, err, errlen);
+}
+
+mossgpu_engine *mossgpu_create_rows(const char *weights_path, int device_id, int max_streams, int max_ctx, int kv_pages,
+                                    int max_rows, char *err, int errlen) {
     if (!weights_path) {
         copy_err(err, errlen, "weights_path is NULL");
         return nullptr;
     }
     try {
         auto *h = new mossgpu_engine();
-        h->eng = std::make_unique<mossgpu::Engine>(weights_path, device_id, max_streams, max_ctx, kv_pages);
+        h->eng = std::make_unique<mossgpu::Engine>(weights_path, device_id, max_streams, max_ctx, kv_pages, max_rows);
         return h;
     } catch (const std::exception &ex) {
         copy_err(err, errlen, ex.what());
@@ -113,6 +118,26 @@ int mossgpu_prefill_embeds(mossgpu_engine *e, int stream_id, const float *x, int
         if (!x && m > 0) throw std::runtime_error("x is NULL");
         g.prefill_embeds(stream_id, x, m, start);
     });
+}
+
+int mossgpu_prefill_batch(mossgpu_engine *e, int n, const int32_t *stream_ids, const int32_t *m, const int32_t *start,
+                          const int32_t *rows) {
+    return guarded(e, [&](mossgpu::Engine &g) {
+        if (n > 0 && (!stream_ids || !m || !start || !rows)) throw std::runtime_error("NULL argument");
+        g.prefill_batch(n, stream_ids, m, start, rows, nullptr);
+    });
+}
+
+int mossgpu_prefill_embeds_batch(mossgpu_engine *e, int n, const int32_t *stream_ids, const int32_t *m,
+                                 const int32_t *start, const float *x) {
+    return guarded(e, [&](mossgpu::Engine &g) {
+        if (n > 0 && (!stream_ids || !m || !start || !x)) throw std::runtime_error("NULL argument");
+        g.prefill_batch(n, stream_ids, m, start, nullptr, x);
+    });
+}
+
+int mossgpu_set_tc_policy(mossgpu_engine *e, int direct_min_rows, int direct_rows) {
+    return guarded(e, [&](mossgpu::Engine &g) { g.set_tc_policy(direct_min_rows, direct_rows); });
 }
 
 int mossgpu_generate_begin(mossgpu_engine *e, int stream_id, uint64_t seed) {

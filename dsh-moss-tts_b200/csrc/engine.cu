@@ -56,9 +56,11 @@ uint64_t fnv(uint64_t h, const void *data, size_t n) {
 
 // ------------------------------------------------------------------ construction
 
-Engine::Engine(const std::string &path, int device, int max_streams, int max_ctx, int kv_pages)
+Engine::Engine(const std::string &path, int device, int max_streams, int max_ctx, int kv_pages, int max_rows)
     : device_(device), max_streams_(max_streams), max_ctx_(max_ctx) {
     if (max_streams <= 0 || max_ctx <= 0) throw std::runtime_error("max_streams and max_ctx must be positive");
+    if (max_rows < 0 || max_rows > kMaxRowsLimit)
+        throw std::runtime_error("max_rows must be in 0.." + std::to_string(kMaxRowsLimit));
     CK(cudaSetDevice(device));
     CK(cudaStreamCreateWithFlags(&own_stream_, cudaStreamNonBlocking));
     stream_ = own_stream_;
@@ -66,7 +68,7 @@ Engine::Engine(const std::string &path, int device, int max_streams, int max_ctx
     load_weights(path);
     pages_per_stream_ = (max_ctx + kPage - 1) / kPage;
     n_pages_ = kv_pages > 0 ? kv_pages : max_streams * pages_per_stream_;
-    r_max_ = std::max(max_streams, kPrefillRows);
+    r_max_ = std::max(max_streams, max_rows > 0 ? max_rows : kPrefillRows);
     allocate_state();
 }
 
@@ -217,8 +219,9 @@ void Engine::allocate_state() {
     gate_ = dalloc<float>(R * 2, owned_);
     rows17_ = dalloc<int>(R * (kNVq + 1), owned_);
     codes_hist_ = dalloc<int>(size_t(kMaxFramesPerCall) * max_streams_ * kNVq, owned_);
-    bimg_a_ = dalloc<uint8_t>(2 * size_t(kHidden) * kTcMaxRows * 2, owned_);  // hi and lo parts
-    bimg_mlp_ = dalloc<uint8_t>(2 * size_t(kFF) * kTcMaxRows * 2, owned_);
+    const size_t rows16 = (R + 15) / 16 * 16;  // padded batch rows of an activation image
+    bimg_a_ = dalloc<uint8_t>(2 * size_t(kHidden) * rows16 * 2, owned_);  // hi and lo parts
+    bimg_mlp_ = dalloc<uint8_t>(2 * size_t(kFF) * rows16 * 2, owned_);
     dev_err_ = dalloc<int>(4, owned_);
     CK(cudaMemset(dev_err_, 0, 4 * sizeof(int)));
     {
@@ -355,6 +358,25 @@ void launch_gemv(GemvArgs a, cudaStream_t st, bool pdl) {
     else launch_gemv_r<PRO, EPI, 8>(a, st, pdl);
 }
 
+// largest footprint over the batch slices a launch may use (16..64 rows split-K, 16..256
+// direct, most stages)
+template <int EPI>
+void set_tc_attr() {
+    int s1 = 0, s3 = 0, d1 = 0, d3 = 0;
+    for (int n = 16; n <= kTcMaxNS; n += 16) {
+        s1 = std::max(s1, tc_smem_bytes(n, TC_F16, tc_max_stages(n, TC_F16)));
+        s3 = std::max(s3, tc_smem_bytes(n, TC_F16X3, tc_max_stages(n, TC_F16X3)));
+    }
+    for (int n = 16; n <= kTcMaxND; n += 16) {
+        d1 = std::max(d1, tc_smem_bytes_direct(n, TC_F16, tc_max_stages_direct(n, TC_F16)));
+        d3 = std::max(d3, tc_smem_bytes_direct(n, TC_F16X3, tc_max_stages_direct(n, TC_F16X3)));
+    }
+    CK(cudaFuncSetAttribute(k_gemm_tc<EPI, TC_F16, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, s1));
+    CK(cudaFuncSetAttribute(k_gemm_tc<EPI, TC_F16X3, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, s3));
+    CK(cudaFuncSetAttribute(k_gemm_tc<EPI, TC_F16, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, d1));
+    CK(cudaFuncSetAttribute(k_gemm_tc<EPI, TC_F16X3, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, d3));
+}
+
 }  // namespace
 
 void Engine::set_smem_limits() {
@@ -363,20 +385,10 @@ void Engine::set_smem_limits() {
     set_attr_all<PRO_NONE, EPI_RESID>();
     set_attr_all<PRO_LN, EPI_GELU>();
     set_attr_all<PRO_LN, EPI_STORE>();
-    // largest footprint over the batch slices a launch may use (16..64 rows, most stages)
-    int s1 = 0, s3 = 0;
-    for (int n = 16; n <= kTcMaxNS; n += 16) {
-        s1 = std::max(s1, tc_smem_bytes(n, TC_F16, tc_max_stages(n, TC_F16)));
-        s3 = std::max(s3, tc_smem_bytes(n, TC_F16X3, tc_max_stages(n, TC_F16X3)));
-    }
-    CK(cudaFuncSetAttribute(k_gemm_tc<TC_STORE, TC_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, s1));
-    CK(cudaFuncSetAttribute(k_gemm_tc<TC_QKV, TC_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, s1));
-    CK(cudaFuncSetAttribute(k_gemm_tc<TC_RESID, TC_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, s1));
-    CK(cudaFuncSetAttribute(k_gemm_tc<TC_GELU_B, TC_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, s1));
-    CK(cudaFuncSetAttribute(k_gemm_tc<TC_STORE, TC_F16X3>, cudaFuncAttributeMaxDynamicSharedMemorySize, s3));
-    CK(cudaFuncSetAttribute(k_gemm_tc<TC_QKV, TC_F16X3>, cudaFuncAttributeMaxDynamicSharedMemorySize, s3));
-    CK(cudaFuncSetAttribute(k_gemm_tc<TC_RESID, TC_F16X3>, cudaFuncAttributeMaxDynamicSharedMemorySize, s3));
-    CK(cudaFuncSetAttribute(k_gemm_tc<TC_GELU_B, TC_F16X3>, cudaFuncAttributeMaxDynamicSharedMemorySize, s3));
+    set_tc_attr<TC_STORE>();
+    set_tc_attr<TC_QKV>();
+    set_tc_attr<TC_RESID>();
+    set_tc_attr<TC_GELU_B>();
     CK(cudaFuncSetAttribute(k_build_bimg, cudaFuncAttributeMaxDynamicSharedMemorySize, kFF * 4));
 }
 
@@ -387,18 +399,51 @@ void Engine::set_gemm_path(int mode) {
     gemm_path_ = mode;
 }
 
+void Engine::set_tc_policy(int direct_min_rows, int direct_rows) {
+    if (direct_min_rows < 0 || direct_rows < 16 || direct_rows > kTcMaxND || direct_rows % 16)
+        throw std::runtime_error("direct rows must be a multiple of 16 in 16..256");
+    if (direct_min_rows == tc_direct_min_rows_ && direct_rows == tc_direct_rows_) return;
+    tc_direct_min_rows_ = direct_min_rows;
+    tc_direct_rows_ = direct_rows;
+    // captured frames hold the old launch shapes
+    CK(cudaStreamSynchronize(stream_));
+    for (auto &kv : graphs_) {
+        if (kv.second.exec) CK(cudaGraphExecDestroy(kv.second.exec));
+        for (cudaEvent_t ev : kv.second.events) CK(cudaEventDestroy(ev));
+    }
+    graphs_.clear();
+    last_graph_ = nullptr;
+}
+
 bool Engine::use_tc(int R) const {
-    if (R > kTcMaxRows || gemm_path_ == 1) return false;
+    if (gemm_path_ == 1) return false;
     return gemm_path_ >= 2 || R > kGemvMaxRows;
 }
 
 namespace {
 
-// Grid: weight tiles x cluster CTAs (split-K) x batch slices of <= 64 rows.  At 64 rows a QKV
-// GEMM has 18 weight tiles; clusters of 8 give it 144 CTAs streaming 1-2 K chunks each.
+// Decode batches (split-K form): grid = weight tiles x cluster CTAs x batch slices of <= 64
+// rows.  At 64 rows a QKV GEMM has 18 weight tiles; clusters of 8 give it 144 CTAs streaming
+// 1-2 K chunks each.  Batches of at least direct_min padded rows (prefill passes) take the
+// direct form instead: weight tiles x slices of <= direct_ns rows, every K chunk in one CTA.
 template <int EPI>
-void launch_tc(TcArgs a, int prec, cudaStream_t st, bool pdl) {
+void launch_tc(TcArgs a, int prec, cudaStream_t st, bool pdl, int direct_min, int direct_ns) {
     const int tiles = a.rows / kTcM, nchunks = a.K / kTcK;
+    if (direct_min > 0 && a.N >= direct_min) {
+        int ns = std::min(a.N, direct_ns);
+        while (a.N % ns) ns -= 16;
+        a.nsub = ns;
+        a.csize = 1;
+        a.stages = std::min(nchunks, tc_max_stages_direct(ns, prec));
+        const dim3 grid(tiles, 1, a.N / ns);
+        if (prec == TC_F16X3)
+            launch_kc(pdl, 0, k_gemm_tc<EPI, TC_F16X3, true>, grid, dim3(kTcThreads),
+                      tc_smem_bytes_direct(ns, TC_F16X3, a.stages), st, a);
+        else
+            launch_kc(pdl, 0, k_gemm_tc<EPI, TC_F16, true>, grid, dim3(kTcThreads), tc_smem_bytes_direct(ns, TC_F16, a.stages),
+                      st, a);
+        return;
+    }
     int nsub = std::min(a.N, kTcMaxNS);
     while (a.N % nsub) nsub -= 16;  // N is a multiple of 16
     const int nz = a.N / nsub;
@@ -411,10 +456,10 @@ void launch_tc(TcArgs a, int prec, cudaStream_t st, bool pdl) {
     a.stages = std::min(per, tc_max_stages(nsub, prec));
     const dim3 grid(tiles * C, 1, nz);
     if (prec == TC_F16X3)
-        launch_kc(pdl, C, k_gemm_tc<EPI, TC_F16X3>, grid, dim3(kTcThreads), tc_smem_bytes(nsub, TC_F16X3, a.stages), st,
+        launch_kc(pdl, C, k_gemm_tc<EPI, TC_F16X3, false>, grid, dim3(kTcThreads), tc_smem_bytes(nsub, TC_F16X3, a.stages), st,
                   a);
     else
-        launch_kc(pdl, C, k_gemm_tc<EPI, TC_F16>, grid, dim3(kTcThreads), tc_smem_bytes(nsub, TC_F16, a.stages), st, a);
+        launch_kc(pdl, C, k_gemm_tc<EPI, TC_F16, false>, grid, dim3(kTcThreads), tc_smem_bytes(nsub, TC_F16, a.stages), st, a);
 }
 
 }  // namespace
@@ -449,7 +494,7 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
         a.page_table = page_table_;
         a.pages_per_stream = pages_per_stream_;
     }
-    launch_tc<TC_QKV>(a, prec, stream_, pdl_);
+    launch_tc<TC_QKV>(a, prec, stream_, pdl_, tc_direct_min_rows_, tc_direct_rows_);
     mark(local ? KK_QKV_L : KK_QKV_G);
     // attention writes straight into proj's activation image; its padding rows are still
     // zero from the LN1 image built above with the same N
@@ -493,7 +538,7 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
     p.bias = L.proj_b;
     p.out = x;
     p.ldo = kHidden;
-    launch_tc<TC_RESID>(p, prec, stream_, pdl_);
+    launch_tc<TC_RESID>(p, prec, stream_, pdl_, tc_direct_min_rows_, tc_direct_rows_);
     mark(local ? KK_PROJ_L : KK_PROJ_G);
     launch_k(pdl_, k_build_bimg, dim3(N), dim3(256), kHidden * 4, stream_, x, kHidden, R, N, kHidden, L.ln2_w, L.ln2_b, tc_parts(prec), bimg_a_);
     mark(KK_BIMG);
@@ -508,7 +553,7 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
     f.K = kHidden;
     f.bias = L.fc_in_b;
     f.bimg_out = bimg_mlp_;
-    launch_tc<TC_GELU_B>(f, prec, stream_, pdl_);
+    launch_tc<TC_GELU_B>(f, prec, stream_, pdl_, tc_direct_min_rows_, tc_direct_rows_);
     mark(local ? KK_FCIN_L : KK_FCIN_G);
     TcArgs o{};
     o.N = N;
@@ -522,7 +567,7 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
     o.bias = L.fc_out_b;
     o.out = x;
     o.ldo = kHidden;
-    launch_tc<TC_RESID>(o, prec, stream_, pdl_);
+    launch_tc<TC_RESID>(o, prec, stream_, pdl_, tc_direct_min_rows_, tc_direct_rows_);
     mark(local ? KK_FCOUT_L : KK_FCOUT_G);
 }
 
@@ -543,7 +588,7 @@ void Engine::heads_tc(int ch, int R) {
     h.K = kHidden;
     h.out = logits_ + size_t(ch) * kCodebook;
     h.ldo = kNVq * kCodebook;
-    launch_tc<TC_STORE>(h, prec, stream_, pdl_);
+    launch_tc<TC_STORE>(h, prec, stream_, pdl_, tc_direct_min_rows_, tc_direct_rows_);
     mark(KK_HEADS);
 }
 
@@ -670,7 +715,7 @@ void Engine::block(const Layer &L, int li, bool local, int R, const int *row_slo
 // 12 global layers over rows already embedded in x_ (row_pos = positions being written).
 void Engine::global_layers(int R, const int *row_slot, const int *row_pos) {
     // ordinary launch: in a global step alone this kernel follows a host-to-device copy
-    launch_k(false, k_attn_plan, dim3(1), dim3(32), 0, stream_, row_pos, row_slot, pages_per_stream_, R, attn_items_,
+    launch_k(false, k_attn_plan, dim3(1), dim3(kPlanThreads), 0, stream_, row_pos, row_slot, pages_per_stream_, R, attn_items_,
              plan_, desc_, work_, kLayers);
     mark(KK_PLAN);
     for (int li = 0; li < kLayers; ++li) block(global_[li], li, false, R, row_slot, row_pos, 0, x_);
@@ -819,55 +864,94 @@ int Engine::position(int sid) const {
     return slots_[size_t(sid)].pos;
 }
 
-void Engine::prefill_common(int sid, int m, int start, const int32_t *rows, const float *xin) {
-    check_slot(sid);
-    Slot &s = slots_[size_t(sid)];
-    start = std::max(0, std::min(start, max_ctx_));
-    m = std::min(m, max_ctx_ - start);  // llm.cpp:329-331
-    if (m <= 0) return;
+// LlmModel::prefill (llm.cpp:327-401) for several streams at once.  Each stream's rows are
+// clamped as the reference clamps them (llm.cpp:329-331); the rows of all streams form one
+// sequence that runs through the layers in passes of up to r_max_ rows (a pass may hold
+// rows of several streams and a stream may span passes: each row attends to its own
+// stream's positions <= its own, all of which are in the KV cache by the time its layer's
+// attention runs).  The ln_f of a stream's last row becomes its hidden state.
+void Engine::prefill_batch(int n, const int32_t *sids, const int32_t *m_in, const int32_t *start_in,
+                           const int32_t *rows, const float *xin) {
+    if (n <= 0) return;
+    std::vector<int> sid(static_cast<size_t>(n)), m(static_cast<size_t>(n)), start(static_cast<size_t>(n));
+    for (int i = 0; i < n; ++i) {
+        check_slot(sids[i]);
+        for (int j = 0; j < i; ++j)
+            if (sids[j] == sids[i]) throw std::runtime_error("stream " + std::to_string(sids[i]) + " repeated in a prefill batch");
+        sid[size_t(i)] = sids[i];
+        start[size_t(i)] = std::max(0, std::min(start_in[i], max_ctx_));
+        m[size_t(i)] = std::max(0, std::min(m_in[i], max_ctx_ - start[size_t(i)]));
+    }
+    // input row of stream i's first row (rows are taken stream after stream, before clamping)
+    std::vector<size_t> src0(static_cast<size_t>(n) + 1, 0);
+    for (int i = 0; i < n; ++i) src0[size_t(i) + 1] = src0[size_t(i)] + size_t(std::max(0, m_in[i]));
+    if (rows) {
+        for (int i = 0; i < n; ++i)
+            for (int r = 0; r < std::max(0, m_in[i]); ++r) {
+                const int v = rows[(src0[size_t(i)] + size_t(r)) * (kNVq + 1)];
+                if (v < 0 || v >= kVocab)
+                    throw std::runtime_error("text id out of range in prefill row " + std::to_string(r));
+            }
+    }
     std::vector<int> upd;
-    ensure_pages(sid, start, start + m - 1, upd);
+    for (int i = 0; i < n; ++i)
+        if (m[size_t(i)] > 0) ensure_pages(sid[size_t(i)], start[size_t(i)], start[size_t(i)] + m[size_t(i)] - 1, upd);
     upload_page_updates(upd);
-    for (int c0 = 0; c0 < m; c0 += r_max_) {
-        const int R = std::min(r_max_, m - c0);
+    // flat row list: (stream index, row within the stream)
+    std::vector<std::pair<int, int>> flat;
+    for (int i = 0; i < n; ++i)
+        for (int r = 0; r < m[size_t(i)]; ++r) flat.emplace_back(i, r);
+    const size_t total = flat.size();
+    for (size_t c0 = 0; c0 < total; c0 += size_t(r_max_)) {
+        const int R = int(std::min(size_t(r_max_), total - c0));
         int *slot = h_ctl_, *pos = h_ctl_ + r_max_;
-        for (int i = 0; i < R; ++i) {
-            slot[i] = sid;
-            pos[i] = start + c0 + i;
+        for (int k = 0; k < R; ++k) {
+            const auto &fr = flat[c0 + size_t(k)];
+            slot[k] = sid[size_t(fr.first)];
+            pos[k] = start[size_t(fr.first)] + fr.second;
         }
         CK(cudaMemcpyAsync(d_ctl_, h_ctl_, size_t(2 * r_max_) * sizeof(int), cudaMemcpyHostToDevice, stream_));
-        if (rows) {
-            CK(cudaMemcpyAsync(rows17_, rows + size_t(c0) * (kNVq + 1), size_t(R) * (kNVq + 1) * sizeof(int),
-                               cudaMemcpyHostToDevice, stream_));
-            launch_k(false, k_embed_rows, dim3(R), dim3(256), 0, stream_, tables(), rows17_, R, x_);
-        } else {
-            CK(cudaMemcpyAsync(x_, xin + size_t(c0) * kHidden, size_t(R) * kHidden * sizeof(float),
-                               cudaMemcpyHostToDevice, stream_));
+        // the pass's inputs: runs of consecutive rows of one stream are contiguous in the input
+        for (int k = 0; k < R;) {
+            const auto &fr = flat[c0 + size_t(k)];
+            int len = 1;
+            while (k + len < R && flat[c0 + size_t(k + len)].first == fr.first) ++len;
+            const size_t src = src0[size_t(fr.first)] + size_t(fr.second);
+            if (rows)
+                CK(cudaMemcpyAsync(rows17_ + size_t(k) * (kNVq + 1), rows + src * (kNVq + 1),
+                                   size_t(len) * (kNVq + 1) * sizeof(int), cudaMemcpyHostToDevice, stream_));
+            else
+                CK(cudaMemcpyAsync(x_ + size_t(k) * kHidden, xin + src * kHidden, size_t(len) * kHidden * sizeof(float),
+                                   cudaMemcpyHostToDevice, stream_));
+            k += len;
         }
+        if (rows) launch_k(false, k_embed_rows, dim3(R), dim3(256), 0, stream_, tables(), rows17_, R, x_);
         global_layers(R, d_ctl_, d_ctl_ + r_max_);
-        if (c0 + R == m) {
-            // ln_f of the last row becomes the stream's hidden state (llm.cpp:395-399)
-            launch_k(pdl_, k_layernorm_rows, dim3(1), dim3(256), 0, stream_, x_ + size_t(R - 1) * kHidden, 1, lnf_w_, lnf_b_,
-                                                     hidden_ + size_t(sid) * kHidden, nullptr, nullptr);
+        // ln_f of each stream's last row in this pass becomes its hidden state (llm.cpp:395-399)
+        for (int k = 0; k < R; ++k) {
+            const auto &fr = flat[c0 + size_t(k)];
+            if (fr.second != m[size_t(fr.first)] - 1) continue;
+            launch_k(pdl_, k_layernorm_rows, dim3(1), dim3(256), 0, stream_, x_ + size_t(k) * kHidden, 1, lnf_w_, lnf_b_,
+                     hidden_ + size_t(sid[size_t(fr.first)]) * kHidden, nullptr, nullptr);
         }
         CK(cudaGetLastError());
         CK(cudaMemcpyAsync(h_err_, dev_err_, sizeof(int), cudaMemcpyDeviceToHost, stream_));
         CK(cudaStreamSynchronize(stream_));
         check_device_error();
     }
-    s.pos = start + m;
+    for (int i = 0; i < n; ++i)
+        if (m[size_t(i)] > 0) slots_[size_t(sid[size_t(i)])].pos = start[size_t(i)] + m[size_t(i)];
 }
 
 void Engine::prefill(int sid, const int32_t *rows, int m, int start) {
-    for (int i = 0; i < m * (kNVq + 1); ++i) {
-        const int v = rows[i];
-        if ((i % (kNVq + 1)) == 0 ? (v < 0 || v >= kVocab) : false)
-            throw std::runtime_error("text id out of range in prefill row " + std::to_string(i / (kNVq + 1)));
-    }
-    prefill_common(sid, m, start, rows, nullptr);
+    const int32_t s = sid, mm = m, st = start;
+    prefill_batch(1, &s, &mm, &st, rows, nullptr);
 }
 
-void Engine::prefill_embeds(int sid, const float *x, int m, int start) { prefill_common(sid, m, start, nullptr, x); }
+void Engine::prefill_embeds(int sid, const float *x, int m, int start) {
+    const int32_t s = sid, mm = m, st = start;
+    prefill_batch(1, &s, &mm, &st, nullptr, x);
+}
 
 namespace {
 // The sampler's generator as generate() seeds it (sampler.h:28-48): xoshiro128** with the

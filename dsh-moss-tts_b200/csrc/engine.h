@@ -59,11 +59,14 @@ struct CapturedGraph {
 
 class Engine {
 public:
-    static constexpr int kPrefillRows = 256;    // rows per prefill pass
+    static constexpr int kPrefillRows = 256;    // rows per prefill pass unless max_rows says otherwise
+    static constexpr int kMaxRowsLimit = 16384;
     static constexpr int kAttnGrid = 148;       // decode-attention CTAs: one per SM (205 KB smem each)
     static constexpr int kAttnItems = kAttnGrid * 8 * kHeads;  // split-K partials: ~8 chunks per CTA
 
-    Engine(const std::string &weights_path, int device, int max_streams, int max_ctx, int kv_pages);
+    // max_rows: rows of one pass through the layers (a prefill pass over one or several
+    // streams, or a decode batch); 0 = max(max_streams, kPrefillRows)
+    Engine(const std::string &weights_path, int device, int max_streams, int max_ctx, int kv_pages, int max_rows = 0);
     ~Engine();
     Engine(const Engine &) = delete;
     Engine &operator=(const Engine &) = delete;
@@ -75,6 +78,11 @@ public:
     int position(int sid) const;
     void prefill(int sid, const int32_t *rows, int m, int start);
     void prefill_embeds(int sid, const float *x, int m, int start);
+    // Several streams' prompts in shared passes of up to max_rows rows: stream sids[i] gets
+    // m[i] rows at positions start[i].., its rows taken in order from rows ([.][17]) or x
+    // ([.][768]), stream after stream.
+    void prefill_batch(int n, const int32_t *sids, const int32_t *m, const int32_t *start, const int32_t *rows,
+                       const float *x);
     void generate_begin(int sid, uint64_t seed);
     void step(const int32_t *sids, int n, const SampleParamsC &p, const int32_t *forced, int32_t *out_codes,
               uint8_t *out_stop, float *out_logits, float *out_gate, bool run_global);
@@ -95,7 +103,10 @@ public:
     // 0 = automatic (tensor cores above kGemvMaxRows rows), 1 = CUDA-core GEMV, 2 = tensor cores
     void set_gemm_path(int mode);
     static constexpr int kGemvMaxRows = 8;
-    static constexpr int kTcMaxRows = 256;
+    int max_rows() const { return r_max_; }
+    // tensor-core GEMM form: batches of at least direct_min_rows padded rows run one CTA per
+    // (weight tile, slice of <= direct_rows rows) with no split-K (0 = never)
+    void set_tc_policy(int direct_min_rows, int direct_rows);
     int last_launches() const { return launches_; }
     uint64_t weights_fingerprint() const { return weights_fp_; }
     int device() const { return device_; }
@@ -134,7 +145,6 @@ private:
     void copy_page(int dst, int src);
     void release_pages(Slot &s);
     void upload_page_updates(const std::vector<int> &updates);
-    void prefill_common(int sid, int m, int start, const int32_t *rows, const float *x);
 
     // control-block layout (ints) for R = r_max_ rows
     int off_slot() const { return 0; }
@@ -148,6 +158,7 @@ private:
 
     int device_ = 0;
     int max_streams_ = 0, max_ctx_ = 0, pages_per_stream_ = 0, n_pages_ = 0, r_max_ = 0;
+    int tc_direct_min_rows_ = 512, tc_direct_rows_ = 256;
     cudaStream_t stream_ = nullptr, own_stream_ = nullptr;
     std::vector<void *> owned_, pinned_;
     size_t weights_bytes_ = 0;

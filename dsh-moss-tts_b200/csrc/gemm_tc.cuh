@@ -3,21 +3,24 @@
 //   Y[n][m] = sum_k X[n][k] * W[m][k],   W = int8 Q8_0 blocks x fp16 scales, X fp16
 //
 // "Swap AB" so the weight rows form the MMA M dimension (128 per tile) and the batch rows the
-// N dimension (16..64 per CTA): D[128][N] fp32 lives in tensor memory (TMEM).  The K chunks
-// (64 each) of one weight tile are split over a thread-block cluster of C CTAs (split-K);
-// per K chunk of a CTA:
+// N dimension: D[128][N] fp32 lives in tensor memory (TMEM).  Per K chunk (64) of a CTA:
 //   - one producer thread bulk-copies (cp.async.bulk, no tensor map, no multicast) the
 //     weight tile's int8 quants (8 KB), its fp16 scales (512 B) and the activation tile
 //     (N x 128 B, already stored in the SWIZZLE_128B K-major image by the previous kernel);
-//   - four dequant warps convert int8 x scale -> fp16 into the A tile (SWIZZLE_128B K-major
-//     image, 16 KB), fence the async proxy and arrive;
-//   - one MMA thread issues four tcgen05.mma.kind::f16 (K = 16 each) and commits to the
-//     stage's "empty" barrier.
-// After the last chunk the four warps read the partial D back with tcgen05.ld and scatter it
-// through distributed shared memory: CTA j of the cluster receives every CTA's partial of
-// tile rows [128 j / C, 128 (j + 1) / C), sums the C partials in a fixed order and runs the
-// epilogue for those rows (bias / RoPE / KV append, GELU into the next GEMM's activation
-// image, residual add, or a plain store).  No atomics; the result does not depend on timing.
+//   - eight dequant warps (each thread half of a weight row) convert int8 x scale -> fp16
+//     into the A tile (SWIZZLE_128B K-major image, 16 KB), fence the async proxy and arrive;
+//   - one MMA thread issues four tcgen05.mma.kind::f16 (K = 16 each) per operand part and
+//     commits to the stage's "empty" barrier.
+// Two forms:
+//   split-K (decode batches, <= 64 batch rows per CTA): the K chunks of a weight tile are
+//     split over a thread-block cluster of C CTAs.  After the last chunk the eight warps read
+//     the partial D back with tcgen05.ld and scatter it through distributed shared memory:
+//     CTA j of the cluster receives every CTA's partial of tile rows [128 j / C, 128 (j+1) / C),
+//     sums the C partials in a fixed order and runs the epilogue for those rows;
+//   direct (prefill passes, <= 256 batch rows per CTA): one CTA runs every K chunk of its
+//     (weight tile, batch slice) and the eight warps run the epilogue straight from TMEM.
+// Epilogues: bias / RoPE / KV append, GELU into the next GEMM's activation image, residual
+// add, or a plain store.  No atomics; the result does not depend on timing.
 // Every mbarrier wait is bounded: on time-out the kernel records an error code and leaves
 // through the normal exit path (TMEM is always freed, every CTA reaches the cluster barriers).
 //
@@ -41,8 +44,10 @@ namespace {
 
 constexpr int kTcM = 128;      // weight rows per CTA (MMA M)
 constexpr int kTcK = 64;       // K per pipeline stage (one 128-byte swizzle row of fp16)
-constexpr int kTcThreads = 192;
-constexpr int kTcMaxNS = 64;   // batch rows per CTA (MMA N); more rows split over gridDim.z
+constexpr int kTcEpiThreads = 256;  // dequant / epilogue threads (8 warps, two per TMEM lane quarter)
+constexpr int kTcThreads = 64 + kTcEpiThreads;
+constexpr int kTcMaxNS = 64;   // batch rows per CTA (MMA N) with split-K; more rows split over gridDim.z
+constexpr int kTcMaxND = 256;  // batch rows per CTA in the direct (no split-K) form
 constexpr int kTcMaxCluster = 8;
 
 enum { TC_STORE = 0, TC_QKV = 1, TC_RESID = 2, TC_GELU_B = 3 };
@@ -136,6 +141,15 @@ __host__ __device__ constexpr int tc_max_stages(int NS, int prec) {
                : 4;
 }
 
+// direct form (one CTA per tile, accumulators read straight from TMEM): no receive buffer;
+// 3 KB are left for the static shared memory (barriers, per-row positions)
+__host__ __device__ constexpr int tc_smem_bytes_direct(int NS, int prec, int stages) {
+    return stages * tc_stage_bytes(NS, prec) + 1024;
+}
+__host__ __device__ constexpr int tc_max_stages_direct(int NS, int prec) {
+    return ((224 * 1024 - 1024) / tc_stage_bytes(NS, prec)) < 4 ? ((224 * 1024 - 1024) / tc_stage_bytes(NS, prec)) : 4;
+}
+
 __device__ __forceinline__ uint32_t cluster_rank() {
     uint32_t r;
     asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -162,19 +176,73 @@ __device__ __forceinline__ __half2 i8x2_to_h2(uint32_t w_flipped, uint32_t sel) 
     return __hsub2(*reinterpret_cast<const __half2 *>(&h), __half2half2(__ushort_as_half((unsigned short)0x6480)));
 }
 
-template <int EPI, int PREC>
+// One element of the direct form's epilogue: weight row gm (this thread's TMEM lane), batch row
+// rr, accumulator v, bias b, `pre` = what tc_epi_pre fetched for it.  Uniform over the warp
+// for a given rr (the QKV pair exchange is a shuffle between lanes gm and gm ^ 1).
+// The global inputs of a group of elements (residual rows, RoPE table entries) are fetched
+// for the whole group first: interleaved with the group's stores, each load would wait a
+// full L2 round trip behind the previous element's store.
+template <int EPI>
+__device__ __forceinline__ float2 tc_epi_pre(const TcArgs &a, int gm, int rr, int pos) {
+    if (EPI == TC_RESID) return make_float2(rr < a.R ? a.out[(size_t)rr * a.ldo + gm] : 0.f, 0.f);
+    if (EPI == TC_QKV && gm < 2 * kHidden && rr < a.R) return a.rope[(size_t)pos * (kHeadDim / 2) + ((gm % kHeadDim) >> 1)];
+    return make_float2(0.f, 0.f);
+}
+
+template <int EPI, int NP>
+__device__ __forceinline__ void tc_epi_one(const TcArgs &a, int gm, int rr, int N, float v, float b, int pos, int dst,
+                                           float2 pre) {
+    if (EPI == TC_STORE) {
+        if (rr < a.R) a.out[(size_t)rr * a.ldo + gm] = a.bias ? __fadd_rn(v, b) : v;
+    } else if (EPI == TC_RESID) {
+        if (rr < a.R) a.out[(size_t)rr * a.ldo + gm] = __fadd_rn(pre.x, __fadd_rn(v, b));
+    } else if (EPI == TC_GELU_B) {
+        const float g = rr < a.R ? gelu_new(__fadd_rn(v, b)) : 0.f;
+        const __half h = __float2half_rn(g);
+        const size_t off = bimg_off(rr, gm, N);
+        *reinterpret_cast<__half *>(a.bimg_out + off) = h;
+        if (NP == 2) *reinterpret_cast<__half *>(a.bimg_out + (size_t)a.rows * N * 2 + off) = __float2half_rn(g - __half2float(h));
+    } else if (rr < a.R) {  // TC_QKV
+        const float y = __fadd_rn(v, b);
+        const float yp = __shfl_xor_sync(0xffffffffu, y, 1);  // the other row of the RoPE pair
+        float o = y;
+        if (gm < 2 * kHidden) {
+            const float2 cs = pre;
+            o = (gm & 1) ? __fadd_rn(__fmul_rn(y, cs.x), __fmul_rn(yp, cs.y))
+                         : __fsub_rn(__fmul_rn(y, cs.x), __fmul_rn(yp, cs.y));
+        }
+        if (gm < kHidden) {
+            a.q_out[(size_t)rr * kHidden + gm] = o;
+        } else {
+            const int kvsel = gm < 2 * kHidden ? 0 : 1;
+            const int c = gm - kHidden * (1 + kvsel);
+            if (a.kv)
+                a.kv[(size_t)dst * kPageHalfs + ((kvsel * kHeads + c / kHeadDim) * kPage + pos % kPage) * kHeadDim +
+                     (c % kHeadDim)] = __float2half_rn(o);
+            else
+                a.lkv[(((size_t)dst * 2 + kvsel) * kLocalLen + pos) * kHidden + c] = o;
+        }
+    }
+}
+
+// DIRECT = false: split-K over a cluster of a.csize CTAs, partials reduce-scattered through
+// DSMEM, <= 64 batch rows per CTA (decode batches).  DIRECT = true: one CTA per (weight tile,
+// batch slice of <= 256 rows) runs every K chunk and its epilogue reads the accumulators
+// straight from TMEM (prefill and large batches, where the grid is already wide).
+template <int EPI, int PREC, bool DIRECT>
 __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
     extern __shared__ uint8_t tc_smem_raw[];
     __shared__ __align__(8) uint64_t full_bar[4], bfull_bar[4], dq_bar[4], empty_bar[4], acc_bar;
     __shared__ uint32_t tmem_base_sh;
-    __shared__ int s_pos[kTcMaxNS], s_dst[kTcMaxNS];  // TC_QKV: per batch row position and page/slot
+    constexpr int kRowsMax = DIRECT ? kTcMaxND : kTcMaxNS;
+    __shared__ int s_pos[kRowsMax], s_dst[kRowsMax];  // TC_QKV: per batch row position and page/slot
     constexpr int NP = tc_parts(PREC);  // operand parts (hi, lo)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int N = a.N;                  // rows of the activation image
     const int NS = a.nsub;              // rows handled by this CTA (MMA N)
-    const int C = a.csize;              // CTAs of the cluster (split-K)
+    const int C = DIRECT ? 1 : a.csize; // CTAs of the cluster (split-K)
     const int S = a.stages;
-    const int rank = (int)cluster_rank();
+    const int rank = DIRECT ? 0 : (int)cluster_rank();
     const int tile = blockIdx.x / C;
     const int r0 = blockIdx.z * NS;     // first batch row of this CTA
     const int SB = tc_stage_bytes(NS, PREC);
@@ -195,7 +263,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full_bar[s], 1);   // weight quants + scales of the stage landed
             mbar_init(&bfull_bar[s], 1);  // activation tile(s) of the stage landed
-            mbar_init(&dq_bar[s], 128);
+            mbar_init(&dq_bar[s], kTcEpiThreads);
             mbar_init(&empty_bar[s], 1);
         }
         mbar_init(&acc_bar, 1);
@@ -208,7 +276,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
                      "r"(ncols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
-    cluster_arrive_relaxed();  // this CTA runs; matched by the wait before the first remote store
+    if (!DIRECT) cluster_arrive_relaxed();  // this CTA runs; matched by the wait before the first remote store
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -282,8 +350,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
             tc_commit(&acc_bar);
         }
     } else {
-        // ---------------- dequant (then epilogue): warps 2..5, 128 threads
-        const int t = threadIdx.x - 64;  // 0..127: the weight row this thread dequantises
+        // ---------------- dequant (then epilogue): warps 2..9, 256 threads; thread u converts
+        // half hf of weight row t (16-byte pieces 2 hf and 2 hf + 1, k 32 hf .. 32 hf + 31)
+        const int u = threadIdx.x - 64;
+        const int t = u & (kTcM - 1), hf = u >> 7;
         bool ok = true;
         for (int i = 0; i < nch && ok; ++i) {
             const int s = i % S;
@@ -296,7 +366,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
             const __half *sc = reinterpret_cast<const __half *>(st + OFF_SC) + t * 2;
             uint8_t *arow = st + t * 128;
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {  // 16-byte piece j of the row = k 16j..16j+15
+            for (int jj = 0; jj < 2; ++jj) {  // 16-byte piece j of the row = k 16j..16j+15
+                const int j = 2 * hf + jj;
                 const int4 q = *reinterpret_cast<const int4 *>(w8 + ((j ^ ((t >> 1) & 3)) << 4));
                 const __half2 d2 = __half2half2(sc[j >> 1]);
                 const uint32_t words[4] = {(uint32_t)q.x ^ 0x80808080u, (uint32_t)q.y ^ 0x80808080u,
@@ -328,7 +399,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
         pdl_wait();  // from here on this warp touches data of earlier kernels (outputs, row metadata)
         if (EPI == TC_QKV) {
             // per-row position and KV page (or local slot), fetched once per CTA
-            for (int j = t; j < NS; j += 128) {
+            for (int j = u; j < NS; j += kTcEpiThreads) {
                 const int rr = r0 + j;
                 int pos = 0, dst = 0;
                 if (rr < a.R) {
@@ -342,24 +413,54 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
         }
         const int q = warp & 3;                 // TMEM lane quarter this warp may read
         const int m = q * 32 + lane;            // weight row within the tile
+        // the two warps of a lane quarter split the columns: [0, split) and [split, NS)
+        const int split = ((NS / 16 + 1) / 2) * 16;
+        const int cb = hf ? split : 0, ce = hf ? NS : split;
         const bool acc_ok = nch > 0 && mbar_wait(&acc_bar, 0, a.err, 5);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        cluster_wait();  // every CTA of the cluster is running: its shared memory may be written
-        const uint32_t dst_rank = (uint32_t)(m / RS);
-        const uint32_t rbase =
-            cluster_map(smem_u32(recv), dst_rank) + (uint32_t)(((rank * NS) * RS + (m % RS)) * 4);
-        for (int n0 = 0; n0 < NS; n0 += 16) {
-            float v[16];
-            if (acc_ok && ok) {
-                tc_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)n0, v);
-            } else {
+        if (DIRECT) {
+            // the epilogue threads: s_pos / s_dst written above are visible
+            asm volatile("barrier.sync 1, %0;" ::"n"(kTcEpiThreads) : "memory");
+            const int gm = tile * kTcM + m;
+            const float b = a.bias ? a.bias[gm] : 0.f;
+            for (int n0 = cb; n0 < ce; n0 += 16) {
+                float2 pre[16];
 #pragma unroll
-                for (int j = 0; j < 16; ++j) v[j] = 0.f;
+                for (int j = 0; j < 16; ++j)
+                    pre[j] = tc_epi_pre<EPI>(a, gm, r0 + n0 + j, EPI == TC_QKV ? s_pos[n0 + j] : 0);
+                float v[16];
+                if (acc_ok && ok) {
+                    tc_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)n0, v);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) v[j] = 0.f;
+                }
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int n = n0 + j;
+                    tc_epi_one<EPI, NP>(a, gm, r0 + n, N, v[j], b, EPI == TC_QKV ? s_pos[n] : 0,
+                                        EPI == TC_QKV ? s_dst[n] : 0, pre[j]);
+                }
             }
+        } else {
+            cluster_wait();  // every CTA of the cluster is running: its shared memory may be written
+            const uint32_t dst_rank = (uint32_t)(m / RS);
+            const uint32_t rbase =
+                cluster_map(smem_u32(recv), dst_rank) + (uint32_t)(((rank * NS) * RS + (m % RS)) * 4);
+            for (int n0 = cb; n0 < ce; n0 += 16) {
+                float v[16];
+                if (acc_ok && ok) {
+                    tc_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)n0, v);
+                } else {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) st_cluster_f32(rbase + (uint32_t)((n0 + j) * RS * 4), v[j]);
+                    for (int j = 0; j < 16; ++j) v[j] = 0.f;
+                }
+#pragma unroll
+                for (int j = 0; j < 16; ++j) st_cluster_f32(rbase + (uint32_t)((n0 + j) * RS * 4), v[j]);
+            }
         }
     }
+    if (!DIRECT) {
     // every thread of every CTA: the partial slices are delivered (release / acquire)
     __syncwarp();
     if (warp < 2) cluster_wait();  // matches the arrive at the start (warps 2..5 waited above)
@@ -367,66 +468,91 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
     cluster_wait();
 
     if (warp >= 2) {
-        // ---------------- reduce this CTA's rows and run the epilogue, two rows per item
-        const int t = threadIdx.x - 64;
+        // ---------------- reduce this CTA's rows and run the epilogue, two rows per item, in
+        // batches of 4 items per thread whose global inputs are fetched before any store
+        const int u = threadIdx.x - 64;
         const int HP = RS / 2;
+        const int total = HP * NS;
         const float2 *rv = reinterpret_cast<const float2 *>(recv);  // [C][NS][HP]
-        for (int idx = t; idx < HP * NS; idx += 128) {
-            const int pr = idx % HP, n = idx / HP;
-            float v0 = 0.f, v1 = 0.f;
-            for (int src = 0; src < C; ++src) {
-                const float2 pv = rv[((size_t)src * NS + n) * HP + pr];
-                v0 += pv.x;
-                v1 += pv.y;
+        constexpr int kB = 4;
+        for (int base = u; base < total; base += kB * kTcEpiThreads) {
+            float2 pre[kB];
+#pragma unroll
+            for (int bi = 0; bi < kB; ++bi) {
+                const int idx = base + bi * kTcEpiThreads;
+                pre[bi] = make_float2(0.f, 0.f);
+                if (idx < total) {
+                    const int pr = idx % HP, n = idx / HP;
+                    const int gm = tile * kTcM + rank * RS + 2 * pr;
+                    const int rr = r0 + n;
+                    if (EPI == TC_RESID && rr < a.R)
+                        pre[bi] = *reinterpret_cast<const float2 *>(a.out + (size_t)rr * a.ldo + gm);
+                    if (EPI == TC_QKV && rr < a.R && gm < 2 * kHidden)
+                        pre[bi] = a.rope[(size_t)s_pos[n] * (kHeadDim / 2) + ((gm % kHeadDim) >> 1)];
+                }
             }
-            const int gm = tile * kTcM + rank * RS + 2 * pr;  // even global weight row
-            const int rr = r0 + n;
-            const float b0 = a.bias ? a.bias[gm] : 0.f, b1 = a.bias ? a.bias[gm + 1] : 0.f;
-            if (EPI == TC_STORE) {
-                if (rr < a.R)
-                    *reinterpret_cast<float2 *>(a.out + (size_t)rr * a.ldo + gm) =
-                        a.bias ? make_float2(__fadd_rn(v0, b0), __fadd_rn(v1, b1)) : make_float2(v0, v1);
-            } else if (EPI == TC_RESID) {
-                if (rr < a.R) {
-                    float2 *o = reinterpret_cast<float2 *>(a.out + (size_t)rr * a.ldo + gm);
-                    const float2 x = *o;
-                    *o = make_float2(__fadd_rn(x.x, __fadd_rn(v0, b0)), __fadd_rn(x.y, __fadd_rn(v1, b1)));
+#pragma unroll
+            for (int bi = 0; bi < kB; ++bi) {
+                const int idx = base + bi * kTcEpiThreads;
+                if (idx >= total) break;
+                const int pr = idx % HP, n = idx / HP;
+                float v0 = 0.f, v1 = 0.f;
+                for (int src = 0; src < C; ++src) {
+                    const float2 pv = rv[((size_t)src * NS + n) * HP + pr];
+                    v0 += pv.x;
+                    v1 += pv.y;
                 }
-            } else if (EPI == TC_GELU_B) {
-                const float g0 = rr < a.R ? gelu_new(__fadd_rn(v0, b0)) : 0.f;
-                const float g1 = rr < a.R ? gelu_new(__fadd_rn(v1, b1)) : 0.f;
-                const __half2 gh = __floats2half2_rn(g0, g1);
-                const size_t off = bimg_off(rr, gm, N);  // gm even: both halves in one 16-byte unit
-                *reinterpret_cast<__half2 *>(a.bimg_out + off) = gh;
-                if (NP == 2)  // the next GEMM's K is this one's rows
-                    *reinterpret_cast<__half2 *>(a.bimg_out + (size_t)a.rows * N * 2 + off) =
-                        __floats2half2_rn(g0 - __low2float(gh), g1 - __high2float(gh));
-            } else if (rr < a.R) {  // TC_QKV: bias, RoPE on the (gm, gm + 1) pair, q out / KV append
-                const int pos = s_pos[n];
-                const float yb = __fadd_rn(v0, b0), other = __fadd_rn(v1, b1);
-                float o0 = yb, o1 = other;
-                if (gm < 2 * kHidden) {
-                    const float2 cs = a.rope[(size_t)pos * (kHeadDim / 2) + ((gm % kHeadDim) >> 1)];
-                    o0 = __fsub_rn(__fmul_rn(yb, cs.x), __fmul_rn(other, cs.y));
-                    o1 = __fadd_rn(__fmul_rn(other, cs.x), __fmul_rn(yb, cs.y));
-                }
-                if (gm < kHidden) {
-                    *reinterpret_cast<float2 *>(a.q_out + (size_t)rr * kHidden + gm) = make_float2(o0, o1);
-                } else {
-                    const int kvsel = gm < 2 * kHidden ? 0 : 1;
-                    const int c = gm - kHidden * (1 + kvsel);
-                    if (a.kv) {
-                        __half *dst = a.kv + (size_t)s_dst[n] * kPageHalfs +
-                                      ((kvsel * kHeads + c / kHeadDim) * kPage + pos % kPage) * kHeadDim + (c % kHeadDim);
-                        *reinterpret_cast<__half2 *>(dst) = __floats2half2_rn(o0, o1);
+                const int gm = tile * kTcM + rank * RS + 2 * pr;  // even global weight row
+                const int rr = r0 + n;
+                const float b0 = a.bias ? a.bias[gm] : 0.f, b1 = a.bias ? a.bias[gm + 1] : 0.f;
+                if (EPI == TC_STORE) {
+                    if (rr < a.R)
+                        *reinterpret_cast<float2 *>(a.out + (size_t)rr * a.ldo + gm) =
+                            a.bias ? make_float2(__fadd_rn(v0, b0), __fadd_rn(v1, b1)) : make_float2(v0, v1);
+                } else if (EPI == TC_RESID) {
+                    if (rr < a.R) {
+                        const float2 x = pre[bi];
+                        *reinterpret_cast<float2 *>(a.out + (size_t)rr * a.ldo + gm) =
+                            make_float2(__fadd_rn(x.x, __fadd_rn(v0, b0)), __fadd_rn(x.y, __fadd_rn(v1, b1)));
+                    }
+                } else if (EPI == TC_GELU_B) {
+                    const float g0 = rr < a.R ? gelu_new(__fadd_rn(v0, b0)) : 0.f;
+                    const float g1 = rr < a.R ? gelu_new(__fadd_rn(v1, b1)) : 0.f;
+                    const __half2 gh = __floats2half2_rn(g0, g1);
+                    const size_t off = bimg_off(rr, gm, N);  // gm even: both halves in one 16-byte unit
+                    *reinterpret_cast<__half2 *>(a.bimg_out + off) = gh;
+                    if (NP == 2)  // the next GEMM's K is this one's rows
+                        *reinterpret_cast<__half2 *>(a.bimg_out + (size_t)a.rows * N * 2 + off) =
+                            __floats2half2_rn(g0 - __low2float(gh), g1 - __high2float(gh));
+                } else if (rr < a.R) {  // TC_QKV: bias, RoPE on the (gm, gm + 1) pair, q out / KV append
+                    const int pos = s_pos[n];
+                    const float yb = __fadd_rn(v0, b0), other = __fadd_rn(v1, b1);
+                    float o0 = yb, o1 = other;
+                    if (gm < 2 * kHidden) {
+                        const float2 cs = pre[bi];
+                        o0 = __fsub_rn(__fmul_rn(yb, cs.x), __fmul_rn(other, cs.y));
+                        o1 = __fadd_rn(__fmul_rn(other, cs.x), __fmul_rn(yb, cs.y));
+                    }
+                    if (gm < kHidden) {
+                        *reinterpret_cast<float2 *>(a.q_out + (size_t)rr * kHidden + gm) = make_float2(o0, o1);
                     } else {
-                        float *dst = a.lkv + (((size_t)s_dst[n] * 2 + kvsel) * kLocalLen + pos) * kHidden + c;
-                        *reinterpret_cast<float2 *>(dst) = make_float2(o0, o1);
+                        const int kvsel = gm < 2 * kHidden ? 0 : 1;
+                        const int c = gm - kHidden * (1 + kvsel);
+                        if (a.kv) {
+                            __half *dst = a.kv + (size_t)s_dst[n] * kPageHalfs +
+                                          ((kvsel * kHeads + c / kHeadDim) * kPage + pos % kPage) * kHeadDim +
+                                          (c % kHeadDim);
+                            *reinterpret_cast<__half2 *>(dst) = __floats2half2_rn(o0, o1);
+                        } else {
+                            float *dst = a.lkv + (((size_t)s_dst[n] * 2 + kvsel) * kLocalLen + pos) * kHidden + c;
+                            *reinterpret_cast<float2 *>(dst) = make_float2(o0, o1);
+                        }
                     }
                 }
             }
         }
     }
+    }  // !DIRECT
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     if (warp == 1) {

@@ -398,27 +398,39 @@ __global__ void __launch_bounds__(512) k_gemv(const GemvArgs a) {
 // multiple of kAttnChunk keeping chunks * heads within `max_items` (the partial-result
 // capacity).  desc[g] describes chunk g for the decode kernel: {row | split << 30, first
 // position, end position, page-table offset of the first page}, split = the row has more
-// than one chunk.  One warp; it also zeroes the decode kernel's work counters.
-__global__ void k_attn_plan(const int *__restrict__ row_pos, const int *__restrict__ row_slot, int pages_per_stream,
-                            int R, int max_items, int *__restrict__ plan, int4 *__restrict__ desc,
-                            int *__restrict__ work, int nwork) {
+// than one chunk.  One CTA of kPlanThreads threads; it also zeroes the decode kernel's work
+// counters.
+__global__ void __launch_bounds__(kPlanThreads) k_attn_plan(const int *__restrict__ row_pos, const int *__restrict__ row_slot,
+                                                        int pages_per_stream, int R, int max_items, int *__restrict__ plan,
+                                                        int4 *__restrict__ desc, int *__restrict__ work, int nwork) {
     pdl_enter();
-    const int lane = threadIdx.x & 31;
-    for (int i = lane; i < nwork; i += 32) work[i] = 0;
+    __shared__ long long red_t[kPlanThreads / 32];
+    __shared__ int red_i[kPlanThreads / 32];
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    constexpr int NW = kPlanThreads / 32;
+    for (int i = tid; i < nwork; i += kPlanThreads) work[i] = 0;
+    // chunk length: kAttnChunk doubled until all rows' chunks x 12 heads fit max_items
     int chunk = kAttnChunk;
     for (;;) {
         long long t = 0;
-        for (int r = lane; r < R; r += 32) t += max(0, row_pos[r] + chunk) / chunk;
+        for (int r = tid; r < R; r += kPlanThreads) t += max(0, row_pos[r] + chunk) / chunk;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-        if (t * kHeads <= max_items || chunk >= (1 << 20)) break;
+        if (lane == 0) red_t[wid] = t;
+        __syncthreads();
+        long long tot = 0;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) tot += red_t[w];
+        __syncthreads();  // red_t is rewritten by the next iteration
+        if (tot * kHeads <= max_items || chunk >= (1 << 20)) break;
         chunk *= 2;
     }
+    // rows in tiles of kPlanThreads: exclusive prefix sum of the chunk counts (warp scans, then
+    // the warp totals), one thread writes its row's chunk descriptors
     int acc = 0;
-    for (int b = 0; b < R; b += 32) {  // 32 rows at a time: prefix sum of chunk counts
-        const int r = b + lane;
+    for (int b = 0; b < R; b += kPlanThreads) {
+        const int r = b + tid;
         const int n = r < R ? row_pos[r] + 1 : 0;
-        const int base = r < R ? row_slot[r] * pages_per_stream : 0;
         const int v = max(0, n - 1 + chunk) / chunk;  // rows with pos < 0 have no chunk
         int inc = v;
 #pragma unroll
@@ -426,20 +438,28 @@ __global__ void k_attn_plan(const int *__restrict__ row_pos, const int *__restri
             const int y = __shfl_up_sync(0xffffffffu, inc, o);
             if (lane >= o) inc += y;
         }
-        const int g0 = acc + inc - v;
-        if (r < R) plan[2 + r] = g0;
-        const int rows = min(32, R - b);
-        for (int k = 0; k < rows; ++k) {
-            const int nk = __shfl_sync(0xffffffffu, n, k), ck = __shfl_sync(0xffffffffu, v, k);
-            const int bk = __shfl_sync(0xffffffffu, base, k), gk = __shfl_sync(0xffffffffu, g0, k);
-            for (int c = lane; c < ck; c += 32) {
+        if (lane == 31) red_i[wid] = inc;
+        __syncthreads();
+        int before = 0, total = 0;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+            const int x = red_i[w];
+            before += w < wid ? x : 0;
+            total += x;
+        }
+        __syncthreads();  // red_i is rewritten by the next tile
+        const int g0 = acc + before + inc - v;
+        if (r < R) {
+            plan[2 + r] = g0;
+            const int base = row_slot[r] * pages_per_stream;
+            for (int c = 0; c < v; ++c) {
                 const int p0 = c * chunk;
-                desc[gk + c] = make_int4((b + k) | ((ck > 1) << 30), p0, min(nk, p0 + chunk), bk + p0 / kPage);
+                desc[g0 + c] = make_int4(r | ((v > 1) << 30), p0, min(n, p0 + chunk), base + p0 / kPage);
             }
         }
-        acc += __shfl_sync(0xffffffffu, inc, 31);
+        acc += total;
     }
-    if (lane == 0) {
+    if (tid == 0) {
         plan[0] = chunk;
         plan[1] = acc;
         plan[2 + R] = acc;

@@ -46,7 +46,7 @@ int run_attention(mossgpu::AttnArgs t, int *work, int4 *desc, int max_items, cud
             g_attr_set[dev] = true;
         }
     }
-    k_attn_plan<<<1, 32, 0, st>>>(t.row_pos, t.row_slot, t.pages_per_stream, t.R, max_items, const_cast<int *>(t.plan),
+    k_attn_plan<<<1, kPlanThreads, 0, st>>>(t.row_pos, t.row_slot, t.pages_per_stream, t.R, max_items, const_cast<int *>(t.plan),
                                   desc, work, 1);
     t.desc = desc;
     t.work = work;

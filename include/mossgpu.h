@@ -53,6 +53,12 @@ typedef struct {
  * failure with the reason in err (may be NULL). */
 mossgpu_engine *mossgpu_create(const char *weights_path, int device_id, int max_streams, int max_ctx,
                                int kv_pages, char *err, int errlen);
+/* Same, with max_rows = the rows of one pass through the layers: a prefill pass over one or
+ * several streams (mossgpu_prefill_batch), or a decode batch.  0 = max(max_streams, 256).
+ * A pass of thousands of rows makes every weight GEMM a dense contraction on the tensor
+ * cores; device memory grows by ~33 KB per row. */
+mossgpu_engine *mossgpu_create_rows(const char *weights_path, int device_id, int max_streams, int max_ctx,
+                                    int kv_pages, int max_rows, char *err, int errlen);
 void mossgpu_destroy(mossgpu_engine *e);
 const char *mossgpu_last_error(mossgpu_engine *e);
 const char *mossgpu_version(void);
@@ -82,6 +88,14 @@ int mossgpu_stream_fork(mossgpu_engine *e, int src_stream, int n_pos, int *new_s
 int mossgpu_prefill(mossgpu_engine *e, int stream_id, const int32_t *rows, int m, int start);
 /* Same with the token embeddings given directly, x[m][768] fp32. */
 int mossgpu_prefill_embeds(mossgpu_engine *e, int stream_id, const float *x, int m, int start);
+/* LlmModel::prefill for n distinct streams in shared passes (the Runtime batching many
+ * utterances): stream_ids[i] gets m[i] rows at positions start[i].. (clamped as the single
+ * prefill clamps them), its rows taken in order from rows[.][17] (or x[.][768]), stream
+ * after stream.  Each stream ends exactly as if it had been prefilled alone. */
+int mossgpu_prefill_batch(mossgpu_engine *e, int n, const int32_t *stream_ids, const int32_t *m, const int32_t *start,
+                          const int32_t *rows);
+int mossgpu_prefill_embeds_batch(mossgpu_engine *e, int n, const int32_t *stream_ids, const int32_t *m,
+                                 const int32_t *start, const float *x);
 
 /* Start a generate() call on a stream (llm.cpp:637-641): clears the per-channel code
  * history and sets the frame counter to 0. */
@@ -141,6 +155,11 @@ int mossgpu_fill_state_random(mossgpu_engine *e, int stream_id, int n_pos, uint6
  * rounding on weights and activations; the default split keeps fp32-level accuracy). */
 int mossgpu_set_graphs(mossgpu_engine *e, int enable);
 int mossgpu_set_gemm_path(mossgpu_engine *e, int mode);
+/* Tensor-core GEMM form by batch size: batches of at least direct_min_rows padded rows run
+ * one CTA per (128 weight rows, slice of direct_rows batch rows) over the whole K with the
+ * accumulators read straight from tensor memory; smaller batches split K over thread-block
+ * clusters.  direct_min_rows = 0 disables the direct form.  Default (512, 256). */
+int mossgpu_set_tc_policy(mossgpu_engine *e, int direct_min_rows, int direct_rows);
 
 /* Same as mossgpu_debug_matrix_bytes for the tensor-core tile copy of the matrix. */
 int mossgpu_debug_matrix_tile_bytes(mossgpu_engine *e, const char *name, uint8_t *out, size_t out_bytes);
