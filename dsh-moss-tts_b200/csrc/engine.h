@@ -44,7 +44,7 @@ enum KernelKind {
     KK_PAGES, KK_GATHER, KK_LOOKUP, KK_EMBED, KK_PLAN,
     KK_QKV_G, KK_ATTN_DECODE, KK_PROJ_G, KK_FCIN_G, KK_FCOUT_G, KK_LNF,
     KK_QKV_L, KK_ATTN_LOCAL, KK_PROJ_L, KK_FCIN_L, KK_FCOUT_L, KK_GATE, KK_HEADS, KK_SAMPLE, KK_COMMIT,
-    KK_BIMG, KK_ATTN_COMBINE,
+    KK_BIMG, KK_ATTN_COMBINE, KK_ATTN_PREFILL,
     KK_COUNT
 };
 const char *kernel_kind_name(int kind);
@@ -145,6 +145,8 @@ private:
     void copy_page(int dst, int src);
     void release_pages(Slot &s);
     void upload_page_updates(const std::vector<int> &updates);
+    // flash-prefill work list of one pass (rows' slots and positions on the host)
+    void plan_prefill_attention(int R, const int *slot, const int *pos);
 
     // control-block layout (ints) for R = r_max_ rows
     int off_slot() const { return 0; }
@@ -159,6 +161,13 @@ private:
     int device_ = 0;
     int max_streams_ = 0, max_ctx_ = 0, pages_per_stream_ = 0, n_pages_ = 0, r_max_ = 0;
     int tc_direct_min_rows_ = 512, tc_direct_rows_ = 256;
+    // flash-prefill plan of the current pass: items (2 x int4 each) on the device, with a
+    // pinned staging copy; active while a prefill pass runs on the tensor-core path
+    int4 *pf_items_ = nullptr;
+    int4 *h_pf_items_ = nullptr;
+    int *h_pf_plan_ = nullptr;
+    size_t pf_cap_items_ = 0;
+    bool pf_active_ = false, pf_split_ = false;
     cudaStream_t stream_ = nullptr, own_stream_ = nullptr;
     std::vector<void *> owned_, pinned_;
     size_t weights_bytes_ = 0;

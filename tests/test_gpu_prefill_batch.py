@@ -142,3 +142,35 @@ def test_prefill_batch_rejects_bad_batches(pkg, weights_path):
         assert e.position(a) == 0 and e.position(b) == 0
     finally:
         e.close()
+
+
+def test_prefill_batch_after_long_prefixes_merges_chunks(pkg, weights_path):
+    # prefixes of 600 and 1030 positions: the new rows' groups attend over 2 and 3 chunks
+    # (partials per chunk, merged by the combine kernel); 13 and 9 rows make partial groups
+    e = pkg.Engine(weights_path, device=0, max_streams=4, max_ctx=1100, max_rows=64)
+    try:
+        e.set_tc_policy(16, 64)
+        plan = [(600, 13, 51), (1030, 9, 52)]
+        sids, states, rows = [], [], []
+        for L, n, seed in plan:
+            s = e.open()
+            k, v, h0, _ = global_state(L, seed=seed)
+            e.set_state(s, k, v, h0)
+            sids.append(s)
+            states.append((k, v, h0))
+            rows.append(prompt_rows(n, seed=seed + 10))
+        e.prefill_batch(sids, rows, starts=[L for L, _, _ in plan])
+        for i, (L, n, _) in enumerate(plan):
+            k, v, h0 = states[i]
+            o = Oracle(weights_path, max_ctx=1100, a16_prefill=True)
+            o.set_state(k, v, h0)
+            o.prefill_rows(rows[i], start=L)
+            assert e.position(sids[i]) == o.position == L + n
+            assert np.abs(e.hidden(sids[i]) - o.hidden()).max() < TOL
+            for layer in (0, 11):
+                kk, vv = e.kv(sids[i], layer, L, n)
+                ok, ov = o.kv(layer, L, n)
+                assert np.abs(kk - ok).max() < TOL
+                assert np.abs(vv - ov).max() < TOL
+    finally:
+        e.close()
