@@ -382,6 +382,8 @@ void set_tc_attr() {
         d3 = std::max(d3, tc_smem_bytes_direct(n, TC_F16X3, tc_max_stages_direct(n, TC_F16X3)));
     }
     CK(cudaFuncSetAttribute(k_gemm_tc<EPI, TC_F16, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, s1));
+    CK(cudaFuncSetAttribute(k_gemm_tc<EPI, TC_F16, false>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    CK(cudaFuncSetAttribute(k_gemm_tc<EPI, TC_F16X3, false>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
     CK(cudaFuncSetAttribute(k_gemm_tc<EPI, TC_F16X3, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, s3));
     CK(cudaFuncSetAttribute(k_gemm_tc<EPI, TC_F16, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, d1));
     CK(cudaFuncSetAttribute(k_gemm_tc<EPI, TC_F16X3, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, d3));
@@ -458,7 +460,7 @@ void launch_tc(TcArgs a, int prec, cudaStream_t st, bool pdl, int direct_min, in
     int nsub = std::min(a.N, kTcMaxNS);
     while (a.N % nsub) nsub -= 16;  // N is a multiple of 16
     const int nz = a.N / nsub;
-    // split K over the largest cluster (<= 8) that keeps every CTA of the grid resident
+    // split K over the largest cluster (<= 16) that keeps every CTA of the grid resident
     int C = kTcMaxCluster;
     while (C > 1 && (tiles * C * nz > 148 || C > nchunks)) C >>= 1;
     const int per = (nchunks + C - 1) / C;  // most chunks one CTA handles

@@ -48,7 +48,7 @@ constexpr int kTcEpiThreads = 256;  // dequant / epilogue threads (8 warps, two 
 constexpr int kTcThreads = 64 + kTcEpiThreads;
 constexpr int kTcMaxNS = 64;   // batch rows per CTA (MMA N) with split-K; more rows split over gridDim.z
 constexpr int kTcMaxND = 256;  // batch rows per CTA in the direct (no split-K) form
-constexpr int kTcMaxCluster = 8;
+constexpr int kTcMaxCluster = 16;  // 16 is a non-portable cluster size (opted in per kernel)
 
 enum { TC_STORE = 0, TC_QKV = 1, TC_RESID = 2, TC_GELU_B = 3 };
 
@@ -127,7 +127,7 @@ __host__ __device__ constexpr int tc_stage_bytes(int N, int prec) {
     return (16384 * tc_parts(prec) + N * 128 * tc_parts(prec) + 8192 + 512 + 1023) / 1024 * 1024;
 }
 
-// receive buffer of the split-K reduction: C partial slices of (128 / C) rows x NS columns
+// receive buffer of the split-K reduction: C partial slices of NS columns x (128 / C) rows
 __host__ __device__ constexpr int tc_recv_bytes(int NS) { return kTcM * NS * 4; }
 
 __host__ __device__ constexpr int tc_smem_bytes(int NS, int prec, int stages) {
@@ -225,6 +225,29 @@ __device__ __forceinline__ void tc_epi_one(const TcArgs &a, int gm, int rr, int 
     }
 }
 
+// Split-K epilogue items are (pair of tile rows, batch row); thread u takes items u,
+// u + 256, ...  Global inputs of kTcPreB items starting at `base`: the residual pair (RESID) or
+// the RoPE entry (QKV).
+constexpr int kTcPreB = 4;
+template <int EPI>
+__device__ __forceinline__ void tc_splitk_pre(const TcArgs &a, int base, int tile, int rank, int RS, int NS, int r0,
+                                              const int *s_pos, float2 *pre) {
+    const int HP = RS / 2, total = HP * NS;
+#pragma unroll
+    for (int bi = 0; bi < kTcPreB; ++bi) {
+        const int idx = base + bi * kTcEpiThreads;
+        pre[bi] = make_float2(0.f, 0.f);
+        if (idx < total) {
+            const int pr = idx % HP, n = idx / HP;
+            const int gm = tile * kTcM + rank * RS + 2 * pr;
+            const int rr = r0 + n;
+            if (EPI == TC_RESID && rr < a.R) pre[bi] = *reinterpret_cast<const float2 *>(a.out + (size_t)rr * a.ldo + gm);
+            if (EPI == TC_QKV && rr < a.R && gm < 2 * kHidden)
+                pre[bi] = a.rope[(size_t)s_pos[n] * (kHeadDim / 2) + ((gm % kHeadDim) >> 1)];
+        }
+    }
+}
+
 // DIRECT = false: split-K over a cluster of a.csize CTAs, partials reduce-scattered through
 // DSMEM, <= 64 batch rows per CTA (decode batches).  DIRECT = true: one CTA per (weight tile,
 // batch slice of <= 256 rows) runs every K chunk and its epilogue reads the accumulators
@@ -253,6 +276,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
     const size_t bimg_part = (size_t)a.K * N * 2;  // bytes of one activation image part
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
     float *recv = reinterpret_cast<float *>(smem + (size_t)S * SB);  // [C][NS][RS] partial slices
+    float2 pre0[kTcPreB];  // split-K epilogue: first batch of global inputs, fetched early
     const int RS = kTcM / C;                                         // tile rows reduced here
     const int nchunks_total = a.K / kTcK;
     const int c0 = rank * nchunks_total / C;
@@ -411,6 +435,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
                 s_dst[j] = dst;
             }
         }
+        if (!DIRECT) {
+            // the split-K epilogue's first batch of global inputs (residual rows, RoPE entries:
+            // outputs of earlier kernels) is fetched now, while the MMAs run
+            asm volatile("barrier.sync 1, %0;" ::"n"(kTcEpiThreads) : "memory");  // s_pos visible
+            tc_splitk_pre<EPI>(a, u, tile, rank, RS, NS, r0, s_pos, pre0);
+        }
         const int q = warp & 3;                 // TMEM lane quarter this warp may read
         const int m = q * 32 + lane;            // weight row within the tile
         // the two warps of a lane quarter split the columns: [0, split) and [split, NS)
@@ -456,6 +486,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
                     for (int j = 0; j < 16; ++j) v[j] = 0.f;
                 }
 #pragma unroll
+                // a warp's stores for one column land as two 64-byte runs (lanes = consecutive
+                // rows); 16-byte stores along the columns measured slower
+#pragma unroll
                 for (int j = 0; j < 16; ++j) st_cluster_f32(rbase + (uint32_t)((n0 + j) * RS * 4), v[j]);
             }
         }
@@ -473,32 +506,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
         const int u = threadIdx.x - 64;
         const int HP = RS / 2;
         const int total = HP * NS;
-        const float2 *rv = reinterpret_cast<const float2 *>(recv);  // [C][NS][HP]
-        constexpr int kB = 4;
-        for (int base = u; base < total; base += kB * kTcEpiThreads) {
-            float2 pre[kB];
+        for (int base = u; base < total; base += kTcPreB * kTcEpiThreads) {
+            float2 pre[kTcPreB];
+            if (base == u) {
 #pragma unroll
-            for (int bi = 0; bi < kB; ++bi) {
-                const int idx = base + bi * kTcEpiThreads;
-                pre[bi] = make_float2(0.f, 0.f);
-                if (idx < total) {
-                    const int pr = idx % HP, n = idx / HP;
-                    const int gm = tile * kTcM + rank * RS + 2 * pr;
-                    const int rr = r0 + n;
-                    if (EPI == TC_RESID && rr < a.R)
-                        pre[bi] = *reinterpret_cast<const float2 *>(a.out + (size_t)rr * a.ldo + gm);
-                    if (EPI == TC_QKV && rr < a.R && gm < 2 * kHidden)
-                        pre[bi] = a.rope[(size_t)s_pos[n] * (kHeadDim / 2) + ((gm % kHeadDim) >> 1)];
-                }
+                for (int bi = 0; bi < kTcPreB; ++bi) pre[bi] = pre0[bi];
+            } else {
+                tc_splitk_pre<EPI>(a, base, tile, rank, RS, NS, r0, s_pos, pre);
             }
 #pragma unroll
-            for (int bi = 0; bi < kB; ++bi) {
+            for (int bi = 0; bi < kTcPreB; ++bi) {
                 const int idx = base + bi * kTcEpiThreads;
                 if (idx >= total) break;
                 const int pr = idx % HP, n = idx / HP;
                 float v0 = 0.f, v1 = 0.f;
                 for (int src = 0; src < C; ++src) {
-                    const float2 pv = rv[((size_t)src * NS + n) * HP + pr];
+                    const float2 pv = reinterpret_cast<const float2 *>(recv)[((size_t)src * NS + n) * HP + pr];
                     v0 += pv.x;
                     v1 += pv.y;
                 }
