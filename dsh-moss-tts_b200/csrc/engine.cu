@@ -387,6 +387,8 @@ void set_tc_attr() {
     CK(cudaFuncSetAttribute(k_gemm_tc<EPI, TC_F16X3, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, s3));
     CK(cudaFuncSetAttribute(k_gemm_tc<EPI, TC_F16, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, d1));
     CK(cudaFuncSetAttribute(k_gemm_tc<EPI, TC_F16X3, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, d3));
+    CK(cudaFuncSetAttribute(k_gemm_tp<EPI, TC_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, d1));
+    CK(cudaFuncSetAttribute(k_gemm_tp<EPI, TC_F16X3>, cudaFuncAttributeMaxDynamicSharedMemorySize, d3));
 }
 
 }  // namespace
@@ -447,14 +449,15 @@ void launch_tc(TcArgs a, int prec, cudaStream_t st, bool pdl, int direct_min, in
         while (a.N % ns) ns -= 16;
         a.nsub = ns;
         a.csize = 1;
-        a.stages = std::min(nchunks, tc_max_stages_direct(ns, prec));
-        const dim3 grid(tiles, 1, a.N / ns);
+        a.stages = tc_max_stages_direct(ns, prec);
+        // tile-persistent: at most one CTA per SM walks the (weight tile, slice) tiles
+        const dim3 grid(std::min(tiles * (a.N / ns), kNumSMs));
         if (prec == TC_F16X3)
-            launch_kc(pdl, 0, k_gemm_tc<EPI, TC_F16X3, true>, grid, dim3(kTcThreads),
-                      tc_smem_bytes_direct(ns, TC_F16X3, a.stages), st, a);
-        else
-            launch_kc(pdl, 0, k_gemm_tc<EPI, TC_F16, true>, grid, dim3(kTcThreads), tc_smem_bytes_direct(ns, TC_F16, a.stages),
+            launch_kc(pdl, 0, k_gemm_tp<EPI, TC_F16X3>, grid, dim3(kTpThreads), tc_smem_bytes_direct(ns, TC_F16X3, a.stages),
                       st, a);
+        else
+            launch_kc(pdl, 0, k_gemm_tp<EPI, TC_F16>, grid, dim3(kTpThreads), tc_smem_bytes_direct(ns, TC_F16, a.stages), st,
+                      a);
         return;
     }
     int nsub = std::min(a.N, kTcMaxNS);

@@ -176,6 +176,32 @@ __device__ __forceinline__ __half2 i8x2_to_h2(uint32_t w_flipped, uint32_t sel) 
     return __hsub2(*reinterpret_cast<const __half2 *>(&h), __half2half2(__ushort_as_half((unsigned short)0x6480)));
 }
 
+// Dequantise 16-byte piece j (k = 16 j .. 16 j + 15) of weight row t of a stage: int8 x fp16
+// scale -> hi = fp16(q d) and (NP = 2) lo = fp16(q d - hi), one rounding each, as fp16 of the
+// exact fp32 product and of its remainder.  k = 16 j + e goes to 16-byte unit 2 j (+1) of the
+// row's 128-byte line in the A tile, stored at unit ^ (t % 8) (SWIZZLE_128B).
+template <int NP>
+__device__ __forceinline__ void tc_dequant_piece(const int8_t *w8, const __half *sc, uint8_t *arow, int t, int j) {
+    const int4 q = *reinterpret_cast<const int4 *>(w8 + ((j ^ ((t >> 1) & 3)) << 4));
+    const __half2 d2 = __half2half2(sc[j >> 1]);
+    const uint32_t words[4] = {(uint32_t)q.x ^ 0x80808080u, (uint32_t)q.y ^ 0x80808080u, (uint32_t)q.z ^ 0x80808080u,
+                               (uint32_t)q.w ^ 0x80808080u};
+    __align__(16) __half2 h[8];
+    __align__(16) __half2 l[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        const __half2 qq = i8x2_to_h2(words[e >> 1], (e & 1) ? 0x7362u : 0x5140u);
+        h[e] = __hmul2_rn(qq, d2);
+        if (NP == 2) l[e] = __hfma2(qq, d2, __hneg2(h[e]));
+    }
+    *reinterpret_cast<int4 *>(arow + (((2 * j) ^ (t & 7)) << 4)) = *reinterpret_cast<const int4 *>(h);
+    *reinterpret_cast<int4 *>(arow + (((2 * j + 1) ^ (t & 7)) << 4)) = *reinterpret_cast<const int4 *>(h + 4);
+    if (NP == 2) {
+        *reinterpret_cast<int4 *>(arow + 16384 + (((2 * j) ^ (t & 7)) << 4)) = *reinterpret_cast<const int4 *>(l);
+        *reinterpret_cast<int4 *>(arow + 16384 + (((2 * j + 1) ^ (t & 7)) << 4)) = *reinterpret_cast<const int4 *>(l + 4);
+    }
+}
+
 // One element of the direct form's epilogue: weight row gm (this thread's TMEM lane), batch row
 // rr, accumulator v, bias b, `pre` = what tc_epi_pre fetched for it.  Uniform over the warp
 // for a given rr (the QKV pair exchange is a shuffle between lanes gm and gm ^ 1).
@@ -390,32 +416,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
             const __half *sc = reinterpret_cast<const __half *>(st + OFF_SC) + t * 2;
             uint8_t *arow = st + t * 128;
 #pragma unroll
-            for (int jj = 0; jj < 2; ++jj) {  // 16-byte piece j of the row = k 16j..16j+15
-                const int j = 2 * hf + jj;
-                const int4 q = *reinterpret_cast<const int4 *>(w8 + ((j ^ ((t >> 1) & 3)) << 4));
-                const __half2 d2 = __half2half2(sc[j >> 1]);
-                const uint32_t words[4] = {(uint32_t)q.x ^ 0x80808080u, (uint32_t)q.y ^ 0x80808080u,
-                                           (uint32_t)q.z ^ 0x80808080u, (uint32_t)q.w ^ 0x80808080u};
-                // hi = fp16(q d), lo = fp16(q d - hi): one rounding each, as fp16(fp32 product)
-                // and fp16(fp32 product - hi) (q d is exact in fp32)
-                __align__(16) __half2 h[8];
-                __align__(16) __half2 l[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const __half2 qq = i8x2_to_h2(words[e >> 1], (e & 1) ? 0x7362u : 0x5140u);
-                    h[e] = __hmul2_rn(qq, d2);
-                    if (NP == 2) l[e] = __hfma2(qq, d2, __hneg2(h[e]));
-                }
-                // k = 16j + e -> 16-byte unit u = 2j (+1), stored at u ^ (t % 8)
-                *reinterpret_cast<int4 *>(arow + (((2 * j) ^ (t & 7)) << 4)) = *reinterpret_cast<const int4 *>(h);
-                *reinterpret_cast<int4 *>(arow + (((2 * j + 1) ^ (t & 7)) << 4)) = *reinterpret_cast<const int4 *>(h + 4);
-                if (NP == 2) {
-                    *reinterpret_cast<int4 *>(arow + 16384 + (((2 * j) ^ (t & 7)) << 4)) =
-                        *reinterpret_cast<const int4 *>(l);
-                    *reinterpret_cast<int4 *>(arow + 16384 + (((2 * j + 1) ^ (t & 7)) << 4)) =
-                        *reinterpret_cast<const int4 *>(l + 4);
-                }
-            }
+            for (int jj = 0; jj < 2; ++jj) tc_dequant_piece<NP>(w8, sc, arow, t, 2 * hf + jj);
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             mbar_arrive(&dq_bar[s]);
         }
@@ -576,6 +577,224 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
         }
     }
     }  // !DIRECT
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 1) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols));
+    }
+}
+
+// Tile-persistent form of the direct GEMM (prefill passes): a grid of <= 148 CTAs walks the
+// (weight tile, batch slice) tiles round-robin.  The producer, dequant and MMA roles stream
+// every K chunk of every tile of the CTA through one stage ring, and the accumulators are
+// double-buffered in TMEM (2 x NS columns), so the epilogue warps drain tile j while the MMAs
+// of tile j + 1 run.  Roles: warp 0 producer, warp 1 MMA issuer, warps 2..5 dequant (a weight
+// row per thread), warps 6..13 epilogue (two per TMEM lane quarter, splitting the columns).
+// acc_full[b]: the MMAs of the tile in buffer b are done; acc_empty[b]: its epilogue has read
+// it.  Every wait is bounded.
+constexpr int kTpDqThreads = 128;
+constexpr int kTpEpiThreads = 256;
+constexpr int kTpThreads = 64 + kTpDqThreads + kTpEpiThreads;
+
+template <int EPI, int PREC>
+__global__ void __launch_bounds__(kTpThreads, 1) k_gemm_tp(const TcArgs a) {
+    extern __shared__ uint8_t tc_smem_raw[];
+    __shared__ __align__(8) uint64_t full_bar[4], bfull_bar[4], dq_bar[4], empty_bar[4], accf_bar[2], acce_bar[2];
+    __shared__ uint32_t tmem_base_sh;
+    __shared__ int s_pos[kTcMaxND], s_dst[kTcMaxND];
+    constexpr int NP = tc_parts(PREC);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int N = a.N, NS = a.nsub, S = a.stages;
+    const int SB = tc_stage_bytes(NS, PREC);
+    const int OFF_B = 16384 * NP;
+    const int OFF_W8 = OFF_B + NS * 128 * NP;
+    const int OFF_SC = OFF_W8 + 8192;
+    const size_t bimg_part = (size_t)a.K * N * 2;
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
+    const int nchunks = a.K / kTcK;
+    const int n_m = a.rows / kTcM;
+    const int n_tiles = n_m * (N / NS);
+    const int G = gridDim.x;
+    const int my_tiles = (int)blockIdx.x < n_tiles ? (n_tiles - 1 - (int)blockIdx.x) / G + 1 : 0;
+    const int total = my_tiles * nchunks;  // K chunks this CTA streams
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&bfull_bar[s], 1);
+            mbar_init(&dq_bar[s], kTpDqThreads);
+            mbar_init(&empty_bar[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&accf_bar[b], 1);
+            mbar_init(&acce_bar[b], kTpEpiThreads);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    uint32_t ncols = 32;
+    while (ncols < (uint32_t)(2 * NS)) ncols <<= 1;
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_sh)),
+                     "r"(ncols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = tmem_base_sh;
+
+    if (warp == 0) {
+        // ---------------- producer
+        if (lane == 0 && total > 0) {
+            auto src = [&](int seq, int &mt, int &z, int &c) {
+                const int t = (int)blockIdx.x + (seq / nchunks) * G;
+                c = seq % nchunks;
+                mt = t % n_m;
+                z = t / n_m;
+            };
+            auto load_w = [&](int seq) {
+                int mt, z, c;
+                src(seq, mt, z, c);
+                const int s = seq % S;
+                uint8_t *st = smem + (size_t)s * SB;
+                mbar_expect_tx(&full_bar[s], 8192 + 512);
+                bulk_g2s(st + OFF_W8, a.qt + ((size_t)mt * nchunks + c) * 8192, 8192, &full_bar[s]);
+                bulk_g2s(st + OFF_SC, a.st + ((size_t)mt * nchunks + c) * 256, 512, &full_bar[s]);
+            };
+            auto load_b = [&](int seq) {
+                int mt, z, c;
+                src(seq, mt, z, c);
+                const int s = seq % S;
+                uint8_t *st = smem + (size_t)s * SB;
+                mbar_expect_tx(&bfull_bar[s], (uint32_t)(NS * 128 * NP));
+#pragma unroll
+                for (int p = 0; p < NP; ++p)
+                    bulk_g2s(st + OFF_B + p * NS * 128, a.bimg + p * bimg_part + ((size_t)c * N + (size_t)z * NS) * 128,
+                             (uint32_t)NS * 128, &bfull_bar[s]);
+            };
+            const int pre = min(S, total);
+            for (int i = 0; i < pre; ++i) load_w(i);
+            pdl_wait();
+            pdl_trigger();
+            for (int i = 0; i < pre; ++i) load_b(i);
+            int issued = pre;
+            for (int i = pre; i < total; ++i) {
+                const int s = i % S;
+                if (!mbar_wait(&empty_bar[s], ((i / S) - 1) & 1, a.err, 11)) break;
+                load_w(i);
+                load_b(i);
+                ++issued;
+            }
+            for (int i = max(0, issued - S); i < issued; ++i) {
+                mbar_wait(&full_bar[i % S], (i / S) & 1, a.err, 12);
+                mbar_wait(&bfull_bar[i % S], (i / S) & 1, a.err, 12);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer
+        if (lane == 0 && total > 0) {
+            const uint32_t idesc = (1u << 4) | ((uint32_t)(NS >> 3) << 17) | ((uint32_t)(kTcM >> 4) << 24);
+            int seq = 0;
+            bool ok = true;
+            for (int j = 0; j < my_tiles && ok; ++j) {
+                const int ab = j & 1;
+                if (j >= 2 && !mbar_wait(&acce_bar[ab], ((j >> 1) - 1) & 1, a.err, 13)) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t dcol = tmem + (uint32_t)(ab * NS);
+                for (int c = 0; c < nchunks; ++c, ++seq) {
+                    const int s = seq % S;
+                    if (!mbar_wait(&dq_bar[s], (seq / S) & 1, a.err, 14) ||
+                        !mbar_wait(&bfull_bar[s], (seq / S) & 1, a.err, 14)) {
+                        ok = false;
+                        break;
+                    }
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    uint8_t *st = smem + (size_t)s * SB;
+                    const uint32_t abase = smem_u32(st), bbase = smem_u32(st + OFF_B);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        tc_mma(dcol, sw128_desc(abase + k * 32), sw128_desc(bbase + k * 32), idesc, (c > 0 || k > 0) ? 1u : 0u);
+                        if (NP == 2) {
+                            tc_mma(dcol, sw128_desc(abase + k * 32), sw128_desc(bbase + NS * 128 + k * 32), idesc, 1u);
+                            tc_mma(dcol, sw128_desc(abase + 16384 + k * 32), sw128_desc(bbase + k * 32), idesc, 1u);
+                        }
+                    }
+                    tc_commit(&empty_bar[s]);
+                }
+                tc_commit(&accf_bar[ab]);  // also on the error path: the epilogue leaves on its own
+            }
+        }
+    } else if (warp < 2 + kTpDqThreads / 32) {
+        // ---------------- dequant: thread t converts weight row t of every chunk
+        const int t = threadIdx.x - 64;
+        for (int i = 0; i < total; ++i) {
+            const int s = i % S;
+            if (!mbar_wait(&full_bar[s], (i / S) & 1, a.err, 15)) break;
+            uint8_t *st = smem + (size_t)s * SB;
+            const int8_t *w8 = reinterpret_cast<const int8_t *>(st + OFF_W8) + t * 64;
+            const __half *sc = reinterpret_cast<const __half *>(st + OFF_SC) + t * 2;
+            uint8_t *arow = st + t * 128;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) tc_dequant_piece<NP>(w8, sc, arow, t, j);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_arrive(&dq_bar[s]);
+        }
+    } else {
+        // ---------------- epilogue: tile j's accumulators from TMEM buffer j & 1
+        const int e = threadIdx.x - 64 - kTpDqThreads;  // 0..255
+        const int q = warp & 3;                         // TMEM lane quarter of this warp
+        const int hf = e >> 7;                          // column half
+        const int mrow = q * 32 + lane;
+        const int split = ((NS / 16 + 1) / 2) * 16;
+        const int cb = hf ? split : 0, ce = hf ? NS : split;
+        pdl_wait();
+        for (int j = 0; j < my_tiles; ++j) {
+            const int t = (int)blockIdx.x + j * G;
+            const int mt = t % n_m, r0 = (t / n_m) * NS, ab = j & 1;
+            if (EPI == TC_QKV) {
+                asm volatile("barrier.sync 2, %0;" ::"n"(kTpEpiThreads) : "memory");  // previous tile's readers
+                for (int jj = e; jj < NS; jj += kTpEpiThreads) {
+                    const int rr = r0 + jj;
+                    int pos = 0, dst = 0;
+                    if (rr < a.R) {
+                        pos = a.row_pos ? a.row_pos[rr] : a.fixed_pos;
+                        const int slot = a.row_slot[rr];
+                        dst = a.kv ? a.page_table[(size_t)slot * a.pages_per_stream + pos / kPage] : slot;
+                    }
+                    s_pos[jj] = pos;
+                    s_dst[jj] = dst;
+                }
+                asm volatile("barrier.sync 2, %0;" ::"n"(kTpEpiThreads) : "memory");
+            }
+            const bool acc_ok = mbar_wait(&accf_bar[ab], (j >> 1) & 1, a.err, 16);
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const int gm = mt * kTcM + mrow;
+            const float b = a.bias ? a.bias[gm] : 0.f;
+            for (int n0 = cb; n0 < ce; n0 += 16) {
+                float2 pre[16];
+#pragma unroll
+                for (int jj = 0; jj < 16; ++jj)
+                    pre[jj] = tc_epi_pre<EPI>(a, gm, r0 + n0 + jj, EPI == TC_QKV ? s_pos[n0 + jj] : 0);
+                float v[16];
+                if (acc_ok) {
+                    tc_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * NS + n0), v);
+                } else {
+#pragma unroll
+                    for (int jj = 0; jj < 16; ++jj) v[jj] = 0.f;
+                }
+#pragma unroll
+                for (int jj = 0; jj < 16; ++jj) {
+                    const int n = n0 + jj;
+                    tc_epi_one<EPI, NP>(a, gm, r0 + n, N, v[jj], b, EPI == TC_QKV ? s_pos[n] : 0,
+                                        EPI == TC_QKV ? s_dst[n] : 0, pre[jj]);
+                }
+            }
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            mbar_arrive(&acce_bar[ab]);
+            if (!acc_ok) break;
+        }
+    }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     if (warp == 1) {

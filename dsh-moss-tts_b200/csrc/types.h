@@ -21,6 +21,7 @@ constexpr int kLocalLen = 17;
 constexpr int kLayers = 12;
 constexpr int kPage = 16;                                  // positions per KV page
 constexpr int kPageHalfs = 2 * kHeads * kPage * kHeadDim;  // one page of one layer (k and v)
+constexpr int kNumSMs = 148;                                // B200: persistent grids (one CTA per SM)
 constexpr int kPlanThreads = 1024;                          // threads of the split-K plan kernel
 constexpr int kAttnChunk = 16;                             // minimum split-K chunk (positions, one page)
 constexpr int kPartStride = 68;  // floats per split-K partial: m, l, 2 pad, o[64] (16-byte rows)
