@@ -381,12 +381,10 @@ void set_tc_attr() {
         d1 = std::max(d1, tc_smem_bytes_direct(n, TC_F16, tc_max_stages_direct(n, TC_F16)));
         d3 = std::max(d3, tc_smem_bytes_direct(n, TC_F16X3, tc_max_stages_direct(n, TC_F16X3)));
     }
-    CK(cudaFuncSetAttribute(k_gemm_tc<EPI, TC_F16, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, s1));
-    CK(cudaFuncSetAttribute(k_gemm_tc<EPI, TC_F16, false>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
-    CK(cudaFuncSetAttribute(k_gemm_tc<EPI, TC_F16X3, false>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
-    CK(cudaFuncSetAttribute(k_gemm_tc<EPI, TC_F16X3, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, s3));
-    CK(cudaFuncSetAttribute(k_gemm_tc<EPI, TC_F16, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, d1));
-    CK(cudaFuncSetAttribute(k_gemm_tc<EPI, TC_F16X3, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, d3));
+    CK(cudaFuncSetAttribute(k_gemm_tc<EPI, TC_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, s1));
+    CK(cudaFuncSetAttribute(k_gemm_tc<EPI, TC_F16>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    CK(cudaFuncSetAttribute(k_gemm_tc<EPI, TC_F16X3>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    CK(cudaFuncSetAttribute(k_gemm_tc<EPI, TC_F16X3>, cudaFuncAttributeMaxDynamicSharedMemorySize, s3));
     CK(cudaFuncSetAttribute(k_gemm_tp<EPI, TC_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, d1));
     CK(cudaFuncSetAttribute(k_gemm_tp<EPI, TC_F16X3>, cudaFuncAttributeMaxDynamicSharedMemorySize, d3));
 }
@@ -472,10 +470,10 @@ void launch_tc(TcArgs a, int prec, cudaStream_t st, bool pdl, int direct_min, in
     a.stages = std::min(per, tc_max_stages(nsub, prec));
     const dim3 grid(tiles * C, 1, nz);
     if (prec == TC_F16X3)
-        launch_kc(pdl, C, k_gemm_tc<EPI, TC_F16X3, false>, grid, dim3(kTcThreads), tc_smem_bytes(nsub, TC_F16X3, a.stages), st,
+        launch_kc(pdl, C, k_gemm_tc<EPI, TC_F16X3>, grid, dim3(kTcThreads), tc_smem_bytes(nsub, TC_F16X3, a.stages), st,
                   a);
     else
-        launch_kc(pdl, C, k_gemm_tc<EPI, TC_F16, false>, grid, dim3(kTcThreads), tc_smem_bytes(nsub, TC_F16, a.stages), st, a);
+        launch_kc(pdl, C, k_gemm_tc<EPI, TC_F16>, grid, dim3(kTcThreads), tc_smem_bytes(nsub, TC_F16, a.stages), st, a);
 }
 
 }  // namespace
@@ -486,7 +484,14 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
                       float *x) {
     const int N = (R + 15) / 16 * 16;
     const int prec = gemm_path_ == 3 ? TC_F16 : TC_F16X3;
-    launch_k(pdl_, k_build_bimg, dim3(N), dim3(256), kHidden * 4, stream_, x, kHidden, R, N, kHidden, L.ln1_w, L.ln1_b, tc_parts(prec), bimg_a_);
+    // GEMMs in the direct form (prefill passes) store plain outputs; the QKV epilogue (RoPE, KV
+    // append) runs as its own pass and residual adds move into the next LayerNorm kernel, which
+    // reads x anyway.  The last global layer's fc_out keeps its residual epilogue (ln_f reads x).
+    const bool direct = !local && tc_direct_min_rows_ > 0 && N >= tc_direct_min_rows_;
+    const float *add1 = pending_resid_;
+    pending_resid_ = nullptr;
+    launch_k(pdl_, k_build_bimg, dim3(N), dim3(256), kHidden * 4, stream_, x, kHidden, R, N, kHidden, L.ln1_w, L.ln1_b,
+             tc_parts(prec), bimg_a_, add1);
     mark(KK_BIMG);
     TcArgs a{};
     a.N = N;
@@ -510,8 +515,18 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
         a.page_table = page_table_;
         a.pages_per_stream = pages_per_stream_;
     }
-    launch_tc<TC_QKV>(a, prec, stream_, pdl_, tc_direct_min_rows_, tc_direct_rows_);
-    mark(local ? KK_QKV_L : KK_QKV_G);
+    if (direct) {
+        a.out = mlp_;  // raw [R][2304], bias included
+        a.ldo = kQKV;
+        launch_tc<TC_STORE>(a, prec, stream_, pdl_, tc_direct_min_rows_, tc_direct_rows_);
+        mark(KK_QKV_G);
+        launch_k(pdl_, k_qkv_rope, dim3(unsigned((size_t(R) * (kQKV / 2) + 255) / 256)), dim3(256), 0, stream_, mlp_, R,
+                 row_slot, row_pos, rope_, q_, a.kv, page_table_, pages_per_stream_);
+        mark(KK_QKV_ROPE);
+    } else {
+        launch_tc<TC_QKV>(a, prec, stream_, pdl_, tc_direct_min_rows_, tc_direct_rows_);
+        mark(local ? KK_QKV_L : KK_QKV_G);
+    }
     // attention writes straight into proj's activation image; its padding rows are still
     // zero from the LN1 image built above with the same N
     if (local) {
@@ -575,11 +590,15 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
     p.rows = kHidden;
     p.K = kHidden;
     p.bias = L.proj_b;
-    p.out = x;
+    p.out = direct ? attn_ : x;
     p.ldo = kHidden;
-    launch_tc<TC_RESID>(p, prec, stream_, pdl_, tc_direct_min_rows_, tc_direct_rows_);
+    if (direct)
+        launch_tc<TC_STORE>(p, prec, stream_, pdl_, tc_direct_min_rows_, tc_direct_rows_);
+    else
+        launch_tc<TC_RESID>(p, prec, stream_, pdl_, tc_direct_min_rows_, tc_direct_rows_);
     mark(local ? KK_PROJ_L : KK_PROJ_G);
-    launch_k(pdl_, k_build_bimg, dim3(N), dim3(256), kHidden * 4, stream_, x, kHidden, R, N, kHidden, L.ln2_w, L.ln2_b, tc_parts(prec), bimg_a_);
+    launch_k(pdl_, k_build_bimg, dim3(N), dim3(256), kHidden * 4, stream_, x, kHidden, R, N, kHidden, L.ln2_w, L.ln2_b,
+             tc_parts(prec), bimg_a_, direct ? static_cast<const float *>(attn_) : nullptr);
     mark(KK_BIMG);
     TcArgs f{};
     f.N = N;
@@ -604,9 +623,15 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
     o.rows = kHidden;
     o.K = kFF;
     o.bias = L.fc_out_b;
-    o.out = x;
     o.ldo = kHidden;
-    launch_tc<TC_RESID>(o, prec, stream_, pdl_, tc_direct_min_rows_, tc_direct_rows_);
+    if (direct && li < kLayers - 1) {  // the next layer's LN1 kernel adds it to x
+        o.out = attn_;
+        launch_tc<TC_STORE>(o, prec, stream_, pdl_, tc_direct_min_rows_, tc_direct_rows_);
+        pending_resid_ = attn_;
+    } else {
+        o.out = x;
+        launch_tc<TC_RESID>(o, prec, stream_, pdl_, tc_direct_min_rows_, tc_direct_rows_);
+    }
     mark(local ? KK_FCOUT_L : KK_FCOUT_G);
 }
 
@@ -614,7 +639,8 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
 void Engine::heads_tc(int ch, int R) {
     const int N = (R + 15) / 16 * 16;
     const int prec = gemm_path_ == 3 ? TC_F16 : TC_F16X3;
-    launch_k(pdl_, k_build_bimg, dim3(N), dim3(256), kHidden * 4, stream_, lx_, kHidden, R, N, kHidden, llnf_w_, llnf_b_, tc_parts(prec), bimg_a_);
+    launch_k(pdl_, k_build_bimg, dim3(N), dim3(256), kHidden * 4, stream_, lx_, kHidden, R, N, kHidden, llnf_w_, llnf_b_,
+             tc_parts(prec), bimg_a_, static_cast<const float *>(nullptr));
     mark(KK_BIMG);
     TcArgs h{};
     h.N = N;
@@ -753,6 +779,7 @@ void Engine::block(const Layer &L, int li, bool local, int R, const int *row_slo
 
 // 12 global layers over rows already embedded in x_ (row_pos = positions being written).
 void Engine::global_layers(int R, const int *row_slot, const int *row_pos) {
+    pending_resid_ = nullptr;
     if (pf_active_) {  // a prefill pass: the host-built flash-prefill plan is already on the device
         for (int li = 0; li < kLayers; ++li) block(global_[li], li, false, R, row_slot, row_pos, 0, x_);
         return;
@@ -1353,7 +1380,7 @@ const char *kernel_kind_name(int kind) {
         "page_updates", "gather_hidden", "lookup_slot_row", "embed_frame", "attn_plan",
         "qkv_global", "attn_decode_paged", "proj_global", "fc_in_global", "fc_out_global", "ln_f",
         "qkv_local", "attn_local", "proj_local", "fc_in_local", "fc_out_local", "gate_w8a8",
-        "audio_heads", "sample", "frame_commit", "build_activation_image", "attn_combine", "attn_prefill"};
+        "audio_heads", "sample", "frame_commit", "build_activation_image", "attn_combine", "attn_prefill", "qkv_rope"};
     return (kind >= 0 && kind < KK_COUNT) ? names[kind] : "?";
 }
 

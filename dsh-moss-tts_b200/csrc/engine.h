@@ -44,7 +44,7 @@ enum KernelKind {
     KK_PAGES, KK_GATHER, KK_LOOKUP, KK_EMBED, KK_PLAN,
     KK_QKV_G, KK_ATTN_DECODE, KK_PROJ_G, KK_FCIN_G, KK_FCOUT_G, KK_LNF,
     KK_QKV_L, KK_ATTN_LOCAL, KK_PROJ_L, KK_FCIN_L, KK_FCOUT_L, KK_GATE, KK_HEADS, KK_SAMPLE, KK_COMMIT,
-    KK_BIMG, KK_ATTN_COMBINE, KK_ATTN_PREFILL,
+    KK_BIMG, KK_ATTN_COMBINE, KK_ATTN_PREFILL, KK_QKV_ROPE,
     KK_COUNT
 };
 const char *kernel_kind_name(int kind);
@@ -168,6 +168,8 @@ private:
     int *h_pf_plan_ = nullptr;
     size_t pf_cap_items_ = 0;
     bool pf_active_ = false, pf_split_ = false;
+    // a direct-form fc_out stored its output here; the next layer's LN1 kernel adds it to x
+    const float *pending_resid_ = nullptr;
     cudaStream_t stream_ = nullptr, own_stream_ = nullptr;
     std::vector<void *> owned_, pinned_;
     size_t weights_bytes_ = 0;

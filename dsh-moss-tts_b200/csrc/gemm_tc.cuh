@@ -17,8 +17,9 @@
 //     the partial D back with tcgen05.ld and scatter it through distributed shared memory:
 //     CTA j of the cluster receives every CTA's partial of tile rows [128 j / C, 128 (j+1) / C),
 //     sums the C partials in a fixed order and runs the epilogue for those rows;
-//   direct (prefill passes, <= 256 batch rows per CTA): one CTA runs every K chunk of its
-//     (weight tile, batch slice) and the eight warps run the epilogue straight from TMEM.
+//   direct (prefill passes, <= 256 batch rows per CTA; k_gemm_tp below): one CTA runs every
+//     K chunk of its (weight tile, batch slice) tiles and epilogue warps read the
+//     accumulators straight from TMEM, double-buffered so that epilogue and MMAs overlap.
 // Epilogues: bias / RoPE / KV append, GELU into the next GEMM's activation image, residual
 // add, or a plain store.  No atomics; the result does not depend on timing.
 // Every mbarrier wait is bounded: on time-out the kernel records an error code and leaves
@@ -274,24 +275,21 @@ __device__ __forceinline__ void tc_splitk_pre(const TcArgs &a, int base, int til
     }
 }
 
-// DIRECT = false: split-K over a cluster of a.csize CTAs, partials reduce-scattered through
-// DSMEM, <= 64 batch rows per CTA (decode batches).  DIRECT = true: one CTA per (weight tile,
-// batch slice of <= 256 rows) runs every K chunk and its epilogue reads the accumulators
-// straight from TMEM (prefill and large batches, where the grid is already wide).
-template <int EPI, int PREC, bool DIRECT>
+// Split-K form (decode batches): a cluster of a.csize CTAs shares a weight tile's K chunks,
+// partials reduce-scattered through DSMEM, <= 64 batch rows per CTA.
+template <int EPI, int PREC>
 __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
     extern __shared__ uint8_t tc_smem_raw[];
     __shared__ __align__(8) uint64_t full_bar[4], bfull_bar[4], dq_bar[4], empty_bar[4], acc_bar;
     __shared__ uint32_t tmem_base_sh;
-    constexpr int kRowsMax = DIRECT ? kTcMaxND : kTcMaxNS;
-    __shared__ int s_pos[kRowsMax], s_dst[kRowsMax];  // TC_QKV: per batch row position and page/slot
+    __shared__ int s_pos[kTcMaxNS], s_dst[kTcMaxNS];  // TC_QKV: per batch row position and page/slot
     constexpr int NP = tc_parts(PREC);  // operand parts (hi, lo)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int N = a.N;                  // rows of the activation image
     const int NS = a.nsub;              // rows handled by this CTA (MMA N)
-    const int C = DIRECT ? 1 : a.csize; // CTAs of the cluster (split-K)
+    const int C = a.csize;              // CTAs of the cluster (split-K)
     const int S = a.stages;
-    const int rank = DIRECT ? 0 : (int)cluster_rank();
+    const int rank = (int)cluster_rank();
     const int tile = blockIdx.x / C;
     const int r0 = blockIdx.z * NS;     // first batch row of this CTA
     const int SB = tc_stage_bytes(NS, PREC);
@@ -326,7 +324,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
                      "r"(ncols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
-    if (!DIRECT) cluster_arrive_relaxed();  // this CTA runs; matched by the wait before the first remote store
+    cluster_arrive_relaxed();  // this CTA runs; matched by the wait before the first remote store
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -436,12 +434,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
                 s_dst[j] = dst;
             }
         }
-        if (!DIRECT) {
-            // the split-K epilogue's first batch of global inputs (residual rows, RoPE entries:
-            // outputs of earlier kernels) is fetched now, while the MMAs run
-            asm volatile("barrier.sync 1, %0;" ::"n"(kTcEpiThreads) : "memory");  // s_pos visible
-            tc_splitk_pre<EPI>(a, u, tile, rank, RS, NS, r0, s_pos, pre0);
-        }
+        // the epilogue's first batch of global inputs (residual rows, RoPE entries: outputs of
+        // earlier kernels) is fetched now, while the MMAs run
+        asm volatile("barrier.sync 1, %0;" ::"n"(kTcEpiThreads) : "memory");  // s_pos visible
+        tc_splitk_pre<EPI>(a, u, tile, rank, RS, NS, r0, s_pos, pre0);
         const int q = warp & 3;                 // TMEM lane quarter this warp may read
         const int m = q * 32 + lane;            // weight row within the tile
         // the two warps of a lane quarter split the columns: [0, split) and [split, NS)
@@ -449,31 +445,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
         const int cb = hf ? split : 0, ce = hf ? NS : split;
         const bool acc_ok = nch > 0 && mbar_wait(&acc_bar, 0, a.err, 5);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        if (DIRECT) {
-            // the epilogue threads: s_pos / s_dst written above are visible
-            asm volatile("barrier.sync 1, %0;" ::"n"(kTcEpiThreads) : "memory");
-            const int gm = tile * kTcM + m;
-            const float b = a.bias ? a.bias[gm] : 0.f;
-            for (int n0 = cb; n0 < ce; n0 += 16) {
-                float2 pre[16];
-#pragma unroll
-                for (int j = 0; j < 16; ++j)
-                    pre[j] = tc_epi_pre<EPI>(a, gm, r0 + n0 + j, EPI == TC_QKV ? s_pos[n0 + j] : 0);
-                float v[16];
-                if (acc_ok && ok) {
-                    tc_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)n0, v);
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) v[j] = 0.f;
-                }
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int n = n0 + j;
-                    tc_epi_one<EPI, NP>(a, gm, r0 + n, N, v[j], b, EPI == TC_QKV ? s_pos[n] : 0,
-                                        EPI == TC_QKV ? s_dst[n] : 0, pre[j]);
-                }
-            }
-        } else {
+        {
             cluster_wait();  // every CTA of the cluster is running: its shared memory may be written
             const uint32_t dst_rank = (uint32_t)(m / RS);
             const uint32_t rbase =
@@ -486,7 +458,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
 #pragma unroll
                     for (int j = 0; j < 16; ++j) v[j] = 0.f;
                 }
-#pragma unroll
                 // a warp's stores for one column land as two 64-byte runs (lanes = consecutive
                 // rows); 16-byte stores along the columns measured slower
 #pragma unroll
@@ -494,7 +465,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
             }
         }
     }
-    if (!DIRECT) {
     // every thread of every CTA: the partial slices are delivered (release / acquire)
     __syncwarp();
     if (warp < 2) cluster_wait();  // matches the arrive at the start (warps 2..5 waited above)
@@ -576,7 +546,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
             }
         }
     }
-    }  // !DIRECT
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     if (warp == 1) {
@@ -805,10 +774,13 @@ __global__ void __launch_bounds__(kTpThreads, 1) k_gemm_tp(const TcArgs a) {
 
 // x fp32 [R][K] (optionally LayerNormed, K = 768) -> activation image with N padded rows;
 // rows R..N-1 are written as zeros.  parts = 2 also writes the image of the fp16 remainders
-// (x - fp16(x)) right after the first one.  One CTA per padded row.
-__global__ void __launch_bounds__(256) k_build_bimg(const float *__restrict__ x, int ldx, int R, int N, int K,
+// (x - fp16(x)) right after the first one.  add != null: first the residual add x += add
+// (written back to x; the preceding GEMM stored its output, bias included, in add).  One CTA
+// per padded row.
+__global__ void __launch_bounds__(256) k_build_bimg(float *__restrict__ x, int ldx, int R, int N, int K,
                                                     const float *__restrict__ ln_w, const float *__restrict__ ln_b,
-                                                    int parts, uint8_t *__restrict__ bimg) {
+                                                    int parts, uint8_t *__restrict__ bimg,
+                                                    const float *__restrict__ add) {
     extern __shared__ __align__(16) float xs_b[];
     pdl_enter();
     const int n = blockIdx.x;
@@ -819,7 +791,15 @@ __global__ void __launch_bounds__(256) k_build_bimg(const float *__restrict__ x,
                 *reinterpret_cast<int4 *>(bimg + p * part + bimg_off(n, k, N)) = make_int4(0, 0, 0, 0);
         return;
     }
-    for (int k = threadIdx.x; k < K; k += blockDim.x) xs_b[k] = x[(size_t)n * ldx + k];
+    if (add) {
+        for (int k = threadIdx.x; k < K; k += blockDim.x) {
+            const float v = __fadd_rn(x[(size_t)n * ldx + k], add[(size_t)n * ldx + k]);
+            x[(size_t)n * ldx + k] = v;
+            xs_b[k] = v;
+        }
+    } else {
+        for (int k = threadIdx.x; k < K; k += blockDim.x) xs_b[k] = x[(size_t)n * ldx + k];
+    }
     __syncthreads();
     if (ln_w) {  // LayerNorm (llm.cpp:159-171) with CTA-wide reductions, K = 768
         __shared__ float red[8];
@@ -865,6 +845,39 @@ __global__ void __launch_bounds__(256) k_build_bimg(const float *__restrict__ x,
         }
         *reinterpret_cast<int4 *>(bimg + bimg_off(n, k, N)) = *reinterpret_cast<const int4 *>(h);
         if (parts == 2) *reinterpret_cast<int4 *>(bimg + part + bimg_off(n, k, N)) = *reinterpret_cast<const int4 *>(l);
+    }
+}
+
+// The QKV epilogue of a prefill pass as its own pass over the GEMM's stored output (bias
+// included): raw [R][2304] -> RoPE on (2i, 2i + 1) pairs of q and k, q to q_out [R][768], k
+// and v appended to the paged fp16 KV -- the same arithmetic as the fused epilogue.  One
+// thread per column pair.
+__global__ void __launch_bounds__(256) k_qkv_rope(const float *__restrict__ raw, int R, const int *__restrict__ row_slot,
+                                                  const int *__restrict__ row_pos, const float2 *__restrict__ rope,
+                                                  float *__restrict__ q_out, __half *__restrict__ kv,
+                                                  const int *__restrict__ page_table, int pages_per_stream) {
+    pdl_enter();
+    constexpr int kPairs = kQKV / 2;
+    const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= (long long)R * kPairs) return;
+    const int rr = (int)(t / kPairs), gm = 2 * (int)(t % kPairs);
+    const float2 y = *reinterpret_cast<const float2 *>(raw + (size_t)rr * kQKV + gm);
+    const int pos = row_pos[rr];
+    float o0 = y.x, o1 = y.y;
+    if (gm < 2 * kHidden) {
+        const float2 cs = rope[(size_t)pos * (kHeadDim / 2) + ((gm % kHeadDim) >> 1)];
+        o0 = __fsub_rn(__fmul_rn(y.x, cs.x), __fmul_rn(y.y, cs.y));
+        o1 = __fadd_rn(__fmul_rn(y.y, cs.x), __fmul_rn(y.x, cs.y));
+    }
+    if (gm < kHidden) {
+        *reinterpret_cast<float2 *>(q_out + (size_t)rr * kHidden + gm) = make_float2(o0, o1);
+    } else {
+        const int kvsel = gm < 2 * kHidden ? 0 : 1;
+        const int c = gm - kHidden * (1 + kvsel);
+        const int page = page_table[(size_t)row_slot[rr] * pages_per_stream + pos / kPage];
+        __half *dst = kv + (size_t)page * kPageHalfs + ((kvsel * kHeads + c / kHeadDim) * kPage + pos % kPage) * kHeadDim +
+                      (c % kHeadDim);
+        *reinterpret_cast<__half2 *>(dst) = __floats2half2_rn(o0, o1);
     }
 }
 
