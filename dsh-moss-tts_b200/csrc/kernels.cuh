@@ -895,9 +895,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_prefill(const PfArgs a
     }
 
     // ---------------------------------------------------------------------- consumer warps
+    // Packed fp32 pairs (fma.rn.f32x2) halve the FMA instructions: a lane's 8-dim dot product
+    // accumulates even and odd dims separately, then adds the two.
     const int hd = wid;
     const int rg = lane >> 3, ds = lane & 7;
-    float qv[2][8], o[2][8], m[2], l[2];
+    float2 qv[2][4], o[2][4];
+    float m[2], l[2];
     int lim[2];
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
@@ -905,7 +908,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_prefill(const PfArgs a
         l[i] = 0.f;
         lim[i] = 0;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) o[i][j] = 0.f, qv[i][j] = 0.f;
+        for (int j = 0; j < 4; ++j) o[i][j] = make_float2(0.f, 0.f), qv[i][j] = make_float2(0.f, 0.f);
     }
     for (int seq = 0;; ++seq) {
         const int s = seq % kPfStages;
@@ -923,19 +926,29 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_prefill(const PfArgs a
                     const float4 *qp = reinterpret_cast<const float4 *>(qs + ((size_t)s * kPfGroup + gi) * kHidden +
                                                                         hd * kHeadDim + ds * 8);
                     const float4 x0 = qp[0], x1 = qp[1];
-                    qv[i][0] = x0.x * 0.125f; qv[i][1] = x0.y * 0.125f; qv[i][2] = x0.z * 0.125f; qv[i][3] = x0.w * 0.125f;
-                    qv[i][4] = x1.x * 0.125f; qv[i][5] = x1.y * 0.125f; qv[i][6] = x1.z * 0.125f; qv[i][7] = x1.w * 0.125f;
+                    qv[i][0] = make_float2(x0.x * 0.125f, x0.y * 0.125f);
+                    qv[i][1] = make_float2(x0.z * 0.125f, x0.w * 0.125f);
+                    qv[i][2] = make_float2(x1.x * 0.125f, x1.y * 0.125f);
+                    qv[i][3] = make_float2(x1.z * 0.125f, x1.w * 0.125f);
                 }
             }
         }
         const uint8_t *kb = pages + (size_t)s * kAttnPageBytes + hd * (kPage * kHeadDim * 2) + ds * 16;
         const uint8_t *vb = kb + kHeads * kPage * kHeadDim * 2;
         for (int blk = 0; blk < 4; ++blk) {
-            int4 kr[4], vr[4];
+            float2 kf[4][4], vf[4][4];
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
-                kr[u] = *reinterpret_cast<const int4 *>(kb + (4 * blk + u) * 128);
-                vr[u] = *reinterpret_cast<const int4 *>(vb + (4 * blk + u) * 128);
+                int4 kr = *reinterpret_cast<const int4 *>(kb + (4 * blk + u) * 128);
+                int4 vr = *reinterpret_cast<const int4 *>(vb + (4 * blk + u) * 128);
+                if (st.pb + 4 * blk + u >= st.p1) vr = make_int4(0, 0, 0, 0);  // past the chunk: stale bits
+                const __half2 *kh = reinterpret_cast<const __half2 *>(&kr);
+                const __half2 *vh = reinterpret_cast<const __half2 *>(&vr);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    kf[u][e] = __half22float2(kh[e]);
+                    vf[u][e] = __half22float2(vh[e]);
+                }
             }
             if (blk == 3) {
                 __syncwarp();
@@ -946,15 +959,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_prefill(const PfArgs a
                 float sc[4];
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
-                    const __half2 *kh = reinterpret_cast<const __half2 *>(&kr[u]);
-                    float dd = 0.f;
+                    float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const float2 kf = __half22float2(kh[e]);
-                        dd = fmaf(qv[i][2 * e], kf.x, dd);
-                        dd = fmaf(qv[i][2 * e + 1], kf.y, dd);
-                    }
-                    sc[u] = dd;
+                    for (int e = 0; e < 4; ++e) acc = __ffma2_rn(qv[i][e], kf[u][e], acc);
+                    sc[u] = acc.x + acc.y;
                 }
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
@@ -968,22 +976,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_prefill(const PfArgs a
                     const float corr = __expf(m[i] - mn);
                     float pw[4];
 #pragma unroll
-                    for (int u = 0; u < 4; ++u) pw[u] = __expf(sc[u] - mn);
+                    for (int u = 0; u < 4; ++u) pw[u] = __expf(sc[u] - mn);  // 0 for masked positions
                     l[i] = l[i] * corr + ((pw[0] + pw[1]) + (pw[2] + pw[3]));
+                    const float2 c2 = make_float2(corr, corr);
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) o[i][e] *= corr;
+                    for (int e = 0; e < 4; ++e) o[i][e] = __fmul2_rn(o[i][e], c2);
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
-                        // masked positions have pw = 0, but their V may hold stale bits (NaN):
-                        // skip them instead of multiplying
-                        if (pw[u] == 0.f) continue;
-                        const __half2 *vh = reinterpret_cast<const __half2 *>(&vr[u]);
+                        const float2 p2 = make_float2(pw[u], pw[u]);
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const float2 vf = __half22float2(vh[e]);
-                            o[i][2 * e] = fmaf(pw[u], vf.x, o[i][2 * e]);
-                            o[i][2 * e + 1] = fmaf(pw[u], vf.y, o[i][2 * e + 1]);
-                        }
+                        for (int e = 0; e < 4; ++e) o[i][e] = __ffma2_rn(p2, vf[u][e], o[i][e]);
                     }
                     m[i] = mn;
                 }
@@ -998,21 +1000,24 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_prefill(const PfArgs a
                 const int r = st.row0 + gi;
                 if (st.flags & 8) {
                     float *pp = a.part + ((size_t)(a.plan[2 + r] + st.c) * kHeads + hd) * kPartStride;
-                    reinterpret_cast<float4 *>(pp + 4 + ds * 8)[0] = make_float4(o[i][0], o[i][1], o[i][2], o[i][3]);
-                    reinterpret_cast<float4 *>(pp + 4 + ds * 8)[1] = make_float4(o[i][4], o[i][5], o[i][6], o[i][7]);
+                    reinterpret_cast<float4 *>(pp + 4 + ds * 8)[0] = make_float4(o[i][0].x, o[i][0].y, o[i][1].x, o[i][1].y);
+                    reinterpret_cast<float4 *>(pp + 4 + ds * 8)[1] = make_float4(o[i][2].x, o[i][2].y, o[i][3].x, o[i][3].y);
                     if (ds == 0) *reinterpret_cast<float2 *>(pp) = make_float2(m[i], l[i]);
                 } else {
                     const float inv = 1.f / l[i];
                     float y[8];
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) y[j] = o[i][j] * inv;
+                    for (int j = 0; j < 4; ++j) {
+                        y[2 * j] = o[i][j].x * inv;
+                        y[2 * j + 1] = o[i][j].y * inv;
+                    }
                     pf_store8(a, r, hd * kHeadDim + ds * 8, y);
                 }
             }
             m[i] = -INFINITY;
             l[i] = 0.f;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) o[i][j] = 0.f;
+            for (int j = 0; j < 4; ++j) o[i][j] = make_float2(0.f, 0.f);
         }
     }
 }
