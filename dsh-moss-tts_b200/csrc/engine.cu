@@ -402,7 +402,6 @@ void Engine::set_smem_limits() {
     set_tc_attr<TC_QKV>();
     set_tc_attr<TC_RESID>();
     set_tc_attr<TC_GELU_B>();
-    CK(cudaFuncSetAttribute(k_build_bimg, cudaFuncAttributeMaxDynamicSharedMemorySize, kFF * 4));
 }
 
 void Engine::set_gemm_path(int mode) {
@@ -490,7 +489,7 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
     const bool direct = !local && tc_direct_min_rows_ > 0 && N >= tc_direct_min_rows_;
     const float *add1 = pending_resid_;
     pending_resid_ = nullptr;
-    launch_k(pdl_, k_build_bimg, dim3(N), dim3(256), kHidden * 4, stream_, x, kHidden, R, N, kHidden, L.ln1_w, L.ln1_b,
+    launch_k(pdl_, k_build_bimg, dim3((N + 7) / 8), dim3(256), 0, stream_, x, kHidden, R, N, L.ln1_w, L.ln1_b,
              tc_parts(prec), bimg_a_, add1);
     mark(KK_BIMG);
     TcArgs a{};
@@ -597,7 +596,7 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
     else
         launch_tc<TC_RESID>(p, prec, stream_, pdl_, tc_direct_min_rows_, tc_direct_rows_);
     mark(local ? KK_PROJ_L : KK_PROJ_G);
-    launch_k(pdl_, k_build_bimg, dim3(N), dim3(256), kHidden * 4, stream_, x, kHidden, R, N, kHidden, L.ln2_w, L.ln2_b,
+    launch_k(pdl_, k_build_bimg, dim3((N + 7) / 8), dim3(256), 0, stream_, x, kHidden, R, N, L.ln2_w, L.ln2_b,
              tc_parts(prec), bimg_a_, direct ? static_cast<const float *>(attn_) : nullptr);
     mark(KK_BIMG);
     TcArgs f{};
@@ -639,7 +638,7 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
 void Engine::heads_tc(int ch, int R) {
     const int N = (R + 15) / 16 * 16;
     const int prec = gemm_path_ == 3 ? TC_F16 : TC_F16X3;
-    launch_k(pdl_, k_build_bimg, dim3(N), dim3(256), kHidden * 4, stream_, lx_, kHidden, R, N, kHidden, llnf_w_, llnf_b_,
+    launch_k(pdl_, k_build_bimg, dim3((N + 7) / 8), dim3(256), 0, stream_, lx_, kHidden, R, N, llnf_w_, llnf_b_,
              tc_parts(prec), bimg_a_, static_cast<const float *>(nullptr));
     mark(KK_BIMG);
     TcArgs h{};

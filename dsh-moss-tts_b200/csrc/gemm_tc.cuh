@@ -772,79 +772,85 @@ __global__ void __launch_bounds__(kTpThreads, 1) k_gemm_tp(const TcArgs a) {
     }
 }
 
-// x fp32 [R][K] (optionally LayerNormed, K = 768) -> activation image with N padded rows;
-// rows R..N-1 are written as zeros.  parts = 2 also writes the image of the fp16 remainders
+// x fp32 [R][768] (optionally LayerNormed) -> activation image with N padded rows; rows
+// R..N-1 are written as zeros.  parts = 2 also writes the image of the fp16 remainders
 // (x - fp16(x)) right after the first one.  add != null: first the residual add x += add
-// (written back to x; the preceding GEMM stored its output, bias included, in add).  One CTA
-// per padded row.
-__global__ void __launch_bounds__(256) k_build_bimg(float *__restrict__ x, int ldx, int R, int N, int K,
+// (written back to x; the preceding GEMM stored its output, bias included, in add).  One
+// warp per row: lane l holds the 8-element units l, l + 32, l + 64 of the row (one 16-byte
+// unit of the image each), the LayerNorm statistics are warp reductions.
+constexpr int kBimgUnits = kHidden / 256;  // 8-element units per lane
+__global__ void __launch_bounds__(256) k_build_bimg(float *__restrict__ x, int ldx, int R, int N,
                                                     const float *__restrict__ ln_w, const float *__restrict__ ln_b,
                                                     int parts, uint8_t *__restrict__ bimg,
                                                     const float *__restrict__ add) {
-    extern __shared__ __align__(16) float xs_b[];
     pdl_enter();
-    const int n = blockIdx.x;
-    const size_t part = (size_t)K * N * 2;
+    const int lane = threadIdx.x & 31;
+    const int n = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (n >= N) return;
+    const size_t part = (size_t)kHidden * N * 2;
     if (n >= R) {
-        for (int k = threadIdx.x * 8; k < K; k += blockDim.x * 8)
+#pragma unroll
+        for (int j = 0; j < kBimgUnits; ++j)
             for (int p = 0; p < parts; ++p)
-                *reinterpret_cast<int4 *>(bimg + p * part + bimg_off(n, k, N)) = make_int4(0, 0, 0, 0);
+                *reinterpret_cast<int4 *>(bimg + p * part + bimg_off(n, 8 * (lane + 32 * j), N)) = make_int4(0, 0, 0, 0);
         return;
     }
-    if (add) {
-        for (int k = threadIdx.x; k < K; k += blockDim.x) {
-            const float v = __fadd_rn(x[(size_t)n * ldx + k], add[(size_t)n * ldx + k]);
-            x[(size_t)n * ldx + k] = v;
-            xs_b[k] = v;
+    float v[kBimgUnits][8];
+#pragma unroll
+    for (int j = 0; j < kBimgUnits; ++j) {
+        float4 *xp = reinterpret_cast<float4 *>(x + (size_t)n * ldx + 8 * (lane + 32 * j));
+        float4 a0 = xp[0], a1 = xp[1];
+        if (add) {
+            const float4 *ap = reinterpret_cast<const float4 *>(add + (size_t)n * ldx + 8 * (lane + 32 * j));
+            const float4 b0 = ap[0], b1 = ap[1];
+            a0 = make_float4(__fadd_rn(a0.x, b0.x), __fadd_rn(a0.y, b0.y), __fadd_rn(a0.z, b0.z), __fadd_rn(a0.w, b0.w));
+            a1 = make_float4(__fadd_rn(a1.x, b1.x), __fadd_rn(a1.y, b1.y), __fadd_rn(a1.z, b1.z), __fadd_rn(a1.w, b1.w));
+            xp[0] = a0;
+            xp[1] = a1;
         }
-    } else {
-        for (int k = threadIdx.x; k < K; k += blockDim.x) xs_b[k] = x[(size_t)n * ldx + k];
+        v[j][0] = a0.x; v[j][1] = a0.y; v[j][2] = a0.z; v[j][3] = a0.w;
+        v[j][4] = a1.x; v[j][5] = a1.y; v[j][6] = a1.z; v[j][7] = a1.w;
     }
-    __syncthreads();
-    if (ln_w) {  // LayerNorm (llm.cpp:159-171) with CTA-wide reductions, K = 768
-        __shared__ float red[8];
-        __shared__ float stat[2];
-        float s = 0.f;
-        for (int k = threadIdx.x; k < kHidden; k += blockDim.x) s += xs_b[k];
-        s = warp_sum(s);
-        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            float t = 0.f;
-            for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
-            stat[0] = __fdiv_rn(t, (float)kHidden);
+    if (ln_w) {  // LayerNorm (llm.cpp:159-171)
+        float sum = 0.f;
+#pragma unroll
+        for (int j = 0; j < kBimgUnits; ++j)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) sum += v[j][e];
+        const float mean = __fdiv_rn(warp_sum(sum), (float)kHidden);
+        float var = 0.f;
+#pragma unroll
+        for (int j = 0; j < kBimgUnits; ++j)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const float d = v[j][e] - mean;
+                var = fmaf(d, d, var);
+            }
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(warp_sum(var), (float)kHidden) + 1e-5f));
+#pragma unroll
+        for (int j = 0; j < kBimgUnits; ++j) {
+            const int k0 = 8 * (lane + 32 * j);
+            const float4 w0 = *reinterpret_cast<const float4 *>(ln_w + k0), w1 = *reinterpret_cast<const float4 *>(ln_w + k0 + 4);
+            const float4 c0 = *reinterpret_cast<const float4 *>(ln_b + k0), c1 = *reinterpret_cast<const float4 *>(ln_b + k0 + 4);
+            const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+            const float bv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+                v[j][e] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[j][e], mean), inv), wv[e]), bv[e]);
         }
-        __syncthreads();
-        const float mean = stat[0];
-        float v = 0.f;
-        for (int k = threadIdx.x; k < kHidden; k += blockDim.x) {
-            const float d = xs_b[k] - mean;
-            v = fmaf(d, d, v);
-        }
-        v = warp_sum(v);
-        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            float t = 0.f;
-            for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
-            stat[1] = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(t, (float)kHidden) + 1e-5f));
-        }
-        __syncthreads();
-        const float inv = stat[1];
-        for (int k = threadIdx.x; k < kHidden; k += blockDim.x)
-            xs_b[k] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xs_b[k], mean), inv), ln_w[k]), ln_b[k]);
-        __syncthreads();
     }
-    for (int k = threadIdx.x * 8; k < K; k += blockDim.x * 8) {
+#pragma unroll
+    for (int j = 0; j < kBimgUnits; ++j) {
         __align__(16) __half h[8];
         __align__(16) __half l[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-            h[e] = __float2half_rn(xs_b[k + e]);
-            l[e] = __float2half_rn(xs_b[k + e] - __half2float(h[e]));
+            h[e] = __float2half_rn(v[j][e]);
+            l[e] = __float2half_rn(v[j][e] - __half2float(h[e]));
         }
-        *reinterpret_cast<int4 *>(bimg + bimg_off(n, k, N)) = *reinterpret_cast<const int4 *>(h);
-        if (parts == 2) *reinterpret_cast<int4 *>(bimg + part + bimg_off(n, k, N)) = *reinterpret_cast<const int4 *>(l);
+        const size_t off = bimg_off(n, 8 * (lane + 32 * j), N);
+        *reinterpret_cast<int4 *>(bimg + off) = *reinterpret_cast<const int4 *>(h);
+        if (parts == 2) *reinterpret_cast<int4 *>(bimg + part + off) = *reinterpret_cast<const int4 *>(l);
     }
 }
 
