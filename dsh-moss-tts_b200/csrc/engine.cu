@@ -18,6 +18,7 @@
 
 #include "kernels.cuh"
 #include "gemm_tc.cuh"
+#include "attn_tc.cuh"
 
 namespace mossgpu {
 
@@ -212,15 +213,13 @@ void Engine::allocate_state() {
     part_ = dalloc<float>(size_t(attn_items_) * kPartStride, owned_);
     desc_ = dalloc<int4>(attn_items_ / kHeads, owned_);
     work_ = dalloc<int>(kLayers, owned_);  // per-layer chunk counters of the decode attention
-    // flash-prefill items: at most one group per row, each cut into chunks of >= 32 pages
-    pf_cap_items_ = size_t(r_max_) * size_t((max_ctx_ + kPfMinChunkPos - 1) / kPfMinChunkPos) + 1;
-    pf_items_ = dalloc<int4>(2 * pf_cap_items_, owned_);
+    // flash-prefill tiles: at most one per row
+    pf_items_ = dalloc<int4>(size_t(r_max_), owned_);
     {
         void *hp = nullptr;
-        CK(cudaMallocHost(&hp, 2 * pf_cap_items_ * sizeof(int4) + size_t(r_max_ + 3) * sizeof(int)));
+        CK(cudaMallocHost(&hp, size_t(r_max_) * sizeof(int4)));
         pinned_.push_back(hp);
         h_pf_items_ = static_cast<int4 *>(hp);
-        h_pf_plan_ = reinterpret_cast<int *>(h_pf_items_ + 2 * pf_cap_items_);
     }
     CK(cudaMemset(work_, 0, kLayers * sizeof(int)));
     active_ = dalloc<int>(R, owned_);
@@ -393,7 +392,7 @@ void set_tc_attr() {
 
 void Engine::set_smem_limits() {
     CK(cudaFuncSetAttribute(k_attn_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem));
-    CK(cudaFuncSetAttribute(k_attn_prefill, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmem));
+    CK(cudaFuncSetAttribute(k_attn_prefill_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kPtSmem));
     set_attr_all<PRO_LN, EPI_QKV>();
     set_attr_all<PRO_NONE, EPI_RESID>();
     set_attr_all<PRO_LN, EPI_GELU>();
@@ -552,26 +551,18 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
         t.work = work_ + li;
         t.err = dev_err_;
         if (pf_active_) {
-            PfArgs f{};
+            PtArgs f{};
             f.q = q_;
             f.kv = t.kv;
             f.page_table = page_table_;
+            f.pages_per_stream = pages_per_stream_;
             f.items = pf_items_;
-            f.n_items = plan_;
-            f.plan = plan_;
-            f.part = part_;
-            f.work = work_ + li;
             f.bimg = bimg_a_;
             f.bimg_N = N;
             f.bimg_parts = tc_parts(prec);
-            f.out = attn_;
             f.err = dev_err_;
-            launch_k(pdl_, k_attn_prefill, dim3(kAttnGrid), dim3(kAttnThreads), kPfSmem, stream_, f);
+            launch_k(pdl_, k_attn_prefill_tc, dim3(unsigned(pf_tc_items_), kHeads), dim3(kPtThreads), kPtSmem, stream_, f);
             mark(KK_ATTN_PREFILL);
-            if (pf_split_) {
-                launch_k(pdl_, k_attn_combine, dim3((R * kHeads + 7) / 8), dim3(256), 0, stream_, t);
-                mark(KK_ATTN_COMBINE);
-            }
         } else {
             launch_k(pdl_, k_attn_decode, dim3(kAttnGrid), dim3(kAttnThreads), kAttnSmem, stream_, t);
             mark(KK_ATTN_DECODE);
@@ -934,70 +925,20 @@ int Engine::position(int sid) const {
 }
 
 // The flash-prefill work list of a pass whose row k has slot[k] and position pos[k]: runs of
-// consecutive positions of one stream are cut into groups of kPfGroup rows; a group attends to
-// positions [0, last + 1), cut into chunks of the same length (a power-of-two multiple of
-// kPfMinChunkPos, the smallest whose partial results fit the partial buffer).  A group with
-// several chunks writes partials for its rows (plan[2 + r] = row r's first, k_attn_combine
-// merges them).  Items go longest first.  plan[0] = items, plan[1] = partials.
+// consecutive positions of one stream cut into tiles of <= 128 rows (k_attn_prefill_tc, one
+// CTA per tile and head), longest key range first.
 void Engine::plan_prefill_attention(int R, const int *slot, const int *pos) {
-    struct Group {
-        int row0, nrows, pos0, slot;
-    };
-    std::vector<Group> groups;
+    std::vector<int4> tiles;
     for (int k = 0; k < R;) {
         int n = 1;
-        while (k + n < R && n < kPfGroup && slot[k + n] == slot[k] && pos[k + n] == pos[k] + n) ++n;
-        groups.push_back({k, n, pos[k], slot[k]});
+        while (k + n < R && n < kPtRows && slot[k + n] == slot[k] && pos[k + n] == pos[k] + n) ++n;
+        tiles.push_back(make_int4(k, n, pos[k], slot[k]));
         k += n;
     }
-    const int cap_partials = attn_items_ / kHeads;
-    int chunk = kPfMinChunkPos;
-    for (;;) {
-        long long parts = 0, items = 0;
-        for (const Group &g : groups) {
-            const int end = g.pos0 + g.nrows;
-            const int nch = (end + chunk - 1) / chunk;
-            items += nch;
-            if (nch > 1) parts += (long long)nch * g.nrows;
-        }
-        if (parts <= cap_partials && items <= (long long)pf_cap_items_) break;
-        chunk *= 2;
-    }
-    struct Item {
-        int4 d0, d1;
-        int pages;
-    };
-    std::vector<Item> items;
-    int *plan = h_pf_plan_;
-    int nparts = 0;
-    pf_split_ = false;
-    for (const Group &g : groups) {
-        const int end = g.pos0 + g.nrows;
-        const int nch = (end + chunk - 1) / chunk;
-        const bool split = nch > 1;
-        pf_split_ = pf_split_ || split;
-        for (int i = 0; i < g.nrows; ++i) {
-            plan[2 + g.row0 + i] = nparts;
-            if (split) nparts += nch;
-        }
-        for (int c = 0; c < nch; ++c) {
-            const int p0 = c * chunk, p1 = std::min(end, p0 + chunk);
-            items.push_back({make_int4(g.row0, g.nrows, p0, p1),
-                             make_int4(g.slot * pages_per_stream_ + p0 / kPage, g.pos0, c, split ? 1 : 0),
-                             (p1 - p0 + kPage - 1) / kPage});
-        }
-    }
-    plan[0] = int(items.size());
-    plan[1] = nparts;
-    plan[2 + R] = nparts;
-    std::stable_sort(items.begin(), items.end(), [](const Item &a, const Item &b) { return a.pages > b.pages; });
-    for (size_t i = 0; i < items.size(); ++i) {
-        h_pf_items_[2 * i] = items[i].d0;
-        h_pf_items_[2 * i + 1] = items[i].d1;
-    }
-    CK(cudaMemcpyAsync(pf_items_, h_pf_items_, 2 * items.size() * sizeof(int4), cudaMemcpyHostToDevice, stream_));
-    CK(cudaMemcpyAsync(plan_, plan, size_t(R + 3) * sizeof(int), cudaMemcpyHostToDevice, stream_));
-    CK(cudaMemsetAsync(work_, 0, kLayers * sizeof(int), stream_));
+    std::stable_sort(tiles.begin(), tiles.end(), [](const int4 &a, const int4 &b) { return a.z + a.y > b.z + b.y; });
+    for (size_t i = 0; i < tiles.size(); ++i) h_pf_items_[i] = tiles[i];
+    pf_tc_items_ = int(tiles.size());
+    CK(cudaMemcpyAsync(pf_items_, h_pf_items_, tiles.size() * sizeof(int4), cudaMemcpyHostToDevice, stream_));
 }
 
 // LlmModel::prefill (llm.cpp:327-401) for several streams at once.  Each stream's rows are

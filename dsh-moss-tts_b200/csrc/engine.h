@@ -161,13 +161,12 @@ private:
     int device_ = 0;
     int max_streams_ = 0, max_ctx_ = 0, pages_per_stream_ = 0, n_pages_ = 0, r_max_ = 0;
     int tc_direct_min_rows_ = 512, tc_direct_rows_ = 256;
-    // flash-prefill plan of the current pass: items (2 x int4 each) on the device, with a
-    // pinned staging copy; active while a prefill pass runs on the tensor-core path
+    // flash-prefill tiles of the current pass (int4 each) on the device, with a pinned staging
+    // copy; active while a prefill pass runs on the tensor-core path
     int4 *pf_items_ = nullptr;
     int4 *h_pf_items_ = nullptr;
-    int *h_pf_plan_ = nullptr;
-    size_t pf_cap_items_ = 0;
-    bool pf_active_ = false, pf_split_ = false;
+    bool pf_active_ = false;
+    int pf_tc_items_ = 0;
     // a direct-form fc_out stored its output here; the next layer's LN1 kernel adds it to x
     const float *pending_resid_ = nullptr;
     cudaStream_t stream_ = nullptr, own_stream_ = nullptr;

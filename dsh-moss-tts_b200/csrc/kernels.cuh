@@ -766,262 +766,6 @@ __global__ void __launch_bounds__(256) k_attn_combine(const AttnArgs a) {
     }
 }
 
-// Causal flash-prefill over fp16 pages (LlmModel::prefill's attention, llm.cpp:360-384): the
-// rows of a prefill pass are runs of consecutive positions of one stream, so a group of up
-// to kPfGroup such rows shares every page it attends to.  A work item is (group, chunk of
-// pages); the host lists the items (longest first) with the partial-result layout, and a
-// producer warp claims them from an atomic counter and streams each chunk's 48 KB pages --
-// and, with the first page, the group's query rows -- into a 3-stage ring.  Consumer warp h
-// handles head h for the whole group: lane (rg, ds) keeps rows rg and rg + 4 of the group
-// (8 dims each, query and output in registers), takes the page's positions 4 at a time,
-// reduces the 64-dim scores over the 8 ds lanes and runs the online softmax in fp32.  A
-// group with one chunk writes its rows' outputs; otherwise each chunk writes per-row partials
-// that k_attn_combine merges (row r's partials start at plan[2 + r]).  Rows attend to their
-// own positions and below: row pos0 + g sees positions < min(chunk end, pos0 + g + 1).
-constexpr int kPfGroup = 8;                                 // rows per group
-constexpr int kPfMinChunkPos = 512;                         // shortest chunk (positions)
-constexpr int kPfStages = 3;
-constexpr int kPfQBytes = kPfGroup * kHidden * 4;           // the group's query rows, fp32
-constexpr int kPfSmem = kPfStages * (kAttnPageBytes + kPfQBytes) + 1024;  // 222,208
-
-struct PfStage {
-    int row0, nrows, pos0;  // the group: rows row0.., positions pos0..
-    int pb, p1;             // first position of the page, end of the chunk (exclusive)
-    int flags;              // 1: first page of the item, 2: last page, 4: no more work, 8: split
-    int c;                  // chunk index of the item within its rows' partials
-    int pad;
-};
-
-// item = {row0, nrows, p0, p1} {page-table offset of page p0 / 16, pos0, chunk index, split}
-struct PfArgs {
-    const float *q;
-    const __half *kv;
-    const int *page_table;
-    const int4 *items;      // 2 x int4 per item
-    const int *n_items;
-    const int *plan;        // plan[2 + r]: first partial of row r (split rows)
-    float *part;
-    int *work;              // zeroed before the launch
-    uint8_t *bimg;          // output image (tensor-core path) or null: `out`
-    int bimg_N, bimg_parts;
-    float *out;
-    int *err;
-};
-
-__device__ __forceinline__ void pf_store8(const PfArgs &a, int r, int k0, const float *y) {
-    AttnArgs t{};
-    t.bimg = a.bimg;
-    t.bimg_N = a.bimg_N;
-    t.bimg_parts = a.bimg_parts;
-    t.out = a.out;
-    attn_store8(t, r, k0, y);
-}
-
-__global__ void __launch_bounds__(kAttnThreads, 1) k_attn_prefill(const PfArgs a) {
-    extern __shared__ __align__(128) uint8_t pf_smem[];
-    uint8_t *pages = pf_smem;                                                         // [stage][49152]
-    float *qs = reinterpret_cast<float *>(pf_smem + kPfStages * kAttnPageBytes);      // [stage][8][768]
-    PfStage *meta = reinterpret_cast<PfStage *>(pf_smem + kPfStages * (kAttnPageBytes + kPfQBytes));
-    uint64_t *full = reinterpret_cast<uint64_t *>(meta + kPfStages);
-    uint64_t *empty = full + kPfStages;
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < kPfStages; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kAttnConsumers);
-        }
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    __syncthreads();
-    pdl_enter();
-    const int total = *a.n_items;
-
-    if (wid == kAttnConsumers) {
-        // ------------------------------------------------------------------ producer warp
-        int seq = 0;
-        bool ok = true;
-        int g = 0;
-        if (lane == 0) g = atomicAdd(a.work, 1);
-        g = __shfl_sync(0xffffffffu, g, 0);
-        for (;;) {
-            const bool stop = g >= total;
-            int gn = 0;
-            if (!stop && lane == 0) gn = atomicAdd(a.work, 1);
-            const int4 d0 = stop ? make_int4(0, 0, 0, 0) : a.items[2 * g];
-            const int4 d1 = stop ? make_int4(0, 0, 0, 0) : a.items[2 * g + 1];
-            const int npg = stop ? 1 : (d0.w - d0.z + kPage - 1) / kPage;
-            for (int jb = 0; jb < npg && ok; jb += 32) {
-                const int pid = (!stop && jb + lane < npg) ? a.page_table[d1.x + jb + lane] : 0;
-                const int jend = min(npg, jb + 32);
-                for (int j = jb; j < jend; ++j) {
-                    const int page = __shfl_sync(0xffffffffu, pid, j - jb);
-                    if (lane == 0) {
-                        const int s = seq % kPfStages;
-                        if (!mbar_wait(&empty[s], ((seq / kPfStages) & 1) ^ 1, a.err, 9)) {
-                            ok = false;
-                        } else {
-                            PfStage &m = meta[s];
-                            m.row0 = d0.x;
-                            m.nrows = d0.y;
-                            m.pos0 = d1.y;
-                            m.pb = d0.z + j * kPage;
-                            m.p1 = d0.w;
-                            m.flags = stop ? 4 : ((j == 0 ? 1 : 0) | (j == npg - 1 ? 2 : 0) | (d1.w ? 8 : 0));
-                            m.c = d1.z;
-                            if (stop) {
-                                mbar_arrive(&full[s]);
-                            } else {
-                                const uint32_t qb = j == 0 ? (uint32_t)d0.y * kHidden * 4 : 0u;
-                                mbar_expect_tx(&full[s], kAttnPageBytes + qb);
-                                bulk_g2s(pages + (size_t)s * kAttnPageBytes, a.kv + (size_t)page * kPageHalfs,
-                                         kAttnPageBytes, &full[s]);
-                                if (qb) bulk_g2s(qs + (size_t)s * kPfGroup * kHidden, a.q + (size_t)d0.x * kHidden, qb, &full[s]);
-                            }
-                        }
-                    }
-                    ok = __shfl_sync(0xffffffffu, ok, 0);
-                    ++seq;
-                    if (!ok) break;
-                }
-            }
-            if (stop || !ok) break;
-            g = __shfl_sync(0xffffffffu, gn, 0);
-        }
-        if (!ok && lane == 0) {
-            for (int k = max(0, seq - kPfStages); k < seq - 1; ++k)
-                mbar_wait(&full[k % kPfStages], (k / kPfStages) & 1, nullptr, 0);
-        }
-        return;
-    }
-
-    // ---------------------------------------------------------------------- consumer warps
-    // Packed fp32 pairs (fma.rn.f32x2) halve the FMA instructions: a lane's 8-dim dot product
-    // accumulates even and odd dims separately, then adds the two.
-    const int hd = wid;
-    const int rg = lane >> 3, ds = lane & 7;
-    float2 qv[2][4], o[2][4];
-    float m[2], l[2];
-    int lim[2];
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-        m[i] = -INFINITY;
-        l[i] = 0.f;
-        lim[i] = 0;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) o[i][j] = make_float2(0.f, 0.f), qv[i][j] = make_float2(0.f, 0.f);
-    }
-    for (int seq = 0;; ++seq) {
-        const int s = seq % kPfStages;
-        if (!mbar_wait(&full[s], (seq / kPfStages) & 1, a.err, 10)) return;
-        const PfStage st = meta[s];
-        if (st.flags & 4) break;
-        if (st.flags & 1) {
-#pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                const int gi = rg + 4 * i;
-                // rows past the group attend to nothing (their lanes still take part in the
-                // shuffles)
-                lim[i] = gi < st.nrows ? min(st.p1, st.pos0 + gi + 1) : 0;
-                if (gi < st.nrows) {
-                    const float4 *qp = reinterpret_cast<const float4 *>(qs + ((size_t)s * kPfGroup + gi) * kHidden +
-                                                                        hd * kHeadDim + ds * 8);
-                    const float4 x0 = qp[0], x1 = qp[1];
-                    qv[i][0] = make_float2(x0.x * 0.125f, x0.y * 0.125f);
-                    qv[i][1] = make_float2(x0.z * 0.125f, x0.w * 0.125f);
-                    qv[i][2] = make_float2(x1.x * 0.125f, x1.y * 0.125f);
-                    qv[i][3] = make_float2(x1.z * 0.125f, x1.w * 0.125f);
-                }
-            }
-        }
-        const uint8_t *kb = pages + (size_t)s * kAttnPageBytes + hd * (kPage * kHeadDim * 2) + ds * 16;
-        const uint8_t *vb = kb + kHeads * kPage * kHeadDim * 2;
-        for (int blk = 0; blk < 4; ++blk) {
-            float2 kf[4][4], vf[4][4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                int4 kr = *reinterpret_cast<const int4 *>(kb + (4 * blk + u) * 128);
-                int4 vr = *reinterpret_cast<const int4 *>(vb + (4 * blk + u) * 128);
-                if (st.pb + 4 * blk + u >= st.p1) vr = make_int4(0, 0, 0, 0);  // past the chunk: stale bits
-                const __half2 *kh = reinterpret_cast<const __half2 *>(&kr);
-                const __half2 *vh = reinterpret_cast<const __half2 *>(&vr);
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    kf[u][e] = __half22float2(kh[e]);
-                    vf[u][e] = __half22float2(vh[e]);
-                }
-            }
-            if (blk == 3) {
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[s]);  // the page's data of this head is in registers
-            }
-#pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                float sc[4];
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    float2 acc = make_float2(0.f, 0.f);
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) acc = __ffma2_rn(qv[i][e], kf[u][e], acc);
-                    sc[u] = acc.x + acc.y;
-                }
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], 1);
-                    sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], 2);
-                    sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], 4);
-                    if (st.pb + 4 * blk + u >= lim[i]) sc[u] = -INFINITY;
-                }
-                const float mn = fmaxf(fmaxf(m[i], fmaxf(sc[0], sc[1])), fmaxf(sc[2], sc[3]));
-                if (mn != -INFINITY) {
-                    const float corr = __expf(m[i] - mn);
-                    float pw[4];
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) pw[u] = __expf(sc[u] - mn);  // 0 for masked positions
-                    l[i] = l[i] * corr + ((pw[0] + pw[1]) + (pw[2] + pw[3]));
-                    const float2 c2 = make_float2(corr, corr);
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) o[i][e] = __fmul2_rn(o[i][e], c2);
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const float2 p2 = make_float2(pw[u], pw[u]);
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) o[i][e] = __ffma2_rn(p2, vf[u][e], o[i][e]);
-                    }
-                    m[i] = mn;
-                }
-            }
-        }
-        if (!(st.flags & 2)) continue;
-        // ---- end of the item: each lane holds 8 dims of its two rows
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            const int gi = rg + 4 * i;
-            if (gi < st.nrows) {
-                const int r = st.row0 + gi;
-                if (st.flags & 8) {
-                    float *pp = a.part + ((size_t)(a.plan[2 + r] + st.c) * kHeads + hd) * kPartStride;
-                    reinterpret_cast<float4 *>(pp + 4 + ds * 8)[0] = make_float4(o[i][0].x, o[i][0].y, o[i][1].x, o[i][1].y);
-                    reinterpret_cast<float4 *>(pp + 4 + ds * 8)[1] = make_float4(o[i][2].x, o[i][2].y, o[i][3].x, o[i][3].y);
-                    if (ds == 0) *reinterpret_cast<float2 *>(pp) = make_float2(m[i], l[i]);
-                } else {
-                    const float inv = 1.f / l[i];
-                    float y[8];
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        y[2 * j] = o[i][j].x * inv;
-                        y[2 * j + 1] = o[i][j].y * inv;
-                    }
-                    pf_store8(a, r, hd * kHeadDim + ds * 8, y);
-                }
-            }
-            m[i] = -INFINITY;
-            l[i] = 0.f;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) o[i][j] = make_float2(0.f, 0.f);
-        }
-    }
-}
-
 // Local decoder attention: n = lpos + 1 <= 17 positions of fp32 local KV.
 // One warp per (row, head); scores in llm.cpp:189-217 order per position.  With bimg set the
 // output goes straight into the next tensor-core GEMM's activation image (N rows, parts).
