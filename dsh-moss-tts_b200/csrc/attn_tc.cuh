@@ -14,9 +14,10 @@
 //   - O_blk = P V: 8 tcgen05.mma with V as an MN-major B operand (the same position-major rows),
 //     into a second TMEM region; each thread rescales its register accumulator o[64] and adds
 //     its row of O_blk.
-// The output o / l goes into the next GEMM's activation image (hi and lo parts).  The block
-// loop is serial (copy -> MMA -> softmax -> MMA); two CTAs share an SM (96 KB of shared memory
-// and 128 TMEM columns each), so one CTA's copies overlap the other's math.  Every mbarrier
+// The output o / l goes into the next GEMM's activation image (hi and lo parts).  K and V blocks
+// are double-buffered: the asynchronous copies (cp.async, 16 B each, into the swizzled rows) of
+// block b + 1 run while block b's MMAs and softmax do.  Two CTAs share an SM (~97 KB of shared
+// memory and 128 TMEM columns each).  Every mbarrier
 // wait is bounded; a time-out records an error code and the CTA leaves through the normal exit.
 #pragma once
 
@@ -30,7 +31,7 @@ constexpr int kPtBlk = 64;                        // key positions per block
 constexpr int kPtThreads = 128;
 constexpr int kPtTile = kPtRows * 128;            // a 128-row x 128-byte operand tile (16 KB)
 constexpr int kPtKvTile = kPtBlk * 128;           // a 64-row x 128-byte K or V block (8 KB)
-constexpr int kPtSmem = 4 * kPtTile + 2 * kPtKvTile + 1024;  // Q hi/lo, P hi/lo, K, V (+align)
+constexpr int kPtSmem = 4 * kPtTile + 4 * kPtKvTile + 1024;  // Q hi/lo, P hi/lo, 2 x (K, V) (+align)
 
 // item = {first row, rows (<= 128), position of the first row, stream slot}
 struct PtArgs {
@@ -78,7 +79,7 @@ __global__ void __launch_bounds__(kPtThreads, 2) k_attn_prefill_tc(const PtArgs 
     __shared__ uint32_t tmem_sh;
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(pt_smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *q_hi = smem, *q_lo = smem + kPtTile, *p_hi = smem + 2 * kPtTile, *p_lo = smem + 3 * kPtTile;
-    uint8_t *kt = smem + 4 * kPtTile, *vt = kt + kPtKvTile;
+    uint8_t *kv_buf = smem + 4 * kPtTile;  // [2][K block, V block]
     const int tid = threadIdx.x, warp = tid >> 5;
     const int hd = blockIdx.y;
     const int4 it = a.items[blockIdx.x];
@@ -141,23 +142,38 @@ __global__ void __launch_bounds__(kPtThreads, 2) k_attn_prefill_tc(const PtArgs 
     bool ok = true;
     const __half *kbase = a.kv + (size_t)hd * kPage * kHeadDim;                    // K of head hd in a page
     const __half *vbase = a.kv + (size_t)(kHeads + hd) * kPage * kHeadDim;         // V of head hd
-    for (int b = 0; b < nblk && ok; ++b) {
-        // ---- K and V rows of positions 64 b .. 64 b + 63 -> swizzled 128-byte rows
+    // K and V rows of positions 64 b .. 64 b + 63 -> swizzled 128-byte rows of buffer b & 1
+    auto copy_block = [&](int b) {
+        uint8_t *kt = kv_buf + (b & 1) * 2 * kPtKvTile, *vt = kt + kPtKvTile;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
             const int j = tid + kPtThreads * k;   // 512 units of 16 B per block: row j / 8, unit j % 8
             const int r = j >> 3, u = j & 7;
             const int p = b * kPtBlk + r;
-            int4 kk = make_int4(0, 0, 0, 0), vv = make_int4(0, 0, 0, 0);
+            const uint32_t dk = smem_u32(kt + r * 128 + ((u ^ (r & 7)) << 4));
+            const uint32_t dv = smem_u32(vt + r * 128 + ((u ^ (r & 7)) << 4));
             if (p < end) {
                 const int page = a.page_table[(size_t)slot * a.pages_per_stream + p / kPage];
                 const size_t off = (size_t)page * kPageHalfs + (size_t)(p % kPage) * kHeadDim + u * 8;
-                kk = *reinterpret_cast<const int4 *>(kbase + off);
-                vv = *reinterpret_cast<const int4 *>(vbase + off);
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dk), "l"(kbase + off) : "memory");
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dv), "l"(vbase + off) : "memory");
+            } else {
+                asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(dk), "r"(0) : "memory");
+                asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(dv), "r"(0) : "memory");
             }
-            *reinterpret_cast<int4 *>(kt + r * 128 + ((u ^ (r & 7)) << 4)) = kk;
-            *reinterpret_cast<int4 *>(vt + r * 128 + ((u ^ (r & 7)) << 4)) = vv;
         }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    if (nblk > 0) copy_block(0);
+    for (int b = 0; b < nblk && ok; ++b) {
+        // buffer (b + 1) & 1 was read by block b - 1's MMAs, which have completed
+        if (b + 1 < nblk) {
+            copy_block(b + 1);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        uint8_t *kt = kv_buf + (b & 1) * 2 * kPtKvTile, *vt = kt + kPtKvTile;
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncthreads();
         // ---- S = (Q_hi + Q_lo) K^T
@@ -221,6 +237,7 @@ __global__ void __launch_bounds__(kPtThreads, 2) k_attn_prefill_tc(const PtArgs 
         for (int j = 0; j < 64; ++j) o[j] = fmaf(o[j], corr, s[j]);
         ok = __syncthreads_and(ok);  // K, V and P are free for the next block; a time-out stops all
     }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");  // no copy in flight past this point
     // ---- o / l -> the proj GEMM's activation image (row, dims 64 hd ..)
     if (tid < nrows && ok) {
         const float inv = 1.f / l;
