@@ -384,8 +384,15 @@ void set_tc_attr() {
     CK(cudaFuncSetAttribute(k_gemm_tc<EPI, TC_F16>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
     CK(cudaFuncSetAttribute(k_gemm_tc<EPI, TC_F16X3>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
     CK(cudaFuncSetAttribute(k_gemm_tc<EPI, TC_F16X3>, cudaFuncAttributeMaxDynamicSharedMemorySize, s3));
-    CK(cudaFuncSetAttribute(k_gemm_tp<EPI, TC_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, d1));
-    CK(cudaFuncSetAttribute(k_gemm_tp<EPI, TC_F16X3>, cudaFuncAttributeMaxDynamicSharedMemorySize, d3));
+    CK(cudaFuncSetAttribute(k_gemm_tp<EPI, TC_F16, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, d1));
+    CK(cudaFuncSetAttribute(k_gemm_tp<EPI, TC_F16X3, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, d3));
+    int m1 = 0, m3 = 0;
+    for (int n = 16; n <= 128; n += 16) {
+        m1 = std::max(m1, tc_smem_bytes_atm(n, TC_F16, tc_max_stages_atm(n, TC_F16)));
+        m3 = std::max(m3, tc_smem_bytes_atm(n, TC_F16X3, tc_max_stages_atm(n, TC_F16X3)));
+    }
+    CK(cudaFuncSetAttribute(k_gemm_tp<EPI, TC_F16, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, m1));
+    CK(cudaFuncSetAttribute(k_gemm_tp<EPI, TC_F16X3, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, m3));
 }
 
 }  // namespace
@@ -445,15 +452,18 @@ void launch_tc(TcArgs a, int prec, cudaStream_t st, bool pdl, int direct_min, in
         while (a.N % ns) ns -= 16;
         a.nsub = ns;
         a.csize = 1;
-        a.stages = tc_max_stages_direct(ns, prec);
-        // tile-persistent: at most one CTA per SM walks the (weight tile, slice) tiles
+        // tile-persistent: at most one CTA per SM walks the (weight tile, slice) tiles; slices
+        // of <= 128 rows keep A in tensor memory beside the two accumulators
         const dim3 grid(std::min(tiles * (a.N / ns), kNumSMs));
+        const bool atm = ns <= 128;
+        a.stages = atm ? tc_max_stages_atm(ns, prec) : tc_max_stages_direct(ns, prec);
+        const size_t smem = atm ? tc_smem_bytes_atm(ns, prec, a.stages) : tc_smem_bytes_direct(ns, prec, a.stages);
         if (prec == TC_F16X3)
-            launch_kc(pdl, 0, k_gemm_tp<EPI, TC_F16X3>, grid, dim3(kTpThreads), tc_smem_bytes_direct(ns, TC_F16X3, a.stages),
-                      st, a);
+            launch_kc(pdl, 0, atm ? k_gemm_tp<EPI, TC_F16X3, true> : k_gemm_tp<EPI, TC_F16X3, false>, grid,
+                      dim3(kTpThreads), smem, st, a);
         else
-            launch_kc(pdl, 0, k_gemm_tp<EPI, TC_F16>, grid, dim3(kTpThreads), tc_smem_bytes_direct(ns, TC_F16, a.stages), st,
-                      a);
+            launch_kc(pdl, 0, atm ? k_gemm_tp<EPI, TC_F16, true> : k_gemm_tp<EPI, TC_F16, false>, grid, dim3(kTpThreads),
+                      smem, st, a);
         return;
     }
     int nsub = std::min(a.N, kTcMaxNS);

@@ -95,6 +95,14 @@ __device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc), "r"(0), "r"(0), "r"(0), "r"(0));
 }
 
+// A operand from tensor memory (lane = row, two fp16 K elements per 32-bit column)
+__device__ __forceinline__ void tc_mma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(acc), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
 __device__ __forceinline__ void tc_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                  : "memory");
@@ -140,6 +148,21 @@ __host__ __device__ constexpr int tc_max_stages(int NS, int prec) {
     return ((227 * 1024 - 1024 - tc_recv_bytes(NS)) / tc_stage_bytes(NS, prec)) < 4
                ? ((227 * 1024 - 1024 - tc_recv_bytes(NS)) / tc_stage_bytes(NS, prec))
                : 4;
+}
+
+// stage of the A-in-TMEM form: [B parts][W8 8 KB][scales 512 B] (the A tile lives in TMEM)
+__host__ __device__ constexpr int tc_stage_bytes_atm(int N, int prec) {
+    return (N * 128 * tc_parts(prec) + 8192 + 512 + 1023) / 1024 * 1024;
+}
+__host__ __device__ constexpr int tc_smem_bytes_atm(int NS, int prec, int stages) {
+    return stages * tc_stage_bytes_atm(NS, prec) + 1024;
+}
+// stages of the A-in-TMEM form: shared memory, and 64 TMEM columns each beside 2 x NS
+// accumulator columns in 512
+__host__ __device__ constexpr int tc_max_stages_atm(int NS, int prec) {
+    return ((224 * 1024 - 1024) / tc_stage_bytes_atm(NS, prec)) < ((512 - 2 * NS) / 64)
+               ? (((224 * 1024 - 1024) / tc_stage_bytes_atm(NS, prec)) < 4 ? ((224 * 1024 - 1024) / tc_stage_bytes_atm(NS, prec)) : 4)
+               : (((512 - 2 * NS) / 64) < 4 ? ((512 - 2 * NS) / 64) : 4);
 }
 
 // direct form (one CTA per tile, accumulators read straight from TMEM): no receive buffer;
@@ -201,6 +224,39 @@ __device__ __forceinline__ void tc_dequant_piece(const int8_t *w8, const __half 
         *reinterpret_cast<int4 *>(arow + 16384 + (((2 * j) ^ (t & 7)) << 4)) = *reinterpret_cast<const int4 *>(l);
         *reinterpret_cast<int4 *>(arow + 16384 + (((2 * j + 1) ^ (t & 7)) << 4)) = *reinterpret_cast<const int4 *>(l + 4);
     }
+}
+
+// The same conversion into registers: 8 packed fp16 pairs (k = 16 j + 2 e, + 1) of hi and lo,
+// for tcgen05.st into an A tile in tensor memory (column 8 j + e of the row).
+template <int NP>
+__device__ __forceinline__ void tc_dequant_piece_regs(const int8_t *w8, const __half *sc, int t, int j, uint32_t *hi,
+                                                      uint32_t *lo) {
+    const int4 q = *reinterpret_cast<const int4 *>(w8 + ((j ^ ((t >> 1) & 3)) << 4));
+    const __half2 d2 = __half2half2(sc[j >> 1]);
+    const uint32_t words[4] = {(uint32_t)q.x ^ 0x80808080u, (uint32_t)q.y ^ 0x80808080u, (uint32_t)q.z ^ 0x80808080u,
+                               (uint32_t)q.w ^ 0x80808080u};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        const __half2 qq = i8x2_to_h2(words[e >> 1], (e & 1) ? 0x7362u : 0x5140u);
+        const __half2 h = __hmul2_rn(qq, d2);
+        hi[e] = *reinterpret_cast<const uint32_t *>(&h);
+        if (NP == 2) {
+            const __half2 l = __hfma2(qq, d2, __hneg2(h));
+            lo[e] = *reinterpret_cast<const uint32_t *>(&l);
+        }
+    }
+}
+
+// 32 consecutive 32-bit columns of this thread's TMEM lane
+__device__ __forceinline__ void tc_st32(uint32_t taddr, const uint32_t *r) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+        "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+        "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
 }
 
 // One element of the direct form's epilogue: weight row gm (this thread's TMEM lane), batch row
@@ -566,7 +622,10 @@ constexpr int kTpDqThreads = 128;
 constexpr int kTpEpiThreads = 256;
 constexpr int kTpThreads = 64 + kTpDqThreads + kTpEpiThreads;
 
-template <int EPI, int PREC>
+// ATM = true: the dequantised A tiles go to tensor memory (tcgen05.st, 64 columns per stage
+// beside the two accumulators) and the MMAs read A from there, which takes 48 KB of operand
+// reads and 32 KB of stores per K chunk off shared memory (the main loop's bound).
+template <int EPI, int PREC, bool ATM>
 __global__ void __launch_bounds__(kTpThreads, 1) k_gemm_tp(const TcArgs a) {
     extern __shared__ uint8_t tc_smem_raw[];
     __shared__ __align__(8) uint64_t full_bar[4], bfull_bar[4], dq_bar[4], empty_bar[4], accf_bar[2], acce_bar[2];
@@ -575,14 +634,15 @@ __global__ void __launch_bounds__(kTpThreads, 1) k_gemm_tp(const TcArgs a) {
     constexpr int NP = tc_parts(PREC);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int N = a.N, NS = a.nsub, S = a.stages;
-    const int SB = tc_stage_bytes(NS, PREC);
-    const int OFF_B = 16384 * NP;
+    const int SB = ATM ? tc_stage_bytes_atm(NS, PREC) : tc_stage_bytes(NS, PREC);
+    const int OFF_B = ATM ? 0 : 16384 * NP;
     const int OFF_W8 = OFF_B + NS * 128 * NP;
     const int OFF_SC = OFF_W8 + 8192;
     const size_t bimg_part = (size_t)a.K * N * 2;
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
     const int nchunks = a.K / kTcK;
     const int n_m = a.rows / kTcM;
+    const int acol0 = 2 * NS;  // ATM: A stage s at TMEM columns acol0 + 64 s (hi) and + 32 (lo)
     const int n_tiles = n_m * (N / NS);
     const int G = gridDim.x;
     const int my_tiles = (int)blockIdx.x < n_tiles ? (n_tiles - 1 - (int)blockIdx.x) / G + 1 : 0;
@@ -602,7 +662,7 @@ __global__ void __launch_bounds__(kTpThreads, 1) k_gemm_tp(const TcArgs a) {
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     uint32_t ncols = 32;
-    while (ncols < (uint32_t)(2 * NS)) ncols <<= 1;
+    while (ncols < (uint32_t)(2 * NS + (ATM ? 64 * S : 0))) ncols <<= 1;
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_sh)),
                      "r"(ncols));
@@ -681,12 +741,22 @@ __global__ void __launch_bounds__(kTpThreads, 1) k_gemm_tp(const TcArgs a) {
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                     uint8_t *st = smem + (size_t)s * SB;
                     const uint32_t abase = smem_u32(st), bbase = smem_u32(st + OFF_B);
+                    const uint32_t ahi = tmem + (uint32_t)(acol0 + 64 * s), alo = ahi + 32;  // ATM
 #pragma unroll
                     for (int k = 0; k < 4; ++k) {
-                        tc_mma(dcol, sw128_desc(abase + k * 32), sw128_desc(bbase + k * 32), idesc, (c > 0 || k > 0) ? 1u : 0u);
-                        if (NP == 2) {
-                            tc_mma(dcol, sw128_desc(abase + k * 32), sw128_desc(bbase + NS * 128 + k * 32), idesc, 1u);
-                            tc_mma(dcol, sw128_desc(abase + 16384 + k * 32), sw128_desc(bbase + k * 32), idesc, 1u);
+                        const uint32_t acc = (c > 0 || k > 0) ? 1u : 0u;
+                        if (ATM) {
+                            tc_mma_ts(dcol, ahi + 8 * k, sw128_desc(bbase + k * 32), idesc, acc);
+                            if (NP == 2) {
+                                tc_mma_ts(dcol, ahi + 8 * k, sw128_desc(bbase + NS * 128 + k * 32), idesc, 1u);
+                                tc_mma_ts(dcol, alo + 8 * k, sw128_desc(bbase + k * 32), idesc, 1u);
+                            }
+                        } else {
+                            tc_mma(dcol, sw128_desc(abase + k * 32), sw128_desc(bbase + k * 32), idesc, acc);
+                            if (NP == 2) {
+                                tc_mma(dcol, sw128_desc(abase + k * 32), sw128_desc(bbase + NS * 128 + k * 32), idesc, 1u);
+                                tc_mma(dcol, sw128_desc(abase + 16384 + k * 32), sw128_desc(bbase + k * 32), idesc, 1u);
+                            }
                         }
                     }
                     tc_commit(&empty_bar[s]);
@@ -695,18 +765,30 @@ __global__ void __launch_bounds__(kTpThreads, 1) k_gemm_tp(const TcArgs a) {
             }
         }
     } else if (warp < 2 + kTpDqThreads / 32) {
-        // ---------------- dequant: thread t converts weight row t of every chunk
-        const int t = threadIdx.x - 64;
+        // ---------------- dequant: thread t converts weight row t of every chunk (ATM: the row
+        // of this warp's TMEM lane quarter)
+        const int t = ATM ? ((warp & 3) * 32 + lane) : (int)threadIdx.x - 64;
         for (int i = 0; i < total; ++i) {
             const int s = i % S;
             if (!mbar_wait(&full_bar[s], (i / S) & 1, a.err, 15)) break;
             uint8_t *st = smem + (size_t)s * SB;
             const int8_t *w8 = reinterpret_cast<const int8_t *>(st + OFF_W8) + t * 64;
             const __half *sc = reinterpret_cast<const __half *>(st + OFF_SC) + t * 2;
-            uint8_t *arow = st + t * 128;
+            if (ATM) {
+                uint32_t hi[32], lo[32];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) tc_dequant_piece<NP>(w8, sc, arow, t, j);
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                for (int j = 0; j < 4; ++j) tc_dequant_piece_regs<NP>(w8, sc, t, j, hi + 8 * j, lo + 8 * j);
+                const uint32_t ta = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(acol0 + 64 * s);
+                tc_st32(ta, hi);
+                if (NP == 2) tc_st32(ta + 32, lo);
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            } else {
+                uint8_t *arow = st + t * 128;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) tc_dequant_piece<NP>(w8, sc, arow, t, j);
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            }
             mbar_arrive(&dq_bar[s]);
         }
     } else {
