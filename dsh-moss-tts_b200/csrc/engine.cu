@@ -454,7 +454,9 @@ void launch_tc(TcArgs a, int prec, cudaStream_t st, bool pdl, int direct_min, in
         a.csize = 1;
         // tile-persistent: at most one CTA per SM walks the (weight tile, slice) tiles; slices
         // of <= 128 rows keep A in tensor memory beside the two accumulators
-        const dim3 grid(std::min(tiles * (a.N / ns), kNumSMs));
+        const int ks = (EPI == TC_STORE && a.ksplit > 1 && nchunks % a.ksplit == 0) ? a.ksplit : 1;
+        a.ksplit = ks;
+        const dim3 grid(std::min(tiles * (a.N / ns) * ks, kNumSMs));
         const bool atm = ns <= 128;
         a.stages = atm ? tc_max_stages_atm(ns, prec) : tc_max_stages_direct(ns, prec);
         const size_t smem = atm ? tc_smem_bytes_atm(ns, prec, a.stages) : tc_smem_bytes_direct(ns, prec, a.stages);
@@ -497,9 +499,10 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
     // reads x anyway.  The last global layer's fc_out keeps its residual epilogue (ln_f reads x).
     const bool direct = !local && tc_direct_min_rows_ > 0 && N >= tc_direct_min_rows_;
     const float *add1 = pending_resid_;
+    const int nadd1 = pending_parts_;
     pending_resid_ = nullptr;
     launch_k(pdl_, k_build_bimg, dim3((N + 7) / 8), dim3(256), 0, stream_, x, kHidden, R, N, L.ln1_w, L.ln1_b,
-             tc_parts(prec), bimg_a_, add1);
+             tc_parts(prec), bimg_a_, add1, nadd1, part_stride());
     mark(KK_BIMG);
     TcArgs a{};
     a.N = N;
@@ -590,15 +593,17 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
     p.rows = kHidden;
     p.K = kHidden;
     p.bias = L.proj_b;
-    p.out = direct ? attn_ : x;
+    p.out = direct ? mlp_ : x;  // direct: kTcKParts K parts at mlp_ + part_stride() apart
     p.ldo = kHidden;
+    p.ksplit = direct ? kTcKParts : 1;
+    p.part_stride = part_stride();
     if (direct)
         launch_tc<TC_STORE>(p, prec, stream_, pdl_, tc_direct_min_rows_, tc_direct_rows_);
     else
         launch_tc<TC_RESID>(p, prec, stream_, pdl_, tc_direct_min_rows_, tc_direct_rows_);
     mark(local ? KK_PROJ_L : KK_PROJ_G);
     launch_k(pdl_, k_build_bimg, dim3((N + 7) / 8), dim3(256), 0, stream_, x, kHidden, R, N, L.ln2_w, L.ln2_b,
-             tc_parts(prec), bimg_a_, direct ? static_cast<const float *>(attn_) : nullptr);
+             tc_parts(prec), bimg_a_, direct ? static_cast<const float *>(mlp_) : nullptr, kTcKParts, part_stride());
     mark(KK_BIMG);
     TcArgs f{};
     f.N = N;
@@ -624,10 +629,13 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
     o.K = kFF;
     o.bias = L.fc_out_b;
     o.ldo = kHidden;
-    if (direct && li < kLayers - 1) {  // the next layer's LN1 kernel adds it to x
-        o.out = attn_;
+    if (direct && li < kLayers - 1) {  // the next layer's LN1 kernel adds its K parts to x
+        o.out = mlp_;
+        o.ksplit = kTcKParts;
+        o.part_stride = part_stride();
         launch_tc<TC_STORE>(o, prec, stream_, pdl_, tc_direct_min_rows_, tc_direct_rows_);
-        pending_resid_ = attn_;
+        pending_resid_ = mlp_;
+        pending_parts_ = kTcKParts;
     } else {
         o.out = x;
         launch_tc<TC_RESID>(o, prec, stream_, pdl_, tc_direct_min_rows_, tc_direct_rows_);
@@ -640,7 +648,7 @@ void Engine::heads_tc(int ch, int R) {
     const int N = (R + 15) / 16 * 16;
     const int prec = gemm_path_ == 3 ? TC_F16 : TC_F16X3;
     launch_k(pdl_, k_build_bimg, dim3((N + 7) / 8), dim3(256), 0, stream_, lx_, kHidden, R, N, llnf_w_, llnf_b_,
-             tc_parts(prec), bimg_a_, static_cast<const float *>(nullptr));
+             tc_parts(prec), bimg_a_, static_cast<const float *>(nullptr), 0, size_t(0));
     mark(KK_BIMG);
     TcArgs h{};
     h.N = N;
@@ -712,7 +720,9 @@ void Engine::block(const Layer &L, int li, bool local, int R, const int *row_slo
         a.page_table = page_table_;
         a.pages_per_stream = pages_per_stream_;
     }
-    launch_gemv<PRO_LN, EPI_QKV>(a, stream_, pdl_);
+    // the first kernel of a global step without the plan kernel follows host-to-device copies
+    launch_gemv<PRO_LN, EPI_QKV>(a, stream_, pdl_ && !(plain_first_ && li == 0 && !local));
+    if (!local && li == 0) plain_first_ = false;
     mark(local ? KK_QKV_L : KK_QKV_G);
     // attention
     if (local) {
@@ -735,10 +745,16 @@ void Engine::block(const Layer &L, int li, bool local, int R, const int *row_slo
         t.out = attn_;
         t.work = work_ + li;
         t.err = dev_err_;
-        launch_k(pdl_, k_attn_decode, dim3(kAttnGrid), dim3(kAttnThreads), kAttnSmem, stream_, t);
-        mark(KK_ATTN_DECODE);
-        launch_k(pdl_, k_attn_combine, dim3((R * kHeads + 7) / 8), dim3(256), 0, stream_, t);
-        mark(KK_ATTN_COMBINE);
+        if (R <= kGemvMaxRows) {
+            launch_k(pdl_, k_attn_rows, dim3(R * kHeads), dim3(kArWarps * 32), 0, stream_, q_,
+                     static_cast<const __half *>(a.kv), page_table_, pages_per_stream_, row_slot, row_pos, attn_);
+            mark(KK_ATTN_DECODE);
+        } else {
+            launch_k(pdl_, k_attn_decode, dim3(kAttnGrid), dim3(kAttnThreads), kAttnSmem, stream_, t);
+            mark(KK_ATTN_DECODE);
+            launch_k(pdl_, k_attn_combine, dim3((R * kHeads + 7) / 8), dim3(256), 0, stream_, t);
+            mark(KK_ATTN_COMBINE);
+        }
     }
     // proj + residual
     GemvArgs p{};
@@ -781,6 +797,11 @@ void Engine::block(const Layer &L, int li, bool local, int R, const int *row_slo
 void Engine::global_layers(int R, const int *row_slot, const int *row_pos) {
     pending_resid_ = nullptr;
     if (pf_active_) {  // a prefill pass: the host-built flash-prefill plan is already on the device
+        for (int li = 0; li < kLayers; ++li) block(global_[li], li, false, R, row_slot, row_pos, 0, x_);
+        return;
+    }
+    if (!use_tc(R) && R <= kGemvMaxRows) {  // every layer on k_attn_rows: no split-K plan
+        plain_first_ = true;
         for (int li = 0; li < kLayers; ++li) block(global_[li], li, false, R, row_slot, row_pos, 0, x_);
         return;
     }

@@ -169,6 +169,13 @@ private:
     int pf_tc_items_ = 0;
     // a direct-form fc_out stored its output here; the next layer's LN1 kernel adds it to x
     const float *pending_resid_ = nullptr;
+    int pending_parts_ = 1;
+    // direct-form proj / fc_out split K in kTcKParts parts (their 768-row GEMMs have 96 tiles
+    // for 148 SMs) and store the parts part_stride() floats apart in mlp_ ([R][3072] floats)
+    static constexpr int kTcKParts = 3;
+    size_t part_stride() const { return size_t(r_max_) * kHidden; }
+    // a global step that starts without the plan kernel launches its first kernel plainly
+    bool plain_first_ = false;
     cudaStream_t stream_ = nullptr, own_stream_ = nullptr;
     std::vector<void *> owned_, pinned_;
     size_t weights_bytes_ = 0;

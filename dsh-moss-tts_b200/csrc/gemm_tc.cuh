@@ -79,6 +79,10 @@ struct TcArgs {
     // TC_GELU_B: output activation image for the next GEMM (K_next = rows)
     uint8_t *bimg_out;
     int *err;               // error flag (0 = fine)
+    // tile-persistent TC_STORE only: K split in ksplit equal parts (1 = none); part p stores its
+    // partial sums at out + p * part_stride (bias in part 0), for a consumer that adds them
+    int ksplit;
+    size_t part_stride;
 };
 
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
@@ -273,12 +277,12 @@ __device__ __forceinline__ float2 tc_epi_pre(const TcArgs &a, int gm, int rr, in
 }
 
 template <int EPI, int NP>
-__device__ __forceinline__ void tc_epi_one(const TcArgs &a, int gm, int rr, int N, float v, float b, int pos, int dst,
-                                           float2 pre) {
+__device__ __forceinline__ void tc_epi_one(const TcArgs &a, float *out, int gm, int rr, int N, float v, float b, int pos,
+                                           int dst, float2 pre) {
     if (EPI == TC_STORE) {
-        if (rr < a.R) a.out[(size_t)rr * a.ldo + gm] = a.bias ? __fadd_rn(v, b) : v;
+        if (rr < a.R) out[(size_t)rr * a.ldo + gm] = b != 0.f ? __fadd_rn(v, b) : v;
     } else if (EPI == TC_RESID) {
-        if (rr < a.R) a.out[(size_t)rr * a.ldo + gm] = __fadd_rn(pre.x, __fadd_rn(v, b));
+        if (rr < a.R) out[(size_t)rr * a.ldo + gm] = __fadd_rn(pre.x, __fadd_rn(v, b));
     } else if (EPI == TC_GELU_B) {
         const float g = rr < a.R ? gelu_new(__fadd_rn(v, b)) : 0.f;
         const __half h = __float2half_rn(g);
@@ -644,9 +648,14 @@ __global__ void __launch_bounds__(kTpThreads, 1) k_gemm_tp(const TcArgs a) {
     const int n_m = a.rows / kTcM;
     const int acol0 = 2 * NS;  // ATM: A stage s at TMEM columns acol0 + 64 s (hi) and + 32 (lo)
     const int n_tiles = n_m * (N / NS);
+    // work units = (K part, tile): part kp of unit u = u / n_tiles covers K chunks
+    // [kp nchu, (kp + 1) nchu) of tile u % n_tiles
+    const int KS = (EPI == TC_STORE && a.ksplit > 1) ? a.ksplit : 1;
+    const int nchu = nchunks / KS;
+    const int n_units = n_tiles * KS;
     const int G = gridDim.x;
-    const int my_tiles = (int)blockIdx.x < n_tiles ? (n_tiles - 1 - (int)blockIdx.x) / G + 1 : 0;
-    const int total = my_tiles * nchunks;  // K chunks this CTA streams
+    const int my_tiles = (int)blockIdx.x < n_units ? (n_units - 1 - (int)blockIdx.x) / G + 1 : 0;
+    const int total = my_tiles * nchu;  // K chunks this CTA streams
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -677,8 +686,9 @@ __global__ void __launch_bounds__(kTpThreads, 1) k_gemm_tp(const TcArgs a) {
         // ---------------- producer
         if (lane == 0 && total > 0) {
             auto src = [&](int seq, int &mt, int &z, int &c) {
-                const int t = (int)blockIdx.x + (seq / nchunks) * G;
-                c = seq % nchunks;
+                const int u = (int)blockIdx.x + (seq / nchu) * G;
+                const int t = u % n_tiles;
+                c = (u / n_tiles) * nchu + seq % nchu;
                 mt = t % n_m;
                 z = t / n_m;
             };
@@ -731,7 +741,7 @@ __global__ void __launch_bounds__(kTpThreads, 1) k_gemm_tp(const TcArgs a) {
                 if (j >= 2 && !mbar_wait(&acce_bar[ab], ((j >> 1) - 1) & 1, a.err, 13)) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t dcol = tmem + (uint32_t)(ab * NS);
-                for (int c = 0; c < nchunks; ++c, ++seq) {
+                for (int c = 0; c < nchu; ++c, ++seq) {
                     const int s = seq % S;
                     if (!mbar_wait(&dq_bar[s], (seq / S) & 1, a.err, 14) ||
                         !mbar_wait(&bfull_bar[s], (seq / S) & 1, a.err, 14)) {
@@ -801,8 +811,10 @@ __global__ void __launch_bounds__(kTpThreads, 1) k_gemm_tp(const TcArgs a) {
         const int cb = hf ? split : 0, ce = hf ? NS : split;
         pdl_wait();
         for (int j = 0; j < my_tiles; ++j) {
-            const int t = (int)blockIdx.x + j * G;
+            const int uu = (int)blockIdx.x + j * G;
+            const int t = uu % n_tiles, kp = uu / n_tiles;
             const int mt = t % n_m, r0 = (t / n_m) * NS, ab = j & 1;
+            float *outp = a.out ? a.out + (size_t)kp * a.part_stride : nullptr;
             if (EPI == TC_QKV) {
                 asm volatile("barrier.sync 2, %0;" ::"n"(kTpEpiThreads) : "memory");  // previous tile's readers
                 for (int jj = e; jj < NS; jj += kTpEpiThreads) {
@@ -821,7 +833,7 @@ __global__ void __launch_bounds__(kTpThreads, 1) k_gemm_tp(const TcArgs a) {
             const bool acc_ok = mbar_wait(&accf_bar[ab], (j >> 1) & 1, a.err, 16);
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const int gm = mt * kTcM + mrow;
-            const float b = a.bias ? a.bias[gm] : 0.f;
+            const float b = (a.bias && kp == 0) ? a.bias[gm] : 0.f;
             for (int n0 = cb; n0 < ce; n0 += 16) {
                 float2 pre[16];
 #pragma unroll
@@ -837,7 +849,7 @@ __global__ void __launch_bounds__(kTpThreads, 1) k_gemm_tp(const TcArgs a) {
 #pragma unroll
                 for (int jj = 0; jj < 16; ++jj) {
                     const int n = n0 + jj;
-                    tc_epi_one<EPI, NP>(a, gm, r0 + n, N, v[jj], b, EPI == TC_QKV ? s_pos[n] : 0,
+                    tc_epi_one<EPI, NP>(a, outp, gm, r0 + n, N, v[jj], b, EPI == TC_QKV ? s_pos[n] : 0,
                                         EPI == TC_QKV ? s_dst[n] : 0, pre[jj]);
                 }
             }
@@ -857,14 +869,15 @@ __global__ void __launch_bounds__(kTpThreads, 1) k_gemm_tp(const TcArgs a) {
 // x fp32 [R][768] (optionally LayerNormed) -> activation image with N padded rows; rows
 // R..N-1 are written as zeros.  parts = 2 also writes the image of the fp16 remainders
 // (x - fp16(x)) right after the first one.  add != null: first the residual add x += add
-// (written back to x; the preceding GEMM stored its output, bias included, in add).  One
+// (written back to x; the preceding GEMM stored its output, bias included, in add -- or in
+// n_add K parts add_stride floats apart, summed in order).  One
 // warp per row: lane l holds the 8-element units l, l + 32, l + 64 of the row (one 16-byte
 // unit of the image each), the LayerNorm statistics are warp reductions.
 constexpr int kBimgUnits = kHidden / 256;  // 8-element units per lane
 __global__ void __launch_bounds__(256) k_build_bimg(float *__restrict__ x, int ldx, int R, int N,
                                                     const float *__restrict__ ln_w, const float *__restrict__ ln_b,
                                                     int parts, uint8_t *__restrict__ bimg,
-                                                    const float *__restrict__ add) {
+                                                    const float *__restrict__ add, int n_add, size_t add_stride) {
     pdl_enter();
     const int lane = threadIdx.x & 31;
     const int n = blockIdx.x * 8 + (threadIdx.x >> 5);
@@ -883,8 +896,15 @@ __global__ void __launch_bounds__(256) k_build_bimg(float *__restrict__ x, int l
         float4 *xp = reinterpret_cast<float4 *>(x + (size_t)n * ldx + 8 * (lane + 32 * j));
         float4 a0 = xp[0], a1 = xp[1];
         if (add) {
+            // the GEMM's output, or its K parts in order: x + (p0 + p1 + ...)
             const float4 *ap = reinterpret_cast<const float4 *>(add + (size_t)n * ldx + 8 * (lane + 32 * j));
-            const float4 b0 = ap[0], b1 = ap[1];
+            float4 b0 = ap[0], b1 = ap[1];
+            for (int p = 1; p < n_add; ++p) {
+                const float4 *cp = reinterpret_cast<const float4 *>(reinterpret_cast<const char *>(ap) + p * add_stride * 4);
+                const float4 c0 = cp[0], c1 = cp[1];
+                b0 = make_float4(__fadd_rn(b0.x, c0.x), __fadd_rn(b0.y, c0.y), __fadd_rn(b0.z, c0.z), __fadd_rn(b0.w, c0.w));
+                b1 = make_float4(__fadd_rn(b1.x, c1.x), __fadd_rn(b1.y, c1.y), __fadd_rn(b1.z, c1.z), __fadd_rn(b1.w, c1.w));
+            }
             a0 = make_float4(__fadd_rn(a0.x, b0.x), __fadd_rn(a0.y, b0.y), __fadd_rn(a0.z, b0.z), __fadd_rn(a0.w, b0.w));
             a1 = make_float4(__fadd_rn(a1.x, b1.x), __fadd_rn(a1.y, b1.y), __fadd_rn(a1.z, b1.z), __fadd_rn(a1.w, b1.w));
             xp[0] = a0;

@@ -766,6 +766,133 @@ __global__ void __launch_bounds__(256) k_attn_combine(const AttnArgs a) {
     }
 }
 
+// Decode attention for small batches (the CUDA-core path, <= 8 rows): one CTA per (row, head),
+// its 16 warps taking the row's pages round-robin (warp w: pages w, w + 16, ...), each with
+// the lane layout and online softmax of k_attn_decode (8 lanes per position, 8 dims a lane, 4
+// positions a step); the warps' partial (max, sum, output) merge in shared memory.  One launch
+// per layer and no plan: the split-K path needs three (plan, decode, combine), which at one
+// row is latency, not bandwidth.
+constexpr int kArWarps = 16;
+__global__ void __launch_bounds__(kArWarps * 32) k_attn_rows(const float *__restrict__ q, const __half *__restrict__ kv,
+                                                            const int *__restrict__ page_table, int pages_per_stream,
+                                                            const int *__restrict__ row_slot, const int *__restrict__ row_pos,
+                                                            float *__restrict__ out) {
+    __shared__ float sm_m[kArWarps], sm_l[kArWarps];
+    __shared__ __align__(16) float sm_o[kArWarps][kHeadDim];
+    pdl_enter();
+    const int r = blockIdx.x / kHeads, hd = blockIdx.x % kHeads;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ps = lane >> 3, ds = lane & 7;
+    const int n = row_pos[r] + 1;  // positions 0 .. pos
+    const int npg = (n + kPage - 1) / kPage;
+    const int slot = row_slot[r];
+    float qv[8];
+    {
+        const float4 *qp = reinterpret_cast<const float4 *>(q + (size_t)r * kHidden + hd * kHeadDim + ds * 8);
+        const float4 x0 = qp[0], x1 = qp[1];
+        qv[0] = x0.x * 0.125f; qv[1] = x0.y * 0.125f; qv[2] = x0.z * 0.125f; qv[3] = x0.w * 0.125f;
+        qv[4] = x1.x * 0.125f; qv[5] = x1.y * 0.125f; qv[6] = x1.z * 0.125f; qv[7] = x1.w * 0.125f;
+    }
+    float m = -INFINITY, l = 0.f, o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = 0.f;
+    for (int pg = warp; pg < npg; pg += kArWarps) {
+        const int page = page_table[(size_t)slot * pages_per_stream + pg];
+        const __half *kb = kv + (size_t)page * kPageHalfs + (size_t)hd * kPage * kHeadDim + ds * 8;
+        const __half *vb = kb + (size_t)kHeads * kPage * kHeadDim;
+        const int pb = pg * kPage;
+        int4 kr[4], vr[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int pp = ps + 4 * u;
+            kr[u] = *reinterpret_cast<const int4 *>(kb + pp * kHeadDim);
+            vr[u] = *reinterpret_cast<const int4 *>(vb + pp * kHeadDim);
+            if (pb + pp >= n) vr[u] = make_int4(0, 0, 0, 0);  // past the row's end: stale bits
+        }
+        float sc[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const __half2 *kh = reinterpret_cast<const __half2 *>(&kr[u]);
+            float dd = 0.f;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float2 kf = __half22float2(kh[e]);
+                dd = fmaf(qv[2 * e], kf.x, dd);
+                dd = fmaf(qv[2 * e + 1], kf.y, dd);
+            }
+            sc[u] = dd;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], 1);
+            sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], 2);
+            sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], 4);
+            if (pb + ps + 4 * u >= n) sc[u] = -INFINITY;
+        }
+        const float mn = fmaxf(fmaxf(m, fmaxf(sc[0], sc[1])), fmaxf(sc[2], sc[3]));
+        if (mn != -INFINITY) {
+            const float corr = __expf(m - mn);
+            float pw[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) pw[u] = __expf(sc[u] - mn);
+            l = l * corr + ((pw[0] + pw[1]) + (pw[2] + pw[3]));
+#pragma unroll
+            for (int e = 0; e < 8; ++e) o[e] *= corr;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const __half2 *vh = reinterpret_cast<const __half2 *>(&vr[u]);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 vf = __half22float2(vh[e]);
+                    o[2 * e] = fmaf(pw[u], vf.x, o[2 * e]);
+                    o[2 * e + 1] = fmaf(pw[u], vf.y, o[2 * e + 1]);
+                }
+            }
+            m = mn;
+        }
+    }
+    // merge the 4 position groups of the warp (lanes ds, ds + 8, ds + 16, ds + 24)
+#pragma unroll
+    for (int off = 8; off <= 16; off <<= 1) {
+        const float mo = __shfl_xor_sync(0xffffffffu, m, off);
+        const float lo2 = __shfl_xor_sync(0xffffffffu, l, off);
+        const float mx = fmaxf(m, mo);
+        const float c1 = (m == -INFINITY) ? 0.f : __expf(m - mx);
+        const float c2 = (mo == -INFINITY) ? 0.f : __expf(mo - mx);
+        l = l * c1 + lo2 * c2;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float oo = __shfl_xor_sync(0xffffffffu, o[j], off);
+            o[j] = o[j] * c1 + oo * c2;
+        }
+        m = mx;
+    }
+    if (lane < 8) {
+        if (lane == 0) {
+            sm_m[warp] = m;
+            sm_l[warp] = l;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) sm_o[warp][ds * 8 + j] = o[j];
+    }
+    __syncthreads();
+    // merge the warps (a warp without pages has m = -inf and weighs nothing)
+    if (threadIdx.x < kHeadDim) {
+        const int d = threadIdx.x;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kArWarps; ++w) M = fmaxf(M, sm_m[w]);
+        float L = 0.f, y = 0.f;
+#pragma unroll
+        for (int w = 0; w < kArWarps; ++w) {
+            const float wgt = sm_m[w] == -INFINITY ? 0.f : __expf(sm_m[w] - M);
+            L = fmaf(sm_l[w], wgt, L);
+            y = fmaf(sm_o[w][d], wgt, y);
+        }
+        out[(size_t)r * kHidden + hd * kHeadDim + d] = y / L;
+    }
+}
+
 // Local decoder attention: n = lpos + 1 <= 17 positions of fp32 local KV.
 // One warp per (row, head); scores in llm.cpp:189-217 order per position.  With bimg set the
 // output goes straight into the next tensor-core GEMM's activation image (N rows, parts).
