@@ -501,8 +501,9 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
     const float *add1 = pending_resid_;
     const int nadd1 = pending_parts_;
     pending_resid_ = nullptr;
-    launch_k(pdl_, k_build_bimg, dim3((N + 7) / 8), dim3(256), 0, stream_, x, kHidden, R, N, L.ln1_w, L.ln1_b,
-             tc_parts(prec), bimg_a_, add1, nadd1, part_stride());
+    launch_k(pdl_ && !(plain_first_ && li == 0 && !local), k_build_bimg, dim3((N + 7) / 8), dim3(256), 0, stream_, x,
+             kHidden, R, N, L.ln1_w, L.ln1_b, tc_parts(prec), bimg_a_, add1, nadd1, part_stride());
+    if (!local && li == 0) plain_first_ = false;
     mark(KK_BIMG);
     TcArgs a{};
     a.N = N;
@@ -576,6 +577,11 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
             f.err = dev_err_;
             launch_k(pdl_, k_attn_prefill_tc, dim3(unsigned(pf_tc_items_), kHeads), dim3(kPtThreads), kPtSmem, stream_, f);
             mark(KK_ATTN_PREFILL);
+        } else if (R <= kAttnRowsMaxTc) {
+            launch_k(pdl_, k_attn_rows, dim3(R * kHeads), dim3(kArWarps * 32), 0, stream_, q_,
+                     static_cast<const __half *>(t.kv), page_table_, pages_per_stream_, row_slot, row_pos, attn_,
+                     bimg_a_, N, tc_parts(prec));
+            mark(KK_ATTN_DECODE);
         } else {
             launch_k(pdl_, k_attn_decode, dim3(kAttnGrid), dim3(kAttnThreads), kAttnSmem, stream_, t);
             mark(KK_ATTN_DECODE);
@@ -747,7 +753,8 @@ void Engine::block(const Layer &L, int li, bool local, int R, const int *row_slo
         t.err = dev_err_;
         if (R <= kGemvMaxRows) {
             launch_k(pdl_, k_attn_rows, dim3(R * kHeads), dim3(kArWarps * 32), 0, stream_, q_,
-                     static_cast<const __half *>(a.kv), page_table_, pages_per_stream_, row_slot, row_pos, attn_);
+                     static_cast<const __half *>(a.kv), page_table_, pages_per_stream_, row_slot, row_pos, attn_,
+                     static_cast<uint8_t *>(nullptr), 0, 0);
             mark(KK_ATTN_DECODE);
         } else {
             launch_k(pdl_, k_attn_decode, dim3(kAttnGrid), dim3(kAttnThreads), kAttnSmem, stream_, t);
@@ -800,7 +807,7 @@ void Engine::global_layers(int R, const int *row_slot, const int *row_pos) {
         for (int li = 0; li < kLayers; ++li) block(global_[li], li, false, R, row_slot, row_pos, 0, x_);
         return;
     }
-    if (!use_tc(R) && R <= kGemvMaxRows) {  // every layer on k_attn_rows: no split-K plan
+    if (use_tc(R) ? R <= kAttnRowsMaxTc : R <= kGemvMaxRows) {  // every layer on k_attn_rows: no plan
         plain_first_ = true;
         for (int li = 0; li < kLayers; ++li) block(global_[li], li, false, R, row_slot, row_pos, 0, x_);
         return;

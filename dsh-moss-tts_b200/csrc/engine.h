@@ -103,6 +103,10 @@ public:
     // 0 = automatic (tensor cores above kGemvMaxRows rows), 1 = CUDA-core GEMV, 2 = tensor cores
     void set_gemm_path(int mode);
     static constexpr int kGemvMaxRows = 8;
+    // decode batches up to this many rows on the tensor-core path also use k_attn_rows (one
+    // launch per layer; measured faster than plan + split-K decode + combine at 32 and 64 rows,
+    // slower at 256, where the split-K kernel's page ring keeps HBM busier)
+    static constexpr int kAttnRowsMaxTc = 96;
     int max_rows() const { return r_max_; }
     // tensor-core GEMM form: batches of at least direct_min_rows padded rows run one CTA per
     // (weight tile, slice of <= direct_rows rows) with no split-K (0 = never)

@@ -776,7 +776,8 @@ constexpr int kArWarps = 16;
 __global__ void __launch_bounds__(kArWarps * 32) k_attn_rows(const float *__restrict__ q, const __half *__restrict__ kv,
                                                             const int *__restrict__ page_table, int pages_per_stream,
                                                             const int *__restrict__ row_slot, const int *__restrict__ row_pos,
-                                                            float *__restrict__ out) {
+                                                            float *__restrict__ out, uint8_t *__restrict__ bimg, int bimg_N,
+                                                            int bimg_parts) {
     __shared__ float sm_m[kArWarps], sm_l[kArWarps];
     __shared__ __align__(16) float sm_o[kArWarps][kHeadDim];
     pdl_enter();
@@ -889,7 +890,16 @@ __global__ void __launch_bounds__(kArWarps * 32) k_attn_rows(const float *__rest
             L = fmaf(sm_l[w], wgt, L);
             y = fmaf(sm_o[w][d], wgt, y);
         }
-        out[(size_t)r * kHidden + hd * kHeadDim + d] = y / L;
+        const float res = y / L;
+        if (bimg) {  // the tensor-core path: straight into the proj GEMM's activation image
+            const __half h = __float2half_rn(res);
+            const size_t off = bimg_off(r, hd * kHeadDim + d, bimg_N);
+            *reinterpret_cast<__half *>(bimg + off) = h;
+            if (bimg_parts == 2)
+                *reinterpret_cast<__half *>(bimg + (size_t)kHidden * bimg_N * 2 + off) = __float2half_rn(res - __half2float(h));
+        } else {
+            out[(size_t)r * kHidden + hd * kHeadDim + d] = res;
+        }
     }
 }
 
