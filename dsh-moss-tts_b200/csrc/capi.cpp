@@ -18,10 +18,22 @@ struct mossgpu_engine {
 
 namespace {
 
+// The engine's device becomes the calling thread's current device first: a handle is used
+// from threads other than its creator (a runtime worker, the reference's generate producer
+// thread, engine.cpp:466-475), whose current device starts at 0.
+void make_current(const mossgpu::Engine &g) {
+    int d = -1;
+    if (cudaGetDevice(&d) != cudaSuccess || d != g.device()) {
+        const cudaError_t rc = cudaSetDevice(g.device());
+        if (rc != cudaSuccess) throw std::runtime_error(std::string("cudaSetDevice: ") + cudaGetErrorString(rc));
+    }
+}
+
 template <class F>
 int guarded(mossgpu_engine *e, F &&f) {
     if (!e || !e->eng) return 1;
     try {
+        make_current(*e->eng);
         f(*e->eng);
         e->error.clear();
         return 0;

@@ -1,0 +1,127 @@
+// BatchRuntime over the real engine (MossGpuOps, the C ABI): reads a job file, runs every job
+// through the runtime's worker thread, and writes what each job's sink received.
+//
+//   batch_runtime_demo <weights.moss> <jobs.bin> <out.txt> <max_active> <frames_per_call>
+//
+// jobs.bin (int32 little endian): n_jobs, prefix_m, prefix rows [prefix_m][17], then per job
+// seed, greedy, rep_x1000, min_frames, max_frames, chunk_frames, use_prefix, m, rows [m][17].
+// out.txt: per job "job <i> <state> <frames>", then one "blk <segment> <n> <16 n codes>" line
+// per block.  Exit 0 when every job ended (in any state), 2 on a load or input error.
+#include "batch_runtime.h"
+
+#include <cstdio>
+#include <cstdlib>
+#include <fstream>
+#include <string>
+#include <vector>
+
+using namespace moss::gpu;
+
+namespace {
+
+constexpr int kMaxCtx = 512;
+constexpr int kMaxStreams = 16;
+
+bool read_ints(std::ifstream &f, int32_t *v, size_t n) {
+    f.read(reinterpret_cast<char *>(v), static_cast<std::streamsize>(n * sizeof(int32_t)));
+    return static_cast<size_t>(f.gcount()) == n * sizeof(int32_t);
+}
+
+bool read_rows(std::ifstream &f, int m, std::vector<FrameRow> *rows) {
+    rows->resize(static_cast<size_t>(m));
+    for (auto &r : *rows)
+        if (!read_ints(f, r.data(), r.size())) return false;
+    return true;
+}
+
+}  // namespace
+
+int main(int argc, char **argv) {
+    if (argc != 6) {
+        std::fprintf(stderr, "usage: %s weights jobs.bin out.txt max_active frames_per_call\n", argv[0]);
+        return 2;
+    }
+    std::ifstream in(argv[2], std::ios::binary);
+    int32_t hdr[2];
+    if (!in || !read_ints(in, hdr, 2)) {
+        std::fprintf(stderr, "bad job file\n");
+        return 2;
+    }
+    std::vector<FrameRow> prefix;
+    if (!read_rows(in, hdr[1], &prefix)) return 2;
+    std::vector<GenJobRequest> jobs(static_cast<size_t>(hdr[0]));
+    std::vector<int> use_prefix(jobs.size());
+    for (size_t i = 0; i < jobs.size(); ++i) {
+        int32_t v[8];
+        if (!read_ints(in, v, 8)) return 2;
+        GenJobRequest &r = jobs[i];
+        r.id = "job" + std::to_string(i);
+        r.seed = static_cast<uint64_t>(v[0]);
+        r.greedy = v[1] != 0;
+        r.repetition_penalty = static_cast<float>(v[2]) / 1000.0f;
+        r.min_frames = v[3];
+        r.max_frames = v[4];
+        r.chunk_frames = v[5];
+        use_prefix[i] = v[6];
+        r.segments.emplace_back();
+        if (!read_rows(in, v[7], &r.segments.back())) return 2;
+    }
+
+    char err[1024] = {0};
+    mossgpu_engine *h = mossgpu_create(argv[1], 0, kMaxStreams, kMaxCtx, 0, err, sizeof(err));
+    if (!h) {
+        std::fprintf(stderr, "load failed: %s\n", err);
+        return 2;
+    }
+    int rc = 0;
+    {
+        int prefix_sid = -1;
+        if (!prefix.empty()) {
+            if (mossgpu_stream_open(h, &prefix_sid) != 0 ||
+                mossgpu_prefill(h, prefix_sid, prefix[0].data(), static_cast<int>(prefix.size()), 0) != 0) {
+                std::fprintf(stderr, "prefix: %s\n", mossgpu_last_error(h));
+                mossgpu_destroy(h);
+                return 2;
+            }
+        }
+        for (size_t i = 0; i < jobs.size(); ++i)
+            if (use_prefix[i]) {
+                jobs[i].prefix_stream = prefix_sid;
+                jobs[i].prefix_len = static_cast<int>(prefix.size());
+            }
+
+        MossGpuOps ops(h, kMaxCtx);
+        BatchRuntime<MossGpuOps> rt(ops, BatchRuntimeOptions{std::atoi(argv[4]), 64, std::atoi(argv[5])});
+        std::vector<std::vector<std::string>> blocks(jobs.size());
+        std::vector<std::string> ids(jobs.size());
+        for (size_t i = 0; i < jobs.size(); ++i) {
+            std::string e;
+            auto sink = [&blocks, i](int segment, const int32_t *codes, int n) {
+                std::string line = "blk " + std::to_string(segment) + " " + std::to_string(n);
+                for (int k = 0; k < 16 * n; ++k) line += " " + std::to_string(codes[k]);
+                blocks[i].push_back(line);
+                return true;
+            };
+            if (!rt.submit(jobs[i], sink, &ids[i], &e)) {
+                std::fprintf(stderr, "submit %zu: %s\n", i, e.c_str());
+                rc = 2;
+            }
+        }
+        rt.start();
+        std::ofstream out(argv[3]);
+        for (size_t i = 0; i < jobs.size() && rc == 0; ++i) {
+            GenJobInfo info;
+            if (!rt.wait(ids[i], 120000, &info)) {
+                std::fprintf(stderr, "job %zu did not end\n", i);
+                rc = 2;
+                break;
+            }
+            out << "job " << i << " " << gen_job_state_name(info.state) << " " << info.frames << "\n";
+            if (!info.error.empty()) std::fprintf(stderr, "job %zu: %s\n", i, info.error.c_str());
+            for (auto &l : blocks[i]) out << l << "\n";
+        }
+        rt.shutdown();
+    }
+    mossgpu_destroy(h);
+    return rc;
+}

@@ -1,0 +1,468 @@
+// BatchRuntime (batch_runtime.h) on a host-only test double of the engine.  The double's
+// codes and end gate depend only on a stream's own contents, the frame index, the sampling
+// parameters and the seed, so a job must produce the same blocks however the runtime
+// batches it.  Expected blocks come from a sequential restatement of TtsEngine::synthesize's
+// frame loop (one frame per call, reference engine.cpp:455-530) with its own chunking
+// (decode_pending, engine.cpp:480-502).  Exit 0 = all checks passed; failures print and exit 1.
+#include "batch_runtime.h"
+
+#include <cstdio>
+#include <map>
+#include <string>
+#include <vector>
+
+using namespace moss::gpu;
+
+namespace {
+
+int g_failures = 0;
+#define CHECK(cond, ...)                                   \
+    do {                                                   \
+        if (!(cond)) {                                     \
+            std::printf("FAIL %s:%d: ", __FILE__, __LINE__); \
+            std::printf(__VA_ARGS__);                      \
+            std::printf("\n");                             \
+            ++g_failures;                                  \
+        }                                                  \
+    } while (0)
+
+uint64_t mix(uint64_t h, uint64_t v) {
+    h ^= v + 0x9E3779B97F4A7C15ull + (h << 6) + (h >> 2);
+    return h * 0x100000001B3ull;
+}
+
+struct FakeOps {
+    struct Stream {
+        bool open = false;
+        std::vector<uint64_t> toks;  // one entry per position
+        uint64_t seed = 0;
+        int frame = 0;
+    };
+    explicit FakeOps(int streams, int ctx) : s(static_cast<size_t>(streams)), ctx_(ctx) {}
+    std::vector<Stream> s;
+    int ctx_;
+    std::string err;
+    std::vector<int> prefill_n, step_n, step_frames_n;
+
+    bool bad(int sid) const { return sid < 0 || sid >= static_cast<int>(s.size()) || !s[static_cast<size_t>(sid)].open; }
+    int fail(const char *why) {
+        err = why;
+        return 1;
+    }
+    int open(int *sid) {
+        for (size_t i = 0; i < s.size(); ++i)
+            if (!s[i].open) {
+                s[i] = Stream{};
+                s[i].open = true;
+                *sid = static_cast<int>(i);
+                return 0;
+            }
+        return fail("no free stream slot");
+    }
+    int fork(int src, int n_pos, int *sid) {
+        if (bad(src) || n_pos > static_cast<int>(s[static_cast<size_t>(src)].toks.size())) return fail("bad fork");
+        if (open(sid)) return 1;
+        auto &t = s[static_cast<size_t>(src)].toks;
+        s[static_cast<size_t>(*sid)].toks.assign(t.begin(), t.begin() + n_pos);
+        return 0;
+    }
+    int close(int sid) {
+        if (bad(sid)) return fail("stream not open");
+        s[static_cast<size_t>(sid)] = Stream{};
+        return 0;
+    }
+    int position(int sid, int *pos) {
+        if (bad(sid)) return fail("stream not open");
+        *pos = static_cast<int>(s[static_cast<size_t>(sid)].toks.size());
+        return 0;
+    }
+    int prefill_batch(int n, const int32_t *sids, const int32_t *m, const int32_t *start, const int32_t *rows) {
+        size_t k = 0;
+        for (int i = 0; i < n; ++i) {  // validate everything first: nothing changes on failure
+            if (bad(sids[i])) return fail("stream not open");
+            if (start[i] != static_cast<int>(s[static_cast<size_t>(sids[i])].toks.size())) return fail("bad start");
+            if (start[i] + m[i] > ctx_) return fail("context full");
+            for (int r = 0; r < m[i]; ++r, ++k)
+                if (rows[k * 17] < 0 || rows[k * 17] >= 16384) return fail("text id out of range");
+        }
+        k = 0;
+        for (int i = 0; i < n; ++i)
+            for (int r = 0; r < m[i]; ++r, ++k) {
+                uint64_t h = 1469598103934665603ull;
+                for (int c = 0; c < 17; ++c) h = mix(h, static_cast<uint64_t>(rows[k * 17 + c]) + 1);
+                s[static_cast<size_t>(sids[i])].toks.push_back(h);
+            }
+        prefill_n.push_back(n);
+        return 0;
+    }
+    int generate_begin(int sid, uint64_t seed) {
+        if (bad(sid)) return fail("stream not open");
+        s[static_cast<size_t>(sid)].seed = seed;
+        s[static_cast<size_t>(sid)].frame = 0;
+        return 0;
+    }
+    int step_frames(const int32_t *sids, int n, const mossgpu_sample_params &p, int frames, int32_t *codes,
+                    int32_t *done) {
+        if (frames < 1 || frames > 1024) return fail("bad frame count");
+        for (int i = 0; i < n; ++i) {
+            if (bad(sids[i])) return fail("stream not open");
+            if (static_cast<int>(s[static_cast<size_t>(sids[i])].toks.size()) + frames > ctx_) return fail("context full");
+        }
+        const uint64_t pk = static_cast<uint64_t>(p.greedy) * 5 + static_cast<uint64_t>(p.repetition_penalty * 1000.0f) * 7 +
+                            static_cast<uint64_t>(p.min_frames) * 11 + static_cast<uint64_t>(p.top_k) * 13;
+        for (int i = 0; i < n; ++i) {
+            Stream &st = s[static_cast<size_t>(sids[i])];
+            int f = 0;
+            for (; f < frames; ++f) {
+                uint64_t h = 1469598103934665603ull;
+                for (uint64_t t : st.toks) h = mix(h, t);
+                h = mix(mix(h, st.seed), pk);
+                if (st.frame >= p.min_frames && (h >> 11) % 9 == 0) break;  // the end gate
+                uint64_t row = h;
+                for (int ch = 0; ch < 16; ++ch) {
+                    const int32_t c = static_cast<int32_t>(mix(h, static_cast<uint64_t>(ch) * 131 + static_cast<uint64_t>(st.frame)) % 1024);
+                    codes[(static_cast<size_t>(f) * n + i) * 16 + ch] = c;
+                    row = mix(row, static_cast<uint64_t>(c));
+                }
+                st.toks.push_back(row);
+                ++st.frame;
+            }
+            for (int g = f; g < frames; ++g)
+                for (int ch = 0; ch < 16; ++ch) codes[(static_cast<size_t>(g) * n + i) * 16 + ch] = -1;
+            done[i] = f;
+        }
+        step_n.push_back(n);
+        step_frames_n.push_back(frames);
+        return 0;
+    }
+    const char *last_error() { return err.c_str(); }
+    int max_ctx() const { return ctx_; }
+    int open_streams() const {
+        int c = 0;
+        for (auto &x : s) c += x.open ? 1 : 0;
+        return c;
+    }
+};
+
+struct Block {
+    int segment;
+    std::vector<int32_t> codes;  // [16][n]
+    bool operator==(const Block &o) const { return segment == o.segment && codes == o.codes; }
+};
+
+std::vector<FrameRow> rows_of(int m, uint64_t seed, int bad_row = -1) {
+    std::vector<FrameRow> out(static_cast<size_t>(m));
+    uint64_t h = seed * 7919 + 1;
+    for (int r = 0; r < m; ++r) {
+        h = mix(h, static_cast<uint64_t>(r));
+        out[static_cast<size_t>(r)][0] = r == bad_row ? 16384 : static_cast<int32_t>(h % 16384);
+        for (int c = 1; c < 17; ++c) out[static_cast<size_t>(r)][static_cast<size_t>(c)] = static_cast<int32_t>(mix(h, static_cast<uint64_t>(c)) % 1025);
+    }
+    return out;
+}
+
+mossgpu_sample_params params_of(const GenJobRequest &r) {
+    mossgpu_sample_params p{};
+    p.greedy = r.greedy;
+    p.temperature = r.temperature > 0 ? r.temperature : 0.8f;
+    p.top_k = r.top_k > 0 ? r.top_k : 25;
+    p.top_p = r.top_p > 0 ? r.top_p : 0.95f;
+    p.repetition_penalty = r.repetition_penalty > 0 ? r.repetition_penalty : 1.2f;
+    p.end_greedy = 1;
+    p.min_frames = r.min_frames;
+    p.greedy_frames = r.greedy_frames;
+    return p;
+}
+
+// synthesize's loop, one frame per call, on its own engine double
+std::vector<Block> expected_blocks(FakeOps &eng, const GenJobRequest &r) {
+    std::vector<Block> out;
+    const int chunk = r.chunk_frames > 0 ? r.chunk_frames : 8;
+    const int max_frames = r.max_frames > 0 ? r.max_frames : 375;
+    const mossgpu_sample_params p = params_of(r);
+    int frames_total = 0;
+    for (size_t si = 0; si < r.segments.size(); ++si) {
+        const auto &seg = r.segments[si];
+        if (seg.empty()) continue;
+        int sid = -1;
+        if (r.prefix_stream >= 0)
+            eng.fork(r.prefix_stream, r.prefix_len, &sid);
+        else
+            eng.open(&sid);
+        const int32_t m = static_cast<int32_t>(seg.size()), st = r.prefix_stream >= 0 ? r.prefix_len : 0;
+        std::vector<int32_t> flat;
+        for (auto &row : seg) flat.insert(flat.end(), row.begin(), row.end());
+        if (eng.prefill_batch(1, &sid, &m, &st, flat.data()) != 0) {
+            eng.close(sid);
+            return {};
+        }
+        eng.generate_begin(sid, r.seed);
+        std::vector<std::array<int32_t, 16>> pending;
+        auto decode_pending = [&](bool force) {
+            const size_t want = frames_total == 0 ? std::min<size_t>(4, static_cast<size_t>(chunk)) : static_cast<size_t>(chunk);
+            const size_t n = pending.size();
+            if (n == 0 || (!force && n < want)) return;
+            Block b{static_cast<int>(si), std::vector<int32_t>(16 * n)};
+            for (size_t ch = 0; ch < 16; ++ch)
+                for (size_t j = 0; j < n; ++j) b.codes[ch * n + j] = pending[j][ch];
+            out.push_back(b);
+            frames_total += static_cast<int>(n);
+            pending.clear();
+        };
+        for (int f = 0; f < max_frames; ++f) {
+            int pos = 0;
+            eng.position(sid, &pos);
+            if (pos >= eng.max_ctx()) break;
+            int32_t codes[16], done = 0;
+            eng.step_frames(&sid, 1, p, 1, codes, &done);
+            if (done == 0) break;
+            std::array<int32_t, 16> c{};
+            std::copy(codes, codes + 16, c.begin());
+            pending.push_back(c);
+            decode_pending(false);
+        }
+        decode_pending(true);
+        eng.close(sid);
+    }
+    return out;
+}
+
+int setup_prefix(FakeOps &eng, int m) {
+    int sid = -1;
+    eng.open(&sid);
+    auto rows = rows_of(m, 999);
+    std::vector<int32_t> flat;
+    for (auto &row : rows) flat.insert(flat.end(), row.begin(), row.end());
+    const int32_t mm = m, st = 0;
+    eng.prefill_batch(1, &sid, &mm, &st, flat.data());
+    eng.prefill_n.clear();
+    return sid;
+}
+
+std::vector<GenJobRequest> mixed_jobs(int prefix_sid, int prefix_len) {
+    std::vector<GenJobRequest> jobs;
+    for (int i = 0; i < 12; ++i) {
+        GenJobRequest r;
+        r.seed = 100 + static_cast<uint64_t>(i);
+        const int nseg = 1 + i % 3;
+        for (int k = 0; k < nseg; ++k) r.segments.push_back(rows_of(3 + (i * 5 + k * 7) % 17, static_cast<uint64_t>(i * 10 + k)));
+        if (i == 4) r.segments.insert(r.segments.begin() + 1, std::vector<FrameRow>{});  // empty text segment
+        r.greedy = i % 2 == 0;
+        r.repetition_penalty = i % 4 == 1 ? 1.1f : 0.0f;
+        r.min_frames = i % 5 == 0 ? 3 : 0;
+        r.chunk_frames = (i % 4 == 0) ? 1 : (i % 4 == 1) ? 3 : (i % 4 == 2) ? 0 : 8;
+        r.max_frames = (i % 3 == 0) ? 5 : (i % 3 == 1) ? 40 : 0;
+        if (i % 2 == 1) {
+            r.prefix_stream = prefix_sid;
+            r.prefix_len = prefix_len - (i % 3);
+        }
+        jobs.push_back(r);
+    }
+    return jobs;
+}
+
+struct Collected {
+    std::map<std::string, std::vector<Block>> blocks;
+    CodeSink sink_for(const std::string &key) {
+        return [this, key](int segment, const int32_t *codes, int n) {
+            blocks[key].push_back(Block{segment, std::vector<int32_t>(codes, codes + 16 * n)});
+            return true;
+        };
+    }
+};
+
+void drain(BatchRuntime<FakeOps> &rt) {
+    for (int it = 0; it < 100000 && rt.run_once(); ++it) {
+    }
+}
+
+// A: batched results equal the sequential ones; calls really batch; every stream closes.
+void test_batched_equals_sequential() {
+    FakeOps eng(16, 4096), ref(16, 4096);
+    const int psid = setup_prefix(eng, 20), rsid = setup_prefix(ref, 20);
+    CHECK(psid == rsid, "prefix stream ids differ");
+    auto jobs = mixed_jobs(psid, 20);
+    BatchRuntime<FakeOps> rt(eng, BatchRuntimeOptions{8, 64, 4});
+    Collected got;
+    std::vector<std::string> ids;
+    for (size_t i = 0; i < jobs.size(); ++i) {
+        std::string id, err;
+        jobs[i].id = "job" + std::to_string(i);
+        CHECK(rt.submit(jobs[i], got.sink_for(jobs[i].id), &id, &err), "submit %zu: %s", i, err.c_str());
+        CHECK(id == jobs[i].id, "job id");
+        ids.push_back(id);
+    }
+    drain(rt);
+    int total_frames = 0;
+    for (size_t i = 0; i < jobs.size(); ++i) {
+        GenJobInfo info;
+        CHECK(rt.job(ids[i], &info), "job %zu missing", i);
+        CHECK(info.state == GenJobState::Completed, "job %zu state %s (%s)", i, gen_job_state_name(info.state), info.error.c_str());
+        const auto want = expected_blocks(ref, jobs[i]);
+        CHECK(got.blocks[ids[i]] == want, "job %zu: %zu blocks, expected %zu", i, got.blocks[ids[i]].size(), want.size());
+        int frames = 0;
+        for (auto &b : want) frames += static_cast<int>(b.codes.size() / 16);
+        CHECK(info.frames == frames, "job %zu frames %d vs %d", i, info.frames, frames);
+        const int nonempty = static_cast<int>(jobs[i].segments.size()) - (i == 4 ? 1 : 0);
+        CHECK(info.segments_done == nonempty, "job %zu segments %d", i, info.segments_done);
+        total_frames += frames;
+    }
+    CHECK(eng.open_streams() == 1, "streams left open: %d", eng.open_streams() - 1);
+    int pmax = 0, smax = 0, fmax = 0;
+    for (int n : eng.prefill_n) pmax = std::max(pmax, n);
+    for (int n : eng.step_n) smax = std::max(smax, n);
+    for (int n : eng.step_frames_n) fmax = std::max(fmax, n);
+    CHECK(pmax > 1 && smax > 1, "no batching: prefill %d step %d", pmax, smax);
+    CHECK(smax <= 8 && fmax <= 4, "limits: %d streams, %d frames per call", smax, fmax);
+    std::printf("A frames=%d prefill_calls=%zu prefill_max=%d step_calls=%zu step_max=%d\n", total_frames,
+                eng.prefill_n.size(), pmax, eng.step_n.size(), smax);
+}
+
+// B: queue limit, cancel while queued, cancel while running, a failing sink, shutdown.
+void test_queue_cancel_sink() {
+    FakeOps eng(8, 4096);
+    BatchRuntime<FakeOps> rt(eng, BatchRuntimeOptions{1, 2, 2});
+    GenJobRequest r;
+    r.segments.push_back(rows_of(6, 1));
+    r.max_frames = 300;
+    r.min_frames = 200;  // no end gate before frame 200
+    std::string a, b, c, err;
+    Collected got;
+    CHECK(rt.submit(r, got.sink_for("a"), &a, &err), "submit a");
+    CHECK(rt.submit(r, got.sink_for("b"), &b, &err), "submit b");
+    CHECK(!rt.submit(r, nullptr, &c, &err) && err == "busy", "third submit: %s", err.c_str());
+    CHECK(rt.queue_depth() == 2, "queue depth %d", rt.queue_depth());
+    CHECK(a != b && a.size() == 12, "generated ids");
+    rt.run_once();  // admits a (max_active 1), prefills, one 2-frame call
+    CHECK(rt.queue_depth() == 1 && rt.running() == 1, "after one iteration");
+    CHECK(rt.cancel(b), "cancel b");
+    rt.run_once();
+    CHECK(rt.cancel(a), "cancel a");
+    drain(rt);
+    GenJobInfo ia, ib;
+    rt.job(a, &ia);
+    rt.job(b, &ib);
+    // a: two 2-frame calls made its first 4-frame block; the frames after cancel are dropped
+    CHECK(ia.state == GenJobState::Cancelled && ia.frames == 4, "a: %s %d", gen_job_state_name(ia.state), ia.frames);
+    CHECK(ib.state == GenJobState::Cancelled && ib.frames == 0, "b: %s", gen_job_state_name(ib.state));
+    CHECK(eng.prefill_n.size() == 1, "b never reached the engine");
+    CHECK(eng.open_streams() == 0, "cancelled stream left open");
+
+    // a sink that fails on its second block
+    GenJobRequest s = r;
+    s.chunk_frames = 2;
+    int calls = 0;
+    std::string d;
+    CHECK(rt.submit(s, [&](int, const int32_t *, int) { return ++calls < 2; }, &d, &err), "submit d");
+    drain(rt);
+    GenJobInfo id_;
+    rt.job(d, &id_);
+    CHECK(id_.state == GenJobState::Cancelled && calls == 2 && id_.frames == 4, "d: %s calls %d frames %d",
+          gen_job_state_name(id_.state), calls, id_.frames);
+    CHECK(eng.open_streams() == 0, "sink-cancelled stream left open");
+
+    // a throwing sink fails the same way
+    std::string t;
+    CHECK(rt.submit(s, [&](int, const int32_t *, int) -> bool { throw std::runtime_error("x"); }, &t, &err), "submit t");
+    drain(rt);
+    GenJobInfo it_;
+    rt.job(t, &it_);
+    CHECK(it_.state == GenJobState::Cancelled, "throwing sink: %s", gen_job_state_name(it_.state));
+
+    // shutdown cancels queued jobs
+    std::string e1, e2;
+    rt.submit(r, nullptr, &e1, &err);
+    rt.submit(r, nullptr, &e2, &err);
+    rt.shutdown();
+    GenJobInfo ie;
+    rt.job(e2, &ie);
+    CHECK(ie.state == GenJobState::Cancelled && ie.error == "shutting down", "shutdown: %s", ie.error.c_str());
+    CHECK(!rt.submit(r, nullptr, &e1, &err) && err == "shutting down", "submit after shutdown");
+    std::printf("B ok\n");
+}
+
+// C: a bad segment fails its own job only; the context cap ends a segment without error.
+void test_failures_and_context_cap() {
+    FakeOps eng(8, 4096), ref(8, 4096);
+    BatchRuntime<FakeOps> rt(eng, BatchRuntimeOptions{8, 8, 16});
+    std::vector<GenJobRequest> jobs(3);
+    for (int i = 0; i < 3; ++i) {
+        jobs[static_cast<size_t>(i)].segments.push_back(rows_of(5 + i, static_cast<uint64_t>(40 + i), i == 1 ? 2 : -1));
+        jobs[static_cast<size_t>(i)].greedy = true;
+        jobs[static_cast<size_t>(i)].seed = static_cast<uint64_t>(i);
+    }
+    Collected got;
+    std::vector<std::string> ids(3);
+    std::string err;
+    for (int i = 0; i < 3; ++i) rt.submit(jobs[static_cast<size_t>(i)], got.sink_for(std::to_string(i)), &ids[static_cast<size_t>(i)], &err);
+    drain(rt);
+    for (int i = 0; i < 3; ++i) {
+        GenJobInfo info;
+        rt.job(ids[static_cast<size_t>(i)], &info);
+        if (i == 1) {
+            CHECK(info.state == GenJobState::Failed && info.error == "text id out of range", "bad job: %s %s",
+                  gen_job_state_name(info.state), info.error.c_str());
+        } else {
+            CHECK(info.state == GenJobState::Completed, "good job %d: %s", i, info.error.c_str());
+            CHECK(got.blocks[std::to_string(i)] == expected_blocks(ref, jobs[static_cast<size_t>(i)]), "good job %d blocks", i);
+        }
+    }
+    CHECK(eng.open_streams() == 0, "failed job's stream left open");
+
+    // context of 17 positions: 10 prompt rows leave 7 frames
+    FakeOps small(4, 17), small_ref(4, 17);
+    BatchRuntime<FakeOps> rt2(small, BatchRuntimeOptions{4, 4, 5});
+    GenJobRequest r;
+    r.segments.push_back(rows_of(10, 3));
+    r.segments.push_back(rows_of(17, 4));  // fills the context: no frames
+    r.min_frames = 100;
+    r.chunk_frames = 3;
+    std::string id;
+    rt2.submit(r, got.sink_for("cap"), &id, &err);
+    drain(rt2);
+    GenJobInfo info;
+    rt2.job(id, &info);
+    CHECK(info.state == GenJobState::Completed && info.frames == 7 && info.segments_done == 2, "cap: %s frames %d (%s)",
+          gen_job_state_name(info.state), info.frames, info.error.c_str());
+    CHECK(got.blocks["cap"] == expected_blocks(small_ref, r), "cap blocks");
+    std::printf("C ok\n");
+}
+
+// D: the worker thread with wait().
+void test_worker_thread() {
+    FakeOps eng(16, 4096), ref(16, 4096);
+    const int psid = setup_prefix(eng, 12);
+    setup_prefix(ref, 12);
+    auto jobs = mixed_jobs(psid, 12);
+    jobs.resize(8);
+    BatchRuntime<FakeOps> rt(eng, BatchRuntimeOptions{4, 16, 8});
+    Collected got;
+    std::vector<std::string> ids(jobs.size());
+    std::string err;
+    for (size_t i = 0; i < jobs.size(); ++i)
+        CHECK(rt.submit(jobs[i], got.sink_for(std::to_string(i)), &ids[i], &err), "submit %zu", i);
+    rt.start();
+    for (size_t i = 0; i < jobs.size(); ++i) {
+        GenJobInfo info;
+        CHECK(rt.wait(ids[i], 20000, &info), "wait %zu timed out", i);
+        CHECK(info.state == GenJobState::Completed, "job %zu: %s", i, info.error.c_str());
+    }
+    rt.shutdown();
+    for (size_t i = 0; i < jobs.size(); ++i)
+        CHECK(got.blocks[std::to_string(i)] == expected_blocks(ref, jobs[i]), "threaded job %zu blocks", i);
+    std::printf("D ok\n");
+}
+
+}  // namespace
+
+int main() {
+    test_batched_equals_sequential();
+    test_queue_cancel_sink();
+    test_failures_and_context_cap();
+    test_worker_thread();
+    if (g_failures) {
+        std::printf("%d failures\n", g_failures);
+        return 1;
+    }
+    return 0;
+}
