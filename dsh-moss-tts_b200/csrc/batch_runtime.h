@@ -46,8 +46,10 @@
 #include <cstring>
 #include <deque>
 #include <functional>
+#include <map>
 #include <memory>
 #include <mutex>
+#include <stdexcept>
 #include <string>
 #include <thread>
 #include <tuple>
@@ -188,6 +190,7 @@ public:
         if (j->req.chunk_frames <= 0) j->req.chunk_frames = 8;
         j->assembler = ChunkAssembler(j->req.chunk_frames);
         j->params = make_params(j->req);
+        j->cost = job_cost(j->req);
         {
             std::lock_guard<std::mutex> lock(mutex_);
             if (stop_) return fail_submit(err, "shutting down");
@@ -195,6 +198,7 @@ public:
             j->info.id = j->req.id.empty() ? make_job_id_locked() : j->req.id;
             queue_.push_back(j);
             jobs_.push_back(j);
+            load_ += j->cost;
             prune_locked();
         }
         job_added_.notify_one();
@@ -235,6 +239,18 @@ public:
     }
     int max_queue() const { return opt_.max_queue; }
     int running() const { return running_count_.load(); }
+    // Outstanding work: the summed job_cost of the jobs queued or running.
+    int64_t load() const { return load_.load(); }
+
+    // A job's work for load balancing: every non-empty segment attends over the prefix and its
+    // own rows and generates up to max_frames frames (max_frames <= 0 counts as 375).
+    static int64_t job_cost(const GenJobRequest &r) {
+        const int64_t frames = r.max_frames > 0 ? r.max_frames : 375;
+        int64_t c = 0;
+        for (const auto &seg : r.segments)
+            if (!seg.empty()) c += (r.prefix_stream >= 0 ? r.prefix_len : 0) + static_cast<int64_t>(seg.size()) + frames;
+        return c;
+    }
 
     // One scheduling iteration; false when there was nothing to do (no queued or running job).
     bool run_once() {
@@ -257,6 +273,7 @@ private:
         GenJobInfo info;
         Clock::time_point submitted, finished;
         mossgpu_sample_params params{};
+        int64_t cost = 0;
         // worker-side state
         ChunkAssembler assembler{8};
         size_t seg = 0;        // next segment to open (or the live one)
@@ -319,6 +336,7 @@ private:
             jobs_.erase(jobs_.begin());
     }
     void end_locked(Job &j, GenJobState s, const std::string &error) {
+        if (!j.ended) load_ -= j.cost;
         j.info.state = s;
         j.info.error = error;
         j.finished = Clock::now();
@@ -543,8 +561,122 @@ private:
     std::vector<std::shared_ptr<Job>> jobs_;     // recent jobs, for job() / wait()
     std::vector<std::shared_ptr<Job>> running_;  // worker-side
     std::atomic<int> running_count_{0};
+    std::atomic<int64_t> load_{0};
     bool stop_ = false;
     std::thread worker_;
+    uint64_t counter_ = 0;
+};
+
+// Several engines (one per GPU) behind one job API.  Each shard is a BatchRuntime with its own
+// worker thread, so every GPU has its own scheduler thread and stream of engine calls; the
+// streams of an utterance never leave their GPU and no data crosses between GPUs.  A new job
+// goes to the shard with the least outstanding work (longest-processing-time greedy on
+// BatchRuntime::job_cost; a shard whose queue is full is passed over).  A voice prefix lives on
+// every shard: set_prefix registers its stream on each engine under one slot number, and a
+// request's prefix_stream names that slot.
+template <class Ops>
+class ShardedRuntime {
+public:
+    ShardedRuntime(const std::vector<Ops *> &engines, BatchRuntimeOptions opt) {
+        for (Ops *o : engines) rts_.push_back(std::make_unique<BatchRuntime<Ops>>(*o, opt));
+    }
+    int shards() const { return static_cast<int>(rts_.size()); }
+    BatchRuntime<Ops> &shard(int i) { return *rts_[static_cast<size_t>(i)]; }
+    void start() {
+        for (auto &r : rts_) r->start();
+    }
+    void shutdown() {
+        for (auto &r : rts_) r->shutdown();
+    }
+
+    // Prefix slot `slot`: stream stream_per_shard[i] on engine i, its first `len` positions.
+    void set_prefix(int slot, const std::vector<int> &stream_per_shard, int len) {
+        if (stream_per_shard.size() != rts_.size()) throw std::invalid_argument("one prefix stream per shard");
+        std::lock_guard<std::mutex> lock(mutex_);
+        prefixes_[slot] = {stream_per_shard, len};
+    }
+
+    // As BatchRuntime::submit; shard_out (may be null) receives the shard that took the job.
+    bool submit(const GenJobRequest &req, CodeSink sink, std::string *job_id, std::string *err,
+                int *shard_out = nullptr) {
+        std::vector<int> order(rts_.size());
+        for (size_t i = 0; i < order.size(); ++i) order[i] = static_cast<int>(i);
+        std::stable_sort(order.begin(), order.end(),
+                         [&](int a, int b) { return rts_[size_t(a)]->load() < rts_[size_t(b)]->load(); });
+        GenJobRequest r = req;
+        std::vector<int> prefix_streams;
+        {
+            std::lock_guard<std::mutex> lock(mutex_);
+            if (r.id.empty()) r.id = make_id_locked();
+            if (req.prefix_stream >= 0) {
+                auto it = prefixes_.find(req.prefix_stream);
+                if (it == prefixes_.end()) {
+                    if (err) *err = "unknown prefix slot";
+                    return false;
+                }
+                prefix_streams = it->second.first;
+                r.prefix_len = it->second.second;
+            }
+        }
+        std::string why = "busy";
+        for (int s : order) {
+            if (req.prefix_stream >= 0) r.prefix_stream = prefix_streams[static_cast<size_t>(s)];
+            std::string e;
+            if (rts_[static_cast<size_t>(s)]->submit(r, sink, job_id, &e)) {
+                std::lock_guard<std::mutex> lock(mutex_);
+                where_[r.id] = s;
+                prune_locked();
+                if (shard_out) *shard_out = s;
+                return true;
+            }
+            if (e != "busy") why = e;
+        }
+        if (err) *err = why;
+        return false;
+    }
+
+    bool wait(const std::string &id, int timeout_ms, GenJobInfo *out) {
+        const int s = find(id);
+        return s >= 0 && rts_[static_cast<size_t>(s)]->wait(id, timeout_ms, out);
+    }
+    bool job(const std::string &id, GenJobInfo *out) const {
+        const int s = find(id);
+        return s >= 0 && rts_[static_cast<size_t>(s)]->job(id, out);
+    }
+    bool cancel(const std::string &id) {
+        const int s = find(id);
+        return s >= 0 && rts_[static_cast<size_t>(s)]->cancel(id);
+    }
+    int queue_depth() const {
+        int d = 0;
+        for (auto &r : rts_) d += r->queue_depth();
+        return d;
+    }
+
+private:
+    int find(const std::string &id) const {
+        std::lock_guard<std::mutex> lock(mutex_);
+        auto it = where_.find(id);
+        return it == where_.end() ? -1 : it->second;
+    }
+    std::string make_id_locked() {
+        ++counter_;
+        char buf[40];
+        std::snprintf(buf, sizeof(buf), "s%08llx%04llx", static_cast<unsigned long long>(counter_),
+                      static_cast<unsigned long long>(std::chrono::steady_clock::now().time_since_epoch().count() & 0xFFFF));
+        return buf;
+    }
+    // forget jobs their shard no longer keeps (BatchRuntime keeps the recent kKeepJobs)
+    void prune_locked() {
+        if (where_.size() <= 4 * rts_.size() * BatchRuntime<Ops>::kKeepJobs) return;
+        for (auto it = where_.begin(); it != where_.end();)
+            it = rts_[static_cast<size_t>(it->second)]->job(it->first, nullptr) ? std::next(it) : where_.erase(it);
+    }
+
+    std::vector<std::unique_ptr<BatchRuntime<Ops>>> rts_;
+    mutable std::mutex mutex_;
+    std::map<int, std::pair<std::vector<int>, int>> prefixes_;
+    std::map<std::string, int> where_;
     uint64_t counter_ = 0;
 };
 

@@ -8,6 +8,7 @@
 
 #include <cstdio>
 #include <map>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -261,10 +262,16 @@ std::vector<GenJobRequest> mixed_jobs(int prefix_sid, int prefix_len) {
     return jobs;
 }
 
-struct Collected {
+struct Collected {  // sinks of several worker threads (one per shard) write here
     std::map<std::string, std::vector<Block>> blocks;
+    std::mutex mu;
     CodeSink sink_for(const std::string &key) {
+        {
+            std::lock_guard<std::mutex> lock(mu);
+            blocks[key];  // the entry exists before any worker writes
+        }
         return [this, key](int segment, const int32_t *codes, int n) {
+            std::lock_guard<std::mutex> lock(mu);
             blocks[key].push_back(Block{segment, std::vector<int32_t>(codes, codes + 16 * n)});
             return true;
         };
@@ -453,6 +460,58 @@ void test_worker_thread() {
     std::printf("D ok\n");
 }
 
+// E: two engines behind one ShardedRuntime: jobs spread by outstanding work, a voice prefix
+// registered on both, every job's blocks as if run alone, loads back to zero at the end.
+void test_sharded() {
+    FakeOps e0(16, 4096), e1(16, 4096), ref(16, 4096);
+    int busy = -1;
+    e1.open(&busy);  // stream 0 of engine 1 is taken, so its prefix gets another stream id
+    const int p0 = setup_prefix(e0, 9), p1 = setup_prefix(e1, 9), pref = setup_prefix(ref, 9);
+    CHECK(p0 == 0 && p1 == 1 && pref == 0, "prefix streams %d %d %d", p0, p1, pref);
+    ShardedRuntime<FakeOps> rt({&e0, &e1}, BatchRuntimeOptions{4, 16, 3});
+    rt.set_prefix(7, {p0, p1}, 9);
+    auto jobs = mixed_jobs(0, 9);
+    for (auto &j : jobs) {
+        if (j.prefix_stream >= 0) j.prefix_stream = 7;  // the slot
+        j.prefix_len = 0;
+    }
+    Collected got;
+    std::vector<std::string> ids(jobs.size());
+    std::vector<int> where(jobs.size(), -1);
+    int64_t cost[2] = {0, 0}, most = 0;
+    std::string err;
+    for (size_t i = 0; i < jobs.size(); ++i) {
+        CHECK(rt.submit(jobs[i], got.sink_for(std::to_string(i)), &ids[i], &err, &where[i]), "submit %zu: %s", i, err.c_str());
+        GenJobRequest as_run = jobs[i];
+        if (as_run.prefix_stream >= 0) as_run.prefix_len = 9;
+        const int64_t c = BatchRuntime<FakeOps>::job_cost(as_run);
+        cost[where[i]] += c;
+        most = std::max(most, c);
+    }
+    CHECK(rt.shard(0).load() == cost[0] && rt.shard(1).load() == cost[1], "loads before start");
+    CHECK(std::llabs(cost[0] - cost[1]) <= most, "unbalanced: %lld vs %lld", (long long)cost[0], (long long)cost[1]);
+    GenJobRequest bad = jobs[1];
+    bad.prefix_stream = 3;
+    std::string bid;
+    CHECK(!rt.submit(bad, nullptr, &bid, &err) && err == "unknown prefix slot", "unknown slot: %s", err.c_str());
+    rt.start();
+    for (size_t i = 0; i < jobs.size(); ++i) {
+        GenJobInfo info;
+        CHECK(rt.wait(ids[i], 20000, &info), "wait %zu", i);
+        CHECK(info.state == GenJobState::Completed, "sharded job %zu: %s", i, info.error.c_str());
+        GenJobRequest as_run = jobs[i];
+        if (as_run.prefix_stream >= 0) {
+            as_run.prefix_stream = pref;
+            as_run.prefix_len = 9;
+        }
+        CHECK(got.blocks[std::to_string(i)] == expected_blocks(ref, as_run), "sharded job %zu blocks", i);
+    }
+    rt.shutdown();
+    CHECK(rt.shard(0).load() == 0 && rt.shard(1).load() == 0, "loads after the end");
+    CHECK(e0.open_streams() == 1 && e1.open_streams() == 2, "streams left open");
+    std::printf("E shard0_cost=%lld shard1_cost=%lld\n", (long long)cost[0], (long long)cost[1]);
+}
+
 }  // namespace
 
 int main() {
@@ -460,6 +519,7 @@ int main() {
     test_queue_cancel_sink();
     test_failures_and_context_cap();
     test_worker_thread();
+    test_sharded();
     if (g_failures) {
         std::printf("%d failures\n", g_failures);
         return 1;

@@ -4,7 +4,8 @@ shared mossgpu_prefill_batch / mossgpu_step_frames calls, each job producing wha
 TtsEngine::synthesize's token loop produces for it (engine.cpp:415-545).
 
 CPU: the runtime over a host-only engine double, against a sequential restatement of the
-reference loop (tests/cpp/batch_runtime_test.cpp).  GPU: the runtime over the real engine
+reference loop, and ShardedRuntime over two doubles (one per GPU) with jobs balanced by
+outstanding work (tests/cpp/batch_runtime_test.cpp).  GPU: the runtime over the real engine
 through the C ABI (tests/cpp/batch_runtime_demo.cpp), against the same engine calls made
 directly through the Python API in the order the runtime makes them."""
 from __future__ import annotations
@@ -29,10 +30,13 @@ def test_batch_runtime_on_engine_double(tmp_path):
     r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
     assert r.returncode == 0, r.stdout + r.stderr
     lines = dict(line.split(" ", 1) for line in r.stdout.strip().splitlines())
-    assert set(lines) == {"A", "B", "C", "D"}
+    assert set(lines) == {"A", "B", "C", "D", "E"}
     stats = dict(kv.split("=") for kv in lines["A"].split())
     # jobs really shared calls: several segments per prefill call, several streams per step call
     assert int(stats["prefill_max"]) > 1 and int(stats["step_max"]) > 1
+    # two engines behind ShardedRuntime: both took work
+    shards = dict(kv.split("=") for kv in lines["E"].split())
+    assert int(shards["shard0_cost"]) > 0 and int(shards["shard1_cost"]) > 0
 
 
 # ---- GPU: the runtime over the engine, replayed through the Python API
