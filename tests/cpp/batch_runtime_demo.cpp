@@ -1,17 +1,21 @@
 // BatchRuntime over the real engine (MossGpuOps, the C ABI): reads a job file, runs every job
 // through the runtime's worker thread, and writes what each job's sink received.
 //
-//   batch_runtime_demo <weights.moss> <jobs.bin> <out.txt> <max_active> <frames_per_call>
+//   batch_runtime_demo <weights.moss> <jobs.bin> <out.txt> <max_active> <frames_per_call> [n_gpus]
+//
+// With n_gpus > 1 the jobs go through ShardedRuntime over one engine per GPU (devices
+// 0..n_gpus-1), the prefix prefilled on each and registered as slot 0.
 //
 // jobs.bin (int32 little endian): n_jobs, prefix_m, prefix rows [prefix_m][17], then per job
 // seed, greedy, rep_x1000, min_frames, max_frames, chunk_frames, use_prefix, m, rows [m][17].
-// out.txt: per job "job <i> <state> <frames>", then one "blk <segment> <n> <16 n codes>" line
+// out.txt: per job "job <i> <state> <frames> <shard>", then one "blk <segment> <n> <16 n codes>" line
 // per block.  Exit 0 when every job ended (in any state), 2 on a load or input error.
 #include "batch_runtime.h"
 
 #include <cstdio>
 #include <cstdlib>
 #include <fstream>
+#include <memory>
 #include <string>
 #include <vector>
 
@@ -37,10 +41,12 @@ bool read_rows(std::ifstream &f, int m, std::vector<FrameRow> *rows) {
 }  // namespace
 
 int main(int argc, char **argv) {
-    if (argc != 6) {
-        std::fprintf(stderr, "usage: %s weights jobs.bin out.txt max_active frames_per_call\n", argv[0]);
+    if (argc != 6 && argc != 7) {
+        std::fprintf(stderr, "usage: %s weights jobs.bin out.txt max_active frames_per_call [n_gpus]\n", argv[0]);
         return 2;
     }
+    const int n_gpus = argc == 7 ? std::atoi(argv[6]) : 1;
+    if (n_gpus < 1 || n_gpus > 8) return 2;
     std::ifstream in(argv[2], std::ios::binary);
     int32_t hdr[2];
     if (!in || !read_ints(in, hdr, 2)) {
@@ -67,33 +73,51 @@ int main(int argc, char **argv) {
         if (!read_rows(in, v[7], &r.segments.back())) return 2;
     }
 
-    char err[1024] = {0};
-    mossgpu_engine *h = mossgpu_create(argv[1], 0, kMaxStreams, kMaxCtx, 0, err, sizeof(err));
-    if (!h) {
-        std::fprintf(stderr, "load failed: %s\n", err);
-        return 2;
-    }
-    int rc = 0;
-    {
-        int prefix_sid = -1;
+    std::vector<mossgpu_engine *> hs;
+    std::vector<int> prefix_sid;
+    for (int d = 0; d < n_gpus; ++d) {
+        char err[1024] = {0};
+        mossgpu_engine *h = mossgpu_create(argv[1], d, kMaxStreams, kMaxCtx, 0, err, sizeof(err));
+        if (!h) {
+            std::fprintf(stderr, "load failed on device %d: %s\n", d, err);
+            for (auto *o : hs) mossgpu_destroy(o);
+            return 2;
+        }
+        hs.push_back(h);
+        int sid = -1;
         if (!prefix.empty()) {
-            if (mossgpu_stream_open(h, &prefix_sid) != 0 ||
-                mossgpu_prefill(h, prefix_sid, prefix[0].data(), static_cast<int>(prefix.size()), 0) != 0) {
+            if (mossgpu_stream_open(h, &sid) != 0 ||
+                mossgpu_prefill(h, sid, prefix[0].data(), static_cast<int>(prefix.size()), 0) != 0) {
                 std::fprintf(stderr, "prefix: %s\n", mossgpu_last_error(h));
-                mossgpu_destroy(h);
+                for (auto *o : hs) mossgpu_destroy(o);
                 return 2;
             }
         }
+        prefix_sid.push_back(sid);
+    }
+    int rc = 0;
+    {
+        std::vector<MossGpuOps> ops;
+        for (auto *h : hs) ops.emplace_back(h, kMaxCtx);
+        const BatchRuntimeOptions opt{std::atoi(argv[4]), 64, std::atoi(argv[5])};
+        std::unique_ptr<BatchRuntime<MossGpuOps>> single;
+        std::unique_ptr<ShardedRuntime<MossGpuOps>> sharded;
+        if (n_gpus == 1) {
+            single = std::make_unique<BatchRuntime<MossGpuOps>>(ops[0], opt);
+        } else {
+            std::vector<MossGpuOps *> ptrs;
+            for (auto &o : ops) ptrs.push_back(&o);
+            sharded = std::make_unique<ShardedRuntime<MossGpuOps>>(ptrs, opt);
+            sharded->set_prefix(0, prefix_sid, static_cast<int>(prefix.size()));
+        }
         for (size_t i = 0; i < jobs.size(); ++i)
             if (use_prefix[i]) {
-                jobs[i].prefix_stream = prefix_sid;
+                jobs[i].prefix_stream = single ? prefix_sid[0] : 0;  // sharded: the slot
                 jobs[i].prefix_len = static_cast<int>(prefix.size());
             }
-
-        MossGpuOps ops(h, kMaxCtx);
-        BatchRuntime<MossGpuOps> rt(ops, BatchRuntimeOptions{std::atoi(argv[4]), 64, std::atoi(argv[5])});
         std::vector<std::vector<std::string>> blocks(jobs.size());
         std::vector<std::string> ids(jobs.size());
+        std::vector<int> shard(jobs.size(), 0);
         for (size_t i = 0; i < jobs.size(); ++i) {
             std::string e;
             auto sink = [&blocks, i](int segment, const int32_t *codes, int n) {
@@ -102,26 +126,35 @@ int main(int argc, char **argv) {
                 blocks[i].push_back(line);
                 return true;
             };
-            if (!rt.submit(jobs[i], sink, &ids[i], &e)) {
+            const bool ok = single ? single->submit(jobs[i], sink, &ids[i], &e)
+                                   : sharded->submit(jobs[i], sink, &ids[i], &e, &shard[i]);
+            if (!ok) {
                 std::fprintf(stderr, "submit %zu: %s\n", i, e.c_str());
                 rc = 2;
             }
         }
-        rt.start();
+        if (single)
+            single->start();
+        else
+            sharded->start();
         std::ofstream out(argv[3]);
         for (size_t i = 0; i < jobs.size() && rc == 0; ++i) {
             GenJobInfo info;
-            if (!rt.wait(ids[i], 120000, &info)) {
+            const bool ended = single ? single->wait(ids[i], 120000, &info) : sharded->wait(ids[i], 120000, &info);
+            if (!ended) {
                 std::fprintf(stderr, "job %zu did not end\n", i);
                 rc = 2;
                 break;
             }
-            out << "job " << i << " " << gen_job_state_name(info.state) << " " << info.frames << "\n";
+            out << "job " << i << " " << gen_job_state_name(info.state) << " " << info.frames << " " << shard[i] << "\n";
             if (!info.error.empty()) std::fprintf(stderr, "job %zu: %s\n", i, info.error.c_str());
             for (auto &l : blocks[i]) out << l << "\n";
         }
-        rt.shutdown();
+        if (single)
+            single->shutdown();
+        else
+            sharded->shutdown();
     }
-    mossgpu_destroy(h);
+    for (auto *h : hs) mossgpu_destroy(h);
     return rc;
 }

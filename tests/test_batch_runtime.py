@@ -148,3 +148,70 @@ def test_batch_runtime_on_engine_matches_direct_calls(tmp_path, weights_path):
             assert (frames == want[i]).all(), i
         total += n_frames
     assert total > 0
+
+
+# Two GPUs, one process: ShardedRuntime over an engine per device.  Every job has the same cost
+# (no prefix, 24 prompt rows, 10 frames), so the least-loaded rule alternates: even jobs on
+# GPU 0, odd jobs on GPU 1.  Each GPU's jobs are then replayed directly on that device.
+JOBS2 = [(31 + i, int(i % 4 < 2), 1200, 2, 10, 4 + i % 3, 0, 24) for i in range(8)]
+
+
+@pytest.mark.gpu
+def test_sharded_runtime_on_two_gpus_matches_direct_calls(tmp_path, weights_path):
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import moss_b200 as pkg
+    pkg.build()
+    exe = tmp_path / "batch_runtime_demo"
+    subprocess.run([*CXX, str(ROOT / "tests" / "cpp" / "batch_runtime_demo.cpp"), "-L", str(PKG), "-lmossgpu",
+                    f"-Wl,-rpath,{PKG}", "-o", str(exe)], check=True, capture_output=True, text=True)
+    prefix = prompt_rows(PREFIX_M, seed=71)
+    rows = [prompt_rows(job[7], seed=90 + i) for i, job in enumerate(JOBS2)]
+    ints = [len(JOBS2), PREFIX_M, *prefix.reshape(-1).tolist()]
+    for job, r in zip(JOBS2, rows):
+        ints += [*job[:7], r.shape[0], *r.reshape(-1).tolist()]
+    np.asarray(ints, np.int32).tofile(tmp_path / "jobs.bin")
+    r = subprocess.run([str(exe), weights_path, str(tmp_path / "jobs.bin"), str(tmp_path / "out.txt"), "8",
+                        str(FRAMES_PER_CALL), "2"], capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr
+    text = (tmp_path / "out.txt").read_text()
+    shard_of = {int(l.split()[1]): int(l.split()[4]) for l in text.splitlines() if l.startswith("job ")}
+    assert shard_of == {i: i % 2 for i in range(len(JOBS2))}
+    got = parse_output(text)
+
+    want = {}
+    for dev in (0, 1):
+        mine = [i for i in range(len(JOBS2)) if i % 2 == dev]
+        e = pkg.Engine(weights_path, device=dev, max_streams=MAX_STREAMS, max_ctx=MAX_CTX)
+        try:
+            p0 = e.open()
+            e.prefill(p0, prefix)
+            sids = [e.open() for _ in mine]
+            e.prefill_batch(sids, [rows[i] for i in mine], starts=[0] * len(mine))
+            for s, i in zip(sids, mine):
+                e.generate_begin(s, JOBS2[i][0])
+            groups = []
+            for k, i in enumerate(mine):
+                key = JOBS2[i][1:5]
+                for g in groups:
+                    if g[0] == key:
+                        g[1].append(k)
+                        break
+                else:
+                    groups.append((key, [k]))
+            for key, members in groups:
+                frames = min(FRAMES_PER_CALL, *(JOBS2[mine[k]][4] for k in members))
+                codes, done = e.step_frames([sids[k] for k in members], params_for(pkg, JOBS2[mine[members[0]]]),
+                                            frames)
+                for c, k in enumerate(members):
+                    want[mine[k]] = codes[: int(done[c]), c, :]
+        finally:
+            e.close()
+    for i in range(len(JOBS2)):
+        assert got[i]["state"] == "completed", (i, got[i]["state"])
+        n = want[i].shape[0]
+        assert got[i]["frames"] == n
+        if n:
+            frames = np.concatenate([c.T for _, c in got[i]["blocks"]], axis=0)
+            assert (frames == want[i]).all(), i
