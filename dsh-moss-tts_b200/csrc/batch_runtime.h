@@ -113,6 +113,12 @@ struct BatchRuntimeOptions {
     int max_active = 64;       // jobs advanced together; each holds one engine stream
     int max_queue = 4;         // queued (not yet admitted) jobs before submit answers "busy"
     int frames_per_call = 8;   // frames per mossgpu_step_frames call (1..1024)
+    // Admission hold: while other jobs run, queued jobs wait until admit_min of them are
+    // queued or the oldest has waited admit_wait_ms, so that more new segments share one
+    // prefill pass (at the cost of their first codes' latency).  An idle runtime admits at
+    // once.  admit_min <= 1: no hold.
+    int admit_min = 1;
+    int admit_wait_ms = 0;
 };
 
 // The engine through the C ABI.
@@ -370,7 +376,9 @@ private:
         std::vector<std::shared_ptr<Job>> admitted;
         {
             std::lock_guard<std::mutex> lock(mutex_);
-            while (!queue_.empty() && static_cast<int>(running_.size() + admitted.size()) < opt_.max_active) {
+            const bool hold = !running_.empty() && !queue_.empty() && static_cast<int>(queue_.size()) < opt_.admit_min &&
+                              ms_since(queue_.front()->submitted) < static_cast<double>(opt_.admit_wait_ms);
+            while (!hold && !queue_.empty() && static_cast<int>(running_.size() + admitted.size()) < opt_.max_active) {
                 auto j = queue_.front();
                 queue_.pop_front();
                 did = true;

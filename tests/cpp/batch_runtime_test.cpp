@@ -512,6 +512,47 @@ void test_sharded() {
     std::printf("E shard0_cost=%lld shard1_cost=%lld\n", (long long)cost[0], (long long)cost[1]);
 }
 
+// F: the admission hold groups late arrivals into one prefill pass.
+void test_admission_hold() {
+    FakeOps eng(16, 4096);
+    BatchRuntimeOptions opt{8, 16, 2};
+    opt.admit_min = 3;
+    opt.admit_wait_ms = 600000;  // never expires within the test
+    BatchRuntime<FakeOps> rt(eng, opt);
+    GenJobRequest r;
+    r.segments.push_back(rows_of(5, 11));
+    r.min_frames = 1000;
+    r.max_frames = 1000;
+    std::string a, b, c, d, err;
+    rt.submit(r, nullptr, &a, &err);
+    rt.run_once();  // idle: admitted at once
+    CHECK(rt.running() == 1 && eng.prefill_n.size() == 1, "idle runtime admits at once");
+    rt.submit(r, nullptr, &b, &err);
+    rt.submit(r, nullptr, &c, &err);
+    rt.run_once();
+    CHECK(rt.queue_depth() == 2 && rt.running() == 1, "two queued jobs are held");
+    rt.submit(r, nullptr, &d, &err);
+    rt.run_once();
+    CHECK(rt.queue_depth() == 0 && rt.running() == 4, "the third releases them");
+    CHECK(eng.prefill_n.size() == 2 && eng.prefill_n.back() == 3, "one prefill call for the three");
+    for (const std::string &id : {a, b, c, d}) rt.cancel(id);
+    drain(rt);
+    CHECK(eng.open_streams() == 0, "streams left open");
+
+    // no hold by default
+    FakeOps eng2(16, 4096);
+    BatchRuntime<FakeOps> rt2(eng2, BatchRuntimeOptions{8, 16, 2});
+    rt2.submit(r, nullptr, &a, &err);
+    rt2.run_once();
+    rt2.submit(r, nullptr, &b, &err);
+    rt2.run_once();
+    CHECK(rt2.running() == 2 && eng2.prefill_n.size() == 2, "default admits every iteration");
+    rt2.cancel(a);
+    rt2.cancel(b);
+    drain(rt2);
+    std::printf("F ok\n");
+}
+
 }  // namespace
 
 int main() {
@@ -520,6 +561,7 @@ int main() {
     test_failures_and_context_cap();
     test_worker_thread();
     test_sharded();
+    test_admission_hold();
     if (g_failures) {
         std::printf("%d failures\n", g_failures);
         return 1;

@@ -30,7 +30,7 @@ def test_batch_runtime_on_engine_double(tmp_path):
     r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
     assert r.returncode == 0, r.stdout + r.stderr
     lines = dict(line.split(" ", 1) for line in r.stdout.strip().splitlines())
-    assert set(lines) == {"A", "B", "C", "D", "E"}
+    assert set(lines) == {"A", "B", "C", "D", "E", "F"}
     stats = dict(kv.split("=") for kv in lines["A"].split())
     # jobs really shared calls: several segments per prefill call, several streams per step call
     assert int(stats["prefill_max"]) > 1 and int(stats["step_max"]) > 1
