@@ -35,6 +35,8 @@
 //
 // Ops is the engine: MossGpuOps below (the C ABI of mossgpu.h) or a test double with the same
 // members.  Use either start() (a worker thread) or run_once() from one thread, not both.
+// Once the worker runs, the engine is the worker's: open and prefill prefix streams before
+// start(), since calls on one engine must not overlap.
 #pragma once
 
 #include <algorithm>

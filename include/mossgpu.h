@@ -15,6 +15,10 @@
  * Streams: one "stream" is one utterance's LLM state (global KV, last hidden, local
  * decoder state, repetition-penalty history).  mossgpu_step() advances any set of open
  * streams by one audio frame in one batched pass.
+ *
+ * Threads: calls on one engine must not overlap; any thread may make them, and each call
+ * first makes the engine's device current on the calling thread.  Different engines (one
+ * per GPU) may be called concurrently from different threads.
  */
 #ifndef MOSSGPU_H
 #define MOSSGPU_H
