@@ -29,8 +29,8 @@ OUT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "oracle"))
 sys.path.insert(0, str(ROOT / "tests"))
 
-from golden_inputs import (WEIGHTS_SEED, global_state, prompt_rows, forced_codes, sampler_case,  # noqa: E402
-                           sha)
+from golden_inputs import (SAMPLER_SWEEP, WEIGHTS_SEED, global_state, prompt_rows, forced_codes,  # noqa: E402
+                           sampler_case, sampler_sweep_case, sha)
 
 REF_ROOT = Path(os.environ.get("REF_ROOT", "/root/reference"))
 
@@ -161,6 +161,20 @@ def decode_fixture(weights: Path):
     np.savez_compressed(OUT / "decode.npz", **out)
 
 
+def sampler_sweep_fixture():
+    """The reference's sample_token (sampler.cpp:9-77) over SAMPLER_SWEEP seeded cases of its
+    parameter space (golden_inputs.sampler_sweep_case); only the picks are stored."""
+    import ctypes
+    from oracle_py import RefModel
+    lib = RefModel.lib("decode")
+    picks = []
+    for case in range(SAMPLER_SWEEP):
+        logits, prev, greedy, t, k, p, rep, seed = sampler_sweep_case(case)
+        picks.append(lib.ref_sample_token(logits, logits.size, greedy, t, k, p, rep,
+                                          prev.ctypes.data_as(ctypes.c_void_p), prev.size, seed))
+    np.savez_compressed(OUT / "sampler_sweep.npz", picks=np.array(picks, np.int32))
+
+
 def prefill_a16_fixture(weights: Path):
     """MOSS_A16=all is read once per process, so this runs in its own interpreter."""
     from oracle_py import RefModel
@@ -182,6 +196,9 @@ def main():
     if len(sys.argv) > 1 and sys.argv[1] == "--a16-prefill":
         prefill_a16_fixture(weights)
         return
+    if len(sys.argv) > 1 and sys.argv[1] == "--sampler-sweep":
+        sampler_sweep_fixture()
+        return
     ex = reference_export_module()
     # the synthetic-weight writer must produce the reference writer's bytes
     rng = np.random.default_rng(0)
@@ -191,6 +208,7 @@ def main():
                                                    "sha256": digest}, indent=1) + "\n")
     format_fixture(weights)
     decode_fixture(weights)
+    sampler_sweep_fixture()
     subprocess.run([sys.executable, __file__, "--a16-prefill"], check=True)
     for p in sorted(OUT.glob("*.npz")):
         print(p.name, p.stat().st_size)

@@ -57,3 +57,24 @@ def sampler_case(case: int):
     prev = np.concatenate([rng.integers(0, CODEBOOK, 12), [top, top, top]]).astype(np.int32)
     greedy = int(case % 2 == 0)
     return logits, prev, greedy, 1000 + case
+
+
+SAMPLER_SWEEP = 400
+
+
+def sampler_sweep_case(case: int):
+    """(logits[1024], history, greedy, temperature, top_k, top_p, penalty, seed): the sampler
+    over its parameter space -- peaked to near-uniform logits, histories of 0-299 codes,
+    temperature 0 (no scaling) to 1.5, top-k none / 1 / 5 / 25 / all / above the codebook,
+    top-p 0 (keep one) to 1 (no cut), penalties below, at and above 1.  Random logits, so no
+    two candidates tie."""
+    rng = np.random.default_rng(2000 + case)
+    scale = (0.01, 0.5, 2.0, 8.0, 30.0)[case % 5]
+    logits = (rng.standard_normal(CODEBOOK) * scale).astype(np.float32)
+    prev = rng.integers(0, CODEBOOK, int(rng.integers(0, 300))).astype(np.int32)
+    greedy = int(rng.random() < 0.2)
+    temperature = (0.5, 0.8, 1.0, 1.5, 0.0)[int(rng.integers(0, 5))]
+    top_k = (0, 1, 5, 25, 1024, 5000)[int(rng.integers(0, 6))]
+    top_p = (0.0, 0.3, 0.95, 1.0)[int(rng.integers(0, 4))]
+    penalty = (1.0, 1.2, 0.9)[int(rng.integers(0, 3))]
+    return logits, prev, greedy, temperature, top_k, top_p, penalty, 5000 + case

@@ -12,7 +12,7 @@ from pathlib import Path
 import numpy as np
 import pytest
 
-from golden_inputs import forced_codes, global_state, prompt_rows, sampler_case, sha
+from golden_inputs import SAMPLER_SWEEP, forced_codes, global_state, prompt_rows, sampler_case, sampler_sweep_case, sha
 from oracle_py import Oracle, lib, sample_params
 
 G = Path(__file__).resolve().parent / "golden"
@@ -147,6 +147,24 @@ def test_sampler_cases(dec):
         p = sample_params(greedy=bool(greedy))
         got = L.or_sample_token(logits, logits.size, C.byref(p), prev.ctypes.data_as(C.c_void_p), prev.size, rng)
         assert got == dec["sampler_picks"][case]
+
+
+def test_sampler_over_its_parameter_space():
+    """400 seeded cases (temperature 0-1.5, top-k none..above the codebook, top-p 0..1,
+    penalties 0.9-1.2, histories of 0-299 codes, peaked to flat logits) against the
+    reference's sample_token.  The logits are random, so no two candidates tie: with exact
+    ties the reference orders candidates by its standard library's unstable sort, which the
+    restatement does not reproduce (it orders ties by index)."""
+    picks = np.load(G / "sampler_sweep.npz")["picks"]
+    assert picks.size == SAMPLER_SWEEP
+    L = lib()
+    for case in range(SAMPLER_SWEEP):
+        logits, prev, greedy, t, k, p, rep, seed = sampler_sweep_case(case)
+        rng = np.zeros(4, np.uint32)
+        L.or_rng_seed(rng, seed)
+        sp = sample_params(greedy=bool(greedy), temperature=t, top_k=k, top_p=p, rep=rep)
+        got = L.or_sample_token(logits, logits.size, C.byref(sp), prev.ctypes.data_as(C.c_void_p), prev.size, rng)
+        assert got == picks[case], case
 
 
 def test_prefill_a16_bitexact(weights_path, weights_digest_ok):
