@@ -29,8 +29,8 @@ OUT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "oracle"))
 sys.path.insert(0, str(ROOT / "tests"))
 
-from golden_inputs import (SAMPLER_SWEEP, WEIGHTS_SEED, global_state, prompt_rows, forced_codes,  # noqa: E402
-                           sampler_case, sampler_sweep_case, sha)
+from golden_inputs import (LONG_CTX, SAMPLER_SWEEP, WEIGHTS_SEED, global_state, prompt_rows,  # noqa: E402
+                           forced_codes, sampler_case, sampler_sweep_case, sha)
 
 REF_ROOT = Path(os.environ.get("REF_ROOT", "/root/reference"))
 
@@ -161,6 +161,25 @@ def decode_fixture(weights: Path):
     np.savez_compressed(OUT / "decode.npz", **out)
 
 
+def long_ctx_fixture(weights: Path):
+    """One global step at L = 4000 injected positions (RoPE rows near the end of a 4608
+    context, a 4001-position attention), then one row step: the long-form configs' lengths."""
+    from oracle_py import RefModel
+    ref = RefModel(weights, threads=4, a16_mode="decode")
+    k, v, h0, x = global_state(LONG_CTX, seed=11)
+    out = {"inputs_sha": sha(k) + sha(v) + sha(h0) + sha(x)}
+    ref.set_state(k, v, h0)
+    out["hidden1"] = ref.global_step_embed(x)
+    for layer in (0, 11):
+        kk, vv = ref.kv(layer, LONG_CTX, 1)
+        out[f"k{layer}"], out[f"v{layer}"] = kk[0], vv[0]
+    row = np.array([9] + list(range(7, 1024, 64)), np.int32)
+    out["row"] = row
+    out["hidden2"] = ref.global_step_row(row)
+    out["position"] = np.int32(ref.position)
+    np.savez_compressed(OUT / "long_ctx.npz", **out)
+
+
 def sampler_sweep_fixture():
     """The reference's sample_token (sampler.cpp:9-77) over SAMPLER_SWEEP seeded cases of its
     parameter space (golden_inputs.sampler_sweep_case); only the picks are stored."""
@@ -199,6 +218,9 @@ def main():
     if len(sys.argv) > 1 and sys.argv[1] == "--sampler-sweep":
         sampler_sweep_fixture()
         return
+    if len(sys.argv) > 1 and sys.argv[1] == "--long-ctx":
+        long_ctx_fixture(weights)
+        return
     ex = reference_export_module()
     # the synthetic-weight writer must produce the reference writer's bytes
     rng = np.random.default_rng(0)
@@ -209,6 +231,7 @@ def main():
     format_fixture(weights)
     decode_fixture(weights)
     sampler_sweep_fixture()
+    long_ctx_fixture(weights)
     subprocess.run([sys.executable, __file__, "--a16-prefill"], check=True)
     for p in sorted(OUT.glob("*.npz")):
         print(p.name, p.stat().st_size)

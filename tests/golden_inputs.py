@@ -60,6 +60,7 @@ def sampler_case(case: int):
 
 
 SAMPLER_SWEEP = 400
+LONG_CTX = 4000  # injected positions of the long-context global-step fixture
 
 
 def sampler_sweep_case(case: int):

@@ -12,7 +12,8 @@ from pathlib import Path
 import numpy as np
 import pytest
 
-from golden_inputs import SAMPLER_SWEEP, forced_codes, global_state, prompt_rows, sampler_case, sampler_sweep_case, sha
+from golden_inputs import (LONG_CTX, SAMPLER_SWEEP, forced_codes, global_state, prompt_rows, sampler_case,
+                           sampler_sweep_case, sha)
 from oracle_py import Oracle, lib, sample_params
 
 G = Path(__file__).resolve().parent / "golden"
@@ -109,6 +110,23 @@ def test_global_step_bitexact(dec, weights_path, weights_digest_ok):
     assert np.array_equal(l0, dec["lc_out0"])
     assert np.array_equal(o.gate(l0), dec["lc_gate"])
     assert np.array_equal(o.audio_logits(0, o.local_step(1, dec["gs_embed_row"])), dec["lc_logits0"])
+
+
+def test_long_context_global_step_bitexact(weights_path, weights_digest_ok):
+    """L = 4000 injected positions: RoPE rows near the end of the context and a 4001-position
+    attention, then a row step (the long-form configs' lengths)."""
+    g = np.load(G / "long_ctx.npz")
+    o = Oracle(weights_path, max_ctx=LONG_CTX + 8)
+    k, v, h0, x = global_state(LONG_CTX, seed=11)
+    assert sha(k) + sha(v) + sha(h0) + sha(x) == str(g["inputs_sha"])
+    o.set_state(k, v, h0)
+    del k, v
+    assert np.array_equal(o.global_step_embed(x), g["hidden1"])
+    for layer in (0, 11):
+        kk, vv = o.kv(layer, LONG_CTX, 1)
+        assert np.array_equal(kk[0], g[f"k{layer}"]) and np.array_equal(vv[0], g[f"v{layer}"])
+    assert np.array_equal(o.global_step_row(g["row"]), g["hidden2"])
+    assert o.position == int(g["position"]) == LONG_CTX + 2
 
 
 def test_teacher_forced_generate_bitexact(dec, weights_path, weights_digest_ok):
