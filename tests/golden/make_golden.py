@@ -29,7 +29,7 @@ OUT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "oracle"))
 sys.path.insert(0, str(ROOT / "tests"))
 
-from golden_inputs import (LONG_CTX, SAMPLER_SWEEP, WEIGHTS_SEED, global_state, prompt_rows,  # noqa: E402
+from golden_inputs import (END_SEEDS, LONG_CTX, SAMPLER_SWEEP, WEIGHTS_SEED, global_state, prompt_rows,  # noqa: E402
                            forced_codes, sampler_case, sampler_sweep_case, sha)
 
 REF_ROOT = Path(os.environ.get("REF_ROOT", "/root/reference"))
@@ -180,6 +180,26 @@ def long_ctx_fixture(weights: Path):
     np.savez_compressed(OUT / "long_ctx.npz", **out)
 
 
+def end_decision_fixture(weights: Path):
+    """generate() with the sampled end decision (end_greedy = 0: one draw per frame against
+    p(slot), llm.cpp:30-35) for three seeds, and with greedy_frames = 3 (the first frames
+    greedy, then sampled codes, llm.cpp:682-684), after the 40-row prompt."""
+    from oracle_py import RefModel
+    rows = prompt_rows(40, seed=3)
+    out = {}
+    for seed in END_SEEDS:
+        ref = RefModel(weights, threads=4, a16_mode="decode")
+        ref.prefill_rows(rows)
+        codes, _ = ref.generate(24, greedy=True, rep=1.2, end_greedy=False, min_frames=1, seed=seed)
+        out[f"se_codes_{seed}"] = codes
+    ref = RefModel(weights, threads=4, a16_mode="decode")
+    ref.prefill_rows(rows)
+    codes, _ = ref.generate(8, greedy=False, temperature=0.8, top_k=25, top_p=0.95, rep=1.2, min_frames=99,
+                            greedy_frames=3, seed=5)
+    out["gf_codes"] = codes
+    np.savez_compressed(OUT / "end_decision.npz", **out)
+
+
 def sampler_sweep_fixture():
     """The reference's sample_token (sampler.cpp:9-77) over SAMPLER_SWEEP seeded cases of its
     parameter space (golden_inputs.sampler_sweep_case); only the picks are stored."""
@@ -221,6 +241,9 @@ def main():
     if len(sys.argv) > 1 and sys.argv[1] == "--long-ctx":
         long_ctx_fixture(weights)
         return
+    if len(sys.argv) > 1 and sys.argv[1] == "--end-decision":
+        end_decision_fixture(weights)
+        return
     ex = reference_export_module()
     # the synthetic-weight writer must produce the reference writer's bytes
     rng = np.random.default_rng(0)
@@ -232,6 +255,7 @@ def main():
     decode_fixture(weights)
     sampler_sweep_fixture()
     long_ctx_fixture(weights)
+    end_decision_fixture(weights)
     subprocess.run([sys.executable, __file__, "--a16-prefill"], check=True)
     for p in sorted(OUT.glob("*.npz")):
         print(p.name, p.stat().st_size)

@@ -12,7 +12,7 @@ from pathlib import Path
 import numpy as np
 import pytest
 
-from golden_inputs import (LONG_CTX, SAMPLER_SWEEP, forced_codes, global_state, prompt_rows, sampler_case,
+from golden_inputs import (END_SEEDS, LONG_CTX, SAMPLER_SWEEP, forced_codes, global_state, prompt_rows, sampler_case,
                            sampler_sweep_case, sha)
 from oracle_py import Oracle, lib, sample_params
 
@@ -165,6 +165,25 @@ def test_sampler_cases(dec):
         p = sample_params(greedy=bool(greedy))
         got = L.or_sample_token(logits, logits.size, C.byref(p), prev.ctypes.data_as(C.c_void_p), prev.size, rng)
         assert got == dec["sampler_picks"][case]
+
+
+def test_sampled_end_decision_and_greedy_frames(weights_path, weights_digest_ok):
+    """end_greedy = 0 (one draw per frame against p(slot), llm.cpp:30-35) for three seeds, and
+    greedy_frames = 3 ahead of sampled codes, after the 40-row prompt: the same frames as the
+    reference's generate()."""
+    g = np.load(G / "end_decision.npz")
+    rows = prompt_rows(40, seed=3)
+    for seed in END_SEEDS:
+        o = Oracle(weights_path, max_ctx=256)
+        o.prefill_rows(rows)
+        codes, _, _ = o.generate(24, sample_params(greedy=True, rep=1.2, end_greedy=False, min_frames=1), seed=seed)
+        want = g[f"se_codes_{seed}"]
+        assert codes.shape == want.shape and np.array_equal(codes, want), seed
+    o = Oracle(weights_path, max_ctx=256)
+    o.prefill_rows(rows)
+    codes, _, _ = o.generate(8, sample_params(greedy=False, temperature=0.8, top_k=25, top_p=0.95, rep=1.2,
+                                              min_frames=99, greedy_frames=3), seed=5)
+    assert np.array_equal(codes, g["gf_codes"])
 
 
 def test_sampler_over_its_parameter_space():
