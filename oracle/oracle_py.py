@@ -232,6 +232,8 @@ class RefModel:
             lib.ref_quantize_act.argtypes = [_f32p, C.c_int, _i8p, _f32p]
             lib.ref_half_to_float_n.argtypes = [np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS"), C.c_int, _f32p]
             lib.ref_float_to_half_n.argtypes = [_f32p, C.c_int, np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")]
+            lib.ref_save_prefix.restype = C.c_int
+            lib.ref_save_prefix.argtypes = [C.c_void_p, C.c_char_p, _i32p, C.c_int]
             lib.ref_sample_token.restype = C.c_int
             lib.ref_sample_token.argtypes = [_f32p, C.c_int, C.c_int, C.c_float, C.c_int, C.c_float, C.c_float,
                                              C.c_void_p, C.c_int, C.c_uint64]
@@ -291,6 +293,12 @@ class RefModel:
     def prefill_rows(self, rows, start=0):
         rows = np.ascontiguousarray(rows, np.int32)
         self.lib.ref_prefill_rows(self.h, rows, rows.shape[0], start)
+
+    def save_prefix(self, path, rows):
+        """LlmModel::save_prefix (llm.cpp:485-509): the reference's .mosskv file."""
+        rows = np.ascontiguousarray(rows, np.int32)
+        if not self.lib.ref_save_prefix(self.h, str(path).encode(), rows, rows.shape[0]):
+            raise RuntimeError("reference save_prefix failed")
 
     def local_step(self, lpos, x):
         out = np.empty(HIDDEN, np.float32)

@@ -66,6 +66,16 @@ void ref_prefill_rows(void *h, const int32_t *rows, int n, int start) {
     static_cast<LlmModel *>(h)->prefill(r, start);
 }
 
+// LlmModel::save_prefix (llm.cpp:485-509): the reference's own .mosskv writer, for the
+// prefix-file interchange fixture.  Returns 1 on success.
+int ref_save_prefix(void *h, const char *path, const int32_t *rows, int n) {
+    std::vector<Row> r(static_cast<size_t>(n));
+    for (int i = 0; i < n; ++i)
+        for (int j = 0; j < kNVq + 1; ++j) r[i][j] = rows[static_cast<size_t>(i) * 17 + j];
+    std::string err;
+    return static_cast<LlmModel *>(h)->save_prefix(path, r, &err) ? 1 : 0;
+}
+
 // llm.cpp:588-632 semantics (state injection) without the file round trip
 int ref_set_state(void *h, const float *k, const float *v, int n_pos, const float *hidden) {
     auto *m = static_cast<LlmModel *>(h);

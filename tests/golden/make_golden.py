@@ -29,7 +29,7 @@ OUT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "oracle"))
 sys.path.insert(0, str(ROOT / "tests"))
 
-from golden_inputs import (END_SEEDS, LONG_CTX, SAMPLER_SWEEP, WEIGHTS_SEED, global_state, prompt_rows,  # noqa: E402
+from golden_inputs import (END_SEEDS, LONG_CTX, PREFIX_FILE_ROWS, SAMPLER_SWEEP, WEIGHTS_SEED, global_state, prompt_rows,  # noqa: E402
                            forced_codes, sampler_case, sampler_sweep_case, sha)
 
 REF_ROOT = Path(os.environ.get("REF_ROOT", "/root/reference"))
@@ -200,6 +200,24 @@ def end_decision_fixture(weights: Path):
     np.savez_compressed(OUT / "end_decision.npz", **out)
 
 
+def prefix_file_fixture(weights: Path):
+    """The reference's .mosskv prefix file (save_prefix, llm.cpp:485-509) after a 3-row prompt:
+    its 40-byte header, the sha256 of its K/V payload, and the weights fingerprint input.  The
+    payload itself is not stored (216 KB): the oracle's prefill reproduces it."""
+    import hashlib
+    from oracle_py import RefModel
+    rows = prompt_rows(PREFIX_FILE_ROWS, seed=61)
+    ref = RefModel(weights, threads=4, a16_mode="decode")
+    ref.prefill_rows(rows)
+    path = Path(tempfile.gettempdir()) / "moss_golden_prefix.mosskv"
+    ref.save_prefix(path, rows)
+    data = path.read_bytes()
+    path.unlink()
+    np.savez_compressed(OUT / "prefix_file.npz", header=np.frombuffer(data[:40], np.uint8),
+                        payload_sha=np.array(hashlib.sha256(data[40:]).hexdigest()),
+                        size=np.int64(len(data)))
+
+
 def sampler_sweep_fixture():
     """The reference's sample_token (sampler.cpp:9-77) over SAMPLER_SWEEP seeded cases of its
     parameter space (golden_inputs.sampler_sweep_case); only the picks are stored."""
@@ -244,6 +262,9 @@ def main():
     if len(sys.argv) > 1 and sys.argv[1] == "--end-decision":
         end_decision_fixture(weights)
         return
+    if len(sys.argv) > 1 and sys.argv[1] == "--prefix-file":
+        prefix_file_fixture(weights)
+        return
     ex = reference_export_module()
     # the synthetic-weight writer must produce the reference writer's bytes
     rng = np.random.default_rng(0)
@@ -256,6 +277,7 @@ def main():
     sampler_sweep_fixture()
     long_ctx_fixture(weights)
     end_decision_fixture(weights)
+    prefix_file_fixture(weights)
     subprocess.run([sys.executable, __file__, "--a16-prefill"], check=True)
     for p in sorted(OUT.glob("*.npz")):
         print(p.name, p.stat().st_size)

@@ -62,6 +62,7 @@ def sampler_case(case: int):
 SAMPLER_SWEEP = 400
 LONG_CTX = 4000  # injected positions of the long-context global-step fixture
 END_SEEDS = (3, 17, 99)  # generator seeds of the sampled-end-decision fixture
+PREFIX_FILE_ROWS = 3  # prompt rows of the .mosskv interchange fixture
 
 
 def sampler_sweep_case(case: int):
