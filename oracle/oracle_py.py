@@ -234,6 +234,8 @@ class RefModel:
             lib.ref_float_to_half_n.argtypes = [_f32p, C.c_int, np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")]
             lib.ref_save_prefix.restype = C.c_int
             lib.ref_save_prefix.argtypes = [C.c_void_p, C.c_char_p, _i32p, C.c_int]
+            lib.ref_save_state.restype = C.c_int
+            lib.ref_save_state.argtypes = [C.c_void_p, C.c_char_p, _i32p, C.c_int]
             lib.ref_sample_token.restype = C.c_int
             lib.ref_sample_token.argtypes = [_f32p, C.c_int, C.c_int, C.c_float, C.c_int, C.c_float, C.c_float,
                                              C.c_void_p, C.c_int, C.c_uint64]
@@ -299,6 +301,12 @@ class RefModel:
         rows = np.ascontiguousarray(rows, np.int32)
         if not self.lib.ref_save_prefix(self.h, str(path).encode(), rows, rows.shape[0]):
             raise RuntimeError("reference save_prefix failed")
+
+    def save_state(self, path, rows):
+        """LlmModel::save_state (llm.cpp:561-587): header, K/V layer by layer, then hidden."""
+        rows = np.ascontiguousarray(rows, np.int32)
+        if not self.lib.ref_save_state(self.h, str(path).encode(), rows, rows.shape[0]):
+            raise RuntimeError("reference save_state failed")
 
     def local_step(self, lpos, x):
         out = np.empty(HIDDEN, np.float32)

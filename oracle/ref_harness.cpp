@@ -76,6 +76,15 @@ int ref_save_prefix(void *h, const char *path, const int32_t *rows, int n) {
     return static_cast<LlmModel *>(h)->save_prefix(path, r, &err) ? 1 : 0;
 }
 
+// LlmModel::save_state (llm.cpp:561-587): the reference's state-file writer.  Returns 1 on success.
+int ref_save_state(void *h, const char *path, const int32_t *rows, int n) {
+    std::vector<Row> r(static_cast<size_t>(n));
+    for (int i = 0; i < n; ++i)
+        for (int j = 0; j < kNVq + 1; ++j) r[i][j] = rows[static_cast<size_t>(i) * 17 + j];
+    std::string err;
+    return static_cast<LlmModel *>(h)->save_state(path, r, &err) ? 1 : 0;
+}
+
 // llm.cpp:588-632 semantics (state injection) without the file round trip
 int ref_set_state(void *h, const float *k, const float *v, int n_pos, const float *hidden) {
     auto *m = static_cast<LlmModel *>(h);

@@ -3,8 +3,8 @@
 // the file size and first 4 KB, llm.cpp:426-439), printed for comparison with a header the
 // reference's save_prefix wrote.  Host-only: no engine call is made, so no GPU is needed.
 //   prefix_header_test <weights.moss> <rows.bin [n][17] int32>
-// Prints "size <bytes> offsets <magic> <version> <layers> <n_pos> <hidden> <rows_fp> <weights_fp>"
-// and "fp <rows_fp> <weights_fp>".
+// Prints "size <bytes> offsets <magic> <version> <layers> <n_pos> <hidden> <rows_fp> <weights_fp>",
+// "fp <rows_fp> <weights_fp>" and "magic <prefix-file magic bytes> <state-file magic bytes>".
 #include <array>
 #include <atomic>
 #include <chrono>
@@ -36,5 +36,9 @@ int main(int argc, char **argv) {
                 offsetof(H, weights_fp));
     std::printf("fp %llu %llu\n", static_cast<unsigned long long>(moss::gpu::LlmModel::fp_rows(rows)),
                 static_cast<unsigned long long>(moss::gpu::LlmModel::fp_weights(argv[1])));
+    std::printf("magic");
+    for (const char *m : {moss::gpu::LlmModel::kKvMagic, moss::gpu::LlmModel::kStateMagic})
+        for (int i = 0; i < 8; ++i) std::printf(" %d", static_cast<int>(static_cast<unsigned char>(m[i])));
+    std::printf("\n");
     return 0;
 }

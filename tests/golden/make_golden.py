@@ -212,10 +212,14 @@ def prefix_file_fixture(weights: Path):
     path = Path(tempfile.gettempdir()) / "moss_golden_prefix.mosskv"
     ref.save_prefix(path, rows)
     data = path.read_bytes()
+    ref.save_state(path, rows)  # the debug state file: the same header and payload, then hidden
+    state = path.read_bytes()
     path.unlink()
     np.savez_compressed(OUT / "prefix_file.npz", header=np.frombuffer(data[:40], np.uint8),
                         payload_sha=np.array(hashlib.sha256(data[40:]).hexdigest()),
-                        size=np.int64(len(data)))
+                        size=np.int64(len(data)), state_header=np.frombuffer(state[:40], np.uint8),
+                        state_payload_sha=np.array(hashlib.sha256(state[40:]).hexdigest()),
+                        state_size=np.int64(len(state)))
 
 
 def sampler_sweep_fixture():

@@ -1,4 +1,5 @@
-""".mosskv prefix-file interchange with the reference (save_prefix / load_prefix, llm.cpp:441-550).
+""".mosskv prefix-file and state-file interchange with the reference (save_prefix / load_prefix /
+save_state / load_state, llm.cpp:441-632).
 
 tests/golden/prefix_file.npz holds the header and payload digest of a file written by the
 reference's own save_prefix after a 3-row prompt (tests/golden/make_golden.py).  Here:
@@ -54,6 +55,8 @@ def test_shim_header_and_fingerprints_match_the_reference(tmp_path, weights_path
     g = np.load(G / "prefix_file.npz")
     _, _, _, _, _, rows_fp, weights_fp = struct.unpack("<8s4I2Q", g["header"].tobytes())
     assert int(fp[1]) == rows_fp and int(fp[2]) == weights_fp
+    magic = [int(v) for v in out[2].split()[1:]]
+    assert bytes(magic[:8]) == g["header"].tobytes()[:8] and bytes(magic[8:]) == g["state_header"].tobytes()[:8]
 
 
 def test_payload_is_the_prompts_kv_layer_by_layer(weights_path, weights_digest_ok):
@@ -67,3 +70,24 @@ def test_payload_is_the_prompts_kv_layer_by_layer(weights_path, weights_digest_o
         h.update(k.astype("<f4").tobytes())
         h.update(v.astype("<f4").tobytes())
     assert h.hexdigest() == str(g["payload_sha"])
+
+
+def test_state_file_is_the_prefix_file_plus_hidden(weights_path, weights_digest_ok):
+    """save_state (llm.cpp:561-587): the prefix header with magic "MOSSST1", the same K/V payload,
+    then the last hidden state."""
+    g = np.load(G / "prefix_file.npz")
+    magic, version, layers, n_pos, hidden, rows_fp, weights_fp = struct.unpack("<8s4I2Q",
+                                                                               g["state_header"].tobytes())
+    assert magic == b"MOSSST1\0" and (version, layers, n_pos, hidden) == (1, 12, PREFIX_FILE_ROWS, 768)
+    assert g["state_header"].tobytes()[8:] == g["header"].tobytes()[8:]
+    assert int(g["state_size"]) == int(g["size"]) + 768 * 4
+    rows = prompt_rows(PREFIX_FILE_ROWS, seed=61)
+    o = Oracle(weights_path, max_ctx=64)
+    o.prefill_rows(rows)
+    h = hashlib.sha256()
+    for layer in range(12):
+        k, v = o.kv(layer, 0, PREFIX_FILE_ROWS)
+        h.update(k.astype("<f4").tobytes())
+        h.update(v.astype("<f4").tobytes())
+    h.update(o.hidden().astype("<f4").tobytes())
+    assert h.hexdigest() == str(g["state_payload_sha"])
