@@ -222,6 +222,35 @@ def prefix_file_fixture(weights: Path):
                         state_size=np.int64(len(state)))
 
 
+def prefill_continue_fixture(weights: Path):
+    """prefill(rows, start) (llm.cpp:327-401) in the product mode: 10 rows, then 7 more at
+    start = 10; and rows past the context limit, which prefill clamps to kMaxCtx - start
+    (llm.cpp:329-331): 20 rows at start = kMaxCtx - 8 after an injected state."""
+    from oracle_py import RefModel
+    out = {}
+    a, b = prompt_rows(10, seed=41), prompt_rows(7, seed=42)
+    ref = RefModel(weights, threads=4, a16_mode="decode")
+    ref.prefill_rows(a)
+    ref.prefill_rows(b, start=10)
+    out["cont_hidden"] = ref.hidden()
+    out["cont_position"] = np.int32(ref.position)
+    for layer in (0, 11):
+        kk, vv = ref.kv(layer, 10, 7)
+        out[f"cont_k{layer}"], out[f"cont_v{layer}"] = kk, vv
+    ref2 = RefModel(weights, threads=4, a16_mode="decode")
+    L = ref2.max_ctx - 8
+    k, v, h0, _ = global_state(L, seed=43)
+    ref2.set_state(k, v, h0)
+    del k, v
+    ref2.prefill_rows(prompt_rows(20, seed=44), start=L)
+    out["clamp_max_ctx"] = np.int32(ref2.max_ctx)
+    out["clamp_position"] = np.int32(ref2.position)
+    out["clamp_hidden"] = ref2.hidden()
+    kk, vv = ref2.kv(11, L, 8)
+    out["clamp_k11"], out["clamp_v11"] = kk, vv
+    np.savez_compressed(OUT / "prefill_continue.npz", **out)
+
+
 def sampler_sweep_fixture():
     """The reference's sample_token (sampler.cpp:9-77) over SAMPLER_SWEEP seeded cases of its
     parameter space (golden_inputs.sampler_sweep_case); only the picks are stored."""
@@ -269,6 +298,9 @@ def main():
     if len(sys.argv) > 1 and sys.argv[1] == "--prefix-file":
         prefix_file_fixture(weights)
         return
+    if len(sys.argv) > 1 and sys.argv[1] == "--prefill-continue":
+        prefill_continue_fixture(weights)
+        return
     ex = reference_export_module()
     # the synthetic-weight writer must produce the reference writer's bytes
     rng = np.random.default_rng(0)
@@ -282,6 +314,7 @@ def main():
     long_ctx_fixture(weights)
     end_decision_fixture(weights)
     prefix_file_fixture(weights)
+    prefill_continue_fixture(weights)
     subprocess.run([sys.executable, __file__, "--a16-prefill"], check=True)
     for p in sorted(OUT.glob("*.npz")):
         print(p.name, p.stat().st_size)

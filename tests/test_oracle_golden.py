@@ -167,6 +167,30 @@ def test_sampler_cases(dec):
         assert got == dec["sampler_picks"][case]
 
 
+def test_prefill_continuation_and_context_clamp(weights_path, weights_digest_ok):
+    """prefill(rows, start) after an earlier prefill, and rows past the context limit, which the
+    reference clamps to kMaxCtx - start (llm.cpp:329-331), in the product (W8A8) prefill mode."""
+    g = np.load(G / "prefill_continue.npz")
+    o = Oracle(weights_path, max_ctx=64)
+    o.prefill_rows(prompt_rows(10, seed=41))
+    o.prefill_rows(prompt_rows(7, seed=42), start=10)
+    assert o.position == int(g["cont_position"]) == 17
+    assert np.array_equal(o.hidden(), g["cont_hidden"])
+    for layer in (0, 11):
+        kk, vv = o.kv(layer, 10, 7)
+        assert np.array_equal(kk, g[f"cont_k{layer}"]) and np.array_equal(vv, g[f"cont_v{layer}"])
+    max_ctx = int(g["clamp_max_ctx"])
+    o = Oracle(weights_path, max_ctx=max_ctx)
+    k, v, h0, _ = global_state(max_ctx - 8, seed=43)
+    o.set_state(k, v, h0)
+    del k, v
+    o.prefill_rows(prompt_rows(20, seed=44), start=max_ctx - 8)
+    assert o.position == int(g["clamp_position"]) == max_ctx
+    assert np.array_equal(o.hidden(), g["clamp_hidden"])
+    kk, vv = o.kv(11, max_ctx - 8, 8)
+    assert np.array_equal(kk, g["clamp_k11"]) and np.array_equal(vv, g["clamp_v11"])
+
+
 def test_sampled_end_decision_and_greedy_frames(weights_path, weights_digest_ok):
     """end_greedy = 0 (one draw per frame against p(slot), llm.cpp:30-35) for three seeds, and
     greedy_frames = 3 ahead of sampled codes, after the 40-row prompt: the same frames as the
