@@ -201,6 +201,9 @@ public:
     }
 
     void set_logits_dump(const std::string &path) { logits_dump_path_ = path; }
+    // CSV "frame,slot_minus_end": the gate margin of every frame.  The reference's dump adds the
+    // argmax over the full 16384-row text head (llm.cpp:664-676,721-730), which this engine
+    // does not compute (the gate evaluates rows 7 and 9 only, as assistant_logits does).
     void set_gate_dump(const std::string &path) { gate_dump_path_ = path; }
     void set_cancel_flag(const std::atomic<bool> *flag) { cancel_ = flag; }
 
