@@ -169,7 +169,8 @@ public:
     }
 
     // Queued jobs end Cancelled ("shutting down"); running jobs run to their end first
-    // (runtime.cpp:172-186).
+    // (runtime.cpp:172-186).  Without a worker (run_once mode) nothing runs them: call
+    // run_once until it returns false before shutting down, or their streams stay open.
     void shutdown() {
         {
             std::lock_guard<std::mutex> lock(mutex_);
