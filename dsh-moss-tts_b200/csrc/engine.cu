@@ -564,6 +564,7 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
         t.bimg_parts = tc_parts(prec);
         t.work = work_ + li;
         t.err = dev_err_;
+        t.inject = li == 0 ? dev_err_ + 1 : nullptr;
         if (pf_active_) {
             PtArgs f{};
             f.q = q_;
@@ -751,6 +752,7 @@ void Engine::block(const Layer &L, int li, bool local, int R, const int *row_slo
         t.out = attn_;
         t.work = work_ + li;
         t.err = dev_err_;
+        t.inject = li == 0 ? dev_err_ + 1 : nullptr;
         if (R <= kGemvMaxRows) {
             launch_k(pdl_, k_attn_rows, dim3(R * kHeads), dim3(kArWarps * 32), 0, stream_, q_,
                      static_cast<const __half *>(a.kv), page_table_, pages_per_stream_, row_slot, row_pos, attn_,
@@ -1616,6 +1618,12 @@ __global__ void k_fill_state_normal(__half *__restrict__ kv, int n_pages, const 
 
 // Synthetic prefilled state for benchmarks and tests: K, V ~ N(0,1) rounded to fp16 for
 // positions 0..n_pos-1 of every layer, hidden ~ N(0,1); deterministic for a seed.
+void Engine::debug_inject_wait_timeout(bool on) {
+    const int v = on ? 1 : 0;
+    CK(cudaMemcpyAsync(dev_err_ + 1, &v, sizeof(int), cudaMemcpyHostToDevice, stream_));
+    CK(cudaStreamSynchronize(stream_));
+}
+
 void Engine::fill_state_random(int sid, int n_pos, uint64_t seed) {
     check_slot(sid);
     if (n_pos <= 0 || n_pos > max_ctx_) throw std::runtime_error("bad state length");

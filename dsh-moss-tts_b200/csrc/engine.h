@@ -95,6 +95,9 @@ public:
     void get_hidden(int sid, float *out);
     void debug_matrix_bytes(const std::string &name, uint8_t *out, size_t out_bytes);
     void debug_matrix_tile_bytes(const std::string &name, uint8_t *out, size_t out_bytes);
+    // Fault injection for the time-out test: while on, the first global layer's split-K decode
+    // attention leaves one ring stage unfilled, so its bounded wait runs out (code 7).
+    void debug_inject_wait_timeout(bool on);
     void set_cuda_stream(void *s);
     void fill_state_random(int sid, int n_pos, uint64_t seed);
     void set_kernel_timing(bool on);
@@ -209,7 +212,7 @@ private:
     int *codes_hist_ = nullptr;  // [kMaxFramesPerCall][max_streams][16] codes of a multi-frame call
     uint8_t *bimg_a_ = nullptr;    // activation image, K = 768, up to 256 rows
     uint8_t *bimg_mlp_ = nullptr;  // activation image, K = 3072 (fc_in output -> fc_out input)
-    int *dev_err_ = nullptr;       // tensor-core kernels' time-out flag
+    int *dev_err_ = nullptr;       // [0]: kernels' time-out flag; [1]: fault-injection word
     int *h_err_ = nullptr;         // pinned host copy of it
     int gemm_path_ = 0;
     int *d_ctl_ = nullptr, *h_ctl_ = nullptr;

@@ -483,6 +483,10 @@ struct AttnArgs {
     uint8_t *bimg;
     int bimg_N, bimg_parts;
     int *err;               // bounded-wait time-out flag (may be null)
+    // Fault injection for the time-out test (may be null; 0 = off): when *inject != 0 the
+    // producer leaves the first ring stage it fills unfilled -- no copy issued, no arrival --
+    // so the consumers' bounded wait on it runs out.  Nothing is in flight on that stage.
+    const int *inject;
 };
 
 // byte offset of element (n, k) in a tensor-core activation image with N rows: the
@@ -561,6 +565,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_decode(const AttnArgs 
         int seq = 0;
         bool ok = true;
         int g = 0;
+        const bool inject = a.inject != nullptr && *a.inject != 0;
         if (lane == 0) g = atomicAdd(a.work, 1);
         g = __shfl_sync(0xffffffffu, g, 0);
         int4 d = g < total ? a.desc[g] : make_int4(0, 0, 0, 0);
@@ -579,6 +584,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_decode(const AttnArgs 
                         const int s = seq % kAttnStages;
                         if (!mbar_wait(&empty[s], ((seq / kAttnStages) & 1) ^ 1, a.err, 8)) {
                             ok = false;
+                        } else if (inject && seq == 0 && !stop) {
+                            // fault injection: this stage stays unfilled (see AttnArgs::inject)
                         } else {
                             AttnStage &m = meta[s];
                             m.r = r;
@@ -606,10 +613,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_decode(const AttnArgs 
             g = __shfl_sync(0xffffffffu, gn, 0);
             d = g < total ? a.desc[g] : make_int4(0, 0, 0, 0);
         }
-        if (!ok && lane == 0) {
-            // a consumer stopped answering: let the copies already issued land before exiting
-            for (int k = max(0, seq - kAttnStages); k < seq - 1; ++k)
-                mbar_wait(&full[k % kAttnStages], (k / kAttnStages) & 1, nullptr, 0);
+        if ((!ok || inject) && lane == 0) {
+            // the consumers may have stopped waiting (a time-out): let every copy this warp
+            // issued land before the CTA exits.  The stage that failed its wait (when !ok)
+            // and the injected unfilled stage issued nothing and are skipped.
+            const int issued = ok ? seq : seq - 1;
+            for (int k = max(0, issued - kAttnStages); k < issued; ++k)
+                if (!(inject && k == 0)) mbar_wait(&full[k % kAttnStages], (k / kAttnStages) & 1, nullptr, 0);
         }
         return;
     }
@@ -1207,7 +1217,9 @@ __global__ void __launch_bounds__(256) k_sample(const float *__restrict__ logits
         if (threadIdx.x == 0) {
             for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
                 if (bv[w] > best || (bv[w] == best && bi[w] < besti)) { best = bv[w]; besti = bi[w]; }
-            s_pred = besti;
+            // all-NaN logits compare false everywhere: code 0, as the reference's first-max
+            // scan (best index starts at 0) returns
+            s_pred = besti < kCodebook ? besti : 0;
         }
     } else {
         const float temp = ctl->temperature;

@@ -25,27 +25,48 @@ int op_fail(const std::string &msg) {
 
 constexpr size_t kAlign = 256;
 
+// Device status of the standalone ops: a kernel whose bounded barrier wait ran out records its
+// code here (7: a consumer warp waited for a page, 8: the producer waited for a free stage),
+// so that the failure is not silent; mossgpu_op_device_status() reads and clears it.
+static __device__ int g_op_status;
+
 // The decode-attention kernel uses 205 KB of dynamic shared memory (its page ring), above the
 // 48 KB a launch gets without opting in; the opt-in is per device.
 constexpr int kMaxDevices = 64;
 std::mutex g_attr_mu;
 bool g_attr_set[kMaxDevices] = {};
 
-// plan -> decode -> combine on `st` over caller-provided scratch.
-int run_attention(mossgpu::AttnArgs t, int *work, int4 *desc, int max_items, cudaStream_t st, const char *who) {
-    using namespace mossgpu;
+int *g_status_ptr[kMaxDevices] = {};
+
+// Per-device set-up, once per device with that device current: the shared-memory opt-in and
+// the device address of g_op_status (in host code the symbol is only a handle).
+int device_setup(int *dev_out, const char *who) {
     int dev = -1;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return op_fail(std::string("cudaGetDevice: ") + cudaGetErrorString(e));
     if (dev < 0 || dev >= kMaxDevices) return op_fail(std::string(who) + ": device ordinal out of range");
-    {
-        std::lock_guard<std::mutex> lock(g_attr_mu);
-        if (!g_attr_set[dev]) {
-            e = cudaFuncSetAttribute(k_attn_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem);
-            if (e != cudaSuccess) return op_fail(std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
-            g_attr_set[dev] = true;
-        }
+    std::lock_guard<std::mutex> lock(g_attr_mu);
+    if (!g_attr_set[dev]) {
+        e = cudaFuncSetAttribute(mossgpu::k_attn_decode, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 mossgpu::kAttnSmem);
+        if (e != cudaSuccess) return op_fail(std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_op_status);
+        if (e != cudaSuccess || !p) return op_fail(std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+        g_status_ptr[dev] = static_cast<int *>(p);
+        g_attr_set[dev] = true;
     }
+    *dev_out = dev;
+    return 0;
+}
+
+// plan -> decode -> combine on `st` over caller-provided scratch.
+int run_attention(mossgpu::AttnArgs t, int *work, int4 *desc, int max_items, cudaStream_t st, const char *who) {
+    using namespace mossgpu;
+    int dev = -1;
+    if (device_setup(&dev, who) != 0) return 1;
+    cudaError_t e;
+    t.err = g_status_ptr[dev];
     k_attn_plan<<<1, kPlanThreads, 0, st>>>(t.row_pos, t.row_slot, t.pages_per_stream, t.R, max_items, const_cast<int *>(t.plan),
                                   desc, work, 1);
     t.desc = desc;
@@ -92,6 +113,21 @@ Layout layout_for(int R, size_t bytes) {
 extern "C" {
 
 const char *mossgpu_op_last_error(void) { return g_op_error.c_str(); }
+
+int mossgpu_op_device_status(int *code) {
+    if (!code) return op_fail("op_device_status: code is NULL");
+    int dev = -1;
+    if (device_setup(&dev, "op_device_status") != 0) return 1;
+    int v = 0;
+    cudaError_t e = cudaMemcpy(&v, g_status_ptr[dev], sizeof(int), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && v != 0) {
+        const int zero = 0;
+        e = cudaMemcpy(g_status_ptr[dev], &zero, sizeof(int), cudaMemcpyHostToDevice);
+    }
+    if (e != cudaSuccess) return op_fail(std::string("op_device_status: ") + cudaGetErrorString(e));
+    *code = v;
+    return 0;
+}
 
 size_t mossgpu_attention_workspace_bytes(int R) {
     if (R <= 0) return 0;

@@ -165,6 +165,15 @@ int mossgpu_set_gemm_path(mossgpu_engine *e, int mode);
  * clusters.  direct_min_rows = 0 disables the direct form.  Default (512, 256). */
 int mossgpu_set_tc_policy(mossgpu_engine *e, int direct_min_rows, int direct_rows);
 
+/* Fault injection for testing the bounded-wait error path: while enabled, the first global
+ * layer's split-K decode attention (batches above 96 rows on the tensor-core path, above 8 on
+ * the CUDA-core path) leaves one stage of its page ring unfilled -- no copy is issued for it --
+ * so the consumer warps' bounded wait runs out after about a second.  The frame's kernels all
+ * finish, the step returns non-zero with "wait timed out (code 7)", and the streams in that
+ * frame keep their host-side positions but hold undefined device state (re-initialise them).
+ * Off by default; the engine keeps stepping normally once it is disabled again. */
+int mossgpu_debug_inject_wait_timeout(mossgpu_engine *e, int enable);
+
 /* Same as mossgpu_debug_matrix_bytes for the tensor-core tile copy of the matrix. */
 int mossgpu_debug_matrix_tile_bytes(mossgpu_engine *e, const char *name, uint8_t *out, size_t out_bytes);
 
@@ -194,16 +203,29 @@ int mossgpu_attention_decode_paged(const float *q, const void *kv_layer, const i
                                    float *out, void *workspace, size_t workspace_bytes, void *cuda_stream);
 const char *mossgpu_op_last_error(void);
 
+/* Device status of the standalone ops on the calling thread's current device.  Every kernel
+ * wait in these ops is bounded (about a second); a wait that runs out ends its kernel early,
+ * leaves `out` incomplete, and records a code here instead of hanging the GPU: 7 = a consumer
+ * warp waited for a KV page, 8 = the page producer waited for a free ring stage.  The op's
+ * own return value cannot report it, because the call only enqueues work.  Call this after
+ * the op's stream has been synchronised: *code = 0 when no wait ran out, else the first code
+ * recorded since the last read (the status is then cleared).  Returns non-zero on a CUDA
+ * error.  No counterpart in the reference (its CPU attention has no waits). */
+int mossgpu_op_device_status(int *code);
+
 /* mossgpu_attention_decode_paged_noalloc: the same attention for callers that cannot
  * allocate device memory when they run it -- for example a real-time audio callback in a
  * plugin host, where cudaMalloc/cudaFree may block for milliseconds (cudaFree synchronises
  * the device), or a program whose device memory belongs to another allocator.  It takes no
- * workspace and allocates nothing: its scratch (~1.07 MiB) is a fixed array that the library
- * places on every GPU that loads it, kept until the process exits.
+ * workspace and allocates nothing: its scratch (1,120,960 bytes, about 1.07 MiB) is a fixed
+ * array that the library places on every GPU that loads it, kept until the process exits.
  *   - R must be <= 256 rows; larger batches are rejected with an error (use the workspace
  *     entry point above).
- *   - The first call on each device looks up that array's device address (with the device
- *     current); make that first call before any CUDA stream capture.
+ *   - The first call on each device does a one-time set-up with the device current: it looks
+ *     up that array's device address and opts the kernel into its shared memory.  Under CUDA
+ *     lazy loading that set-up may also load the library's kernels onto the device, which can
+ *     block and allocate.  So make the first call on each device a warm-up call outside the
+ *     real-time or no-allocation context, and before any CUDA stream capture.
  *   - All calls on a device share the one array.  Each call clears the parts that must start
  *     at zero, but two calls whose kernels overlap on the GPU (different streams, or other
  *     host threads) race on it: serialise them on one stream.

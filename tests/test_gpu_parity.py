@@ -80,22 +80,38 @@ def test_config1_global_step_matches_reference_golden(eng, sid, weights_path):
     assert eng.position(sid) == 129
 
 
-def test_local_decoder_matches_reference_golden(eng, sid, pkg):
-    """The golden decode case continued: a row-input global step, then local step 0, the
-    gate and channel 0's logits, all produced by the reference's LlmModel."""
+def test_local_decoder_matches_reference_golden(eng, sid, pkg, weights_path):
+    """The golden decode case continued.  The reference ran a second global step on the row
+    gs_row (a pad code among its codes) -> gs_hidden2, then local step 0 on that hidden state
+    and the W8A8 end gate on its output -> lc_gate.  Here the second step takes the
+    reference's own embedding of that row (gs_embed_row: embed_row skips the pad code), then
+    one frame runs without the global step: its gate must equal the reference's lc_gate, and
+    its 16 channels' logits and codes the oracle's."""
     dec = np.load(G / "decode.npz")
     k, v, h0, x = global_state(128)
     eng.set_state(sid, k, v, h0)
-    eng.global_step_embed([sid], x[None])
-    # the row-input step goes through a frame with forced codes = the golden row's codes;
-    # compare its embedding path via the hidden it produces
-    orc_row = dec["gs_row"]
-    assert np.abs(eng.hidden(sid) - dec["gs_hidden1"]).max() < TOL
+    h1 = eng.global_step_embed([sid], x[None])[0]
+    assert np.abs(h1 - dec["gs_hidden1"]).max() < TOL
+    h2 = eng.global_step_embed([sid], dec["gs_embed_row"][None])[0]
+    assert np.abs(h2 - dec["gs_hidden2"]).max() < TOL
     eng.generate_begin(sid, 0)
-    p = pkg.SampleParams.make(greedy=True, repetition_penalty=1.0, min_frames=99)
-    _, _, gate, _ = eng.step([sid], p, forced=orc_row[1:].clip(0, 1023), want_logits=True, run_global=False)
-    # gate of local step 0 on hidden1 vs the oracle chain is covered below; here only sanity
-    assert np.isfinite(gate).all()
+    p = pkg.SampleParams.make(greedy=True, repetition_penalty=1.2, min_frames=99)
+    forced = forced_codes(1, seed=12)
+    codes, stop, gate, logits = eng.step([sid], p, forced=forced[0], want_logits=True, run_global=False)
+    assert not stop[0]
+    assert np.abs(gate[0] - dec["lc_gate"]).max() < TOL
+    orc = Oracle(weights_path, max_ctx=256)
+    orc.set_state(k, v, h0)
+    orc.global_step_embed(x)
+    orc.global_step_embed(dec["gs_embed_row"])
+    assert np.abs(orc.gate(orc.local_step(0, orc.hidden())) - dec["lc_gate"]).max() < 1e-6
+    o_codes, o_logits, o_gate = orc.generate(1, sample_params(greedy=True, rep=1.2, min_frames=99), forced=forced,
+                                             want_logits=True)
+    assert np.abs(logits[0] - o_logits[0]).max() <= TOL
+    assert kl_per_frame(o_logits, logits).max() <= KL_TOL
+    assert (codes[0] == o_codes[0]).all()
+    assert np.abs(gate[0] - o_gate[0]).max() < TOL
+    assert eng.position(sid) == 130
 
 
 def test_teacher_forced_generate_vs_oracle(eng, sid, pkg, weights_path):

@@ -1,0 +1,338 @@
+"""GPU parity at the shapes the benchmark times, against the C oracle (pinned bit for bit to
+the reference's own LlmModel by tests/test_oracle_golden.py).
+
+* the benched frame: 64 streams with configs[1] lengths U{64..1024}, stepped through
+  mossgpu_step_frames (the multi-frame CUDA graph that bench.py's `value` times);
+* a 256-row frame with configs[3] lengths U{128..2048}: the engine's split-K attention
+  (plan -> decode -> combine) and the 4-slice tensor-core GEMM grid;
+* the configs[2] prefill: 16 prompts x 256 rows in one 4096-row pass;
+* long contexts: the reference's 4,000-position golden step, and a 100-stream batch at
+  4,300-4,500 cached positions (configs[4]'s end);
+* long teacher-forced runs: >= 200 frames over several prompts on both GEMM paths.
+
+A free-running GPU run is checked by teacher-forcing the oracle with the GPU's own codes
+(generate()'s `forced`, llm.cpp:694,706): the oracle then sees exactly the inputs and the
+repetition history the GPU saw, and its own predictions must equal the GPU's codes.
+
+Tolerances (north_star): logits max-abs-err <= 2e-2; per-frame KL <= 1e-4 (softmax T=1, mean
+over the 16 channels); argmax codes identical on >= 99% of frames.  Hidden states and KV rows
+are held to the same 2e-2 bound (the engine stores KV in fp16).
+"""
+from __future__ import annotations
+
+import os
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from golden_inputs import forced_codes, fp16_normal, global_state, prompt_rows
+from oracle_py import Oracle, sample_params
+
+pytestmark = pytest.mark.gpu
+G = Path(__file__).resolve().parent / "golden"
+TOL = 2e-2
+KL_TOL = 1e-4
+FRAME_AGREE = 0.99
+GREEDY_NEVER_STOP = dict(greedy=True, repetition_penalty=1.2, min_frames=1 << 30)
+
+
+def kl_per_frame(ref: np.ndarray, test: np.ndarray, t: float = 1.0) -> np.ndarray:
+    """[frames][16][1024] logits -> per-frame mean KL(softmax(ref) || softmax(test))."""
+    def sm(x):
+        z = x.astype(np.float64) / t
+        z -= z.max(-1, keepdims=True)
+        e = np.exp(z)
+        return e / e.sum(-1, keepdims=True)
+    p, q = sm(ref), sm(test)
+    return np.sum(p * (np.log(p + 1e-12) - np.log(q + 1e-12)), -1).mean(-1)
+
+
+def pool():
+    return ThreadPoolExecutor(max_workers=max(2, min(8, (os.cpu_count() or 2))))
+
+
+@pytest.fixture(scope="module")
+def pkg():
+    import moss_b200
+    moss_b200.build()
+    return moss_b200
+
+
+def read_state(eng, sid, L):
+    """A stream's cached K/V (all layers, fp16 values widened to fp32) and its hidden state."""
+    k = np.empty((12, L, 768), np.float32)
+    v = np.empty((12, L, 768), np.float32)
+    for layer in range(12):
+        k[layer], v[layer] = eng.kv(sid, layer, 0, L)
+    return k, v, eng.hidden(sid)
+
+
+def oracle_forced(weights, state, forced, frames_with_global, want_logits=False):
+    """The oracle from an injected state, teacher-forced with `forced` [F][16] for F frames.
+    Runs F+1 frames so that every one of the F frames is followed by its global step (the
+    reference skips the global step after the last frame of a generate call).  Returns
+    (codes [F][16], logits [F][16][1024] or None, gate [F][2], hidden, oracle)."""
+    k, v, h = state
+    F = forced.shape[0]
+    orc = Oracle(weights, max_ctx=k.shape[1] + F + 8)
+    orc.set_state(k, v, h)
+    f = np.concatenate([forced, np.zeros((1, 16), np.int32)]) if frames_with_global else forced
+    codes, logits, gate = orc.generate(f.shape[0], sample_params(greedy=True, rep=1.2, min_frames=1 << 30),
+                                       forced=f, want_logits=want_logits)
+    return codes[:F], (None if logits is None else logits[:F]), gate[:F], orc.hidden(), orc
+
+
+def check_codes(gpu_codes, orc_codes, what):
+    agree = (gpu_codes == orc_codes).all(-1).mean()
+    assert agree >= FRAME_AGREE, f"{what}: {agree:.3f} of frames agree ({(gpu_codes != orc_codes).sum()} codes differ)"
+
+
+# ------------------------------------------------------------------------- (i) benched frame
+
+def test_benched_frame_64_streams_step_frames(pkg, weights_path):
+    """bench.py's N=1 workload on the graph path it times: 64 streams, KV lengths
+    U{64..1024} (bench.py's seed), 6 free-running greedy frames through mossgpu_step_frames,
+    then 8 sampled streams (the shortest, the longest, and a spread) against the oracle."""
+    lens = [int(x) for x in np.random.default_rng(1234).integers(64, 1025, 64)]
+    F = 6
+    eng = pkg.Engine(weights_path, device=0, max_streams=65, max_ctx=1024 + F + 16)
+    try:
+        sids = [eng.open() for _ in lens]
+        for i, (s, L) in enumerate(zip(sids, lens)):
+            eng.fill_state_random(s, L, seed=500 + i)
+            eng.generate_begin(s, 0)
+        sample = sorted({int(np.argmin(lens)), int(np.argmax(lens)), 0, 9, 22, 35, 48, 63})
+        states = {i: read_state(eng, sids[i], lens[i]) for i in sample}
+        codes, done = eng.step_frames(sids, pkg.SampleParams.make(**GREEDY_NEVER_STOP), F)
+        assert (done == F).all()
+        with pool() as ex:
+            res = dict(zip(sample, ex.map(lambda i: oracle_forced(weights_path, states[i], codes[:, i], True),
+                                          sample)))
+        for i in sample:
+            o_codes, _, _, o_hidden, orc = res[i]
+            check_codes(codes[:, i], o_codes, f"stream {i} (L={lens[i]})")
+            assert eng.position(sids[i]) == lens[i] + F
+            assert np.abs(eng.hidden(sids[i]) - o_hidden).max() < TOL, i
+            for layer in (0, 11):
+                gk, gv = eng.kv(sids[i], layer, lens[i], F)
+                ok, ov = orc.kv(layer, lens[i], F)
+                assert np.abs(gk - ok).max() < TOL and np.abs(gv - ov).max() < TOL, (i, layer)
+            orc.close()
+    finally:
+        eng.close()
+
+
+# ------------------------------------------------------------------------- (ii) 256-row frame
+
+def test_256_row_frame_split_k_attention(pkg, weights_path):
+    """configs[3]'s per-frame batch on one GPU: 256 streams, KV lengths U{128..2048}.  Above
+    96 rows the global step's attention is the split-K plan -> decode -> combine path and the
+    GEMMs split the batch into 64-row z-slices.  One teacher-forced frame through mossgpu_step
+    (logits, gate, codes, the hidden state after the global step), then 3 free-running frames
+    through mossgpu_step_frames; 8 sampled streams against the oracle."""
+    lens = [int(x) for x in np.random.default_rng(4242).integers(128, 2049, 256)]
+    F = 3
+    eng = pkg.Engine(weights_path, device=0, max_streams=257, max_ctx=2048 + F + 16)
+    try:
+        sids = [eng.open() for _ in lens]
+        for i, (s, L) in enumerate(zip(sids, lens)):
+            eng.fill_state_random(s, L, seed=900 + i)
+            eng.generate_begin(s, 0)
+        sample = sorted({int(np.argmin(lens)), int(np.argmax(lens)), 0, 57, 100, 160, 201, 255})
+        states = {i: read_state(eng, sids[i], lens[i]) for i in sample}
+        forced = forced_codes(256, seed=31)
+        p = pkg.SampleParams.make(**GREEDY_NEVER_STOP)
+        c1, stop, gate, logits = eng.step(sids, p, forced=forced, want_logits=True)
+        assert not stop.any()
+        hid1 = {i: eng.hidden(sids[i]) for i in sample}
+        cF, done = eng.step_frames(sids, p, F)
+        assert (done == F).all()
+
+        def run(i):
+            f = np.concatenate([forced[i][None], cF[:, i]])
+            return oracle_forced(weights_path, states[i], f, True, want_logits=True)
+
+        def hidden_after_first(i):
+            orc = Oracle(weights_path, max_ctx=lens[i] + 8)
+            orc.set_state(*states[i])
+            orc.generate(2, sample_params(greedy=True, rep=1.2, min_frames=1 << 30),
+                         forced=np.stack([forced[i], forced[i]]))
+            h = orc.hidden()
+            orc.close()
+            return h
+
+        with pool() as ex:
+            res = dict(zip(sample, ex.map(run, sample)))
+            h1 = dict(zip(sample, ex.map(hidden_after_first, sample)))
+        for i in sample:
+            o_codes, o_logits, o_gate, o_hidden, orc = res[i]
+            assert np.abs(logits[i] - o_logits[0]).max() <= TOL, i
+            assert kl_per_frame(o_logits[:1], logits[i][None]).max() <= KL_TOL, i
+            assert np.abs(gate[i] - o_gate[0]).max() < TOL, i
+            assert (c1[i] == o_codes[0]).all(), i
+            assert np.abs(hid1[i] - h1[i]).max() < TOL, i
+            check_codes(cF[:, i], o_codes[1:], f"stream {i} (L={lens[i]})")
+            assert np.abs(eng.hidden(sids[i]) - o_hidden).max() < TOL, i
+            gk, gv = eng.kv(sids[i], 11, lens[i], F + 1)
+            ok, ov = orc.kv(11, lens[i], F + 1)
+            assert np.abs(gk - ok).max() < TOL and np.abs(gv - ov).max() < TOL, i
+            orc.close()
+    finally:
+        eng.close()
+
+
+# ------------------------------------------------------------------------- (iii) prefill
+
+def test_configs2_prefill_4096_rows_one_pass(pkg, weights_path):
+    """bench.py's prefill: 16 prompts x 256 rows of N(0,1) fp16 embeddings in one
+    mossgpu_prefill_embeds_batch call (one 4096-row pass: full 128 x 256 GEMM tiles on every
+    SM, 128-row flash-prefill tiles).  Three prompts against the oracle's A16 prefill
+    (the reference's MOSS_A16=all mode): last hidden, and K/V at the first, middle and last
+    positions of three layers."""
+    P, M = 16, 256
+    rng = np.random.default_rng(2024)
+    x = fp16_normal(rng, (P * M, 768))
+    eng = pkg.Engine(weights_path, device=0, max_streams=P, max_ctx=M + 16, max_rows=P * M)
+    try:
+        sids = [eng.open() for _ in range(P)]
+        eng.prefill_embeds_batch(sids, x, m=np.full(P, M, np.int32))
+        check = (0, 7, 15)
+
+        def run(p):
+            orc = Oracle(weights_path, max_ctx=M + 16, a16_prefill=True)
+            orc.prefill_embeds(x[p * M:(p + 1) * M])
+            out = {"hidden": orc.hidden()}
+            for layer in (0, 5, 11):
+                out[layer] = orc.kv(layer, 0, M)
+            orc.close()
+            return out
+
+        with pool() as ex:
+            res = dict(zip(check, ex.map(run, check)))
+        for p in check:
+            s = sids[p]
+            assert eng.position(s) == M
+            assert np.abs(eng.hidden(s) - res[p]["hidden"]).max() < TOL, p
+            for layer in (0, 5, 11):
+                gk, gv = eng.kv(s, layer, 0, M)
+                ok, ov = res[p][layer]
+                rows = [0, 1, M // 2, M - 2, M - 1]
+                assert np.abs(gk[rows] - ok[rows]).max() < TOL, (p, layer)
+                assert np.abs(gv[rows] - ov[rows]).max() < TOL, (p, layer)
+                assert np.abs(gk - ok).max() < TOL and np.abs(gv - ov).max() < TOL, (p, layer)
+    finally:
+        eng.close()
+
+
+# ------------------------------------------------------------------------- (iv) long contexts
+
+def test_long_context_golden_on_gpu(pkg, weights_path):
+    """The reference's own step at 4,000 injected positions (tests/golden/long_ctx.npz): a
+    global step from an embedding, then one from the row [9, codes] (a frame with those codes
+    forced), RoPE rows near the end of a 4,608-position context."""
+    g = np.load(G / "long_ctx.npz")
+    k, v, h0, x = global_state(4000, seed=11)
+    eng = pkg.Engine(weights_path, device=0, max_streams=2, max_ctx=4608)
+    try:
+        s = eng.open()
+        eng.set_state(s, k, v, h0)
+        del k, v
+        h1 = eng.global_step_embed([s], x[None])[0]
+        assert np.abs(h1 - g["hidden1"]).max() < TOL
+        for layer in (0, 11):
+            kk, vv = eng.kv(s, layer, 4000, 1)
+            assert np.abs(kk[0] - g[f"k{layer}"]).max() < TOL
+            assert np.abs(vv[0] - g[f"v{layer}"]).max() < TOL
+        eng.generate_begin(s, 0)
+        row = g["row"]
+        assert int(row[0]) == 9 and (row[1:] < 1024).all()
+        eng.step([s], pkg.SampleParams.make(**GREEDY_NEVER_STOP), forced=row[1:])
+        assert eng.position(s) == int(g["position"])
+        assert np.abs(eng.hidden(s) - g["hidden2"]).max() < TOL
+    finally:
+        eng.close()
+
+
+def test_long_context_batch_near_configs4_end(pkg, weights_path):
+    """100 streams at 4,300-4,500 cached positions (configs[4] ends near 4,500): the split-K
+    attention over ~280 pages per row and RoPE angles at the end of the context.  One
+    teacher-forced frame with logits; 3 sampled streams against the oracle."""
+    lens = [int(x) for x in np.random.default_rng(77).integers(4300, 4501, 100)]
+    eng = pkg.Engine(weights_path, device=0, max_streams=101, max_ctx=4608)
+    try:
+        sids = [eng.open() for _ in lens]
+        for i, (s, L) in enumerate(zip(sids, lens)):
+            eng.fill_state_random(s, L, seed=3000 + i)
+            eng.generate_begin(s, 0)
+        sample = sorted({int(np.argmax(lens)), 0, 50})
+        states = {i: read_state(eng, sids[i], lens[i]) for i in sample}
+        forced = forced_codes(100, seed=41)
+        c, stop, gate, logits = eng.step(sids, pkg.SampleParams.make(**GREEDY_NEVER_STOP), forced=forced,
+                                         want_logits=True)
+        assert not stop.any()
+        with pool() as ex:
+            res = dict(zip(sample, ex.map(
+                lambda i: oracle_forced(weights_path, states[i], forced[i][None], True, want_logits=True), sample)))
+        for i in sample:
+            o_codes, o_logits, o_gate, o_hidden, orc = res[i]
+            assert np.abs(logits[i] - o_logits[0]).max() <= TOL, i
+            assert kl_per_frame(o_logits, logits[i][None]).max() <= KL_TOL, i
+            assert (c[i] == o_codes[0]).all(), i
+            assert np.abs(eng.hidden(sids[i]) - o_hidden).max() < TOL, i
+            assert eng.position(sids[i]) == lens[i] + 1
+            orc.close()
+    finally:
+        eng.close()
+
+
+# ------------------------------------------------------------------------- (vi) long teacher forcing
+
+@pytest.mark.parametrize("n_prompts,frames,gemm_path", [(4, 50, 0), (12, 20, 0), (4, 50, 2)],
+                         ids=["4x50-cuda-core", "12x20-tensor-core", "4x50-tensor-core"])
+def test_long_teacher_forced_runs(pkg, weights_path, n_prompts, frames, gemm_path):
+    """>= 200 teacher-forced frames over several prompts (A16 prefill on both sides), all
+    prompts stepped together: per-frame KL <= 1e-4 on every frame, logits within 2e-2, and
+    >= 99% of frames with identical codes.  4 streams run the CUDA-core GEMV (<= 8 rows) unless
+    the tensor cores are forced; 12 streams run the tensor-core GEMM."""
+    lens = [40, 57, 83, 120, 33, 64, 71, 97, 45, 110, 52, 88][:n_prompts]
+    prompts = [prompt_rows(n, seed=60 + i) for i, n in enumerate(lens)]
+    forced = [forced_codes(frames, seed=80 + i) for i in range(n_prompts)]
+    eng = pkg.Engine(weights_path, device=0, max_streams=n_prompts, max_ctx=256)
+    try:
+        eng.set_gemm_path(gemm_path)
+        sids = [eng.open() for _ in prompts]
+        eng.prefill_batch(sids, prompts)
+        for s in sids:
+            eng.generate_begin(s, 0)
+        p = pkg.SampleParams.make(**GREEDY_NEVER_STOP)
+        g_logits = np.empty((n_prompts, frames, 16, 1024), np.float32)
+        g_codes = np.empty((n_prompts, frames, 16), np.int32)
+        for f in range(frames):
+            fc = np.stack([forced[i][f] for i in range(n_prompts)])
+            c, stop, _, lg = eng.step(sids, p, forced=fc, want_logits=True, run_global=f + 1 < frames)
+            assert not stop.any()
+            g_logits[:, f], g_codes[:, f] = lg, c
+
+        def run(i):
+            orc = Oracle(weights_path, max_ctx=256, a16_prefill=True)
+            orc.prefill_rows(prompts[i])
+            codes, logits, _ = orc.generate(frames, sample_params(greedy=True, rep=1.2, min_frames=1 << 30),
+                                            forced=forced[i], want_logits=True)
+            orc.close()
+            return codes, logits
+
+        with pool() as ex:
+            res = list(ex.map(run, range(n_prompts)))
+        kl = np.concatenate([kl_per_frame(res[i][1], g_logits[i]) for i in range(n_prompts)])
+        err = max(float(np.abs(g_logits[i] - res[i][1]).max()) for i in range(n_prompts))
+        same = np.concatenate([(g_codes[i] == res[i][0]).all(-1) for i in range(n_prompts)])
+        print(f"{kl.size} frames: KL max {kl.max():.2e} mean {kl.mean():.2e}, logits max-abs {err:.2e}, "
+              f"identical frames {same.mean():.4f}")
+        assert kl.size >= 200
+        assert kl.max() <= KL_TOL
+        assert err <= TOL
+        assert same.mean() >= FRAME_AGREE
+    finally:
+        eng.close()

@@ -65,6 +65,44 @@ def test_noalloc_attention_matches_workspace_entry_point_twice():
         assert (got - want).abs().max().item() <= TOL
 
 
+def torch_fp32(q, kv, table, slots, pos):
+    """The attention of llm.cpp:189-217 (scores q.k / 8, softmax, weighted sum of v) in fp32."""
+    import torch
+    out = torch.empty_like(q)
+    for r in range(q.shape[0]):
+        n = int(pos[r]) + 1
+        pages = table[int(slots[r]), : (n + PAGE - 1) // PAGE].long()
+        k = kv[pages, 0].float().permute(1, 0, 2, 3).reshape(HEADS, -1, HD)[:, :n]
+        v = kv[pages, 1].float().permute(1, 0, 2, 3).reshape(HEADS, -1, HD)[:, :n]
+        s = (q[r].reshape(HEADS, 1, HD) @ k.transpose(1, 2)) * 0.125
+        out[r] = (torch.softmax(s, -1) @ v).reshape(-1)
+    return out
+
+
+def test_noalloc_attention_full_batch_widens_chunks():
+    """256 rows (the limit) at up to ~4,000 positions: at the base chunk size the plan would cut
+    far more than the array's 341 chunks, so it widens them to fit.  The result must still
+    match the workspace entry point and a plain fp32 computation, and no wait may run out."""
+    import ctypes
+    import numpy as np
+    import torch
+    import moss_b200
+    moss_b200.build()
+    L = moss_b200.lib()
+    positions = tuple(int(x) for x in np.random.default_rng(21).integers(0, 4000, 256))
+    case = make_case(14, n_pages=700, pps=250, positions=positions)
+    got = without_alloc(L, *case)
+    want = with_workspace(L, *case)
+    ref = torch_fp32(*case)
+    torch.cuda.synchronize()
+    assert torch.isfinite(got).all()
+    assert (got - want).abs().max().item() <= TOL
+    assert (got - ref).abs().max().item() <= TOL
+    code = ctypes.c_int(-1)
+    assert L.mossgpu_op_device_status(ctypes.byref(code)) == 0, L.mossgpu_op_last_error()
+    assert code.value == 0
+
+
 def test_noalloc_attention_rejects_batches_over_the_limit():
     import torch
     import moss_b200
