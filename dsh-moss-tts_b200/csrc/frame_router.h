@@ -3,13 +3,14 @@
 // call.  Header-only C++17, host side.
 //
 // The reference hands frames from one LlmModel::generate thread to one decoder through a
-// bounded queue (FrameQueue, engine.cpp:91-124): the producer blocks while the queue is full,
+// bounded queue (engine.cpp:91-124): the producer blocks while the queue is full,
 // the consumer pops rows and, once enough are pending, turns them into an nq-major code block
 // [16][n] for decode_chunk -- the first block after min(4, chunk_frames) frames, later blocks
 // after chunk_frames frames, the remainder when the stream ends (engine.cpp:480-502).
 //
 // Here one batched step produces a frame for every live job at once:
-//   FrameQueue     - the same bounded, closable queue of Row = [text id, code0..15];
+//   FrameQueue     - a stream's bounded ring of Row = [text id, code0..15], filled in bulk
+//                    straight from a step result's code array;
 //   FrameRouter    - one FrameQueue per stream id; dispatch() pushes the rows of a
 //                    mossgpu_step result (codes [n][16], stop[n]) or of a mossgpu_step_frames
 //                    result (codes [frames][n][16], frames_done[n]) to their streams' queues and
@@ -37,48 +38,72 @@ namespace gpu {
 constexpr int kRouterNVq = 16;
 using FrameRow = std::array<int32_t, kRouterNVq + 1>;  // [text id, code0..15], as moss::Row
 
-// Bounded blocking queue with close (engine.cpp:91-124 semantics): push waits while full and
-// drops the row once closed; pop waits while empty and returns false once closed and drained.
+// A stream's frames between the batched step and its codec consumer: a fixed ring of
+// `capacity` rows, allocated once, that a step result is copied into straight from its code
+// array (append(), many frames at a time for a mossgpu_step_frames result).  The writer
+// blocks while the ring is full, so a slow decoder holds back its own stream only; the reader
+// blocks while it is empty.  finish() marks the end of the utterance: the reader drains what
+// is left and then sees the end, and a writer that is still waiting gives up (the rows it had
+// not written are dropped, as after a cancel).  One mutex guards the ring and one condition
+// variable wakes both sides: each side waits for a different predicate on the same counters.
 class FrameQueue {
 public:
-    explicit FrameQueue(size_t capacity) : capacity_(capacity ? capacity : 1) {}
-    void push(const FrameRow &row) {
-        std::unique_lock<std::mutex> lock(mutex_);
-        not_full_.wait(lock, [this] { return closed_ || queue_.size() < capacity_; });
-        if (closed_) return;
-        queue_.push_back(row);
-        not_empty_.notify_one();
+    explicit FrameQueue(size_t capacity) : ring_(capacity ? capacity : 1) {}
+
+    // Appends `frames` rows whose 16 codes start at codes + f * stride, each behind the text
+    // id `text` (0 in generate's rows).  Returns the rows written (< frames once finished).
+    size_t append(const int32_t *codes, size_t frames, size_t stride, int32_t text = 0) {
+        std::unique_lock<std::mutex> lk(mu_);
+        size_t done = 0;
+        while (done < frames) {
+            cv_.wait(lk, [&] { return ended_ || count_ < ring_.size(); });
+            if (ended_) break;
+            const size_t room = std::min(ring_.size() - count_, frames - done);
+            for (size_t k = 0; k < room; ++k, ++done) {
+                FrameRow &row = ring_[(head_ + count_ + k) % ring_.size()];
+                row[0] = text;
+                std::copy(codes + done * stride, codes + done * stride + kRouterNVq, row.begin() + 1);
+            }
+            count_ += room;
+            cv_.notify_all();
+        }
+        return done;
     }
+    // One complete row (text id included).
+    void push(const FrameRow &row) { append(row.data() + 1, 1, 0, row[0]); }
+
+    // Takes the oldest row; false once the utterance ended and the ring is drained.
     bool pop(FrameRow *row) {
-        std::unique_lock<std::mutex> lock(mutex_);
-        not_empty_.wait(lock, [this] { return closed_ || !queue_.empty(); });
-        if (queue_.empty()) return false;
-        *row = queue_.front();
-        queue_.pop_front();
-        not_full_.notify_one();
+        std::unique_lock<std::mutex> lk(mu_);
+        cv_.wait(lk, [&] { return ended_ || count_ > 0; });
+        if (count_ == 0) return false;
+        *row = ring_[head_];
+        head_ = (head_ + 1) % ring_.size();
+        --count_;
+        cv_.notify_all();
         return true;
     }
-    void close() {
-        std::lock_guard<std::mutex> lock(mutex_);
-        closed_ = true;
-        not_empty_.notify_all();
-        not_full_.notify_all();
+    void finish() {
+        std::lock_guard<std::mutex> lk(mu_);
+        ended_ = true;
+        cv_.notify_all();
     }
+    void close() { finish(); }
     bool closed() const {
-        std::lock_guard<std::mutex> lock(mutex_);
-        return closed_;
+        std::lock_guard<std::mutex> lk(mu_);
+        return ended_;
     }
     size_t size() const {
-        std::lock_guard<std::mutex> lock(mutex_);
-        return queue_.size();
+        std::lock_guard<std::mutex> lk(mu_);
+        return count_;
     }
 
 private:
-    mutable std::mutex mutex_;
-    std::condition_variable not_empty_, not_full_;
-    std::deque<FrameRow> queue_;
-    size_t capacity_;
-    bool closed_ = false;
+    mutable std::mutex mu_;
+    std::condition_variable cv_;
+    std::vector<FrameRow> ring_;
+    size_t head_ = 0, count_ = 0;
+    bool ended_ = false;
 };
 
 class FrameRouter {
@@ -105,7 +130,7 @@ public:
                 q->close();
                 continue;
             }
-            q->push(make_row(codes + static_cast<size_t>(i) * kRouterNVq));
+            q->append(codes + static_cast<size_t>(i) * kRouterNVq, 1, 0);
         }
     }
     // One mossgpu_step_frames result: codes[frames][n][16], frames_done[n] (the frames each
@@ -115,18 +140,14 @@ public:
         for (int i = 0; i < n; ++i) {
             auto q = get(stream_ids[i]);
             const int done = frames_done ? frames_done[i] : frames;
-            for (int f = 0; f < done && f < frames; ++f)
-                q->push(make_row(codes + (static_cast<size_t>(f) * n + i) * kRouterNVq));
+            // the stream's rows sit n rows apart in the [frames][n][16] result
+            q->append(codes + static_cast<size_t>(i) * kRouterNVq, static_cast<size_t>(std::min(done, frames)),
+                      static_cast<size_t>(n) * kRouterNVq);
             if (done < frames) q->close();
         }
     }
 
 private:
-    static FrameRow make_row(const int32_t *c) {
-        FrameRow r{};
-        for (int ch = 0; ch < kRouterNVq; ++ch) r[static_cast<size_t>(ch) + 1] = c[ch];
-        return r;
-    }
     std::shared_ptr<FrameQueue> get(int stream_id) {
         std::lock_guard<std::mutex> lock(mutex_);
         auto it = queues_.find(stream_id);

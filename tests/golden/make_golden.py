@@ -32,7 +32,8 @@ sys.path.insert(0, str(ROOT / "tests"))
 from golden_inputs import (END_SEEDS, LONG_CTX, PREFIX_FILE_ROWS, SAMPLER_SWEEP, WEIGHTS_SEED, global_state, prompt_rows,  # noqa: E402
                            forced_codes, sampler_case, sampler_sweep_case, sha)
 
-REF_ROOT = Path(os.environ.get("REF_ROOT", "/root/reference"))
+# the reference checkout: REF_ROOT, else a directory named `reference` beside this repository
+REF_ROOT = Path(os.environ.get("REF_ROOT", Path(__file__).resolve().parents[3] / "reference"))
 
 
 def load_pkg():
