@@ -16,6 +16,7 @@
 #include <array>
 #include <atomic>
 #include <chrono>
+#include <cstddef>
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
@@ -52,6 +53,25 @@ struct SampleParams {  // sampler.h:8-22, same defaults
     bool end_greedy = true;
     int min_frames = 0;
     int greedy_frames = 0;
+};
+
+// Where generate() reports per-frame timings: nothing (nullptr), or a std::vector of any
+// struct with the members {global_ms, local_ms} -- this header's FrameTiming or the
+// reference's moss::FrameTiming (llm.h:34-37), so that callers written against the reference
+// pass their own vectors unchanged.
+class TimingOut {
+public:
+    TimingOut(std::nullptr_t = nullptr) {}
+    template <class T>
+    TimingOut(std::vector<T> *v) {
+        if (v) push_ = [v](double global_ms, double local_ms) { v->push_back(T{global_ms, local_ms}); };
+    }
+    void operator()(double global_ms, double local_ms) const {
+        if (push_) push_(global_ms, local_ms);
+    }
+
+private:
+    std::function<void(double, double)> push_;
 };
 
 class Engine {  // one mossgpu_engine per GPU, shareable by several LlmModel objects
@@ -147,9 +167,11 @@ public:
         return load_file(path, rows, kStateMagic, true, ignore_weights_fp, err);
     }
 
-    // llm.h:75-79, llm.cpp:634-733
-    std::vector<Row> generate(int max_frames, const SampleParams &audio_params, uint64_t seed,
-                              std::vector<FrameTiming> *timing = nullptr, const std::vector<Row> *forced = nullptr,
+    // llm.h:75-79, llm.cpp:634-733.  Params: this header's SampleParams or the reference's
+    // moss::SampleParams (sampler.h:8-22) -- any struct with its eight members.
+    template <class Params>
+    std::vector<Row> generate(int max_frames, const Params &audio_params, uint64_t seed, TimingOut timing = nullptr,
+                              const std::vector<Row> *forced = nullptr,
                               const std::function<void(int, const Row &)> &on_frame = {}) {
         using Clock = std::chrono::steady_clock;
         std::vector<Row> frames;
@@ -182,7 +204,7 @@ public:
             Row row{};
             for (int ch = 0; ch < kNVq; ++ch) row[ch + 1] = codes[ch];
             frames.push_back(row);
-            if (timing) timing->push_back(FrameTiming{last ? 0.0 : ms, 0.0});
+            timing(last ? 0.0 : ms, 0.0);
             if (on_frame) on_frame(f, row);
         }
         if (!logits_dump_path_.empty()) {

@@ -39,6 +39,20 @@ def test_batch_runtime_on_engine_double(tmp_path):
     assert int(shards["shard0_cost"]) > 0 and int(shards["shard1_cost"]) > 0
 
 
+def test_text_job_runtime_on_engine_double(tmp_path):
+    """TextJobRuntime (job_runtime.h): the reference Runtime's text-level submit(JobRequest,
+    PcmSink) over the batching runtime, with a test front end and codec: every job's PCM equals
+    the sequential synthesis of the same text, decoded and converted as the reference does;
+    unknown voices, a full queue, failing sinks and codecs, and cancel end jobs as the reference's
+    Runtime does."""
+    exe = tmp_path / "job_runtime_test"
+    subprocess.run([*CXX, "-I", str(ROOT / "tests" / "cpp"), str(ROOT / "tests" / "cpp" / "job_runtime_test.cpp"),
+                    "-o", str(exe)], check=True, capture_output=True, text=True)
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert r.stdout.split() == ["A", "jobs=10", "B", "ok"]
+
+
 # ---- GPU: the runtime over the engine, replayed through the Python API
 
 PREFIX_M = 24
