@@ -1,33 +1,42 @@
 #!/usr/bin/env python
-"""Benchmark: MOSS-TTS-Nano per-frame LLM step on B200, frames/s for the whole job.
+"""Benchmark: MOSS-TTS-Nano per-frame LLM step on B200, frames/s for the whole box.
 
-Workload: per GPU, 64 independent streams with KV lengths drawn
-uniformly from 64..1024 (seeded), paged fp16 KV with 16-token pages.  One step = one full
-audio frame for every stream: the 17-step local decoder with the W8A8 end gate and 16
-greedy codes (repetition penalty 1.2), then the 12-layer global decode step that appends one
-KV position.  Weights: the reference architecture with seeded synthetic N(0,0.02) weights in
-the reference's Q8_0_4X4 format; KV ~ N(0,1) fp16.  The KV working set (about 1.3 GB per GPU)
-is far larger than L2, so no explicit L2 flush is needed between steps.
+Default workload (the long-form streaming sweep, strong scaling):
+512 independent streams for the whole job with starting KV lengths drawn uniformly from
+256..4096 (seeded), sharded over the N ranks by total KV length (512/N streams per GPU), paged
+fp16 KV with 16-token pages.  One step = one audio frame for every stream: the 17-step local
+decoder with the W8A8 end gate and 16 greedy codes (repetition penalty 1.2), then the 12-layer
+global decode step that appends one KV position.  Weights: the reference architecture with
+seeded synthetic N(0,0.02) weights in the reference's Q8_0_4X4 format; KV ~ N(0,1) fp16.  The
+KV working set (~41 GB for the whole job) is far larger than L2, so no L2 flush is needed.
+`--workload configs1` runs BASELINE configs[1] instead: 64 streams per GPU, KV U{64..1024}
+(weak scaling).
 
-  value   K frames per stream on the device (mossgpu_step_frames, no host round trip per
-          frame), CUDA events on the engine's stream, max over ranks.
+  value   K frames of every stream on the device (one mossgpu_step_frames call: no host
+          round trip per frame), CUDA events on the engine's stream, max over ranks.
   e2e     the same K frames as K calls of mossgpu_step through the C ABI with host buffers
-          (control block H2D and codes/flags/gate D2H every frame), wall clock, max over ranks.
-  roofline: the kernel class with the largest device time, timed live with CUDA events
-          recorded between the kernels of the captured frame graph (a separate pass);
-          `rooflines` gives the same figures for every class, `traffic` the DRAM bytes per
-          launch of the committed ncu capture of that kernel (profiles/traffic.json).
+          (control block H2D, codes/flags/gate D2H every frame), wall clock, max over ranks;
+          p50/p99 of that per-frame call latency per GPU are gathered in `stats`.
+  roofline: the kernel function with the largest device time in a separate profiled pass
+          (CUDA events recorded between the kernels of the captured frame graph).  Event
+          separation breaks the launch overlap and adds a gap to every launch; that gap is
+          taken as one overhead per launch ((event time - frame time) / launches) and
+          subtracted, so that launches x time adds up to the frame.
+  stats   one all_gather of per-GPU frames, device time, e2e time and per-frame latency
+          percentiles (the only collective besides the shard broadcast and the max).
 
 --impl reference runs the reference's own CPU implementation (oracle/_ref, compiled from the
-reference sources; the C port in oracle/ when that is absent) on a bounded sample of the
-same workload, on rank 0 only.
+reference sources; the C port in oracle/ when that is absent) as K independent single-thread
+processes on K physical cores, one stream each at the quantiles of the same KV distribution, on
+rank 0 only.
 """
 from __future__ import annotations
 
 import argparse
-import ctypes as C
+import importlib
 import importlib.util
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -43,6 +52,8 @@ PKG_DIR = ROOT / "dsh-moss-tts_b200"
 PEAKS = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 METRIC = "LLM frames/sec (whole box)"
+kPAGE = 16
+POS_BYTES = 36_864  # fp16 K and V of one position, all 12 layers
 
 
 def load_package():
@@ -65,6 +76,33 @@ def peaks():
 
 def q8x4_bytes(rows, cols):
     return rows // 4 * cols // 32 * 136
+
+
+# ----------------------------------------------------------------------------- workload
+
+def workload(args, world):
+    """(all stream lengths of the job, streams per rank, scaling)."""
+    if args.workload == "configs4":
+        lens = [int(x) for x in np.random.default_rng(4096).integers(args.lmin, args.lmax + 1, args.streams_total)]
+        return lens, math.ceil(len(lens) / world), "strong"
+    lens = [int(x) for x in np.random.default_rng(1234).integers(args.lmin, args.lmax + 1, args.streams * world)]
+    return lens, args.streams, "weak"
+
+
+def workload_config(args, world=1):
+    if args.workload == "configs4":
+        w = (f"configs[4]: {args.streams_total} streams for the whole box, start KV U{{{args.lmin}..{args.lmax}}}, "
+             f"sharded over the GPUs (strong scaling); step = one full frame of every stream "
+             f"(17-step local decoder + gate + 16 greedy codes + 12-layer global decode)")
+        shape = {"streams_total": args.streams_total, "streams_per_gpu": math.ceil(args.streams_total / world)}
+    else:
+        w = (f"configs[1]: {args.streams} ragged streams per GPU, full per-frame step "
+             f"(17-step local decoder + gate + 16 greedy codes + 12-layer global decode)")
+        shape = {"streams_per_gpu": args.streams}
+    return {"workload": w, **shape, "kv_len": [args.lmin, args.lmax], "page_tokens": kPAGE,
+            "model": "MOSS-TTS-Nano LLM (reference architecture, Q8_0_4X4 weights, synthetic)",
+            "compute": "int8 weights x fp32 activations (W8A16 as the reference's MOSS_A16), fp32 accumulate, fp16 KV",
+            "l2": "not flushed: KV working set per GPU >> 126 MB L2", "parallelism": f"dp{world} (streams sharded)"}
 
 
 # ----------------------------------------------------------------------------- clocks
@@ -107,79 +145,141 @@ class Clocks:
 
 # ----------------------------------------------------------------------------- CPU legs
 
-def cpu_frames_per_s(weights: str, lens: list[int], budget_s: float, max_frames: int, threads: int):
-    """Time whole frames of the reference (oracle/_ref) or, failing that, of the C port on
-    states with the given KV lengths.  Returns (frames/s, kind, threads, sample description)."""
+def host_cpus() -> dict:
+    """Physical cores this process may use (distinct (package, core) pairs among the CPUs of
+    its affinity mask, capped by a cgroup CPU quota), logical CPUs and the CPU model."""
+    affinity = sorted(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else list(range(os.cpu_count() or 1))
+    model, pairs, cur = "", {}, {}
+    try:
+        for line in open("/proc/cpuinfo"):
+            k, _, v = line.partition(":")
+            k, v = k.strip(), v.strip()
+            if k == "processor":
+                cur = {"cpu": int(v)}
+            elif k == "model name":
+                model = model or v
+                cur["model"] = v
+            elif k == "physical id":
+                cur["pkg"] = v
+            elif k == "core id":
+                cur["core"] = v
+                pairs[cur["cpu"]] = (cur.get("pkg"), v)
+    except OSError:
+        pass
+    physical = len({pairs[c] for c in affinity if c in pairs}) or len(affinity)
+    quota = None
+    try:
+        q, period = Path("/sys/fs/cgroup/cpu.max").read_text().split()[:2]
+        if q != "max":
+            quota = max(1, int(int(q) / int(period)))
+    except (OSError, ValueError):
+        pass
+    usable = min(physical, quota) if quota else physical
+    return {"physical_cores": usable, "logical_cpus": len(affinity), "cpu_model": model or "unknown",
+            "cgroup_cpu_quota": quota}
+
+
+def _cpu_stream_worker(job):
+    """One single-thread reference process: one stream with a random fp16 N(0,1) KV state of
+    length L, greedy frames with repetition penalty 1.2 (MOSS_A16=decode, the product mode)
+    through the reference's own LlmModel::generate, for about budget_s seconds."""
+    weights, L, budget_s, seed, threads = job
     sys.path.insert(0, str(ROOT / "oracle"))
     import oracle_py
-    rng = np.random.default_rng(7)
-    use_ref = oracle_py.RefModel.available()
-    frames = 0
-    elapsed = 0.0
-    per_stream = []
-    for L in lens:
-        k = rng.standard_normal((12, L, 768), dtype=np.float32).astype(np.float16).astype(np.float32)
-        v = rng.standard_normal((12, L, 768), dtype=np.float32).astype(np.float16).astype(np.float32)
-        h = rng.standard_normal(768, dtype=np.float32)
-        if use_ref:
-            m = oracle_py.RefModel(weights, threads=threads)
-            fn = m.lib.ref_frames
-        else:
-            m = oracle_py.Oracle(weights, max_ctx=L + max_frames + 8)
-            fn = m.lib.or_frames
-            threads = 1
-        fn.argtypes = [C.c_void_p, C.c_int, C.c_float, np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")]
-        m.set_state(k, v, h)
-        codes = np.zeros((1, 16), np.int32)
-        fn(m.h, 1, 1.2, codes)  # warm-up frame (first touch of the weights)
-        n = 0
-        t0 = time.perf_counter()
-        while n < max_frames and (n == 0 or time.perf_counter() - t0 < budget_s / len(lens)):
-            fn(m.h, 1, 1.2, codes)
-            n += 1
-        dt = time.perf_counter() - t0
-        frames += n
-        elapsed += dt
-        per_stream.append(n)
-        m.close()
-    kind = "reference" if use_ref else "port"
-    sample = (f"{frames} frames ({'+'.join(map(str, per_stream))}) over {len(lens)} streams with KV lengths "
-              f"{lens} drawn from the same U(64,1024) distribution, one frame = local decoder + 16 codes + "
-              f"global step")
-    return frames / elapsed, kind, threads, sample
+    rng = np.random.default_rng(seed)
+    k = rng.standard_normal((12, L, 768), dtype=np.float32).astype(np.float16).astype(np.float32)
+    v = rng.standard_normal((12, L, 768), dtype=np.float32).astype(np.float16).astype(np.float32)
+    h = rng.standard_normal(768, dtype=np.float32)
+    if oracle_py.RefModel.available():
+        m, kind = oracle_py.RefModel(weights, threads=threads, a16_mode="decode"), "reference"
+        run = lambda n: m.generate(n, greedy=True, rep=1.2, min_frames=1 << 30)  # noqa: E731
+    else:
+        m, kind = oracle_py.Oracle(weights, max_ctx=min(4608, L + 4096)), "port"
+        sp = oracle_py.sample_params(greedy=True, rep=1.2, min_frames=1 << 30)
+        run = lambda n: m.generate(n, sp)  # noqa: E731
+    room = m.max_ctx - L - 2
+    m.set_state(k, v, h)
+    del k, v
+    t0 = time.perf_counter()
+    run(2)  # warm-up (first touch of the weights); also sizes the timed call
+    per = (time.perf_counter() - t0) / 2
+    n = int(max(2, min(room - 2, budget_s / max(per, 1e-4))))
+    t0 = time.perf_counter()
+    got = run(n)[0].shape[0]
+    dt = time.perf_counter() - t0
+    m.close()
+    return got, dt, kind
 
 
-def run_reference_arm(args, rank):
+def cpu_throughput(weights: str, lmin: int, lmax: int, budget_s: float, procs: int | None = None) -> dict:
+    """The reference CPU engine's throughput mode: P independent single-thread processes on P
+    physical cores, one stream each with KV lengths at the P quantiles of U{lmin..lmax}."""
+    import multiprocessing as mp
+    cpus = host_cpus()
+    P = procs or max(1, min(cpus["physical_cores"], 32))
+    lens = [int(round(lmin + (i + 0.5) / P * (lmax - lmin))) for i in range(P)]
+    with mp.get_context("spawn").Pool(P) as pool:
+        res = pool.map(_cpu_stream_worker, [(weights, L, budget_s, 7 + i, 1) for i, L in enumerate(lens)])
+    fps = sum(f / dt for f, dt, _ in res)
+    frames = sum(f for f, _, _ in res)
+    kind = res[0][2]
+    return {"value": round(fps, 3), "unit": "frames/s", "cores": P, "kind": kind,
+            "sample": (f"{P} single-thread {'reference' if kind == 'reference' else 'C-port'} processes on {P} physical "
+                       f"cores ({cpus['cpu_model']}; {cpus['logical_cpus']} logical CPUs usable), one stream each, "
+                       f"KV lengths at the {P} quantiles of U{{{lmin}..{lmax}}} ({min(lens)}..{max(lens)}), "
+                       f"{frames} greedy frames in ~{budget_s:.0f} s per process through LlmModel::generate, "
+                       f"MOSS_A16=decode"),
+            "host": cpus}
+
+
+def cpu_single_stream(weights: str, L: int, budget_s: float) -> dict:
+    """One stream, one process, all logical CPUs as the reference's --threads (single-stream mode)."""
+    import multiprocessing as mp
+    cpus = host_cpus()
+    T = cpus["logical_cpus"]
+    with mp.get_context("spawn").Pool(1) as pool:
+        f, dt, kind = pool.map(_cpu_stream_worker, [(weights, L, budget_s, 99, T)])[0]
+    return {"frames_per_s": round(f / dt, 3), "ms_per_frame": round(1000 * dt / f, 2), "threads": T, "kv_len": L,
+            "kind": kind}
+
+
+def run_reference_arm(args, rank, world):
     if rank != 0:
         return
-    pkg = load_package()
+    load_package()
     from moss_b200 import mossfile
-    weights = mossfile.ensure_synth_weights(Path(tempfile.gettempdir()) / "moss_b200_w0.moss", 0)
-    rng = np.random.default_rng(1234)
-    lens = [int(x) for x in rng.integers(args.lmin, args.lmax + 1, 2)]
-    threads = os.cpu_count() or 1
-    # each step is one frame for each sampled stream; bound the run to a few minutes
-    budget = min(120.0, 0.5 * (args.steps + args.warmup))
-    fps, kind, cores, sample = cpu_frames_per_s(weights, lens, budget, max(2, args.steps), threads)
-    line = {"impl": "reference", "metric": METRIC, "value": round(fps, 3), "unit": "frames/s",
-            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * len(lens) / fps, 3),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": workload_config(args),
-            "cpu_baseline": {"value": round(fps, 3), "unit": "frames/s", "cores": cores, "kind": kind, "sample": sample},
-            "e2e": {"value": round(fps, 3), "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    weights = str(mossfile.ensure_synth_weights(Path(tempfile.gettempdir()) / "moss_b200_w0.moss", 0))
+    budget = min(60.0, max(10.0, 0.6 * (args.steps + args.warmup)))
+    cb = cpu_throughput(weights, args.lmin, args.lmax, budget)
+    single = cpu_single_stream(weights, (args.lmin + args.lmax) // 2, min(budget, 15.0))
+    lens, per_rank, scaling = workload(args, world)
+    n_streams = len(lens)
+    line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "frames/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * n_streams / cb["value"], 3),
+            "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": workload_config(args, world),
+            "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "cpu_host": cb["host"], "single_stream_all_threads": single,
+            "e2e": {"value": cb["value"], "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
-def workload_config(args):
-    return {"workload": f"configs[1]: {args.streams} ragged streams per GPU, full per-frame step "
-                        f"(17-step local decoder + gate + 16 greedy codes + 12-layer global decode)",
-            "streams_per_gpu": args.streams, "kv_len": [args.lmin, args.lmax], "page_tokens": 16,
-            "model": "MOSS-TTS-Nano LLM (reference architecture, Q8_0_4X4 weights, synthetic)",
-            "compute": "int8 weights x fp32 activations (W8A16 as the reference's MOSS_A16), fp32 accumulate, fp16 KV",
-            "l2": "not flushed: KV working set per GPU >> 126 MB L2", "parallelism": f"dp{args.gpus} (streams sharded)"}
-
-
 # ----------------------------------------------------------------------------- GPU arm
+
+def kernel_classes(R: int):
+    """Algorithmic bytes and FLOPs per launch of each kernel class at R batch rows."""
+    act = 4  # bytes per input element: fp32 rows, or the tensor-core image's two fp16 parts
+    gemm = {  # class -> (rows, K, output bytes per row)
+        "qkv_global": (2304, 768, 768 * 4 + 1536 * 2), "proj_global": (768, 768, 768 * 8),
+        "fc_in_global": (3072, 768, 3072 * 4), "fc_out_global": (768, 3072, 768 * 8),
+        "qkv_local": (2304, 768, 768 * 4 + 1536 * 4), "proj_local": (768, 768, 768 * 8),
+        "fc_in_local": (3072, 768, 3072 * 4), "fc_out_local": (768, 3072, 768 * 8),
+        "audio_heads": (1024, 768, 1024 * 4),
+    }
+    algo = {k: q8x4_bytes(m, kk) + m * 4 + R * (kk * act + ob) for k, (m, kk, ob) in gemm.items()}
+    flops = {k: 2.0 * m * kk * R for k, (m, kk, _) in gemm.items()}
+    return gemm, algo, flops
+
 
 def run_ours(args, rank, world, local_rank, dist):
     import torch
@@ -190,23 +290,26 @@ def run_ours(args, rank, world, local_rank, dist):
     if dist is not None:
         dist.barrier()
     from moss_b200 import mossfile
-    weights = mossfile.ensure_synth_weights(Path(tempfile.gettempdir()) / "moss_b200_w0.moss", 0)
-    B, K, W = args.streams, args.steps, args.warmup
-    prof_frames = min(K, 16)
-    max_ctx = args.lmax + W + 2 * K + prof_frames + 64
-    eng = pkg.Engine(weights, device=local_rank, max_streams=B + 1, max_ctx=max_ctx)
-    eng.set_cuda_stream(torch.cuda.current_stream().cuda_stream)
-    # one workload of B streams per GPU, KV lengths U{lmin..lmax}, sharded across the ranks
-    # by total KV length (rank 0 decides, every rank gets B streams)
-    import importlib
     sharding = importlib.import_module("moss_b200.sharding")
-    all_lens = [int(x) for x in np.random.default_rng(1234).integers(args.lmin, args.lmax + 1, B * world)]
-    lens = [all_lens[i] for i in sharding.agree_shards(dist, all_lens, per_rank=B)[rank]]
+    weights = str(mossfile.ensure_synth_weights(Path(tempfile.gettempdir()) / "moss_b200_w0.moss", 0))
+    K, W = args.steps, args.warmup
+    prof_frames = min(K, 16)
+    all_lens, per_rank, scaling = workload(args, world)
+    lens = [all_lens[i] for i in sharding.agree_shards(dist, all_lens, per_rank=per_rank)[rank]]
+    B = len(lens)
+    extra = max(W + 1, K, prof_frames) + 2  # positions a phase appends before the next reset
+    b1_extra = 128 + 64
+    pages = sum((L + extra + kPAGE - 1) // kPAGE + 1 for L in lens) + (b1_extra + kPAGE - 1) // kPAGE + 16
+    eng = pkg.Engine(weights, device=local_rank, max_streams=B + 2, max_ctx=max(lens) + extra + 32, kv_pages=pages,
+                     max_rows=max(B + 2, 256))
+    eng.set_cuda_stream(torch.cuda.current_stream().cuda_stream)
+    if args.tc_direct_min is not None:
+        eng.set_tc_policy(args.tc_direct_min, 256)
     sids = [eng.open() for _ in lens]
 
     def reset_states():
-        # every measured phase starts from the same cached lengths (lmin..lmax), not from
-        # where the previous phase left the streams
+        # every measured phase starts from the same cached lengths, not from where the
+        # previous phase left the streams
         for i, (s, L) in enumerate(zip(sids, lens)):
             eng.fill_state_random(s, L, seed=1000 * rank + i)
             eng.generate_begin(s, 0)
@@ -244,7 +347,8 @@ def run_ours(args, rank, world, local_rank, dist):
     _, done = eng.step_frames(sids, params, K, want_codes=False)
     e1.record()
     torch.cuda.synchronize()
-    dev_ms = max_over_ranks(e0.elapsed_time(e1))
+    my_dev_ms = e0.elapsed_time(e1)
+    dev_ms = max_over_ranks(my_dev_ms)
     launches = eng.last_launch_count()
     assert int(done.min()) == K, "a stream stopped during the timed region"
     # ---- e2e: K calls through the C ABI, host buffers in and out every frame
@@ -252,11 +356,15 @@ def run_ours(args, rank, world, local_rank, dist):
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize()
+    lat = []
     t0 = time.perf_counter()
     for _ in range(K):
-        codes, stop, gate, _ = eng.step(sids, params)
+        c0 = time.perf_counter()
+        eng.step(sids, params)  # returns after the frame's codes reached the host
+        lat.append(time.perf_counter() - c0)
     torch.cuda.synchronize()
-    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    my_e2e_s = time.perf_counter() - t0
+    e2e_s = max_over_ranks(my_e2e_s)
     clk = clocks.stop()
 
     # ---- per-kernel device time (separate pass, events inside the frame graph)
@@ -284,31 +392,23 @@ def run_ours(args, rank, world, local_rank, dist):
     torch.cuda.synchronize()
     b1_us = 1000 * b0.elapsed_time(b1) / n1
     b1_bytes = 12 * (q8x4_bytes(2304, 768) + q8x4_bytes(768, 768) + q8x4_bytes(3072, 768) + q8x4_bytes(768, 3072)) \
-        + 485_376 + 36_864 * (128 + n1 // 2 + 1) + 36_864
+        + 485_376 + POS_BYTES * (128 + n1 // 2 + 1) + POS_BYTES
     pk = peaks()
+    h2d = eng_ctl_bytes(B)
+    d2h = B * (16 * 4 + 4 + 8)
+    eng.close()
 
-    # ---- prefill: 16 prompts x 256 rows (192 text + 64 voice-frame embeddings,
-    # N(0,1) rounded to fp16) in one 4096-row pass through the 12 layers on the tensor cores,
-    # writing the fp16 KV; embeddings are copied from host memory inside the timing
-    for s_ in sids + [s1]:
-        eng.close_stream(s_)
+    # ---- configs[1] frame (64 streams per GPU, KV U{64..1024}) and configs[2] prefill:
+    # reported beside the headline, each in an engine of its own
+    c1 = run_configs1_frame(pkg, weights, local_rank, torch, rank, K, W) if args.workload == "configs4" else None
     pf = run_prefill(pkg, weights, local_rank, torch, n_prompts=16, rows=256)
     pf["frac_of_bf16_peak"] = round(pf["tflops"] / pk["bf16_tflops"], 4)
 
-    # ---- rooflines.  Classes run on the tcgen05 GEMM (R > 8) or the CUDA-core GEMV (R <= 8);
-    # algorithmic bytes = weights (Q8_0_4X4) + bias + activations in and out, FLOPs = 2 rows K R.
+    # ---- rooflines
     R = B
+    step_ms = dev_ms / K
     mean_ctx = float(np.mean(base_pos)) + prof_frames / 2.0 + 1.0  # attended positions per row
-    act = 4  # bytes per input element: fp32 rows, or the tensor-core image's two fp16 parts
-    gemm = {  # class -> (rows, K, output bytes per row)
-        "qkv_global": (2304, 768, 768 * 4 + 1536 * 2), "proj_global": (768, 768, 768 * 8),
-        "fc_in_global": (3072, 768, 3072 * 4), "fc_out_global": (768, 3072, 768 * 8),
-        "qkv_local": (2304, 768, 768 * 4 + 1536 * 4), "proj_local": (768, 768, 768 * 8),
-        "fc_in_local": (3072, 768, 3072 * 4), "fc_out_local": (768, 3072, 768 * 8),
-        "audio_heads": (1024, 768, 1024 * 4),
-    }
-    algo = {k: q8x4_bytes(m, kk) + m * 4 + R * (kk * act + ob) for k, (m, kk, ob) in gemm.items()}
-    flops = {k: 2.0 * m * kk * R for k, (m, kk, _) in gemm.items()}
+    gemm, algo, flops = kernel_classes(R)
     algo.update({
         "attn_decode_paged": R * mean_ctx * 12 * 64 * 2 * 2 + R * 768 * 8,
         "attn_combine": R * 12 * 8 * 68 * 4 + R * 768 * 4,
@@ -316,65 +416,87 @@ def run_ours(args, rank, world, local_rank, dist):
         "build_activation_image": R * 768 * 4 + max(16, R) * 768 * 4,
         "sample_greedy": R * 1024 * 4 + R * 1024 * 2,
     })
-    tf = Path(__file__).resolve().parent / "profiles" / "traffic.json"
-    traffic_db = json.loads(tf.read_text()) if tf.exists() else {}  # dram bytes per launch, committed ncu captures
+    tf = ROOT / "profiles" / "traffic.json"
+    traffic_db = json.loads(tf.read_text()) if tf.exists() else {}  # dram bytes per launch, committed captures
+    # Event-separated class times each carry the launch gap that the graph overlaps.  Take
+    # that gap as one overhead per launch: delta = (event time - frame time) / launches, and
+    # each launch's time = its event time - delta, so that launches x time add up to the frame.
+    event_ms_per_frame = sum(tot for tot, nl in prof.values() if nl) / prof_frames
+    launches_per_frame = sum(nl for _, nl in prof.values()) / prof_frames
+    delta_ms = max(0.0, (event_ms_per_frame - step_ms) / max(launches_per_frame, 1))
+
+    def launch_ms(tot, nl):  # apportioned mean time of one launch of a class
+        return max(tot / nl - delta_ms, 0.05 * tot / nl)
+
     rooflines = {}
     for k, (tot, nl) in prof.items():
         if nl and k in algo:
-            us = 1000 * tot / nl
+            us = 1000 * launch_ms(tot, nl)
             r_ = {"avg_launch_us": round(us, 2), "achieved_gbs": round(algo[k] / (us / 1e6) / 1e9, 1),
                   "frac_of_hbm": round(algo[k] / (us / 1e6) / 1e9 / pk["hbm_gbs"], 4)}
             if k in flops:
                 r_["achieved_tflops"] = round(flops[k] / (us / 1e6) / 1e12, 2)
-            if k in traffic_db:
-                r_["traffic"] = traffic_db[k]["dram_bytes_per_launch"]
             rooflines[k] = r_
-    # the dominant kernel: the kernel function with the most device time in the profiled
-    # frames; the weight-matrix roles all run one function (k_gemm_tc above 8 rows, else k_gemv)
-    fn_of = {k: ("k_gemm_tc" if R > 8 else "k_gemv") for k in gemm}
+    direct = args.tc_direct_min if args.tc_direct_min is not None else 1024  # the engine's default
+    gemm_fn = "k_gemm_tp" if (direct > 0 and R >= direct) else ("k_gemm_tc" if R > 8 else "k_gemv")
+    attn_fn = "k_attn_decode" if R > 96 else "k_attn_rows"
+    fn_of = {**{k: gemm_fn for k in gemm}, "attn_decode_paged": attn_fn}
     fns = {}
     for k, (tot, nl) in prof.items():
         if nl and k in algo:
-            f = fn_of.get(k, k)
-            e = fns.setdefault(f, [0.0, 0, 0.0, []])
+            e = fns.setdefault(fn_of.get(k, k), [0.0, 0, 0.0, []])
             e[0] += tot
             e[1] += nl
             e[2] += algo[k] * nl
             e[3].append(k)
     name, (tot_ms, nl, bytes_all, classes) = max(fns.items(), key=lambda kv: kv[1][0])
-    avg_ms = tot_ms / max(nl, 1)
+    avg_ms = launch_ms(tot_ms, max(nl, 1))
     algo_launch = bytes_all / max(nl, 1)  # mean algorithmic bytes per launch of that function
     achieved = algo_launch / (avg_ms / 1e3) / 1e9
-    traffic = traffic_db.get(name, {}).get("dram_bytes_per_launch")
-    step_ms = dev_ms / K
-    value = B * world * K / (dev_ms / 1e3)
-    e2e = B * world * K / e2e_s
-    h2d = eng_ctl_bytes(B)
-    d2h = B * (16 * 4 + 4 + 8)
-    breakdown = {k: {"ms_per_frame": round(v[0] / prof_frames, 4), "launches_per_frame": v[1] // prof_frames}
+    tentry = traffic_db.get(f"{name}@{args.workload}", {})  # committed ncu capture of that kernel
+    traffic = tentry.get("dram_bytes_per_launch")
+    if traffic is None and "dram_per_algorithmic_byte" in tentry:  # captured on a smaller case, scaled by units
+        traffic = round(tentry["dram_per_algorithmic_byte"] * algo_launch)
+    value = len(all_lens) * K / (dev_ms / 1e3)
+    e2e = len(all_lens) * K / e2e_s
+    breakdown = {k: {"ms_per_frame": round(launch_ms(v[0], v[1]) * v[1] / prof_frames, 4),
+                     "launches_per_frame": v[1] // prof_frames}
                  for k, v in sorted(prof.items(), key=lambda kv: -kv[1][0]) if v[1]}
 
+    # ---- stats gather: per-GPU frames, device ms, e2e s, per-frame call latency p50/p99 (ms)
+    mine = [float(B * K), my_dev_ms, my_e2e_s, 1000 * float(np.percentile(lat, 50)),
+            1000 * float(np.percentile(lat, 99)), float(sum(lens))]
+    per_gpu = gather_stats(dist, mine)
+    stats = {"per_gpu": [{"rank": i, "streams": int(g[0] // K), "frames": int(g[0]), "device_ms": round(g[1], 3),
+                          "e2e_s": round(g[2], 4), "p50_frame_ms": round(g[3], 3), "p99_frame_ms": round(g[4], 3),
+                          "kv_positions": int(g[5])} for i, g in enumerate(per_gpu)],
+             "device_ms_max_over_min": round(max(g[1] for g in per_gpu) / min(g[1] for g in per_gpu), 4),
+             "p50_frame_ms": round(max(g[3] for g in per_gpu), 3), "p99_frame_ms": round(max(g[4] for g in per_gpu), 3)}
+
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_frames_per_s(weights, lens[:2], budget_s=20.0, max_frames=64, threads=os.cpu_count() or 1)
-        cpu_baseline = {"value": round(cpu[0], 3), "unit": "frames/s", "cores": cpu[2], "kind": cpu[1], "sample": cpu[3]}
+        cb = cpu_throughput(weights, args.lmin, args.lmax, budget_s=15.0)
+        cpu_baseline = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
     else:
         cpu_baseline = None
 
     line = {"metric": METRIC, "value": round(value, 2), "unit": "frames/s", "n_gpus": world, "steps": K, "warmup": W,
-            "ms_per_step": round(step_ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "ms_per_step": round(step_ms, 4), "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
             "dtype": "f32", "data": "synthetic (seeded N(0,0.02) Q8_0_4X4 weights, N(0,1) fp16 KV)",
-            "config": workload_config(args),
+            "config": workload_config(args, world),
             "roofline": {"kernel": name, "classes": sorted(classes), "bound": "hbm", "achieved": round(achieved, 1),
                          "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
                          "traffic": traffic, "algorithmic_bytes_per_launch": round(algo_launch),
-                         "launches_per_frame": nl // prof_frames,
-                         "avg_launch_us": round(1000 * avg_ms, 3), "peak_source": pk["source"]},
+                         "launches_per_frame": nl // prof_frames, "avg_launch_us": round(1000 * avg_ms, 3),
+                         "avg_launch_us_event_separated": round(1000 * tot_ms / max(nl, 1), 3),
+                         "launch_overhead_us": round(1000 * delta_ms, 3), "peak_source": pk["source"]},
             "rooflines": rooflines,
             "cpu_baseline": cpu_baseline,
             "e2e": {"value": round(e2e, 2), "unit": "frames/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "api": "mossgpu_step (C ABI), one call per frame, host buffers"},
+                    "api": "mossgpu_step (C ABI), one call per frame for all of a GPU's streams, host buffers"},
             "gpu_launches": launches,
             "clocks": clk,
+            "stats": stats,
+            "configs1_frame": c1,
             "prefill": pf,
             "batch1_global_step": {"us": round(b1_us, 2), "kv_len": 128, "algorithmic_bytes": b1_bytes,
                                    "achieved_gbs": round(b1_bytes / (b1_us / 1e6) / 1e9, 1),
@@ -382,7 +504,44 @@ def run_ours(args, rank, world, local_rank, dist):
             "kernel_breakdown_ms_per_frame": breakdown}
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+def gather_stats(dist, values: list[float]) -> list[list[float]]:
+    """One all_gather of a small float vector per rank (the end-of-run stats gather)."""
+    if dist is None or not dist.is_initialized():
+        return [list(values)]
+    import torch
+    t = torch.tensor(values, dtype=torch.float64, device="cuda")
+    out = [torch.empty_like(t) for _ in range(dist.get_world_size())]
+    dist.all_gather(out, t)
+    return [o.cpu().tolist() for o in out]
+
+
+def run_configs1_frame(pkg, weights, device, torch, rank, K, W) -> dict:
+    """configs[1] on this GPU: 64 streams, KV U{64..1024}, K frames on the device."""
+    lens = [int(x) for x in np.random.default_rng(1234 + rank).integers(64, 1025, 64)]
+    eng = pkg.Engine(weights, device=device, max_streams=65, max_ctx=1024 + W + K + 32)
+    eng.set_cuda_stream(torch.cuda.current_stream().cuda_stream)
+    sids = [eng.open() for _ in lens]
+    p = pkg.SampleParams.make(greedy=True, repetition_penalty=1.2, min_frames=1 << 30)
+
+    def reset():
+        for i, (s, L) in enumerate(zip(sids, lens)):
+            eng.fill_state_random(s, L, seed=i)
+            eng.generate_begin(s, 0)
+
+    reset()
+    eng.step_frames(sids, p, W, want_codes=False)
+    reset()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    eng.step_frames(sids, p, K, want_codes=False)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / K
     eng.close()
+    return {"streams": 64, "kv_len": [64, 1024], "ms_per_frame": round(ms, 4), "frames_per_s_per_gpu": round(64 / ms * 1e3, 1)}
 
 
 # model FLOPs per prefilled row: 2 x the 84,934,656 weights of the 12 layers; causal attention
@@ -420,13 +579,11 @@ def run_prefill(pkg, weights, device, torch, n_prompts: int, rows: int, warmup: 
 
 
 def run_sweep(args, rank, world, local_rank, dist):
-    """Long-form streaming: every stream generates `frames` frames from a
-    starting KV length drawn from U{256..4096}, appending one position per frame.  Streams are
-    sharded over the ranks by KV length; each GPU steps its streams in groups of <= 256 rows
-    through mossgpu_step (C ABI, host buffers).  value = all frames of all streams / the
-    slowest rank's wall time; p50 / p99 = per-call latency of one frame for one group."""
-    import importlib
-    import math
+    """Long-form streaming sustained over the whole 400 frames: every
+    stream generates `frames` frames from its starting KV length, appending one position per
+    frame.  Streams are sharded over the ranks by KV length; each GPU steps all its streams in
+    one mossgpu_step call per frame (C ABI, host buffers).  value = all frames of all streams /
+    the slowest rank's wall time; p50 / p99 = per-call latency of one frame of a GPU's streams."""
     import torch
     torch.cuda.set_device(local_rank)
     pkg = load_package()
@@ -436,84 +593,91 @@ def run_sweep(args, rank, world, local_rank, dist):
         dist.barrier()
     from moss_b200 import mossfile
     sharding = importlib.import_module("moss_b200.sharding")
-    weights = mossfile.ensure_synth_weights(Path(tempfile.gettempdir()) / "moss_b200_w0.moss", 0)
-    frames, n_all, warm = args.sweep_frames, args.sweep_streams, 2
-    all_lens = [int(x) for x in np.random.default_rng(4096).integers(256, 4097, n_all)]
+    weights = str(mossfile.ensure_synth_weights(Path(tempfile.gettempdir()) / "moss_b200_w0.moss", 0))
+    frames, n_all, warm = args.sweep_frames, args.streams_total, 2
+    all_lens = [int(x) for x in np.random.default_rng(4096).integers(args.lmin, args.lmax + 1, n_all)]
     mine = [all_lens[i] for i in sharding.agree_shards(dist, all_lens, per_rank=math.ceil(n_all / world))[rank]]
     pages = sum((L + frames + warm + kPAGE) // kPAGE + 1 for L in mine) + 16
-    eng = pkg.Engine(weights, device=local_rank, max_streams=len(mine) + 1, max_ctx=4096 + frames + warm + 32,
-                     kv_pages=pages)
+    eng = pkg.Engine(weights, device=local_rank, max_streams=len(mine) + 1, max_ctx=args.lmax + frames + warm + 32,
+                     kv_pages=pages, max_rows=max(len(mine) + 1, 256))
+    if args.tc_direct_min is not None:
+        eng.set_tc_policy(args.tc_direct_min, 256)
     sids = [eng.open() for _ in mine]
     for i, (s, L) in enumerate(zip(sids, mine)):
         eng.fill_state_random(s, L, seed=7000 + 1000 * rank + i)
         eng.generate_begin(s, 0)
-    groups = [sids[i:i + 256] for i in range(0, len(sids), 256)]
     params = pkg.SampleParams.make(greedy=True, repetition_penalty=1.2, min_frames=1 << 30)
     for _ in range(warm):
-        for g in groups:
-            eng.step(g, params)
+        eng.step(sids, params)
     torch.cuda.synchronize()
     if dist is not None:
         dist.barrier()
     lat = []
     t0 = time.perf_counter()
     for _ in range(frames):
-        for g in groups:
-            c0 = time.perf_counter()
-            eng.step(g, params)  # returns after the frame's codes reached the host
-            lat.append(time.perf_counter() - c0)
-    wall = sharding.max_over_ranks(dist, time.perf_counter() - t0, device="cuda")
-    p50 = sharding.max_over_ranks(dist, float(np.percentile(lat, 50)), device="cuda")
-    p99 = sharding.max_over_ranks(dist, float(np.percentile(lat, 99)), device="cuda")
-    kv_end = sum(L + warm + frames for L in all_lens) * 36_864
+        c0 = time.perf_counter()
+        eng.step(sids, params)  # returns after the frame's codes reached the host
+        lat.append(time.perf_counter() - c0)
+    my_wall = time.perf_counter() - t0
+    wall = sharding.max_over_ranks(dist, my_wall, device="cuda")
+    per_gpu = gather_stats(dist, [float(len(mine) * frames), my_wall, 1000 * float(np.percentile(lat, 50)),
+                                  1000 * float(np.percentile(lat, 99))])
+    kv_end = sum(L + warm + frames for L in all_lens) * POS_BYTES
     line = {"metric": "long-form streaming frames/sec (whole box)", "value": round(n_all * frames / wall, 1),
             "unit": "frames/s", "n_gpus": world, "higher_is_better": True, "scaling": "strong",
             "config": {"workload": "configs[4]: long-form sweep", "streams": n_all, "frames_per_stream": frames,
-                       "start_kv_len": [256, 4096], "rows_per_step_call": 256, "streams_per_gpu": len(mine)},
-            "p50_step_ms": round(1000 * p50, 3), "p99_step_ms": round(1000 * p99, 3),
+                       "start_kv_len": [args.lmin, args.lmax], "streams_per_gpu": len(mine)},
+            "p50_step_ms": round(max(g[2] for g in per_gpu), 3), "p99_step_ms": round(max(g[3] for g in per_gpu), 3),
+            "per_gpu": [{"rank": i, "frames": int(g[0]), "wall_s": round(g[1], 3), "p50_ms": round(g[2], 3),
+                         "p99_ms": round(g[3], 3)} for i, g in enumerate(per_gpu)],
             "wall_s": round(wall, 3), "kv_bytes_at_end": kv_end, "dtype": "f32", "data": "synthetic"}
     if rank == 0:
         print(json.dumps(line), flush=True)
     eng.close()
 
 
-kPAGE = 16
-
-
 def eng_ctl_bytes(B: int) -> int:
     """Bytes of the engine's per-call control block (engine.h off_* layout): slots, positions,
     frames, forced codes, page updates, FrameCtl (12 ints), active flags, frame counter."""
-    r_max = max(B + 1, 256)
+    r_max = max(B + 2, 256)
     return 4 * (22 * r_max + 1 + 12 + r_max + 4)
 
 
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--streams", type=int, default=64)
-    ap.add_argument("--lmin", type=int, default=64)
-    ap.add_argument("--lmax", type=int, default=1024)
+    ap.add_argument("--workload", choices=["configs4", "configs1"], default="configs4",
+                    help="configs4 (default): 512 streams for the whole box, KV U{256..4096}, strong scaling; "
+                         "configs1: 64 streams per GPU, KV U{64..1024}, weak scaling")
+    ap.add_argument("--streams-total", type=int, default=512, help="configs4: streams of the whole job")
+    ap.add_argument("--streams", type=int, default=64, help="configs1: streams per GPU")
+    ap.add_argument("--lmin", type=int, default=None)
+    ap.add_argument("--lmax", type=int, default=None)
+    ap.add_argument("--tc-direct-min", type=int, default=None,
+                    help="batch rows from which the GEMMs use the direct tile form (mossgpu_set_tc_policy)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep", action="store_true",
-                    help="BASELINE configs[4] instead: 512 streams from KV lengths U{256..4096}, 400 frames each, "
-                         "sharded over the ranks; sustained frames/s and p50/p99 step latency")
+                    help="configs[4] sustained: every stream runs --sweep-frames frames (400), per-frame latency")
     ap.add_argument("--sweep-frames", type=int, default=400)
-    ap.add_argument("--sweep-streams", type=int, default=512)
     ap.add_argument("--profile-prefill", type=int, default=0,
                     help="prefill this many 256-row prompts after one warm-up prompt and exit (ncu captures)")
     ap.add_argument("--profile-frames", type=int, default=0,
-                    help="run this many frames of the N=1 workload after one warm-up frame and exit "
+                    help="run this many frames of the workload after one warm-up frame and exit "
                          "(the command the ncu captures under profiles/ use)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.lmin is None:
+        args.lmin = 256 if args.workload == "configs4" else 64
+    if args.lmax is None:
+        args.lmax = 4096 if args.workload == "configs4" else 1024
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
-        run_reference_arm(args, rank)
+        run_reference_arm(args, rank, world)
         return
     dist = None
     if world > 1:

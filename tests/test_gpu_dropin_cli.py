@@ -50,7 +50,9 @@ def test_reference_cli_on_gpu_matches_reference_cli_on_cpu(weights_path, tmp_pat
     prompt, forced = tmp_path / "prompt.txt", tmp_path / "forced.txt"
     prompt.write_text("\n".join(" ".join(map(str, r)) for r in prompt_rows(40, seed=3)) + "\n")
     forced.write_text("\n".join(" ".join(map(str, r)) for r in forced_codes(FRAMES, seed=4)) + "\n")
-    common = ["--weights", weights_path, "--prompt", prompt, "--frames", FRAMES, "--greedy", "--force-codes", forced]
+    # --min-frames: the synthetic model's end gate would otherwise stop generate at frame 0
+    common = ["--weights", weights_path, "--prompt", prompt, "--frames", FRAMES, "--greedy", "--force-codes", forced,
+              "--min-frames", 1000]
     cpu = run(CPU_CLI, [*common, "--threads", min(8, os.cpu_count() or 1), "--dump-logits", tmp_path / "cpu.bin",
                         "--save-state", tmp_path / "state.bin"], env={"MOSS_A16": "all"})
     gpu = run(GPU_CLI, [*common, "--dump-logits", tmp_path / "gpu.bin"])
