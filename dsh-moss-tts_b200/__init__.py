@@ -41,7 +41,7 @@ EXPORTS = [
     "mossgpu_attention_workspace_bytes", "mossgpu_attention_decode_paged", "mossgpu_op_last_error",
     "mossgpu_attention_decode_paged_noalloc", "mossgpu_set_gemm_path", "mossgpu_debug_matrix_tile_bytes",
     "mossgpu_stream_fork", "mossgpu_create_rows", "mossgpu_prefill_batch", "mossgpu_prefill_embeds_batch",
-    "mossgpu_set_tc_policy", "mossgpu_op_device_status", "mossgpu_debug_inject_wait_timeout",
+    "mossgpu_set_tc_policy", "mossgpu_op_device_status", "mossgpu_debug_inject_wait_timeout", "mossgpu_set_local_path",
 ]
 
 
@@ -131,6 +131,7 @@ def lib() -> C.CDLL:
         L.mossgpu_op_last_error.restype = C.c_char_p
         L.mossgpu_op_device_status.argtypes = [C.POINTER(C.c_int)]
         L.mossgpu_debug_inject_wait_timeout.argtypes = [C.c_void_p, C.c_int]
+        L.mossgpu_set_local_path.argtypes = [C.c_void_p, C.c_int]
         L.mossgpu_attention_decode_paged_noalloc.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p,
                                                              C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]
         _LIB = L
@@ -294,6 +295,10 @@ class Engine:
     def debug_inject_wait_timeout(self, enable: bool):
         """Test hook: make the next frames' first split-K attention wait run out (see mossgpu.h)."""
         self._check(self.lib.mossgpu_debug_inject_wait_timeout(self.h, int(enable)))
+
+    def set_local_path(self, mode: int):
+        """0 = fused local decoder for greedy frames (default), 1 = per-step kernels for every frame."""
+        self._check(self.lib.mossgpu_set_local_path(self.h, mode))
 
     def set_graphs(self, enable: bool):
         self._check(self.lib.mossgpu_set_graphs(self.h, int(enable)))

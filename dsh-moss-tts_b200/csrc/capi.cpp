@@ -226,6 +226,10 @@ int mossgpu_debug_inject_wait_timeout(mossgpu_engine *e, int enable) {
     return guarded(e, [&](mossgpu::Engine &g) { g.debug_inject_wait_timeout(enable != 0); });
 }
 
+int mossgpu_set_local_path(mossgpu_engine *e, int mode) {
+    return guarded(e, [&](mossgpu::Engine &g) { g.set_local_path(mode); });
+}
+
 int mossgpu_set_gemm_path(mossgpu_engine *e, int mode) {
     return guarded(e, [&](mossgpu::Engine &g) { g.set_gemm_path(mode); });
 }

@@ -19,6 +19,7 @@
 #include "kernels.cuh"
 #include "gemm_tc.cuh"
 #include "attn_tc.cuh"
+#include "local_fused.cuh"
 
 namespace mossgpu {
 
@@ -183,6 +184,16 @@ void Engine::load_weights(const std::string &path) {
     llnf_b_ = vec("local.lnf.b", kHidden);
     wte_ = mat("wte", kVocab, kHidden);
     for (int ch = 0; ch < kNVq; ++ch) aemb_[ch] = mat("aemb." + std::to_string(ch), kCodebook, kHidden);
+    // the fused local decoder reads the local layer and the audio heads as MMA fragment records
+    auto mma_copy = [&](DevMat &m) {
+        const long long threads = (long long)(m.rows / 16) * (m.cols / 32) * 32;
+        m.qm = dalloc<int8_t>(size_t(m.rows) * m.cols, owned_);
+        m.sm = dalloc<__half>(size_t(m.rows) * (m.cols / 32), owned_);
+        k_repack_mma<<<unsigned((threads + 255) / 256), 256>>>(m.qs, m.sc, m.rows, m.cols, m.qm, m.sm);
+        CK(cudaGetLastError());
+    };
+    for (DevMat *m : {&local_.attn, &local_.proj, &local_.fc_in, &local_.fc_out}) mma_copy(*m);
+    for (int ch = 0; ch < kNVq; ++ch) mma_copy(aemb_[ch]);
     CK(cudaDeviceSynchronize());
     CK(cudaFree(staging));
     weights_bytes_ = file.size();
@@ -408,6 +419,89 @@ void Engine::set_smem_limits() {
     set_tc_attr<TC_QKV>();
     set_tc_attr<TC_RESID>();
     set_tc_attr<TC_GELU_B>();
+    // fused local decoder: 16-CTA clusters (a non-portable size) when the device can co-schedule
+    // one, else 8
+    CK(cudaFuncSetAttribute(k_local_fused<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, LfSmem<16>::total));
+    CK(cudaFuncSetAttribute(k_local_fused<16>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    CK(cudaFuncSetAttribute(k_local_fused<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, LfSmem<8>::total));
+    lf_cluster_ = 0;
+    int only = 0;  // MOSSGPU_LOCAL_CLUSTER=8 or 16 pins the cluster size (A/B measurements)
+    if (const char *v = std::getenv("MOSSGPU_LOCAL_CLUSTER")) only = std::atoi(v);
+    for (int C : {16, 8}) {
+        if (only && C != only) continue;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(C);
+        cfg.blockDim = dim3(kLfThreads);
+        cfg.dynamicSmemBytes = C == 16 ? LfSmem<16>::total : LfSmem<8>::total;
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = C;
+        attr.val.clusterDim.y = 1;
+        attr.val.clusterDim.z = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        const cudaError_t rc = C == 16 ? cudaOccupancyMaxActiveClusters(&n, k_local_fused<16>, &cfg)
+                                       : cudaOccupancyMaxActiveClusters(&n, k_local_fused<8>, &cfg);
+        if (rc == cudaSuccess && n > 0) {
+            lf_cluster_ = C;
+            break;
+        }
+        cudaGetLastError();  // a refused size is not an engine error
+    }
+}
+
+void Engine::set_local_path(int mode) {
+    if (mode < 0 || mode > 1) throw std::runtime_error("local path must be 0 (fused for greedy frames) or 1 (per-step kernels)");
+    local_path_ = mode;
+}
+
+void Engine::launch_local_fused(int R, int step0, int step1) {
+    const int *d_slot = d_ctl_ + off_slot();
+    LfArgs a{};
+    auto lm = [](const DevMat &m) { return LfMat{m.qm, m.sm, m.cols / 32}; };
+    a.attn = lm(local_.attn);
+    a.proj = lm(local_.proj);
+    a.fc_in = lm(local_.fc_in);
+    a.fc_out = lm(local_.fc_out);
+    for (int ch = 0; ch < kNVq; ++ch) {
+        a.head[ch] = lm(aemb_[ch]);
+        a.aemb[ch] = qm(aemb_[ch]);
+    }
+    a.attn_b = local_.attn_b;
+    a.proj_b = local_.proj_b;
+    a.fc_in_b = local_.fc_in_b;
+    a.fc_out_b = local_.fc_out_b;
+    a.ln1_w = local_.ln1_w;
+    a.ln1_b = local_.ln1_b;
+    a.ln2_w = local_.ln2_w;
+    a.ln2_b = local_.ln2_b;
+    a.lnf_w = llnf_w_;
+    a.lnf_b = llnf_b_;
+    a.rope = rope_;
+    a.wte = qm(wte_);
+    a.hidden = hidden_;
+    a.row_slot = d_slot;
+    a.R = R;
+    a.lkv = lkv_;
+    a.qbuf = q_;
+    a.lx_out = lx_;
+    a.logits = logits_;
+    a.counts = counts_;
+    a.ctl = reinterpret_cast<const FrameCtl *>(d_ctl_ + off_fctl());
+    a.forced = d_ctl_ + off_forced();
+    a.active = active_;
+    a.codes_out = codes_;
+    a.used_out = used_;
+    a.step0 = step0;
+    a.step1 = step1;
+    a.err = dev_err_;
+    const int clusters = (R + kLfG - 1) / kLfG;
+    if (lf_cluster_ == 16)
+        launch_kc(pdl_, 16, k_local_fused<16>, dim3(clusters * 16), dim3(kLfThreads), LfSmem<16>::total, stream_, a);
+    else
+        launch_kc(pdl_, 8, k_local_fused<8>, dim3(clusters * 8), dim3(kLfThreads), LfSmem<8>::total, stream_, a);
+    mark(KK_LOCAL_FUSED);
 }
 
 void Engine::set_gemm_path(int mode) {
@@ -681,8 +775,10 @@ void Engine::check_device_error() {
         *h_err_ = 0;
         CK(cudaMemsetAsync(dev_err_, 0, sizeof(int), stream_));
         CK(cudaStreamSynchronize(stream_));
-        throw std::runtime_error(std::string(e == 7 || e == 8 ? "decode-attention page ring" : "tensor-core GEMM barrier") +
-                                 " wait timed out (code " + std::to_string(e) + ")");
+        const char *what = e == 7 || e == 8 ? "decode-attention page ring"
+                           : (e >= 31 && e <= 33) ? "fused local decoder barrier"
+                                                  : "tensor-core GEMM barrier";
+        throw std::runtime_error(std::string(what) + " wait timed out (code " + std::to_string(e) + ")");
     }
 }
 
@@ -1155,7 +1251,9 @@ void Engine::step(const int32_t *sids, int n, const SampleParamsC &p, const int3
     h_ctl_[off_pages()] = int(upd.size() / 3);
     std::memcpy(h_ctl_ + off_pages() + 1, upd.data(), upd.size() * sizeof(int));
     CK(cudaMemcpyAsync(d_ctl_, h_ctl_, size_t(ctl_ints_) * sizeof(int), cudaMemcpyHostToDevice, stream_));
-    run_captured((uint64_t(1) << 40) | (uint64_t(run_global) << 32) | uint64_t(R), [&] { issue_frame(R, run_global); });
+    frame_fused_ = fused_ok(p);
+    run_captured((uint64_t(1) << 40) | (uint64_t(frame_fused_) << 36) | (uint64_t(run_global) << 32) | uint64_t(R),
+                 [&] { issue_frame(R, run_global); });
     // ---- outputs
     uint8_t *ho = h_out_;
     int *h_codes = reinterpret_cast<int *>(ho);
@@ -1230,8 +1328,10 @@ void Engine::step_frames(const int32_t *sids, int n, const SampleParamsC &p, int
     fc->has_forced = 0;
     CK(cudaMemcpyAsync(d_ctl_, h_ctl_, size_t(ctl_ints_) * sizeof(int), cudaMemcpyHostToDevice, stream_));
     int total_launches = 0;
+    frame_fused_ = fused_ok(p);
     for (int f = 0; f < n_frames; ++f) {
-        run_captured((uint64_t(1) << 40) | (uint64_t(1) << 32) | uint64_t(R), [&] { issue_frame(R, true); });
+        run_captured((uint64_t(1) << 40) | (uint64_t(frame_fused_) << 36) | (uint64_t(1) << 32) | uint64_t(R),
+                     [&] { issue_frame(R, true); });
         total_launches += launches_;
         if (timing_ && f + 1 < n_frames) {
             CK(cudaStreamSynchronize(stream_));
@@ -1297,6 +1397,13 @@ void Engine::issue_frame(int R, bool run_global) {
     k_page_updates<<<unsigned((R + 127) / 128), 128, 0, stream_>>>(d_ctl_ + off_pages(), page_table_, pages_per_stream_);
     mark(KK_PAGES);
     // ---- local decoder: 17 steps (llm.cpp:648-698)
+    if (frame_fused_) {  // greedy frames: step 0, the end gate, steps 1..16 with heads and codes
+        launch_local_fused(R, 0, 1);
+        launch_k(pdl_, k_gate, dim3(R), dim3(256), 0, stream_, lx_, R, llnf_w_, llnf_b_, qm(wte_), d_frame, d_fc,
+                 d_ctl_ + off_active_in(), active_, gate_, d_slot, rng_);
+        mark(KK_GATE);
+        launch_local_fused(R, 1, kLocalLen);
+    } else {
     launch_k(pdl_, k_gather_rows, dim3(R), dim3(256), 0, stream_, hidden_, d_slot, R, lx_);
     mark(KK_GATHER);
     for (int ls = 0; ls < kLocalLen; ++ls) {
@@ -1332,6 +1439,7 @@ void Engine::issue_frame(int R, bool run_global) {
             mark(KK_SAMPLE);
         }
     }
+    }
     // ---- global step on [9, used codes] (llm.cpp:703-708)
     if (run_global) {
         launch_k(pdl_, k_embed_frame, dim3(R), dim3(256), 0, stream_, tables(), used_, R, x_);
@@ -1360,7 +1468,8 @@ const char *kernel_kind_name(int kind) {
         "page_updates", "gather_hidden", "lookup_slot_row", "embed_frame", "attn_plan",
         "qkv_global", "attn_decode_paged", "proj_global", "fc_in_global", "fc_out_global", "ln_f",
         "qkv_local", "attn_local", "proj_local", "fc_in_local", "fc_out_local", "gate_w8a8",
-        "audio_heads", "sample", "frame_commit", "build_activation_image", "attn_combine", "attn_prefill", "qkv_rope"};
+        "audio_heads", "sample", "frame_commit", "build_activation_image", "attn_combine", "attn_prefill", "qkv_rope",
+        "local_decoder_fused"};
     return (kind >= 0 && kind < KK_COUNT) ? names[kind] : "?";
 }
 

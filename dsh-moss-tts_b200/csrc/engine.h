@@ -30,6 +30,8 @@ struct DevMat {
     __half *sc = nullptr;   //              [rows/4][cols/32][4] fp16
     int8_t *qt = nullptr;   // tensor-core tiles: [rows/128][cols/64][128][64] int8 (swizzled pieces)
     __half *st = nullptr;   //                    [rows/128][cols/64][128][2] fp16
+    int8_t *qm = nullptr;   // MMA fragment records (local layer, audio heads): [rows/16][cols/32][512] int8
+    __half *sm = nullptr;   //                                                  [rows/16][cols/32][16] fp16
     int rows = 0, cols = 0;
 };
 
@@ -44,7 +46,7 @@ enum KernelKind {
     KK_PAGES, KK_GATHER, KK_LOOKUP, KK_EMBED, KK_PLAN,
     KK_QKV_G, KK_ATTN_DECODE, KK_PROJ_G, KK_FCIN_G, KK_FCOUT_G, KK_LNF,
     KK_QKV_L, KK_ATTN_LOCAL, KK_PROJ_L, KK_FCIN_L, KK_FCOUT_L, KK_GATE, KK_HEADS, KK_SAMPLE, KK_COMMIT,
-    KK_BIMG, KK_ATTN_COMBINE, KK_ATTN_PREFILL, KK_QKV_ROPE,
+    KK_BIMG, KK_ATTN_COMBINE, KK_ATTN_PREFILL, KK_QKV_ROPE, KK_LOCAL_FUSED,
     KK_COUNT
 };
 const char *kernel_kind_name(int kind);
@@ -98,6 +100,10 @@ public:
     // Fault injection for the time-out test: while on, the first global layer's split-K decode
     // attention leaves one ring stage unfilled, so its bounded wait runs out (code 7).
     void debug_inject_wait_timeout(bool on);
+    // Local decoder: 0 = the fused cluster kernel for greedy frames, 1 = the chain of per-step
+    // kernels for every frame (default: measured as fast at 64 streams and faster above).
+    void set_local_path(int mode);
+    int local_cluster() const { return lf_cluster_; }
     void set_cuda_stream(void *s);
     void fill_state_random(int sid, int n_pos, uint64_t seed);
     void set_kernel_timing(bool on);
@@ -215,6 +221,13 @@ private:
     int *dev_err_ = nullptr;       // [0]: kernels' time-out flag; [1]: fault-injection word
     int *h_err_ = nullptr;         // pinned host copy of it
     int gemm_path_ = 0;
+    int local_path_ = 1;     // set_local_path (the fused kernel is opt-in)
+    int lf_cluster_ = 0;     // CTAs per cluster of the fused local decoder (16 or 8; 0 = unavailable)
+    bool frame_fused_ = false;  // the frame being issued runs the fused local decoder
+    void launch_local_fused(int R, int step0, int step1);
+    bool fused_ok(const SampleParamsC &p) const {
+        return local_path_ == 0 && lf_cluster_ > 0 && (p.greedy != 0 || p.top_k == 1);
+    }
     int *d_ctl_ = nullptr, *h_ctl_ = nullptr;
     int ctl_ints_ = 0;
     uint8_t *h_out_ = nullptr;

@@ -158,6 +158,15 @@ int mossgpu_fill_state_random(mossgpu_engine *e, int stream_id, int n_pos, uint6
  * with single fp16 operands instead of the default hi/lo fp16 split (faster, ~5e-4 relative
  * rounding on weights and activations; the default split keeps fp32-level accuracy). */
 int mossgpu_set_graphs(mossgpu_engine *e, int enable);
+/* Local decoder (the 17 one-layer steps, the audio heads and the codes of a frame):
+ * 0 = for greedy frames (params.greedy, or top_k == 1), one fused kernel per frame segment --
+ *   step 0, then steps 1..16 after the end gate -- in which thread-block clusters of 8 rows keep
+ *   the activations on chip and stream the local weights from L2; other frames take the
+ *   per-step kernels;
+ * 1 (default) = the per-step kernels for every frame (about 10 launches per step).  Measured
+ *   on one B200: 1.97 ms per 64-stream frame either way, and at 512 streams the fused form is
+ *   slower (5.1 against 2.5 ms for the local decoder), so it is not the default. */
+int mossgpu_set_local_path(mossgpu_engine *e, int mode);
 int mossgpu_set_gemm_path(mossgpu_engine *e, int mode);
 /* Tensor-core GEMM form by batch size: batches of at least direct_min_rows padded rows run
  * one CTA per (128 weight rows, slice of direct_rows batch rows) over the whole K with the
