@@ -305,6 +305,8 @@ def run_ours(args, rank, world, local_rank, dist):
     eng.set_cuda_stream(torch.cuda.current_stream().cuda_stream)
     if args.tc_direct_min is not None:
         eng.set_tc_policy(args.tc_direct_min, 256)
+    if args.local_path is not None:
+        eng.set_local_path(args.local_path)
     sids = [eng.open() for _ in lens]
 
     def reset_states():
@@ -400,7 +402,8 @@ def run_ours(args, rank, world, local_rank, dist):
 
     # ---- configs[1] frame (64 streams per GPU, KV U{64..1024}) and configs[2] prefill:
     # reported beside the headline, each in an engine of its own
-    c1 = run_configs1_frame(pkg, weights, local_rank, torch, rank, K, W) if args.workload == "configs4" else None
+    c1 = run_configs1_frame(pkg, weights, local_rank, torch, rank, K, W, args.local_path) \
+        if args.workload == "configs4" else None
     pf = run_prefill(pkg, weights, local_rank, torch, n_prompts=16, rows=256)
     pf["frac_of_bf16_peak"] = round(pf["tflops"] / pk["bf16_tflops"], 4)
 
@@ -517,11 +520,13 @@ def gather_stats(dist, values: list[float]) -> list[list[float]]:
     return [o.cpu().tolist() for o in out]
 
 
-def run_configs1_frame(pkg, weights, device, torch, rank, K, W) -> dict:
+def run_configs1_frame(pkg, weights, device, torch, rank, K, W, local_path=None) -> dict:
     """configs[1] on this GPU: 64 streams, KV U{64..1024}, K frames on the device."""
     lens = [int(x) for x in np.random.default_rng(1234 + rank).integers(64, 1025, 64)]
     eng = pkg.Engine(weights, device=device, max_streams=65, max_ctx=1024 + W + K + 32)
     eng.set_cuda_stream(torch.cuda.current_stream().cuda_stream)
+    if local_path is not None:
+        eng.set_local_path(local_path)
     sids = [eng.open() for _ in lens]
     p = pkg.SampleParams.make(greedy=True, repetition_penalty=1.2, min_frames=1 << 30)
 
@@ -658,6 +663,9 @@ def main():
     ap.add_argument("--lmax", type=int, default=None)
     ap.add_argument("--tc-direct-min", type=int, default=None,
                     help="batch rows from which the GEMMs use the direct tile form (mossgpu_set_tc_policy)")
+    ap.add_argument("--local-path", type=int, default=None,
+                    help="local decoder: 0 = fused cluster kernel for greedy frames, 1 = per-step kernels "
+                         "(mossgpu_set_local_path; default: the engine's)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep", action="store_true",
                     help="configs[4] sustained: every stream runs --sweep-frames frames (400), per-frame latency")

@@ -55,11 +55,12 @@ constexpr int kLfUnitS = 768;         // its fp16 scales (24 x 16)
 constexpr int kLfStage = kLfUnitQ + kLfUnitS;
 constexpr int kLfActStride = kHidden + 32;  // halves per activation row (conflict-free 16 B loads)
 
-// Weight matrix in the MMA fragment layout (k_repack_mma): [rows/16][nb][512] int8 and
+// Weight matrix in the MMA fragment layout (k_repack_mma): [rows/16][nb][512] bytes and
 // [rows/16][nb][16] fp16.  In the 512-byte record of (16-row tile, 32-column block), lane
 // L = 4 g + t owns bytes [16 L, 16 L + 16): row g at columns 2t + (j & 1) + 8 (j >> 1) for
-// j = 0..7, then row g + 8 at the same columns.  The 16 scales are ordered (row g, row g + 8)
-// for g = 0..7.
+// j = 0..7, then row g + 8 at the same columns.  Each byte holds q + 128 (the int8 quant in
+// offset binary, ready for the fp16 conversion below).  The 16 scales are ordered (row g,
+// row g + 8) for g = 0..7.
 struct LfMat {
     const int8_t *qm;
     const __half *sm;
@@ -84,7 +85,7 @@ __global__ void k_repack_mma(const int8_t *__restrict__ qs, const __half *__rest
     for (int j = 0; j < 16; ++j) {
         const int row = tile * 16 + g + 8 * (j >> 3);
         const int col = 2 * t + (j & 1) + 8 * ((j >> 1) & 3);
-        out[j] = qs[((size_t)(row >> 2) * nb + b) * 128 + (row & 3) * 32 + col];
+        out[j] = (int8_t)(qs[((size_t)(row >> 2) * nb + b) * 128 + (row & 3) * 32 + col] ^ 0x80);
     }
     *reinterpret_cast<int4 *>(qm + (size_t)tb * 512 + lane * 16) = *reinterpret_cast<const int4 *>(out);
     if (lane < 16) {
@@ -120,12 +121,11 @@ struct LfArgs {
 
 __device__ __forceinline__ int4 lds128(const void *p) { return *reinterpret_cast<const int4 *>(p); }
 
-// 4 int8 -> two half2 (bytes 0,1 and bytes 2,3), exact: 0x64XX is 1024 + XX as fp16, and
-// XX = b ^ 0x80 = b + 128, so (0x64XX - 1152) = b.
+// 4 offset-binary bytes (q + 128) -> two half2 of q (bytes 0,1 and bytes 2,3), exact: 0x64XX
+// is 1024 + XX as fp16, and XX = q + 128, so (0x64XX - 1152) = q.
 __device__ __forceinline__ void i8x4_to_h2x2(uint32_t w, uint32_t &lo, uint32_t &hi) {
-    const uint32_t v = w ^ 0x80808080u;
-    const uint32_t a = __byte_perm(v, 0x64646464u, 0x5140);
-    const uint32_t b = __byte_perm(v, 0x64646464u, 0x7362);
+    const uint32_t a = __byte_perm(w, 0x64646464u, 0x5140);
+    const uint32_t b = __byte_perm(w, 0x64646464u, 0x7362);
     const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));  // 1152
     const __half2 ha = __hsub2(*reinterpret_cast<const __half2 *>(&a), bias);
     const __half2 hb = __hsub2(*reinterpret_cast<const __half2 *>(&b), bias);
@@ -169,6 +169,11 @@ __device__ __forceinline__ void lf_st_f32(uint32_t addr, float v) {
 }
 __device__ __forceinline__ void lf_st_u32(uint32_t addr, uint32_t v) {
     asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ float lf_ld_f32(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
 }
 __device__ __forceinline__ void lf_st_s32(uint32_t addr, int v) {
     asm volatile("st.shared::cluster.s32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
@@ -262,14 +267,16 @@ struct LfSmem {
     static constexpr int act_lo = act_hi + kLfG * kLfActStride * 2;
     static constexpr int gel_hi = act_lo + kLfG * kLfActStride * 2; // half [8][kGel]
     static constexpr int gel_lo = gel_hi + kLfG * kGel * 2;
-    static constexpr int recv = gel_lo + kLfG * kGel * 2;           // float [C][8][kMo]
-    static constexpr int lgt = recv + C * kLfG * kMo * 4;           // float [8][kMh]
+    static constexpr int part = gel_lo + kLfG * kGel * 2;           // float [8][768]: fc_out partials
+    static constexpr int lnp = part + kLfG * kHidden * 4;           // float [6][768]: LN1, LN2, ln_f w and b
+    static constexpr int lgt = lnp + 6 * kHidden * 4;               // float [8][kMh]
     static constexpr int cand_v = lgt + kLfG * kMh * 4;             // float [C][8]
     static constexpr int cand_i = cand_v + C * kLfG * 4;            // int [C][8]
     static constexpr int used = cand_i + C * kLfG * 4;              // int [8]
-    static constexpr int flags = used + kLfG * 4;                   // int failed + pad
+    static constexpr int hist = used + kLfG * 4;                    // int [8][16]: codes used per channel
+    static constexpr int flags = hist + kLfG * kNVq * 4;            // int failed + pad
     static constexpr int bars = (flags + 16 + 7) / 8 * 8;
-    static constexpr int kStages = 10 + (C >= 16 ? 1 : 0);
+    static constexpr int kStages = 9;
     static constexpr int ring = (bars + (2 * kStages + 2) * 8 + 127) / 128 * 128;
     static constexpr int total = ring + kStages * kLfStage;
 };
@@ -399,7 +406,9 @@ __global__ void __launch_bounds__(kLfThreads, 1) k_local_fused(const LfArgs a) {
     __half *act_lo = reinterpret_cast<__half *>(lf_smem + S::act_lo);
     __half *gel_hi = reinterpret_cast<__half *>(lf_smem + S::gel_hi);
     __half *gel_lo = reinterpret_cast<__half *>(lf_smem + S::gel_lo);
-    float *recv = reinterpret_cast<float *>(lf_smem + S::recv);
+    float *part = reinterpret_cast<float *>(lf_smem + S::part);
+    float *lnp = reinterpret_cast<float *>(lf_smem + S::lnp);
+    int *hist = reinterpret_cast<int *>(lf_smem + S::hist);
     float *lgt = reinterpret_cast<float *>(lf_smem + S::lgt);
     float *cand_v = reinterpret_cast<float *>(lf_smem + S::cand_v);
     int *cand_i = reinterpret_cast<int *>(lf_smem + S::cand_i);
@@ -470,7 +479,14 @@ __global__ void __launch_bounds__(kLfThreads, 1) k_local_fused(const LfArgs a) {
         const int g = lane >> 2, t = lane & 3;
         // remote (cluster) addresses of the exchanged buffers: base of CTA d's copy
         const uint32_t xres_s = smem_u32(xres), acth_s = smem_u32(act_hi), actl_s = smem_u32(act_lo);
-        const uint32_t recv_s = smem_u32(recv), cv_s = smem_u32(cand_v), ci_s = smem_u32(cand_i);
+        const uint32_t part_s = smem_u32(part), cv_s = smem_u32(cand_v), ci_s = smem_u32(cand_i);
+        {   // LayerNorm parameters (LN1, LN2, ln_f; weight and bias) stay in shared memory
+            const float *src[6] = {a.ln1_w, a.ln1_b, a.ln2_w, a.ln2_b, a.lnf_w, a.lnf_b};
+#pragma unroll
+            for (int v = 0; v < 6; ++v)
+                for (int i = tid; i < kHidden / 4; i += kLfWarps * 32)
+                    reinterpret_cast<float4 *>(lnp + v * kHidden)[i] = reinterpret_cast<const float4 *>(src[v])[i];
+        }
         // initial residual stream: the global hidden state (step 0) or the slot-token row (step 1)
         if (a.step0 == 0) {
             constexpr int per = kLfG * kHidden / 4 / (kLfWarps * 32);  // float4s per thread
@@ -519,7 +535,7 @@ __global__ void __launch_bounds__(kLfThreads, 1) k_local_fused(const LfArgs a) {
 
         for (int ls = a.step0; ls < a.step1; ++ls) {
             // ---- LN1 -> QKV slice
-            if (warp < kLfG) lf_layernorm(xres, warp, a.ln1_w, a.ln1_b, act_hi, act_lo, lane);
+            if (warp < kLfG) lf_layernorm(xres, warp, lnp, lnp + kHidden, act_hi, act_lo, lane);
             lf_named_sync();
             {
                 const LfPhase p = lf_phase<C>(a, LF_QKV, ls, c);
@@ -626,7 +642,7 @@ __global__ void __launch_bounds__(kLfThreads, 1) k_local_fused(const LfArgs a) {
             }
             cluster_phase();
             // ---- LN2 -> fc_in slice + bias + GELU -> own fc_out input
-            if (warp < kLfG) lf_layernorm(xres, warp, a.ln2_w, a.ln2_b, act_hi, act_lo, lane);
+            if (warp < kLfG) lf_layernorm(xres, warp, lnp + 2 * kHidden, lnp + 3 * kHidden, act_hi, act_lo, lane);
             lf_named_sync();
             {
                 const LfPhase p = lf_phase<C>(a, LF_FCIN, ls, c);
@@ -648,7 +664,7 @@ __global__ void __launch_bounds__(kLfThreads, 1) k_local_fused(const LfArgs a) {
                 });
             }
             lf_named_sync();
-            // ---- fc_out partial over the K slice -> the CTA that owns each output row
+            // ---- fc_out partial over the K slice, kept here until its owner CTA pulls it
             {
                 const LfPhase p = lf_phase<C>(a, LF_FCOUT, ls, c);
                 gemm(p, gel_hi, gel_lo, S::kGel, Fco{}, [&](float(&acc)[Fco::MT][4], int i) {
@@ -657,25 +673,25 @@ __global__ void __launch_bounds__(kLfThreads, 1) k_local_fused(const LfArgs a) {
 #pragma unroll
                         for (int h = 0; h < 2; ++h) {
                             const int f = i * p.rstep + mt * 16 + g + 8 * h;
-                            const int d = f / S::kMo, j = f - d * S::kMo;
 #pragma unroll
-                            for (int e = 0; e < 2; ++e) {
-                                const int n = 2 * t + e;
-                                const uint32_t off = (uint32_t)(((c * kLfG + n) * S::kMo) + j) * 4;
-                                lf_st_f32(lf_map(recv_s + off, (uint32_t)d), acc[mt][2 * h + e]);
-                            }
+                            for (int e = 0; e < 2; ++e) part[(2 * t + e) * kHidden + f] = acc[mt][2 * h + e];
                         }
                 });
             }
             cluster_phase();
-            // ---- this CTA's rows of fc_out: the C partials in order + bias + residual -> everyone
+            // ---- this CTA's rows of fc_out: the C partials in order (read from every CTA) + bias +
+            // residual -> everyone
             for (int i = tid; i < kLfG * S::kMo; i += kLfWarps * 32) {
                 const int n = i / S::kMo, j = i - n * S::kMo, f = c * S::kMo + j;
-                float sum = recv[(0 * kLfG + n) * S::kMo + j];
-                for (int src = 1; src < C; ++src) sum = __fadd_rn(sum, recv[(src * kLfG + n) * S::kMo + j]);
-                const float xn = __fadd_rn(xres[n * kHidden + f], __fadd_rn(sum, a.fc_out_b[f]));
                 const uint32_t off = (uint32_t)(n * kHidden + f) * 4;
-                for (int d = 0; d < C; ++d) lf_st_f32(lf_map(xres_s + off, (uint32_t)d), xn);
+                float pv[C];
+#pragma unroll
+                for (int src = 0; src < C; ++src) pv[src] = lf_ld_f32(lf_map(part_s + off, (uint32_t)src));
+                float sum = pv[0];
+#pragma unroll
+                for (int src = 1; src < C; ++src) sum = __fadd_rn(sum, pv[src]);
+                const float xn = __fadd_rn(xres[n * kHidden + f], __fadd_rn(sum, a.fc_out_b[f]));
+                for (int d = 0; d < C; ++d) lf_st_f32(lf_map(xres_s + off, (uint32_t)d), xn);  // same [8][768] layout
             }
             cluster_phase();
             if (ls == 0) {  // step 0's output: the end gate's input; step 1's input is the slot token
@@ -689,7 +705,7 @@ __global__ void __launch_bounds__(kLfThreads, 1) k_local_fused(const LfArgs a) {
             }
             // ---- ln_f -> head slice -> logits and this CTA's candidate per row
             const int ch = ls - 1;
-            if (warp < kLfG) lf_layernorm(xres, warp, a.lnf_w, a.lnf_b, act_hi, act_lo, lane);
+            if (warp < kLfG) lf_layernorm(xres, warp, lnp + 4 * kHidden, lnp + 5 * kHidden, act_hi, act_lo, lane);
             lf_named_sync();
             {
                 const LfPhase p = lf_phase<C>(a, LF_HEAD, ls, c);
@@ -766,18 +782,29 @@ __global__ void __launch_bounds__(kLfThreads, 1) k_local_fused(const LfArgs a) {
                     if (c == 0 && lane == 0) {
                         a.codes_out[r * kNVq + ch] = pred;
                         a.used_out[r * kNVq + ch] = usedc;
-                        if (a.active[r] && usedc >= 0 && usedc < kCodebook) {
-                            uint16_t *cnt = a.counts + ((size_t)a.row_slot[r] * kNVq + ch) * kCodebook;
-                            cnt[usedc] = (uint16_t)(cnt[usedc] + 1);
-                        }
                     }
                 }
-                if (lane == 0) used_s[n] = usedc;
+                if (lane == 0) {
+                    used_s[n] = usedc;
+                    hist[n * kNVq + ch] = usedc;
+                }
             }
             lf_named_sync();
             if (ch + 1 < kNVq) {
                 lf_gather_rows(xres, a.aemb[ch], used_s, tid);
                 lf_named_sync();
+            }
+        }
+    }
+    // the repetition history (sampler.cpp:14-21): a channel's counts are read only when that
+    // channel samples, so the frame's increments can wait until every channel has sampled
+    if (warp < kLfG && c == 0 && a.step1 > 1 && lane < kNVq) {
+        const int n = warp, ch = lane;
+        if (n < nrows && ch >= max(a.step0, 1) - 1 && ch < a.step1 - 1) {
+            const int r = rbase + n, uc = hist[n * kNVq + ch];
+            if (a.active[r] && uc >= 0 && uc < kCodebook) {
+                uint16_t *cnt = a.counts + ((size_t)a.row_slot[r] * kNVq + ch) * kCodebook;
+                cnt[uc] = (uint16_t)(cnt[uc] + 1);
             }
         }
     }
