@@ -10,6 +10,10 @@ csrc/).  This module is the Python host side over that ABI:
                 stream, with the same method names, argument meaning and error behaviour
                 (load() returns (ok, err); generate() stops on the end gate, honours
                 teacher forcing, the cancel flag and the logits dump).
+* `Codec`    -- the batched audio codec decoder (mossgpu_codec_*): codec streams, chunked
+                decode of many streams per call, whole-utterance decode.
+* `AudioDecoder` -- the reference's `moss::AudioDecoder` interface (decoder.h:16-33) over one
+                Codec stream: load, decode, reset_stream, decode_chunk.
 
 There is no CPU fallback: constructing an Engine without the built library or without a
 CUDA device raises.
@@ -42,6 +46,10 @@ EXPORTS = [
     "mossgpu_attention_decode_paged_noalloc", "mossgpu_set_gemm_path", "mossgpu_debug_matrix_tile_bytes",
     "mossgpu_stream_fork", "mossgpu_create_rows", "mossgpu_prefill_batch", "mossgpu_prefill_embeds_batch",
     "mossgpu_set_tc_policy", "mossgpu_op_device_status", "mossgpu_debug_inject_wait_timeout", "mossgpu_set_local_path",
+    "mossgpu_codec_create", "mossgpu_codec_destroy", "mossgpu_codec_last_error", "mossgpu_codec_samples_per_frame",
+    "mossgpu_codec_launches_per_call", "mossgpu_codec_device_bytes", "mossgpu_codec_set_cuda_stream",
+    "mossgpu_codec_open", "mossgpu_codec_close", "mossgpu_codec_reset", "mossgpu_codec_decode_chunk",
+    "mossgpu_codec_decode_batch", "mossgpu_codec_decode_batch_device", "mossgpu_codec_decode",
 ]
 
 
@@ -134,6 +142,24 @@ def lib() -> C.CDLL:
         L.mossgpu_set_local_path.argtypes = [C.c_void_p, C.c_int]
         L.mossgpu_attention_decode_paged_noalloc.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p,
                                                              C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]
+        L.mossgpu_codec_create.restype = C.c_void_p
+        L.mossgpu_codec_create.argtypes = [C.c_char_p, C.c_int, C.c_int, C.c_int, C.c_char_p, C.c_int]
+        L.mossgpu_codec_destroy.argtypes = [C.c_void_p]
+        L.mossgpu_codec_last_error.restype = C.c_char_p
+        L.mossgpu_codec_last_error.argtypes = [C.c_void_p]
+        L.mossgpu_codec_samples_per_frame.argtypes = [C.c_void_p]
+        L.mossgpu_codec_launches_per_call.argtypes = [C.c_void_p]
+        L.mossgpu_codec_device_bytes.restype = C.c_size_t
+        L.mossgpu_codec_device_bytes.argtypes = [C.c_void_p]
+        L.mossgpu_codec_set_cuda_stream.argtypes = [C.c_void_p, C.c_void_p]
+        L.mossgpu_codec_open.argtypes = [C.c_void_p, C.POINTER(C.c_int)]
+        L.mossgpu_codec_close.argtypes = [C.c_void_p, C.c_int]
+        L.mossgpu_codec_reset.argtypes = [C.c_void_p, C.c_int]
+        L.mossgpu_codec_decode_chunk.argtypes = [C.c_void_p, C.c_int, _i32, C.c_int, _f32, C.c_size_t,
+                                                 C.POINTER(C.c_int)]
+        L.mossgpu_codec_decode_batch.argtypes = [C.c_void_p, _i32, C.c_int, _i32, C.c_int, _f32, C.c_size_t]
+        L.mossgpu_codec_decode_batch_device.argtypes = [C.c_void_p, _i32, C.c_int, C.c_void_p, C.c_int, C.c_void_p]
+        L.mossgpu_codec_decode.argtypes = [C.c_void_p, _i32, C.c_int, _f32, C.c_size_t, C.POINTER(C.c_int)]
         _LIB = L
         return L
 
@@ -431,3 +457,119 @@ class LlmModel:
                 for f, m in gate_dump:
                     fh.write(f"{f},{m:.4f}\n")
         return frames
+
+
+class Codec:
+    """One GPU's batched audio codec decoder (mossgpu_codec_create)."""
+
+    def __init__(self, decoder_path: str, device: int = 0, max_streams: int = 8, max_batch_frames: int = 64):
+        self.lib = lib()
+        err = C.create_string_buffer(1024)
+        self.h = self.lib.mossgpu_codec_create(str(decoder_path).encode(), device, max_streams, max_batch_frames,
+                                               err, 1024)
+        if not self.h:
+            raise MossGpuError(err.value.decode(errors="replace"))
+        self.max_streams, self.max_batch_frames = max_streams, max_batch_frames
+        self.samples_per_frame = self.lib.mossgpu_codec_samples_per_frame(self.h)
+
+    def _check(self, rc: int):
+        if rc != 0:
+            raise MossGpuError(self.lib.mossgpu_codec_last_error(self.h).decode(errors="replace"))
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.mossgpu_codec_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def set_cuda_stream(self, stream_handle: int | None):
+        self._check(self.lib.mossgpu_codec_set_cuda_stream(self.h, C.c_void_p(stream_handle or 0)))
+
+    def launches_per_call(self) -> int:
+        return self.lib.mossgpu_codec_launches_per_call(self.h)
+
+    def device_bytes(self) -> int:
+        return self.lib.mossgpu_codec_device_bytes(self.h)
+
+    def open(self) -> int:
+        sid = C.c_int(-1)
+        self._check(self.lib.mossgpu_codec_open(self.h, C.byref(sid)))
+        return sid.value
+
+    def close_stream(self, sid: int):
+        self._check(self.lib.mossgpu_codec_close(self.h, sid))
+
+    def reset(self, sid: int):
+        self._check(self.lib.mossgpu_codec_reset(self.h, sid))
+
+    def decode_chunk(self, sid: int, codes) -> np.ndarray:
+        """codes [16][frames] -> samples [frames * samples_per_frame]."""
+        codes = np.ascontiguousarray(codes, np.int32).reshape(NVQ, -1)
+        frames = codes.shape[1]
+        out = np.empty(frames * self.samples_per_frame, np.float32)
+        n = C.c_int(0)
+        self._check(self.lib.mossgpu_codec_decode_chunk(self.h, sid, codes, frames, out, out.size, C.byref(n)))
+        return out[:n.value]
+
+    def decode_batch(self, sids, codes) -> np.ndarray:
+        """codes [n][16][frames] -> samples [n][frames * samples_per_frame]."""
+        sids = np.ascontiguousarray(sids, np.int32).reshape(-1)
+        codes = np.ascontiguousarray(codes, np.int32).reshape(sids.size, NVQ, -1)
+        frames = codes.shape[2]
+        out = np.empty((sids.size, frames * self.samples_per_frame), np.float32)
+        self._check(self.lib.mossgpu_codec_decode_batch(self.h, sids, sids.size, codes, frames, out, out.size))
+        return out
+
+    def decode_batch_device(self, sids, codes_ptr: int, frames: int, out_ptr: int):
+        """Enqueue a batch with device codes [n][16][frames] (int32) and output (fp32)."""
+        sids = np.ascontiguousarray(sids, np.int32).reshape(-1)
+        self._check(self.lib.mossgpu_codec_decode_batch_device(self.h, sids, sids.size, C.c_void_p(codes_ptr),
+                                                               frames, C.c_void_p(out_ptr)))
+
+    def decode(self, codes) -> np.ndarray:
+        """A whole utterance, codes [16][frames], from a clean state."""
+        codes = np.ascontiguousarray(codes, np.int32).reshape(NVQ, -1)
+        frames = codes.shape[1]
+        out = np.empty(frames * self.samples_per_frame, np.float32)
+        n = C.c_int(0)
+        self._check(self.lib.mossgpu_codec_decode(self.h, codes, frames, out, out.size, C.byref(n)))
+        return out[:n.value]
+
+
+class AudioDecoder:
+    """The reference's moss::AudioDecoder interface (decoder.h:16-33) over one Codec stream.
+
+    `threads` is accepted for the signature and ignored (the work runs on the GPU)."""
+
+    def __init__(self, threads: int = 1, device: int = 0, max_chunk_frames: int = 64):
+        self._device, self._max_chunk = device, max_chunk_frames
+        self._codec = None
+        self._sid = None
+        self._info = ""
+
+    def load(self, path: str) -> tuple[bool, str]:  # decoder.h:21
+        try:
+            self._codec = Codec(path, self._device, max_streams=1, max_batch_frames=self._max_chunk)
+            self._sid = self._codec.open()
+        except (MossGpuError, OSError) as e:
+            return False, str(e)
+        self._info = f"decoder weights={path} device={self._device}"
+        return True, ""
+
+    def decode(self, codes, frames: int) -> np.ndarray:  # decoder.h:24
+        return self._codec.decode(np.asarray(codes, np.int32).reshape(NVQ, frames))
+
+    def reset_stream(self):  # decoder.h:27
+        self._codec.reset(self._sid)
+
+    def decode_chunk(self, codes, frames: int) -> np.ndarray:  # decoder.h:29
+        codes = np.asarray(codes, np.int32).reshape(NVQ, frames)
+        if frames <= self._max_chunk:
+            return self._codec.decode_chunk(self._sid, codes)
+        return np.concatenate([self._codec.decode_chunk(self._sid, codes[:, f:f + self._max_chunk])
+                               for f in range(0, frames, self._max_chunk)])
+
+    def info(self) -> str:
+        return self._info

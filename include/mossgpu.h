@@ -246,6 +246,56 @@ int mossgpu_attention_decode_paged_noalloc(const float *q, const void *kv_layer,
                                            int pages_per_stream, const int32_t *row_slot, const int32_t *row_pos,
                                            int R, float *out, void *cuda_stream);
 
+/* ---- the audio codec decoder (codes -> 48 kHz interleaved stereo samples) ----
+ *
+ * Replaces moss::AudioDecoder (reference csrc/include/moss/decoder.h:16-79,
+ * csrc/src/decoder.cpp) with a batched device decoder.  One codec holds up to max_streams
+ * "codec streams"; each is one utterance's streaming state as AudioDecoder keeps it (the
+ * RoPE offset of each of the 4 stages and the last 500 / 800 / 1200 / 1600 K and V rows of
+ * each of their 12 layers).  Codes are laid out [16][frames] per stream (decoder.h:23, the
+ * codebook index major), each in [0, 1024); samples are fp32, frames * 7680 per stream
+ * (samples_per_frame: 32 rows x 240 of the last stage, interleaved L, R at 48 kHz).
+ * The decoder file is the reference's .moss export with f16 matrices (decoder_f16.moss,
+ * tools/export_decoder.py --dtype f16); other matrix types are rejected at create.
+ * Products are fp32 accumulations of fp16 weights and fp32 activations, as the reference's
+ * gemm_par on f16 matrices; results agree with the reference's to float rounding, not bit
+ * for bit.  Conventions as above: 0 on success, the message from mossgpu_codec_last_error. */
+typedef struct mossgpu_codec mossgpu_codec;
+
+/* AudioDecoder(threads) + load (decoder.cpp:26-71).  max_batch_frames bounds the frames one
+ * call decodes over all its streams (streams x frames); it sizes the activation buffers. */
+mossgpu_codec *mossgpu_codec_create(const char *decoder_path, int device_id, int max_streams, int max_batch_frames,
+                                    char *err, int errlen);
+void mossgpu_codec_destroy(mossgpu_codec *c);
+const char *mossgpu_codec_last_error(mossgpu_codec *c);
+int mossgpu_codec_samples_per_frame(mossgpu_codec *c);
+/* Kernel launches one decode call enqueues (whatever its batch). */
+int mossgpu_codec_launches_per_call(mossgpu_codec *c);
+size_t mossgpu_codec_device_bytes(mossgpu_codec *c);
+/* The CUDA stream (cudaStream_t; NULL = legacy default) every later call enqueues on. */
+int mossgpu_codec_set_cuda_stream(mossgpu_codec *c, void *cuda_stream);
+/* A codec stream in the clean state; close frees its slot. */
+int mossgpu_codec_open(mossgpu_codec *c, int *stream_id);
+int mossgpu_codec_close(mossgpu_codec *c, int stream_id);
+/* AudioDecoder::reset_stream (decoder.cpp:105-114): back to the clean state. */
+int mossgpu_codec_reset(mossgpu_codec *c, int stream_id);
+/* AudioDecoder::decode_chunk (decoder.cpp:211-225): codes [16][frames] -> out
+ * [frames * samples_per_frame]; *out_n = samples written.  Chunks of one stream must come in
+ * order; the call returns when the samples are in `out`. */
+int mossgpu_codec_decode_chunk(mossgpu_codec *c, int stream_id, const int32_t *codes, int frames, float *out,
+                               size_t out_cap, int *out_n);
+/* decode_chunk for n distinct streams at once, each `frames` frames: codes [n][16][frames],
+ * out [n][frames * samples_per_frame]; each stream ends as after its own decode_chunk. */
+int mossgpu_codec_decode_batch(mossgpu_codec *c, const int32_t *stream_ids, int n, const int32_t *codes, int frames,
+                               float *out, size_t out_cap);
+/* The same with DEVICE codes and output; only enqueues work on the codec's stream.  A code
+ * outside [0, 1024) is clamped here (the host entry points reject it). */
+int mossgpu_codec_decode_batch_device(mossgpu_codec *c, const int32_t *stream_ids, int n, const int32_t *codes_dev,
+                                      int frames, float *out_dev);
+/* AudioDecoder::decode (decoder.cpp:254-280): a whole utterance, codes [16][frames], from a
+ * clean state, leaving every codec stream untouched. */
+int mossgpu_codec_decode(mossgpu_codec *c, const int32_t *codes, int frames, float *out, size_t out_cap, int *out_n);
+
 #ifdef __cplusplus
 }
 #endif

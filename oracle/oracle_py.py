@@ -332,3 +332,49 @@ class RefModel:
         n = self.lib.ref_generate(self.h, frames, int(greedy), temperature, top_k, top_p, rep, int(end_greedy),
                                   min_frames, greedy_frames, seed, _ptr(f), codes, _ptr(logits), tmp)
         return codes[:n], (logits[:n] if want_logits else None)
+
+
+class RefCodec:
+    """The reference's own AudioDecoder (decoder.cpp) in oracle/_ref/libmossref.so: streaming
+    decode_chunk / reset_stream and the whole-utterance decode."""
+
+    def __init__(self, weights: str, threads: int = 1):
+        self.lib = RefModel.lib()
+        L = self.lib
+        L.ref_codec_create.restype = C.c_void_p
+        L.ref_codec_create.argtypes = [C.c_char_p, C.c_int]
+        L.ref_codec_destroy.argtypes = [C.c_void_p]
+        L.ref_codec_reset.argtypes = [C.c_void_p]
+        L.ref_codec_decode_chunk.restype = C.c_int
+        L.ref_codec_decode_chunk.argtypes = [C.c_void_p, _i32p, C.c_int, _f32p, C.c_int]
+        L.ref_codec_decode.restype = C.c_int
+        L.ref_codec_decode.argtypes = [C.c_void_p, _i32p, C.c_int, _f32p, C.c_int]
+        self.h = L.ref_codec_create(str(weights).encode(), threads)
+        if not self.h:
+            raise RuntimeError("reference failed to load the decoder")
+
+    def close(self):
+        if self.h:
+            self.lib.ref_codec_destroy(self.h)
+            self.h = None
+
+    __del__ = close
+
+    def reset(self):
+        self.lib.ref_codec_reset(self.h)
+
+    def _run(self, fn, codes):
+        codes = np.ascontiguousarray(codes, np.int32)  # [16][frames]
+        frames = codes.shape[1]
+        out = np.empty(frames * 7680 + 16, np.float32)
+        n = fn(self.h, codes, frames, out, out.size)
+        if n < 0:
+            raise RuntimeError("output buffer too small")
+        return out[:n].copy()
+
+    def decode_chunk(self, codes):
+        return self._run(self.lib.ref_codec_decode_chunk, codes)
+
+    def decode(self, codes):
+        return self._run(self.lib.ref_codec_decode, codes)
+

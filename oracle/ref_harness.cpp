@@ -32,6 +32,7 @@
 #include "moss/gemv.h"
 #include "moss/sampler.h"
 #include "moss/fp16.h"
+#include "moss/decoder.h"
 
 using namespace moss;
 
@@ -261,6 +262,41 @@ int ref_sample_token(const float *logits, int n, int greedy, float temperature, 
     rng.seed(seed);
     std::vector<float> scratch;
     return sample_token(logits, n, p, prev, n_prev, rng, scratch);
+}
+
+// ---- the reference's audio codec decoder (decoder.cpp), through its public API
+
+void *ref_codec_create(const char *path, int threads) {
+    auto *d = new AudioDecoder(threads);
+    std::string err;
+    if (!d->load(path, &err)) {
+        std::fprintf(stderr, "ref_codec_create: %s\n", err.c_str());
+        delete d;
+        return nullptr;
+    }
+    d->reset_stream();
+    return d;
+}
+
+void ref_codec_destroy(void *h) { delete static_cast<AudioDecoder *>(h); }
+
+void ref_codec_reset(void *h) { static_cast<AudioDecoder *>(h)->reset_stream(); }
+
+// AudioDecoder::decode_chunk: codes [16][frames] (nq-major); returns the sample count written
+// to out (at most cap), or -1 when out is too small.
+int ref_codec_decode_chunk(void *h, const int32_t *codes, int frames, float *out, int cap) {
+    const std::vector<float> y = static_cast<AudioDecoder *>(h)->decode_chunk(codes, frames);
+    if (static_cast<int>(y.size()) > cap) return -1;
+    std::memcpy(out, y.data(), y.size() * sizeof(float));
+    return static_cast<int>(y.size());
+}
+
+// AudioDecoder::decode: a whole utterance, non-streaming
+int ref_codec_decode(void *h, const int32_t *codes, int frames, float *out, int cap) {
+    const std::vector<float> y = static_cast<AudioDecoder *>(h)->decode(codes, frames);
+    if (static_cast<int>(y.size()) > cap) return -1;
+    std::memcpy(out, y.data(), y.size() * sizeof(float));
+    return static_cast<int>(y.size());
 }
 
 }  // extern "C"

@@ -52,3 +52,17 @@ def weights_digest_ok(weights_path) -> bool:
     meta = json.loads((ROOT / "tests" / "golden" / "weights.json").read_text())
     h = hashlib.sha256(Path(weights_path).read_bytes()).hexdigest()
     return h == meta["sha256"]
+
+
+@pytest.fixture(scope="session")
+def golden_dir() -> Path:
+    return ROOT / "tests" / "golden"
+
+
+@pytest.fixture(scope="session")
+def decoder_file() -> str:
+    """The seed-1 synthetic audio codec decoder, generated once per machine (about a second)."""
+    from golden_inputs import CODEC_DECODER_SEED
+    from moss_b200 import codecfile
+    path = Path(tempfile.gettempdir()) / f"moss_b200_dec{CODEC_DECODER_SEED}.moss"
+    return codecfile.ensure_synth_decoder(path, CODEC_DECODER_SEED)

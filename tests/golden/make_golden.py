@@ -30,7 +30,8 @@ sys.path.insert(0, str(ROOT / "oracle"))
 sys.path.insert(0, str(ROOT / "tests"))
 
 from golden_inputs import (END_SEEDS, LONG_CTX, PREFIX_FILE_ROWS, SAMPLER_SWEEP, WEIGHTS_SEED, global_state, prompt_rows,  # noqa: E402
-                           forced_codes, sampler_case, sampler_sweep_case, sha)
+                           forced_codes, sampler_case, sampler_sweep_case, sha, CODEC_CASES, CODEC_DECODER_SEED,
+                           CODEC_STRIDE, codec_codes, codec_frame_energy)
 
 # the reference checkout: REF_ROOT, else a directory named `reference` beside this repository
 REF_ROOT = Path(os.environ.get("REF_ROOT", Path(__file__).resolve().parents[3] / "reference"))
@@ -279,6 +280,36 @@ def prefill_a16_fixture(weights: Path):
     np.savez_compressed(OUT / "prefill_a16.npz", **out)
 
 
+def codec_fixture():
+    """The reference's AudioDecoder (decoder.cpp, compiled into oracle/_ref/libmossref.so) on
+    the seeded synthetic decoder file: decode() of 12 frames, and two streaming runs through
+    decode_chunk from reset_stream -- chunks of 4, 8, 8, 3 frames, and 160 frames in the
+    engine's chunking (4, then 8s; engine.cpp:482-486), long enough that every stage's ring
+    (500 / 800 / 1200 / 1600 rows = 125 / 100 / 75 / 50 frames) wraps."""
+    from oracle_py import RefCodec
+    from moss_b200 import codecfile
+    path = Path(tempfile.gettempdir()) / "moss_golden_dec1.moss"
+    digest = codecfile.synth_decoder(path, CODEC_DECODER_SEED)
+    ref = RefCodec(path, threads=8)
+    out = {"decoder_sha256": np.array(digest), "decoder_bytes": np.int64(path.stat().st_size)}
+    for name, seed, chunks in CODEC_CASES:
+        codes = codec_codes(sum(chunks), seed)
+        if name == "whole":
+            pcm = ref.decode(codes)
+        else:
+            ref.reset()
+            parts, f0 = [], 0
+            for k in chunks:
+                parts.append(ref.decode_chunk(codes[:, f0:f0 + k]))
+                f0 += k
+            pcm = np.concatenate(parts)
+        assert pcm.size == sum(chunks) * 7680
+        out[f"{name}_codes_sha"] = np.array(sha(codes))
+        out[f"{name}_sub"] = pcm[::CODEC_STRIDE].copy()
+        out[f"{name}_energy"] = codec_frame_energy(pcm)
+    np.savez_compressed(OUT / "codec.npz", **out)
+
+
 def main():
     weights = Path(tempfile.gettempdir()) / "moss_golden_w0.moss"
     load_pkg()
@@ -302,6 +333,9 @@ def main():
     if len(sys.argv) > 1 and sys.argv[1] == "--prefill-continue":
         prefill_continue_fixture(weights)
         return
+    if len(sys.argv) > 1 and sys.argv[1] == "--codec":
+        codec_fixture()
+        return
     ex = reference_export_module()
     # the synthetic-weight writer must produce the reference writer's bytes
     rng = np.random.default_rng(0)
@@ -316,6 +350,7 @@ def main():
     end_decision_fixture(weights)
     prefix_file_fixture(weights)
     prefill_continue_fixture(weights)
+    codec_fixture()
     subprocess.run([sys.executable, __file__, "--a16-prefill"], check=True)
     for p in sorted(OUT.glob("*.npz")):
         print(p.name, p.stat().st_size)

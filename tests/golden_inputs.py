@@ -81,3 +81,20 @@ def sampler_sweep_case(case: int):
     top_p = (0.0, 0.3, 0.95, 1.0)[int(rng.integers(0, 4))]
     penalty = (1.0, 1.2, 0.9)[int(rng.integers(0, 3))]
     return logits, prev, greedy, temperature, top_k, top_p, penalty, 5000 + case
+
+
+# The audio codec decoder: the seeded synthetic decoder file (codecfile.synth_decoder) and
+# three streaming cases -- (name, codes seed, chunk sizes); "whole" is one decode() call.
+CODEC_DECODER_SEED = 1
+CODEC_CASES = (("whole", 21, (12,)), ("chunks", 22, (4, 8, 8, 3)), ("long", 23, (4,) + (8,) * 19 + (4,)))
+CODEC_STRIDE = 53  # the fixtures keep samples [::53] plus per-frame sums of squares
+
+
+def codec_codes(frames: int, seed: int) -> np.ndarray:
+    """[16][frames] int32 codes, uniform in [0, 1024)."""
+    return np.random.default_rng(seed).integers(0, CODEBOOK, (NVQ, frames)).astype(np.int32)
+
+
+def codec_frame_energy(pcm: np.ndarray) -> np.ndarray:
+    """Per-frame sum of squares (float64) of samples [frames * 7680]."""
+    return (pcm.astype(np.float64).reshape(-1, 7680) ** 2).sum(axis=1)
