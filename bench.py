@@ -232,6 +232,128 @@ def cpu_throughput(weights: str, lmin: int, lmax: int, budget_s: float, procs: i
             "host": cpus}
 
 
+def _cpu_codec_worker(job):
+    """One reference audio-decoder process (AudioDecoder::decode_chunk, decoder.cpp:211-225)
+    on one stream: a 4-frame first chunk, then 8-frame chunks (engine.cpp:482-486) for about
+    budget_s seconds."""
+    path, budget_s, seed, threads = job
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle_py
+    if oracle_py.REF_SO.exists():
+        dec, kind = oracle_py.RefCodec(path, threads=threads), "reference"
+    else:
+        import codec_oracle
+        dec, kind = codec_oracle.CodecOracle(path), "port"
+    rng = np.random.default_rng(seed)
+    dec.decode_chunk(rng.integers(0, 1024, (16, 4)).astype(np.int32))
+    frames, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < budget_s:
+        dec.decode_chunk(rng.integers(0, 1024, (16, 8)).astype(np.int32))
+        frames += 8
+    return frames, time.perf_counter() - t0, kind
+
+
+def cpu_codec_throughput(path: str, budget_s: float, procs: int | None = None) -> dict:
+    """The reference codec decoder's throughput mode: P single-thread processes on P physical
+    cores, one stream each."""
+    import multiprocessing as mp
+    cpus = host_cpus()
+    P = procs or max(1, min(cpus["physical_cores"], 32))
+    with mp.get_context("spawn").Pool(P) as pool:
+        res = pool.map(_cpu_codec_worker, [(path, budget_s, 31 + i, 1) for i in range(P)])
+    fps = sum(f / dt for f, dt, _ in res)
+    kind = res[0][2]
+    return {"value": round(fps, 3), "unit": "codec frames/s", "cores": P, "kind": kind,
+            "sample": (f"{P} single-thread {'reference' if kind == 'reference' else 'numpy-port'} AudioDecoder "
+                       f"processes on {P} physical cores ({cpus['cpu_model']}), one stream each: a 4-frame chunk, "
+                       f"then 8-frame decode_chunk calls for ~{budget_s:.0f} s (rings filling from empty, so "
+                       f"attention is shorter than in the GPU leg's full-ring steady state)")}
+
+
+def run_codec(pkg, device, torch, n: int, K: int, peaks_: dict, chunk: int = 8, fill_chunks: int = 16,
+              cpu_budget_s: float = 0.0) -> dict:
+    """The audio codec decoder (mossgpu_codec_*) on n codec streams, one chunk of `chunk`
+    frames per stream per call (the reference engine's chunk, engine.cpp:482-486).  The rings
+    are filled first (16 chunks = 128 frames > the longest ring, 500 rows = 125 frames), so the
+    timed calls run at the steady state of long-form streaming.  value: K calls with device
+    codes and output, CUDA events; e2e: K calls of mossgpu_codec_decode_batch with host codes
+    and host samples (the samples' D2H inside the timed region), wall clock."""
+    from moss_b200 import codecfile
+    path = codecfile.ensure_synth_decoder(Path(tempfile.gettempdir()) / "moss_b200_dec1.moss", 1)
+    codec = pkg.Codec(path, device, max_streams=n, max_batch_frames=n * chunk)
+    stream = torch.cuda.current_stream()
+    codec.set_cuda_stream(stream.cuda_stream)
+    sids = [codec.open() for _ in range(n)]
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5)
+    codes = torch.randint(0, 1024, (fill_chunks + 2 * K + 2, n, 16, chunk), dtype=torch.int32, device="cuda",
+                          generator=g)
+    out = torch.empty((n, chunk * codec.samples_per_frame), dtype=torch.float32, device="cuda")
+    for i in range(fill_chunks):
+        codec.decode_batch_device(sids, codes[i].data_ptr(), chunk, out.data_ptr())
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(K):
+        codec.decode_batch_device(sids, codes[fill_chunks + i].data_ptr(), chunk, out.data_ptr())
+    e1.record(stream)
+    e1.synchronize()
+    dev_ms = e0.elapsed_time(e1) / K
+    # per-class device time of one more call (events between launches; one gap per launch removed)
+    codec.profile(True)
+    codec.decode_batch_device(sids, codes[fill_chunks + K].data_ptr(), chunk, out.data_ptr())
+    prof = codec.profile_read()
+    codec.profile(False)
+    nl_all = sum(v[1] for v in prof.values())
+    gap = max(0.0, (sum(v[0] for v in prof.values()) - dev_ms) / max(nl_all, 1))
+    # e2e through the host entry point
+    hcodes = codes[fill_chunks + K + 1:fill_chunks + 2 * K + 1].cpu().numpy()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(K):
+        pcm = codec.decode_batch(sids, hcodes[i])
+    e2e_s = (time.perf_counter() - t0) / K
+    assert pcm.shape == (n, chunk * codec.samples_per_frame) and np.isfinite(pcm[:, :64]).all()
+    launches = codec.launches_per_call()
+    codec.close()
+    frames = n * chunk
+    # algorithmic FLOPs per call: the GEMMs, and the attention at full rings
+    rows_f, gemm_macs, attn_macs = 1, 512 * 1024, 0
+    cin = 1024
+    for s, (p, L, ctx, cout) in enumerate(((4, 4, 500, 512), (2, 2, 800, 512), (2, 2, 1200, 512), (2, 4, 1600, 240))):
+        rows_f *= p
+        gemm_macs += rows_f * (256 * cin // p + L * (768 * 256 + 256 * 256 + 2 * 1024 * 256) + cout * 256)
+        attn_macs += rows_f * L * 4 * ctx * 64 * 2
+        cin = cout
+    flops = {"k_gemm_f16w": 2.0 * gemm_macs * frames, "k_window_attn": 2.0 * attn_macs * frames}
+    classes = {}
+    for k, (ms, nl) in prof.items():
+        if nl:
+            t = max(ms - gap * nl, 0.05 * ms)
+            classes[k] = {"ms_per_call": round(t, 4), "launches": nl, "share": round(t / dev_ms, 4)}
+            if k in flops:
+                classes[k]["achieved_tflops"] = round(flops[k] / (t / 1e3) / 1e12, 2)
+    top = max((k for k in classes if k in flops), key=lambda k: classes[k]["ms_per_call"])
+    fp32_peak = 148 * 128 * 2 * 1.965e9 / 1e12  # nominal FFMA peak at the 1965 MHz max SM clock
+    r = {"api": "mossgpu_codec_decode_batch_device (value) / mossgpu_codec_decode_batch (e2e)",
+         "streams": n, "chunk_frames": chunk, "ms_per_call": round(dev_ms, 3),
+         "value": round(frames / (dev_ms / 1e3), 1), "unit": "codec frames/s",
+         "e2e": {"value": round(frames / e2e_s, 1), "unit": "codec frames/s", "ms_per_call": round(1e3 * e2e_s, 3),
+                 "h2d_bytes_per_step": int(n * 16 * chunk * 4),
+                 "d2h_bytes_per_step": int(n * chunk * codec.samples_per_frame * 4)},
+         "audio_seconds_per_s": round(frames * 0.08 / (dev_ms / 1e3), 1),
+         "gpu_launches_per_call": launches,
+         "gflop_per_call": round(sum(flops.values()) / 1e9, 1),
+         "roofline": {"kernel": top, "bound": "fp32", "achieved": classes[top]["achieved_tflops"],
+                      "peak": round(fp32_peak, 1), "unit": "TFLOP/s",
+                      "frac": round(classes[top]["achieved_tflops"] / fp32_peak, 4),
+                      "peak_source": "nominal FP32 FFMA rate, 148 SMs x 128 lanes x 2 x 1965 MHz (not measured)"},
+         "kernels": classes, "profile_gap_us": round(1000 * gap, 2)}
+    if cpu_budget_s > 0:
+        r["cpu_baseline"] = cpu_codec_throughput(path, cpu_budget_s)
+    return r
+
+
 def cpu_single_stream(weights: str, L: int, budget_s: float) -> dict:
     """One stream, one process, all logical CPUs as the reference's --threads (single-stream mode)."""
     import multiprocessing as mp
@@ -406,6 +528,9 @@ def run_ours(args, rank, world, local_rank, dist):
         if args.workload == "configs4" else None
     pf = run_prefill(pkg, weights, local_rank, torch, n_prompts=16, rows=256)
     pf["frac_of_bf16_peak"] = round(pf["tflops"] / pk["bf16_tflops"], 4)
+    # ---- the audio codec decoder on this rank's streams (8-frame chunks, full rings)
+    codec = run_codec(pkg, local_rank, torch, B, min(K, 8), pk,
+                      cpu_budget_s=10.0 if (rank == 0 and world == 1 and not args.no_cpu_baseline) else 0.0)
 
     # ---- rooflines
     R = B
@@ -501,6 +626,7 @@ def run_ours(args, rank, world, local_rank, dist):
             "stats": stats,
             "configs1_frame": c1,
             "prefill": pf,
+            "codec": codec,
             "batch1_global_step": {"us": round(b1_us, 2), "kv_len": 128, "algorithmic_bytes": b1_bytes,
                                    "achieved_gbs": round(b1_bytes / (b1_us / 1e6) / 1e9, 1),
                                    "frac_of_hbm": round(b1_bytes / (b1_us / 1e6) / 1e9 / pk["hbm_gbs"], 4)},
@@ -672,6 +798,9 @@ def main():
     ap.add_argument("--sweep-frames", type=int, default=400)
     ap.add_argument("--profile-prefill", type=int, default=0,
                     help="prefill this many 256-row prompts after one warm-up prompt and exit (ncu captures)")
+    ap.add_argument("--profile-codec", type=int, default=0,
+                    help="codec: fill the rings of this many streams (16 chunks of 8 frames), decode one more "
+                         "chunk and exit (the command the codec ncu captures use)")
     ap.add_argument("--profile-frames", type=int, default=0,
                     help="run this many frames of the workload after one warm-up frame and exit "
                          "(the command the ncu captures under profiles/ use)")
@@ -686,6 +815,22 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference_arm(args, rank, world)
+        return
+    if args.profile_codec:
+        import torch
+        pkg = load_package()
+        pkg.build()
+        from moss_b200 import codecfile
+        path = codecfile.ensure_synth_decoder(Path(tempfile.gettempdir()) / "moss_b200_dec1.moss", 1)
+        n = args.profile_codec
+        codec = pkg.Codec(path, 0, max_streams=n, max_batch_frames=n * 8)
+        sids = [codec.open() for _ in range(n)]
+        codes = torch.randint(0, 1024, (n, 16, 8), dtype=torch.int32, device="cuda")
+        out = torch.empty((n, 8 * codec.samples_per_frame), dtype=torch.float32, device="cuda")
+        for _ in range(17):
+            codec.decode_batch_device(sids, codes.data_ptr(), 8, out.data_ptr())
+        torch.cuda.synchronize()
+        codec.close()
         return
     dist = None
     if world > 1:

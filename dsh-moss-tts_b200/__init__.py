@@ -50,6 +50,7 @@ EXPORTS = [
     "mossgpu_codec_launches_per_call", "mossgpu_codec_device_bytes", "mossgpu_codec_set_cuda_stream",
     "mossgpu_codec_open", "mossgpu_codec_close", "mossgpu_codec_reset", "mossgpu_codec_decode_chunk",
     "mossgpu_codec_decode_batch", "mossgpu_codec_decode_batch_device", "mossgpu_codec_decode",
+    "mossgpu_codec_profile", "mossgpu_codec_profile_read", "mossgpu_codec_kernel_name",
 ]
 
 
@@ -160,6 +161,10 @@ def lib() -> C.CDLL:
         L.mossgpu_codec_decode_batch.argtypes = [C.c_void_p, _i32, C.c_int, _i32, C.c_int, _f32, C.c_size_t]
         L.mossgpu_codec_decode_batch_device.argtypes = [C.c_void_p, _i32, C.c_int, C.c_void_p, C.c_int, C.c_void_p]
         L.mossgpu_codec_decode.argtypes = [C.c_void_p, _i32, C.c_int, _f32, C.c_size_t, C.POINTER(C.c_int)]
+        L.mossgpu_codec_profile.argtypes = [C.c_void_p, C.c_int]
+        L.mossgpu_codec_profile_read.argtypes = [C.c_void_p, _f32, _i32, C.c_int, C.POINTER(C.c_int)]
+        L.mossgpu_codec_kernel_name.restype = C.c_char_p
+        L.mossgpu_codec_kernel_name.argtypes = [C.c_int]
         _LIB = L
         return L
 
@@ -489,6 +494,17 @@ class Codec:
 
     def launches_per_call(self) -> int:
         return self.lib.mossgpu_codec_launches_per_call(self.h)
+
+    def profile(self, enable: bool):
+        self._check(self.lib.mossgpu_codec_profile(self.h, int(enable)))
+
+    def profile_read(self) -> dict:
+        """{kernel class: (device ms, launches)} since the last read (synchronises)."""
+        ms = np.zeros(16, np.float32)
+        n = np.zeros(16, np.int32)
+        k = C.c_int()
+        self._check(self.lib.mossgpu_codec_profile_read(self.h, ms, n, 16, C.byref(k)))
+        return {self.lib.mossgpu_codec_kernel_name(i).decode(): (float(ms[i]), int(n[i])) for i in range(k.value)}
 
     def device_bytes(self) -> int:
         return self.lib.mossgpu_codec_device_bytes(self.h)

@@ -421,6 +421,11 @@ __global__ void k_ring_append(const float *__restrict__ qkv, int t, int n_stream
 
 // ------------------------------------------------------------------------------- host
 
+// kernel classes of the optional per-launch profile (mossgpu_codec_profile)
+enum Kind { KD_FRONT = 0, KD_GEMM, KD_PATCH, KD_LAYERNORM, KD_ROPE, KD_ATTN, KD_RING, KD_COUNT };
+const char *const kKindNames[KD_COUNT] = {"k_front", "k_gemm_f16w", "k_patch", "k_layernorm256",
+                                          "k_rope", "k_window_attn", "k_ring_append"};
+
 struct Mat {
     __half *w = nullptr;
     int rows = 0, cols = 0;
@@ -482,7 +487,30 @@ public:
     ~Codec() {
         cudaSetDevice(device_);
         cudaDeviceSynchronize();
+        for (cudaEvent_t e : events_) cudaEventDestroy(e);
         for (void *p : owned_) cudaFree(p);
+    }
+
+    // Per-launch profile: while enabled, every launch is bracketed by two events on the
+    // codec's stream; profile_read synchronises, adds up the time of each kernel class and
+    // starts over.  The events add a gap to every launch; callers subtract it.
+    void set_profile(bool on) {
+        profile_ = on;
+        marks_.clear();
+    }
+    void profile_read(float *ms, int *launches) {
+        CK(cudaStreamSynchronize(stream_));
+        for (int k = 0; k < KD_COUNT; ++k) {
+            ms[k] = 0.f;
+            launches[k] = 0;
+        }
+        for (size_t i = 0; i < marks_.size(); ++i) {
+            float t = 0.f;
+            CK(cudaEventElapsedTime(&t, events_[2 * i], events_[2 * i + 1]));
+            ms[marks_[i]] += t;
+            launches[marks_[i]] += 1;
+        }
+        marks_.clear();
     }
 
     int device() const { return device_; }
@@ -613,6 +641,22 @@ public:
     }
 
 private:
+    // bracket the next launch with a pair of events when profiling
+    void mark_begin(int kind) {
+        if (!profile_) return;
+        const size_t i = marks_.size();
+        while (events_.size() < 2 * (i + 1)) {
+            cudaEvent_t e;
+            CK(cudaEventCreate(&e));
+            events_.push_back(e);
+        }
+        marks_.push_back(kind);
+        CK(cudaEventRecord(events_[2 * i], stream_));
+    }
+    void mark_end() {
+        if (profile_) CK(cudaEventRecord(events_[2 * (marks_.size() - 1) + 1], stream_));
+    }
+
     void check_sid(int sid) const {
         if (sid < 0 || sid >= max_streams_ || !slots_[size_t(sid)].open)
             throw std::runtime_error("codec stream " + std::to_string(sid) + " is not open");
@@ -630,6 +674,7 @@ private:
 
     void gemm(const Mat &m, const float *x, int T, float *y, int epi, const float *vec) {
         const dim3 grid((m.rows + kBN - 1) / kBN, (T + kBM - 1) / kBM);
+        mark_begin(KD_GEMM);
         if (epi == EPI_PLAIN)
             k_gemm_f16w<EPI_PLAIN><<<grid, kGemmThreads, 0, stream_>>>(m.w, x, T, m.rows, m.cols, vec, y);
         else if (epi == EPI_GELU)
@@ -637,12 +682,15 @@ private:
         else
             k_gemm_f16w<EPI_SCALED_ADD><<<grid, kGemmThreads, 0, stream_>>>(m.w, x, T, m.rows, m.cols, vec, y);
         CK(cudaGetLastError());
+        mark_end();
     }
 
     void run(const Meta &md, int n, const int *codes, int frames, float *pcm) {
         int rows = n * frames;  // all streams' rows of the current stage
+        mark_begin(KD_FRONT);
         k_front<<<rows, 256, 0, stream_>>>(codes, frames, d_cb_, d_ow_, d_ob_, ln_);
         CK(cudaGetLastError());
+        mark_end();
         gemm(q_out_, ln_, rows, xa_, EPI_PLAIN, q_out_b_);
         int c = c0_, t = frames, li = 0;
         for (int s = 0; s < kStages; ++s) {
@@ -650,8 +698,10 @@ private:
             const int p = kPatch[s];
             const size_t nel = size_t(rows) * size_t(c);
             const int pblocks = int(std::min<size_t>((nel + 255) / 256, 148 * 16));
+            mark_begin(KD_PATCH);
             k_patch<<<pblocks, 256, 0, stream_>>>(xa_, size_t(rows), c, p, xb_);
             CK(cudaGetLastError());
+            mark_end();
             rows *= p;
             t *= p;
             c /= p;
@@ -666,17 +716,27 @@ private:
     // decoder.cpp:116-196 run_layer_stream, on y_ [rows][256] in place
     void layer(Layer &l, const Meta &md, int n, int rows, int t, int window, int li, const int *offset) {
         const int lnb = (rows + 7) / 8;
+        mark_begin(KD_LAYERNORM);
         k_layernorm256<<<lnb, 256, 0, stream_>>>(y_, rows, l.n1w, l.n1b, ln_);
+        mark_end();
         gemm(l.attn, ln_, rows, qkv_, EPI_PLAIN, nullptr);
+        mark_begin(KD_ROPE);
         k_rope<<<rows, 256, 0, stream_>>>(qkv_, rows, t, offset);
+        mark_end();
         const dim3 ag((t + kAQ - 1) / kAQ, kHeads, n);
+        mark_begin(KD_ATTN);
         k_window_attn<<<ag, 256, kAttnSmem, stream_>>>(qkv_, t, l.ring_k, l.ring_v, window, li, md, n, att_);
+        mark_end();
         const size_t items = size_t(n) * size_t(std::min(t, window)) * (kDModel / 4);
+        mark_begin(KD_RING);
         k_ring_append<<<int(std::min<size_t>((items + 255) / 256, 148 * 8)), 256, 0, stream_>>>(
             qkv_, t, n, l.ring_k, l.ring_v, window, li, md);
         CK(cudaGetLastError());
+        mark_end();
         gemm(l.proj, att_, rows, y_, EPI_SCALED_ADD, l.ls1);
+        mark_begin(KD_LAYERNORM);
         k_layernorm256<<<lnb, 256, 0, stream_>>>(y_, rows, l.n2w, l.n2b, ln_);
+        mark_end();
         gemm(l.f1, ln_, rows, ffn_, EPI_GELU, nullptr);
         gemm(l.f2, ffn_, rows, y_, EPI_SCALED_ADD, l.ls2);
     }
@@ -806,6 +866,9 @@ private:
     float *xa_ = nullptr, *xb_ = nullptr, *y_ = nullptr, *ln_ = nullptr, *qkv_ = nullptr, *att_ = nullptr,
           *ffn_ = nullptr, *pcm_ = nullptr;
     int *codes_ = nullptr, *meta_d_ = nullptr;
+    bool profile_ = false;
+    std::vector<int> marks_;            // kernel class of each bracketed launch
+    std::vector<cudaEvent_t> events_;   // two per bracketed launch, reused
 };
 
 }  // namespace codec
@@ -865,6 +928,25 @@ int mossgpu_codec_samples_per_frame(mossgpu_codec *h) { return h && h->c ? h->c-
 int mossgpu_codec_launches_per_call(mossgpu_codec *h) { return h && h->c ? h->c->launches_per_call() : 0; }
 
 size_t mossgpu_codec_device_bytes(mossgpu_codec *h) { return h && h->c ? h->c->device_bytes() : 0; }
+
+int mossgpu_codec_profile(mossgpu_codec *h, int enable) {
+    return codec_guarded(h, [&](mossgpu::codec::Codec &c) { c.set_profile(enable != 0); });
+}
+
+int mossgpu_codec_profile_read(mossgpu_codec *h, float *total_ms, int *launches, int max_kinds, int *n_kinds) {
+    return codec_guarded(h, [&](mossgpu::codec::Codec &c) {
+        using namespace mossgpu::codec;
+        if (!total_ms || !launches || !n_kinds || max_kinds < KD_COUNT)
+            throw std::runtime_error("profile_read needs arrays of at least " + std::to_string(KD_COUNT) + " kinds");
+        c.profile_read(total_ms, launches);
+        *n_kinds = KD_COUNT;
+    });
+}
+
+const char *mossgpu_codec_kernel_name(int kind) {
+    using namespace mossgpu::codec;
+    return kind >= 0 && kind < KD_COUNT ? kKindNames[kind] : "";
+}
 
 int mossgpu_codec_set_cuda_stream(mossgpu_codec *h, void *cuda_stream) {
     return codec_guarded(h, [&](mossgpu::codec::Codec &c) { c.set_stream(static_cast<cudaStream_t>(cuda_stream)); });

@@ -274,6 +274,13 @@ int mossgpu_codec_launches_per_call(mossgpu_codec *c);
 size_t mossgpu_codec_device_bytes(mossgpu_codec *c);
 /* The CUDA stream (cudaStream_t; NULL = legacy default) every later call enqueues on. */
 int mossgpu_codec_set_cuda_stream(mossgpu_codec *c, void *cuda_stream);
+/* Per-kernel-class device time: while enabled, each launch is bracketed by CUDA events (which
+ * add a gap per launch); profile_read synchronises, writes the milliseconds and launch count of
+ * each class since the last read (max_kinds >= 7) and the class count to *n_kinds.  Class
+ * names: mossgpu_codec_kernel_name. */
+int mossgpu_codec_profile(mossgpu_codec *c, int enable);
+int mossgpu_codec_profile_read(mossgpu_codec *c, float *total_ms, int *launches, int max_kinds, int *n_kinds);
+const char *mossgpu_codec_kernel_name(int kind);
 /* A codec stream in the clean state; close frees its slot. */
 int mossgpu_codec_open(mossgpu_codec *c, int *stream_id);
 int mossgpu_codec_close(mossgpu_codec *c, int stream_id);
