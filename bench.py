@@ -325,7 +325,7 @@ def run_codec(pkg, device, torch, n: int, K: int, peaks_: dict, chunk: int = 8, 
         gemm_macs += rows_f * (256 * cin // p + L * (768 * 256 + 256 * 256 + 2 * 1024 * 256) + cout * 256)
         attn_macs += rows_f * L * 4 * ctx * 64 * 2
         cin = cout
-    flops = {"k_gemm_f16w": 2.0 * gemm_macs * frames, "k_window_attn": 2.0 * attn_macs * frames}
+    flops = {"k_gemm_mma": 2.0 * gemm_macs * frames, "k_window_attn": 2.0 * attn_macs * frames}
     classes = {}
     for k, (ms, nl) in prof.items():
         if nl:
@@ -334,7 +334,6 @@ def run_codec(pkg, device, torch, n: int, K: int, peaks_: dict, chunk: int = 8, 
             if k in flops:
                 classes[k]["achieved_tflops"] = round(flops[k] / (t / 1e3) / 1e12, 2)
     top = max((k for k in classes if k in flops), key=lambda k: classes[k]["ms_per_call"])
-    fp32_peak = 148 * 128 * 2 * 1.965e9 / 1e12  # nominal FFMA peak at the 1965 MHz max SM clock
     r = {"api": "mossgpu_codec_decode_batch_device (value) / mossgpu_codec_decode_batch (e2e)",
          "streams": n, "chunk_frames": chunk, "ms_per_call": round(dev_ms, 3),
          "value": round(frames / (dev_ms / 1e3), 1), "unit": "codec frames/s",
@@ -344,10 +343,13 @@ def run_codec(pkg, device, torch, n: int, K: int, peaks_: dict, chunk: int = 8, 
          "audio_seconds_per_s": round(frames * 0.08 / (dev_ms / 1e3), 1),
          "gpu_launches_per_call": launches,
          "gflop_per_call": round(sum(flops.values()) / 1e9, 1),
-         "roofline": {"kernel": top, "bound": "fp32", "achieved": classes[top]["achieved_tflops"],
-                      "peak": round(fp32_peak, 1), "unit": "TFLOP/s",
-                      "frac": round(classes[top]["achieved_tflops"] / fp32_peak, 4),
-                      "peak_source": "nominal FP32 FFMA rate, 148 SMs x 128 lanes x 2 x 1965 MHz (not measured)"},
+         "roofline": {"kernel": top, "bound": "tensor", "achieved": classes[top]["achieved_tflops"],
+                      "peak": peaks_["bf16_tflops"], "unit": "TFLOP/s",
+                      "frac": round(classes[top]["achieved_tflops"] / peaks_["bf16_tflops"], 4),
+                      "tensor_products_per_flop": 2 if top == "k_gemm_mma" else 3,
+                      "note": ("algorithmic FLOPs; each product runs as 2 (GEMM: W.x_hi + W.x_lo) or 3 "
+                               "(attention: hi/lo of both operands) fp16 tensor products"),
+                      "peak_source": peaks_["source"]},
          "kernels": classes, "profile_gap_us": round(1000 * gap, 2)}
     if cpu_budget_s > 0:
         r["cpu_baseline"] = cpu_codec_throughput(path, cpu_budget_s)

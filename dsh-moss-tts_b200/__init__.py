@@ -50,7 +50,7 @@ EXPORTS = [
     "mossgpu_codec_launches_per_call", "mossgpu_codec_device_bytes", "mossgpu_codec_set_cuda_stream",
     "mossgpu_codec_open", "mossgpu_codec_close", "mossgpu_codec_reset", "mossgpu_codec_decode_chunk",
     "mossgpu_codec_decode_batch", "mossgpu_codec_decode_batch_device", "mossgpu_codec_decode",
-    "mossgpu_codec_profile", "mossgpu_codec_profile_read", "mossgpu_codec_kernel_name",
+    "mossgpu_codec_profile", "mossgpu_codec_profile_read", "mossgpu_codec_kernel_name", "mossgpu_codec_status",
 ]
 
 
@@ -165,6 +165,7 @@ def lib() -> C.CDLL:
         L.mossgpu_codec_profile_read.argtypes = [C.c_void_p, _f32, _i32, C.c_int, C.POINTER(C.c_int)]
         L.mossgpu_codec_kernel_name.restype = C.c_char_p
         L.mossgpu_codec_kernel_name.argtypes = [C.c_int]
+        L.mossgpu_codec_status.argtypes = [C.c_void_p, C.POINTER(C.c_int)]
         _LIB = L
         return L
 
@@ -543,6 +544,12 @@ class Codec:
         sids = np.ascontiguousarray(sids, np.int32).reshape(-1)
         self._check(self.lib.mossgpu_codec_decode_batch_device(self.h, sids, sids.size, C.c_void_p(codes_ptr),
                                                                frames, C.c_void_p(out_ptr)))
+
+    def status(self) -> int:
+        """1 when an activation since the last read left the fp16 range (synchronises)."""
+        code = C.c_int(0)
+        self._check(self.lib.mossgpu_codec_status(self.h, C.byref(code)))
+        return code.value
 
     def decode(self, codes) -> np.ndarray:
         """A whole utterance, codes [16][frames], from a clean state."""

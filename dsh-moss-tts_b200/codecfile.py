@@ -53,11 +53,13 @@ def decoder_specs() -> list[tuple[str, str, int, int]]:
     return s
 
 
-def synth_decoder(path: str | os.PathLike, seed: int = 1) -> str:
+def synth_decoder(path: str | os.PathLike, seed: int = 1, add: dict[str, float] | None = None) -> str:
     """Write the seeded synthetic decoder; returns the file's sha256.  Matrices N(0, 1/cols)
     (so activations keep their scale through the stages), codebooks N(0, 1), LayerNorm weights
-    1 + N(0, 0.05), biases N(0, 0.02), layer scales 0.1 + N(0, 0.02)."""
+    1 + N(0, 0.05), biases N(0, 0.02), layer scales 0.1 + N(0, 0.02).  `add` adds a constant to
+    the named f32 tensors (for tests of out-of-range activations)."""
     rng = np.random.default_rng(seed)
+    add = add or {}
     entries = []
     for name, kind, rows, cols in decoder_specs():
         if kind == "matrix":
@@ -71,7 +73,7 @@ def synth_decoder(path: str | os.PathLike, seed: int = 1) -> str:
             entries.append((name, DT_F32, (rows, cols), w.tobytes()))
         else:
             base, sd = {"lnw": (1.0, 0.05), "bias": (0.0, 0.02), "scale": (0.1, 0.02)}[kind]
-            v = (base + sd * rng.standard_normal(cols, dtype=np.float32)).astype(np.float32)
+            v = (base + sd * rng.standard_normal(cols, dtype=np.float32) + add.get(name, 0.0)).astype(np.float32)
             entries.append((name, DT_F32, (1, cols), v.tobytes()))
     write_moss(path, entries)
     return hashlib.sha256(Path(path).read_bytes()).hexdigest()

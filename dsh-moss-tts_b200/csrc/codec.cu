@@ -16,10 +16,18 @@
 // up to max_streams utterances ("codec streams"), each with the reference's streaming state
 // (the RoPE offset of every stage, the last `context` K and V rows of every layer), and one
 // call decodes a chunk of the same length for any set of them: the rows of all streams run
-// through each GEMM together, attention is tiled per (stream, head, 32 rows).  Activations are
-// fp32 [rows][channels] with stream b's rows contiguous; matrices stay fp16 as in the file and
-// are widened in shared memory, products accumulated in fp32 like the reference's gemm_par on
-// f16 matrices.  The K/V rings are fp32 [slot][context][256], slot = stream id.
+// through each GEMM together, attention is tiled per (stream, head, 64 rows).
+//
+// Arithmetic.  The reference computes in fp32 with fp16 matrices (gemm_par on f16 matrices,
+// gemv.cpp:331-359).  Here the products run on the tensor cores (mma.sync m16n8k16, fp16
+// operands, fp32 accumulation) with every fp32 operand split into fp16 hi + lo (hi = fp16(x),
+// lo = fp16(x - hi), ~22 significant bits): a GEMM is W.x_hi + W.x_lo (the fp16 weights are
+// exact), a score q.k_hi + q.k_lo... as q_hi.k_hi + q_hi.k_lo + q_lo.k_hi, and p.v likewise.
+// Activations stay fp32 in memory [rows][channels]; the qkv GEMM's epilogue applies RoPE and
+// writes q / 8 (exact scaling) and k, v as fp16 hi/lo planes, which is also the format of the
+// K/V rings ([slot][context][kh, kl, vh, vl][256] fp16, slot = stream id).  A value that fp16
+// cannot hold (|x| >= 65504, or NaN) sets the codec's range flag: the host entry points then
+// fail, and the device entry point reports it through mossgpu_codec_status.
 #include "../../include/mossgpu.h"
 
 #include <cuda_fp16.h>
@@ -63,108 +71,232 @@ struct Meta {
     const int *sid, *offset, *rstart, *rcount;
 };
 
-// y[t][r] = sum_k W[r][k] x[t][k] (W fp16 [R][K], x fp32 [T][K]), then the epilogue:
-// EPI_PLAIN y = acc (+ vec[r] when vec is given), EPI_GELU y = gelu(acc),
-// EPI_SCALED_ADD y = y + vec[r] * acc (the layer-scale residual, decoder.cpp:173-177).
-enum { EPI_PLAIN = 0, EPI_GELU = 1, EPI_SCALED_ADD = 2 };
-constexpr int kBM = 128, kBN = 64, kBK = 16, kGemmThreads = 256;
+// ---- tensor-core building blocks: mma.sync m16n8k16 (fp16 in, fp32 accumulate), ldmatrix,
+// and cp.async (16-byte asynchronous copies from this GPU's own memory; no multicast)
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void *p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_addr(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void *p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_addr(p)));
+}
+// src_bytes = 0 reads nothing and fills the 16 destination bytes with zeros
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, int src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// (a, b) -> fp16 pairs hi and lo, hi + lo == (a, b) to ~22 significant bits
+__device__ __forceinline__ void split_pair(float a, float b, uint32_t &hi, uint32_t &lo) {
+    const __half2 h = __floats2half2_rn(a, b);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(a - hf.x, b - hf.y);
+    hi = *reinterpret_cast<const uint32_t *>(&h);
+    lo = *reinterpret_cast<const uint32_t *>(&l);
+}
+// the same, flagging a value outside fp16's range (or a NaN) in *err
+__device__ __forceinline__ void split_pair_checked(float a, float b, uint32_t &hi, uint32_t &lo, int *err) {
+    if (!(fabsf(a) < 65504.f) || !(fabsf(b) < 65504.f)) *err = 1;
+    split_pair(a, b, hi, lo);
+}
 
 __device__ __forceinline__ float gelu_erf(float v) {  // audio_layer.cpp:46
     return 0.5f * v * (1.0f + erff(v * 0.7071067811865476f));
 }
 
+// y[t][r] = sum_k W[r][k] x[t][k] (W fp16 [R][K], x fp32 [T][K]), then the epilogue:
+//   EPI_PLAIN       y = acc (+ vec[r] when vec is given)
+//   EPI_GELU        y = gelu(acc)
+//   EPI_SCALED_ADD  y = y + vec[r] * acc (the layer-scale residual, decoder.cpp:173-177)
+//   EPI_QKV         r < 256: q, 256..511: k, 512..767: v of the row; RoPE on q and k at the
+//                   row's position (audio_layer.cpp:31-44: frequency exp(-ln(1e4) 2i / 64) of
+//                   pair (2i, 2i+1) in each 64-wide head), then q / 8 -> q16 planes and k, v ->
+//                   kv16 planes as fp16 hi/lo (an accumulator pair is a RoPE pair)
+// Block tile 128 rows x 128 outputs, k step 32, two stages (x converted to hi/lo on its way to
+// shared memory, W by cp.async); 8 warps as 2 x 4, each 64 rows x 32 outputs.  Each k16 step
+// starts its two products from zero and is added to the fp32 accumulators with a rounded add:
+// the tensor cores' own accumulation does not round to nearest, and a long chain of it into
+// one accumulator biases the sum toward zero (~2^-24 per step).
+enum { EPI_PLAIN = 0, EPI_GELU = 1, EPI_SCALED_ADD = 2, EPI_QKV = 3 };
+constexpr int kTM = 128, kTN = 128, kTK = 32, kTS = 40;  // tile rows, tile outputs, k step, smem row (halves)
+constexpr int kStageHalves = 3 * kTM * kTS;              // x hi, x lo, W
+constexpr size_t kGemmSmem = 2 * kStageHalves * sizeof(__half);  // 61,440 bytes
+
+struct Epi {
+    const float *vec = nullptr;    // bias (PLAIN) or layer scale (SCALED_ADD)
+    float *y = nullptr;            // [T][R] (PLAIN, GELU, SCALED_ADD)
+    __half *q16 = nullptr;         // QKV: [T][2][256] hi, lo of q / 8
+    __half *kv16 = nullptr;        // QKV: [T][4][256] hi, lo of k; hi, lo of v
+    const int *offset = nullptr;   // QKV: RoPE position of each stream's first chunk row
+    int t_per_stream = 1;          // QKV: rows of one stream in this stage
+    int *err = nullptr;            // range flag
+};
+
 template <int EPI>
-__global__ void __launch_bounds__(kGemmThreads) k_gemm_f16w(const __half *__restrict__ W, const float *__restrict__ x,
-                                                            int T, int R, int K, const float *__restrict__ vec,
-                                                            float *__restrict__ y) {
-    __shared__ __align__(16) float xs[2][kBK][kBM + 4];
-    __shared__ __align__(16) float ws[2][kBK][kBN + 4];
-    const int tid = threadIdx.x;
-    const int t0 = blockIdx.y * kBM, r0 = blockIdx.x * kBN;
-    const int tx = tid & 15, ty = tid >> 4;  // outputs r0 + 4 tx .. +3, rows t0 + 8 ty .. +7
-    // loaders: x tile 128 x 16 floats = 512 float4 (2 per thread); W tile 64 x 16 halves = 128 x 8
-    const int xm = tid >> 2, xk = (tid & 3) * 4;  // rows xm and xm + 64, k xk..xk+3
-    const int wr = tid >> 1, wk = (tid & 1) * 8;  // threads 0..127: row wr, k wk..wk+7
-    float4 px[2];
-    uint4 pw = make_uint4(0, 0, 0, 0);
-    auto load = [&](int k0) {
+__global__ void __launch_bounds__(256) k_gemm_mma(const __half *__restrict__ W, const float *__restrict__ x, int T,
+                                                  int R, int K, Epi ep) {
+    extern __shared__ __align__(16) __half gsm[];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int wm = warp >> 2, wn = warp & 3, g = lane >> 2, tg = lane & 3;
+    const int t0 = blockIdx.y * kTM, r0 = blockIdx.x * kTN;
+    const int ar = tid >> 3, ak = (tid & 7) * 4;  // x loader: rows ar + 32 j, k ak..ak+3
+    const int br = tid >> 2, bk = (tid & 3) * 8;  // W loader: rows br + 64 j, k bk..bk+7
+    float4 pa[4];
+    auto load_a = [&](int k0) {
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-            const int t = t0 + xm + 64 * j, k = k0 + xk;
-            px[j] = (t < T && k < K) ? *reinterpret_cast<const float4 *>(x + (size_t)t * K + k)
+        for (int j = 0; j < 4; ++j) {
+            const int t = t0 + ar + 32 * j, k = k0 + ak;
+            pa[j] = (t < T && k < K) ? __ldg(reinterpret_cast<const float4 *>(x + (size_t)t * K + k))
                                      : make_float4(0.f, 0.f, 0.f, 0.f);
         }
-        if (tid < 128) {
-            const int r = r0 + wr, k = k0 + wk;
-            pw = (r < R && k < K) ? *reinterpret_cast<const uint4 *>(W + (size_t)r * K + k) : make_uint4(0, 0, 0, 0);
-        }
     };
-    auto store = [&](int buf) {
+    auto issue_b = [&](int st, int k0) {
+        __half *bt = gsm + st * kStageHalves + 2 * kTM * kTS;
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
-            xs[buf][xk + 0][xm + 64 * j] = px[j].x;
-            xs[buf][xk + 1][xm + 64 * j] = px[j].y;
-            xs[buf][xk + 2][xm + 64 * j] = px[j].z;
-            xs[buf][xk + 3][xm + 64 * j] = px[j].w;
+            const int r = r0 + br + 64 * j, k = k0 + bk;
+            const bool ok = r < R && k < K;
+            cp_async16(bt + (br + 64 * j) * kTS + bk, ok ? static_cast<const void *>(W + (size_t)r * K + k) : W,
+                       ok ? 16 : 0);
         }
-        if (tid < 128) {
-            const __half2 *h = reinterpret_cast<const __half2 *>(&pw);
+        cp_async_commit();
+    };
+    auto store_a = [&](int st) {
+        __half *ah = gsm + st * kStageHalves, *al = ah + kTM * kTS;
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const float2 f = __half22float2(h[j]);
-                ws[buf][wk + 2 * j][wr] = f.x;
-                ws[buf][wk + 2 * j + 1][wr] = f.y;
-            }
+        for (int j = 0; j < 4; ++j) {
+            uint32_t h0, l0, h1, l1;
+            split_pair_checked(pa[j].x, pa[j].y, h0, l0, ep.err);
+            split_pair_checked(pa[j].z, pa[j].w, h1, l1, ep.err);
+            const int off = (ar + 32 * j) * kTS + ak;
+            *reinterpret_cast<uint2 *>(ah + off) = make_uint2(h0, h1);
+            *reinterpret_cast<uint2 *>(al + off) = make_uint2(l0, l1);
         }
     };
-    float acc[8][4];
+    float acc[4][4][4];
 #pragma unroll
-    for (int a = 0; a < 8; ++a)
+    for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
-    load(0);
-    store(0);
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) acc[i][j][c] = 0.f;
+    load_a(0);
+    issue_b(0, 0);
+    store_a(0);
+    cp_async_wait<0>();
     __syncthreads();
-    int buf = 0;
-    for (int k0 = 0; k0 < K; k0 += kBK) {
-        const bool more = k0 + kBK < K;
-        if (more) load(k0 + kBK);
+    const int nk = (K + kTK - 1) / kTK;
+    for (int it = 0; it < nk; ++it) {
+        const int st = it & 1;
+        const bool more = it + 1 < nk;
+        if (more) {
+            load_a((it + 1) * kTK);
+            issue_b(st ^ 1, (it + 1) * kTK);
+        }
+        const __half *ah = gsm + st * kStageHalves, *al = ah + kTM * kTS, *bt = ah + 2 * kTM * kTS;
 #pragma unroll
-        for (int kk = 0; kk < kBK; ++kk) {
-            const float4 xa = *reinterpret_cast<const float4 *>(&xs[buf][kk][ty * 8]);
-            const float4 xb = *reinterpret_cast<const float4 *>(&xs[buf][kk][ty * 8 + 4]);
-            const float4 wv = *reinterpret_cast<const float4 *>(&ws[buf][kk][tx * 4]);
-            const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-            const float wf[4] = {wv.x, wv.y, wv.z, wv.w};
+        for (int kk = 0; kk < kTK; kk += 16) {
+            uint32_t bf[4][2];
 #pragma unroll
-            for (int a = 0; a < 8; ++a)
+            for (int nj = 0; nj < 4; nj += 2) {
+                uint32_t r[4];
+                ldsm_x4(r, bt + (wn * 32 + nj * 8 + (lane & 7) + ((lane >> 4) << 3)) * kTS + kk + ((lane >> 3) & 1) * 8);
+                bf[nj][0] = r[0];
+                bf[nj][1] = r[1];
+                bf[nj + 1][0] = r[2];
+                bf[nj + 1][1] = r[3];
+            }
 #pragma unroll
-                for (int b = 0; b < 4; ++b) acc[a][b] = fmaf(xv[a], wf[b], acc[a][b]);
+            for (int mi = 0; mi < 4; ++mi) {
+                uint32_t fh[4], fl[4];
+                const int off = (wm * 64 + mi * 16 + (lane & 15)) * kTS + kk + (lane >> 4) * 8;
+                ldsm_x4(fh, ah + off);
+                ldsm_x4(fl, al + off);
+#pragma unroll
+                for (int nj = 0; nj < 4; ++nj) {
+                    float part[4] = {0.f, 0.f, 0.f, 0.f};
+                    mma16816(part, fh, bf[nj][0], bf[nj][1]);
+                    mma16816(part, fl, bf[nj][0], bf[nj][1]);
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) acc[mi][nj][c] += part[c];
+                }
+            }
         }
         if (more) {
-            store(buf ^ 1);
-            __syncthreads();
-            buf ^= 1;
+            store_a(st ^ 1);
+            cp_async_wait<0>();
         }
+        __syncthreads();
     }
 #pragma unroll
-    for (int a = 0; a < 8; ++a) {
-        const int t = t0 + ty * 8 + a;
-        if (t >= T) continue;
+    for (int mi = 0; mi < 4; ++mi)
 #pragma unroll
-        for (int b = 0; b < 4; ++b) {
-            const int r = r0 + tx * 4 + b;
-            if (r >= R) continue;
-            const float v = acc[a][b];
-            float *dst = y + (size_t)t * R + r;
-            if (EPI == EPI_PLAIN)
-                *dst = vec ? v + vec[r] : v;
-            else if (EPI == EPI_GELU)
-                *dst = gelu_erf(v);
-            else
-                *dst = *dst + vec[r] * v;
+        for (int nj = 0; nj < 4; ++nj) {
+            const int c = r0 + wn * 32 + nj * 8 + 2 * tg;  // even; R is a multiple of 8
+            if (c >= R) continue;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int t = t0 + wm * 64 + mi * 16 + g + 8 * h;
+                if (t >= T) continue;
+                float v0 = acc[mi][nj][2 * h], v1 = acc[mi][nj][2 * h + 1];
+                if (EPI == EPI_QKV) {
+                    const int which = c >> 8, d = c & 255;
+                    if (which < 2) {
+                        const int b = t / ep.t_per_stream;
+                        const int pos = ep.offset[b] + (t - b * ep.t_per_stream);
+                        const int i = (d & 63) >> 1;
+                        const float freq = expf(-logf(10000.0f) * 2.0f * (float)i / (float)kHeadDim);
+                        const float ang = (float)pos * freq;
+                        const float cs = cosf(ang), sn = sinf(ang);
+                        const float x0 = v0, x1 = v1;
+                        v0 = x0 * cs - x1 * sn;
+                        v1 = x0 * sn + x1 * cs;
+                    }
+                    uint32_t hi, lo;
+                    if (which == 0) {
+                        split_pair_checked(v0 * 0.125f, v1 * 0.125f, hi, lo, ep.err);
+                        *reinterpret_cast<uint32_t *>(ep.q16 + ((size_t)t * 2 + 0) * kDModel + d) = hi;
+                        *reinterpret_cast<uint32_t *>(ep.q16 + ((size_t)t * 2 + 1) * kDModel + d) = lo;
+                    } else {
+                        const int plane = which == 1 ? 0 : 2;
+                        split_pair_checked(v0, v1, hi, lo, ep.err);
+                        *reinterpret_cast<uint32_t *>(ep.kv16 + ((size_t)t * 4 + plane) * kDModel + d) = hi;
+                        *reinterpret_cast<uint32_t *>(ep.kv16 + ((size_t)t * 4 + plane + 1) * kDModel + d) = lo;
+                    }
+                } else {
+                    float2 *dst = reinterpret_cast<float2 *>(ep.y + (size_t)t * R + c);
+                    if (EPI == EPI_PLAIN) {
+                        if (ep.vec) {
+                            v0 += ep.vec[c];
+                            v1 += ep.vec[c + 1];
+                        }
+                        *dst = make_float2(v0, v1);
+                    } else if (EPI == EPI_GELU) {
+                        *dst = make_float2(gelu_erf(v0), gelu_erf(v1));
+                    } else {
+                        const float2 o = *dst;
+                        *dst = make_float2(o.x + ep.vec[c] * v0, o.y + ep.vec[c + 1] * v1);
+                    }
+                }
+            }
         }
-    }
 }
 
 // z[row][r] = sum_i (b_i[r] + sum_k W_i[r][k] e_i[k]), e_i = codebook i's row for the row's code
@@ -241,190 +373,217 @@ __global__ void k_layernorm256(const float *__restrict__ x, int T, const float *
     }
 }
 
-// Interleaved RoPE on q and k of every row, position = the stream's stage offset + the row's
-// index in its chunk; frequency exp(-ln(10000) 2 i / 64) in fp32 (audio_layer.cpp:31-44).
-// One row per block: thread = (q or k head hq, pair i).
-__global__ void k_rope(float *__restrict__ qkv, int T, int t_per_stream, const int *__restrict__ offset) {
-    const int row = blockIdx.x;
-    if (row >= T) return;
-    const int b = row / t_per_stream;
-    const int pos = offset[b] + (row - b * t_per_stream);
-    const int i = threadIdx.x & 31;   // pair within a head
-    const int hq = threadIdx.x >> 5;  // 0..7: q heads 0..3, then k heads 0..3
-    const float freq = expf(-logf(10000.0f) * 2.0f * (float)i / (float)kHeadDim);
-    const float ang = (float)pos * freq;
-    const float c = cosf(ang), s = sinf(ang);
-    float *base = qkv + (size_t)row * 3 * kDModel + (hq >> 2) * kDModel + (hq & 3) * kHeadDim;
-    const float x0 = base[2 * i], x1 = base[2 * i + 1];
-    base[2 * i] = x0 * c - x1 * s;
-    base[2 * i + 1] = x0 * s + x1 * c;
-}
-
 // Windowed causal attention of a chunk (attn_scalar.cpp:165-203 attention_window_scalar):
 // chunk row i of a stream sees keys u in [max(0, i + n - window + 1), i + n], where keys
 // 0..n-1 are the stream's ring (physical slot (start + u) % window) and keys n.. the chunk's
-// own rows.  Block = (32 rows, head, stream), 256 threads; keys in tiles of 64 staged in
-// shared memory, softmax online across tiles.  Thread (g = tid / 16, j = tid % 16): scores of
-// rows 2g, 2g + 1 against keys 4j..4j+3 of a tile, then output dims 4j..4j+3 of those rows.
-constexpr int kAQ = 32, kAK = 64;
-constexpr size_t kAttnSmem = sizeof(float) * (kHeadDim * kAQ + kHeadDim * kAK + kAK * (kHeadDim + 4) +
-                                              kAQ * (kAK + 4));  // 50,688 bytes
-__global__ void __launch_bounds__(256) k_window_attn(const float *__restrict__ qkv, int t,
-                                                     const float *__restrict__ ring_k,
-                                                     const float *__restrict__ ring_v, int window, int layer,
+// own rows.  Block = (64 rows, head, stream), 4 warps of 16 rows; keys in tiles of 64 copied
+// (cp.async, two stages) into shared memory as fp16 hi/lo planes of k and v; scores and the
+// weighted sum on the tensor cores (3 products each for the hi/lo split), softmax online
+// across tiles with the probabilities scaled by 1024 (exact) so that small ones stay normal
+// fp16 numbers in the split.  Output: fp32 [rows][256].
+constexpr int kQT = 64, kKT = 64, kAS = 72;  // rows per block, keys per tile, smem row (halves)
+constexpr int kPlane = kKT * kAS;            // halves per plane of a tile
+constexpr size_t kAttnSmem = 2 * 4 * kPlane * sizeof(__half);  // 73,728 bytes
+
+__global__ void __launch_bounds__(128) k_window_attn(const __half *__restrict__ q16, const __half *__restrict__ kv16,
+                                                     int t, const __half *__restrict__ ring, int window, int layer,
                                                      Meta meta, int n_streams, float *__restrict__ out) {
-    extern __shared__ __align__(16) float attn_smem[];
-    auto qs = reinterpret_cast<float (*)[kAQ]>(attn_smem);                  // [64][32]
-    auto ks = reinterpret_cast<float (*)[kAK]>(attn_smem + kHeadDim * kAQ);  // [64][64]
-    auto vs = reinterpret_cast<float (*)[kHeadDim + 4]>(attn_smem + kHeadDim * kAQ + kHeadDim * kAK);  // [64][68]
-    auto ps = reinterpret_cast<float (*)[kAK + 4]>(attn_smem + kHeadDim * kAQ + kHeadDim * kAK + kAK * (kHeadDim + 4));
-    const int b = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * kAQ;
-    const int tid = threadIdx.x, g = tid >> 4, j = tid & 15;
+    extern __shared__ __align__(16) __half asmem[];
+    const int b = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * kQT;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, tg = lane & 3;
     const int n = meta.rcount[layer * n_streams + b], start = meta.rstart[layer * n_streams + b];
-    const size_t slot = (size_t)meta.sid[b];
-    const float *rk = ring_k + slot * window * kDModel + h * kHeadDim;
-    const float *rv = ring_v + slot * window * kDModel + h * kHeadDim;
-    const float *base = qkv + (size_t)b * t * 3 * kDModel;
-    const int nq = min(kAQ, t - q0);
-    for (int idx = tid; idx < kAQ * 16; idx += 256) {
-        const int q = idx & (kAQ - 1), d4 = idx / kAQ;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (q < nq) v = *reinterpret_cast<const float4 *>(base + (size_t)(q0 + q) * 3 * kDModel + h * kHeadDim + d4 * 4);
-        qs[d4 * 4 + 0][q] = v.x;
-        qs[d4 * 4 + 1][q] = v.y;
-        qs[d4 * 4 + 2][q] = v.z;
-        qs[d4 * 4 + 3][q] = v.w;
-    }
+    const __half *rbase = ring + (size_t)meta.sid[b] * window * 4 * kDModel;
+    const size_t row0 = (size_t)b * t;  // the stream's first chunk row
+    const int nq = min(kQT, t - q0);
     const int ulo = max(0, q0 + n - window + 1), uhi = q0 + nq - 1 + n;
-    const float scale = 1.0f / sqrtf((float)kHeadDim);
-    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f}, o[2][4] = {};
-    for (int u0 = ulo; u0 <= uhi; u0 += kAK) {
-        __syncthreads();  // the Q stores, and the previous tile's K and V reads, are done
-        for (int idx = tid; idx < kAK * 16; idx += 256) {
-            const int kk = idx & (kAK - 1), d4 = idx / kAK;
-            const int u = u0 + kk;
-            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+    const int i0 = q0 + warp * 16;       // this warp's first chunk row
+    const bool wact = warp * 16 < nq;
+    const int wlo = max(0, i0 + n - window + 1), whi = min(i0 + 15, q0 + nq - 1) + n;
+    const int ra = i0 + g, rb = ra + 8;  // this thread's two rows
+    const bool oka = ra - q0 < nq, okb = rb - q0 < nq;
+
+    auto issue_tile = [&](int st, int u0) {
+        __half *dst = asmem + st * 4 * kPlane;
+        for (int c = tid; c < kKT * 32; c += 128) {  // 64 keys x 4 planes x 8 chunks of 16 bytes
+            const int key = c >> 5, plane = (c >> 3) & 3, ch = c & 7;
+            const int u = u0 + key;
+            const __half *src = ring;
+            int bytes = 0;
             if (u <= uhi) {
-                const float *kp, *vp;
-                if (u < n) {
-                    const size_t at = (size_t)((start + u) % window) * kDModel + d4 * 4;
-                    kp = rk + at;
-                    vp = rv + at;
-                } else {
-                    kp = base + (size_t)(u - n) * 3 * kDModel + kDModel + h * kHeadDim + d4 * 4;
-                    vp = kp + kDModel;
-                }
-                kv = *reinterpret_cast<const float4 *>(kp);
-                vv = *reinterpret_cast<const float4 *>(vp);
+                src = u < n ? rbase + ((size_t)((start + u) % window) * 4 + plane) * kDModel + h * kHeadDim + ch * 8
+                            : kv16 + ((row0 + (size_t)(u - n)) * 4 + plane) * kDModel + h * kHeadDim + ch * 8;
+                bytes = 16;
             }
-            ks[d4 * 4 + 0][kk] = kv.x;
-            ks[d4 * 4 + 1][kk] = kv.y;
-            ks[d4 * 4 + 2][kk] = kv.z;
-            ks[d4 * 4 + 3][kk] = kv.w;
-            *reinterpret_cast<float4 *>(&vs[kk][d4 * 4]) = vv;
+            cp_async16(dst + plane * kPlane + key * kAS + ch * 8, src, bytes);
+        }
+        cp_async_commit();
+    };
+
+    // q fragments (hi, lo) of rows ra, rb: a0 (ra, d), a1 (rb, d), a2 (ra, d + 8), a3 (rb, d + 8)
+    uint32_t qh[4][4], ql[4][4];
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const int row = (r & 1) ? rb : ra;
+            const bool ok = (r & 1) ? okb : oka;
+            const int d = h * kHeadDim + ks * 16 + 2 * tg + (r >> 1) * 8;
+            qh[ks][r] = ok ? *reinterpret_cast<const uint32_t *>(q16 + ((row0 + row) * 2 + 0) * kDModel + d) : 0u;
+            ql[ks][r] = ok ? *reinterpret_cast<const uint32_t *>(q16 + ((row0 + row) * 2 + 1) * kDModel + d) : 0u;
+        }
+
+    float o[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) o[i][c] = 0.f;
+    float ma = -INFINITY, mb = -INFINITY, la = 0.f, lb = 0.f;
+    const int ntiles = (uhi - ulo) / kKT + 1;
+    issue_tile(0, ulo);
+    for (int it = 0; it < ntiles; ++it) {
+        const int st = it & 1, u0 = ulo + it * kKT;
+        if (it + 1 < ntiles) {
+            issue_tile(st ^ 1, u0 + kKT);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
         }
         __syncthreads();
-        float s[2][4] = {};
-#pragma unroll 16
-        for (int d = 0; d < kHeadDim; ++d) {
-            const float2 qv = *reinterpret_cast<const float2 *>(&qs[d][2 * g]);
-            const float4 kv = *reinterpret_cast<const float4 *>(&ks[d][4 * j]);
-            s[0][0] = fmaf(qv.x, kv.x, s[0][0]);
-            s[0][1] = fmaf(qv.x, kv.y, s[0][1]);
-            s[0][2] = fmaf(qv.x, kv.z, s[0][2]);
-            s[0][3] = fmaf(qv.x, kv.w, s[0][3]);
-            s[1][0] = fmaf(qv.y, kv.x, s[1][0]);
-            s[1][1] = fmaf(qv.y, kv.y, s[1][1]);
-            s[1][2] = fmaf(qv.y, kv.z, s[1][2]);
-            s[1][3] = fmaf(qv.y, kv.w, s[1][3]);
-        }
+        if (wact && u0 <= whi && u0 + kKT - 1 >= wlo) {
+            const __half *kh = asmem + st * 4 * kPlane, *kl = kh + kPlane, *vh = kh + 2 * kPlane,
+                         *vl = kh + 3 * kPlane;
+            float s[8][4];
 #pragma unroll
-        for (int a = 0; a < 2; ++a) {
-            const int i = q0 + 2 * g + a;  // chunk row
-            const bool row_ok = 2 * g + a < nq;
-            const int lo = i + n - window + 1, hi = i + n;
-            float tmax = -INFINITY;
+            for (int i = 0; i < 8; ++i)
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                const int u = u0 + 4 * j + c;
-                s[a][c] = (row_ok && u >= lo && u <= hi) ? s[a][c] * scale : -INFINITY;
-                tmax = fmaxf(tmax, s[a][c]);
-            }
+                for (int c = 0; c < 4; ++c) s[i][c] = 0.f;
 #pragma unroll
-            for (int off = 8; off > 0; off >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, off));
-            const float mnew = fmaxf(m[a], tmax);
-            float alpha = 1.f, rs = 0.f;
-            if (mnew != -INFINITY) {
-                alpha = expf(m[a] - mnew);  // 0 while m is still -inf
+            for (int ks = 0; ks < 4; ++ks)
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    s[a][c] = expf(s[a][c] - mnew);
-                    rs += s[a][c];
+                for (int nj = 0; nj < 8; nj += 2) {
+                    uint32_t rh[4], rl[4];
+                    const int off = (nj * 8 + (lane & 7) + ((lane >> 4) << 3)) * kAS + ks * 16 + ((lane >> 3) & 1) * 8;
+                    ldsm_x4(rh, kh + off);
+                    ldsm_x4(rl, kl + off);
+                    mma16816(s[nj], qh[ks], rh[0], rh[1]);
+                    mma16816(s[nj], qh[ks], rl[0], rl[1]);
+                    mma16816(s[nj], ql[ks], rh[0], rh[1]);
+                    mma16816(s[nj + 1], qh[ks], rh[2], rh[3]);
+                    mma16816(s[nj + 1], qh[ks], rl[2], rl[3]);
+                    mma16816(s[nj + 1], ql[ks], rh[2], rh[3]);
                 }
-            } else {
+            // mask to each row's window, then the online softmax of rows ra (c = 0, 1) and rb (c = 2, 3)
+            const int alo = ra + n - window + 1, ahi = ra + n, blo = alo + 8, bhi = ahi + 8;
+            float xa = -INFINITY, xb = -INFINITY;
 #pragma unroll
-                for (int c = 0; c < 4; ++c) s[a][c] = 0.f;
+            for (int nj = 0; nj < 8; ++nj)
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    const int u = u0 + nj * 8 + 2 * tg + c;
+                    s[nj][c] = (oka && u >= alo && u <= ahi) ? s[nj][c] : -INFINITY;
+                    s[nj][2 + c] = (okb && u >= blo && u <= bhi) ? s[nj][2 + c] : -INFINITY;
+                    xa = fmaxf(xa, s[nj][c]);
+                    xb = fmaxf(xb, s[nj][2 + c]);
+                }
+#pragma unroll
+            for (int off = 1; off <= 2; off <<= 1) {
+                xa = fmaxf(xa, __shfl_xor_sync(0xffffffffu, xa, off));
+                xb = fmaxf(xb, __shfl_xor_sync(0xffffffffu, xb, off));
+            }
+            const float na = fmaxf(ma, xa), nb = fmaxf(mb, xb);
+            const float fa = na == -INFINITY ? 1.f : expf(ma - na), fb = nb == -INFINITY ? 1.f : expf(mb - nb);
+            float sa = 0.f, sb = 0.f;
+#pragma unroll
+            for (int nj = 0; nj < 8; ++nj)
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    s[nj][c] = na == -INFINITY ? 0.f : expf(s[nj][c] - na) * 1024.f;
+                    s[nj][2 + c] = nb == -INFINITY ? 0.f : expf(s[nj][2 + c] - nb) * 1024.f;
+                    sa += s[nj][c];
+                    sb += s[nj][2 + c];
+                }
+            la = la * fa + sa;
+            lb = lb * fb + sb;
+            ma = na;
+            mb = nb;
+            // ov = p v over the tile's 64 keys, 16 at a time, from zero; then o = o f + ov with
+            // rounded fp32 arithmetic (a short tensor-core chain per tile, see k_gemm_mma)
+            float ov[8][4];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) ov[i][c] = 0.f;
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+                uint32_t ph[4], pl[4];
+                split_pair(s[2 * ks][0], s[2 * ks][1], ph[0], pl[0]);
+                split_pair(s[2 * ks][2], s[2 * ks][3], ph[1], pl[1]);
+                split_pair(s[2 * ks + 1][0], s[2 * ks + 1][1], ph[2], pl[2]);
+                split_pair(s[2 * ks + 1][2], s[2 * ks + 1][3], ph[3], pl[3]);
+#pragma unroll
+                for (int nd = 0; nd < 8; nd += 2) {
+                    uint32_t rh[4], rl[4];
+                    const int off = (ks * 16 + (lane & 7) + (((lane >> 3) & 1) << 3)) * kAS + (nd + (lane >> 4)) * 8;
+                    ldsm_x4_t(rh, vh + off);
+                    ldsm_x4_t(rl, vl + off);
+                    mma16816(ov[nd], ph, rh[0], rh[1]);
+                    mma16816(ov[nd], ph, rl[0], rl[1]);
+                    mma16816(ov[nd], pl, rh[0], rh[1]);
+                    mma16816(ov[nd + 1], ph, rh[2], rh[3]);
+                    mma16816(ov[nd + 1], ph, rl[2], rl[3]);
+                    mma16816(ov[nd + 1], pl, rh[2], rh[3]);
+                }
             }
 #pragma unroll
-            for (int off = 8; off > 0; off >>= 1) rs += __shfl_xor_sync(0xffffffffu, rs, off);
-            l[a] = l[a] * alpha + rs;
-            m[a] = mnew;
-#pragma unroll
-            for (int c = 0; c < 4; ++c) o[a][c] *= alpha;
-            *reinterpret_cast<float4 *>(&ps[2 * g + a][4 * j]) = make_float4(s[a][0], s[a][1], s[a][2], s[a][3]);
+            for (int nd = 0; nd < 8; ++nd) {
+                o[nd][0] = o[nd][0] * fa + ov[nd][0];
+                o[nd][1] = o[nd][1] * fa + ov[nd][1];
+                o[nd][2] = o[nd][2] * fb + ov[nd][2];
+                o[nd][3] = o[nd][3] * fb + ov[nd][3];
+            }
         }
-        __syncwarp();  // rows 2g, 2g+1 are written and read by the same 16 lanes
-#pragma unroll 8
-        for (int kk = 0; kk < kAK; ++kk) {
-            const float p0 = ps[2 * g][kk], p1 = ps[2 * g + 1][kk];
-            const float4 vv = *reinterpret_cast<const float4 *>(&vs[kk][4 * j]);
-            o[0][0] = fmaf(p0, vv.x, o[0][0]);
-            o[0][1] = fmaf(p0, vv.y, o[0][1]);
-            o[0][2] = fmaf(p0, vv.z, o[0][2]);
-            o[0][3] = fmaf(p0, vv.w, o[0][3]);
-            o[1][0] = fmaf(p1, vv.x, o[1][0]);
-            o[1][1] = fmaf(p1, vv.y, o[1][1]);
-            o[1][2] = fmaf(p1, vv.z, o[1][2]);
-            o[1][3] = fmaf(p1, vv.w, o[1][3]);
-        }
-        __syncwarp();
+        __syncthreads();  // every warp is done with this stage before the next issue refills it
     }
 #pragma unroll
-    for (int a = 0; a < 2; ++a) {
-        if (2 * g + a >= nq) continue;
-        const float inv = 1.0f / l[a];
-        float *dst = out + ((size_t)b * t + q0 + 2 * g + a) * kDModel + h * kHeadDim + 4 * j;
-        *reinterpret_cast<float4 *>(dst) = make_float4(o[a][0] * inv, o[a][1] * inv, o[a][2] * inv, o[a][3] * inv);
+    for (int off = 1; off <= 2; off <<= 1) {
+        la += __shfl_xor_sync(0xffffffffu, la, off);
+        lb += __shfl_xor_sync(0xffffffffu, lb, off);
+    }
+    if (!wact) return;
+#pragma unroll
+    for (int nd = 0; nd < 8; ++nd) {
+        const int d = h * kHeadDim + nd * 8 + 2 * tg;
+        if (oka) *reinterpret_cast<float2 *>(out + (row0 + ra) * kDModel + d) = make_float2(o[nd][0] / la, o[nd][1] / la);
+        if (okb) *reinterpret_cast<float2 *>(out + (row0 + rb) * kDModel + d) = make_float2(o[nd][2] / lb, o[nd][3] / lb);
     }
 }
 
-// Append each stream's chunk K and V rows to its ring (decoder.cpp:150-169): chunk row i goes
-// to slot (start + n + i) % window; only the last `window` rows of a chunk can survive, so only
-// they are written.
-__global__ void k_ring_append(const float *__restrict__ qkv, int t, int n_streams, float *__restrict__ ring_k,
-                              float *__restrict__ ring_v, int window, int layer, Meta meta) {
+// Append each stream's chunk K and V rows (kv16 planes) to its ring (decoder.cpp:150-169):
+// chunk row i goes to slot (start + n + i) % window; only the last `window` rows of a chunk can
+// survive, so only they are written.  One row = 4 planes x 256 halves = 128 x 16 bytes.
+__global__ void k_ring_append(const __half *__restrict__ kv16, int t, int n_streams, __half *__restrict__ ring,
+                              int window, int layer, Meta meta) {
     const int first = max(0, t - window);
     const int rows = t - first;
-    const size_t total = (size_t)n_streams * rows * (kDModel / 4);
+    const size_t total = (size_t)n_streams * rows * 128;
     for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
          idx += (size_t)gridDim.x * blockDim.x) {
-        const int d4 = (int)(idx % (kDModel / 4));
-        const size_t rr = idx / (kDModel / 4);
+        const int c = (int)(idx & 127);
+        const size_t rr = idx >> 7;
         const int b = (int)(rr / rows), i = first + (int)(rr % rows);
         const int n = meta.rcount[layer * n_streams + b], start = meta.rstart[layer * n_streams + b];
         const size_t slot = (size_t)meta.sid[b] * window + (size_t)((start + n + i) % window);
-        const float *src = qkv + ((size_t)b * t + i) * 3 * kDModel + d4 * 4;
-        reinterpret_cast<float4 *>(ring_k + slot * kDModel)[d4] = *reinterpret_cast<const float4 *>(src + kDModel);
-        reinterpret_cast<float4 *>(ring_v + slot * kDModel)[d4] = *reinterpret_cast<const float4 *>(src + 2 * kDModel);
+        reinterpret_cast<uint4 *>(ring + slot * 4 * kDModel)[c] =
+            reinterpret_cast<const uint4 *>(kv16 + ((size_t)b * t + i) * 4 * kDModel)[c];
     }
 }
 
 // ------------------------------------------------------------------------------- host
 
 // kernel classes of the optional per-launch profile (mossgpu_codec_profile)
-enum Kind { KD_FRONT = 0, KD_GEMM, KD_PATCH, KD_LAYERNORM, KD_ROPE, KD_ATTN, KD_RING, KD_COUNT };
-const char *const kKindNames[KD_COUNT] = {"k_front", "k_gemm_f16w", "k_patch", "k_layernorm256",
-                                          "k_rope", "k_window_attn", "k_ring_append"};
+enum Kind { KD_FRONT = 0, KD_GEMM, KD_PATCH, KD_LAYERNORM, KD_ATTN, KD_RING, KD_COUNT };
+const char *const kKindNames[KD_COUNT] = {"k_front", "k_gemm_mma", "k_patch", "k_layernorm256",
+                                          "k_window_attn", "k_ring_append"};
 
 struct Mat {
     __half *w = nullptr;
@@ -434,7 +593,7 @@ struct Mat {
 struct Layer {
     Mat attn, proj, f1, f2;
     float *n1w, *n1b, *n2w, *n2b, *ls1, *ls2;
-    float *ring_k = nullptr, *ring_v = nullptr;  // [slots][context][256]
+    __half *ring = nullptr;  // [slots][context][kh, kl, vh, vl][256]
 };
 
 struct Stage {
@@ -460,17 +619,21 @@ public:
         if (max_batch_frames > (1 << 20)) throw std::runtime_error("max_batch_frames must be at most 1048576");
         CK(cudaSetDevice(device));
         CK(cudaFuncSetAttribute(k_window_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kAttnSmem)));
+        CK(cudaFuncSetAttribute(k_gemm_mma<EPI_PLAIN>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kGemmSmem)));
+        CK(cudaFuncSetAttribute(k_gemm_mma<EPI_GELU>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kGemmSmem)));
+        CK(cudaFuncSetAttribute(k_gemm_mma<EPI_SCALED_ADD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(kGemmSmem)));
+        CK(cudaFuncSetAttribute(k_gemm_mma<EPI_QKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kGemmSmem)));
         slots_.resize(size_t(max_streams) + 1);  // the last slot serves decode()
         load(path);
         // activation buffers, each sized for its widest use over the stages
         const size_t F = size_t(max_frames_);
-        size_t x_elems = F * size_t(std::max(c0_, kZ)), y_elems = 0, qkv_elems = 0, ffn_elems = 0;
+        size_t x_elems = F * size_t(std::max(c0_, kZ)), y_elems = 0, ffn_elems = 0;
         size_t rows = F;
         for (int s = 0; s < kStages; ++s) {
             rows *= kPatch[s];
             x_elems = std::max(x_elems, rows * size_t(stages_[size_t(s)].out.rows));
             y_elems = std::max(y_elems, rows * kDModel);
-            qkv_elems = std::max(qkv_elems, rows * 3 * kDModel);
             for (auto &l : stages_[size_t(s)].layers) ffn_elems = std::max(ffn_elems, rows * size_t(l.f1.rows));
         }
         xa_ = alloc<float>(x_elems);
@@ -478,8 +641,11 @@ public:
         y_ = alloc<float>(y_elems);
         ln_ = alloc<float>(std::max(y_elems, F * kZ));
         att_ = alloc<float>(y_elems);
-        qkv_ = alloc<float>(qkv_elems);
+        q16_ = alloc<__half>(y_elems * 2);
+        kv16_ = alloc<__half>(y_elems * 4);
         ffn_ = alloc<float>(ffn_elems);
+        err_ = alloc<int>(1);
+        CK(cudaMemset(err_, 0, sizeof(int)));
         codes_ = alloc<int>(size_t(kNCb) * F);
         meta_d_ = alloc<int>(size_t(1 + kStages + 2 * kLayersTotal) * (size_t(max_streams_) + 1));
         pcm_ = alloc<float>(F * size_t(samples_per_frame()));
@@ -606,7 +772,19 @@ public:
         decode_device(sids, n, codes_, frames, pcm_);
         CK(cudaMemcpyAsync(pcm, pcm_, size_t(n) * size_t(frames) * spf * sizeof(float), cudaMemcpyDeviceToHost,
                            stream_));
+        if (status() != 0)
+            throw std::runtime_error("an activation left the fp16 range (|x| >= 65504 or NaN); the streams of this "
+                                     "call must be reset");
+    }
+
+    // Synchronise the codec's stream and return (and clear) the range flag: 1 when a value of
+    // some call since the last read could not be held in fp16.
+    int status() {
+        int v = 0;
+        CK(cudaMemcpyAsync(&v, err_, sizeof(int), cudaMemcpyDeviceToHost, stream_));
         CK(cudaStreamSynchronize(stream_));
+        if (v) CK(cudaMemset(err_, 0, sizeof(int)));
+        return v;
     }
 
     // AudioDecoder::decode (decoder.cpp:254-280): the whole utterance from a clean state; the
@@ -636,7 +814,7 @@ public:
 
     int launches_per_call() const {
         int l = 2;
-        for (auto &s : stages_) l += 3 + 9 * int(s.layers.size());
+        for (auto &s : stages_) l += 3 + 8 * int(s.layers.size());
         return l;
     }
 
@@ -672,17 +850,26 @@ private:
         return static_cast<T *>(p);
     }
 
-    void gemm(const Mat &m, const float *x, int T, float *y, int epi, const float *vec) {
-        const dim3 grid((m.rows + kBN - 1) / kBN, (T + kBM - 1) / kBM);
+    void gemm(const Mat &m, const float *x, int T, int epi, Epi ep) {
+        const dim3 grid((m.rows + kTN - 1) / kTN, (T + kTM - 1) / kTM);
+        ep.err = err_;
         mark_begin(KD_GEMM);
         if (epi == EPI_PLAIN)
-            k_gemm_f16w<EPI_PLAIN><<<grid, kGemmThreads, 0, stream_>>>(m.w, x, T, m.rows, m.cols, vec, y);
+            k_gemm_mma<EPI_PLAIN><<<grid, 256, kGemmSmem, stream_>>>(m.w, x, T, m.rows, m.cols, ep);
         else if (epi == EPI_GELU)
-            k_gemm_f16w<EPI_GELU><<<grid, kGemmThreads, 0, stream_>>>(m.w, x, T, m.rows, m.cols, vec, y);
+            k_gemm_mma<EPI_GELU><<<grid, 256, kGemmSmem, stream_>>>(m.w, x, T, m.rows, m.cols, ep);
+        else if (epi == EPI_SCALED_ADD)
+            k_gemm_mma<EPI_SCALED_ADD><<<grid, 256, kGemmSmem, stream_>>>(m.w, x, T, m.rows, m.cols, ep);
         else
-            k_gemm_f16w<EPI_SCALED_ADD><<<grid, kGemmThreads, 0, stream_>>>(m.w, x, T, m.rows, m.cols, vec, y);
+            k_gemm_mma<EPI_QKV><<<grid, 256, kGemmSmem, stream_>>>(m.w, x, T, m.rows, m.cols, ep);
         CK(cudaGetLastError());
         mark_end();
+    }
+    static Epi out(float *y, const float *vec = nullptr) {
+        Epi e;
+        e.y = y;
+        e.vec = vec;
+        return e;
     }
 
     void run(const Meta &md, int n, const int *codes, int frames, float *pcm) {
@@ -691,7 +878,7 @@ private:
         k_front<<<rows, 256, 0, stream_>>>(codes, frames, d_cb_, d_ow_, d_ob_, ln_);
         CK(cudaGetLastError());
         mark_end();
-        gemm(q_out_, ln_, rows, xa_, EPI_PLAIN, q_out_b_);
+        gemm(q_out_, ln_, rows, EPI_PLAIN, out(xa_, q_out_b_));
         int c = c0_, t = frames, li = 0;
         for (int s = 0; s < kStages; ++s) {
             Stage &st = stages_[size_t(s)];
@@ -705,10 +892,10 @@ private:
             rows *= p;
             t *= p;
             c /= p;
-            gemm(st.in, xb_, rows, y_, EPI_PLAIN, nullptr);
+            gemm(st.in, xb_, rows, EPI_PLAIN, out(y_));
             for (auto &l : st.layers) layer(l, md, n, rows, t, kContext[s], li++, md.offset + s * n);
             float *dst = s + 1 < kStages ? xa_ : pcm;  // the final patch of 240 is the identity
-            gemm(st.out, y_, rows, dst, EPI_PLAIN, nullptr);
+            gemm(st.out, y_, rows, EPI_PLAIN, out(dst));
             c = st.out.rows;
         }
     }
@@ -719,26 +906,28 @@ private:
         mark_begin(KD_LAYERNORM);
         k_layernorm256<<<lnb, 256, 0, stream_>>>(y_, rows, l.n1w, l.n1b, ln_);
         mark_end();
-        gemm(l.attn, ln_, rows, qkv_, EPI_PLAIN, nullptr);
-        mark_begin(KD_ROPE);
-        k_rope<<<rows, 256, 0, stream_>>>(qkv_, rows, t, offset);
-        mark_end();
-        const dim3 ag((t + kAQ - 1) / kAQ, kHeads, n);
+        Epi qkv;
+        qkv.q16 = q16_;
+        qkv.kv16 = kv16_;
+        qkv.offset = offset;
+        qkv.t_per_stream = t;
+        gemm(l.attn, ln_, rows, EPI_QKV, qkv);
+        const dim3 ag((t + kQT - 1) / kQT, kHeads, n);
         mark_begin(KD_ATTN);
-        k_window_attn<<<ag, 256, kAttnSmem, stream_>>>(qkv_, t, l.ring_k, l.ring_v, window, li, md, n, att_);
+        k_window_attn<<<ag, 128, kAttnSmem, stream_>>>(q16_, kv16_, t, l.ring, window, li, md, n, att_);
         mark_end();
-        const size_t items = size_t(n) * size_t(std::min(t, window)) * (kDModel / 4);
+        const size_t items = size_t(n) * size_t(std::min(t, window)) * 128;
         mark_begin(KD_RING);
         k_ring_append<<<int(std::min<size_t>((items + 255) / 256, 148 * 8)), 256, 0, stream_>>>(
-            qkv_, t, n, l.ring_k, l.ring_v, window, li, md);
+            kv16_, t, n, l.ring, window, li, md);
         CK(cudaGetLastError());
         mark_end();
-        gemm(l.proj, att_, rows, y_, EPI_SCALED_ADD, l.ls1);
+        gemm(l.proj, att_, rows, EPI_SCALED_ADD, out(y_, l.ls1));
         mark_begin(KD_LAYERNORM);
         k_layernorm256<<<lnb, 256, 0, stream_>>>(y_, rows, l.n2w, l.n2b, ln_);
         mark_end();
-        gemm(l.f1, ln_, rows, ffn_, EPI_GELU, nullptr);
-        gemm(l.f2, ffn_, rows, y_, EPI_SCALED_ADD, l.ls2);
+        gemm(l.f1, ln_, rows, EPI_GELU, out(ffn_));
+        gemm(l.f2, ffn_, rows, EPI_SCALED_ADD, out(y_, l.ls2));
     }
 
     void load(const std::string &path) {
@@ -784,7 +973,8 @@ private:
         auto mat = [&](const std::string &name) {  // f16 matrix [rows][cols]
             const Entry &e = find(name);
             const size_t cnt = size_t(e.rows) * size_t(e.cols);
-            if (e.cols % 8) throw std::runtime_error("matrix " + name + " needs a column count that is a multiple of 8");
+            if (e.cols % 8 || e.rows % 8)
+                throw std::runtime_error("matrix " + name + " needs row and column counts that are multiples of 8");
             if (e.dtype != 0 || e.nbytes != cnt * 2) throw std::runtime_error("matrix is not f16: " + name);
             Mat m;
             m.rows = e.rows;
@@ -845,9 +1035,7 @@ private:
                 L.n2b = f32(lp + "n2.b", kDModel);
                 L.ls1 = f32(lp + "ls1", kDModel);
                 L.ls2 = f32(lp + "ls2", kDModel);
-                const size_t ring = nslots * size_t(kContext[s]) * kDModel;
-                L.ring_k = alloc<float>(ring);
-                L.ring_v = alloc<float>(ring);
+                L.ring = alloc<__half>(nslots * size_t(kContext[s]) * 4 * kDModel);
             }
             c = st.out.rows;
         }
@@ -863,9 +1051,10 @@ private:
     float *q_out_b_ = nullptr;
     const float **d_cb_ = nullptr, **d_ow_ = nullptr, **d_ob_ = nullptr;
     std::vector<Stage> stages_;
-    float *xa_ = nullptr, *xb_ = nullptr, *y_ = nullptr, *ln_ = nullptr, *qkv_ = nullptr, *att_ = nullptr,
-          *ffn_ = nullptr, *pcm_ = nullptr;
-    int *codes_ = nullptr, *meta_d_ = nullptr;
+    float *xa_ = nullptr, *xb_ = nullptr, *y_ = nullptr, *ln_ = nullptr, *att_ = nullptr, *ffn_ = nullptr,
+          *pcm_ = nullptr;
+    __half *q16_ = nullptr, *kv16_ = nullptr;
+    int *codes_ = nullptr, *meta_d_ = nullptr, *err_ = nullptr;
     bool profile_ = false;
     std::vector<int> marks_;            // kernel class of each bracketed launch
     std::vector<cudaEvent_t> events_;   // two per bracketed launch, reused
@@ -946,6 +1135,13 @@ int mossgpu_codec_profile_read(mossgpu_codec *h, float *total_ms, int *launches,
 const char *mossgpu_codec_kernel_name(int kind) {
     using namespace mossgpu::codec;
     return kind >= 0 && kind < KD_COUNT ? kKindNames[kind] : "";
+}
+
+int mossgpu_codec_status(mossgpu_codec *h, int *code) {
+    return codec_guarded(h, [&](mossgpu::codec::Codec &c) {
+        if (!code) throw std::runtime_error("code is NULL");
+        *code = c.status();
+    });
 }
 
 int mossgpu_codec_set_cuda_stream(mossgpu_codec *h, void *cuda_stream) {

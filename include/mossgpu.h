@@ -257,9 +257,13 @@ int mossgpu_attention_decode_paged_noalloc(const float *q, const void *kv_layer,
  * (samples_per_frame: 32 rows x 240 of the last stage, interleaved L, R at 48 kHz).
  * The decoder file is the reference's .moss export with f16 matrices (decoder_f16.moss,
  * tools/export_decoder.py --dtype f16); other matrix types are rejected at create.
- * Products are fp32 accumulations of fp16 weights and fp32 activations, as the reference's
- * gemm_par on f16 matrices; results agree with the reference's to float rounding, not bit
- * for bit.  Conventions as above: 0 on success, the message from mossgpu_codec_last_error. */
+ * Arithmetic: the reference computes in fp32 with fp16 matrices; here the products run on
+ * the tensor cores with each fp32 operand split into fp16 hi + lo (~22 significant bits)
+ * and fp32 accumulation, so results agree with the reference's to float rounding, not bit for
+ * bit.  The split needs every activation below 65504 in magnitude: a larger one (or a NaN)
+ * makes the host entry points fail and is reported by mossgpu_codec_status; the streams of
+ * that call must then be reset.  Conventions as above: 0 on success, the message from
+ * mossgpu_codec_last_error. */
 typedef struct mossgpu_codec mossgpu_codec;
 
 /* AudioDecoder(threads) + load (decoder.cpp:26-71).  max_batch_frames bounds the frames one
@@ -276,7 +280,7 @@ size_t mossgpu_codec_device_bytes(mossgpu_codec *c);
 int mossgpu_codec_set_cuda_stream(mossgpu_codec *c, void *cuda_stream);
 /* Per-kernel-class device time: while enabled, each launch is bracketed by CUDA events (which
  * add a gap per launch); profile_read synchronises, writes the milliseconds and launch count of
- * each class since the last read (max_kinds >= 7) and the class count to *n_kinds.  Class
+ * each class since the last read (max_kinds >= 6) and the class count to *n_kinds.  Class
  * names: mossgpu_codec_kernel_name. */
 int mossgpu_codec_profile(mossgpu_codec *c, int enable);
 int mossgpu_codec_profile_read(mossgpu_codec *c, float *total_ms, int *launches, int max_kinds, int *n_kinds);
@@ -302,6 +306,9 @@ int mossgpu_codec_decode_batch_device(mossgpu_codec *c, const int32_t *stream_id
 /* AudioDecoder::decode (decoder.cpp:254-280): a whole utterance, codes [16][frames], from a
  * clean state, leaving every codec stream untouched. */
 int mossgpu_codec_decode(mossgpu_codec *c, const int32_t *codes, int frames, float *out, size_t out_cap, int *out_n);
+/* Synchronise the codec's stream; *code = 1 when an activation of a call since the last read
+ * left the fp16 range (then cleared), else 0.  The device entry point's only error report. */
+int mossgpu_codec_status(mossgpu_codec *c, int *code);
 
 #ifdef __cplusplus
 }

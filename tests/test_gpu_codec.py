@@ -4,8 +4,9 @@ whole-utterance decode, chunked streaming and 160 frames of streaming that wrap 
 ring, then the batched entry points against per-stream decoding by the reference (or the
 numpy restatement where oracle/_ref is not built), and the error behaviour.
 
-Tolerance: samples within 5e-4 absolute (outputs reach about 20; the GPU and the reference
-differ in fp32 summation order only), per-frame energies within 1e-5 relative."""
+Tolerance: samples within 5e-4 absolute (outputs reach about 20), per-frame energies within
+1e-5 relative: the GPU's products use fp16 hi + lo splits of the fp32 operands (about 22
+significant bits) with fp32 accumulation in another order than the reference's."""
 from __future__ import annotations
 
 import numpy as np
@@ -210,3 +211,27 @@ def test_audio_decoder_interface(pkg, decoder_file, golden):
     bad = pkg.AudioDecoder()
     ok, err = bad.load("/nonexistent/decoder.moss")
     assert not ok and "cannot open" in err
+
+
+def test_activation_outside_fp16_range_is_reported(pkg, tmp_path):
+    """The tensor-core split needs activations below 65504 in magnitude: a decoder whose q.out
+    bias is 1e5 overflows it, the host entry point fails with the reason, the device entry point
+    reports it through mossgpu_codec_status, and a normal call afterwards succeeds."""
+    import torch
+    from moss_b200 import codecfile
+    path = tmp_path / "big.moss"
+    codecfile.synth_decoder(path, 1, add={"q.out.b": 1e5})
+    codec = pkg.Codec(str(path), device=0, max_streams=2, max_batch_frames=8)
+    try:
+        sid = codec.open()
+        with pytest.raises(pkg.MossGpuError, match="fp16 range"):
+            codec.decode_chunk(sid, codec_codes(2, seed=8))
+        assert codec.status() == 0  # the failed call's flag was read and cleared
+        dcodes = torch.from_numpy(codec_codes(2, seed=9)[None]).cuda()
+        dout = torch.empty((1, 2 * SPF), dtype=torch.float32, device="cuda")
+        codec.reset(sid)
+        codec.decode_batch_device([sid], dcodes.data_ptr(), 2, dout.data_ptr())
+        assert codec.status() == 1
+        assert codec.status() == 0
+    finally:
+        codec.close()
