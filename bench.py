@@ -428,7 +428,7 @@ def run_ours(args, rank, world, local_rank, dist):
                      max_rows=max(B + 2, 256))
     eng.set_cuda_stream(torch.cuda.current_stream().cuda_stream)
     if args.tc_direct_min is not None:
-        eng.set_tc_policy(args.tc_direct_min, 256)
+        eng.set_tc_policy(args.tc_direct_min, args.tc_direct_rows)
     if args.local_path is not None:
         eng.set_local_path(args.local_path)
     sids = [eng.open() for _ in lens]
@@ -734,7 +734,7 @@ def run_sweep(args, rank, world, local_rank, dist):
     eng = pkg.Engine(weights, device=local_rank, max_streams=len(mine) + 1, max_ctx=args.lmax + frames + warm + 32,
                      kv_pages=pages, max_rows=max(len(mine) + 1, 256))
     if args.tc_direct_min is not None:
-        eng.set_tc_policy(args.tc_direct_min, 256)
+        eng.set_tc_policy(args.tc_direct_min, args.tc_direct_rows)
     sids = [eng.open() for _ in mine]
     for i, (s, L) in enumerate(zip(sids, mine)):
         eng.fill_state_random(s, L, seed=7000 + 1000 * rank + i)
@@ -791,6 +791,8 @@ def main():
     ap.add_argument("--lmax", type=int, default=None)
     ap.add_argument("--tc-direct-min", type=int, default=None,
                     help="batch rows from which the GEMMs use the direct tile form (mossgpu_set_tc_policy)")
+    ap.add_argument("--tc-direct-rows", type=int, default=0,
+                    help="batch rows per tile of the direct form (mossgpu_set_tc_policy; 0 = by batch size)")
     ap.add_argument("--local-path", type=int, default=None,
                     help="local decoder: 0 = fused cluster kernel for greedy frames, 1 = per-step kernels "
                          "(mossgpu_set_local_path; default: the engine's)")

@@ -512,8 +512,8 @@ void Engine::set_gemm_path(int mode) {
 }
 
 void Engine::set_tc_policy(int direct_min_rows, int direct_rows) {
-    if (direct_min_rows < 0 || direct_rows < 16 || direct_rows > kTcMaxND || direct_rows % 16)
-        throw std::runtime_error("direct rows must be a multiple of 16 in 16..256");
+    if (direct_min_rows < 0 || (direct_rows != 0 && (direct_rows < 16 || direct_rows > kTcMaxND || direct_rows % 16)))
+        throw std::runtime_error("direct rows must be 0 (by batch size) or a multiple of 16 in 16..256");
     if (direct_min_rows == tc_direct_min_rows_ && direct_rows == tc_direct_rows_) return;
     tc_direct_min_rows_ = direct_min_rows;
     tc_direct_rows_ = direct_rows;
@@ -536,19 +536,38 @@ namespace {
 
 // Decode batches (split-K form): grid = weight tiles x cluster CTAs x batch slices of <= 64
 // rows.  At 64 rows a QKV GEMM has 18 weight tiles; clusters of 8 give it 144 CTAs streaming
-// 1-2 K chunks each.  Batches of at least direct_min padded rows (prefill passes) take the
-// direct form instead: weight tiles x slices of <= direct_ns rows, every K chunk in one CTA.
+// 1-2 K chunks each.  Batches of at least direct_min padded rows take the direct form instead:
+// weight tiles x slices of <= direct_ns rows (x K parts), every K chunk of a part in one CTA.
+// direct_ns = 0 sizes the slices by the batch: 256 rows from 1024 rows on (prefill passes);
+// below that the smallest of 64 / 128 / 256 rows whose tiles fit one wave of the SMs, and the
+// split-K form when even 64-row slices leave fewer than 72 tiles and the output is not stored
+// in K parts (a 768-row matrix with a residual epilogue, the audio heads).  Measured per GEMM on a 512-stream frame (one B200, ms per frame,
+// split-K / 128-row / 64-row slices): global QKV 0.35 / 0.20 / 0.18, fc_in 0.55 / 0.26 / 0.35,
+// local fc_out 0.51 / 0.81 / 0.78, audio heads 0.21 / 0.27 / 0.24.
 template <int EPI>
 void launch_tc(TcArgs a, int prec, cudaStream_t st, bool pdl, int direct_min, int direct_ns) {
     const int tiles = a.rows / kTcM, nchunks = a.K / kTcK;
-    if (direct_min > 0 && a.N >= direct_min) {
-        int ns = std::min(a.N, direct_ns);
+    const int ks = (EPI == TC_STORE && a.ksplit > 1 && nchunks % a.ksplit == 0) ? a.ksplit : 1;
+    bool direct = direct_min > 0 && a.N >= direct_min;
+    int ns = 0;
+    if (direct && direct_ns > 0) {
+        ns = std::min(a.N, direct_ns);
+    } else if (direct && a.N >= 1024) {
+        ns = std::min(a.N, kTcMaxND);
+    } else if (direct) {
+        for (int cand : {64, 128, 256}) {
+            ns = std::min(a.N, cand);
+            if (tiles * ((a.N + ns - 1) / ns) * ks <= kNumSMs) break;
+        }
+        // a STORE in K parts stays direct: its consumer adds the parts, split-K writes one
+        if (ks == 1 && tiles * ((a.N + 63) / 64) < 72) direct = false;
+    }
+    if (direct) {
         while (a.N % ns) ns -= 16;
         a.nsub = ns;
         a.csize = 1;
         // tile-persistent: at most one CTA per SM walks the (weight tile, slice) tiles; slices
         // of <= 128 rows keep A in tensor memory beside the two accumulators
-        const int ks = (EPI == TC_STORE && a.ksplit > 1 && nchunks % a.ksplit == 0) ? a.ksplit : 1;
         a.ksplit = ks;
         const dim3 grid(std::min(tiles * (a.N / ns) * ks, kNumSMs));
         const bool atm = ns <= 128;

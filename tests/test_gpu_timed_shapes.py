@@ -1,7 +1,8 @@
 """GPU parity at the shapes the benchmark times, against the C oracle (pinned bit for bit to
 the reference's own LlmModel by tests/test_oracle_golden.py).
 
-* the benched frame: 64 streams with configs[1] lengths U{64..1024}, stepped through
+* the benched frames: 64 streams with configs[1] lengths U{64..1024}, and 512 streams with
+  configs[4] lengths U{256..4096} (the default workload: direct GEMM form), stepped through
   mossgpu_step_frames (the multi-frame CUDA graph that bench.py's `value` times);
 * a 256-row frame with configs[3] lengths U{128..2048}: the engine's split-K attention
   (plan -> decode -> combine) and the 4-slice tensor-core GEMM grid;
@@ -251,6 +252,40 @@ def test_long_context_golden_on_gpu(pkg, weights_path):
         eng.step([s], pkg.SampleParams.make(**GREEDY_NEVER_STOP), forced=row[1:])
         assert eng.position(s) == int(g["position"])
         assert np.abs(eng.hidden(s) - g["hidden2"]).max() < TOL
+    finally:
+        eng.close()
+
+
+def test_benched_frame_512_streams_direct_form(pkg, weights_path):
+    """bench.py's default workload (BASELINE configs[4] at N=1): 512 streams, KV lengths
+    U{256..4096} (bench.py's seed), 3 free-running greedy frames through mossgpu_step_frames
+    with the engine's default tensor-core policy -- at 512 rows the direct GEMM form in
+    128-row slices -- then 6 sampled streams against the oracle."""
+    lens = [int(x) for x in np.random.default_rng(4096).integers(256, 4097, 512)]
+    F = 3
+    pages = sum((L + F + 8 + 15) // 16 + 1 for L in lens) + 16
+    eng = pkg.Engine(weights_path, device=0, max_streams=513, max_ctx=4096 + F + 16, kv_pages=pages)
+    try:
+        sids = [eng.open() for _ in lens]
+        for i, (s, L) in enumerate(zip(sids, lens)):
+            eng.fill_state_random(s, L, seed=700 + i)
+            eng.generate_begin(s, 0)
+        sample = sorted({int(np.argmin(lens)), int(np.argmax(lens)), 0, 200, 383, 511})
+        states = {i: read_state(eng, sids[i], lens[i]) for i in sample}
+        codes, done = eng.step_frames(sids, pkg.SampleParams.make(**GREEDY_NEVER_STOP), F)
+        assert (done == F).all()
+        with pool() as ex:
+            res = dict(zip(sample, ex.map(lambda i: oracle_forced(weights_path, states[i], codes[:, i], True),
+                                          sample)))
+        for i in sample:
+            o_codes, _, _, o_hidden, orc = res[i]
+            check_codes(codes[:, i], o_codes, f"stream {i} (L={lens[i]})")
+            assert eng.position(sids[i]) == lens[i] + F
+            assert np.abs(eng.hidden(sids[i]) - o_hidden).max() < TOL, i
+            gk, gv = eng.kv(sids[i], 11, lens[i], F)
+            ok, ov = orc.kv(11, lens[i], F)
+            assert np.abs(gk - ok).max() < TOL and np.abs(gv - ov).max() < TOL, i
+            orc.close()
     finally:
         eng.close()
 
