@@ -76,9 +76,10 @@ struct Meta {
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
+// (not volatile: a pure register operation, so the compiler may interleave independent ones)
 __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-                 "{%0,%1,%2,%3};"
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
                  : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
                  : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
@@ -135,6 +136,14 @@ __device__ __forceinline__ float gelu_erf(float v) {  // audio_layer.cpp:46
 // the tensor cores' own accumulation does not round to nearest, and a long chain of it into
 // one accumulator biases the sum toward zero (~2^-24 per step).
 enum { EPI_PLAIN = 0, EPI_GELU = 1, EPI_SCALED_ADD = 2, EPI_QKV = 3 };
+
+// RoPE frequencies exp(-ln(1e4) 2i / 64) of the 32 pairs of a head, computed on the device
+// with the expression of audio_layer.cpp:36 (k_rope_freq runs when a codec is created)
+__device__ float g_rope_freq[kHeadDim / 2];
+__global__ void k_rope_freq() {
+    const int i = threadIdx.x;
+    if (i < kHeadDim / 2) g_rope_freq[i] = expf(-logf(10000.0f) * 2.0f * (float)i / (float)kHeadDim);
+}
 constexpr int kTM = 128, kTN = 128, kTK = 32, kTS = 40;  // tile rows, tile outputs, k step, smem row (halves)
 constexpr int kStageHalves = 3 * kTM * kTS;              // x hi, x lo, W
 constexpr size_t kGemmSmem = 2 * kStageHalves * sizeof(__half);  // 61,440 bytes
@@ -150,7 +159,7 @@ struct Epi {
 };
 
 template <int EPI>
-__global__ void __launch_bounds__(256) k_gemm_mma(const __half *__restrict__ W, const float *__restrict__ x, int T,
+__global__ void __launch_bounds__(256, 2) k_gemm_mma(const __half *__restrict__ W, const float *__restrict__ x, int T,
                                                   int R, int K, Epi ep) {
     extern __shared__ __align__(16) __half gsm[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -261,9 +270,7 @@ __global__ void __launch_bounds__(256) k_gemm_mma(const __half *__restrict__ W, 
                     if (which < 2) {
                         const int b = t / ep.t_per_stream;
                         const int pos = ep.offset[b] + (t - b * ep.t_per_stream);
-                        const int i = (d & 63) >> 1;
-                        const float freq = expf(-logf(10000.0f) * 2.0f * (float)i / (float)kHeadDim);
-                        const float ang = (float)pos * freq;
+                        const float ang = (float)pos * g_rope_freq[(d & 63) >> 1];
                         const float cs = cosf(ang), sn = sinf(ang);
                         const float x0 = v0, x1 = v1;
                         v0 = x0 * cs - x1 * sn;
@@ -385,7 +392,7 @@ constexpr int kQT = 64, kKT = 64, kAS = 72;  // rows per block, keys per tile, s
 constexpr int kPlane = kKT * kAS;            // halves per plane of a tile
 constexpr size_t kAttnSmem = 2 * 4 * kPlane * sizeof(__half);  // 73,728 bytes
 
-__global__ void __launch_bounds__(128) k_window_attn(const __half *__restrict__ q16, const __half *__restrict__ kv16,
+__global__ void __launch_bounds__(128, 3) k_window_attn(const __half *__restrict__ q16, const __half *__restrict__ kv16,
                                                      int t, const __half *__restrict__ ring, int window, int layer,
                                                      Meta meta, int n_streams, float *__restrict__ out) {
     extern __shared__ __align__(16) __half asmem[];
@@ -466,39 +473,49 @@ __global__ void __launch_bounds__(128) k_window_attn(const __half *__restrict__ 
                     ldsm_x4(rh, kh + off);
                     ldsm_x4(rl, kl + off);
                     mma16816(s[nj], qh[ks], rh[0], rh[1]);
-                    mma16816(s[nj], qh[ks], rl[0], rl[1]);
-                    mma16816(s[nj], ql[ks], rh[0], rh[1]);
                     mma16816(s[nj + 1], qh[ks], rh[2], rh[3]);
+                    mma16816(s[nj], qh[ks], rl[0], rl[1]);
                     mma16816(s[nj + 1], qh[ks], rl[2], rl[3]);
+                    mma16816(s[nj], ql[ks], rh[0], rh[1]);
                     mma16816(s[nj + 1], ql[ks], rh[2], rh[3]);
                 }
-            // mask to each row's window, then the online softmax of rows ra (c = 0, 1) and rb (c = 2, 3)
-            const int alo = ra + n - window + 1, ahi = ra + n, blo = alo + 8, bhi = ahi + 8;
+            // mask to each row's window (only tiles at the window's edges, or with rows past the
+            // chunk, need it), then the online softmax of rows ra (c = 0, 1) and rb (c = 2, 3)
+            const bool inner = i0 + 15 < q0 + nq && u0 >= i0 + 15 + n - window + 1 && u0 + kKT - 1 <= i0 + n;
+            if (!inner) {
+                const int alo = ra + n - window + 1, ahi = ra + n, blo = alo + 8, bhi = ahi + 8;
+#pragma unroll
+                for (int nj = 0; nj < 8; ++nj)
+#pragma unroll
+                    for (int c = 0; c < 2; ++c) {
+                        const int u = u0 + nj * 8 + 2 * tg + c;
+                        s[nj][c] = (oka && u >= alo && u <= ahi) ? s[nj][c] : -INFINITY;
+                        s[nj][2 + c] = (okb && u >= blo && u <= bhi) ? s[nj][2 + c] : -INFINITY;
+                    }
+            }
             float xa = -INFINITY, xb = -INFINITY;
 #pragma unroll
-            for (int nj = 0; nj < 8; ++nj)
-#pragma unroll
-                for (int c = 0; c < 2; ++c) {
-                    const int u = u0 + nj * 8 + 2 * tg + c;
-                    s[nj][c] = (oka && u >= alo && u <= ahi) ? s[nj][c] : -INFINITY;
-                    s[nj][2 + c] = (okb && u >= blo && u <= bhi) ? s[nj][2 + c] : -INFINITY;
-                    xa = fmaxf(xa, s[nj][c]);
-                    xb = fmaxf(xb, s[nj][2 + c]);
-                }
+            for (int nj = 0; nj < 8; ++nj) {
+                xa = fmaxf(xa, fmaxf(s[nj][0], s[nj][1]));
+                xb = fmaxf(xb, fmaxf(s[nj][2], s[nj][3]));
+            }
 #pragma unroll
             for (int off = 1; off <= 2; off <<= 1) {
                 xa = fmaxf(xa, __shfl_xor_sync(0xffffffffu, xa, off));
                 xb = fmaxf(xb, __shfl_xor_sync(0xffffffffu, xb, off));
             }
             const float na = fmaxf(ma, xa), nb = fmaxf(mb, xb);
-            const float fa = na == -INFINITY ? 1.f : expf(ma - na), fb = nb == -INFINITY ? 1.f : expf(mb - nb);
+            // __expf: the hardware exponential (relative error ~1e-7 near 0, growing with |x| where
+            // the weights are negligible); a row with no valid key yet keeps weight 0
+            const float fa = na == -INFINITY ? 1.f : __expf(ma - na), fb = nb == -INFINITY ? 1.f : __expf(mb - nb);
+            const float ca = na == -INFINITY ? 0.f : na, cb = nb == -INFINITY ? 0.f : nb;
             float sa = 0.f, sb = 0.f;
 #pragma unroll
             for (int nj = 0; nj < 8; ++nj)
 #pragma unroll
                 for (int c = 0; c < 2; ++c) {
-                    s[nj][c] = na == -INFINITY ? 0.f : expf(s[nj][c] - na) * 1024.f;
-                    s[nj][2 + c] = nb == -INFINITY ? 0.f : expf(s[nj][2 + c] - nb) * 1024.f;
+                    s[nj][c] = __expf(s[nj][c] - ca) * 1024.f;
+                    s[nj][2 + c] = __expf(s[nj][2 + c] - cb) * 1024.f;
                     sa += s[nj][c];
                     sb += s[nj][2 + c];
                 }
@@ -527,10 +544,10 @@ __global__ void __launch_bounds__(128) k_window_attn(const __half *__restrict__ 
                     ldsm_x4_t(rh, vh + off);
                     ldsm_x4_t(rl, vl + off);
                     mma16816(ov[nd], ph, rh[0], rh[1]);
-                    mma16816(ov[nd], ph, rl[0], rl[1]);
-                    mma16816(ov[nd], pl, rh[0], rh[1]);
                     mma16816(ov[nd + 1], ph, rh[2], rh[3]);
+                    mma16816(ov[nd], ph, rl[0], rl[1]);
                     mma16816(ov[nd + 1], ph, rl[2], rl[3]);
+                    mma16816(ov[nd], pl, rh[0], rh[1]);
                     mma16816(ov[nd + 1], pl, rh[2], rh[3]);
                 }
             }
@@ -618,6 +635,9 @@ public:
         if (max_streams > 65535) throw std::runtime_error("max_streams must be at most 65535");
         if (max_batch_frames > (1 << 20)) throw std::runtime_error("max_batch_frames must be at most 1048576");
         CK(cudaSetDevice(device));
+        k_rope_freq<<<1, 32>>>();
+        CK(cudaGetLastError());
+        CK(cudaDeviceSynchronize());
         CK(cudaFuncSetAttribute(k_window_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kAttnSmem)));
         CK(cudaFuncSetAttribute(k_gemm_mma<EPI_PLAIN>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kGemmSmem)));
         CK(cudaFuncSetAttribute(k_gemm_mma<EPI_GELU>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kGemmSmem)));
