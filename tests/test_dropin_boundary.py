@@ -1,7 +1,8 @@
 """The drop-in boundary, built: the reference's own C++ layers -- TtsEngine (engine.cpp), the
-job Runtime (runtime.cpp), the moss_* C ABI (capi.cpp) and the moss_llm CLI (main.cpp) --
-compiled from the reference checkout with no source change against
-dsh-moss-tts_b200/csrc/dropin/moss/llm.h (moss::LlmModel = the GPU engine), llm.cpp left out,
+job Runtime (runtime.cpp), the moss_* C ABI (capi.cpp), the moss_llm CLI (main.cpp) and the
+moss_decoder CLI (decoder_main.cpp) -- compiled from the reference checkout with no source
+change against dsh-moss-tts_b200/csrc/dropin/moss/llm.h (moss::LlmModel = the GPU engine) and
+dropin/moss/decoder.h (moss::AudioDecoder = the GPU codec), llm.cpp and decoder.cpp left out,
 and linked to libmossgpu.so with every symbol resolved (oracle/Makefile `dropin`).
 
 CPU only: the build, the exported C ABI, the engine symbols it binds, and -- on a machine
@@ -44,10 +45,13 @@ def test_reference_layers_link_against_the_gpu_engine(built):
     # no CPU model inside: llm.cpp is not linked, the model is the engine behind mossgpu.h
     demangled = subprocess.run(["nm", "-C", str(lib)], capture_output=True, text=True).stdout
     assert "moss::LlmModel::" not in demangled
+    # no CPU codec decoder either: decoder.cpp is not linked, AudioDecoder is the GPU codec
+    assert "moss::AudioDecoder::" not in demangled
     undefined = subprocess.run(["nm", "-D", "--undefined-only", str(lib)], capture_output=True, text=True).stdout
     bound = set(re.findall(r"\bU (mossgpu_\w+)", undefined))
     declared = set(re.findall(r"\b(mossgpu_\w+)\s*\(", (ROOT / "include" / "mossgpu.h").read_text()))
     assert {"mossgpu_create", "mossgpu_prefill", "mossgpu_step", "mossgpu_stream_fork"} <= bound
+    assert {"mossgpu_codec_create", "mossgpu_codec_reset", "mossgpu_codec_decode_chunk"} <= bound
     assert bound <= declared
 
 
@@ -75,3 +79,15 @@ def test_reference_job_request_drives_the_text_runtime(built, tmp_path):
     assert r.returncode == 0, r.stderr[-4000:]
     out = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
     assert out.returncode == 0 and out.stdout.startswith("ok"), out.stdout + out.stderr
+
+
+def test_reference_codec_cli_on_the_gpu_codec_or_reports_no_device(built, decoder_file, tmp_path):
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present: tests/test_gpu_dropin_cli.py runs the codec CLI against the reference")
+    codes = tmp_path / "codes.txt"
+    codes.write_text("\n".join(" ".join(str((17 * f + 31 * i) % 1024) for i in range(16)) for f in range(3)) + "\n")
+    r = subprocess.run([str(built / "moss_decoder_gpu"), "--weights", decoder_file, "--codes", str(codes),
+                        "--out", str(tmp_path / "a.f32")], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 1
+    assert "cuda" in r.stderr.lower()  # the codec's own error, through AudioDecoder::load's err

@@ -68,3 +68,28 @@ def test_reference_cli_on_gpu_matches_reference_cli_on_cpu(weights_path, tmp_pat
         assert same >= 0.99, (dump, same)
         # the CLI's own teacher-forcing agreement count moves only with the frames that differ
         assert abs(out["teacher_match"] - cpu["teacher_match"]) <= 16 * round((1 - same) * FRAMES), dump
+
+
+CPU_DEC = ROOT / "oracle" / "_ref" / "moss_decoder"
+GPU_DEC = ROOT / "oracle" / "_ref" / "dropin" / "moss_decoder_gpu"
+
+
+@pytest.mark.skipif(not (CPU_DEC.exists() and GPU_DEC.exists()),
+                    reason="reference codec CLIs not built here (make -C oracle ref dropin)")
+@pytest.mark.parametrize("stream", [0, 8, 3])
+def test_reference_codec_cli_on_gpu_matches_reference_codec_cli_on_cpu(decoder_file, tmp_path, stream):
+    """The reference's moss_decoder CLI (decoder_main.cpp, unchanged) on the GPU codec against the
+    same CLI on the reference's CPU AudioDecoder: 40 frames of codes, whole-utterance decode
+    (--stream 0) and streaming in chunks of 8 and 3 frames; samples within 5e-4."""
+    from golden_inputs import codec_codes
+    codes = codec_codes(40, seed=77)
+    path = tmp_path / "codes.txt"
+    path.write_text("\n".join(" ".join(map(str, codes[:, f])) for f in range(codes.shape[1])) + "\n")
+    args = ["--weights", decoder_file, "--codes", path, "--stream", stream]
+    cpu = run(CPU_DEC, [*args, "--threads", min(8, os.cpu_count() or 1), "--out", tmp_path / "cpu.f32"])
+    gpu = run(GPU_DEC, [*args, "--out", tmp_path / "gpu.f32"])
+    a = np.fromfile(tmp_path / "cpu.f32", np.float32)
+    b = np.fromfile(tmp_path / "gpu.f32", np.float32)
+    assert cpu["interleaved_samples"] == gpu["interleaved_samples"] == 40 * 7680 == a.size == b.size
+    assert np.isfinite(b).all()
+    assert np.abs(a - b).max() <= 5e-4, np.abs(a - b).max()
