@@ -530,9 +530,11 @@ def run_ours(args, rank, world, local_rank, dist):
         if args.workload == "configs4" else None
     pf = run_prefill(pkg, weights, local_rank, torch, n_prompts=16, rows=256)
     pf["frac_of_bf16_peak"] = round(pf["tflops"] / pk["bf16_tflops"], 4)
-    # ---- the audio codec decoder on this rank's streams (8-frame chunks, full rings)
+    # ---- the audio codec decoder on this rank's streams (8-frame chunks, full rings), then the
+    # LLM and the codec together on this GPU
     codec = run_codec(pkg, local_rank, torch, B, min(K, 8), pk,
                       cpu_budget_s=10.0 if (rank == 0 and world == 1 and not args.no_cpu_baseline) else 0.0)
+    pipe = run_pipeline(pkg, weights, local_rank, torch, lens, K=max(2, min(K // 8, 4)))
 
     # ---- rooflines
     R = B
@@ -606,6 +608,13 @@ def run_ours(args, rank, world, local_rank, dist):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cb = cpu_throughput(weights, args.lmin, args.lmax, budget_s=15.0)
         cpu_baseline = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        if codec.get("cpu_baseline"):
+            # the reference's LLM and codec each measured on all the cores; run together they
+            # share them, so the pipeline's rate is the harmonic combination of the two
+            lv, cv = cb["value"], codec["cpu_baseline"]["value"]
+            pipe["cpu_reference_frames_per_s"] = round(1.0 / (1.0 / lv + 1.0 / cv), 2)
+            pipe["cpu_reference_note"] = ("1 / (1 / LLM + 1 / codec) of the two measured reference arms on the same "
+                                          f"{cb['cores']} cores ({lv} and {cv} frames/s)")
     else:
         cpu_baseline = None
 
@@ -629,6 +638,7 @@ def run_ours(args, rank, world, local_rank, dist):
             "configs1_frame": c1,
             "prefill": pf,
             "codec": codec,
+            "pipeline": pipe,
             "batch1_global_step": {"us": round(b1_us, 2), "kv_len": 128, "algorithmic_bytes": b1_bytes,
                                    "achieved_gbs": round(b1_bytes / (b1_us / 1e6) / 1e9, 1),
                                    "frac_of_hbm": round(b1_bytes / (b1_us / 1e6) / 1e9 / pk["hbm_gbs"], 4)},
@@ -675,6 +685,67 @@ def run_configs1_frame(pkg, weights, device, torch, rank, K, W, local_path=None)
     ms = e0.elapsed_time(e1) / K
     eng.close()
     return {"streams": 64, "kv_len": [64, 1024], "ms_per_frame": round(ms, 4), "frames_per_s_per_gpu": round(64 / ms * 1e3, 1)}
+
+
+def run_pipeline(pkg, weights, device, torch, lens, K: int, chunk: int = 8, fill_chunks: int = 16) -> dict:
+    """The LLM and the codec decoder on one GPU, as a serving loop runs them: per chunk, one
+    mossgpu_step_frames call of `chunk` frames for every stream (codes to the host), then one
+    mossgpu_codec_decode_batch_device call that turns every stream's block into samples (codes
+    back to the device, samples kept there).  The codec streams' rings are filled first, so
+    the codec runs at its long-form steady state; the LLM streams start at the workload's KV
+    lengths.  Timed: K chunks, wall clock around the host loop (both engines on one CUDA
+    stream), and the device time of the same region from CUDA events."""
+    from moss_b200 import codecfile
+    dec = codecfile.ensure_synth_decoder(Path(tempfile.gettempdir()) / "moss_b200_dec1.moss", 1)
+    B = len(lens)
+    extra = (K + 2) * chunk + 32
+    pages = sum((L + extra + kPAGE - 1) // kPAGE + 1 for L in lens) + 16
+    eng = pkg.Engine(weights, device=device, max_streams=B + 2, max_ctx=max(lens) + extra, kv_pages=pages,
+                     max_rows=max(B + 2, 256))
+    codec = pkg.Codec(dec, device, max_streams=B, max_batch_frames=B * chunk)
+    stream = torch.cuda.current_stream()
+    eng.set_cuda_stream(stream.cuda_stream)
+    codec.set_cuda_stream(stream.cuda_stream)
+    sids = [eng.open() for _ in lens]
+    csids = [codec.open() for _ in lens]
+    for i, (s, L) in enumerate(zip(sids, lens)):
+        eng.fill_state_random(s, L, seed=i)
+        eng.generate_begin(s, 0)
+    p = pkg.SampleParams.make(greedy=True, repetition_penalty=1.2, min_frames=1 << 30)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(11)
+    warm = torch.randint(0, 1024, (B, 16, chunk), dtype=torch.int32, device="cuda", generator=g)
+    pcm = torch.empty((B, chunk * codec.samples_per_frame), dtype=torch.float32, device="cuda")
+    for _ in range(fill_chunks):
+        codec.decode_batch_device(csids, warm.data_ptr(), chunk, pcm.data_ptr())
+    codes_dev = torch.empty((B, 16, chunk), dtype=torch.int32, device="cuda")
+
+    def one_chunk():
+        codes, done = eng.step_frames(sids, p, chunk)  # [chunk][B][16], host
+        codes_dev.copy_(torch.from_numpy(np.ascontiguousarray(codes.transpose(1, 2, 0))))
+        codec.decode_batch_device(csids, codes_dev.data_ptr(), chunk, pcm.data_ptr())
+        return done
+
+    one_chunk()  # warm-up: graphs captured, caches hot
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    e0.record(stream)
+    for _ in range(K):
+        done = one_chunk()
+    e1.record(stream)
+    e1.synchronize()
+    wall = time.perf_counter() - t0
+    dev_ms = e0.elapsed_time(e1)
+    assert (done == chunk).all() and codec.status() == 0
+    eng.close()
+    codec.close()
+    frames = B * chunk * K
+    return {"api": "mossgpu_step_frames (LLM, codes to the host) + mossgpu_codec_decode_batch_device (codec)",
+            "streams": B, "chunk_frames": chunk, "chunks": K,
+            "frames_per_s": round(frames / wall, 1), "device_frames_per_s": round(frames / (dev_ms / 1e3), 1),
+            "audio_seconds_per_s": round(frames * 0.08 / wall, 1),
+            "ms_per_chunk": round(1e3 * wall / K, 3)}
 
 
 # model FLOPs per prefilled row: 2 x the 84,934,656 weights of the 12 layers; causal attention
