@@ -526,15 +526,18 @@ def run_ours(args, rank, world, local_rank, dist):
 
     # ---- configs[1] frame (64 streams per GPU, KV U{64..1024}) and configs[2] prefill:
     # reported beside the headline, each in an engine of its own
-    c1 = run_configs1_frame(pkg, weights, local_rank, torch, rank, K, W, args.local_path) \
-        if args.workload == "configs4" else None
-    pf = run_prefill(pkg, weights, local_rank, torch, n_prompts=16, rows=256)
-    pf["frac_of_bf16_peak"] = round(pf["tflops"] / pk["bf16_tflops"], 4)
-    # ---- the audio codec decoder on this rank's streams (8-frame chunks, full rings), then the
-    # LLM and the codec together on this GPU
-    codec = run_codec(pkg, local_rank, torch, B, min(K, 8), pk,
-                      cpu_budget_s=10.0 if (rank == 0 and world == 1 and not args.no_cpu_baseline) else 0.0)
-    pipe = run_pipeline(pkg, weights, local_rank, torch, lens, K=max(2, min(K // 8, 4)))
+    c1 = pf = codec = pipe = None
+    if not args.frame_only:
+        c1 = run_configs1_frame(pkg, weights, local_rank, torch, rank, K, W, args.local_path) \
+            if args.workload == "configs4" else None
+        pf = run_prefill(pkg, weights, local_rank, torch, n_prompts=16, rows=256)
+        pf["frac_of_bf16_peak"] = round(pf["tflops"] / pk["bf16_tflops"], 4)
+        # ---- the audio codec decoder on this rank's streams (8-frame chunks, full rings), then
+        # the LLM and the codec together on this GPU (per-GPU figures: rank 0's streams)
+        codec = run_codec(pkg, local_rank, torch, B, min(K, 8), pk,
+                          cpu_budget_s=10.0 if (rank == 0 and world == 1 and not args.no_cpu_baseline) else 0.0)
+        pipe = run_pipeline(pkg, weights, local_rank, torch, lens, K=max(2, min(K // 8, 4)))
+        codec["scope"] = pipe["scope"] = "one GPU (rank 0's streams)"
 
     # ---- rooflines
     R = B
@@ -569,8 +572,10 @@ def run_ours(args, rank, world, local_rank, dist):
             if k in flops:
                 r_["achieved_tflops"] = round(flops[k] / (us / 1e6) / 1e12, 2)
             rooflines[k] = r_
-    direct = args.tc_direct_min if args.tc_direct_min is not None else 1024  # the engine's default
-    gemm_fn = "k_gemm_tp" if (direct > 0 and R >= direct) else ("k_gemm_tc" if R > 8 else "k_gemv")
+    direct = args.tc_direct_min if args.tc_direct_min is not None else 256  # the engine's default
+    # from `direct` rows on, launch_tc picks the form per matrix (k_gemm_tp tiles or k_gemm_tc
+    # split-K): the GEMM classes are then reported as one function name covering both
+    gemm_fn = "k_gemm_tp|k_gemm_tc" if (direct > 0 and R >= direct) else ("k_gemm_tc" if R > 8 else "k_gemv")
     attn_fn = "k_attn_decode" if R > 96 else "k_attn_rows"
     fn_of = {**{k: gemm_fn for k in gemm}, "attn_decode_paged": attn_fn}
     fns = {}
@@ -608,7 +613,7 @@ def run_ours(args, rank, world, local_rank, dist):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cb = cpu_throughput(weights, args.lmin, args.lmax, budget_s=15.0)
         cpu_baseline = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
-        if codec.get("cpu_baseline"):
+        if codec and codec.get("cpu_baseline"):
             # the reference's LLM and codec each measured on all the cores; run together they
             # share them, so the pipeline's rate is the harmonic combination of the two
             lv, cv = cb["value"], codec["cpu_baseline"]["value"]
@@ -868,6 +873,8 @@ def main():
                     help="local decoder: 0 = fused cluster kernel for greedy frames, 1 = per-step kernels "
                          "(mossgpu_set_local_path; default: the engine's)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--frame-only", action="store_true",
+                    help="the headline frame only: skip the configs1, prefill, codec and pipeline legs (sweeps)")
     ap.add_argument("--sweep", action="store_true",
                     help="configs[4] sustained: every stream runs --sweep-frames frames (400), per-frame latency")
     ap.add_argument("--sweep-frames", type=int, default=400)

@@ -261,7 +261,7 @@ class Engine:
         s, m, st, flat = self._batch(sids, x, starts, m, HIDDEN, np.float32)
         self._check(self.lib.mossgpu_prefill_embeds_batch(self.h, len(s), s, m, st, flat))
 
-    def set_tc_policy(self, direct_min_rows: int = 512, direct_rows: int = 0):
+    def set_tc_policy(self, direct_min_rows: int = 256, direct_rows: int = 0):
         self._check(self.lib.mossgpu_set_tc_policy(self.h, direct_min_rows, direct_rows))
 
     def generate_begin(self, sid: int, seed: int = 0):

@@ -540,10 +540,12 @@ namespace {
 // weight tiles x slices of <= direct_ns rows (x K parts), every K chunk of a part in one CTA.
 // direct_ns = 0 sizes the slices by the batch: 256 rows from 1024 rows on (prefill passes);
 // below that the smallest of 64 / 128 / 256 rows whose tiles fit one wave of the SMs, and the
-// split-K form when even 64-row slices leave fewer than 72 tiles and the output is not stored
-// in K parts (a 768-row matrix with a residual epilogue, the audio heads).  Measured per GEMM on a 512-stream frame (one B200, ms per frame,
-// split-K / 128-row / 64-row slices): global QKV 0.35 / 0.20 / 0.18, fc_in 0.55 / 0.26 / 0.35,
-// local fc_out 0.51 / 0.81 / 0.78, audio heads 0.21 / 0.27 / 0.24.
+// split-K form when even 64-row slices leave fewer than 96 tiles and the output is not stored
+// in K parts (a 768-row matrix with a residual epilogue, the audio heads; QKV below 384 rows).
+// Measured per GEMM on a 512-stream frame (one B200, ms per frame, split-K / 128-row / 64-row
+// slices): global QKV 0.35 / 0.20 / 0.18, fc_in 0.55 / 0.26 / 0.35, local fc_out 0.51 / 0.81 /
+// 0.78, audio heads 0.21 / 0.27 / 0.24; at 256 rows (split-K / 64-row): fc_in 0.39 / 0.29,
+// local QKV 0.26 / 0.36.
 template <int EPI>
 void launch_tc(TcArgs a, int prec, cudaStream_t st, bool pdl, int direct_min, int direct_ns) {
     const int tiles = a.rows / kTcM, nchunks = a.K / kTcK;
@@ -560,7 +562,7 @@ void launch_tc(TcArgs a, int prec, cudaStream_t st, bool pdl, int direct_min, in
             if (tiles * ((a.N + ns - 1) / ns) * ks <= kNumSMs) break;
         }
         // a STORE in K parts stays direct: its consumer adds the parts, split-K writes one
-        if (ks == 1 && tiles * ((a.N + 63) / 64) < 72) direct = false;
+        if (ks == 1 && tiles * ((a.N + 63) / 64) < 96) direct = false;
     }
     if (direct) {
         while (a.N % ns) ns -= 16;

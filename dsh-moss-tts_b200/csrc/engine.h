@@ -173,7 +173,7 @@ private:
 
     int device_ = 0;
     int max_streams_ = 0, max_ctx_ = 0, pages_per_stream_ = 0, n_pages_ = 0, r_max_ = 0;
-    int tc_direct_min_rows_ = 512, tc_direct_rows_ = 0;  // 0: slice rows by batch size
+    int tc_direct_min_rows_ = 256, tc_direct_rows_ = 0;  // 0: slice rows by batch size
     // flash-prefill tiles of the current pass (int4 each) on the device, with a pinned staging
     // copy; active while a prefill pass runs on the tensor-core path
     int4 *pf_items_ = nullptr;

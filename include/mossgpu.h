@@ -171,10 +171,11 @@ int mossgpu_set_gemm_path(mossgpu_engine *e, int mode);
 /* Tensor-core GEMM form by batch size: batches of at least direct_min_rows padded rows run
  * one CTA per (128 weight rows, slice of direct_rows batch rows) over the whole K with the
  * accumulators read straight from tensor memory; smaller batches split K over thread-block
- * clusters.  direct_min_rows = 0 disables the direct form; direct_rows = 0 takes 128-row
- * slices below 1024 rows and 256-row slices from there on.  Default (512, 0), measured on one
- * B200 on a 512-stream decode frame: 10.18 ms per frame against 10.70 with split-K, 10.24 with
- * 64-row and 11.54 with 256-row slices; at 256 streams and fewer split-K is faster. */
+ * clusters.  direct_min_rows = 0 disables the direct form; direct_rows = 0 sizes the slices
+ * per matrix (the fewest rows whose tiles fit one wave of the SMs; split-K for a matrix with
+ * too few tiles) below 1024 rows and takes 256-row slices from there on.  Default (256, 0),
+ * measured on one B200: 9.75 ms per 512-stream decode frame against 10.70 with split-K
+ * throughout; 5.80 against 5.87 ms at 256 streams; at 128 streams split-K is faster. */
 int mossgpu_set_tc_policy(mossgpu_engine *e, int direct_min_rows, int direct_rows);
 
 /* Fault injection for testing the bounded-wait error path: while enabled, the first global
