@@ -536,7 +536,7 @@ def run_ours(args, rank, world, local_rank, dist):
         # the LLM and the codec together on this GPU (per-GPU figures: rank 0's streams)
         codec = run_codec(pkg, local_rank, torch, B, min(K, 8), pk,
                           cpu_budget_s=10.0 if (rank == 0 and world == 1 and not args.no_cpu_baseline) else 0.0)
-        pipe = run_pipeline(pkg, weights, local_rank, torch, lens, K=max(2, min(K // 8, 4)))
+        pipe = run_pipeline(pkg, weights, local_rank, torch, lens, K=max(2, min(K // 8, 4)), overlap=False)
         codec["scope"] = pipe["scope"] = "one GPU (rank 0's streams)"
 
     # ---- rooflines
@@ -692,14 +692,17 @@ def run_configs1_frame(pkg, weights, device, torch, rank, K, W, local_path=None)
     return {"streams": 64, "kv_len": [64, 1024], "ms_per_frame": round(ms, 4), "frames_per_s_per_gpu": round(64 / ms * 1e3, 1)}
 
 
-def run_pipeline(pkg, weights, device, torch, lens, K: int, chunk: int = 8, fill_chunks: int = 16) -> dict:
+def run_pipeline(pkg, weights, device, torch, lens, K: int, chunk: int = 8, fill_chunks: int = 16,
+                 overlap: bool = False) -> dict:
     """The LLM and the codec decoder on one GPU, as a serving loop runs them: per chunk, one
-    mossgpu_step_frames call of `chunk` frames for every stream (codes to the host), then one
+    mossgpu_step_frames call of `chunk` frames for every stream (codes to the host), and one
     mossgpu_codec_decode_batch_device call that turns every stream's block into samples (codes
-    back to the device, samples kept there).  The codec streams' rings are filled first, so
-    the codec runs at its long-form steady state; the LLM streams start at the workload's KV
-    lengths.  Timed: K chunks, wall clock around the host loop (both engines on one CUDA
-    stream), and the device time of the same region from CUDA events."""
+    back to the device, samples kept there).  overlap: the codec runs on a second CUDA stream,
+    so chunk k's decode overlaps chunk k+1's LLM frames (the host enqueues the decode, then
+    steps the LLM); otherwise both run in turn on one stream.  The codec streams' rings are
+    filled first, so the codec runs at its long-form steady state; the LLM streams start at the
+    workload's KV lengths.  Timed: K chunks, wall clock around the host loop until both
+    streams are idle."""
     from moss_b200 import codecfile
     dec = codecfile.ensure_synth_decoder(Path(tempfile.gettempdir()) / "moss_b200_dec1.moss", 1)
     B = len(lens)
@@ -709,8 +712,9 @@ def run_pipeline(pkg, weights, device, torch, lens, K: int, chunk: int = 8, fill
                      max_rows=max(B + 2, 256))
     codec = pkg.Codec(dec, device, max_streams=B, max_batch_frames=B * chunk)
     stream = torch.cuda.current_stream()
+    cstream = torch.cuda.Stream() if overlap else stream
     eng.set_cuda_stream(stream.cuda_stream)
-    codec.set_cuda_stream(stream.cuda_stream)
+    codec.set_cuda_stream(cstream.cuda_stream)
     sids = [eng.open() for _ in lens]
     csids = [codec.open() for _ in lens]
     for i, (s, L) in enumerate(zip(sids, lens)):
@@ -723,33 +727,37 @@ def run_pipeline(pkg, weights, device, torch, lens, K: int, chunk: int = 8, fill
     pcm = torch.empty((B, chunk * codec.samples_per_frame), dtype=torch.float32, device="cuda")
     for _ in range(fill_chunks):
         codec.decode_batch_device(csids, warm.data_ptr(), chunk, pcm.data_ptr())
-    codes_dev = torch.empty((B, 16, chunk), dtype=torch.int32, device="cuda")
+    # two code buffers: chunk k's block is read by the decode on the codec's stream, chunk k+1's
+    # is written after it in the same stream's order
+    codes_dev = [torch.empty((B, 16, chunk), dtype=torch.int32, device="cuda") for _ in range(2)]
 
-    def one_chunk():
-        codes, done = eng.step_frames(sids, p, chunk)  # [chunk][B][16], host
-        codes_dev.copy_(torch.from_numpy(np.ascontiguousarray(codes.transpose(1, 2, 0))))
-        codec.decode_batch_device(csids, codes_dev.data_ptr(), chunk, pcm.data_ptr())
-        return done
+    def llm_chunk(k):  # frames of chunk k -> codes_dev[k % 2] (on the codec's stream)
+        codes, done = eng.step_frames(sids, p, chunk)  # [chunk][B][16], host; syncs the LLM stream
+        assert (done == chunk).all()
+        with torch.cuda.stream(cstream):
+            codes_dev[k % 2].copy_(torch.from_numpy(np.ascontiguousarray(codes.transpose(1, 2, 0))))
 
-    one_chunk()  # warm-up: graphs captured, caches hot
+    def codec_chunk(k):  # enqueued only: runs on the codec's stream
+        codec.decode_batch_device(csids, codes_dev[k % 2].data_ptr(), chunk, pcm.data_ptr())
+
+    llm_chunk(0)  # warm-up: graphs captured, caches hot
+    codec_chunk(0)
     torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0 = time.perf_counter()
-    e0.record(stream)
-    for _ in range(K):
-        done = one_chunk()
-    e1.record(stream)
-    e1.synchronize()
+    llm_chunk(1)
+    for k in range(1, K + 1):
+        codec_chunk(k)  # chunk k's samples ...
+        if k < K:
+            llm_chunk(k + 1)  # ... while chunk k+1's frames run on the LLM's stream
+    torch.cuda.synchronize()
     wall = time.perf_counter() - t0
-    dev_ms = e0.elapsed_time(e1)
-    assert (done == chunk).all() and codec.status() == 0
+    assert codec.status() == 0
     eng.close()
     codec.close()
     frames = B * chunk * K
     return {"api": "mossgpu_step_frames (LLM, codes to the host) + mossgpu_codec_decode_batch_device (codec)",
-            "streams": B, "chunk_frames": chunk, "chunks": K,
-            "frames_per_s": round(frames / wall, 1), "device_frames_per_s": round(frames / (dev_ms / 1e3), 1),
-            "audio_seconds_per_s": round(frames * 0.08 / wall, 1),
+            "streams": B, "chunk_frames": chunk, "chunks": K, "overlap": overlap,
+            "frames_per_s": round(frames / wall, 1), "audio_seconds_per_s": round(frames * 0.08 / wall, 1),
             "ms_per_chunk": round(1e3 * wall / K, 3)}
 
 
