@@ -10,7 +10,12 @@
 // seed, greedy, rep_x1000, min_frames, max_frames, chunk_frames, use_prefix, m, rows [m][17].
 // out.txt: per job "job <i> <state> <frames> <shard>", then one "blk <segment> <n> <16 n codes>" line
 // per block.  Exit 0 when every job ended (in any state), 2 on a load or input error.
+//
+// With MOSS_DEMO_DECODER=<decoder .moss> in the environment (one GPU), every job's sink also
+// decodes its blocks through its own stream of one GPU codec (CodecStreams, codec_gpu.h), and
+// each job's samples go to <out.txt>.pcm<i> (float32, interleaved stereo).
 #include "batch_runtime.h"
+#include "codec_gpu.h"
 
 #include <cstdio>
 #include <cstdlib>
@@ -118,12 +123,29 @@ int main(int argc, char **argv) {
         std::vector<std::vector<std::string>> blocks(jobs.size());
         std::vector<std::string> ids(jobs.size());
         std::vector<int> shard(jobs.size(), 0);
+        const char *dec_path = std::getenv("MOSS_DEMO_DECODER");
+        std::unique_ptr<CodecStreams> codec;
+        std::vector<std::unique_ptr<CodecStreams::Stream>> dec(jobs.size());
+        std::vector<std::vector<float>> pcm(jobs.size());
+        if (dec_path && *dec_path && n_gpus == 1) {
+            codec = std::make_unique<CodecStreams>(dec_path, 0, static_cast<int>(jobs.size()), 16);
+            for (auto &d : dec) d = codec->open();
+        }
         for (size_t i = 0; i < jobs.size(); ++i) {
             std::string e;
-            auto sink = [&blocks, i](int segment, const int32_t *codes, int n) {
+            auto sink = [&blocks, &dec, &pcm, i](int segment, const int32_t *codes, int n) {
                 std::string line = "blk " + std::to_string(segment) + " " + std::to_string(n);
                 for (int k = 0; k < 16 * n; ++k) line += " " + std::to_string(codes[k]);
                 blocks[i].push_back(line);
+                if (dec[i]) {  // the job's codec stream, in block order (engine.cpp:480-502)
+                    std::vector<float> audio;
+                    std::string why;
+                    if (!dec[i]->decode(segment, codes, n, &audio, &why)) {
+                        std::fprintf(stderr, "decode %zu: %s\n", i, why.c_str());
+                        return false;
+                    }
+                    pcm[i].insert(pcm[i].end(), audio.begin(), audio.end());
+                }
                 return true;
             };
             const bool ok = single ? single->submit(jobs[i], sink, &ids[i], &e)
@@ -154,6 +176,10 @@ int main(int argc, char **argv) {
             single->shutdown();
         else
             sharded->shutdown();
+        for (size_t i = 0; i < jobs.size() && codec; ++i) {
+            std::ofstream f(std::string(argv[3]) + ".pcm" + std::to_string(i), std::ios::binary);
+            f.write(reinterpret_cast<const char *>(pcm[i].data()), static_cast<std::streamsize>(pcm[i].size() * 4));
+        }
     }
     for (auto *h : hs) mossgpu_destroy(h);
     return rc;

@@ -10,6 +10,7 @@ through the C ABI (tests/cpp/batch_runtime_demo.cpp), against the same engine ca
 directly through the Python API in the order the runtime makes them."""
 from __future__ import annotations
 
+import os
 import subprocess
 from pathlib import Path
 
@@ -229,3 +230,38 @@ def test_sharded_runtime_on_two_gpus_matches_direct_calls(tmp_path, weights_path
         if n:
             frames = np.concatenate([c.T for _, c in got[i]["blocks"]], axis=0)
             assert (frames == want[i]).all(), i
+
+
+@pytest.mark.gpu
+def test_batch_runtime_with_gpu_codec_streams(tmp_path, weights_path, decoder_file):
+    """The runtime's frames through the GPU codec (CodecStreams: one codec stream per job, fed
+    each block in order on the worker thread) give the samples that decoding each job's blocks
+    directly with mossgpu_codec_decode_chunk gives -- bit for bit, the same kernels."""
+    import moss_b200 as pkg
+    pkg.build()
+    exe = tmp_path / "batch_runtime_demo"
+    subprocess.run([*CXX, str(ROOT / "tests" / "cpp" / "batch_runtime_demo.cpp"), "-L", str(PKG), "-lmossgpu",
+                    f"-Wl,-rpath,{PKG}", "-o", str(exe)], check=True, capture_output=True, text=True)
+    prefix = prompt_rows(PREFIX_M, seed=70)
+    rows = [prompt_rows(job[7], seed=80 + i) for i, job in enumerate(JOBS)]
+    write_jobs(tmp_path / "jobs.bin", prefix, rows)
+    out = tmp_path / "out.txt"
+    r = subprocess.run([str(exe), weights_path, str(tmp_path / "jobs.bin"), str(out), "8", str(FRAMES_PER_CALL)],
+                       capture_output=True, text=True, timeout=600, env={**os.environ, "MOSS_DEMO_DECODER": decoder_file})
+    assert r.returncode == 0, r.stderr
+    got = parse_output(out.read_text())
+    codec = pkg.Codec(decoder_file, device=0, max_streams=1, max_batch_frames=16)
+    try:
+        sid = codec.open()
+        checked = 0
+        for i in sorted(got):
+            pcm = np.fromfile(f"{out}.pcm{i}", np.float32)
+            codec.reset(sid)
+            want = [codec.decode_chunk(sid, c) for _, c in got[i]["blocks"]]
+            want = np.concatenate(want) if want else np.zeros(0, np.float32)
+            assert pcm.size == sum(c.shape[1] for _, c in got[i]["blocks"]) * 7680
+            assert np.array_equal(pcm, want), i
+            checked += pcm.size > 0
+        assert checked > 0
+    finally:
+        codec.close()
