@@ -647,7 +647,7 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
         a.ldo = kQKV;
         launch_tc<TC_STORE>(a, prec, stream_, pdl_, tc_direct_min_rows_, tc_direct_rows_);
         mark(KK_QKV_G);
-        launch_k(pdl_, k_qkv_rope, dim3(unsigned((size_t(R) * (kQKV / 2) + 255) / 256)), dim3(256), 0, stream_, mlp_, R,
+        launch_k(pdl_, k_qkv_rope, dim3(unsigned(R)), dim3(kQkvRopeThreads), 0, stream_, mlp_, R,
                  row_slot, row_pos, rope_, q_, a.kv, page_table_, pages_per_stream_);
         mark(KK_QKV_ROPE);
     } else {
@@ -1169,12 +1169,21 @@ void Engine::prefill_batch(int n, const int32_t *sids, const int32_t *m_in, cons
             throw;
         }
         pf_active_ = false;
-        // ln_f of each stream's last row in this pass becomes its hidden state (llm.cpp:395-399)
+        // ln_f of each stream's last row in this pass becomes its hidden state (llm.cpp:395-399),
+        // all of them in one launch; the (row, slot) pairs go into rows17_, which the pass has
+        // consumed (k_embed_rows ran before the layers on this stream)
+        std::vector<int> pick;  // [rows of the pass..., their slots...]
         for (int k = 0; k < R; ++k) {
             const auto &fr = flat[c0 + size_t(k)];
-            if (fr.second != m[size_t(fr.first)] - 1) continue;
-            launch_k(pdl_, k_layernorm_rows, dim3(1), dim3(256), 0, stream_, x_ + size_t(k) * kHidden, 1, lnf_w_, lnf_b_,
-                     hidden_ + size_t(sid[size_t(fr.first)]) * kHidden, nullptr, nullptr);
+            if (fr.second == m[size_t(fr.first)] - 1) pick.push_back(k);
+        }
+        const int np = static_cast<int>(pick.size());
+        if (np > 0) {
+            for (int i = 0; i < np; ++i) pick.push_back(sid[size_t(flat[c0 + size_t(pick[size_t(i)])].first)]);
+            CK(cudaMemcpyAsync(rows17_, pick.data(), pick.size() * sizeof(int), cudaMemcpyHostToDevice, stream_));
+            launch_k(pdl_, k_layernorm_pick, dim3(np), dim3(256), 0, stream_, static_cast<const float *>(x_),
+                     static_cast<const int *>(rows17_), static_cast<const int *>(rows17_ + np), np, lnf_w_, lnf_b_,
+                     hidden_);
         }
         CK(cudaGetLastError());
         CK(cudaMemcpyAsync(h_err_, dev_err_, sizeof(int), cudaMemcpyDeviceToHost, stream_));

@@ -958,34 +958,47 @@ __global__ void __launch_bounds__(256) k_build_bimg(float *__restrict__ x, int l
 
 // The QKV epilogue of a prefill pass as its own pass over the GEMM's stored output (bias
 // included): raw [R][2304] -> RoPE on (2i, 2i + 1) pairs of q and k, q to q_out [R][768], k
-// and v appended to the paged fp16 KV -- the same arithmetic as the fused epilogue.  One
-// thread per column pair.
-__global__ void __launch_bounds__(256) k_qkv_rope(const float *__restrict__ raw, int R, const int *__restrict__ row_slot,
-                                                  const int *__restrict__ row_pos, const float2 *__restrict__ rope,
-                                                  float *__restrict__ q_out, __half *__restrict__ kv,
-                                                  const int *__restrict__ page_table, int pages_per_stream) {
+// and v appended to the paged fp16 KV -- the same arithmetic as the fused epilogue.  One block
+// per row (its position, RoPE row and KV page looked up once), one thread per 4 columns.
+constexpr int kQkvRopeThreads = 192;
+__global__ void __launch_bounds__(kQkvRopeThreads) k_qkv_rope(const float *__restrict__ raw, int R,
+                                                              const int *__restrict__ row_slot,
+                                                              const int *__restrict__ row_pos,
+                                                              const float2 *__restrict__ rope, float *__restrict__ q_out,
+                                                              __half *__restrict__ kv, const int *__restrict__ page_table,
+                                                              int pages_per_stream) {
     pdl_enter();
-    constexpr int kPairs = kQKV / 2;
-    const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (t >= (long long)R * kPairs) return;
-    const int rr = (int)(t / kPairs), gm = 2 * (int)(t % kPairs);
-    const float2 y = *reinterpret_cast<const float2 *>(raw + (size_t)rr * kQKV + gm);
+    const int rr = blockIdx.x;
+    if (rr >= R) return;
     const int pos = row_pos[rr];
-    float o0 = y.x, o1 = y.y;
-    if (gm < 2 * kHidden) {
-        const float2 cs = rope[(size_t)pos * (kHeadDim / 2) + ((gm % kHeadDim) >> 1)];
-        o0 = __fsub_rn(__fmul_rn(y.x, cs.x), __fmul_rn(y.y, cs.y));
-        o1 = __fadd_rn(__fmul_rn(y.y, cs.x), __fmul_rn(y.x, cs.y));
-    }
-    if (gm < kHidden) {
-        *reinterpret_cast<float2 *>(q_out + (size_t)rr * kHidden + gm) = make_float2(o0, o1);
-    } else {
-        const int kvsel = gm < 2 * kHidden ? 0 : 1;
-        const int c = gm - kHidden * (1 + kvsel);
-        const int page = page_table[(size_t)row_slot[rr] * pages_per_stream + pos / kPage];
-        __half *dst = kv + (size_t)page * kPageHalfs + ((kvsel * kHeads + c / kHeadDim) * kPage + pos % kPage) * kHeadDim +
-                      (c % kHeadDim);
-        *reinterpret_cast<__half2 *>(dst) = __floats2half2_rn(o0, o1);
+    const int page = page_table[(size_t)row_slot[rr] * pages_per_stream + pos / kPage];
+    const float2 *rp = rope + (size_t)pos * (kHeadDim / 2);
+    for (int q4 = threadIdx.x; q4 < kQKV / 4; q4 += kQkvRopeThreads) {
+        const int gm = 4 * q4;
+        const float4 y = *reinterpret_cast<const float4 *>(raw + (size_t)rr * kQKV + gm);
+        float o[4] = {y.x, y.y, y.z, y.w};
+        if (gm < 2 * kHidden) {
+#pragma unroll
+            for (int p = 0; p < 2; ++p) {
+                const float2 cs = rp[((gm + 2 * p) % kHeadDim) >> 1];
+                const float y0 = o[2 * p], y1 = o[2 * p + 1];
+                o[2 * p] = __fsub_rn(__fmul_rn(y0, cs.x), __fmul_rn(y1, cs.y));
+                o[2 * p + 1] = __fadd_rn(__fmul_rn(y1, cs.x), __fmul_rn(y0, cs.y));
+            }
+        }
+        if (gm < kHidden) {
+            *reinterpret_cast<float4 *>(q_out + (size_t)rr * kHidden + gm) = make_float4(o[0], o[1], o[2], o[3]);
+        } else {
+            const int kvsel = gm < 2 * kHidden ? 0 : 1;
+            const int c = gm - kHidden * (1 + kvsel);  // 4 columns of one head
+            __half *dst = kv + (size_t)page * kPageHalfs +
+                          ((kvsel * kHeads + c / kHeadDim) * kPage + pos % kPage) * kHeadDim + (c % kHeadDim);
+            const __half2 h01 = __floats2half2_rn(o[0], o[1]), h23 = __floats2half2_rn(o[2], o[3]);
+            uint2 w;
+            w.x = *reinterpret_cast<const uint32_t *>(&h01);
+            w.y = *reinterpret_cast<const uint32_t *>(&h23);
+            *reinterpret_cast<uint2 *>(dst) = w;
+        }
     }
 }
 

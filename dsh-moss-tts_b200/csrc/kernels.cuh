@@ -1039,6 +1039,22 @@ __global__ void k_layernorm_rows(const float *__restrict__ x, int R, const float
     for (int c = threadIdx.x; c < kHidden; c += blockDim.x) out[(size_t)dst * kHidden + c] = xs[c];
 }
 
+// out[dst[i]] = LayerNorm(x[src[i]]) for i < n: the ln_f of the rows that end their streams
+// in a prefill pass, in one launch (llm.cpp:395-399)
+__global__ void k_layernorm_pick(const float *__restrict__ x, const int *__restrict__ src, const int *__restrict__ dst,
+                                 int n, const float *__restrict__ w, const float *__restrict__ b, float *__restrict__ out) {
+    __shared__ float xs[kHidden];
+    pdl_enter();
+    const int i = blockIdx.x;
+    if (i >= n) return;
+    const float *row = x + (size_t)src[i] * kHidden;
+    for (int c = threadIdx.x; c < kHidden; c += blockDim.x) xs[c] = row[c];
+    __syncthreads();
+    if (threadIdx.x < 32) warp_layernorm(xs, w, b);
+    __syncthreads();
+    for (int c = threadIdx.x; c < kHidden; c += blockDim.x) out[(size_t)dst[i] * kHidden + c] = xs[c];
+}
+
 // gather rows: dst[r] = src[index[r]]
 __global__ void k_gather_rows(const float *__restrict__ src, const int *__restrict__ index, int R, float *__restrict__ dst) {
     pdl_enter();
