@@ -566,6 +566,11 @@ void launch_tc(TcArgs a, int prec, cudaStream_t st, bool pdl, int direct_min, in
     }
     if (direct) {
         while (a.N % ns) ns -= 16;
+        // the per-matrix choice keeps slices of >= 64 rows (a padded batch that 64 does not
+        // divide, such as 304 rows, takes split-K); an explicit direct_ns is taken as given
+        if (direct_ns == 0 && a.N < 1024 && ns < 64) direct = false;
+    }
+    if (direct) {
         a.nsub = ns;
         a.csize = 1;
         // tile-persistent: at most one CTA per SM walks the (weight tile, slice) tiles; slices

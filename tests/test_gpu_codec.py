@@ -83,6 +83,26 @@ def test_whole_decode_longer_than_one_call(pkg, decoder_file, golden):
         codec.close()
 
 
+def test_one_call_longer_than_every_window(pkg, decoder_file):
+    """decode() of 200 frames in one call: 800 rows at stage 0 against its 500-row window and
+    6,400 rows at stage 3 against 1,600, so rows of the chunk see only the chunk's own last
+    window of keys and only the last `context` rows of a chunk reach the ring.  Against the
+    reference's decode() of the same utterance, and the next chunk against its decode_chunk."""
+    codes = codec_codes(200, seed=31)
+    nxt = codec_codes(8, seed=32)
+    codec = pkg.Codec(decoder_file, device=0, max_streams=1, max_batch_frames=200)
+    ref = checker(decoder_file)
+    try:
+        close_enough(codec.decode(codes)[::7], ref.decode(codes)[::7])
+        sid = codec.open()
+        codec.decode_chunk(sid, codes)  # the same 200 frames as one streaming chunk, then 8 more
+        ref.reset()
+        ref.decode_chunk(codes)
+        close_enough(codec.decode_chunk(sid, nxt), ref.decode_chunk(nxt))
+    finally:
+        codec.close()
+
+
 def test_batched_streams_with_different_histories(pkg, decoder_file):
     """Seven streams with 0..6 earlier chunks of different lengths (ring fill and RoPE offsets
     differ per stream) decode one 8-frame chunk in one batched call, in a scrambled stream
