@@ -122,19 +122,27 @@ __device__ __forceinline__ float gelu_erf(float v) {  // audio_layer.cpp:46
     return 0.5f * v * (1.0f + erff(v * 0.7071067811865476f));
 }
 
-// y[t][r] = sum_k W[r][k] x[t][k] (W fp16 [R][K], x fp32 [T][K]), then the epilogue:
-//   EPI_PLAIN       y = acc (+ vec[r] when vec is given)
-//   EPI_GELU        y = gelu(acc)
-//   EPI_SCALED_ADD  y = y + vec[r] * acc (the layer-scale residual, decoder.cpp:173-177)
+// Activation planes: an fp32 activation x [T][K] that a GEMM consumes is kept as two fp16
+// planes, hi = fp16(x) and lo = fp16(x - hi) (~22 significant bits), written by the kernel that
+// produces x (k_front, k_patch, k_layernorm256, k_window_attn, the GELU epilogue, k_split_rows),
+// which also flags a value that fp16 cannot hold.  The GEMMs then only copy and multiply.
+struct Planes {
+    __half *hi = nullptr, *lo = nullptr;
+};
+
+// y[t][r] = sum_k W[r][k] (xh[t][k] + xl[t][k]) (W fp16 [R][K], x as planes [T][K]), then:
+//   EPI_PLAIN       y = acc (+ vec[r] when vec is given), fp32
+//   EPI_GELU        gelu(acc) as hi/lo planes (the next GEMM's input)
+//   EPI_SCALED_ADD  y = y + vec[r] * acc (the layer-scale residual, decoder.cpp:173-177), fp32
 //   EPI_QKV         r < 256: q, 256..511: k, 512..767: v of the row; RoPE on q and k at the
 //                   row's position (audio_layer.cpp:31-44: frequency exp(-ln(1e4) 2i / 64) of
 //                   pair (2i, 2i+1) in each 64-wide head), then q / 8 -> q16 planes and k, v ->
 //                   kv16 planes as fp16 hi/lo (an accumulator pair is a RoPE pair)
-// Block tile 128 rows x 128 outputs, k step 32, two stages (x converted to hi/lo on its way to
-// shared memory, W by cp.async); 8 warps as 2 x 4, each 64 rows x 32 outputs.  Each k16 step
-// starts its two products from zero and is added to the fp32 accumulators with a rounded add:
-// the tensor cores' own accumulation does not round to nearest, and a long chain of it into
-// one accumulator biases the sum toward zero (~2^-24 per step).
+// Block tile 128 rows x 128 outputs, k step 32, three stages of cp.async copies (x hi, x lo,
+// W); 8 warps as 2 x 4, each 64 rows x 32 outputs.  Each k16 step starts its two products from
+// zero and is added to the fp32 accumulators with a rounded add: the tensor cores' own
+// accumulation does not round to nearest, and a long chain of it into one accumulator biases
+// the sum toward zero (~2^-24 per step).
 enum { EPI_PLAIN = 0, EPI_GELU = 1, EPI_SCALED_ADD = 2, EPI_QKV = 3 };
 
 // RoPE frequencies exp(-ln(1e4) 2i / 64) of the 32 pairs of a head, computed on the device
@@ -145,12 +153,14 @@ __global__ void k_rope_freq() {
     if (i < kHeadDim / 2) g_rope_freq[i] = expf(-logf(10000.0f) * 2.0f * (float)i / (float)kHeadDim);
 }
 constexpr int kTM = 128, kTN = 128, kTK = 32, kTS = 40;  // tile rows, tile outputs, k step, smem row (halves)
-constexpr int kStageHalves = 3 * kTM * kTS;              // x hi, x lo, W
-constexpr size_t kGemmSmem = 2 * kStageHalves * sizeof(__half);  // 61,440 bytes
+constexpr int kGemmStages = 3;
+constexpr int kStageHalves = 3 * kTM * kTS;  // x hi, x lo, W
+constexpr size_t kGemmSmem = kGemmStages * kStageHalves * sizeof(__half);  // 92,160 bytes
 
 struct Epi {
     const float *vec = nullptr;    // bias (PLAIN) or layer scale (SCALED_ADD)
-    float *y = nullptr;            // [T][R] (PLAIN, GELU, SCALED_ADD)
+    float *y = nullptr;            // [T][R] (PLAIN, SCALED_ADD)
+    Planes out;                    // GELU: [T][R] hi, lo
     __half *q16 = nullptr;         // QKV: [T][2][256] hi, lo of q / 8
     __half *kv16 = nullptr;        // QKV: [T][4][256] hi, lo of k; hi, lo of v
     const int *offset = nullptr;   // QKV: RoPE position of each stream's first chunk row
@@ -159,45 +169,28 @@ struct Epi {
 };
 
 template <int EPI>
-__global__ void __launch_bounds__(256, 2) k_gemm_mma(const __half *__restrict__ W, const float *__restrict__ x, int T,
-                                                  int R, int K, Epi ep) {
+__global__ void __launch_bounds__(256, 2) k_gemm_mma(const __half *__restrict__ W, const __half *__restrict__ xh,
+                                                  const __half *__restrict__ xl, int T, int R, int K, Epi ep) {
     extern __shared__ __align__(16) __half gsm[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int wm = warp >> 2, wn = warp & 3, g = lane >> 2, tg = lane & 3;
     const int t0 = blockIdx.y * kTM, r0 = blockIdx.x * kTN;
-    const int ar = tid >> 3, ak = (tid & 7) * 4;  // x loader: rows ar + 32 j, k ak..ak+3
-    const int br = tid >> 2, bk = (tid & 3) * 8;  // W loader: rows br + 64 j, k bk..bk+7
-    float4 pa[4];
-    auto load_a = [&](int k0) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int t = t0 + ar + 32 * j, k = k0 + ak;
-            pa[j] = (t < T && k < K) ? __ldg(reinterpret_cast<const float4 *>(x + (size_t)t * K + k))
-                                     : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-    };
-    auto issue_b = [&](int st, int k0) {
-        __half *bt = gsm + st * kStageHalves + 2 * kTM * kTS;
+    // stage st <- k columns k0..k0+31 of the tile's 128 x rows (hi, lo) and 128 W rows: each
+    // 512 chunks of 16 bytes, chunk c = row c / 4, columns 8 (c % 4)..+7; thread tid copies
+    // chunks tid and tid + 256 of each (rows past T or R, columns past K: zeros)
+    auto issue = [&](int st, int k0) {
+        __half *ah = gsm + st * kStageHalves, *al = ah + kTM * kTS, *bt = al + kTM * kTS;
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
-            const int r = r0 + br + 64 * j, k = k0 + bk;
-            const bool ok = r < R && k < K;
-            cp_async16(bt + (br + 64 * j) * kTS + bk, ok ? static_cast<const void *>(W + (size_t)r * K + k) : W,
-                       ok ? 16 : 0);
+            const int c = tid + 256 * j, row = c >> 2, kc = (c & 3) * 8;
+            const int t = t0 + row, r = r0 + row, k = k0 + kc;
+            const bool okx = t < T && k < K, okw = r < R && k < K;
+            const size_t xo = okx ? (size_t)t * K + k : 0;
+            cp_async16(ah + row * kTS + kc, xh + xo, okx ? 16 : 0);
+            cp_async16(al + row * kTS + kc, xl + xo, okx ? 16 : 0);
+            cp_async16(bt + row * kTS + kc, okw ? W + (size_t)r * K + k : W, okw ? 16 : 0);
         }
         cp_async_commit();
-    };
-    auto store_a = [&](int st) {
-        __half *ah = gsm + st * kStageHalves, *al = ah + kTM * kTS;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            uint32_t h0, l0, h1, l1;
-            split_pair_checked(pa[j].x, pa[j].y, h0, l0, ep.err);
-            split_pair_checked(pa[j].z, pa[j].w, h1, l1, ep.err);
-            const int off = (ar + 32 * j) * kTS + ak;
-            *reinterpret_cast<uint2 *>(ah + off) = make_uint2(h0, h1);
-            *reinterpret_cast<uint2 *>(al + off) = make_uint2(l0, l1);
-        }
     };
     float acc[4][4][4];
 #pragma unroll
@@ -206,19 +199,24 @@ __global__ void __launch_bounds__(256, 2) k_gemm_mma(const __half *__restrict__ 
         for (int j = 0; j < 4; ++j)
 #pragma unroll
             for (int c = 0; c < 4; ++c) acc[i][j][c] = 0.f;
-    load_a(0);
-    issue_b(0, 0);
-    store_a(0);
-    cp_async_wait<0>();
-    __syncthreads();
     const int nk = (K + kTK - 1) / kTK;
+    // prologue: stages 0 .. S-2 in flight (empty commit groups keep the group count uniform)
+#pragma unroll
+    for (int s = 0; s < kGemmStages - 1; ++s) {
+        if (s < nk)
+            issue(s, s * kTK);
+        else
+            cp_async_commit();
+    }
     for (int it = 0; it < nk; ++it) {
-        const int st = it & 1;
-        const bool more = it + 1 < nk;
-        if (more) {
-            load_a((it + 1) * kTK);
-            issue_b(st ^ 1, (it + 1) * kTK);
-        }
+        cp_async_wait<kGemmStages - 2>();  // this thread's copies of stage `it` have landed
+        __syncthreads();                   // everyone's; and stage it-1's buffer is free again
+        const int nxt = it + kGemmStages - 1;
+        if (nxt < nk)
+            issue(nxt % kGemmStages, nxt * kTK);
+        else
+            cp_async_commit();
+        const int st = it % kGemmStages;
         const __half *ah = gsm + st * kStageHalves, *al = ah + kTM * kTS, *bt = ah + 2 * kTM * kTS;
 #pragma unroll
         for (int kk = 0; kk < kTK; kk += 16) {
@@ -248,12 +246,8 @@ __global__ void __launch_bounds__(256, 2) k_gemm_mma(const __half *__restrict__ 
                 }
             }
         }
-        if (more) {
-            store_a(st ^ 1);
-            cp_async_wait<0>();
-        }
-        __syncthreads();
     }
+    cp_async_wait<0>();  // only empty groups can be pending here
 #pragma unroll
     for (int mi = 0; mi < 4; ++mi)
 #pragma unroll
@@ -287,6 +281,11 @@ __global__ void __launch_bounds__(256, 2) k_gemm_mma(const __half *__restrict__ 
                         *reinterpret_cast<uint32_t *>(ep.kv16 + ((size_t)t * 4 + plane) * kDModel + d) = hi;
                         *reinterpret_cast<uint32_t *>(ep.kv16 + ((size_t)t * 4 + plane + 1) * kDModel + d) = lo;
                     }
+                } else if (EPI == EPI_GELU) {
+                    uint32_t hi, lo;
+                    split_pair_checked(gelu_erf(v0), gelu_erf(v1), hi, lo, ep.err);
+                    *reinterpret_cast<uint32_t *>(ep.out.hi + (size_t)t * R + c) = hi;
+                    *reinterpret_cast<uint32_t *>(ep.out.lo + (size_t)t * R + c) = lo;
                 } else {
                     float2 *dst = reinterpret_cast<float2 *>(ep.y + (size_t)t * R + c);
                     if (EPI == EPI_PLAIN) {
@@ -295,8 +294,6 @@ __global__ void __launch_bounds__(256, 2) k_gemm_mma(const __half *__restrict__ 
                             v1 += ep.vec[c + 1];
                         }
                         *dst = make_float2(v0, v1);
-                    } else if (EPI == EPI_GELU) {
-                        *dst = make_float2(gelu_erf(v0), gelu_erf(v1));
                     } else {
                         const float2 o = *dst;
                         *dst = make_float2(o.x + ep.vec[c] * v0, o.y + ep.vec[c + 1] * v1);
@@ -310,8 +307,8 @@ __global__ void __launch_bounds__(256, 2) k_gemm_mma(const __half *__restrict__ 
 // (decoder.cpp:229-244: the same per-element order).  codes [n][16][frames], row = b frames + f;
 // a code outside [0, 1024) is clamped (the host entry points reject such codes first).
 __global__ void k_front(const int *__restrict__ codes, int frames, const float *const *__restrict__ cb,
-                        const float *const *__restrict__ ow, const float *const *__restrict__ ob,
-                        float *__restrict__ z) {
+                        const float *const *__restrict__ ow, const float *const *__restrict__ ob, Planes z,
+                        int *__restrict__ err) {
     const int row = blockIdx.x;
     const int b = row / frames, f = row - b * frames;
     __shared__ float emb[kNCb][kCbDim];
@@ -322,6 +319,7 @@ __global__ void k_front(const int *__restrict__ codes, int frames, const float *
         emb[i][k] = cb[i][(size_t)code * kCbDim + k];
     }
     __syncthreads();
+    __shared__ float zs[kZ];
     for (int r = threadIdx.x; r < kZ; r += blockDim.x) {
         float zi = 0.f;
         for (int i = 0; i < kNCb; ++i) {
@@ -331,52 +329,85 @@ __global__ void k_front(const int *__restrict__ codes, int frames, const float *
             for (int k = 0; k < kCbDim; ++k) acc += w[k] * emb[i][k];
             zi += acc;
         }
-        z[(size_t)row * kZ + r] = zi;
+        zs[r] = zi;
+    }
+    __syncthreads();
+    for (int r2 = threadIdx.x; r2 < kZ / 2; r2 += blockDim.x) {
+        uint32_t hi, lo;
+        split_pair_checked(zs[2 * r2], zs[2 * r2 + 1], hi, lo, err);
+        reinterpret_cast<uint32_t *>(z.hi + (size_t)row * kZ)[r2] = hi;
+        reinterpret_cast<uint32_t *>(z.lo + (size_t)row * kZ)[r2] = lo;
     }
 }
 
-// x [t][c] -> out [t p][c / p]: out[t p + j][ci] = x[t][ci p + j] (decoder.cpp:73-87)
-__global__ void k_patch(const float *__restrict__ x, size_t T, int c, int p, float *__restrict__ out) {
-    const size_t n = T * c;
+// x [t][c] -> out [t p][c / p]: out[t p + j][ci] = x[t][ci p + j] (decoder.cpp:73-87), written
+// as hi/lo planes two columns at a time (c / p is even)
+__global__ void k_patch(const float *__restrict__ x, size_t T, int c, int p, Planes out, int *__restrict__ err) {
+    const size_t n2 = T * c / 2;
     const int d = c / p;
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    for (size_t i2 = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i2 < n2; i2 += (size_t)gridDim.x * blockDim.x) {
+        const size_t i = 2 * i2;
         const size_t row = i / d;
         const int ci = (int)(i - row * d);
         const size_t t = row / p;
         const int j = (int)(row - t * p);
-        out[i] = x[t * c + (size_t)ci * p + j];
+        const float *src = x + t * c + (size_t)ci * p + j;
+        uint32_t hi, lo;
+        split_pair_checked(src[0], src[p], hi, lo, err);
+        reinterpret_cast<uint32_t *>(out.hi)[i2] = hi;
+        reinterpret_cast<uint32_t *>(out.lo)[i2] = lo;
     }
 }
 
-// LayerNorm of 256-wide rows, one warp per row (audio_layer.cpp:17-29)
+// y [n] fp32 -> hi/lo planes (the input of a stage's out.w, read from the residual stream)
+__global__ void k_split_rows(const float *__restrict__ y, size_t n, Planes out, int *__restrict__ err) {
+    const size_t n2 = n / 2;
+    for (size_t i2 = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i2 < n2; i2 += (size_t)gridDim.x * blockDim.x) {
+        const float2 v = reinterpret_cast<const float2 *>(y)[i2];
+        uint32_t hi, lo;
+        split_pair_checked(v.x, v.y, hi, lo, err);
+        reinterpret_cast<uint32_t *>(out.hi)[i2] = hi;
+        reinterpret_cast<uint32_t *>(out.lo)[i2] = lo;
+    }
+}
+
+// LayerNorm of 256-wide rows, one warp per row, lane l holding the column pairs l + 32 j
+// (audio_layer.cpp:17-29), written as hi/lo planes
 __global__ void k_layernorm256(const float *__restrict__ x, int T, const float *__restrict__ w,
-                               const float *__restrict__ bias, float *__restrict__ out) {
+                               const float *__restrict__ bias, Planes out, int *__restrict__ err) {
     const int lane = threadIdx.x & 31;
     const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (t >= T) return;
-    const float *row = x + (size_t)t * kDModel;
-    float v[8], s = 0.f;
+    const float2 *row = reinterpret_cast<const float2 *>(x + (size_t)t * kDModel);
+    float2 v[4];
+    float s = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    for (int j = 0; j < 4; ++j) {
         v[j] = row[lane + 32 * j];
-        s += v[j];
+        s += v[j].x + v[j].y;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     const float mean = s / (float)kDModel;
     float q = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        const float d = v[j] - mean;
-        q += d * d;
+    for (int j = 0; j < 4; ++j) {
+        const float d0 = v[j].x - mean, d1 = v[j].y - mean;
+        q += d0 * d0 + d1 * d1;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
     const float inv = 1.0f / sqrtf(q / (float)kDModel + 1e-5f);
+    uint32_t *oh = reinterpret_cast<uint32_t *>(out.hi + (size_t)t * kDModel);
+    uint32_t *ol = reinterpret_cast<uint32_t *>(out.lo + (size_t)t * kDModel);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        const int k = lane + 32 * j;
-        out[(size_t)t * kDModel + k] = (v[j] - mean) * inv * w[k] + bias[k];
+    for (int j = 0; j < 4; ++j) {
+        const int k = 2 * (lane + 32 * j);
+        uint32_t hi, lo;
+        split_pair_checked((v[j].x - mean) * inv * w[k] + bias[k], (v[j].y - mean) * inv * w[k + 1] + bias[k + 1], hi,
+                           lo, err);
+        oh[lane + 32 * j] = hi;
+        ol[lane + 32 * j] = lo;
     }
 }
 
@@ -387,14 +418,15 @@ __global__ void k_layernorm256(const float *__restrict__ x, int T, const float *
 // (cp.async, two stages) into shared memory as fp16 hi/lo planes of k and v; scores and the
 // weighted sum on the tensor cores (3 products each for the hi/lo split), softmax online
 // across tiles with the probabilities scaled by 1024 (exact) so that small ones stay normal
-// fp16 numbers in the split.  Output: fp32 [rows][256].
+// fp16 numbers in the split.  Output: hi/lo planes [rows][256] (the proj GEMM's input); each
+// output is a convex combination of v values, which the qkv epilogue range-checked already.
 constexpr int kQT = 64, kKT = 64, kAS = 72;  // rows per block, keys per tile, smem row (halves)
 constexpr int kPlane = kKT * kAS;            // halves per plane of a tile
 constexpr size_t kAttnSmem = 2 * 4 * kPlane * sizeof(__half);  // 73,728 bytes
 
 __global__ void __launch_bounds__(128, 3) k_window_attn(const __half *__restrict__ q16, const __half *__restrict__ kv16,
                                                      int t, const __half *__restrict__ ring, int window, int layer,
-                                                     Meta meta, int n_streams, float *__restrict__ out) {
+                                                     Meta meta, int n_streams, Planes out) {
     extern __shared__ __align__(16) __half asmem[];
     const int b = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * kQT;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, tg = lane & 3;
@@ -570,8 +602,17 @@ __global__ void __launch_bounds__(128, 3) k_window_attn(const __half *__restrict
 #pragma unroll
     for (int nd = 0; nd < 8; ++nd) {
         const int d = h * kHeadDim + nd * 8 + 2 * tg;
-        if (oka) *reinterpret_cast<float2 *>(out + (row0 + ra) * kDModel + d) = make_float2(o[nd][0] / la, o[nd][1] / la);
-        if (okb) *reinterpret_cast<float2 *>(out + (row0 + rb) * kDModel + d) = make_float2(o[nd][2] / lb, o[nd][3] / lb);
+        uint32_t hi, lo;
+        if (oka) {
+            split_pair(o[nd][0] / la, o[nd][1] / la, hi, lo);
+            *reinterpret_cast<uint32_t *>(out.hi + (row0 + ra) * kDModel + d) = hi;
+            *reinterpret_cast<uint32_t *>(out.lo + (row0 + ra) * kDModel + d) = lo;
+        }
+        if (okb) {
+            split_pair(o[nd][2] / lb, o[nd][3] / lb, hi, lo);
+            *reinterpret_cast<uint32_t *>(out.hi + (row0 + rb) * kDModel + d) = hi;
+            *reinterpret_cast<uint32_t *>(out.lo + (row0 + rb) * kDModel + d) = lo;
+        }
     }
 }
 
@@ -598,9 +639,9 @@ __global__ void k_ring_append(const __half *__restrict__ kv16, int t, int n_stre
 // ------------------------------------------------------------------------------- host
 
 // kernel classes of the optional per-launch profile (mossgpu_codec_profile)
-enum Kind { KD_FRONT = 0, KD_GEMM, KD_PATCH, KD_LAYERNORM, KD_ATTN, KD_RING, KD_COUNT };
+enum Kind { KD_FRONT = 0, KD_GEMM, KD_PATCH, KD_LAYERNORM, KD_ATTN, KD_RING, KD_SPLIT, KD_COUNT };
 const char *const kKindNames[KD_COUNT] = {"k_front", "k_gemm_mma", "k_patch", "k_layernorm256",
-                                          "k_window_attn", "k_ring_append"};
+                                          "k_window_attn", "k_ring_append", "k_split_rows"};
 
 struct Mat {
     __half *w = nullptr;
@@ -657,13 +698,16 @@ public:
             for (auto &l : stages_[size_t(s)].layers) ffn_elems = std::max(ffn_elems, rows * size_t(l.f1.rows));
         }
         xa_ = alloc<float>(x_elems);
-        xb_ = alloc<float>(x_elems);
         y_ = alloc<float>(y_elems);
-        ln_ = alloc<float>(std::max(y_elems, F * kZ));
-        att_ = alloc<float>(y_elems);
         q16_ = alloc<__half>(y_elems * 2);
         kv16_ = alloc<__half>(y_elems * 4);
-        ffn_ = alloc<float>(ffn_elems);
+        // every GEMM input: the front's [F][512], a patched [rows][c / p] (x_elems), the
+        // [rows][256] activations, the [rows][FFN] GELU output
+        const size_t plane = std::max({F * kZ, x_elems, y_elems, ffn_elems});
+        for (Planes *pl : {&p0_, &p1_}) {
+            pl->hi = alloc<__half>(plane);
+            pl->lo = alloc<__half>(plane);
+        }
         err_ = alloc<int>(1);
         CK(cudaMemset(err_, 0, sizeof(int)));
         codes_ = alloc<int>(size_t(kNCb) * F);
@@ -834,7 +878,7 @@ public:
 
     int launches_per_call() const {
         int l = 2;
-        for (auto &s : stages_) l += 3 + 8 * int(s.layers.size());
+        for (auto &s : stages_) l += 4 + 8 * int(s.layers.size());  // patch, in.w, split, out.w + layers
         return l;
     }
 
@@ -870,18 +914,18 @@ private:
         return static_cast<T *>(p);
     }
 
-    void gemm(const Mat &m, const float *x, int T, int epi, Epi ep) {
+    void gemm(const Mat &m, const Planes &x, int T, int epi, Epi ep) {
         const dim3 grid((m.rows + kTN - 1) / kTN, (T + kTM - 1) / kTM);
         ep.err = err_;
         mark_begin(KD_GEMM);
         if (epi == EPI_PLAIN)
-            k_gemm_mma<EPI_PLAIN><<<grid, 256, kGemmSmem, stream_>>>(m.w, x, T, m.rows, m.cols, ep);
+            k_gemm_mma<EPI_PLAIN><<<grid, 256, kGemmSmem, stream_>>>(m.w, x.hi, x.lo, T, m.rows, m.cols, ep);
         else if (epi == EPI_GELU)
-            k_gemm_mma<EPI_GELU><<<grid, 256, kGemmSmem, stream_>>>(m.w, x, T, m.rows, m.cols, ep);
+            k_gemm_mma<EPI_GELU><<<grid, 256, kGemmSmem, stream_>>>(m.w, x.hi, x.lo, T, m.rows, m.cols, ep);
         else if (epi == EPI_SCALED_ADD)
-            k_gemm_mma<EPI_SCALED_ADD><<<grid, 256, kGemmSmem, stream_>>>(m.w, x, T, m.rows, m.cols, ep);
+            k_gemm_mma<EPI_SCALED_ADD><<<grid, 256, kGemmSmem, stream_>>>(m.w, x.hi, x.lo, T, m.rows, m.cols, ep);
         else
-            k_gemm_mma<EPI_QKV><<<grid, 256, kGemmSmem, stream_>>>(m.w, x, T, m.rows, m.cols, ep);
+            k_gemm_mma<EPI_QKV><<<grid, 256, kGemmSmem, stream_>>>(m.w, x.hi, x.lo, T, m.rows, m.cols, ep);
         CK(cudaGetLastError());
         mark_end();
     }
@@ -891,31 +935,37 @@ private:
         e.vec = vec;
         return e;
     }
+    static int blocks_for(size_t items) { return int(std::min<size_t>((items + 255) / 256, 148 * 16)); }
 
+    // The activation planes: p0_ and p1_ alternate so that no kernel reads the planes it writes
+    // (LN1 -> p0 -> qkv; attention -> p1 -> proj; LN2 -> p0 -> f1 -> p1 -> f2).
     void run(const Meta &md, int n, const int *codes, int frames, float *pcm) {
         int rows = n * frames;  // all streams' rows of the current stage
         mark_begin(KD_FRONT);
-        k_front<<<rows, 256, 0, stream_>>>(codes, frames, d_cb_, d_ow_, d_ob_, ln_);
+        k_front<<<rows, 256, 0, stream_>>>(codes, frames, d_cb_, d_ow_, d_ob_, p0_, err_);
         CK(cudaGetLastError());
         mark_end();
-        gemm(q_out_, ln_, rows, EPI_PLAIN, out(xa_, q_out_b_));
+        gemm(q_out_, p0_, rows, EPI_PLAIN, out(xa_, q_out_b_));
         int c = c0_, t = frames, li = 0;
         for (int s = 0; s < kStages; ++s) {
             Stage &st = stages_[size_t(s)];
             const int p = kPatch[s];
-            const size_t nel = size_t(rows) * size_t(c);
-            const int pblocks = int(std::min<size_t>((nel + 255) / 256, 148 * 16));
             mark_begin(KD_PATCH);
-            k_patch<<<pblocks, 256, 0, stream_>>>(xa_, size_t(rows), c, p, xb_);
+            k_patch<<<blocks_for(size_t(rows) * size_t(c) / 2), 256, 0, stream_>>>(xa_, size_t(rows), c, p, p0_, err_);
             CK(cudaGetLastError());
             mark_end();
             rows *= p;
             t *= p;
             c /= p;
-            gemm(st.in, xb_, rows, EPI_PLAIN, out(y_));
+            gemm(st.in, p0_, rows, EPI_PLAIN, out(y_));
             for (auto &l : st.layers) layer(l, md, n, rows, t, kContext[s], li++, md.offset + s * n);
+            mark_begin(KD_SPLIT);
+            k_split_rows<<<blocks_for(size_t(rows) * kDModel / 2), 256, 0, stream_>>>(y_, size_t(rows) * kDModel, p0_,
+                                                                                        err_);
+            CK(cudaGetLastError());
+            mark_end();
             float *dst = s + 1 < kStages ? xa_ : pcm;  // the final patch of 240 is the identity
-            gemm(st.out, y_, rows, EPI_PLAIN, out(dst));
+            gemm(st.out, p0_, rows, EPI_PLAIN, out(dst));
             c = st.out.rows;
         }
     }
@@ -924,17 +974,17 @@ private:
     void layer(Layer &l, const Meta &md, int n, int rows, int t, int window, int li, const int *offset) {
         const int lnb = (rows + 7) / 8;
         mark_begin(KD_LAYERNORM);
-        k_layernorm256<<<lnb, 256, 0, stream_>>>(y_, rows, l.n1w, l.n1b, ln_);
+        k_layernorm256<<<lnb, 256, 0, stream_>>>(y_, rows, l.n1w, l.n1b, p0_, err_);
         mark_end();
         Epi qkv;
         qkv.q16 = q16_;
         qkv.kv16 = kv16_;
         qkv.offset = offset;
         qkv.t_per_stream = t;
-        gemm(l.attn, ln_, rows, EPI_QKV, qkv);
+        gemm(l.attn, p0_, rows, EPI_QKV, qkv);
         const dim3 ag((t + kQT - 1) / kQT, kHeads, n);
         mark_begin(KD_ATTN);
-        k_window_attn<<<ag, 128, kAttnSmem, stream_>>>(q16_, kv16_, t, l.ring, window, li, md, n, att_);
+        k_window_attn<<<ag, 128, kAttnSmem, stream_>>>(q16_, kv16_, t, l.ring, window, li, md, n, p1_);
         mark_end();
         const size_t items = size_t(n) * size_t(std::min(t, window)) * 128;
         mark_begin(KD_RING);
@@ -942,12 +992,14 @@ private:
             kv16_, t, n, l.ring, window, li, md);
         CK(cudaGetLastError());
         mark_end();
-        gemm(l.proj, att_, rows, EPI_SCALED_ADD, out(y_, l.ls1));
+        gemm(l.proj, p1_, rows, EPI_SCALED_ADD, out(y_, l.ls1));
         mark_begin(KD_LAYERNORM);
-        k_layernorm256<<<lnb, 256, 0, stream_>>>(y_, rows, l.n2w, l.n2b, ln_);
+        k_layernorm256<<<lnb, 256, 0, stream_>>>(y_, rows, l.n2w, l.n2b, p0_, err_);
         mark_end();
-        gemm(l.f1, ln_, rows, EPI_GELU, out(ffn_));
-        gemm(l.f2, ffn_, rows, EPI_SCALED_ADD, out(y_, l.ls2));
+        Epi gelu;
+        gelu.out = p1_;
+        gemm(l.f1, p0_, rows, EPI_GELU, gelu);
+        gemm(l.f2, p1_, rows, EPI_SCALED_ADD, out(y_, l.ls2));
     }
 
     void load(const std::string &path) {
@@ -1071,7 +1123,8 @@ private:
     float *q_out_b_ = nullptr;
     const float **d_cb_ = nullptr, **d_ow_ = nullptr, **d_ob_ = nullptr;
     std::vector<Stage> stages_;
-    float *xa_ = nullptr, *xb_ = nullptr, *y_ = nullptr, *ln_ = nullptr, *att_ = nullptr, *ffn_ = nullptr,
+    Planes p0_, p1_;
+    float *xa_ = nullptr, *y_ = nullptr,
           *pcm_ = nullptr;
     __half *q16_ = nullptr, *kv16_ = nullptr;
     int *codes_ = nullptr, *meta_d_ = nullptr, *err_ = nullptr;

@@ -282,7 +282,7 @@ size_t mossgpu_codec_device_bytes(mossgpu_codec *c);
 int mossgpu_codec_set_cuda_stream(mossgpu_codec *c, void *cuda_stream);
 /* Per-kernel-class device time: while enabled, each launch is bracketed by CUDA events (which
  * add a gap per launch); profile_read synchronises, writes the milliseconds and launch count of
- * each class since the last read (max_kinds >= 6) and the class count to *n_kinds.  Class
+ * each class since the last read (max_kinds >= 7) and the class count to *n_kinds.  Class
  * names: mossgpu_codec_kernel_name. */
 int mossgpu_codec_profile(mossgpu_codec *c, int enable);
 int mossgpu_codec_profile_read(mossgpu_codec *c, float *total_ms, int *launches, int max_kinds, int *n_kinds);
