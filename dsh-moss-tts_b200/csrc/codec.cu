@@ -23,9 +23,10 @@
 // operands, fp32 accumulation) with every fp32 operand split into fp16 hi + lo (hi = fp16(x),
 // lo = fp16(x - hi), ~22 significant bits): a GEMM is W.x_hi + W.x_lo (the fp16 weights are
 // exact), a score q.k_hi + q.k_lo... as q_hi.k_hi + q_hi.k_lo + q_lo.k_hi, and p.v likewise.
-// Activations stay fp32 in memory [rows][channels]; the qkv GEMM's epilogue applies RoPE and
-// writes q / 8 (exact scaling) and k, v as fp16 hi/lo planes, which is also the format of the
-// K/V rings ([slot][context][kh, kl, vh, vl][256] fp16, slot = stream id).  A value that fp16
+// The residual stream and each stage's output stay fp32 [rows][channels]; every GEMM input is
+// kept as two fp16 planes (hi, lo) that the kernel producing it writes.  The qkv GEMM's
+// epilogue applies RoPE and writes q / 8 (exact scaling) and k, v as fp16 hi/lo planes, which is
+// also the format of the K/V rings ([slot][context][kh, kl, vh, vl][256] fp16, slot = stream id).  A value that fp16
 // cannot hold (|x| >= 65504, or NaN) sets the codec's range flag: the host entry points then
 // fail, and the device entry point reports it through mossgpu_codec_status.
 #include "../../include/mossgpu.h"
