@@ -567,8 +567,9 @@ void launch_tc(TcArgs a, int prec, cudaStream_t st, bool pdl, int direct_min, in
     if (direct) {
         while (a.N % ns) ns -= 16;
         // the per-matrix choice keeps slices of >= 64 rows (a padded batch that 64 does not
-        // divide, such as 304 rows, takes split-K); an explicit direct_ns is taken as given
-        if (direct_ns == 0 && a.N < 1024 && ns < 64) direct = false;
+        // divide, such as 304 rows, takes split-K), except for a STORE in K parts, whose
+        // consumer adds the parts; an explicit direct_ns is taken as given
+        if (direct_ns == 0 && a.N < 1024 && ns < 64 && ks == 1) direct = false;
     }
     if (direct) {
         a.nsub = ns;

@@ -290,6 +290,35 @@ def test_benched_frame_512_streams_direct_form(pkg, weights_path):
         eng.close()
 
 
+def test_ragged_batch_not_divisible_by_64(pkg, weights_path):
+    """300 streams: 304 padded rows, which 64 does not divide.  The default policy then mixes
+    forms: the global proj and fc_out stay direct in 16-row slices (their K parts are added by
+    the next LayerNorm), the other matrices take split-K.  3 free-running frames, then 5
+    sampled streams against the oracle."""
+    lens = [int(x) for x in np.random.default_rng(304).integers(64, 300, 300)]
+    F = 3
+    eng = pkg.Engine(weights_path, device=0, max_streams=301, max_ctx=300 + F + 16)
+    try:
+        sids = [eng.open() for _ in lens]
+        for i, (s, L) in enumerate(zip(sids, lens)):
+            eng.fill_state_random(s, L, seed=900 + i)
+            eng.generate_begin(s, 0)
+        sample = sorted({int(np.argmin(lens)), int(np.argmax(lens)), 0, 151, 299})
+        states = {i: read_state(eng, sids[i], lens[i]) for i in sample}
+        codes, done = eng.step_frames(sids, pkg.SampleParams.make(**GREEDY_NEVER_STOP), F)
+        assert (done == F).all()
+        with pool() as ex:
+            res = dict(zip(sample, ex.map(lambda i: oracle_forced(weights_path, states[i], codes[:, i], True),
+                                          sample)))
+        for i in sample:
+            o_codes, _, _, o_hidden, orc = res[i]
+            check_codes(codes[:, i], o_codes, f"stream {i} (L={lens[i]})")
+            assert np.abs(eng.hidden(sids[i]) - o_hidden).max() < TOL, i
+            orc.close()
+    finally:
+        eng.close()
+
+
 def test_long_context_batch_near_configs4_end(pkg, weights_path):
     """100 streams at 4,300-4,500 cached positions (configs[4] ends near 4,500): the split-K
     attention over ~280 pages per row and RoPE angles at the end of the context.  One
