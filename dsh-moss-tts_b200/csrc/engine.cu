@@ -619,6 +619,14 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
     // append) runs as its own pass and residual adds move into the next LayerNorm kernel, which
     // reads x anyway.  The last global layer's fc_out keeps its residual epilogue (ln_f reads x).
     const bool direct = !local && tc_direct_min_rows_ > 0 && N >= tc_direct_min_rows_;
+    // From the direct-form batch size on, proj and fc_out store their outputs in K parts (more
+    // tiles to fill the SMs) and the next activation-image builder adds them to x: LN2 for
+    // proj; for fc_out the next layer's LN1, or in the local decoder the audio head's ln_f
+    // (heads_tc).  Kept as a residual epilogue: the last global layer's fc_out (ln_f reads x)
+    // and local step 0's (the end gate reads x).  The local decoder stores parts from twice the
+    // direct-form batch on (measured per 512-stream frame: local proj + fc_out 0.51 against
+    // 0.74 ms, the builders' adds 0.08 ms more; at 256 streams the frame was 1% slower).
+    const bool parts = tc_direct_min_rows_ > 0 && N >= (local ? 2 : 1) * tc_direct_min_rows_;
     const float *add1 = pending_resid_;
     const int nadd1 = pending_parts_;
     pending_resid_ = nullptr;
@@ -721,17 +729,17 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
     p.rows = kHidden;
     p.K = kHidden;
     p.bias = L.proj_b;
-    p.out = direct ? mlp_ : x;  // direct: kTcKParts K parts at mlp_ + part_stride() apart
+    p.out = parts ? mlp_ : x;  // parts: kTcKParts K parts at mlp_ + part_stride() apart
     p.ldo = kHidden;
-    p.ksplit = direct ? kTcKParts : 1;
+    p.ksplit = parts ? kTcKParts : 1;
     p.part_stride = part_stride();
-    if (direct)
+    if (parts)
         launch_tc<TC_STORE>(p, prec, stream_, pdl_, tc_direct_min_rows_, tc_direct_rows_);
     else
         launch_tc<TC_RESID>(p, prec, stream_, pdl_, tc_direct_min_rows_, tc_direct_rows_);
     mark(local ? KK_PROJ_L : KK_PROJ_G);
     launch_k(pdl_, k_build_bimg, dim3((N + 7) / 8), dim3(256), 0, stream_, x, kHidden, R, N, L.ln2_w, L.ln2_b,
-             tc_parts(prec), bimg_a_, direct ? static_cast<const float *>(mlp_) : nullptr, kTcKParts, part_stride());
+             tc_parts(prec), bimg_a_, parts ? static_cast<const float *>(mlp_) : nullptr, kTcKParts, part_stride());
     mark(KK_BIMG);
     TcArgs f{};
     f.N = N;
@@ -757,7 +765,7 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
     o.K = kFF;
     o.bias = L.fc_out_b;
     o.ldo = kHidden;
-    if (direct && li < kLayers - 1) {  // the next layer's LN1 kernel adds its K parts to x
+    if (parts && (local ? lpos > 0 : li < kLayers - 1)) {  // the next builder adds the K parts to x
         o.out = mlp_;
         o.ksplit = kTcKParts;
         o.part_stride = part_stride();
@@ -775,8 +783,12 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
 void Engine::heads_tc(int ch, int R) {
     const int N = (R + 15) / 16 * 16;
     const int prec = gemm_path_ == 3 ? TC_F16 : TC_F16X3;
+    // the local block's fc_out K parts, when it stored them, are added to lx_ here
+    const float *add = pending_resid_;
+    const int nadd = pending_parts_;
+    pending_resid_ = nullptr;
     launch_k(pdl_, k_build_bimg, dim3((N + 7) / 8), dim3(256), 0, stream_, lx_, kHidden, R, N, llnf_w_, llnf_b_,
-             tc_parts(prec), bimg_a_, static_cast<const float *>(nullptr), 0, size_t(0));
+             tc_parts(prec), bimg_a_, add, add ? nadd : 0, part_stride());
     mark(KK_BIMG);
     TcArgs h{};
     h.N = N;
