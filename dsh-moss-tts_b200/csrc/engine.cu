@@ -630,10 +630,15 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
     const float *add1 = pending_resid_;
     const int nadd1 = pending_parts_;
     pending_resid_ = nullptr;
-    launch_k(pdl_ && !(plain_first_ && li == 0 && !local), k_build_bimg, dim3((N + 7) / 8), dim3(256), 0, stream_, x,
-             kHidden, R, N, L.ln1_w, L.ln1_b, tc_parts(prec), bimg_a_, add1, nadd1, part_stride());
-    if (!local && li == 0) plain_first_ = false;
-    mark(KK_BIMG);
+    if (local && ln1_prebuilt_) {  // k_sample wrote this step's LN1 image with its input row
+        if (add1) throw std::logic_error("local LN1 image prebuilt with a residual add pending");
+        ln1_prebuilt_ = false;
+    } else {
+        launch_k(pdl_ && !(plain_first_ && li == 0 && !local), k_build_bimg, dim3((N + 7) / 8), dim3(256), 0, stream_,
+                 x, kHidden, R, N, L.ln1_w, L.ln1_b, tc_parts(prec), bimg_a_, add1, nadd1, part_stride());
+        if (!local && li == 0) plain_first_ = false;
+        mark(KK_BIMG);
+    }
     TcArgs a{};
     a.N = N;
     a.R = R;
@@ -1442,6 +1447,10 @@ void Engine::issue_frame(int R, bool run_global) {
     const int *d_slot = d_ctl_ + off_slot(), *d_pos = d_ctl_ + off_pos(), *d_frame = d_ctl_ + off_frame();
     const int *d_forced = d_ctl_ + off_forced();
     const FrameCtl *d_fc = reinterpret_cast<const FrameCtl *>(d_ctl_ + off_fctl());
+    // builder state carried between launches of one frame only (an exception in an earlier
+    // frame's issue must not leave it set)
+    ln1_prebuilt_ = false;
+    pending_resid_ = nullptr;
     k_page_updates<<<unsigned((R + 127) / 128), 128, 0, stream_>>>(d_ctl_ + off_pages(), page_table_, pages_per_stream_);
     mark(KK_PAGES);
     // ---- local decoder: 17 steps (llm.cpp:648-698)
@@ -1481,9 +1490,19 @@ void Engine::issue_frame(int R, bool run_global) {
                 launch_gemv<PRO_LN, EPI_STORE>(h, stream_, pdl_);
                 mark(KK_HEADS);
             }
+            // on the tensor-core path the sampler also writes the next step's LN1 image
+            NextImage img;
+            if (use_tc(R) && ch + 1 < kNVq) {
+                img.ln_w = local_.ln1_w;
+                img.ln_b = local_.ln1_b;
+                img.bimg = bimg_a_;
+                img.N = (R + 15) / 16 * 16;
+                img.parts = tc_parts(gemm_path_ == 3 ? TC_F16 : TC_F16X3);
+                ln1_prebuilt_ = true;
+            }
             launch_k(pdl_, k_sample, dim3(R), dim3(256), 0, stream_, logits_ + size_t(ch) * kCodebook, kNVq * kCodebook,
                      ch, d_slot, R, counts_, d_fc, d_forced, active_, codes_, used_, qm(aemb_[ch]),
-                     ch + 1 < kNVq ? lx_ : nullptr, d_frame, rng_);
+                     ch + 1 < kNVq ? lx_ : nullptr, d_frame, rng_, img);
             mark(KK_SAMPLE);
         }
     }

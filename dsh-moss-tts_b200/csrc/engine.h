@@ -183,6 +183,7 @@ private:
     // a direct-form fc_out stored its output here; the next layer's LN1 kernel adds it to x
     const float *pending_resid_ = nullptr;
     int pending_parts_ = 1;
+    bool ln1_prebuilt_ = false;  // the next local block's LN1 image was written by k_sample
     // direct-form proj / fc_out split K in kTcKParts parts (their 768-row GEMMs have 96 tiles
     // for 148 SMs) and store the parts part_stride() floats apart in mlp_ ([R][3072] floats)
     static constexpr int kTcKParts = 3;

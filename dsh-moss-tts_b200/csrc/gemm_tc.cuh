@@ -873,7 +873,7 @@ __global__ void __launch_bounds__(kTpThreads, 1) k_gemm_tp(const TcArgs a) {
 // n_add K parts add_stride floats apart, summed in order).  One
 // warp per row: lane l holds the 8-element units l, l + 32, l + 64 of the row (one 16-byte
 // unit of the image each), the LayerNorm statistics are warp reductions.
-constexpr int kBimgUnits = kHidden / 256;  // 8-element units per lane
+constexpr int kBimgUnits = kBimgRowUnits;  // 8-element units per lane
 __global__ void __launch_bounds__(256) k_build_bimg(float *__restrict__ x, int ldx, int R, int N,
                                                     const float *__restrict__ ln_w, const float *__restrict__ ln_b,
                                                     int parts, uint8_t *__restrict__ bimg,
@@ -913,47 +913,7 @@ __global__ void __launch_bounds__(256) k_build_bimg(float *__restrict__ x, int l
         v[j][0] = a0.x; v[j][1] = a0.y; v[j][2] = a0.z; v[j][3] = a0.w;
         v[j][4] = a1.x; v[j][5] = a1.y; v[j][6] = a1.z; v[j][7] = a1.w;
     }
-    if (ln_w) {  // LayerNorm (llm.cpp:159-171)
-        float sum = 0.f;
-#pragma unroll
-        for (int j = 0; j < kBimgUnits; ++j)
-#pragma unroll
-            for (int e = 0; e < 8; ++e) sum += v[j][e];
-        const float mean = __fdiv_rn(warp_sum(sum), (float)kHidden);
-        float var = 0.f;
-#pragma unroll
-        for (int j = 0; j < kBimgUnits; ++j)
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                const float d = v[j][e] - mean;
-                var = fmaf(d, d, var);
-            }
-        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(warp_sum(var), (float)kHidden) + 1e-5f));
-#pragma unroll
-        for (int j = 0; j < kBimgUnits; ++j) {
-            const int k0 = 8 * (lane + 32 * j);
-            const float4 w0 = *reinterpret_cast<const float4 *>(ln_w + k0), w1 = *reinterpret_cast<const float4 *>(ln_w + k0 + 4);
-            const float4 c0 = *reinterpret_cast<const float4 *>(ln_b + k0), c1 = *reinterpret_cast<const float4 *>(ln_b + k0 + 4);
-            const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-            const float bv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-#pragma unroll
-            for (int e = 0; e < 8; ++e)
-                v[j][e] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[j][e], mean), inv), wv[e]), bv[e]);
-        }
-    }
-#pragma unroll
-    for (int j = 0; j < kBimgUnits; ++j) {
-        __align__(16) __half h[8];
-        __align__(16) __half l[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            h[e] = __float2half_rn(v[j][e]);
-            l[e] = __float2half_rn(v[j][e] - __half2float(h[e]));
-        }
-        const size_t off = bimg_off(n, 8 * (lane + 32 * j), N);
-        *reinterpret_cast<int4 *>(bimg + off) = *reinterpret_cast<const int4 *>(h);
-        if (parts == 2) *reinterpret_cast<int4 *>(bimg + part + off) = *reinterpret_cast<const int4 *>(l);
-    }
+    bimg_row_write(v, lane, n, N, ln_w, ln_b, parts, bimg);
 }
 
 // The QKV epilogue of a prefill pass as its own pass over the GEMM's stored output (bias

@@ -495,6 +495,57 @@ __device__ __forceinline__ size_t bimg_off(int n, int k, int N) {
     return ((size_t)(k >> 6) * N + n) * 128 + ((((k & 63) >> 3) ^ (n & 7)) << 4) + ((k & 7) << 1);
 }
 
+// One row n of an activation image, written by one warp: lane l holds the 8-element units l,
+// l + 32, l + 64 of the row in v; optional LayerNorm (llm.cpp:159-171: warp-reduced mean and
+// variance), then the fp16 value and (parts = 2) the fp16 of its remainder per element.
+constexpr int kBimgRowUnits = kHidden / 256;
+__device__ __forceinline__ void bimg_row_write(float (&v)[kBimgRowUnits][8], int lane, int n, int N,
+                                               const float *__restrict__ ln_w, const float *__restrict__ ln_b,
+                                               int parts, uint8_t *__restrict__ bimg) {
+    if (ln_w) {
+        float sum = 0.f;
+#pragma unroll
+        for (int j = 0; j < kBimgRowUnits; ++j)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) sum += v[j][e];
+        const float mean = __fdiv_rn(warp_sum(sum), (float)kHidden);
+        float var = 0.f;
+#pragma unroll
+        for (int j = 0; j < kBimgRowUnits; ++j)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const float d = v[j][e] - mean;
+                var = fmaf(d, d, var);
+            }
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(warp_sum(var), (float)kHidden) + 1e-5f));
+#pragma unroll
+        for (int j = 0; j < kBimgRowUnits; ++j) {
+            const int k0 = 8 * (lane + 32 * j);
+            const float4 w0 = *reinterpret_cast<const float4 *>(ln_w + k0), w1 = *reinterpret_cast<const float4 *>(ln_w + k0 + 4);
+            const float4 c0 = *reinterpret_cast<const float4 *>(ln_b + k0), c1 = *reinterpret_cast<const float4 *>(ln_b + k0 + 4);
+            const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+            const float bv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+                v[j][e] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[j][e], mean), inv), wv[e]), bv[e]);
+        }
+    }
+    const size_t part = (size_t)kHidden * N * 2;
+#pragma unroll
+    for (int j = 0; j < kBimgRowUnits; ++j) {
+        __align__(16) __half h[8];
+        __align__(16) __half l[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            h[e] = __float2half_rn(v[j][e]);
+            l[e] = __float2half_rn(v[j][e] - __half2float(h[e]));
+        }
+        const size_t off = bimg_off(n, 8 * (lane + 32 * j), N);
+        *reinterpret_cast<int4 *>(bimg + off) = *reinterpret_cast<const int4 *>(h);
+        if (parts == 2) *reinterpret_cast<int4 *>(bimg + part + off) = *reinterpret_cast<const int4 *>(l);
+    }
+}
+
 // Store 8 consecutive output dims (one lane's share of a head) of row r.
 __device__ __forceinline__ void attn_store8(const AttnArgs &a, int r, int k0, const float *y) {
     if (a.bimg) {  // 8 dims = one 16-byte unit of the activation image
@@ -1186,14 +1237,22 @@ __global__ void __launch_bounds__(256) k_frame_commit(const int *__restrict__ co
 // (greedy, top_k == 1, or frame < greedy_frames), or temperature, a sort by (value desc,
 // index asc), top-k, exp / sum in that order, the top-p cut and one xoshiro128** draw walked
 // down the sorted list.  Writes the prediction, the code used (forced or predicted), the
-// counts update and the next local input row aemb[ch][used].
+// counts update and the next local input row aemb[ch][used]; with img != null also that row's
+// LayerNorm activation image (the next local step's LN1, as k_build_bimg writes it), so that
+// the next step starts at its QKV GEMM.
+struct NextImage {
+    const float *ln_w = nullptr, *ln_b = nullptr;
+    uint8_t *bimg = nullptr;
+    int N = 0, parts = 0;
+};
 __global__ void __launch_bounds__(256) k_sample(const float *__restrict__ logits, int ld_logits, int ch,
                                                 const int *__restrict__ row_slot, int R,
                                                 uint16_t *__restrict__ counts, const FrameCtl *__restrict__ ctl,
                                                 const int *__restrict__ forced, const int *__restrict__ active,
                                                 int *__restrict__ codes_out, int *__restrict__ used_out,
                                                 const QMat aemb, float *__restrict__ next_x,
-                                                const int *__restrict__ frame_idx, uint32_t *__restrict__ rng) {
+                                                const int *__restrict__ frame_idx, uint32_t *__restrict__ rng,
+                                                NextImage img) {
     __shared__ float sv[kCodebook];
     __shared__ int si[kCodebook];
     __shared__ float bv[8];
@@ -1312,7 +1371,24 @@ __global__ void __launch_bounds__(256) k_sample(const float *__restrict__ logits
         s_used = used;
     }
     __syncthreads();
-    if (next_x) {
+    if (next_x && img.bimg) {
+        // warp 0: the row in k_build_bimg's lane layout (units l, l + 32, l + 64), to x and image
+        if (threadIdx.x < 32) {
+            const int used = s_used, lane = threadIdx.x;
+            const bool ok = used >= 0 && used < kCodebook;
+            float v[kBimgRowUnits][8];
+#pragma unroll
+            for (int j = 0; j < kBimgRowUnits; ++j) {
+                const int k0 = 8 * (lane + 32 * j);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[j][e] = ok ? deq_elem(aemb, used, k0 + e) : 0.f;
+                float4 *xp = reinterpret_cast<float4 *>(next_x + (size_t)r * kHidden + k0);
+                xp[0] = make_float4(v[j][0], v[j][1], v[j][2], v[j][3]);
+                xp[1] = make_float4(v[j][4], v[j][5], v[j][6], v[j][7]);
+            }
+            bimg_row_write(v, lane, r, img.N, img.ln_w, img.ln_b, img.parts, img.bimg);
+        }
+    } else if (next_x) {
         const int used = s_used;
         for (int c = threadIdx.x; c < kHidden; c += blockDim.x)
             next_x[(size_t)r * kHidden + c] = (used >= 0 && used < kCodebook) ? deq_elem(aemb, used, c) : 0.f;
