@@ -46,6 +46,7 @@ EXPORTS = [
     "mossgpu_attention_decode_paged_noalloc", "mossgpu_set_gemm_path", "mossgpu_debug_matrix_tile_bytes",
     "mossgpu_stream_fork", "mossgpu_create_rows", "mossgpu_prefill_batch", "mossgpu_prefill_embeds_batch",
     "mossgpu_set_tc_policy", "mossgpu_op_device_status", "mossgpu_debug_inject_wait_timeout", "mossgpu_set_local_path",
+    "mossgpu_set_small_layers",
     "mossgpu_codec_create", "mossgpu_codec_destroy", "mossgpu_codec_last_error", "mossgpu_codec_samples_per_frame",
     "mossgpu_codec_launches_per_call", "mossgpu_codec_device_bytes", "mossgpu_codec_set_cuda_stream",
     "mossgpu_codec_open", "mossgpu_codec_close", "mossgpu_codec_reset", "mossgpu_codec_decode_chunk",
@@ -141,6 +142,7 @@ def lib() -> C.CDLL:
         L.mossgpu_op_device_status.argtypes = [C.POINTER(C.c_int)]
         L.mossgpu_debug_inject_wait_timeout.argtypes = [C.c_void_p, C.c_int]
         L.mossgpu_set_local_path.argtypes = [C.c_void_p, C.c_int]
+        L.mossgpu_set_small_layers.argtypes = [C.c_void_p, C.c_int]
         L.mossgpu_attention_decode_paged_noalloc.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p,
                                                              C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]
         L.mossgpu_codec_create.restype = C.c_void_p
@@ -329,8 +331,12 @@ class Engine:
         self._check(self.lib.mossgpu_debug_inject_wait_timeout(self.h, int(enable)))
 
     def set_local_path(self, mode: int):
-        """0 = fused local decoder for greedy frames (default), 1 = per-step kernels for every frame."""
+        """0 = fused local decoder for greedy frames, 1 = per-step kernels for every frame (default)."""
         self._check(self.lib.mossgpu_set_local_path(self.h, mode))
+
+    def set_small_layers(self, mode: int):
+        """Global layers of <= 8-row decode batches: 1 = two launches a layer (default), 0 = five."""
+        self._check(self.lib.mossgpu_set_small_layers(self.h, mode))
 
     def set_graphs(self, enable: bool):
         self._check(self.lib.mossgpu_set_graphs(self.h, int(enable)))

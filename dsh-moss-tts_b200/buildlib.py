@@ -9,7 +9,7 @@ PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libmossgpu.so"
 SOURCES = ["engine.cu", "ops.cu", "codec.cu", "capi.cpp"]
-HEADERS = ["types.h", "kernels.cuh", "gemm_tc.cuh", "attn_tc.cuh", "local_fused.cuh", "engine.h", "../../include/mossgpu.h"]
+HEADERS = ["types.h", "kernels.cuh", "gemm_tc.cuh", "attn_tc.cuh", "local_fused.cuh", "layer_small.cuh", "engine.h", "../../include/mossgpu.h"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
          "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall", "-diag-suppress", "550", "-shared"]

@@ -230,6 +230,10 @@ int mossgpu_set_local_path(mossgpu_engine *e, int mode) {
     return guarded(e, [&](mossgpu::Engine &g) { g.set_local_path(mode); });
 }
 
+int mossgpu_set_small_layers(mossgpu_engine *e, int mode) {
+    return guarded(e, [&](mossgpu::Engine &g) { g.set_small_layers(mode); });
+}
+
 int mossgpu_set_gemm_path(mossgpu_engine *e, int mode) {
     return guarded(e, [&](mossgpu::Engine &g) { g.set_gemm_path(mode); });
 }

@@ -20,6 +20,7 @@
 #include "gemm_tc.cuh"
 #include "attn_tc.cuh"
 #include "local_fused.cuh"
+#include "layer_small.cuh"
 
 namespace mossgpu {
 
@@ -244,6 +245,8 @@ void Engine::allocate_state() {
     bimg_mlp_ = dalloc<uint8_t>(2 * size_t(kFF) * rows16 * 2, owned_);
     dev_err_ = dalloc<int>(4, owned_);
     CK(cudaMemset(dev_err_, 0, 4 * sizeof(int)));
+    sd_ = dalloc<long long>(size_t(3) * kSlMaxRows * kHidden, owned_);
+    CK(cudaMemset(sd_, 0, size_t(3) * kSlMaxRows * kHidden * sizeof(long long)));
     {
         void *he = nullptr;
         CK(cudaMallocHost(&he, 4 * sizeof(int)));
@@ -421,6 +424,20 @@ void Engine::set_smem_limits() {
     set_tc_attr<TC_GELU_B>();
     // fused local decoder: 16-CTA clusters (a non-portable size) when the device can co-schedule
     // one, else 8
+    CK(cudaFuncSetAttribute(k_small_attn<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, SlAttnSmem<1>::total));
+    CK(cudaFuncSetAttribute(k_small_attn<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, SlAttnSmem<2>::total));
+    CK(cudaFuncSetAttribute(k_small_attn<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, SlAttnSmem<4>::total));
+    CK(cudaFuncSetAttribute(k_small_attn<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, SlAttnSmem<8>::total));
+    CK(cudaFuncSetAttribute(k_small_mlp<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, SlMlpSmem<1>::total));
+    CK(cudaFuncSetAttribute(k_small_mlp<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, SlMlpSmem<2>::total));
+    CK(cudaFuncSetAttribute(k_small_mlp<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, SlMlpSmem<4>::total));
+    CK(cudaFuncSetAttribute(k_small_mlp<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, SlMlpSmem<8>::total));
+    // the SMs keep the full shared-memory split, so a launch's CTAs can be resident beside its
+    // predecessor's (programmatic dependent launch) rather than wait for an SM to reconfigure
+    for (const void *f : {(const void *)k_small_attn<1>, (const void *)k_small_attn<2>, (const void *)k_small_attn<4>,
+                          (const void *)k_small_attn<8>, (const void *)k_small_mlp<1>, (const void *)k_small_mlp<2>,
+                          (const void *)k_small_mlp<4>, (const void *)k_small_mlp<8>})
+        CK(cudaFuncSetAttribute(f, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared));
     CK(cudaFuncSetAttribute(k_local_fused<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, LfSmem<16>::total));
     CK(cudaFuncSetAttribute(k_local_fused<16>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
     CK(cudaFuncSetAttribute(k_local_fused<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, LfSmem<8>::total));
@@ -504,6 +521,24 @@ void Engine::launch_local_fused(int R, int step0, int step1) {
     mark(KK_LOCAL_FUSED);
 }
 
+void Engine::set_small_layers(int mode) {
+    if (mode < 0 || mode > 1) throw std::runtime_error("small layers must be 0 (five launches a layer) or 1 (two)");
+    if (mode == small_layers_) return;
+    small_layers_ = mode;
+    drop_graphs();
+}
+
+// captured sequences hold the launch shapes of the policy they were captured under
+void Engine::drop_graphs() {
+    CK(cudaStreamSynchronize(stream_));
+    for (auto &kv : graphs_) {
+        if (kv.second.exec) CK(cudaGraphExecDestroy(kv.second.exec));
+        for (cudaEvent_t ev : kv.second.events) CK(cudaEventDestroy(ev));
+    }
+    graphs_.clear();
+    last_graph_ = nullptr;
+}
+
 void Engine::set_gemm_path(int mode) {
     if (mode < 0 || mode > 3)
         throw std::runtime_error("gemm path must be 0 (auto), 1 (CUDA cores), 2 (tensor cores, fp16x3) or 3 (tensor "
@@ -517,14 +552,7 @@ void Engine::set_tc_policy(int direct_min_rows, int direct_rows) {
     if (direct_min_rows == tc_direct_min_rows_ && direct_rows == tc_direct_rows_) return;
     tc_direct_min_rows_ = direct_min_rows;
     tc_direct_rows_ = direct_rows;
-    // captured frames hold the old launch shapes
-    CK(cudaStreamSynchronize(stream_));
-    for (auto &kv : graphs_) {
-        if (kv.second.exec) CK(cudaGraphExecDestroy(kv.second.exec));
-        for (cudaEvent_t ev : kv.second.events) CK(cudaEventDestroy(ev));
-    }
-    graphs_.clear();
-    last_graph_ = nullptr;
+    drop_graphs();
 }
 
 bool Engine::use_tc(int R) const {
@@ -818,6 +846,8 @@ void Engine::check_device_error() {
     if (e != 0) {
         *h_err_ = 0;
         CK(cudaMemsetAsync(dev_err_, 0, sizeof(int), stream_));
+        // a step cut short may leave a small-batch residual accumulator non-zero
+        CK(cudaMemsetAsync(sd_, 0, size_t(3) * kSlMaxRows * kHidden * sizeof(long long), stream_));
         CK(cudaStreamSynchronize(stream_));
         const char *what = e == 7 || e == 8 ? "decode-attention page ring"
                            : (e >= 31 && e <= 33) ? "fused local decoder barrier"
@@ -945,6 +975,13 @@ void Engine::block(const Layer &L, int li, bool local, int R, const int *row_slo
 // 12 global layers over rows already embedded in x_ (row_pos = positions being written).
 void Engine::global_layers(int R, const int *row_slot, const int *row_pos) {
     pending_resid_ = nullptr;
+    lnf_xfix_ = nullptr;
+    if (small_layers_ && !in_prefill_ && !use_tc(R) && R <= kSlMaxRows) {  // decode rows, one per stream
+        plain_first_ = true;
+        for (int li = 0; li < kLayers; ++li) block_small(global_[li], li, R, row_slot, row_pos);
+        lnf_xfix_ = sd_;  // the layers' output is in D[0] after the 24 launches
+        return;
+    }
     if (pf_active_) {  // a prefill pass: the host-built flash-prefill plan is already on the device
         for (int li = 0; li < kLayers; ++li) block(global_[li], li, false, R, row_slot, row_pos, 0, x_);
         return;
@@ -959,6 +996,61 @@ void Engine::global_layers(int R, const int *row_slot, const int *row_pos) {
              plan_, desc_, work_, kLayers);
     mark(KK_PLAN);
     for (int li = 0; li < kLayers; ++li) block(global_[li], li, false, R, row_slot, row_pos, 0, x_);
+}
+
+// One global layer of a decode batch of R <= 8 rows (one row per stream) in two launches
+// (layer_small.cuh): attention half (launch p = 2 li) and MLP half (p = 2 li + 1), the residual
+// stream passed in the int64 accumulators D[p % 3] (launch 0 reads the embeddings in x_).
+void Engine::block_small(const Layer &L, int li, int R, const int *row_slot, const int *row_pos) {
+    long long *D[3];
+    for (int i = 0; i < 3; ++i) D[i] = sd_ + size_t(i) * kSlMaxRows * kHidden;
+    SmallArgs a{};
+    a.attn = qm(L.attn);
+    a.proj = qm(L.proj);
+    a.fc_in = qm(L.fc_in);
+    a.fc_out = qm(L.fc_out);
+    a.attn_b = L.attn_b;
+    a.proj_b = L.proj_b;
+    a.fc_in_b = L.fc_in_b;
+    a.fc_out_b = L.fc_out_b;
+    a.kv = kv_ + size_t(li) * n_pages_ * kPageHalfs;
+    a.page_table = page_table_;
+    a.pages_per_stream = pages_per_stream_;
+    a.row_slot = row_slot;
+    a.row_pos = row_pos;
+    a.rope = rope_;
+    a.R = R;
+    const int R2 = R <= 1 ? 1 : R <= 2 ? 2 : R <= 4 ? 4 : 8;
+    for (int half = 0; half < 2; ++half) {
+        const int p = 2 * li + half;
+        a.ln_w = half ? L.ln2_w : L.ln1_w;
+        a.ln_b = half ? L.ln2_b : L.ln1_b;
+        a.x0 = x_;
+        a.d_in = p == 0 ? nullptr : D[p % 3];
+        a.d_out = D[(p + 1) % 3];
+        a.d_zero = D[(p + 2) % 3];
+        // the first launch of a step follows host-to-device copies or the embedding kernel
+        const bool pdl = pdl_ && !(plain_first_ && p == 0);
+        const dim3 grid(kSlCtas), block(kSlThreads);
+        if (half == 0) {
+            switch (R2) {
+            case 1: launch_kc(pdl, kSlCluster, k_small_attn<1>, grid, block, SlAttnSmem<1>::total, stream_, a); break;
+            case 2: launch_kc(pdl, kSlCluster, k_small_attn<2>, grid, block, SlAttnSmem<2>::total, stream_, a); break;
+            case 4: launch_kc(pdl, kSlCluster, k_small_attn<4>, grid, block, SlAttnSmem<4>::total, stream_, a); break;
+            default: launch_kc(pdl, kSlCluster, k_small_attn<8>, grid, block, SlAttnSmem<8>::total, stream_, a); break;
+            }
+            mark(KK_SMALL_ATTN);
+        } else {
+            switch (R2) {
+            case 1: launch_kc(pdl, kSlCluster, k_small_mlp<1>, grid, block, SlMlpSmem<1>::total, stream_, a); break;
+            case 2: launch_kc(pdl, kSlCluster, k_small_mlp<2>, grid, block, SlMlpSmem<2>::total, stream_, a); break;
+            case 4: launch_kc(pdl, kSlCluster, k_small_mlp<4>, grid, block, SlMlpSmem<4>::total, stream_, a); break;
+            default: launch_kc(pdl, kSlCluster, k_small_mlp<8>, grid, block, SlMlpSmem<8>::total, stream_, a); break;
+            }
+            mark(KK_SMALL_MLP);
+        }
+    }
+    if (li == 0) plain_first_ = false;
 }
 
 // ------------------------------------------------------------------ host helpers
@@ -1185,13 +1277,16 @@ void Engine::prefill_batch(int n, const int32_t *sids, const int32_t *m_in, cons
         if (rows) launch_k(false, k_embed_rows, dim3(R), dim3(256), 0, stream_, tables(), rows17_, R, x_);
         pf_active_ = use_tc(R);
         if (pf_active_) plan_prefill_attention(R, slot, pos);
+        in_prefill_ = true;  // rows of one stream attend to each other: not the small-batch layers
         try {
             global_layers(R, d_ctl_, d_ctl_ + r_max_);
         } catch (...) {
             pf_active_ = false;
+            in_prefill_ = false;
             throw;
         }
         pf_active_ = false;
+        in_prefill_ = false;
         // ln_f of each stream's last row in this pass becomes its hidden state (llm.cpp:395-399),
         // all of them in one launch; the (row, slot) pairs go into rows17_, which the pass has
         // consumed (k_embed_rows ran before the layers on this stream)
@@ -1512,7 +1607,8 @@ void Engine::issue_frame(int R, bool run_global) {
         launch_k(pdl_, k_embed_frame, dim3(R), dim3(256), 0, stream_, tables(), used_, R, x_);
         mark(KK_EMBED);
         global_layers(R, d_slot, d_pos);
-        launch_k(pdl_, k_layernorm_rows, dim3(R), dim3(256), 0, stream_, x_, R, lnf_w_, lnf_b_, hidden_, d_slot, active_);
+        launch_k(pdl_, k_layernorm_rows, dim3(R), dim3(256), 0, stream_, x_, R, lnf_w_, lnf_b_, hidden_, d_slot, active_,
+                 lnf_xfix_);
         mark(KK_LNF);
     }
     launch_k(pdl_, k_frame_commit, dim3(1), dim3(256), 0, stream_, codes_, active_, R, run_global ? 1 : 0, d_ctl_ + off_pos(),
@@ -1524,7 +1620,8 @@ void Engine::issue_frame(int R, bool run_global) {
 // 12 global layers + ln_f on embeddings already in x_ (llm.cpp:248-255).
 void Engine::issue_global_embed(int R) {
     global_layers(R, d_ctl_ + off_slot(), d_ctl_ + off_pos());
-    launch_k(pdl_, k_layernorm_rows, dim3(R), dim3(256), 0, stream_, x_, R, lnf_w_, lnf_b_, hidden_, d_ctl_ + off_slot(), nullptr);
+    launch_k(pdl_, k_layernorm_rows, dim3(R), dim3(256), 0, stream_, x_, R, lnf_w_, lnf_b_, hidden_, d_ctl_ + off_slot(),
+             static_cast<const int *>(nullptr), lnf_xfix_);
     mark(KK_LNF);
 }
 
@@ -1536,7 +1633,7 @@ const char *kernel_kind_name(int kind) {
         "qkv_global", "attn_decode_paged", "proj_global", "fc_in_global", "fc_out_global", "ln_f",
         "qkv_local", "attn_local", "proj_local", "fc_in_local", "fc_out_local", "gate_w8a8",
         "audio_heads", "sample", "frame_commit", "build_activation_image", "attn_combine", "attn_prefill", "qkv_rope",
-        "local_decoder_fused"};
+        "local_decoder_fused", "small_layer_attn", "small_layer_mlp"};
     return (kind >= 0 && kind < KK_COUNT) ? names[kind] : "?";
 }
 

@@ -46,7 +46,7 @@ enum KernelKind {
     KK_PAGES, KK_GATHER, KK_LOOKUP, KK_EMBED, KK_PLAN,
     KK_QKV_G, KK_ATTN_DECODE, KK_PROJ_G, KK_FCIN_G, KK_FCOUT_G, KK_LNF,
     KK_QKV_L, KK_ATTN_LOCAL, KK_PROJ_L, KK_FCIN_L, KK_FCOUT_L, KK_GATE, KK_HEADS, KK_SAMPLE, KK_COMMIT,
-    KK_BIMG, KK_ATTN_COMBINE, KK_ATTN_PREFILL, KK_QKV_ROPE, KK_LOCAL_FUSED,
+    KK_BIMG, KK_ATTN_COMBINE, KK_ATTN_PREFILL, KK_QKV_ROPE, KK_LOCAL_FUSED, KK_SMALL_ATTN, KK_SMALL_MLP,
     KK_COUNT
 };
 const char *kernel_kind_name(int kind);
@@ -104,6 +104,9 @@ public:
     // kernels for every frame (default: measured as fast at 64 streams and faster above).
     void set_local_path(int mode);
     int local_cluster() const { return lf_cluster_; }
+    // Global layers of decode batches of at most kGemvMaxRows rows: 1 = two launches per layer
+    // (layer_small.cuh, the default), 0 = the five CUDA-core GEMV / attention launches.
+    void set_small_layers(int mode);
     void set_cuda_stream(void *s);
     void fill_state_random(int sid, int n_pos, uint64_t seed);
     void set_kernel_timing(bool on);
@@ -141,8 +144,10 @@ private:
     void block(const Layer &L, int li, bool local, int R, const int *row_slot, const int *row_pos, int lpos, float *x);
     bool use_tc(int R) const;
     void block_tc(const Layer &L, int li, bool local, int R, const int *row_slot, const int *row_pos, int lpos, float *x);
+    void block_small(const Layer &L, int li, int R, const int *row_slot, const int *row_pos);
     void heads_tc(int ch, int R);
     void check_device_error();
+    void drop_graphs();
     void global_layers(int R, const int *row_slot, const int *row_pos);
     void issue_frame(int R, bool run_global);
     void issue_global_embed(int R);
@@ -222,6 +227,13 @@ private:
     int *dev_err_ = nullptr;       // [0]: kernels' time-out flag; [1]: fault-injection word
     int *h_err_ = nullptr;         // pinned host copy of it
     int gemm_path_ = 0;
+    // small-batch layers: the three int64 residual accumulators D ([3][kGemvMaxRows][768]);
+    // lnf_xfix_ is the one the ln_f after the layers reads its rows from (null on the other
+    // paths, whose rows are in x_)
+    int small_layers_ = 1;
+    bool in_prefill_ = false;
+    long long *sd_ = nullptr;
+    const long long *lnf_xfix_ = nullptr;
     int local_path_ = 1;     // set_local_path (the fused kernel is opt-in)
     int lf_cluster_ = 0;     // CTAs per cluster of the fused local decoder (16 or 8; 0 = unavailable)
     bool frame_fused_ = false;  // the frame being issued runs the fused local decoder

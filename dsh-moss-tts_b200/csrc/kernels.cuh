@@ -37,6 +37,11 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
+// Residual accumulators of the small-batch layers (layer_small.cuh): int64 in units of 2^-32,
+// summed with integer atomics so that the result does not depend on the order of the adds.
+__device__ __forceinline__ long long float_to_fixed(float v) { return __double2ll_rn((double)v * 4294967296.0); }
+__device__ __forceinline__ float fixed_to_float(long long s) { return (float)((double)s * (1.0 / 4294967296.0)); }
+
 __device__ __forceinline__ int4 ldg_stream(const void *p) {
     int4 r;
     asm volatile("ld.global.nc.L1::no_allocate.v4.s32 {%0,%1,%2,%3}, [%4];"
@@ -1074,15 +1079,18 @@ __global__ void k_lookup_rows(const QMat m, int row, int R, float *__restrict__ 
 
 // out[r] = LN(x[r]) for rows whose commit flag is set (all rows when commit is null);
 // also copies the result to out2[r] when given.
+// xfix (nullable): the rows come from the int64 residual accumulators of the small-batch
+// layers (2^-32 units) instead of x
 __global__ void k_layernorm_rows(const float *__restrict__ x, int R, const float *__restrict__ w,
                                  const float *__restrict__ b, float *__restrict__ out, const int *__restrict__ out_index,
-                                 const int *__restrict__ commit) {
+                                 const int *__restrict__ commit, const long long *__restrict__ xfix) {
     __shared__ float xs[kHidden];
     pdl_enter();
     const int r = blockIdx.x;
     if (r >= R) return;
     if (commit && !commit[r]) return;
-    for (int c = threadIdx.x; c < kHidden; c += blockDim.x) xs[c] = x[(size_t)r * kHidden + c];
+    for (int c = threadIdx.x; c < kHidden; c += blockDim.x)
+        xs[c] = xfix ? fixed_to_float(xfix[(size_t)r * kHidden + c]) : x[(size_t)r * kHidden + c];
     __syncthreads();
     if (threadIdx.x < 32) warp_layernorm(xs, w, b);
     __syncthreads();

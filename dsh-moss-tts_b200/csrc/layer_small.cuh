@@ -1,0 +1,774 @@
+// layer_small.cuh -- one global transformer layer (llm.cpp:230-246) for decode batches of at
+// most 8 rows, in two launches instead of five.
+//
+// At this batch the layer is a chain of dependent phases, each too small to keep HBM busy, so
+// its time is the hand-offs between them.  Two launches per layer keep only the hand-offs that
+// need the whole layer's output (proj and fc_out read every head / every feature); the rest
+// run inside a thread-block cluster, synchronised by cluster barriers and exchanging data
+// through distributed shared memory (DSMEM).  Everything that does not depend on the previous
+// launch -- the weights, LayerNorm parameters, biases, RoPE factors and the rows' cached K/V
+// pages -- is copied into shared memory before the launch waits for its predecessor
+// (programmatic dependent launch), so those HBM reads overlap the previous launch.  Global
+// stores come after a CTA's last cluster-barrier arrive, so no barrier waits for them.
+//
+// Launch A (k_small_attn), 12 clusters of 8 CTAs, cluster = attention head hd, CTA rank c:
+//   x in; LN1 (every CTA, redundantly); QKV rows for dims 8c..8c+7 of q, k and v of the head
+//   (24 weight rows) with bias and RoPE; q, k, v gathered over DSMEM; attention over pages
+//   c, c+8, ... of each row (online softmax); the 8 partial results merged over DSMEM; proj
+//   rows 96c..96c+95 over the head's 64 columns added into the accumulator; the CTA's k, v
+//   dims appended to the KV cache.
+// Launch B (k_small_mlp), 12 clusters of 8 CTAs, CTA j = blockIdx.x (features 32j..32j+31):
+//   x in; LN2; fc_in rows 32j.. + bias + gelu_new; fc_out column block j (a partial sum of
+//   every output row); the cluster's 8 partials reduced over DSMEM (CTA c: rows 96c..96c+95)
+//   and added into the accumulator.
+//
+// The residual stream between launches is an int64 accumulator per row element in units of
+// 2^-32 (|x| < 2^31), to which the launches add with atomic adds.  Integer addition is
+// associative, so the sum does not depend on the order of the adds and every run gives the
+// same bits.  Launch p of a step (p = 2 * layer + {0: A, 1: B}) reads x from D[p % 3] (launch
+// 0: from the fp32 embedding rows), adds x' = x + its output into D[(p + 1) % 3] -- the CTAs
+// that add the biases (head 0, cluster 0) also add x for their rows -- and zeroes
+// D[(p + 2) % 3], which launch p + 1 adds into.  After 24 launches D[0] holds the layers'
+// output, which the ln_f kernel reads; D[1] is zero again for the next step.
+#pragma once
+
+#include "kernels.cuh"
+#include "gemm_tc.cuh"
+
+namespace mossgpu {
+namespace {
+
+constexpr int kSlThreads = 256;
+constexpr int kSlCluster = 8;
+constexpr int kSlMaxRows = 8;
+constexpr int kSlCtas = 96;            // both launches: 12 clusters of 8
+constexpr int kSlRow = kHidden + 96;   // a row in shared memory: 32-float blocks 36 floats apart
+static_assert(kHeads * kSlCluster == kSlCtas && kFF / 32 == kSlCtas, "layer split");
+
+// (row, page) K/V pairs a CTA stages in shared memory (4 KB each); fewer at 8 rows, so that a
+// launch's CTAs fit on an SM beside its predecessor's
+__host__ __device__ constexpr int sl_kv_slots(int maxr) { return maxr >= 8 ? 8 : 16; }
+
+// column c of a row -> its place in shared memory: lanes that read the same 16 bytes of 8
+// consecutive 128-byte blocks then hit 8 different 4-bank groups
+__device__ __forceinline__ int sl_pad(int c) { return c + ((c >> 5) << 2); }
+
+struct SmallArgs {
+    QMat attn, proj, fc_in, fc_out;
+    const float *attn_b, *proj_b, *fc_in_b, *fc_out_b;
+    const float *ln_w, *ln_b;   // LN1 (launch A) or LN2 (launch B)
+    const float *x0;            // launch 0: the embedding rows [R][768] (fp32)
+    const long long *d_in;      // D[p % 3], [8][768] (launches 1..23)
+    long long *d_out;           // D[(p + 1) % 3]
+    long long *d_zero;          // D[(p + 2) % 3]
+    __half *kv;                 // this layer's KV pages
+    const int *page_table;
+    int pages_per_stream;
+    const int *row_slot, *row_pos;
+    const float2 *rope;
+    int R;
+};
+
+__device__ __forceinline__ void sl_cp16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void sl_cp8(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void sl_cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void sl_cp_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+__device__ __forceinline__ float sl_ld_cluster(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
+}
+__device__ __forceinline__ float4 sl_ld_cluster4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr) : "memory");
+    return v;
+}
+__device__ __forceinline__ void sl_add_fixed(long long *p, long long v) {
+    atomicAdd(reinterpret_cast<unsigned long long *>(p), static_cast<unsigned long long>(v));
+}
+
+// x of rows < R into xs (padded rows), and, for a CTA that adds rows base..base+95 of the
+// output with their bias (xfix != null), those rows of x as fixed point into xfix[r][96]
+__device__ __forceinline__ void sl_residual_in(const SmallArgs &a, float *xs, long long *xfix, int base, int tid) {
+    const int R = a.R;
+    for (int i = tid; i < R * (kHidden / 4); i += kSlThreads) {
+        const int r = i / (kHidden / 4), q4 = i - r * (kHidden / 4);
+        const bool mine = xfix && (unsigned)(4 * q4 - base) < 96u;
+        long long *f = xfix + r * 96 + 4 * q4 - base;
+        float4 v;
+        if (a.d_in) {
+            const longlong2 *dp = reinterpret_cast<const longlong2 *>(a.d_in + (size_t)r * kHidden) + 2 * q4;
+            const longlong2 d0 = dp[0], d1 = dp[1];
+            v = make_float4(fixed_to_float(d0.x), fixed_to_float(d0.y), fixed_to_float(d1.x), fixed_to_float(d1.y));
+            if (mine) {  // the accumulator's own value, exactly
+                f[0] = d0.x;
+                f[1] = d0.y;
+                f[2] = d1.x;
+                f[3] = d1.y;
+            }
+        } else {
+            v = reinterpret_cast<const float4 *>(a.x0 + (size_t)r * kHidden)[q4];
+            if (mine) {
+                f[0] = float_to_fixed(v.x);
+                f[1] = float_to_fixed(v.y);
+                f[2] = float_to_fixed(v.z);
+                f[3] = float_to_fixed(v.w);
+            }
+        }
+        *reinterpret_cast<float4 *>(xs + r * kSlRow + sl_pad(4 * q4)) = v;
+    }
+}
+
+// LayerNorm of rows < R of xs in place (llm.cpp:159-171): TPR = 256 / MAXR threads a row, each
+// with E = 768 / TPR columns; two reductions (sum, then squared deviations) over the thread's
+// columns, the warp and the row's warps (red: 8 floats).  Every thread of the CTA calls it.
+template <int MAXR>
+__device__ __forceinline__ void sl_layernorm(float *xs, int R, const float *w, const float *b, float *red, int tid) {
+    constexpr int TPR = kSlThreads / MAXR, WPR = TPR / 32, E = kHidden / TPR;
+    const int r = tid / TPR, j = tid - r * TPR, lane = tid & 31, wr = j >> 5;
+    const bool on = r < R;
+    float *row = xs + r * kSlRow;
+    float v[E];
+    float s = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        v[e] = on ? row[sl_pad(j + e * TPR)] : 0.f;
+        s += v[e];
+    }
+    s = warp_sum(s);
+    if (WPR > 1) {
+        if (lane == 0) red[r * WPR + wr] = s;
+        __syncthreads();
+        s = 0.f;
+#pragma unroll
+        for (int q = 0; q < WPR; ++q) s += red[r * WPR + q];
+    }
+    const float mean = __fdiv_rn(s, (float)kHidden);
+    float d2 = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        const float d = v[e] - mean;
+        d2 = fmaf(d, d, d2);
+    }
+    d2 = warp_sum(d2);
+    if (WPR > 1) {
+        __syncthreads();  // every thread has read the sums
+        if (lane == 0) red[r * WPR + wr] = d2;
+        __syncthreads();
+        d2 = 0.f;
+#pragma unroll
+        for (int q = 0; q < WPR; ++q) d2 += red[r * WPR + q];
+    }
+    const float var = __fdiv_rn(d2, (float)kHidden);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(var + 1e-5f));
+    if (on) {
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+            const int col = j + e * TPR;
+            row[sl_pad(col)] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[e], mean), inv), w[col]), b[col]);
+        }
+    }
+}
+
+// 4 weight rows (one Q8_0_4X4 group, K = 768, in shared memory) times the rows' activations
+// (padded rows): lane l reads 16 bytes of every 128-byte block (row (l % 8) / 2, half l % 2), 6
+// chunks a lane; the 8 lanes of a row reduce by shuffles.  Returns the row sums in lanes 0, 2,
+// 4, 6 (weight row lane / 2).
+template <int MAXR>
+__device__ __forceinline__ void sl_group_dot(const int8_t *wg, const __half *sg, const float *xs, int R, int lane,
+                                             float (&acc)[MAXR]) {
+    const int k = (lane & 7) >> 1, h = lane & 1;
+#pragma unroll
+    for (int r = 0; r < MAXR; ++r) acc[r] = 0.f;
+#pragma unroll
+    for (int u = 0; u < 6; ++u) {
+        const int i = lane + 32 * u;
+        const int b = i >> 3;
+        const int4 q = *reinterpret_cast<const int4 *>(wg + i * 16);
+        const float d = __half2float(sg[b * 4 + k]);
+        float wf[16];
+        unpack16(q, wf);
+        const int xoff = b * 36 + h * 16;
+#pragma unroll
+        for (int r = 0; r < MAXR; ++r) {
+            if (r < R) {
+                const float4 *xv = reinterpret_cast<const float4 *>(xs + r * kSlRow + xoff);
+                float s = 0.f;
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    const float4 xx = xv[t];
+                    s = fmaf(wf[4 * t + 0], xx.x, s);
+                    s = fmaf(wf[4 * t + 1], xx.y, s);
+                    s = fmaf(wf[4 * t + 2], xx.z, s);
+                    s = fmaf(wf[4 * t + 3], xx.w, s);
+                }
+                acc[r] = fmaf(s, d, acc[r]);
+            }
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < MAXR; ++r) {
+        float v = acc[r];
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 8);
+        v += __shfl_xor_sync(0xffffffffu, v, 16);
+        acc[r] = v;
+    }
+}
+
+// One weight row's 32 int8 values (a block, in shared memory) dotted with 32 activations of
+// each row, times the block scale.
+template <int MAXR>
+__device__ __forceinline__ void sl_block_dot(const int8_t *w32, float d, const float *act, int act_stride, int R,
+                                             float (&out)[MAXR]) {
+    float wf[32];
+    unpack16(*reinterpret_cast<const int4 *>(w32), wf);
+    unpack16(*reinterpret_cast<const int4 *>(w32 + 16), wf + 16);
+#pragma unroll
+    for (int r = 0; r < MAXR; ++r) {
+        out[r] = 0.f;
+        if (r < R) {
+            const float4 *av = reinterpret_cast<const float4 *>(act + r * act_stride);
+            float s = 0.f;
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+                const float4 xx = av[t];
+                s = fmaf(wf[4 * t + 0], xx.x, s);
+                s = fmaf(wf[4 * t + 1], xx.y, s);
+                s = fmaf(wf[4 * t + 2], xx.z, s);
+                s = fmaf(wf[4 * t + 3], xx.w, s);
+            }
+            out[r] = s * d;
+        }
+    }
+}
+
+// ------------------------------------------------------------------ launch A: attention half
+
+template <int MAXR>
+struct SlAttnSmem {
+    static constexpr int kSlots = sl_kv_slots(MAXR);
+    static constexpr int wq = 0;                               // int8 [6 groups][24 blocks][128]
+    static constexpr int wqs = wq + 6 * 3072;                  // half [6][24][4]
+    static constexpr int wp = wqs + 6 * 192;                   // int8 [24 groups][2 blocks][128]
+    static constexpr int wps = wp + 24 * 256;                  // half [24][2][4]
+    static constexpr int lnw = wps + 24 * 16;                  // float [768] LN1 weight, bias
+    static constexpr int lnb = lnw + kHidden * 4;
+    static constexpr int bq = lnb + kHidden * 4;               // float [24] QKV bias of the CTA's rows
+    static constexpr int bp = bq + 24 * 4;                     // float [96] proj bias of its rows
+    static constexpr int rs = bp + 96 * 4;                     // float2 [8][4] RoPE (cos, sin)
+    static constexpr int meta = rs + kSlMaxRows * 4 * 8;       // int [5][8]: pos, slot, pages, first item, page of pos
+    static constexpr int red = meta + 5 * kSlMaxRows * 4;      // float [8] LayerNorm partial sums
+    static constexpr int xs = red + 8 * 4;                     // float [MAXR][kSlRow] x, then LN1(x)
+    static constexpr int xfix = xs + MAXR * kSlRow * 4;        // int64 [MAXR][96] x of the proj rows (head 0)
+    static constexpr int own = xfix + MAXR * 96 * 8;           // float [MAXR][24] q, k, v dims 8c..8c+7
+    static constexpr int full = own + MAXR * 24 * 4;           // float [MAXR][192] the head's q | k | v
+    static constexpr int newkv = full + MAXR * 192 * 4;        // half [MAXR][2][64] k, v of the new position
+    static constexpr int wst = newkv + MAXR * 256;             // float [8 warps][68] m, l, -, -, o[64]
+    static constexpr int part = wst + 8 * kPartStride * 4;     // float [MAXR][68] the CTA's partial
+    static constexpr int oh = part + MAXR * kPartStride * 4;   // float [MAXR][64] attention output
+    static constexpr int kvs = oh + MAXR * kHeadDim * 4;       // half [slots][k|v][16][64]
+    static constexpr int total = kvs + kSlots * 4096;
+    static_assert(rs % 16 == 0 && xs % 16 == 0 && xfix % 16 == 0 && own % 16 == 0 && full % 16 == 0 &&
+                      newkv % 16 == 0 && part % 16 == 0 && oh % 16 == 0 && kvs % 16 == 0,
+                  "16-byte aligned regions");
+};
+
+template <int MAXR>
+__global__ void __launch_bounds__(kSlThreads) k_small_attn(const SmallArgs a) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    using S = SlAttnSmem<MAXR>;
+    uint8_t *sm = smem_raw;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int c = (int)cluster_rank();
+    const int hd = blockIdx.x / kSlCluster;
+    const int R = a.R;
+    int *m_pos = reinterpret_cast<int *>(sm + S::meta);
+    int *m_slot = m_pos + kSlMaxRows, *m_cnt = m_pos + 2 * kSlMaxRows, *m_first = m_pos + 3 * kSlMaxRows;
+    int *m_page = m_pos + 4 * kSlMaxRows;
+    float *xs = reinterpret_cast<float *>(sm + S::xs);
+    long long *xfix = reinterpret_cast<long long *>(sm + S::xfix);
+    float *own = reinterpret_cast<float *>(sm + S::own);
+    float *full = reinterpret_cast<float *>(sm + S::full);
+    __half *newkv = reinterpret_cast<__half *>(sm + S::newkv);
+    float *wst = reinterpret_cast<float *>(sm + S::wst);
+    float *part = reinterpret_cast<float *>(sm + S::part);
+    float *oh = reinterpret_cast<float *>(sm + S::oh);
+    const float *bq = reinterpret_cast<const float *>(sm + S::bq);
+    const float *bp = reinterpret_cast<const float *>(sm + S::bp);
+    const float2 *rs = reinterpret_cast<const float2 *>(sm + S::rs);
+
+    // ---- 0. before the wait: everything that does not depend on the previous launch.  The
+    //      per-row control (slot, position, page table) was written by the host or by a kernel
+    //      at least two launches back, so it is visible here as the weights are.
+    if (tid < kSlMaxRows) {
+        int pos = 0, slot = 0, cnt = 0, page = 0;
+        if (tid < R) {
+            pos = a.row_pos[tid];
+            slot = a.row_slot[tid];
+            const int last = pos / kPage;
+            cnt = c <= last ? (last - c) / kSlCluster + 1 : 0;  // pages c, c + 8, ... <= last
+            page = a.page_table[(size_t)slot * a.pages_per_stream + last];
+        }
+        m_pos[tid] = pos;
+        m_slot[tid] = slot;
+        m_cnt[tid] = cnt;
+        m_page[tid] = page;
+    }
+    const int gq0 = (hd * kHeadDim + 8 * c) / 4;  // first Q8 group of the CTA's q rows
+    // QKV: groups gq0, gq0 + 1 of q, k and v (group g + 192 * part), 3072 B of quants each
+    for (int i = tid; i < 6 * 192; i += kSlThreads) {
+        const int gi = i / 192, ch = i - gi * 192;
+        const size_t g = (size_t)(gi >> 1) * (kHidden / 4) + gq0 + (gi & 1);
+        sl_cp16(sm + S::wq + gi * 3072 + ch * 16, a.attn.qs + g * 3072 + ch * 16);
+    }
+    for (int i = tid; i < 6 * 12; i += kSlThreads) {
+        const int gi = i / 12, ch = i - gi * 12;
+        const size_t g = (size_t)(gi >> 1) * (kHidden / 4) + gq0 + (gi & 1);
+        sl_cp16(sm + S::wqs + gi * 192 + ch * 16, reinterpret_cast<const uint8_t *>(a.attn.sc) + g * 192 + ch * 16);
+    }
+    // proj: rows 96c.. (groups 24c..24c+23), blocks 2hd and 2hd + 1 (the head's columns)
+    for (int i = tid; i < 24 * 16; i += kSlThreads) {
+        const int gl = i >> 4, ch = i & 15;
+        const size_t blk = (size_t)(24 * c + gl) * (kHidden / 32) + 2 * hd;
+        sl_cp16(sm + S::wp + gl * 256 + ch * 16, a.proj.qs + blk * 128 + ch * 16);
+    }
+    if (tid < 24) {
+        const size_t blk = (size_t)(24 * c + tid) * (kHidden / 32) + 2 * hd;
+        sl_cp16(sm + S::wps + tid * 16, reinterpret_cast<const uint8_t *>(a.proj.sc) + blk * 8);
+    }
+    for (int i = tid; i < 2 * (kHidden / 4); i += kSlThreads) {
+        const int ch = i % (kHidden / 4);
+        if (i < kHidden / 4) sl_cp16(sm + S::lnw + ch * 16, a.ln_w + ch * 4);
+        else sl_cp16(sm + S::lnb + ch * 16, a.ln_b + ch * 4);
+    }
+    if (tid < 6) {  // QKV bias: rows part * 768 + hd * 64 + 8c + 4 (tid & 1) ..
+        const int off = (tid >> 1) * kHidden + hd * kHeadDim + 8 * c + 4 * (tid & 1);
+        sl_cp16(sm + S::bq + tid * 16, a.attn_b + off);
+    } else if (tid < 30) {
+        sl_cp16(sm + S::bp + (tid - 6) * 16, a.proj_b + 96 * c + 4 * (tid - 6));
+    }
+    __syncthreads();  // m_* written
+    if (tid < MAXR * 4) {  // RoPE factors of the CTA's 4 q/k pairs (pair index 4c..4c+3)
+        const int r = tid >> 2;
+        if (r < R) sl_cp8(sm + S::rs + tid * 8, a.rope + (size_t)m_pos[r] * (kHeadDim / 2) + 4 * c + (tid & 3));
+    }
+    if (tid == 0) {
+        int first = 0;
+        for (int r = 0; r < kSlMaxRows; ++r) {
+            m_first[r] = first;
+            first += m_cnt[r];
+        }
+    }
+    // the rows' cached K/V pages of this CTA (item t = (row, page c + 8i), row-major): the
+    // head's 2 KB of k and 2 KB of v per page; the page holding the new position is stale
+    // at that position, which is never read from here
+    {
+        int t = 0;
+        for (int r = 0; r < R && t < S::kSlots; ++r) {
+            const int cnt = m_cnt[r];
+            for (int i = 0; i < cnt && t < S::kSlots; ++i, ++t) {
+                const int page = a.page_table[(size_t)m_slot[r] * a.pages_per_stream + c + kSlCluster * i];
+                const __half *src = a.kv + (size_t)page * kPageHalfs + (size_t)((tid >> 7) * kHeads + hd) * kPage * kHeadDim;
+                sl_cp16(sm + S::kvs + t * 4096 + tid * 16, reinterpret_cast<const uint8_t *>(src) + (tid & 127) * 16);
+            }
+        }
+    }
+    sl_cp_commit();
+
+    pdl_wait();
+    pdl_trigger();
+
+    // ---- 1. x in (head 0 keeps its proj rows of x for the accumulator), LN1
+    sl_residual_in(a, xs, hd == 0 ? xfix : nullptr, 96 * c, tid);
+    sl_cp_wait_all();
+    __syncthreads();
+    sl_layernorm<MAXR>(xs, R, reinterpret_cast<const float *>(sm + S::lnw), reinterpret_cast<const float *>(sm + S::lnb),
+                       reinterpret_cast<float *>(sm + S::red), tid);
+    __syncthreads();
+
+    // ---- 2. the CTA's 24 QKV rows: warp gi = group gi (q, q, k, k, v, v)
+    if (warp < 6) {
+        float acc[MAXR];
+        sl_group_dot<MAXR>(reinterpret_cast<const int8_t *>(sm + S::wq) + warp * 3072,
+                           reinterpret_cast<const __half *>(sm + S::wqs) + warp * 96, xs, R, lane, acc);
+        if (lane < 8 && (lane & 1) == 0) {
+#pragma unroll
+            for (int r = 0; r < MAXR; ++r)
+                if (r < R) own[r * 24 + warp * 4 + (lane >> 1)] = acc[r];
+        }
+    }
+    __syncthreads();
+    // bias and RoPE (pairs 2i, 2i+1 of q and k; EPI_QKV order), in place: own[r][part * 8 + j]
+    if (tid < 12 * R) {
+        const int r = tid / 12, pr = tid - r * 12;
+        const int prt = pr >> 2, j = (pr & 3) * 2;
+        float *o = own + r * 24 + prt * 8 + j;
+        const float v0 = __fadd_rn(o[0], bq[prt * 8 + j]);
+        const float v1 = __fadd_rn(o[1], bq[prt * 8 + j + 1]);
+        float o0 = v0, o1 = v1;
+        if (prt < 2) {
+            const float2 cs = rs[r * 4 + (j >> 1)];
+            o0 = __fsub_rn(__fmul_rn(v0, cs.x), __fmul_rn(v1, cs.y));
+            o1 = __fadd_rn(__fmul_rn(v1, cs.x), __fmul_rn(v0, cs.y));
+        }
+        o[0] = o0;
+        o[1] = o1;
+    }
+    __syncthreads();
+    cluster_arrive();
+    cluster_wait();
+
+    // ---- 3. the head's q, k, v from the 8 CTAs; the new position's k, v as the cache holds them
+    for (int i = tid; i < R * 48; i += kSlThreads) {  // (row, part, source CTA, 4-float half)
+        const int r = i / 48, e = i - r * 48;
+        const int prt = e >> 4, src = (e >> 1) & 7, hf = e & 1;
+        const float4 v = sl_ld_cluster4(cluster_map(smem_u32(own + r * 24 + prt * 8 + hf * 4), (uint32_t)src));
+        *reinterpret_cast<float4 *>(full + r * 192 + prt * kHeadDim + src * 8 + hf * 4) = v;
+        if (prt > 0) {
+            __half2 *nk = reinterpret_cast<__half2 *>(newkv + r * 128 + (prt - 1) * kHeadDim + src * 8 + hf * 4);
+            nk[0] = __floats2half2_rn(v.x, v.y);
+            nk[1] = __floats2half2_rn(v.z, v.w);
+        }
+    }
+    __syncthreads();
+
+    // ---- 4. attention over this CTA's pages: warp w takes row w / WPR, items sub, sub + WPR,
+    //      ...; lanes as in k_attn_rows (8 lanes a position, 8 dims a lane, 4 positions a step)
+    constexpr int WPR = 8 / MAXR;
+    {
+        const int r = warp / WPR, sub = warp - r * WPR;
+        const int ps = lane >> 3, ds = lane & 7;
+        float m = -INFINITY, l = 0.f, o[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = 0.f;
+        if (r < R) {
+            const int pos = m_pos[r];
+            float qv[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) qv[j] = full[r * 192 + ds * 8 + j] * 0.125f;
+            const int4 nk = *reinterpret_cast<const int4 *>(newkv + r * 128 + ds * 8);
+            const int4 nv = *reinterpret_cast<const int4 *>(newkv + r * 128 + kHeadDim + ds * 8);
+            const __half *kvs = reinterpret_cast<const __half *>(sm + S::kvs);
+            for (int i = sub; i < m_cnt[r]; i += WPR) {
+                const int pg = c + kSlCluster * i;
+                const int t = m_first[r] + i;
+                const __half *kb, *vb;
+                if (t < S::kSlots) {
+                    kb = kvs + (size_t)t * 2048;
+                    vb = kb + kPage * kHeadDim;
+                } else {
+                    const int page = a.page_table[(size_t)m_slot[r] * a.pages_per_stream + pg];
+                    kb = a.kv + (size_t)page * kPageHalfs + (size_t)hd * kPage * kHeadDim;
+                    vb = kb + (size_t)kHeads * kPage * kHeadDim;
+                }
+                kb += ds * 8;
+                vb += ds * 8;
+                const int pb = pg * kPage;
+                int4 kr[4], vr[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int p = pb + ps + 4 * u;
+                    if (p < pos) {
+                        kr[u] = *reinterpret_cast<const int4 *>(kb + (ps + 4 * u) * kHeadDim);
+                        vr[u] = *reinterpret_cast<const int4 *>(vb + (ps + 4 * u) * kHeadDim);
+                    } else if (p == pos) {
+                        kr[u] = nk;
+                        vr[u] = nv;
+                    } else {
+                        kr[u] = make_int4(0, 0, 0, 0);
+                        vr[u] = make_int4(0, 0, 0, 0);
+                    }
+                }
+                float sc[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const __half2 *kh = reinterpret_cast<const __half2 *>(&kr[u]);
+                    float dd = 0.f;
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 kf = __half22float2(kh[e]);
+                        dd = fmaf(qv[2 * e], kf.x, dd);
+                        dd = fmaf(qv[2 * e + 1], kf.y, dd);
+                    }
+                    sc[u] = dd;
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], 1);
+                    sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], 2);
+                    sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], 4);
+                    if (pb + ps + 4 * u > pos) sc[u] = -INFINITY;
+                }
+                const float mn = fmaxf(fmaxf(m, fmaxf(sc[0], sc[1])), fmaxf(sc[2], sc[3]));
+                if (mn != -INFINITY) {
+                    const float corr = __expf(m - mn);
+                    float pw[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) pw[u] = __expf(sc[u] - mn);
+                    l = l * corr + ((pw[0] + pw[1]) + (pw[2] + pw[3]));
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) o[e] *= corr;
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const __half2 *vh = reinterpret_cast<const __half2 *>(&vr[u]);
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const float2 vf = __half22float2(vh[e]);
+                            o[2 * e] = fmaf(pw[u], vf.x, o[2 * e]);
+                            o[2 * e + 1] = fmaf(pw[u], vf.y, o[2 * e + 1]);
+                        }
+                    }
+                    m = mn;
+                }
+            }
+        }
+        // merge the warp's 4 position groups (lanes ds, ds + 8, ds + 16, ds + 24)
+#pragma unroll
+        for (int off = 8; off <= 16; off <<= 1) {
+            const float mo = __shfl_xor_sync(0xffffffffu, m, off);
+            const float lo2 = __shfl_xor_sync(0xffffffffu, l, off);
+            const float mx = fmaxf(m, mo);
+            const float c1 = (m == -INFINITY) ? 0.f : __expf(m - mx);
+            const float c2 = (mo == -INFINITY) ? 0.f : __expf(mo - mx);
+            l = l * c1 + lo2 * c2;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float oo = __shfl_xor_sync(0xffffffffu, o[j], off);
+                o[j] = o[j] * c1 + oo * c2;
+            }
+            m = mx;
+        }
+        if (lane < 8) {
+            float *w = wst + warp * kPartStride;
+            if (lane == 0) {
+                w[0] = m;
+                w[1] = l;
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) w[4 + ds * 8 + j] = o[j];
+        }
+    }
+    __syncthreads();
+    // the CTA's partial of each row: its WPR warps merged (a warp with no page: m = -inf)
+    for (int i = tid; i < R * kHeadDim; i += kSlThreads) {
+        const int r = i / kHeadDim, d = i - r * kHeadDim;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < WPR; ++w) M = fmaxf(M, wst[(r * WPR + w) * kPartStride]);
+        float L = 0.f, y = 0.f;
+#pragma unroll
+        for (int w = 0; w < WPR; ++w) {
+            const float *ws = wst + (r * WPR + w) * kPartStride;
+            const float wgt = ws[0] == -INFINITY ? 0.f : __expf(ws[0] - M);
+            L = fmaf(ws[1], wgt, L);
+            y = fmaf(ws[4 + d], wgt, y);
+        }
+        float *p = part + r * kPartStride;
+        if (d == 0) {
+            p[0] = M;
+            p[1] = L;
+        }
+        p[4 + d] = y;
+    }
+    __syncthreads();
+    cluster_arrive();
+    cluster_wait();
+
+    // ---- 5. the 8 CTAs' partials merged (every CTA, for its proj rows)
+    for (int i = tid; i < R * kHeadDim; i += kSlThreads) {
+        const int r = i / kHeadDim, d = i - r * kHeadDim;
+        const uint32_t base = smem_u32(part + r * kPartStride);
+        float pm[kSlCluster], pl[kSlCluster], po[kSlCluster];
+        float M = -INFINITY;
+#pragma unroll
+        for (int s = 0; s < kSlCluster; ++s) {
+            const uint32_t ra = cluster_map(base, (uint32_t)s);
+            pm[s] = sl_ld_cluster(ra);
+            pl[s] = sl_ld_cluster(ra + 4);
+            po[s] = sl_ld_cluster(ra + 16 + 4 * d);
+            M = fmaxf(M, pm[s]);
+        }
+        float L = 0.f, y = 0.f;
+#pragma unroll
+        for (int s = 0; s < kSlCluster; ++s) {
+            const float wgt = pm[s] == -INFINITY ? 0.f : __expf(pm[s] - M);
+            L = fmaf(pl[s], wgt, L);
+            y = fmaf(po[s], wgt, y);
+        }
+        oh[r * kHeadDim + d] = y / L;
+    }
+    cluster_arrive();  // done with the other CTAs' shared memory (waited for before exiting)
+    __syncthreads();
+
+    // ---- 6. proj rows 96c..96c+95 over the head's 64 columns (thread: row, block half) into
+    //      the accumulator (head 0 adds x and the bias); then this CTA's global stores: its
+    //      k, v dims of the new position into the KV cache, its 8 columns of D[(p + 2) % 3]
+    if (tid < 192) {
+        const int ol = tid >> 1, bb = tid & 1;
+        const int gl = ol >> 2, k = ol & 3;
+        const int8_t *w32 = reinterpret_cast<const int8_t *>(sm + S::wp) + gl * 256 + bb * 128 + k * 32;
+        const float d = __half2float(reinterpret_cast<const __half *>(sm + S::wps)[gl * 8 + bb * 4 + k]);
+        float v[MAXR];
+        sl_block_dot<MAXR>(w32, d, oh + bb * 32, kHeadDim, R, v);
+#pragma unroll
+        for (int r = 0; r < MAXR; ++r) {
+            const float s = v[r] + __shfl_xor_sync(0xffffffffu, v[r], 1);
+            if (bb == 0 && r < R) {
+                long long f = float_to_fixed(s);
+                if (hd == 0) f += float_to_fixed(bp[ol]) + xfix[r * 96 + ol];
+                sl_add_fixed(a.d_out + (size_t)r * kHidden + 96 * c + ol, f);
+            }
+        }
+    } else if (tid < 192 + 2 * R) {
+        const int r = (tid - 192) >> 1, kvsel = tid & 1;
+        const float *v = own + r * 24 + (1 + kvsel) * 8;
+        __half2 h[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) h[e] = __floats2half2_rn(v[2 * e], v[2 * e + 1]);
+        __half *dst = a.kv + (size_t)m_page[r] * kPageHalfs +
+                      ((size_t)(kvsel * kHeads + hd) * kPage + m_pos[r] % kPage) * kHeadDim + 8 * c;
+        *reinterpret_cast<int4 *>(dst) = *reinterpret_cast<const int4 *>(h);
+    } else if (tid >= 224 && tid < 224 + R * 8 / 2) {
+        const int i = tid - 224;  // 2 columns a thread
+        long long *z = a.d_zero + (size_t)(i >> 2) * kHidden + blockIdx.x * 8 + 2 * (i & 3);
+        z[0] = 0;
+        z[1] = 0;
+    }
+    cluster_wait();
+}
+
+// ------------------------------------------------------------------ launch B: MLP half
+
+template <int MAXR>
+struct SlMlpSmem {
+    static constexpr int wi = 0;                          // int8 [8 groups][24 blocks][128] fc_in rows 32j..
+    static constexpr int wis = wi + 8 * 3072;             // half [8][24][4]
+    static constexpr int wo = wis + 8 * 192;              // int8 [192 groups][128] fc_out block j
+    static constexpr int wos = wo + 192 * 128;            // half [192][4]
+    static constexpr int lnw = wos + 192 * 8;             // float [768] LN2 weight, bias
+    static constexpr int lnb = lnw + kHidden * 4;
+    static constexpr int bi = lnb + kHidden * 4;          // float [32] fc_in bias of the CTA's features
+    static constexpr int bo = bi + 32 * 4;                // float [96] fc_out bias of its reduce rows
+    static constexpr int red = bo + 96 * 4;               // float [8] LayerNorm partial sums
+    static constexpr int xs = red + 8 * 4;                // float [MAXR][kSlRow] x, LN2(x), then fc_out partials
+    static constexpr int xfix = xs + MAXR * kSlRow * 4;   // int64 [MAXR][96] x of the reduce rows (cluster 0)
+    static constexpr int hs = xfix + MAXR * 96 * 8;       // float [MAXR][32] gelu(fc_in)
+    static constexpr int total = hs + MAXR * 32 * 4;
+    static_assert(xs % 16 == 0 && xfix % 16 == 0 && hs % 16 == 0 && bi % 16 == 0 && bo % 16 == 0,
+                  "16-byte aligned regions");
+};
+
+template <int MAXR>
+__global__ void __launch_bounds__(kSlThreads) k_small_mlp(const SmallArgs a) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    using S = SlMlpSmem<MAXR>;
+    constexpr int RPT = (MAXR * 96 + kSlThreads - 1) / kSlThreads;  // reduce outputs a thread
+    uint8_t *sm = smem_raw;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int c = (int)cluster_rank();
+    const int j = blockIdx.x;  // feature block: fc_in rows 32j..32j+31, fc_out columns 32j..
+    const bool first_cluster = blockIdx.x < kSlCluster;  // adds x and the bias of its reduce rows
+    const int R = a.R;
+    float *xs = reinterpret_cast<float *>(sm + S::xs);
+    long long *xfix = reinterpret_cast<long long *>(sm + S::xfix);
+    float *hs = reinterpret_cast<float *>(sm + S::hs);
+
+    // ---- 0. before the wait: weights, LN2, biases
+    for (int i = tid; i < 8 * 192; i += kSlThreads)  // fc_in groups 8j..8j+7: contiguous
+        sl_cp16(sm + S::wi + i * 16, a.fc_in.qs + (size_t)8 * j * 3072 + i * 16);
+    if (tid < 96) sl_cp16(sm + S::wis + tid * 16, reinterpret_cast<const uint8_t *>(a.fc_in.sc) + (size_t)8 * j * 192 + tid * 16);
+    for (int i = tid; i < 192 * 8; i += kSlThreads) {  // fc_out block j of every group
+        const int g = i >> 3, ch = i & 7;
+        sl_cp16(sm + S::wo + g * 128 + ch * 16, a.fc_out.qs + ((size_t)g * (kFF / 32) + j) * 128 + ch * 16);
+    }
+    if (tid < 192)
+        sl_cp8(sm + S::wos + tid * 8, reinterpret_cast<const uint8_t *>(a.fc_out.sc) + ((size_t)tid * (kFF / 32) + j) * 8);
+    for (int i = tid; i < 2 * (kHidden / 4); i += kSlThreads) {
+        const int ch = i % (kHidden / 4);
+        if (i < kHidden / 4) sl_cp16(sm + S::lnw + ch * 16, a.ln_w + ch * 4);
+        else sl_cp16(sm + S::lnb + ch * 16, a.ln_b + ch * 4);
+    }
+    if (tid < 8) sl_cp16(sm + S::bi + tid * 16, a.fc_in_b + 32 * j + 4 * tid);
+    else if (tid < 32) sl_cp16(sm + S::bo + (tid - 8) * 16, a.fc_out_b + 96 * c + 4 * (tid - 8));
+    sl_cp_commit();
+
+    pdl_wait();
+    pdl_trigger();
+
+    // ---- 1. x in (cluster 0 keeps its reduce rows of x for the accumulator), LN2
+    sl_residual_in(a, xs, first_cluster ? xfix : nullptr, 96 * c, tid);
+    sl_cp_wait_all();
+    __syncthreads();
+    sl_layernorm<MAXR>(xs, R, reinterpret_cast<const float *>(sm + S::lnw), reinterpret_cast<const float *>(sm + S::lnb),
+                       reinterpret_cast<float *>(sm + S::red), tid);
+    __syncthreads();
+
+    // ---- 2. fc_in + bias + gelu_new: warp w = group w (features 32j + 4w ..)
+    {
+        float acc[MAXR];
+        sl_group_dot<MAXR>(reinterpret_cast<const int8_t *>(sm + S::wi) + warp * 3072,
+                           reinterpret_cast<const __half *>(sm + S::wis) + warp * 96, xs, R, lane, acc);
+        if (lane < 8 && (lane & 1) == 0) {
+            const int f = warp * 4 + (lane >> 1);
+            const float b = reinterpret_cast<const float *>(sm + S::bi)[f];
+#pragma unroll
+            for (int r = 0; r < MAXR; ++r)
+                if (r < R) hs[r * 32 + f] = gelu_new(__fadd_rn(acc[r], b));
+        }
+    }
+    __syncthreads();
+
+    // ---- 3. fc_out over the 32 features: thread t, output rows t, t + 256, t + 512, partial
+    //      sums into xs as [r][768] (LN2(x) is no longer needed)
+#pragma unroll
+    for (int u = 0; u < 3; ++u) {
+        const int orow = tid + kSlThreads * u;
+        const int g = orow >> 2, k = orow & 3;
+        const float d = __half2float(reinterpret_cast<const __half *>(sm + S::wos)[g * 4 + k]);
+        float v[MAXR];
+        sl_block_dot<MAXR>(reinterpret_cast<const int8_t *>(sm + S::wo) + g * 128 + k * 32, d, hs, 32, R, v);
+#pragma unroll
+        for (int r = 0; r < MAXR; ++r)
+            if (r < R) xs[r * kHidden + orow] = v[r];
+    }
+    __syncthreads();
+    cluster_arrive();
+    cluster_wait();
+
+    // ---- 4. the cluster's 8 partials of rows 96c..96c+95, summed in rank order; after the
+    //      last arrive, into the accumulator (cluster 0 adds x and the bias), and this CTA's 8
+    //      columns of D[(p + 2) % 3] zeroed
+    float sum[RPT];
+#pragma unroll
+    for (int q = 0; q < RPT; ++q) {
+        const int i = tid + q * kSlThreads;
+        sum[q] = 0.f;
+        if (i < R * 96) {
+            const int r = i / 96, ol = i - r * 96;
+            const uint32_t base = smem_u32(xs + r * kHidden + 96 * c + ol);
+#pragma unroll
+            for (int src = 0; src < kSlCluster; ++src) sum[q] += sl_ld_cluster(cluster_map(base, (uint32_t)src));
+        }
+    }
+    cluster_arrive();  // done with the other CTAs' shared memory (waited for before exiting)
+#pragma unroll
+    for (int q = 0; q < RPT; ++q) {
+        const int i = tid + q * kSlThreads;
+        if (i < R * 96) {
+            const int r = i / 96, ol = i - r * 96;
+            long long f = float_to_fixed(sum[q]);
+            if (first_cluster) f += float_to_fixed(reinterpret_cast<const float *>(sm + S::bo)[ol]) + xfix[r * 96 + ol];
+            sl_add_fixed(a.d_out + (size_t)r * kHidden + 96 * c + ol, f);
+        }
+    }
+    if (tid < R * 8) a.d_zero[(size_t)(tid >> 3) * kHidden + blockIdx.x * 8 + (tid & 7)] = 0;
+    cluster_wait();
+}
+
+}  // namespace
+}  // namespace mossgpu

@@ -167,6 +167,15 @@ int mossgpu_set_graphs(mossgpu_engine *e, int enable);
  *   on one B200: 1.97 ms per 64-stream frame either way, and at 512 streams the fused form is
  *   slower (5.1 against 2.5 ms for the local decoder), so it is not the default. */
 int mossgpu_set_local_path(mossgpu_engine *e, int mode);
+/* Global layers of decode batches of at most 8 rows on the CUDA-core path:
+ * 1 (default) = two launches per layer: an attention half in which a thread-block cluster of
+ *   8 CTAs per head runs LN1, QKV, RoPE, the KV append, attention and the head's share of proj,
+ *   and an MLP half (LN2, fc_in, GELU, fc_out over 32 features per CTA); the residual stream
+ *   between them is an int64 accumulator (2^-32 units, atomic adds, so the result is the same
+ *   on every run); limit |activation| < 2^31;
+ * 0 = five launches per layer (QKV, attention, proj, fc_in, fc_out GEMV kernels).
+ * Prefill passes always take the five-launch form. */
+int mossgpu_set_small_layers(mossgpu_engine *e, int mode);
 int mossgpu_set_gemm_path(mossgpu_engine *e, int mode);
 /* Tensor-core GEMM form by batch size: batches of at least direct_min_rows padded rows run
  * one CTA per (128 weight rows, slice of direct_rows batch rows) over the whole K with the
