@@ -185,7 +185,8 @@ void Engine::load_weights(const std::string &path) {
     llnf_b_ = vec("local.lnf.b", kHidden);
     wte_ = mat("wte", kVocab, kHidden);
     for (int ch = 0; ch < kNVq; ++ch) aemb_[ch] = mat("aemb." + std::to_string(ch), kCodebook, kHidden);
-    // the fused local decoder reads the local layer and the audio heads as MMA fragment records
+    // the fused local decoder reads the local layer and the audio heads, the small-batch global
+    // layers (layer_small.cuh) every global matrix, as MMA fragment records
     auto mma_copy = [&](DevMat &m) {
         const long long threads = (long long)(m.rows / 16) * (m.cols / 32) * 32;
         m.qm = dalloc<int8_t>(size_t(m.rows) * m.cols, owned_);
@@ -194,6 +195,8 @@ void Engine::load_weights(const std::string &path) {
         CK(cudaGetLastError());
     };
     for (DevMat *m : {&local_.attn, &local_.proj, &local_.fc_in, &local_.fc_out}) mma_copy(*m);
+    for (Layer &L : global_)
+        for (DevMat *m : {&L.attn, &L.proj, &L.fc_in, &L.fc_out}) mma_copy(*m);
     for (int ch = 0; ch < kNVq; ++ch) mma_copy(aemb_[ch]);
     CK(cudaDeviceSynchronize());
     CK(cudaFree(staging));
@@ -1005,10 +1008,11 @@ void Engine::block_small(const Layer &L, int li, int R, const int *row_slot, con
     long long *D[3];
     for (int i = 0; i < 3; ++i) D[i] = sd_ + size_t(i) * kSlMaxRows * kHidden;
     SmallArgs a{};
-    a.attn = qm(L.attn);
-    a.proj = qm(L.proj);
-    a.fc_in = qm(L.fc_in);
-    a.fc_out = qm(L.fc_out);
+    auto lm = [](const DevMat &m) { return LfMat{m.qm, m.sm, m.cols / 32}; };
+    a.attn = lm(L.attn);
+    a.proj = lm(L.proj);
+    a.fc_in = lm(L.fc_in);
+    a.fc_out = lm(L.fc_out);
     a.attn_b = L.attn_b;
     a.proj_b = L.proj_b;
     a.fc_in_b = L.fc_in_b;

@@ -148,12 +148,17 @@ __device__ __forceinline__ float gelu_new(float v) {
     return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, tanhf(__fmul_rn(k, __fadd_rn(v, c)))));
 }
 
+// 16 int8 -> 16 floats, exact, without integer-to-float conversions (a slow pipe): byte b with
+// its sign bit flipped is b + 128 as an unsigned byte; placed as the low mantissa byte of 2^23
+// (0x4B000000) it reads as 8388608 + (b + 128), and subtracting 8388736 leaves b.
 __device__ __forceinline__ void unpack16(const int4 q, float *w) {
-    const int words[4] = {q.x, q.y, q.z, q.w};
+    const uint32_t words[4] = {(uint32_t)q.x ^ 0x80808080u, (uint32_t)q.y ^ 0x80808080u, (uint32_t)q.z ^ 0x80808080u,
+                               (uint32_t)q.w ^ 0x80808080u};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) w[4 * i + j] = (float)(int8_t)((words[i] >> (8 * j)) & 0xff);
+        for (int j = 0; j < 4; ++j)
+            w[4 * i + j] = __uint_as_float(__byte_perm(words[i], 0x4B000000u, 0x7540u | j)) - 8388736.0f;
     }
 }
 

@@ -11,6 +11,11 @@
 // (programmatic dependent launch), so those HBM reads overlap the previous launch.  Global
 // stores come after a CTA's last cluster-barrier arrive, so no barrier waits for them.
 //
+// The contractions run on the tensor cores (mma.sync m16n8k16, fp32 accumulation): weights as
+// the MMA fragment records of k_repack_mma (exact int8 -> fp16), activations split into fp16
+// hi + lo planes (x = hi + lo to ~2^-22), the 8 batch rows as the MMA's N; each 32-column
+// block's products are scaled by its per-row scale and added in fp32.
+//
 // Launch A (k_small_attn), 12 clusters of 8 CTAs, cluster = attention head hd, CTA rank c:
 //   x in; LN1 (every CTA, redundantly); QKV rows for dims 8c..8c+7 of q, k and v of the head
 //   (24 weight rows) with bias and RoPE; q, k, v gathered over DSMEM; attention over pages
@@ -34,6 +39,7 @@
 
 #include "kernels.cuh"
 #include "gemm_tc.cuh"
+#include "local_fused.cuh"
 
 namespace mossgpu {
 namespace {
@@ -41,20 +47,15 @@ namespace {
 constexpr int kSlThreads = 256;
 constexpr int kSlCluster = 8;
 constexpr int kSlMaxRows = 8;
-constexpr int kSlCtas = 96;            // both launches: 12 clusters of 8
-constexpr int kSlRow = kHidden + 96;   // a row in shared memory: 32-float blocks 36 floats apart
+constexpr int kSlCtas = 96;     // both launches: 12 clusters of 8
 static_assert(kHeads * kSlCluster == kSlCtas && kFF / 32 == kSlCtas, "layer split");
 
-// (row, page) K/V pairs a CTA stages in shared memory (4 KB each); fewer at 8 rows, so that a
-// launch's CTAs fit on an SM beside its predecessor's
-__host__ __device__ constexpr int sl_kv_slots(int maxr) { return maxr >= 8 ? 8 : 16; }
-
-// column c of a row -> its place in shared memory: lanes that read the same 16 bytes of 8
-// consecutive 128-byte blocks then hit 8 different 4-bank groups
-__device__ __forceinline__ int sl_pad(int c) { return c + ((c >> 5) << 2); }
+// (row, page) K/V pairs a CTA of launch A stages in shared memory (4 KB each): as many as let
+// it share an SM with a CTA of launch B (its successor's CTAs start beside it)
+__host__ __device__ constexpr int sl_kv_slots(int maxr) { return maxr <= 1 ? 12 : maxr <= 2 ? 10 : maxr <= 4 ? 6 : 2; }
 
 struct SmallArgs {
-    QMat attn, proj, fc_in, fc_out;
+    LfMat attn, proj, fc_in, fc_out;   // fragment records: [rows/16][nb][512] int8, [rows/16][nb][16] fp16
     const float *attn_b, *proj_b, *fc_in_b, *fc_out_b;
     const float *ln_w, *ln_b;   // LN1 (launch A) or LN2 (launch B)
     const float *x0;            // launch 0: the embedding rows [R][768] (fp32)
@@ -91,7 +92,7 @@ __device__ __forceinline__ void sl_add_fixed(long long *p, long long v) {
     atomicAdd(reinterpret_cast<unsigned long long *>(p), static_cast<unsigned long long>(v));
 }
 
-// x of rows < R into xs (padded rows), and, for a CTA that adds rows base..base+95 of the
+// x of rows < R into xs ([R][768] fp32), and, for a CTA that adds rows base..base+95 of the
 // output with their bias (xfix != null), those rows of x as fixed point into xfix[r][96]
 __device__ __forceinline__ void sl_residual_in(const SmallArgs &a, float *xs, long long *xfix, int base, int tid) {
     const int R = a.R;
@@ -119,24 +120,37 @@ __device__ __forceinline__ void sl_residual_in(const SmallArgs &a, float *xs, lo
                 f[3] = float_to_fixed(v.w);
             }
         }
-        *reinterpret_cast<float4 *>(xs + r * kSlRow + sl_pad(4 * q4)) = v;
+        *reinterpret_cast<float4 *>(xs + r * kHidden + 4 * q4) = v;
     }
 }
 
-// LayerNorm of rows < R of xs in place (llm.cpp:159-171): TPR = 256 / MAXR threads a row, each
-// with E = 768 / TPR columns; two reductions (sum, then squared deviations) over the thread's
-// columns, the warp and the row's warps (red: 8 floats).  Every thread of the CTA calls it.
+
+// column k of activation row r -> its place in an MMA B-operand plane ([8][stride] fp16):
+// lf_bpos order, so that a lane's 16-byte load covers both K steps of a 32-column block
+__device__ __forceinline__ void sl_act(__half *hi, __half *lo, int stride, int r, int k, float v) {
+    const __half h = __float2half_rn(v);
+    const int p = r * stride + lf_bpos(k);
+    hi[p] = h;
+    lo[p] = __float2half_rn(v - __half2float(h));
+}
+
+// LayerNorm of rows < R of xs (llm.cpp:159-171) into the hi / lo planes ([8][768]): TPR =
+// 256 / MAXR threads a row, each with E = 768 / TPR columns; two reductions (sum, then squared
+// deviations) over the thread's columns, the warp and the row's warps (red: 8 floats).  Every
+// thread of the CTA calls it.  Plane rows >= R are left as they are: each MMA output column
+// depends on its own B column only, and those columns are never read.
 template <int MAXR>
-__device__ __forceinline__ void sl_layernorm(float *xs, int R, const float *w, const float *b, float *red, int tid) {
+__device__ __forceinline__ void sl_layernorm(const float *xs, int R, const float *w, const float *b, float *red,
+                                             __half *hi, __half *lo, int tid) {
     constexpr int TPR = kSlThreads / MAXR, WPR = TPR / 32, E = kHidden / TPR;
     const int r = tid / TPR, j = tid - r * TPR, lane = tid & 31, wr = j >> 5;
     const bool on = r < R;
-    float *row = xs + r * kSlRow;
+    const float *row = xs + r * kHidden;
     float v[E];
     float s = 0.f;
 #pragma unroll
     for (int e = 0; e < E; ++e) {
-        v[e] = on ? row[sl_pad(j + e * TPR)] : 0.f;
+        v[e] = on ? row[j + e * TPR] : 0.f;
         s += v[e];
     }
     s = warp_sum(s);
@@ -169,82 +183,56 @@ __device__ __forceinline__ void sl_layernorm(float *xs, int R, const float *w, c
 #pragma unroll
         for (int e = 0; e < E; ++e) {
             const int col = j + e * TPR;
-            row[sl_pad(col)] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[e], mean), inv), w[col]), b[col]);
+            sl_act(hi, lo, kHidden, r, col, __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[e], mean), inv), w[col]), b[col]));
         }
     }
 }
 
-// 4 weight rows (one Q8_0_4X4 group, K = 768, in shared memory) times the rows' activations
-// (padded rows): lane l reads 16 bytes of every 128-byte block (row (l % 8) / 2, half l % 2), 6
-// chunks a lane; the 8 lanes of a row reduce by shuffles.  Returns the row sums in lanes 0, 2,
-// 4, 6 (weight row lane / 2).
-template <int MAXR>
-__device__ __forceinline__ void sl_group_dot(const int8_t *wg, const __half *sg, const float *xs, int R, int lane,
-                                             float (&acc)[MAXR]) {
-    const int k = (lane & 7) >> 1, h = lane & 1;
+// acc[mt][.] = sum over blocks b0 <= b < b1 of scale * (W x) for MT 16-row weight tiles whose
+// fragment records are in shared memory (quants rec[mt][nblk][512], scales srec[mt][nblk][16])
+// and the 8 activation rows of the hi / lo planes ([8][stride], block b at column 32 b).
+// Lane (g, t) = (lane / 4, lane % 4) gets acc[mt] = {(row g, col 2t), (g, 2t + 1), (g + 8, 2t),
+// (g + 8, 2t + 1)} of the tile's 16 x 8 result.  Per block, the hi and the lo products of its
+// two K steps form two MMA chains from zero, added and scaled in fp32.
+template <int MT>
+__device__ __forceinline__ void sl_mma(const uint8_t *rec, const __half *srec, int nblk, int b0, int b1,
+                                       const __half *act_hi, const __half *act_lo, int stride, int lane,
+                                       float (&acc)[MT][4]) {
+    const int g = lane >> 2, t = lane & 3;
 #pragma unroll
-    for (int r = 0; r < MAXR; ++r) acc[r] = 0.f;
+    for (int mt = 0; mt < MT; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
+    const __half *bh = act_hi + g * stride + t * 8;
+    const __half *bl = act_lo + g * stride + t * 8;
+#pragma unroll 2
+    for (int b = b0; b < b1; ++b) {
+        const int4 xh = lds128(bh + b * 32);
+        const int4 xl = lds128(bl + b * 32);
 #pragma unroll
-    for (int u = 0; u < 6; ++u) {
-        const int i = lane + 32 * u;
-        const int b = i >> 3;
-        const int4 q = *reinterpret_cast<const int4 *>(wg + i * 16);
-        const float d = __half2float(sg[b * 4 + k]);
-        float wf[16];
-        unpack16(q, wf);
-        const int xoff = b * 36 + h * 16;
-#pragma unroll
-        for (int r = 0; r < MAXR; ++r) {
-            if (r < R) {
-                const float4 *xv = reinterpret_cast<const float4 *>(xs + r * kSlRow + xoff);
-                float s = 0.f;
-#pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    const float4 xx = xv[t];
-                    s = fmaf(wf[4 * t + 0], xx.x, s);
-                    s = fmaf(wf[4 * t + 1], xx.y, s);
-                    s = fmaf(wf[4 * t + 2], xx.z, s);
-                    s = fmaf(wf[4 * t + 3], xx.w, s);
-                }
-                acc[r] = fmaf(s, d, acc[r]);
-            }
+        for (int mt = 0; mt < MT; ++mt) {
+            const int4 q = lds128(rec + (mt * nblk + b) * 512 + lane * 16);
+            const uint32_t s2 = *reinterpret_cast<const uint32_t *>(srec + (mt * nblk + b) * 16 + 2 * g);
+            uint32_t a00, a02, a01, a03, a10, a12, a11, a13;
+            i8x4_to_h2x2((uint32_t)q.x, a00, a02);  // row g: K step 0 cols 2t.., 2t+8..
+            i8x4_to_h2x2((uint32_t)q.z, a01, a03);  // row g+8
+            i8x4_to_h2x2((uint32_t)q.y, a10, a12);  // row g: K step 1
+            i8x4_to_h2x2((uint32_t)q.w, a11, a13);  // row g+8
+            float h0 = 0.f, h1 = 0.f, h2 = 0.f, h3 = 0.f, l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f;
+            mma16816(h0, h1, h2, h3, a00, a01, a02, a03, (uint32_t)xh.x, (uint32_t)xh.y);
+            mma16816(l0, l1, l2, l3, a00, a01, a02, a03, (uint32_t)xl.x, (uint32_t)xl.y);
+            mma16816(h0, h1, h2, h3, a10, a11, a12, a13, (uint32_t)xh.z, (uint32_t)xh.w);
+            mma16816(l0, l1, l2, l3, a10, a11, a12, a13, (uint32_t)xl.z, (uint32_t)xl.w);
+            const float2 sc = __half22float2(*reinterpret_cast<const __half2 *>(&s2));
+            acc[mt][0] = fmaf(sc.x, h0 + l0, acc[mt][0]);
+            acc[mt][1] = fmaf(sc.x, h1 + l1, acc[mt][1]);
+            acc[mt][2] = fmaf(sc.y, h2 + l2, acc[mt][2]);
+            acc[mt][3] = fmaf(sc.y, h3 + l3, acc[mt][3]);
         }
-    }
-#pragma unroll
-    for (int r = 0; r < MAXR; ++r) {
-        float v = acc[r];
-        v += __shfl_xor_sync(0xffffffffu, v, 1);
-        v += __shfl_xor_sync(0xffffffffu, v, 8);
-        v += __shfl_xor_sync(0xffffffffu, v, 16);
-        acc[r] = v;
     }
 }
 
-// One weight row's 32 int8 values (a block, in shared memory) dotted with 32 activations of
-// each row, times the block scale.
-template <int MAXR>
-__device__ __forceinline__ void sl_block_dot(const int8_t *w32, float d, const float *act, int act_stride, int R,
-                                             float (&out)[MAXR]) {
-    float wf[32];
-    unpack16(*reinterpret_cast<const int4 *>(w32), wf);
-    unpack16(*reinterpret_cast<const int4 *>(w32 + 16), wf + 16);
-#pragma unroll
-    for (int r = 0; r < MAXR; ++r) {
-        out[r] = 0.f;
-        if (r < R) {
-            const float4 *av = reinterpret_cast<const float4 *>(act + r * act_stride);
-            float s = 0.f;
-#pragma unroll
-            for (int t = 0; t < 8; ++t) {
-                const float4 xx = av[t];
-                s = fmaf(wf[4 * t + 0], xx.x, s);
-                s = fmaf(wf[4 * t + 1], xx.y, s);
-                s = fmaf(wf[4 * t + 2], xx.z, s);
-                s = fmaf(wf[4 * t + 3], xx.w, s);
-            }
-            out[r] = s * d;
-        }
-    }
+// copy n 16-byte chunks from src to dst (shared), thread-strided
+__device__ __forceinline__ void sl_copy(uint8_t *dst, const void *src, int n, int tid) {
+    for (int i = tid; i < n; i += kSlThreads) sl_cp16(dst + i * 16, reinterpret_cast<const uint8_t *>(src) + i * 16);
 }
 
 // ------------------------------------------------------------------ launch A: attention half
@@ -252,30 +240,32 @@ __device__ __forceinline__ void sl_block_dot(const int8_t *w32, float d, const f
 template <int MAXR>
 struct SlAttnSmem {
     static constexpr int kSlots = sl_kv_slots(MAXR);
-    static constexpr int wq = 0;                               // int8 [6 groups][24 blocks][128]
-    static constexpr int wqs = wq + 6 * 3072;                  // half [6][24][4]
-    static constexpr int wp = wqs + 6 * 192;                   // int8 [24 groups][2 blocks][128]
-    static constexpr int wps = wp + 24 * 256;                  // half [24][2][4]
-    static constexpr int lnw = wps + 24 * 16;                  // float [768] LN1 weight, bias
+    static constexpr int wq = 0;                               // records [3 tiles: q, k, v][24 blocks][512]
+    static constexpr int wqs = wq + 3 * 24 * 512;              // half [3][24][16]
+    static constexpr int wp = wqs + 3 * 24 * 32;               // records [6 tiles][2 blocks][512] (proj)
+    static constexpr int wps = wp + 6 * 2 * 512;               // half [6][2][16]
+    static constexpr int lnw = wps + 6 * 2 * 32;               // float [768] LN1 weight, bias
     static constexpr int lnb = lnw + kHidden * 4;
-    static constexpr int bq = lnb + kHidden * 4;               // float [24] QKV bias of the CTA's rows
+    static constexpr int bq = lnb + kHidden * 4;               // float [24] QKV bias of the CTA's dims (q, k, v)
     static constexpr int bp = bq + 24 * 4;                     // float [96] proj bias of its rows
     static constexpr int rs = bp + 96 * 4;                     // float2 [8][4] RoPE (cos, sin)
     static constexpr int meta = rs + kSlMaxRows * 4 * 8;       // int [5][8]: pos, slot, pages, first item, page of pos
     static constexpr int red = meta + 5 * kSlMaxRows * 4;      // float [8] LayerNorm partial sums
-    static constexpr int xs = red + 8 * 4;                     // float [MAXR][kSlRow] x, then LN1(x)
-    static constexpr int xfix = xs + MAXR * kSlRow * 4;        // int64 [MAXR][96] x of the proj rows (head 0)
-    static constexpr int own = xfix + MAXR * 96 * 8;           // float [MAXR][24] q, k, v dims 8c..8c+7
+    static constexpr int xs = red + 8 * 4;                     // float [MAXR][768] x
+    static constexpr int xfix = xs + MAXR * kHidden * 4;       // int64 [MAXR][96] x of the proj rows (head 0)
+    static constexpr int act = xfix + MAXR * 96 * 8;           // half [2][8][768] LN1(x) hi, lo; then QKV partials
+    static constexpr int own = act + 2 * 8 * kHidden * 2;      // float [MAXR][24] q, k, v dims 8c..8c+7
     static constexpr int full = own + MAXR * 24 * 4;           // float [MAXR][192] the head's q | k | v
     static constexpr int newkv = full + MAXR * 192 * 4;        // half [MAXR][2][64] k, v of the new position
     static constexpr int wst = newkv + MAXR * 256;             // float [8 warps][68] m, l, -, -, o[64]
     static constexpr int part = wst + 8 * kPartStride * 4;     // float [MAXR][68] the CTA's partial
-    static constexpr int oh = part + MAXR * kPartStride * 4;   // float [MAXR][64] attention output
-    static constexpr int kvs = oh + MAXR * kHeadDim * 4;       // half [slots][k|v][16][64]
+    static constexpr int ohp = part + MAXR * kPartStride * 4;  // half [2][8][64] attention output hi, lo
+    static constexpr int kvs = ohp + 2 * 8 * kHeadDim * 2;     // half [slots][k|v][16][64]
     static constexpr int total = kvs + kSlots * 4096;
-    static_assert(rs % 16 == 0 && xs % 16 == 0 && xfix % 16 == 0 && own % 16 == 0 && full % 16 == 0 &&
-                      newkv % 16 == 0 && part % 16 == 0 && oh % 16 == 0 && kvs % 16 == 0,
+    static_assert(rs % 16 == 0 && xs % 16 == 0 && xfix % 16 == 0 && act % 16 == 0 && own % 16 == 0 &&
+                      full % 16 == 0 && newkv % 16 == 0 && part % 16 == 0 && ohp % 16 == 0 && kvs % 16 == 0,
                   "16-byte aligned regions");
+    static_assert(8 * 3 * 128 * 4 <= 2 * 8 * kHidden * 2, "QKV partials fit the activation planes");
 };
 
 template <int MAXR>
@@ -292,12 +282,14 @@ __global__ void __launch_bounds__(kSlThreads) k_small_attn(const SmallArgs a) {
     int *m_page = m_pos + 4 * kSlMaxRows;
     float *xs = reinterpret_cast<float *>(sm + S::xs);
     long long *xfix = reinterpret_cast<long long *>(sm + S::xfix);
+    __half *act_hi = reinterpret_cast<__half *>(sm + S::act), *act_lo = act_hi + 8 * kHidden;
+    float *qred = reinterpret_cast<float *>(sm + S::act);  // [8 warps][3][128], after the QKV MMAs
     float *own = reinterpret_cast<float *>(sm + S::own);
     float *full = reinterpret_cast<float *>(sm + S::full);
     __half *newkv = reinterpret_cast<__half *>(sm + S::newkv);
     float *wst = reinterpret_cast<float *>(sm + S::wst);
     float *part = reinterpret_cast<float *>(sm + S::part);
-    float *oh = reinterpret_cast<float *>(sm + S::oh);
+    __half *oh_hi = reinterpret_cast<__half *>(sm + S::ohp), *oh_lo = oh_hi + 8 * kHeadDim;
     const float *bq = reinterpret_cast<const float *>(sm + S::bq);
     const float *bp = reinterpret_cast<const float *>(sm + S::bp);
     const float2 *rs = reinterpret_cast<const float2 *>(sm + S::rs);
@@ -319,33 +311,27 @@ __global__ void __launch_bounds__(kSlThreads) k_small_attn(const SmallArgs a) {
         m_cnt[tid] = cnt;
         m_page[tid] = page;
     }
-    const int gq0 = (hd * kHeadDim + 8 * c) / 4;  // first Q8 group of the CTA's q rows
-    // QKV: groups gq0, gq0 + 1 of q, k and v (group g + 192 * part), 3072 B of quants each
-    for (int i = tid; i < 6 * 192; i += kSlThreads) {
-        const int gi = i / 192, ch = i - gi * 192;
-        const size_t g = (size_t)(gi >> 1) * (kHidden / 4) + gq0 + (gi & 1);
-        sl_cp16(sm + S::wq + gi * 3072 + ch * 16, a.attn.qs + g * 3072 + ch * 16);
+    // QKV: the 16-row tiles holding q, k and v dims 8c..8c+7 of the head (rows 8 (c & 1) ..
+    // of tile 4 hd + c / 2, + 48, + 96), all 24 blocks of each (contiguous records)
+    const int tq = 4 * hd + (c >> 1);
+#pragma unroll
+    for (int m = 0; m < 3; ++m) {
+        const size_t tile = (size_t)(tq + 48 * m);
+        sl_copy(sm + S::wq + m * 24 * 512, a.attn.qm + tile * 24 * 512, 24 * 32, tid);
+        sl_copy(sm + S::wqs + m * 24 * 32, a.attn.sm + tile * 24 * 16, 48, tid);
     }
-    for (int i = tid; i < 6 * 12; i += kSlThreads) {
-        const int gi = i / 12, ch = i - gi * 12;
-        const size_t g = (size_t)(gi >> 1) * (kHidden / 4) + gq0 + (gi & 1);
-        sl_cp16(sm + S::wqs + gi * 192 + ch * 16, reinterpret_cast<const uint8_t *>(a.attn.sc) + g * 192 + ch * 16);
-    }
-    // proj: rows 96c.. (groups 24c..24c+23), blocks 2hd and 2hd + 1 (the head's columns)
-    for (int i = tid; i < 24 * 16; i += kSlThreads) {
-        const int gl = i >> 4, ch = i & 15;
-        const size_t blk = (size_t)(24 * c + gl) * (kHidden / 32) + 2 * hd;
-        sl_cp16(sm + S::wp + gl * 256 + ch * 16, a.proj.qs + blk * 128 + ch * 16);
+    // proj: tiles 6c..6c+5 (rows 96c..96c+95), blocks 2hd, 2hd + 1 (the head's 64 columns)
+    for (int i = tid; i < 6 * 64; i += kSlThreads) {
+        const int m = i >> 6, ch = i & 63;
+        const size_t rec = (size_t)(6 * c + m) * (kHidden / 32) + 2 * hd;
+        sl_cp16(sm + S::wp + m * 1024 + ch * 16, a.proj.qm + rec * 512 + ch * 16);
     }
     if (tid < 24) {
-        const size_t blk = (size_t)(24 * c + tid) * (kHidden / 32) + 2 * hd;
-        sl_cp16(sm + S::wps + tid * 16, reinterpret_cast<const uint8_t *>(a.proj.sc) + blk * 8);
+        const size_t rec = (size_t)(6 * c + (tid >> 2)) * (kHidden / 32) + 2 * hd;
+        sl_cp16(sm + S::wps + tid * 16, reinterpret_cast<const uint8_t *>(a.proj.sm + rec * 16) + (tid & 3) * 16);
     }
-    for (int i = tid; i < 2 * (kHidden / 4); i += kSlThreads) {
-        const int ch = i % (kHidden / 4);
-        if (i < kHidden / 4) sl_cp16(sm + S::lnw + ch * 16, a.ln_w + ch * 4);
-        else sl_cp16(sm + S::lnb + ch * 16, a.ln_b + ch * 4);
-    }
+    sl_copy(sm + S::lnw, a.ln_w, kHidden / 4, tid);
+    sl_copy(sm + S::lnb, a.ln_b, kHidden / 4, tid);
     if (tid < 6) {  // QKV bias: rows part * 768 + hd * 64 + 8c + 4 (tid & 1) ..
         const int off = (tid >> 1) * kHidden + hd * kHeadDim + 8 * c + 4 * (tid & 1);
         sl_cp16(sm + S::bq + tid * 16, a.attn_b + off);
@@ -383,41 +369,47 @@ __global__ void __launch_bounds__(kSlThreads) k_small_attn(const SmallArgs a) {
     pdl_wait();
     pdl_trigger();
 
-    // ---- 1. x in (head 0 keeps its proj rows of x for the accumulator), LN1
+    // ---- 1. x in (head 0 keeps its proj rows of x for the accumulator), LN1 into the planes
     sl_residual_in(a, xs, hd == 0 ? xfix : nullptr, 96 * c, tid);
     sl_cp_wait_all();
     __syncthreads();
     sl_layernorm<MAXR>(xs, R, reinterpret_cast<const float *>(sm + S::lnw), reinterpret_cast<const float *>(sm + S::lnb),
-                       reinterpret_cast<float *>(sm + S::red), tid);
+                       reinterpret_cast<float *>(sm + S::red), act_hi, act_lo, tid);
     __syncthreads();
 
-    // ---- 2. the CTA's 24 QKV rows: warp gi = group gi (q, q, k, k, v, v)
-    if (warp < 6) {
-        float acc[MAXR];
-        sl_group_dot<MAXR>(reinterpret_cast<const int8_t *>(sm + S::wq) + warp * 3072,
-                           reinterpret_cast<const __half *>(sm + S::wqs) + warp * 96, xs, R, lane, acc);
-        if (lane < 8 && (lane & 1) == 0) {
+    // ---- 2. QKV: warp w takes blocks 3w..3w+2 of the three tiles; the 8 partial sums are
+    //      added in warp order, then bias and RoPE (pairs 2i, 2i+1 of q and k; EPI_QKV order)
+    {
+        float acc[3][4];
+        sl_mma<3>(sm + S::wq, reinterpret_cast<const __half *>(sm + S::wqs), 24, 3 * warp, 3 * warp + 3, act_hi, act_lo,
+                  kHidden, lane, acc);
+        __syncthreads();  // every warp is done with the planes, which now take the partials
 #pragma unroll
-            for (int r = 0; r < MAXR; ++r)
-                if (r < R) own[r * 24 + warp * 4 + (lane >> 1)] = acc[r];
-        }
+        for (int m = 0; m < 3; ++m)
+            *reinterpret_cast<float4 *>(qred + (warp * 3 + m) * 128 + lane * 4) =
+                make_float4(acc[m][0], acc[m][1], acc[m][2], acc[m][3]);
     }
     __syncthreads();
-    // bias and RoPE (pairs 2i, 2i+1 of q and k; EPI_QKV order), in place: own[r][part * 8 + j]
     if (tid < 12 * R) {
-        const int r = tid / 12, pr = tid - r * 12;
-        const int prt = pr >> 2, j = (pr & 3) * 2;
-        float *o = own + r * 24 + prt * 8 + j;
-        const float v0 = __fadd_rn(o[0], bq[prt * 8 + j]);
-        const float v1 = __fadd_rn(o[1], bq[prt * 8 + j + 1]);
+        const int r = tid / 12, e = tid - r * 12;
+        const int m = e >> 2, i0 = (e & 3) * 2;   // tile (q, k, v), first dim of the pair
+        const int j = 2 * (c & 1) + (r & 1);      // fragment slot: row half, column parity
+        float v0 = 0.f, v1 = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+            v0 += qred[(w * 3 + m) * 128 + (4 * i0 + (r >> 1)) * 4 + j];
+            v1 += qred[(w * 3 + m) * 128 + (4 * (i0 + 1) + (r >> 1)) * 4 + j];
+        }
+        v0 = __fadd_rn(v0, bq[m * 8 + i0]);
+        v1 = __fadd_rn(v1, bq[m * 8 + i0 + 1]);
         float o0 = v0, o1 = v1;
-        if (prt < 2) {
-            const float2 cs = rs[r * 4 + (j >> 1)];
+        if (m < 2) {
+            const float2 cs = rs[r * 4 + (i0 >> 1)];
             o0 = __fsub_rn(__fmul_rn(v0, cs.x), __fmul_rn(v1, cs.y));
             o1 = __fadd_rn(__fmul_rn(v1, cs.x), __fmul_rn(v0, cs.y));
         }
-        o[0] = o0;
-        o[1] = o1;
+        own[r * 24 + m * 8 + i0] = o0;
+        own[r * 24 + m * 8 + i0 + 1] = o1;
     }
     __syncthreads();
     cluster_arrive();
@@ -436,7 +428,6 @@ __global__ void __launch_bounds__(kSlThreads) k_small_attn(const SmallArgs a) {
         }
     }
     __syncthreads();
-
     // ---- 4. attention over this CTA's pages: warp w takes row w / WPR, items sub, sub + WPR,
     //      ...; lanes as in k_attn_rows (8 lanes a position, 8 dims a lane, 4 positions a step)
     constexpr int WPR = 8 / MAXR;
@@ -579,7 +570,8 @@ __global__ void __launch_bounds__(kSlThreads) k_small_attn(const SmallArgs a) {
     cluster_arrive();
     cluster_wait();
 
-    // ---- 5. the 8 CTAs' partials merged (every CTA, for its proj rows)
+
+    // ---- 5. the 8 CTAs' partials merged (every CTA, for its proj rows) into the planes
     for (int i = tid; i < R * kHeadDim; i += kSlThreads) {
         const int r = i / kHeadDim, d = i - r * kHeadDim;
         const uint32_t base = smem_u32(part + r * kPartStride);
@@ -600,28 +592,26 @@ __global__ void __launch_bounds__(kSlThreads) k_small_attn(const SmallArgs a) {
             L = fmaf(pl[s], wgt, L);
             y = fmaf(po[s], wgt, y);
         }
-        oh[r * kHeadDim + d] = y / L;
+        sl_act(oh_hi, oh_lo, kHeadDim, r, d, y / L);
     }
     cluster_arrive();  // done with the other CTAs' shared memory (waited for before exiting)
     __syncthreads();
 
-    // ---- 6. proj rows 96c..96c+95 over the head's 64 columns (thread: row, block half) into
-    //      the accumulator (head 0 adds x and the bias); then this CTA's global stores: its
-    //      k, v dims of the new position into the KV cache, its 8 columns of D[(p + 2) % 3]
-    if (tid < 192) {
-        const int ol = tid >> 1, bb = tid & 1;
-        const int gl = ol >> 2, k = ol & 3;
-        const int8_t *w32 = reinterpret_cast<const int8_t *>(sm + S::wp) + gl * 256 + bb * 128 + k * 32;
-        const float d = __half2float(reinterpret_cast<const __half *>(sm + S::wps)[gl * 8 + bb * 4 + k]);
-        float v[MAXR];
-        sl_block_dot<MAXR>(w32, d, oh + bb * 32, kHeadDim, R, v);
+    // ---- 6. proj rows 96c..96c+95 over the head's 64 columns (warp w: tile 6c + w) into the
+    //      accumulator (head 0 adds x and the bias); then this CTA's global stores: its k, v
+    //      dims of the new position into the KV cache, its 8 columns of D[(p + 2) % 3]
+    if (warp < 6) {
+        float acc[1][4];
+        sl_mma<1>(sm + S::wp + warp * 1024, reinterpret_cast<const __half *>(sm + S::wps) + warp * 32, 2, 0, 2, oh_hi,
+                  oh_lo, kHeadDim, lane, acc);
+        const int g = lane >> 2, t = lane & 3;
 #pragma unroll
-        for (int r = 0; r < MAXR; ++r) {
-            const float s = v[r] + __shfl_xor_sync(0xffffffffu, v[r], 1);
-            if (bb == 0 && r < R) {
-                long long f = float_to_fixed(s);
-                if (hd == 0) f += float_to_fixed(bp[ol]) + xfix[r * 96 + ol];
-                sl_add_fixed(a.d_out + (size_t)r * kHidden + 96 * c + ol, f);
+        for (int j = 0; j < 4; ++j) {
+            const int n = 2 * t + (j & 1), ol = 16 * warp + g + 8 * (j >> 1);
+            if (n < R) {
+                long long f = float_to_fixed(acc[0][j]);
+                if (hd == 0) f += float_to_fixed(bp[ol]) + xfix[n * 96 + ol];
+                sl_add_fixed(a.d_out + (size_t)n * kHidden + 96 * c + ol, f);
             }
         }
     } else if (tid < 192 + 2 * R) {
@@ -646,20 +636,22 @@ __global__ void __launch_bounds__(kSlThreads) k_small_attn(const SmallArgs a) {
 
 template <int MAXR>
 struct SlMlpSmem {
-    static constexpr int wi = 0;                          // int8 [8 groups][24 blocks][128] fc_in rows 32j..
-    static constexpr int wis = wi + 8 * 3072;             // half [8][24][4]
-    static constexpr int wo = wis + 8 * 192;              // int8 [192 groups][128] fc_out block j
-    static constexpr int wos = wo + 192 * 128;            // half [192][4]
-    static constexpr int lnw = wos + 192 * 8;             // float [768] LN2 weight, bias
+    static constexpr int wi = 0;                          // records [2 tiles][24 blocks][512]: fc_in rows 32j..
+    static constexpr int wis = wi + 2 * 24 * 512;         // half [2][24][16]
+    static constexpr int wo = wis + 2 * 24 * 32;          // records [48 tiles][512]: fc_out block j
+    static constexpr int wos = wo + 48 * 512;             // half [48][16]
+    static constexpr int lnw = wos + 48 * 32;             // float [768] LN2 weight, bias
     static constexpr int lnb = lnw + kHidden * 4;
     static constexpr int bi = lnb + kHidden * 4;          // float [32] fc_in bias of the CTA's features
     static constexpr int bo = bi + 32 * 4;                // float [96] fc_out bias of its reduce rows
     static constexpr int red = bo + 96 * 4;               // float [8] LayerNorm partial sums
-    static constexpr int xs = red + 8 * 4;                // float [MAXR][kSlRow] x, LN2(x), then fc_out partials
-    static constexpr int xfix = xs + MAXR * kSlRow * 4;   // int64 [MAXR][96] x of the reduce rows (cluster 0)
-    static constexpr int hs = xfix + MAXR * 96 * 8;       // float [MAXR][32] gelu(fc_in)
-    static constexpr int total = hs + MAXR * 32 * 4;
-    static_assert(xs % 16 == 0 && xfix % 16 == 0 && hs % 16 == 0 && bi % 16 == 0 && bo % 16 == 0,
+    static constexpr int xs = red + 8 * 4;                // float [MAXR][768] x
+    static constexpr int xfix = xs + MAXR * kHidden * 4;  // int64 [MAXR][96] x of the reduce rows (cluster 0)
+    static constexpr int act = xfix + MAXR * 96 * 8;      // half [2][8][768] LN2(x) hi, lo; then fc_in partials
+                                                          // [8 warps][2][128] float; then fc_out partials [8][768] float
+    static constexpr int hpl = act + 2 * 8 * kHidden * 2; // half [2][8][32] gelu(fc_in) hi, lo
+    static constexpr int total = hpl + 2 * 8 * 32 * 2;
+    static_assert(xs % 16 == 0 && xfix % 16 == 0 && act % 16 == 0 && hpl % 16 == 0 && bi % 16 == 0 && bo % 16 == 0,
                   "16-byte aligned regions");
 };
 
@@ -676,23 +668,23 @@ __global__ void __launch_bounds__(kSlThreads) k_small_mlp(const SmallArgs a) {
     const int R = a.R;
     float *xs = reinterpret_cast<float *>(sm + S::xs);
     long long *xfix = reinterpret_cast<long long *>(sm + S::xfix);
-    float *hs = reinterpret_cast<float *>(sm + S::hs);
+    __half *act_hi = reinterpret_cast<__half *>(sm + S::act), *act_lo = act_hi + 8 * kHidden;
+    float *fred = reinterpret_cast<float *>(sm + S::act);   // [8 warps][2][128], after the fc_in MMAs
+    float *opart = reinterpret_cast<float *>(sm + S::act);  // [8][768], after the fc_in sums
+    __half *h_hi = reinterpret_cast<__half *>(sm + S::hpl), *h_lo = h_hi + 8 * 32;
 
     // ---- 0. before the wait: weights, LN2, biases
-    for (int i = tid; i < 8 * 192; i += kSlThreads)  // fc_in groups 8j..8j+7: contiguous
-        sl_cp16(sm + S::wi + i * 16, a.fc_in.qs + (size_t)8 * j * 3072 + i * 16);
-    if (tid < 96) sl_cp16(sm + S::wis + tid * 16, reinterpret_cast<const uint8_t *>(a.fc_in.sc) + (size_t)8 * j * 192 + tid * 16);
-    for (int i = tid; i < 192 * 8; i += kSlThreads) {  // fc_out block j of every group
-        const int g = i >> 3, ch = i & 7;
-        sl_cp16(sm + S::wo + g * 128 + ch * 16, a.fc_out.qs + ((size_t)g * (kFF / 32) + j) * 128 + ch * 16);
+    sl_copy(sm + S::wi, a.fc_in.qm + (size_t)2 * j * 24 * 512, 2 * 24 * 32, tid);  // tiles 2j, 2j + 1: contiguous
+    sl_copy(sm + S::wis, a.fc_in.sm + (size_t)2 * j * 24 * 16, 2 * 24 * 2, tid);
+    for (int i = tid; i < 48 * 32; i += kSlThreads) {  // block j of every fc_out tile
+        const int m = i >> 5, ch = i & 31;
+        sl_cp16(sm + S::wo + m * 512 + ch * 16, a.fc_out.qm + ((size_t)m * (kFF / 32) + j) * 512 + ch * 16);
     }
-    if (tid < 192)
-        sl_cp8(sm + S::wos + tid * 8, reinterpret_cast<const uint8_t *>(a.fc_out.sc) + ((size_t)tid * (kFF / 32) + j) * 8);
-    for (int i = tid; i < 2 * (kHidden / 4); i += kSlThreads) {
-        const int ch = i % (kHidden / 4);
-        if (i < kHidden / 4) sl_cp16(sm + S::lnw + ch * 16, a.ln_w + ch * 4);
-        else sl_cp16(sm + S::lnb + ch * 16, a.ln_b + ch * 4);
-    }
+    if (tid < 96)
+        sl_cp16(sm + S::wos + tid * 16,
+                reinterpret_cast<const uint8_t *>(a.fc_out.sm + ((size_t)(tid >> 1) * (kFF / 32) + j) * 16) + (tid & 1) * 16);
+    sl_copy(sm + S::lnw, a.ln_w, kHidden / 4, tid);
+    sl_copy(sm + S::lnb, a.ln_b, kHidden / 4, tid);
     if (tid < 8) sl_cp16(sm + S::bi + tid * 16, a.fc_in_b + 32 * j + 4 * tid);
     else if (tid < 32) sl_cp16(sm + S::bo + (tid - 8) * 16, a.fc_out_b + 96 * c + 4 * (tid - 8));
     sl_cp_commit();
@@ -700,41 +692,52 @@ __global__ void __launch_bounds__(kSlThreads) k_small_mlp(const SmallArgs a) {
     pdl_wait();
     pdl_trigger();
 
-    // ---- 1. x in (cluster 0 keeps its reduce rows of x for the accumulator), LN2
+    // ---- 1. x in (cluster 0 keeps its reduce rows of x for the accumulator), LN2 into the planes
     sl_residual_in(a, xs, first_cluster ? xfix : nullptr, 96 * c, tid);
     sl_cp_wait_all();
     __syncthreads();
     sl_layernorm<MAXR>(xs, R, reinterpret_cast<const float *>(sm + S::lnw), reinterpret_cast<const float *>(sm + S::lnb),
-                       reinterpret_cast<float *>(sm + S::red), tid);
+                       reinterpret_cast<float *>(sm + S::red), act_hi, act_lo, tid);
     __syncthreads();
 
-    // ---- 2. fc_in + bias + gelu_new: warp w = group w (features 32j + 4w ..)
+    // ---- 2. fc_in: warp w takes blocks 3w..3w+2 of both tiles; the 8 partial sums added in
+    //      warp order, + bias, gelu_new, into the h planes (fc_out's B operand)
     {
-        float acc[MAXR];
-        sl_group_dot<MAXR>(reinterpret_cast<const int8_t *>(sm + S::wi) + warp * 3072,
-                           reinterpret_cast<const __half *>(sm + S::wis) + warp * 96, xs, R, lane, acc);
-        if (lane < 8 && (lane & 1) == 0) {
-            const int f = warp * 4 + (lane >> 1);
-            const float b = reinterpret_cast<const float *>(sm + S::bi)[f];
+        float acc[2][4];
+        sl_mma<2>(sm + S::wi, reinterpret_cast<const __half *>(sm + S::wis), 24, 3 * warp, 3 * warp + 3, act_hi, act_lo,
+                  kHidden, lane, acc);
+        __syncthreads();  // every warp is done with the planes, which now take the partials
 #pragma unroll
-            for (int r = 0; r < MAXR; ++r)
-                if (r < R) hs[r * 32 + f] = gelu_new(__fadd_rn(acc[r], b));
-        }
+        for (int m = 0; m < 2; ++m)
+            *reinterpret_cast<float4 *>(fred + (warp * 2 + m) * 128 + lane * 4) =
+                make_float4(acc[m][0], acc[m][1], acc[m][2], acc[m][3]);
+    }
+    __syncthreads();
+    if (tid < 32 * R) {
+        const int r = tid >> 5, f = tid & 31;   // batch row, feature 32j + f
+        const int m = f >> 4, row = f & 15;
+        const int slot = (row & 7) * 16 + (r >> 1) * 4 + 2 * (row >> 3) + (r & 1);
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) v += fred[(w * 2 + m) * 128 + slot];
+        sl_act(h_hi, h_lo, 32, r, f, gelu_new(__fadd_rn(v, reinterpret_cast<const float *>(sm + S::bi)[f])));
     }
     __syncthreads();
 
-    // ---- 3. fc_out over the 32 features: thread t, output rows t, t + 256, t + 512, partial
-    //      sums into xs as [r][768] (LN2(x) is no longer needed)
+    // ---- 3. fc_out over the 32 features: warp w takes tiles 6w..6w+5 (output rows 96w..),
+    //      partial sums into opart[n][row]
+    {
+        float acc[6][4];
+        sl_mma<6>(sm + S::wo + warp * 6 * 512, reinterpret_cast<const __half *>(sm + S::wos) + warp * 6 * 16, 1, 0, 1,
+                  h_hi, h_lo, 32, lane, acc);
+        const int g = lane >> 2, t = lane & 3;
 #pragma unroll
-    for (int u = 0; u < 3; ++u) {
-        const int orow = tid + kSlThreads * u;
-        const int g = orow >> 2, k = orow & 3;
-        const float d = __half2float(reinterpret_cast<const __half *>(sm + S::wos)[g * 4 + k]);
-        float v[MAXR];
-        sl_block_dot<MAXR>(reinterpret_cast<const int8_t *>(sm + S::wo) + g * 128 + k * 32, d, hs, 32, R, v);
+        for (int m = 0; m < 6; ++m)
 #pragma unroll
-        for (int r = 0; r < MAXR; ++r)
-            if (r < R) xs[r * kHidden + orow] = v[r];
+            for (int q = 0; q < 4; ++q) {
+                const int n = 2 * t + (q & 1);
+                if (n < R) opart[n * kHidden + (6 * warp + m) * 16 + g + 8 * (q >> 1)] = acc[m][q];
+            }
     }
     __syncthreads();
     cluster_arrive();
@@ -750,7 +753,7 @@ __global__ void __launch_bounds__(kSlThreads) k_small_mlp(const SmallArgs a) {
         sum[q] = 0.f;
         if (i < R * 96) {
             const int r = i / 96, ol = i - r * 96;
-            const uint32_t base = smem_u32(xs + r * kHidden + 96 * c + ol);
+            const uint32_t base = smem_u32(opart + r * kHidden + 96 * c + ol);
 #pragma unroll
             for (int src = 0; src < kSlCluster; ++src) sum[q] += sl_ld_cluster(cluster_map(base, (uint32_t)src));
         }
@@ -770,5 +773,16 @@ __global__ void __launch_bounds__(kSlThreads) k_small_mlp(const SmallArgs a) {
     cluster_wait();
 }
 
+}  // namespace
+}  // namespace mossgpu
+
+namespace mossgpu {
+namespace {
+// a CTA of launch A and one of launch B fit on one SM (228 KB of shared memory, 1 KB reserved
+// per CTA) up to 4 rows, so each launch's CTAs start beside its predecessor's
+static_assert(SlAttnSmem<1>::total + SlMlpSmem<1>::total + 2048 <= 228 * 1024 &&
+                  SlAttnSmem<2>::total + SlMlpSmem<2>::total + 2048 <= 228 * 1024 &&
+                  SlAttnSmem<4>::total + SlMlpSmem<4>::total + 2048 <= 228 * 1024,
+              "launch A and B share an SM");
 }  // namespace
 }  // namespace mossgpu
