@@ -390,6 +390,62 @@ def run_reference_arm(args, rank, world):
 
 # ----------------------------------------------------------------------------- GPU arm
 
+SL_ATTN_PHASES = ["issue pre-wait copies", "dependency wait", "x in + LN1", "QKV + RoPE", "cluster barrier 1",
+                  "q/k/v gather + attention + CTA merge", "cluster barrier 2", "DSMEM merge", "proj + stores",
+                  "last cluster wait"]
+SL_MLP_PHASES = ["issue pre-wait copies", "dependency wait", "x in + LN2", "fc_in + GELU", "fc_out partials",
+                 "cluster barrier", "DSMEM reduce", "accumulator adds", "last cluster wait"]
+
+
+def run_phase_stamps(steps: int, stamps: bool = True):
+    """Batch-1 global step (one stream, 128 cached positions) on the library built with phase
+    stamps: thread 0 of every CTA of the 24 small-layer launches stamps %globaltimer at each
+    phase boundary.  Per phase: the median over CTAs, launches and steps; per launch: the
+    hand-off (the predecessor's last CTA ends -> this launch's median CTA leaves its wait)."""
+    import torch
+    if stamps:
+        os.environ["MOSSGPU_LIB_VARIANT"] = "stamps"
+    pkg = load_package()
+    pkg.build()
+    from moss_b200 import mossfile
+    weights = str(mossfile.ensure_synth_weights(Path(tempfile.gettempdir()) / "moss_b200_w0.moss", 0))
+    eng = pkg.Engine(weights, device=0, max_streams=2, max_ctx=128 + steps + 64)
+    s1 = eng.open()
+    x1 = np.random.default_rng(5).standard_normal((1, 768), dtype=np.float32).astype(np.float16).astype(np.float32)
+    eng.fill_state_random(s1, 128, seed=99)
+    for _ in range(5):
+        eng.global_step_embed([s1], x1, want_hidden=False)
+    eng.fill_state_random(s1, 128, seed=99)
+    st, step_us = [], []
+    for _ in range(steps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        eng.global_step_embed([s1], x1, want_hidden=False)
+        b.record()
+        torch.cuda.synchronize()
+        step_us.append(1000 * a.elapsed_time(b))
+        if stamps:
+            st.append(eng.small_layer_stamps().astype(np.int64))
+    eng.close()
+    if not stamps:
+        return
+    st = np.stack(st)  # [steps][24][96][12]
+    out = {"workload": "configs[0] batch-1 global step, 128 cached positions", "steps": steps,
+           "step_us_events": round(float(np.median(step_us)), 2)}
+    last = {0: 10, 1: 9}
+    for half, names in ((0, SL_ATTN_PHASES), (1, SL_MLP_PHASES)):
+        ph = st[:, half::2]  # [steps][12][96][12]
+        d = np.diff(ph[..., : last[half] + 1], axis=-1) / 1000.0
+        out["attn" if half == 0 else "mlp"] = {n: round(float(np.median(d[..., i])), 3) for i, n in enumerate(names)}
+        span = (ph[..., last[half]].max(axis=-1) - np.median(ph[..., 2], axis=-1)) / 1000.0
+        out[("attn" if half == 0 else "mlp") + "_after_wait_us"] = round(float(np.median(span)), 3)
+    ends = np.where(np.arange(24)[None, :, None] % 2 == 0, st[..., 10], st[..., 9]).max(axis=-1)  # [steps][24]
+    release = np.median(st[..., 2], axis=-1)
+    out["handoff_us"] = round(float(np.median((release[:, 1:] - ends[:, :-1]) / 1000.0)), 3)
+    out["layers_us"] = round(float(np.median((ends[:, -1] - st[:, 0, :, 0].min(axis=-1)) / 1000.0)), 2)
+    print(json.dumps(out), flush=True)
+
+
 def kernel_classes(R: int):
     """Algorithmic bytes and FLOPs per launch of each kernel class at R batch rows."""
     act = 4  # bytes per input element: fp32 rows, or the tensor-core image's two fp16 parts
@@ -894,6 +950,12 @@ def main():
     ap.add_argument("--profile-frames", type=int, default=0,
                     help="run this many frames of the workload after one warm-up frame and exit "
                          "(the command the ncu captures under profiles/ use)")
+    ap.add_argument("--profile-batch1", type=int, default=0,
+                    help="run this many batch-1 global steps (configs[0]) after 5 warm-up steps and exit "
+                         "(the command of the small-layer ncu captures)")
+    ap.add_argument("--phase-stamps", type=int, default=0,
+                    help="batch-1 global step (configs[0]) on the phase-stamp build: per-phase times "
+                         "of the two-launch layers over this many steps (profiles/small_layers_b1.md)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.lmin is None:
@@ -905,6 +967,9 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference_arm(args, rank, world)
+        return
+    if args.phase_stamps or args.profile_batch1:
+        run_phase_stamps(args.phase_stamps or args.profile_batch1, stamps=bool(args.phase_stamps))
         return
     if args.profile_codec:
         import torch

@@ -29,7 +29,9 @@ from pathlib import Path
 import numpy as np
 
 PKG = Path(__file__).resolve().parent
-LIB_PATH = PKG / "libmossgpu.so"
+# MOSSGPU_LIB_VARIANT=stamps loads (and builds) the profiling build with phase stamps instead
+LIB_VARIANT = os.environ.get("MOSSGPU_LIB_VARIANT", "")
+LIB_PATH = PKG / ("libmossgpu_stamps.so" if LIB_VARIANT == "stamps" else "libmossgpu.so")
 
 HIDDEN, HEADS, HEAD_DIM, FF, VOCAB = 768, 12, 64, 3072, 16384
 NVQ, CODEBOOK, AUDIO_PAD, SLOT_TOKEN, END_TOKEN, LOCAL_LEN, LAYERS = 16, 1024, 1024, 9, 7, 17, 12
@@ -46,7 +48,7 @@ EXPORTS = [
     "mossgpu_attention_decode_paged_noalloc", "mossgpu_set_gemm_path", "mossgpu_debug_matrix_tile_bytes",
     "mossgpu_stream_fork", "mossgpu_create_rows", "mossgpu_prefill_batch", "mossgpu_prefill_embeds_batch",
     "mossgpu_set_tc_policy", "mossgpu_op_device_status", "mossgpu_debug_inject_wait_timeout", "mossgpu_set_local_path",
-    "mossgpu_set_small_layers",
+    "mossgpu_set_small_layers", "mossgpu_debug_small_layer_stamps",
     "mossgpu_codec_create", "mossgpu_codec_destroy", "mossgpu_codec_last_error", "mossgpu_codec_samples_per_frame",
     "mossgpu_codec_launches_per_call", "mossgpu_codec_device_bytes", "mossgpu_codec_set_cuda_stream",
     "mossgpu_codec_open", "mossgpu_codec_close", "mossgpu_codec_reset", "mossgpu_codec_decode_chunk",
@@ -80,7 +82,7 @@ _LIB_LOCK = threading.Lock()
 
 def build(force: bool = False) -> Path:
     from . import buildlib as _b  # noqa: PLC0415
-    return _b.build(force=force)
+    return _b.build(force=force, variant=LIB_VARIANT)
 
 
 def lib() -> C.CDLL:
@@ -143,6 +145,7 @@ def lib() -> C.CDLL:
         L.mossgpu_debug_inject_wait_timeout.argtypes = [C.c_void_p, C.c_int]
         L.mossgpu_set_local_path.argtypes = [C.c_void_p, C.c_int]
         L.mossgpu_set_small_layers.argtypes = [C.c_void_p, C.c_int]
+        L.mossgpu_debug_small_layer_stamps.argtypes = [C.c_void_p, C.POINTER(C.c_ulonglong), C.c_size_t]
         L.mossgpu_attention_decode_paged_noalloc.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p,
                                                              C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]
         L.mossgpu_codec_create.restype = C.c_void_p
@@ -337,6 +340,14 @@ class Engine:
     def set_small_layers(self, mode: int):
         """Global layers of <= 8-row decode batches: 1 = two launches a layer (default), 0 = five."""
         self._check(self.lib.mossgpu_set_small_layers(self.h, mode))
+
+    def small_layer_stamps(self) -> np.ndarray:
+        """[24 launches][96 CTAs][12 phases] %globaltimer stamps (ns) of the last small-layer step;
+        only in a library built with phase stamps (MOSSGPU_LIB_VARIANT=stamps)."""
+        out = np.zeros((24, 96, 12), dtype=np.uint64)
+        self._check(self.lib.mossgpu_debug_small_layer_stamps(
+            self.h, out.ctypes.data_as(C.POINTER(C.c_ulonglong)), out.size))
+        return out
 
     def set_graphs(self, enable: bool):
         self._check(self.lib.mossgpu_set_graphs(self.h, int(enable)))

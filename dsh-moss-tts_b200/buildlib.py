@@ -15,23 +15,29 @@ FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std
          "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall", "-diag-suppress", "550", "-shared"]
 
 
-def stale() -> bool:
-    if not LIB.exists():
+# variants: "" = the product library; "stamps" = the same sources with phase stamps in the
+# small-batch layer kernels (-DMOSSGPU_PHASE_STAMPS), a profiling build beside it
+VARIANTS = {"": ([], LIB), "stamps": (["-DMOSSGPU_PHASE_STAMPS"], PKG / "libmossgpu_stamps.so")}
+
+
+def stale(lib: Path = LIB) -> bool:
+    if not lib.exists():
         return True
-    t = LIB.stat().st_mtime
+    t = lib.stat().st_mtime
     deps = [CSRC / s for s in SOURCES] + [CSRC / h for h in HEADERS] + [Path(__file__)]
     return any(p.stat().st_mtime > t for p in deps if p.exists())
 
 
-def build(force: bool = False, verbose: bool = False) -> Path:
-    if force or stale():
-        tmp = LIB.with_name(f".libmossgpu.{os.getpid()}.so")
-        cmd = [NVCC, *FLAGS, "-o", str(tmp), *[str(CSRC / s) for s in SOURCES]]
+def build(force: bool = False, verbose: bool = False, variant: str = "") -> Path:
+    defs, lib = VARIANTS[variant]
+    if force or stale(lib):
+        tmp = lib.with_name(f".{lib.stem}.{os.getpid()}.so")
+        cmd = [NVCC, *FLAGS, *defs, "-o", str(tmp), *[str(CSRC / s) for s in SOURCES]]
         r = subprocess.run(cmd, cwd=CSRC, capture_output=True, text=True)
         if r.returncode != 0:
             tmp.unlink(missing_ok=True)
             raise RuntimeError(f"nvcc failed ({r.returncode}):\n{r.stdout}\n{r.stderr}")
-        os.replace(tmp, LIB)  # atomic: concurrent builders never expose a half-written library
+        os.replace(tmp, lib)  # atomic: concurrent builders never expose a half-written library
         if verbose:
             print(r.stdout + r.stderr)
-    return LIB
+    return lib

@@ -234,6 +234,13 @@ int mossgpu_set_small_layers(mossgpu_engine *e, int mode) {
     return guarded(e, [&](mossgpu::Engine &g) { g.set_small_layers(mode); });
 }
 
+int mossgpu_debug_small_layer_stamps(mossgpu_engine *e, unsigned long long *out, size_t n) {
+    return guarded(e, [&](mossgpu::Engine &g) {
+        if (!out) throw std::runtime_error("out is required");
+        g.small_layer_stamps(out, n);
+    });
+}
+
 int mossgpu_set_gemm_path(mossgpu_engine *e, int mode) {
     return guarded(e, [&](mossgpu::Engine &g) { g.set_gemm_path(mode); });
 }

@@ -68,6 +68,7 @@ Engine::Engine(const std::string &path, int device, int max_streams, int max_ctx
     CK(cudaStreamCreateWithFlags(&own_stream_, cudaStreamNonBlocking));
     stream_ = own_stream_;
     if (const char *v = std::getenv("MOSSGPU_PDL")) pdl_ = std::strcmp(v, "0") != 0;
+    if (const char *v = std::getenv("MOSSGPU_ATTN_ROWS_MAX")) attn_rows_max_ = std::atoi(v);
     load_weights(path);
     pages_per_stream_ = (max_ctx + kPage - 1) / kPage;
     n_pages_ = kv_pages > 0 ? kv_pages : max_streams * pages_per_stream_;
@@ -743,7 +744,7 @@ void Engine::block_tc(const Layer &L, int li, bool local, int R, const int *row_
             f.err = dev_err_;
             launch_k(pdl_, k_attn_prefill_tc, dim3(unsigned(pf_tc_items_), kHeads), dim3(kPtThreads), kPtSmem, stream_, f);
             mark(KK_ATTN_PREFILL);
-        } else if (R <= kAttnRowsMaxTc) {
+        } else if (R <= attn_rows_max_) {
             launch_k(pdl_, k_attn_rows, dim3(R * kHeads), dim3(kArWarps * 32), 0, stream_, q_,
                      static_cast<const __half *>(t.kv), page_table_, pages_per_stream_, row_slot, row_pos, attn_,
                      bimg_a_, N, tc_parts(prec));
@@ -989,7 +990,7 @@ void Engine::global_layers(int R, const int *row_slot, const int *row_pos) {
         for (int li = 0; li < kLayers; ++li) block(global_[li], li, false, R, row_slot, row_pos, 0, x_);
         return;
     }
-    if (use_tc(R) ? R <= kAttnRowsMaxTc : R <= kGemvMaxRows) {  // every layer on k_attn_rows: no plan
+    if (use_tc(R) ? R <= attn_rows_max_ : R <= kGemvMaxRows) {  // every layer on k_attn_rows: no plan
         plain_first_ = true;
         for (int li = 0; li < kLayers; ++li) block(global_[li], li, false, R, row_slot, row_pos, 0, x_);
         return;
@@ -1027,6 +1028,7 @@ void Engine::block_small(const Layer &L, int li, int R, const int *row_slot, con
     const int R2 = R <= 1 ? 1 : R <= 2 ? 2 : R <= 4 ? 4 : 8;
     for (int half = 0; half < 2; ++half) {
         const int p = 2 * li + half;
+        a.launch = p;
         a.ln_w = half ? L.ln2_w : L.ln1_w;
         a.ln_b = half ? L.ln2_b : L.ln1_b;
         a.x0 = x_;
@@ -1055,6 +1057,19 @@ void Engine::block_small(const Layer &L, int li, int R, const int *row_slot, con
         }
     }
     if (li == 0) plain_first_ = false;
+}
+
+void Engine::small_layer_stamps(unsigned long long *out, size_t n) {
+#ifdef MOSSGPU_PHASE_STAMPS
+    const size_t total = size_t(kSlStampLaunches) * kSlCtas * kSlStampPhases;
+    if (n < total) throw std::runtime_error("phase stamps need " + std::to_string(total) + " entries");
+    CK(cudaStreamSynchronize(stream_));
+    CK(cudaMemcpyFromSymbol(out, g_sl_stamps, total * sizeof(unsigned long long)));
+#else
+    (void)out;
+    (void)n;
+    throw std::runtime_error("this library was built without phase stamps (-DMOSSGPU_PHASE_STAMPS)");
+#endif
 }
 
 // ------------------------------------------------------------------ host helpers

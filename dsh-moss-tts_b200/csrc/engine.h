@@ -107,6 +107,9 @@ public:
     // Global layers of decode batches of at most kGemvMaxRows rows: 1 = two launches per layer
     // (layer_small.cuh, the default), 0 = the five CUDA-core GEMV / attention launches.
     void set_small_layers(int mode);
+    // Phase stamps of the last small-layer step (builds with -DMOSSGPU_PHASE_STAMPS): copies
+    // [24 launches][96 CTAs][12 phases] %globaltimer values into out; throws in other builds.
+    void small_layer_stamps(unsigned long long *out, size_t n);
     void set_cuda_stream(void *s);
     void fill_state_random(int sid, int n_pos, uint64_t seed);
     void set_kernel_timing(bool on);
@@ -231,6 +234,7 @@ private:
     // lnf_xfix_ is the one the ln_f after the layers reads its rows from (null on the other
     // paths, whose rows are in x_)
     int small_layers_ = 1;
+    int attn_rows_max_ = kAttnRowsMaxTc;  // MOSSGPU_ATTN_ROWS_MAX overrides it (measurement)
     bool in_prefill_ = false;
     long long *sd_ = nullptr;
     const long long *lnf_xfix_ = nullptr;

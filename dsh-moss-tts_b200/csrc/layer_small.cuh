@@ -5,11 +5,15 @@
 // its time is the hand-offs between them.  Two launches per layer keep only the hand-offs that
 // need the whole layer's output (proj and fc_out read every head / every feature); the rest
 // run inside a thread-block cluster, synchronised by cluster barriers and exchanging data
-// through distributed shared memory (DSMEM).  Everything that does not depend on the previous
+// through distributed shared memory (DSMEM).  Every exchange is a push: the producing threads
+// store into the consuming CTAs' shared memory (st.shared::cluster), and one cluster barrier
+// (release / acquire) later the consumers read their own shared memory, so no phase waits on a
+// remote load's round trip; the first remote store of a CTA waits on a cluster barrier phase
+// that every CTA arrives at when it starts.  Everything that does not depend on the previous
 // launch -- the weights, LayerNorm parameters, biases, RoPE factors and the rows' cached K/V
 // pages -- is copied into shared memory before the launch waits for its predecessor
 // (programmatic dependent launch), so those HBM reads overlap the previous launch.  Global
-// stores come after a CTA's last cluster-barrier arrive, so no barrier waits for them.
+// stores come after a CTA's last cluster barrier, so no barrier waits for them.
 //
 // The contractions run on the tensor cores (mma.sync m16n8k16, fp32 accumulation): weights as
 // the MMA fragment records of k_repack_mma (exact int8 -> fp16), activations split into fp16
@@ -17,15 +21,16 @@
 // block's products are scaled by its per-row scale and added in fp32.
 //
 // Launch A (k_small_attn), 12 clusters of 8 CTAs, cluster = attention head hd, CTA rank c:
-//   x in; LN1 (every CTA, redundantly); QKV rows for dims 8c..8c+7 of q, k and v of the head
-//   (24 weight rows) with bias and RoPE; q, k, v gathered over DSMEM; attention over pages
-//   c, c+8, ... of each row (online softmax); the 8 partial results merged over DSMEM; proj
-//   rows 96c..96c+95 over the head's 64 columns added into the accumulator; the CTA's k, v
-//   dims appended to the KV cache.
+//   x in; LN1 (every CTA, redundantly); QKV
+//   rows for dims 8c..8c+7 of q, k and v of the head (24 weight rows) with bias and RoPE,
+//   pushed to the head's 8 CTAs; attention over pages c, c+8, ... of each row (online
+//   softmax); the CTA's partial result pushed to the 8 CTAs and merged there; proj rows
+//   96c..96c+95 over the head's 64 columns added into the accumulator; the CTA's k, v dims
+//   appended to the KV cache.
 // Launch B (k_small_mlp), 12 clusters of 8 CTAs, CTA j = blockIdx.x (features 32j..32j+31):
 //   x in; LN2; fc_in rows 32j.. + bias + gelu_new; fc_out column block j (a partial sum of
-//   every output row); the cluster's 8 partials reduced over DSMEM (CTA c: rows 96c..96c+95)
-//   and added into the accumulator.
+//   every output row), each warp's 96 output rows pushed to the CTA that reduces them (CTA c:
+//   rows 96c..96c+95); the 8 partials summed in rank order and added into the accumulator.
 //
 // The residual stream between launches is an int64 accumulator per row element in units of
 // 2^-32 (|x| < 2^31), to which the launches add with atomic adds.  Integer addition is
@@ -50,9 +55,26 @@ constexpr int kSlMaxRows = 8;
 constexpr int kSlCtas = 96;     // both launches: 12 clusters of 8
 static_assert(kHeads * kSlCluster == kSlCtas && kFF / 32 == kSlCtas, "layer split");
 
+// Phase stamps (builds with -DMOSSGPU_PHASE_STAMPS only, `bench.py --phase-stamps`): thread 0 of
+// every CTA records %globaltimer at each phase boundary of launch p of a step into
+// g_sl_stamps[p][CTA][phase]; small_layer_stamps() in engine.cu copies them out.
+constexpr int kSlStampLaunches = 2 * kLayers;
+constexpr int kSlStampPhases = 12;
+#ifdef MOSSGPU_PHASE_STAMPS
+__device__ unsigned long long g_sl_stamps[kSlStampLaunches][kSlCtas][kSlStampPhases];
+#define SL_STAMP(ph) \
+    do { \
+        if (threadIdx.x == 0) g_sl_stamps[a.launch][blockIdx.x][ph] = global_ns(); \
+    } while (0)
+#else
+#define SL_STAMP(ph) \
+    do { \
+    } while (0)
+#endif
+
 // (row, page) K/V pairs a CTA of launch A stages in shared memory (4 KB each): as many as let
 // it share an SM with a CTA of launch B (its successor's CTAs start beside it)
-__host__ __device__ constexpr int sl_kv_slots(int maxr) { return maxr <= 1 ? 12 : maxr <= 2 ? 10 : maxr <= 4 ? 6 : 2; }
+__host__ __device__ constexpr int sl_kv_slots(int maxr) { return maxr <= 1 ? 12 : maxr <= 2 ? 10 : maxr <= 4 ? 4 : 2; }
 
 struct SmallArgs {
     LfMat attn, proj, fc_in, fc_out;   // fragment records: [rows/16][nb][512] int8, [rows/16][nb][16] fp16
@@ -68,6 +90,7 @@ struct SmallArgs {
     const int *row_slot, *row_pos;
     const float2 *rope;
     int R;
+    int launch;                 // p = 2 * layer + half (phase stamps)
 };
 
 __device__ __forceinline__ void sl_cp16(void *dst, const void *src) {
@@ -78,15 +101,14 @@ __device__ __forceinline__ void sl_cp8(void *dst, const void *src) {
 }
 __device__ __forceinline__ void sl_cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void sl_cp_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
-__device__ __forceinline__ float sl_ld_cluster(uint32_t addr) {
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-    return v;
+__device__ __forceinline__ void sl_st_cluster2(uint32_t addr, float x, float y) {
+    asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(x), "f"(y) : "memory");
 }
-__device__ __forceinline__ float4 sl_ld_cluster4(uint32_t addr) {
-    float4 v;
-    asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr) : "memory");
-    return v;
+__device__ __forceinline__ void sl_st_cluster4(uint32_t addr, float x, float y, float z, float w) {
+    asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(x), "f"(y), "f"(z), "f"(w) : "memory");
+}
+__device__ __forceinline__ void sl_st_cluster_h2(uint32_t addr, __half2 h) {
+    asm volatile("st.shared::cluster.b32 [%0], %1;" ::"r"(addr), "r"(*reinterpret_cast<const uint32_t *>(&h)) : "memory");
 }
 __device__ __forceinline__ void sl_add_fixed(long long *p, long long v) {
     atomicAdd(reinterpret_cast<unsigned long long *>(p), static_cast<unsigned long long>(v));
@@ -123,7 +145,6 @@ __device__ __forceinline__ void sl_residual_in(const SmallArgs &a, float *xs, lo
         *reinterpret_cast<float4 *>(xs + r * kHidden + 4 * q4) = v;
     }
 }
-
 
 // column k of activation row r -> its place in an MMA B-operand plane ([8][stride] fp16):
 // lf_bpos order, so that a lane's 16-byte load covers both K steps of a 32-column block
@@ -253,19 +274,20 @@ struct SlAttnSmem {
     static constexpr int red = meta + 5 * kSlMaxRows * 4;      // float [8] LayerNorm partial sums
     static constexpr int xs = red + 8 * 4;                     // float [MAXR][768] x
     static constexpr int xfix = xs + MAXR * kHidden * 4;       // int64 [MAXR][96] x of the proj rows (head 0)
-    static constexpr int act = xfix + MAXR * 96 * 8;           // half [2][8][768] LN1(x) hi, lo; then QKV partials
+    static constexpr int act = xfix + MAXR * 96 * 8;           // half [2][8][768] LN1(x) hi, lo; then QKV
+                                                               // partials; then [8 CTAs][MAXR][68] attention partials
     static constexpr int own = act + 2 * 8 * kHidden * 2;      // float [MAXR][24] q, k, v dims 8c..8c+7
     static constexpr int full = own + MAXR * 24 * 4;           // float [MAXR][192] the head's q | k | v
     static constexpr int newkv = full + MAXR * 192 * 4;        // half [MAXR][2][64] k, v of the new position
     static constexpr int wst = newkv + MAXR * 256;             // float [8 warps][68] m, l, -, -, o[64]
-    static constexpr int part = wst + 8 * kPartStride * 4;     // float [MAXR][68] the CTA's partial
-    static constexpr int ohp = part + MAXR * kPartStride * 4;  // half [2][8][64] attention output hi, lo
+    static constexpr int ohp = wst + 8 * kPartStride * 4;      // half [2][8][64] attention output hi, lo
     static constexpr int kvs = ohp + 2 * 8 * kHeadDim * 2;     // half [slots][k|v][16][64]
     static constexpr int total = kvs + kSlots * 4096;
-    static_assert(rs % 16 == 0 && xs % 16 == 0 && xfix % 16 == 0 && act % 16 == 0 && own % 16 == 0 &&
-                      full % 16 == 0 && newkv % 16 == 0 && part % 16 == 0 && ohp % 16 == 0 && kvs % 16 == 0,
+    static_assert(rs % 16 == 0 && xs % 16 == 0 && xfix % 16 == 0 && act % 16 == 0 && own % 16 == 0 && full % 16 == 0 &&
+                      newkv % 16 == 0 && ohp % 16 == 0 && kvs % 16 == 0,
                   "16-byte aligned regions");
-    static_assert(8 * 3 * 128 * 4 <= 2 * 8 * kHidden * 2, "QKV partials fit the activation planes");
+    static_assert(8 * 3 * 128 * 4 <= 2 * 8 * kHidden * 2 && kSlCluster * MAXR * kPartStride * 4 <= 2 * 8 * kHidden * 2,
+                  "QKV partials and the cluster's attention partials fit the activation planes");
 };
 
 template <int MAXR>
@@ -284,15 +306,17 @@ __global__ void __launch_bounds__(kSlThreads) k_small_attn(const SmallArgs a) {
     long long *xfix = reinterpret_cast<long long *>(sm + S::xfix);
     __half *act_hi = reinterpret_cast<__half *>(sm + S::act), *act_lo = act_hi + 8 * kHidden;
     float *qred = reinterpret_cast<float *>(sm + S::act);  // [8 warps][3][128], after the QKV MMAs
+    float *precv = reinterpret_cast<float *>(sm + S::act);  // [8 CTAs][MAXR][68], after cluster barrier 1
     float *own = reinterpret_cast<float *>(sm + S::own);
     float *full = reinterpret_cast<float *>(sm + S::full);
     __half *newkv = reinterpret_cast<__half *>(sm + S::newkv);
     float *wst = reinterpret_cast<float *>(sm + S::wst);
-    float *part = reinterpret_cast<float *>(sm + S::part);
     __half *oh_hi = reinterpret_cast<__half *>(sm + S::ohp), *oh_lo = oh_hi + 8 * kHeadDim;
     const float *bq = reinterpret_cast<const float *>(sm + S::bq);
     const float *bp = reinterpret_cast<const float *>(sm + S::bp);
     const float2 *rs = reinterpret_cast<const float2 *>(sm + S::rs);
+    SL_STAMP(0);
+    cluster_arrive_relaxed();  // this CTA runs: matched by the wait before its first remote store
 
     // ---- 0. before the wait: everything that does not depend on the previous launch.  The
     //      per-row control (slot, position, page table) was written by the host or by a kernel
@@ -365,9 +389,11 @@ __global__ void __launch_bounds__(kSlThreads) k_small_attn(const SmallArgs a) {
         }
     }
     sl_cp_commit();
+    SL_STAMP(1);
 
     pdl_wait();
     pdl_trigger();
+    SL_STAMP(2);
 
     // ---- 1. x in (head 0 keeps its proj rows of x for the accumulator), LN1 into the planes
     sl_residual_in(a, xs, hd == 0 ? xfix : nullptr, 96 * c, tid);
@@ -376,6 +402,7 @@ __global__ void __launch_bounds__(kSlThreads) k_small_attn(const SmallArgs a) {
     sl_layernorm<MAXR>(xs, R, reinterpret_cast<const float *>(sm + S::lnw), reinterpret_cast<const float *>(sm + S::lnb),
                        reinterpret_cast<float *>(sm + S::red), act_hi, act_lo, tid);
     __syncthreads();
+    SL_STAMP(3);
 
     // ---- 2. QKV: warp w takes blocks 3w..3w+2 of the three tiles; the 8 partial sums are
     //      added in warp order, then bias and RoPE (pairs 2i, 2i+1 of q and k; EPI_QKV order)
@@ -390,8 +417,12 @@ __global__ void __launch_bounds__(kSlThreads) k_small_attn(const SmallArgs a) {
                 make_float4(acc[m][0], acc[m][1], acc[m][2], acc[m][3]);
     }
     __syncthreads();
-    if (tid < 12 * R) {
-        const int r = tid / 12, e = tid - r * 12;
+    cluster_wait();  // every CTA of the cluster runs: its shared memory may be written
+    // item (row r, part m, dim pair i0) for destination CTA d: the 8 warps' partial sums added in
+    // warp order, bias, RoPE; then pushed into CTA d (each destination's thread recomputes it)
+    for (int it = tid; it < kSlCluster * 12 * R; it += kSlThreads) {
+        const int d = it & (kSlCluster - 1), k = it >> 3;
+        const int r = k / 12, e = k - r * 12;
         const int m = e >> 2, i0 = (e & 3) * 2;   // tile (q, k, v), first dim of the pair
         const int j = 2 * (c & 1) + (r & 1);      // fragment slot: row half, column parity
         float v0 = 0.f, v1 = 0.f;
@@ -408,26 +439,21 @@ __global__ void __launch_bounds__(kSlThreads) k_small_attn(const SmallArgs a) {
             o0 = __fsub_rn(__fmul_rn(v0, cs.x), __fmul_rn(v1, cs.y));
             o1 = __fadd_rn(__fmul_rn(v1, cs.x), __fmul_rn(v0, cs.y));
         }
-        own[r * 24 + m * 8 + i0] = o0;
-        own[r * 24 + m * 8 + i0 + 1] = o1;
-    }
-    __syncthreads();
-    cluster_arrive();
-    cluster_wait();
-
-    // ---- 3. the head's q, k, v from the 8 CTAs; the new position's k, v as the cache holds them
-    for (int i = tid; i < R * 48; i += kSlThreads) {  // (row, part, source CTA, 4-float half)
-        const int r = i / 48, e = i - r * 48;
-        const int prt = e >> 4, src = (e >> 1) & 7, hf = e & 1;
-        const float4 v = sl_ld_cluster4(cluster_map(smem_u32(own + r * 24 + prt * 8 + hf * 4), (uint32_t)src));
-        *reinterpret_cast<float4 *>(full + r * 192 + prt * kHeadDim + src * 8 + hf * 4) = v;
-        if (prt > 0) {
-            __half2 *nk = reinterpret_cast<__half2 *>(newkv + r * 128 + (prt - 1) * kHeadDim + src * 8 + hf * 4);
-            nk[0] = __floats2half2_rn(v.x, v.y);
-            nk[1] = __floats2half2_rn(v.z, v.w);
+        if (d == c) {
+            own[r * 24 + m * 8 + i0] = o0;
+            own[r * 24 + m * 8 + i0 + 1] = o1;
         }
+        // ---- 3. q, k, v dims 8c + i0, 8c + i0 + 1 of row r into CTA d, and the new position's
+        //      k, v as the cache holds them (fp16)
+        sl_st_cluster2(cluster_map(smem_u32(full + r * 192 + m * kHeadDim + c * 8 + i0), (uint32_t)d), o0, o1);
+        if (m > 0)
+            sl_st_cluster_h2(cluster_map(smem_u32(newkv + r * 128 + (m - 1) * kHeadDim + c * 8 + i0), (uint32_t)d),
+                             __floats2half2_rn(o0, o1));
     }
-    __syncthreads();
+    SL_STAMP(4);
+    cluster_arrive();  // release: this thread's pushes
+    cluster_wait();    // acquire: every CTA's pushes are visible
+    SL_STAMP(5);
     // ---- 4. attention over this CTA's pages: warp w takes row w / WPR, items sub, sub + WPR,
     //      ...; lanes as in k_attn_rows (8 lanes a position, 8 dims a lane, 4 positions a step)
     constexpr int WPR = 8 / MAXR;
@@ -545,7 +571,9 @@ __global__ void __launch_bounds__(kSlThreads) k_small_attn(const SmallArgs a) {
         }
     }
     __syncthreads();
-    // the CTA's partial of each row: its WPR warps merged (a warp with no page: m = -inf)
+    // the CTA's partial of each row: its WPR warps merged (a warp with no page: m = -inf), pushed
+    // into slot c of every CTA's partials (the activation planes are free in every CTA once it
+    // passed cluster barrier 1)
     for (int i = tid; i < R * kHeadDim; i += kSlThreads) {
         const int r = i / kHeadDim, d = i - r * kHeadDim;
         float M = -INFINITY;
@@ -559,30 +587,30 @@ __global__ void __launch_bounds__(kSlThreads) k_small_attn(const SmallArgs a) {
             L = fmaf(ws[1], wgt, L);
             y = fmaf(ws[4 + d], wgt, y);
         }
-        float *p = part + r * kPartStride;
-        if (d == 0) {
-            p[0] = M;
-            p[1] = L;
+        const uint32_t pa = smem_u32(precv + (c * MAXR + r) * kPartStride);
+#pragma unroll
+        for (int dst = 0; dst < kSlCluster; ++dst) {
+            const uint32_t ra = cluster_map(pa, (uint32_t)dst);
+            if (d == 0) sl_st_cluster2(ra, M, L);
+            st_cluster_f32(ra + 16 + 4 * d, y);
         }
-        p[4 + d] = y;
     }
-    __syncthreads();
-    cluster_arrive();
-    cluster_wait();
-
+    SL_STAMP(6);
+    cluster_arrive();  // release: this thread's pushes
+    cluster_wait();    // acquire: the 8 partials of every row are here
+    SL_STAMP(7);
 
     // ---- 5. the 8 CTAs' partials merged (every CTA, for its proj rows) into the planes
     for (int i = tid; i < R * kHeadDim; i += kSlThreads) {
         const int r = i / kHeadDim, d = i - r * kHeadDim;
-        const uint32_t base = smem_u32(part + r * kPartStride);
         float pm[kSlCluster], pl[kSlCluster], po[kSlCluster];
         float M = -INFINITY;
 #pragma unroll
         for (int s = 0; s < kSlCluster; ++s) {
-            const uint32_t ra = cluster_map(base, (uint32_t)s);
-            pm[s] = sl_ld_cluster(ra);
-            pl[s] = sl_ld_cluster(ra + 4);
-            po[s] = sl_ld_cluster(ra + 16 + 4 * d);
+            const float *ps = precv + (s * MAXR + r) * kPartStride;
+            pm[s] = ps[0];
+            pl[s] = ps[1];
+            po[s] = ps[4 + d];
             M = fmaxf(M, pm[s]);
         }
         float L = 0.f, y = 0.f;
@@ -594,8 +622,8 @@ __global__ void __launch_bounds__(kSlThreads) k_small_attn(const SmallArgs a) {
         }
         sl_act(oh_hi, oh_lo, kHeadDim, r, d, y / L);
     }
-    cluster_arrive();  // done with the other CTAs' shared memory (waited for before exiting)
     __syncthreads();
+    SL_STAMP(8);
 
     // ---- 6. proj rows 96c..96c+95 over the head's 64 columns (warp w: tile 6c + w) into the
     //      accumulator (head 0 adds x and the bias); then this CTA's global stores: its k, v
@@ -629,7 +657,8 @@ __global__ void __launch_bounds__(kSlThreads) k_small_attn(const SmallArgs a) {
         z[0] = 0;
         z[1] = 0;
     }
-    cluster_wait();
+    SL_STAMP(9);
+    SL_STAMP(10);
 }
 
 // ------------------------------------------------------------------ launch B: MLP half
@@ -648,10 +677,13 @@ struct SlMlpSmem {
     static constexpr int xs = red + 8 * 4;                // float [MAXR][768] x
     static constexpr int xfix = xs + MAXR * kHidden * 4;  // int64 [MAXR][96] x of the reduce rows (cluster 0)
     static constexpr int act = xfix + MAXR * 96 * 8;      // half [2][8][768] LN2(x) hi, lo; then fc_in partials
-                                                          // [8 warps][2][128] float; then fc_out partials [8][768] float
+                                                          // [8 warps][2][128] float
     static constexpr int hpl = act + 2 * 8 * kHidden * 2; // half [2][8][32] gelu(fc_in) hi, lo
-    static constexpr int total = hpl + 2 * 8 * 32 * 2;
-    static_assert(xs % 16 == 0 && xfix % 16 == 0 && act % 16 == 0 && hpl % 16 == 0 && bi % 16 == 0 && bo % 16 == 0,
+    static constexpr int orecv = hpl + 2 * 8 * 32 * 2;    // float [8 CTAs][MAXR][8 g][12 (m, h)]: fc_out
+                                                          // partials of the CTA's reduce row 16 m + g + 8 h,
+                                                          // pushed by the cluster's CTAs
+    static constexpr int total = orecv + kSlCluster * MAXR * 96 * 4;
+    static_assert(xs % 16 == 0 && xfix % 16 == 0 && act % 16 == 0 && hpl % 16 == 0 && orecv % 16 == 0 && bi % 16 == 0 && bo % 16 == 0,
                   "16-byte aligned regions");
 };
 
@@ -670,8 +702,10 @@ __global__ void __launch_bounds__(kSlThreads) k_small_mlp(const SmallArgs a) {
     long long *xfix = reinterpret_cast<long long *>(sm + S::xfix);
     __half *act_hi = reinterpret_cast<__half *>(sm + S::act), *act_lo = act_hi + 8 * kHidden;
     float *fred = reinterpret_cast<float *>(sm + S::act);   // [8 warps][2][128], after the fc_in MMAs
-    float *opart = reinterpret_cast<float *>(sm + S::act);  // [8][768], after the fc_in sums
+    float *orecv = reinterpret_cast<float *>(sm + S::orecv);
     __half *h_hi = reinterpret_cast<__half *>(sm + S::hpl), *h_lo = h_hi + 8 * 32;
+    SL_STAMP(0);
+    cluster_arrive_relaxed();  // this CTA runs: matched by the wait before its first remote store
 
     // ---- 0. before the wait: weights, LN2, biases
     sl_copy(sm + S::wi, a.fc_in.qm + (size_t)2 * j * 24 * 512, 2 * 24 * 32, tid);  // tiles 2j, 2j + 1: contiguous
@@ -688,9 +722,11 @@ __global__ void __launch_bounds__(kSlThreads) k_small_mlp(const SmallArgs a) {
     if (tid < 8) sl_cp16(sm + S::bi + tid * 16, a.fc_in_b + 32 * j + 4 * tid);
     else if (tid < 32) sl_cp16(sm + S::bo + (tid - 8) * 16, a.fc_out_b + 96 * c + 4 * (tid - 8));
     sl_cp_commit();
+    SL_STAMP(1);
 
     pdl_wait();
     pdl_trigger();
+    SL_STAMP(2);
 
     // ---- 1. x in (cluster 0 keeps its reduce rows of x for the accumulator), LN2 into the planes
     sl_residual_in(a, xs, first_cluster ? xfix : nullptr, 96 * c, tid);
@@ -699,6 +735,7 @@ __global__ void __launch_bounds__(kSlThreads) k_small_mlp(const SmallArgs a) {
     sl_layernorm<MAXR>(xs, R, reinterpret_cast<const float *>(sm + S::lnw), reinterpret_cast<const float *>(sm + S::lnb),
                        reinterpret_cast<float *>(sm + S::red), act_hi, act_lo, tid);
     __syncthreads();
+    SL_STAMP(3);
 
     // ---- 2. fc_in: warp w takes blocks 3w..3w+2 of both tiles; the 8 partial sums added in
     //      warp order, + bias, gelu_new, into the h planes (fc_out's B operand)
@@ -723,29 +760,40 @@ __global__ void __launch_bounds__(kSlThreads) k_small_mlp(const SmallArgs a) {
         sl_act(h_hi, h_lo, 32, r, f, gelu_new(__fadd_rn(v, reinterpret_cast<const float *>(sm + S::bi)[f])));
     }
     __syncthreads();
+    SL_STAMP(4);
 
-    // ---- 3. fc_out over the 32 features: warp w takes tiles 6w..6w+5 (output rows 96w..),
-    //      partial sums into opart[n][row]
+    // ---- 3. fc_out over the 32 features: warp w takes tiles 6w..6w+5 (output rows 96w..96w+95,
+    //      which CTA w of the cluster reduces) and pushes its partial sums into slot c of that
+    //      CTA's orecv
+    cluster_wait();  // every CTA of the cluster runs: its shared memory may be written
     {
         float acc[6][4];
         sl_mma<6>(sm + S::wo + warp * 6 * 512, reinterpret_cast<const __half *>(sm + S::wos) + warp * 6 * 16, 1, 0, 1,
                   h_hi, h_lo, 32, lane, acc);
+        // lane (g, t) holds rows 16 m + g + 8 h of batch rows 2t, 2t + 1: 12 contiguous floats
+        // a batch row, three 16-byte remote stores
         const int g = lane >> 2, t = lane & 3;
+        const uint32_t dst = cluster_map(smem_u32(orecv + c * MAXR * 96 + g * 12), (uint32_t)warp);
 #pragma unroll
-        for (int m = 0; m < 6; ++m)
+        for (int par = 0; par < 2; ++par) {
+            const int n = 2 * t + par;
+            if (n < R) {
+                const uint32_t ra = dst + (uint32_t)(n * 96 * 4);
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const int n = 2 * t + (q & 1);
-                if (n < R) opart[n * kHidden + (6 * warp + m) * 16 + g + 8 * (q >> 1)] = acc[m][q];
+                for (int k = 0; k < 3; ++k)
+                    sl_st_cluster4(ra + 16 * k, acc[2 * k][par], acc[2 * k][2 + par], acc[2 * k + 1][par],
+                                   acc[2 * k + 1][2 + par]);
             }
+        }
     }
-    __syncthreads();
-    cluster_arrive();
-    cluster_wait();
+    SL_STAMP(5);
+    cluster_arrive();  // release: this thread's pushes
+    cluster_wait();    // acquire: the 8 partials of the CTA's rows are here
+    SL_STAMP(6);
 
-    // ---- 4. the cluster's 8 partials of rows 96c..96c+95, summed in rank order; after the
-    //      last arrive, into the accumulator (cluster 0 adds x and the bias), and this CTA's 8
-    //      columns of D[(p + 2) % 3] zeroed
+    // ---- 4. the cluster's 8 partials of rows 96c..96c+95, summed in rank order, into the
+    //      accumulator (cluster 0 adds x and the bias), and this CTA's 8 columns of
+    //      D[(p + 2) % 3] zeroed
     float sum[RPT];
 #pragma unroll
     for (int q = 0; q < RPT; ++q) {
@@ -753,12 +801,13 @@ __global__ void __launch_bounds__(kSlThreads) k_small_mlp(const SmallArgs a) {
         sum[q] = 0.f;
         if (i < R * 96) {
             const int r = i / 96, ol = i - r * 96;
-            const uint32_t base = smem_u32(opart + r * kHidden + 96 * c + ol);
 #pragma unroll
-            for (int src = 0; src < kSlCluster; ++src) sum[q] += sl_ld_cluster(cluster_map(base, (uint32_t)src));
+            const int m = ol >> 4, g = ol & 7, h = (ol >> 3) & 1;
+#pragma unroll
+            for (int src = 0; src < kSlCluster; ++src) sum[q] += orecv[(src * MAXR + r) * 96 + g * 12 + 2 * m + h];
         }
     }
-    cluster_arrive();  // done with the other CTAs' shared memory (waited for before exiting)
+    SL_STAMP(7);
 #pragma unroll
     for (int q = 0; q < RPT; ++q) {
         const int i = tid + q * kSlThreads;
@@ -770,7 +819,8 @@ __global__ void __launch_bounds__(kSlThreads) k_small_mlp(const SmallArgs a) {
         }
     }
     if (tid < R * 8) a.d_zero[(size_t)(tid >> 3) * kHidden + blockIdx.x * 8 + (tid & 7)] = 0;
-    cluster_wait();
+    SL_STAMP(8);
+    SL_STAMP(9);
 }
 
 }  // namespace

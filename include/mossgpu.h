@@ -176,6 +176,12 @@ int mossgpu_set_local_path(mossgpu_engine *e, int mode);
  * 0 = five launches per layer (QKV, attention, proj, fc_in, fc_out GEMV kernels).
  * Prefill passes always take the five-launch form. */
 int mossgpu_set_small_layers(mossgpu_engine *e, int mode);
+/* Profiling aid for the two-launch layers: in a library built with -DMOSSGPU_PHASE_STAMPS
+ * (`bench.py --phase-stamps` builds one beside the product library), thread 0 of every CTA
+ * stamps %globaltimer (ns) at each phase boundary of the last step's small-layer launches;
+ * copies them as [24 launches][96 CTAs][12 phases] (n >= 27,648 entries).  Other builds return
+ * non-zero ("built without phase stamps").  No counterpart in the reference. */
+int mossgpu_debug_small_layer_stamps(mossgpu_engine *e, unsigned long long *out, size_t n);
 int mossgpu_set_gemm_path(mossgpu_engine *e, int mode);
 /* Tensor-core GEMM form by batch size: batches of at least direct_min_rows padded rows run
  * one CTA per (128 weight rows, slice of direct_rows batch rows) over the whole K with the
