@@ -83,6 +83,10 @@ Engine::~Engine() {
         if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
         for (cudaEvent_t ev : kv.second.events) cudaEventDestroy(ev);
     }
+    for (auto &ce : call_events_) {
+        cudaEventDestroy(ce.first);
+        cudaEventDestroy(ce.second);
+    }
     for (void *p : owned_) cudaFree(p);
     for (void *p : pinned_) cudaFreeHost(p);
     if (own_stream_) cudaStreamDestroy(own_stream_);
@@ -1652,7 +1656,7 @@ const char *kernel_kind_name(int kind) {
         "qkv_global", "attn_decode_paged", "proj_global", "fc_in_global", "fc_out_global", "ln_f",
         "qkv_local", "attn_local", "proj_local", "fc_in_local", "fc_out_local", "gate_w8a8",
         "audio_heads", "sample", "frame_commit", "build_activation_image", "attn_combine", "attn_prefill", "qkv_rope",
-        "local_decoder_fused", "small_layer_attn", "small_layer_mlp"};
+        "local_decoder_fused", "small_layer_attn", "small_layer_mlp", "call_graph"};
     return (kind >= 0 && kind < KK_COUNT) ? names[kind] : "?";
 }
 
@@ -1671,9 +1675,17 @@ template <class F>
 void Engine::run_captured(uint64_t key, F &&issue) {
     launches_ = 0;
     last_graph_ = nullptr;
+    std::pair<cudaEvent_t, cudaEvent_t> ce{nullptr, nullptr};
+    if (call_timing_) {
+        CK(cudaEventCreate(&ce.first));
+        CK(cudaEventCreate(&ce.second));
+        call_events_.push_back(ce);
+        CK(cudaEventRecord(ce.first, stream_));
+    }
     if (!use_graphs_) {
         issue();
         CK(cudaGetLastError());
+        if (ce.second) CK(cudaEventRecord(ce.second, stream_));
         return;
     }
     key |= (uint64_t(timing_) << 48) | (uint64_t(gemm_path_) << 50);  // both change what is captured
@@ -1705,11 +1717,21 @@ void Engine::run_captured(uint64_t key, F &&issue) {
         it = graphs_.emplace(key, std::move(g)).first;
     }
     CK(cudaGraphLaunch(it->second.exec, stream_));
+    if (ce.second) CK(cudaEventRecord(ce.second, stream_));
     launches_ = it->second.launches;
     last_graph_ = timing_ ? &it->second : nullptr;
 }
 
 void Engine::accumulate_timing() {
+    for (auto &ce : call_events_) {  // the stream was synchronised by the caller
+        float ms = 0.f;
+        CK(cudaEventElapsedTime(&ms, ce.first, ce.second));
+        prof_ms_[KK_CALL] += ms;
+        prof_n_[KK_CALL] += 1;
+        cudaEventDestroy(ce.first);
+        cudaEventDestroy(ce.second);
+    }
+    call_events_.clear();
     if (!timing_ || !last_graph_) return;
     const CapturedGraph &g = *last_graph_;
     for (size_t i = 0; i + 1 < g.events.size(); ++i) {
@@ -1721,8 +1743,15 @@ void Engine::accumulate_timing() {
     last_graph_ = nullptr;
 }
 
-void Engine::set_kernel_timing(bool on) {
-    timing_ = on;
+void Engine::set_kernel_timing(int mode) {
+    if (mode < 0 || mode > 2) throw std::runtime_error("kernel timing must be 0 (off), 1 (per kernel) or 2 (per call)");
+    timing_ = mode == 1;
+    call_timing_ = mode == 2;
+    for (auto &ce : call_events_) {
+        cudaEventDestroy(ce.first);
+        cudaEventDestroy(ce.second);
+    }
+    call_events_.clear();
     for (int k = 0; k < KK_COUNT; ++k) {
         prof_ms_[k] = 0.0;
         prof_n_[k] = 0;
