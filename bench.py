@@ -564,31 +564,22 @@ def run_ours(args, rank, world, local_rank, dist):
     for _ in range(5):
         eng.global_step_embed([s1], x1, want_hidden=False)
     # one step at a time with L2 flushed before each (the 96 MB of weights would otherwise stay
-    # in the 126 MB L2): the call's latency through the C ABI (events around the call, host
-    # copies and the host sync included), then the device time of its launched sequence alone
-    # (kernel timing mode 2: one event pair around the captured step)
+    # in the 126 MB L2): the call's latency through the C ABI, CUDA events around the call (host
+    # copies, the launched step and the host sync included)
     n1 = 30
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    api_us, dev_us = [], []
-    for mode in (0, 2):
-        eng.fill_state_random(s1, 128, seed=99)
-        eng.kernel_profile(mode)
-        for _ in range(n1):
-            flush.fill_(mode + 1)
-            b0.record()
-            eng.global_step_embed([s1], x1, want_hidden=False)
-            b1.record()
-            torch.cuda.synchronize()
-            if mode == 0:
-                api_us.append(1000 * b0.elapsed_time(b1))
-            else:
-                dev_us.append(1000 * eng.kernel_profile_read()["call_graph"][0])
-                eng.kernel_profile(2)  # clears the totals
-    eng.kernel_profile(0)
+    api_us = []
+    eng.fill_state_random(s1, 128, seed=99)
+    for _ in range(n1):
+        flush.fill_(1)
+        b0.record()
+        eng.global_step_embed([s1], x1, want_hidden=False)
+        b1.record()
+        torch.cuda.synchronize()
+        api_us.append(1000 * b0.elapsed_time(b1))
     del flush
     b1_us = float(np.median(api_us))
-    b1_dev_us = float(np.median(dev_us))
     b1_bytes = 12 * (q8x4_bytes(2304, 768) + q8x4_bytes(768, 768) + q8x4_bytes(3072, 768) + q8x4_bytes(768, 3072)) \
         + 485_376 + POS_BYTES * (128 + n1 // 2 + 1) + POS_BYTES
     pk = peaks()
@@ -716,13 +707,13 @@ def run_ours(args, rank, world, local_rank, dist):
             "prefill": pf,
             "codec": codec,
             "pipeline": pipe,
-            "batch1_global_step": {"us": round(b1_us, 2), "device_us": round(b1_dev_us, 2), "kv_len": 128,
-                                   "algorithmic_bytes": b1_bytes, "l2": "flushed before every step",
+            "batch1_global_step": {"us": round(b1_us, 2), "kv_len": 128, "algorithmic_bytes": b1_bytes,
+                                   "l2": "flushed before every step",
                                    "achieved_gbs": round(b1_bytes / (b1_us / 1e6) / 1e9, 1),
                                    "frac_of_hbm": round(b1_bytes / (b1_us / 1e6) / 1e9 / pk["hbm_gbs"], 4),
-                                   "device_frac_of_hbm": round(b1_bytes / (b1_dev_us / 1e6) / 1e9 / pk["hbm_gbs"], 4),
-                                   "path": "two-launch layers (layer_small.cuh); us = one C-ABI call with host "
-                                           "copies and sync, device_us = its launched sequence"},
+                                   "path": "two-launch layers (layer_small.cuh); one C-ABI call with host copies "
+                                           "and sync per step (profiles/small_layers_b1.md: 131 us of it on the "
+                                           "device)"},
             "kernel_breakdown_ms_per_frame": breakdown}
     if rank == 0:
         print(json.dumps(line), flush=True)

@@ -361,8 +361,7 @@ class Engine:
         self._check(self.lib.mossgpu_debug_matrix_tile_bytes(self.h, name.encode(), out, out.size))
         return out
 
-    def kernel_profile(self, enable: int):
-        """1 (or True) = per kernel, 2 = per call (the whole launched sequence), 0 = off."""
+    def kernel_profile(self, enable: bool):
         self._check(self.lib.mossgpu_kernel_profile(self.h, int(enable)))
 
     def kernel_profile_read(self) -> dict[str, tuple[float, int]]:

@@ -253,7 +253,7 @@ int mossgpu_debug_matrix_tile_bytes(mossgpu_engine *e, const char *name, uint8_t
 }
 
 int mossgpu_kernel_profile(mossgpu_engine *e, int enable) {
-    return guarded(e, [&](mossgpu::Engine &g) { g.set_kernel_timing(enable); });
+    return guarded(e, [&](mossgpu::Engine &g) { g.set_kernel_timing(enable != 0); });
 }
 
 int mossgpu_kernel_profile_read(mossgpu_engine *e, float *total_ms, int *launches, int max_kinds, int *n_kinds) {

@@ -83,10 +83,6 @@ Engine::~Engine() {
         if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
         for (cudaEvent_t ev : kv.second.events) cudaEventDestroy(ev);
     }
-    for (auto &ce : call_events_) {
-        cudaEventDestroy(ce.first);
-        cudaEventDestroy(ce.second);
-    }
     for (void *p : owned_) cudaFree(p);
     for (void *p : pinned_) cudaFreeHost(p);
     if (own_stream_) cudaStreamDestroy(own_stream_);
@@ -276,6 +272,11 @@ void Engine::allocate_state() {
     CK(cudaMallocHost(&hp, out_bytes));
     pinned_.push_back(hp);
     h_out_ = static_cast<uint8_t *>(hp);
+    // pinned staging of a global step's input rows, so that their copy is asynchronous (a copy
+    // from pageable memory would first wait for the stream's earlier work)
+    CK(cudaMallocHost(&hp, R * kHidden * sizeof(float)));
+    pinned_.push_back(hp);
+    h_x_ = static_cast<float *>(hp);
 
     // RoPE table in double precision, cast to fp32 (llm.cpp:90-102)
     // rows for every global position and for the 17 local positions
@@ -1544,7 +1545,8 @@ void Engine::global_step_embed(const int32_t *sids, int n, const float *x, float
         pos[r] = slots_[size_t(sids[r])].pos;
     }
     CK(cudaMemcpyAsync(d_ctl_, h_ctl_, size_t(2 * r_max_) * sizeof(int), cudaMemcpyHostToDevice, stream_));
-    CK(cudaMemcpyAsync(x_, x, size_t(n) * kHidden * sizeof(float), cudaMemcpyHostToDevice, stream_));
+    std::memcpy(h_x_, x, size_t(n) * kHidden * sizeof(float));
+    CK(cudaMemcpyAsync(x_, h_x_, size_t(n) * kHidden * sizeof(float), cudaMemcpyHostToDevice, stream_));
     run_captured((uint64_t(2) << 40) | uint64_t(n), [&] { issue_global_embed(n); });
     float *h = reinterpret_cast<float *>(h_out_);
     if (hidden_out) {
@@ -1656,7 +1658,7 @@ const char *kernel_kind_name(int kind) {
         "qkv_global", "attn_decode_paged", "proj_global", "fc_in_global", "fc_out_global", "ln_f",
         "qkv_local", "attn_local", "proj_local", "fc_in_local", "fc_out_local", "gate_w8a8",
         "audio_heads", "sample", "frame_commit", "build_activation_image", "attn_combine", "attn_prefill", "qkv_rope",
-        "local_decoder_fused", "small_layer_attn", "small_layer_mlp", "call_graph"};
+        "local_decoder_fused", "small_layer_attn", "small_layer_mlp"};
     return (kind >= 0 && kind < KK_COUNT) ? names[kind] : "?";
 }
 
@@ -1675,17 +1677,9 @@ template <class F>
 void Engine::run_captured(uint64_t key, F &&issue) {
     launches_ = 0;
     last_graph_ = nullptr;
-    std::pair<cudaEvent_t, cudaEvent_t> ce{nullptr, nullptr};
-    if (call_timing_) {
-        CK(cudaEventCreate(&ce.first));
-        CK(cudaEventCreate(&ce.second));
-        call_events_.push_back(ce);
-        CK(cudaEventRecord(ce.first, stream_));
-    }
     if (!use_graphs_) {
         issue();
         CK(cudaGetLastError());
-        if (ce.second) CK(cudaEventRecord(ce.second, stream_));
         return;
     }
     key |= (uint64_t(timing_) << 48) | (uint64_t(gemm_path_) << 50);  // both change what is captured
@@ -1717,21 +1711,11 @@ void Engine::run_captured(uint64_t key, F &&issue) {
         it = graphs_.emplace(key, std::move(g)).first;
     }
     CK(cudaGraphLaunch(it->second.exec, stream_));
-    if (ce.second) CK(cudaEventRecord(ce.second, stream_));
     launches_ = it->second.launches;
     last_graph_ = timing_ ? &it->second : nullptr;
 }
 
 void Engine::accumulate_timing() {
-    for (auto &ce : call_events_) {  // the stream was synchronised by the caller
-        float ms = 0.f;
-        CK(cudaEventElapsedTime(&ms, ce.first, ce.second));
-        prof_ms_[KK_CALL] += ms;
-        prof_n_[KK_CALL] += 1;
-        cudaEventDestroy(ce.first);
-        cudaEventDestroy(ce.second);
-    }
-    call_events_.clear();
     if (!timing_ || !last_graph_) return;
     const CapturedGraph &g = *last_graph_;
     for (size_t i = 0; i + 1 < g.events.size(); ++i) {
@@ -1743,15 +1727,8 @@ void Engine::accumulate_timing() {
     last_graph_ = nullptr;
 }
 
-void Engine::set_kernel_timing(int mode) {
-    if (mode < 0 || mode > 2) throw std::runtime_error("kernel timing must be 0 (off), 1 (per kernel) or 2 (per call)");
-    timing_ = mode == 1;
-    call_timing_ = mode == 2;
-    for (auto &ce : call_events_) {
-        cudaEventDestroy(ce.first);
-        cudaEventDestroy(ce.second);
-    }
-    call_events_.clear();
+void Engine::set_kernel_timing(bool on) {
+    timing_ = on;
     for (int k = 0; k < KK_COUNT; ++k) {
         prof_ms_[k] = 0.0;
         prof_n_[k] = 0;

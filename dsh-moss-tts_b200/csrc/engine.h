@@ -8,7 +8,6 @@
 #include <array>
 #include <string>
 #include <unordered_map>
-#include <utility>
 #include <vector>
 
 #include "types.h"
@@ -48,7 +47,6 @@ enum KernelKind {
     KK_QKV_G, KK_ATTN_DECODE, KK_PROJ_G, KK_FCIN_G, KK_FCOUT_G, KK_LNF,
     KK_QKV_L, KK_ATTN_LOCAL, KK_PROJ_L, KK_FCIN_L, KK_FCOUT_L, KK_GATE, KK_HEADS, KK_SAMPLE, KK_COMMIT,
     KK_BIMG, KK_ATTN_COMBINE, KK_ATTN_PREFILL, KK_QKV_ROPE, KK_LOCAL_FUSED, KK_SMALL_ATTN, KK_SMALL_MLP,
-    KK_CALL,  // mode 2 of the kernel timing: a call's whole launch sequence
     KK_COUNT
 };
 const char *kernel_kind_name(int kind);
@@ -114,9 +112,7 @@ public:
     void small_layer_stamps(unsigned long long *out, size_t n);
     void set_cuda_stream(void *s);
     void fill_state_random(int sid, int n_pos, uint64_t seed);
-    // 0 = off, 1 = per kernel (events between the kernels of the captured sequence), 2 = per
-    // call (one event pair around each launched sequence; the kernels' overlap is kept)
-    void set_kernel_timing(int mode);
+    void set_kernel_timing(bool on);
     void read_kernel_timing(float *total_ms, int *launches, int max_kinds, int *n_kinds) const;
     void set_use_graphs(bool on) { use_graphs_ = on; }
     // 0 = automatic (tensor cores above kGemvMaxRows rows), 1 = CUDA-core GEMV, 2 = tensor cores
@@ -232,6 +228,7 @@ private:
     uint8_t *bimg_a_ = nullptr;    // activation image, K = 768, up to 256 rows
     uint8_t *bimg_mlp_ = nullptr;  // activation image, K = 3072 (fc_in output -> fc_out input)
     int *dev_err_ = nullptr;       // [0]: kernels' time-out flag; [1]: fault-injection word
+    float *h_x_ = nullptr;         // pinned staging of global_step_embed's input rows
     int *h_err_ = nullptr;         // pinned host copy of it
     int gemm_path_ = 0;
     // small-batch layers: the three int64 residual accumulators D ([3][kGemvMaxRows][768]);
@@ -262,8 +259,6 @@ private:
     bool use_graphs_ = true;
     bool pdl_ = true;  // MOSSGPU_PDL=0 in the environment turns it off (A/B measurements)
     bool timing_ = false;
-    bool call_timing_ = false;
-    std::vector<std::pair<cudaEvent_t, cudaEvent_t>> call_events_;  // mode 2: pairs not yet read
     std::unordered_map<uint64_t, CapturedGraph> graphs_;
     CapturedGraph *capturing_ = nullptr;
     CapturedGraph *last_graph_ = nullptr;

@@ -205,12 +205,9 @@ int mossgpu_debug_inject_wait_timeout(mossgpu_engine *e, int enable);
 /* Same as mossgpu_debug_matrix_bytes for the tensor-core tile copy of the matrix. */
 int mossgpu_debug_matrix_tile_bytes(mossgpu_engine *e, const char *name, uint8_t *out, size_t out_bytes);
 
-/* Device timing.  enable = 1: per kernel, CUDA events recorded between the kernels of the
- * captured frame (which breaks their programmatic-dependent-launch overlap); enable = 2: per
- * call, one event pair around each launched sequence (a frame, a multi-frame run, a global
- * step), reported as the class "call_graph", with the kernels' overlap intact; 0 = off.
- * Enabling clears the totals; read returns, per kernel class, the summed milliseconds and
- * launch counts (n_kinds = number of classes). */
+/* Per-kernel device timing, measured with CUDA events recorded between the kernels of the
+ * captured frame.  enable = 1 clears the totals and starts accumulating; read returns, per
+ * kernel class, the summed milliseconds and launch counts (n_kinds = number of classes). */
 int mossgpu_kernel_profile(mossgpu_engine *e, int enable);
 int mossgpu_kernel_profile_read(mossgpu_engine *e, float *total_ms, int *launches, int max_kinds, int *n_kinds);
 const char *mossgpu_kernel_name(int kind);
