@@ -868,8 +868,13 @@ __global__ void __launch_bounds__(kArWarps * 32) k_attn_rows(const float *__rest
     float m = -INFINITY, l = 0.f, o[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) o[j] = 0.f;
+    // the page-table entry of a warp's next page is fetched one iteration ahead, so that each
+    // iteration waits on one memory round trip (the K/V loads) instead of two
+    const int *pt = page_table + (size_t)slot * pages_per_stream;
+    int page_next = warp < npg ? pt[warp] : 0;
     for (int pg = warp; pg < npg; pg += kArWarps) {
-        const int page = page_table[(size_t)slot * pages_per_stream + pg];
+        const int page = page_next;
+        if (pg + kArWarps < npg) page_next = pt[pg + kArWarps];
         const __half *kb = kv + (size_t)page * kPageHalfs + (size_t)hd * kPage * kHeadDim + ds * 8;
         const __half *vb = kb + (size_t)kHeads * kPage * kHeadDim;
         const int pb = pg * kPage;
