@@ -390,11 +390,36 @@ def run_reference_arm(args, rank, world):
 
 # ----------------------------------------------------------------------------- GPU arm
 
-SL_ATTN_PHASES = ["issue pre-wait copies", "dependency wait", "x in + LN1", "QKV + RoPE", "cluster barrier 1",
-                  "q/k/v gather + attention + CTA merge", "cluster barrier 2", "DSMEM merge", "proj + stores",
-                  "last cluster wait"]
-SL_MLP_PHASES = ["issue pre-wait copies", "dependency wait", "x in + LN2", "fc_in + GELU", "fc_out partials",
-                 "cluster barrier", "DSMEM reduce", "accumulator adds", "last cluster wait"]
+SL_ATTN_PHASES = ["issue pre-wait copies", "dependency wait", "x in + LN1", "QKV + RoPE, pushed to the head's CTAs",
+                  "cluster barrier 1", "attention + CTA merge, pushed", "cluster barrier 2",
+                  "merge of the pushed partials", "proj + accumulator adds + KV append", "exit"]
+SL_MLP_PHASES = ["issue pre-wait copies", "dependency wait", "x in + LN2", "fc_in + GELU",
+                 "fc_out partials, pushed", "cluster barrier", "sum of the pushed partials", "accumulator adds",
+                 "exit"]
+
+
+def phase_stats(st, step_us) -> dict:
+    """Per-phase medians (µs) of the small-layer phase stamps st[steps][24 launches][96 CTAs][12]
+    (ns; launch p = 2 layer + {0: attention half, 1: MLP half}; stamp 2 = the dependency wait
+    returned, the last stamp = the CTA's end).  after_wait: from a launch's median wait return
+    to its last CTA's end; handoff: from a launch's last CTA end to the next launch's median
+    wait return; layers_us: from the first launch's first CTA start to the last launch's end."""
+    st = np.asarray(st, dtype=np.int64)
+    out = {"steps": int(st.shape[0]), "step_us_events": round(float(np.median(step_us)), 2)}
+    last = {0: len(SL_ATTN_PHASES), 1: len(SL_MLP_PHASES)}
+    for half, names in ((0, SL_ATTN_PHASES), (1, SL_MLP_PHASES)):
+        key = "attn" if half == 0 else "mlp"
+        ph = st[:, half::2]  # [steps][12][96][12]
+        d = np.diff(ph[..., : last[half] + 1], axis=-1) / 1000.0
+        out[key] = {n: round(float(np.median(d[..., i])), 3) for i, n in enumerate(names)}
+        span = (ph[..., last[half]].max(axis=-1) - np.median(ph[..., 2], axis=-1)) / 1000.0
+        out[key + "_after_wait_us"] = round(float(np.median(span)), 3)
+    nl = st.shape[1]
+    ends = np.where(np.arange(nl)[None, :, None] % 2 == 0, st[..., last[0]], st[..., last[1]]).max(axis=-1)
+    release = np.median(st[..., 2], axis=-1)
+    out["handoff_us"] = round(float(np.median((release[:, 1:] - ends[:, :-1]) / 1000.0)), 3)
+    out["layers_us"] = round(float(np.median((ends[:, -1] - st[:, 0, :, 0].min(axis=-1)) / 1000.0)), 2)
+    return out
 
 
 def run_phase_stamps(steps: int, stamps: bool = True):
@@ -429,20 +454,7 @@ def run_phase_stamps(steps: int, stamps: bool = True):
     eng.close()
     if not stamps:
         return
-    st = np.stack(st)  # [steps][24][96][12]
-    out = {"workload": "configs[0] batch-1 global step, 128 cached positions", "steps": steps,
-           "step_us_events": round(float(np.median(step_us)), 2)}
-    last = {0: 10, 1: 9}
-    for half, names in ((0, SL_ATTN_PHASES), (1, SL_MLP_PHASES)):
-        ph = st[:, half::2]  # [steps][12][96][12]
-        d = np.diff(ph[..., : last[half] + 1], axis=-1) / 1000.0
-        out["attn" if half == 0 else "mlp"] = {n: round(float(np.median(d[..., i])), 3) for i, n in enumerate(names)}
-        span = (ph[..., last[half]].max(axis=-1) - np.median(ph[..., 2], axis=-1)) / 1000.0
-        out[("attn" if half == 0 else "mlp") + "_after_wait_us"] = round(float(np.median(span)), 3)
-    ends = np.where(np.arange(24)[None, :, None] % 2 == 0, st[..., 10], st[..., 9]).max(axis=-1)  # [steps][24]
-    release = np.median(st[..., 2], axis=-1)
-    out["handoff_us"] = round(float(np.median((release[:, 1:] - ends[:, :-1]) / 1000.0)), 3)
-    out["layers_us"] = round(float(np.median((ends[:, -1] - st[:, 0, :, 0].min(axis=-1)) / 1000.0)), 2)
+    out = {"workload": "configs[0] batch-1 global step, 128 cached positions", **phase_stats(np.stack(st), step_us)}
     print(json.dumps(out), flush=True)
 
 
