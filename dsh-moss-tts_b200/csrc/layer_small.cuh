@@ -157,7 +157,8 @@ __device__ __forceinline__ void sl_act(__half *hi, __half *lo, int stride, int r
 
 // LayerNorm of rows < R of xs (llm.cpp:159-171) into the hi / lo planes ([8][768]): TPR =
 // 256 / MAXR threads a row, each with E = 768 / TPR columns; two reductions (sum, then squared
-// deviations) over the thread's columns, the warp and the row's warps (red: 8 floats).  Every
+// deviations) over the thread's columns, the warp and the row's warps (red: 16 floats, the
+// sums in the first 8 and the squared deviations in the last 8, so two CTA barriers).  Every
 // thread of the CTA calls it.  Plane rows >= R are left as they are: each MMA output column
 // depends on its own B column only, and those columns are never read.
 template <int MAXR>
@@ -191,12 +192,11 @@ __device__ __forceinline__ void sl_layernorm(const float *xs, int R, const float
     }
     d2 = warp_sum(d2);
     if (WPR > 1) {
-        __syncthreads();  // every thread has read the sums
-        if (lane == 0) red[r * WPR + wr] = d2;
+        if (lane == 0) red[8 + r * WPR + wr] = d2;
         __syncthreads();
         d2 = 0.f;
 #pragma unroll
-        for (int q = 0; q < WPR; ++q) d2 += red[r * WPR + q];
+        for (int q = 0; q < WPR; ++q) d2 += red[8 + r * WPR + q];
     }
     const float var = __fdiv_rn(d2, (float)kHidden);
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(var + 1e-5f));
@@ -271,8 +271,8 @@ struct SlAttnSmem {
     static constexpr int bp = bq + 24 * 4;                     // float [96] proj bias of its rows
     static constexpr int rs = bp + 96 * 4;                     // float2 [8][4] RoPE (cos, sin)
     static constexpr int meta = rs + kSlMaxRows * 4 * 8;       // int [5][8]: pos, slot, pages, first item, page of pos
-    static constexpr int red = meta + 5 * kSlMaxRows * 4;      // float [8] LayerNorm partial sums
-    static constexpr int xs = red + 8 * 4;                     // float [MAXR][768] x
+    static constexpr int red = meta + 5 * kSlMaxRows * 4;      // float [16] LayerNorm partial sums
+    static constexpr int xs = red + 16 * 4;                    // float [MAXR][768] x
     static constexpr int xfix = xs + MAXR * kHidden * 4;       // int64 [MAXR][96] x of the proj rows (head 0)
     static constexpr int act = xfix + MAXR * 96 * 8;           // half [2][8][768] LN1(x) hi, lo; then QKV
                                                                // partials; then [8 CTAs][MAXR][68] attention partials
@@ -673,8 +673,8 @@ struct SlMlpSmem {
     static constexpr int lnb = lnw + kHidden * 4;
     static constexpr int bi = lnb + kHidden * 4;          // float [32] fc_in bias of the CTA's features
     static constexpr int bo = bi + 32 * 4;                // float [96] fc_out bias of its reduce rows
-    static constexpr int red = bo + 96 * 4;               // float [8] LayerNorm partial sums
-    static constexpr int xs = red + 8 * 4;                // float [MAXR][768] x
+    static constexpr int red = bo + 96 * 4;               // float [16] LayerNorm partial sums
+    static constexpr int xs = red + 16 * 4;               // float [MAXR][768] x
     static constexpr int xfix = xs + MAXR * kHidden * 4;  // int64 [MAXR][96] x of the reduce rows (cluster 0)
     static constexpr int act = xfix + MAXR * 96 * 8;      // half [2][8][768] LN2(x) hi, lo; then fc_in partials
                                                           // [8 warps][2][128] float
